@@ -1,0 +1,82 @@
+// Shared helpers for the sm_100a kernels and the C-ABI: status codes, the
+// per-thread error message, launch checks and small device utilities.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "flow2surf_b200.h"
+
+namespace f2s {
+
+// Record a formatted message for f2s_last_error() and return `code`.
+int fail(int code, const char* fmt, ...);
+
+// Return F2S_OK, or F2S_ERR_CUDA with the pending launch error named.
+int check_launch(const char* what);
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+inline int ceil_div(int a, int b) { return (a + b - 1) / b; }
+inline int64_t ceil_div64(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// Number of SMs on the current device (cached per device).
+int sm_count();
+
+}  // namespace f2s
+
+#define F2S_REQUIRE(cond, ...)                                        \
+    do {                                                              \
+        if (!(cond)) return f2s::fail(F2S_ERR_INVALID_ARGUMENT, __VA_ARGS__); \
+    } while (0)
+
+#define F2S_LIMIT(cond, ...)                                          \
+    do {                                                              \
+        if (!(cond)) return f2s::fail(F2S_ERR_UNSUPPORTED, __VA_ARGS__); \
+    } while (0)
+
+#define F2S_CUDA_TRY(expr)                                            \
+    do {                                                              \
+        cudaError_t err_ = (expr);                                    \
+        if (err_ != cudaSuccess)                                      \
+            return f2s::fail(F2S_ERR_CUDA, "%s: %s", #expr, cudaGetErrorString(err_)); \
+    } while (0)
+
+#define F2S_TRY(expr)                                                 \
+    do {                                                              \
+        int st_ = (expr);                                             \
+        if (st_ != F2S_OK) return st_;                                \
+    } while (0)
+
+// ---------------------------------------------------------------------------
+// Device helpers
+// ---------------------------------------------------------------------------
+
+// Order-preserving map from float bits to uint32 (the key of the reference's
+// flow2surf_neighbor_key, knn.cuh:7-17): -0 is folded onto +0 first, negative
+// values flip all bits, non-negative values flip the sign bit.
+__device__ __forceinline__ uint32_t f2s_ordered_bits(float d) {
+    const float canonical = d == 0.0f ? 0.0f : d;
+    const uint32_t bits = __float_as_uint(canonical);
+    return bits ^ ((bits & 0x80000000u) ? 0xffffffffu : 0x80000000u);
+}
+
+__device__ __forceinline__ float f2s_warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float f2s_warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+__device__ __forceinline__ float f2s_gelu_erf(float x) {
+    return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
+}
+
+__device__ __forceinline__ float f2s_silu(float x) { return x / (1.0f + expf(-x)); }
+
+__device__ __forceinline__ float f2s_leaky(float x) { return x > 0.0f ? x : 0.2f * x; }

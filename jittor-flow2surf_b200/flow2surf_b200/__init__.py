@@ -1,0 +1,10 @@
+"""B200-native (sm_100a) Flow2Surf reverse-flow denoising.
+
+Drop-in for the reference's hot path: the operators of flow2surf/models/ops,
+the Flow2SurfNet model and patch_denoise, all computed by hand-written CUDA
+kernels in libflow2surf_sm100.so behind a C-ABI (include/flow2surf_b200.h).
+"""
+
+from .ops import knn_indices
+
+__all__ = ["knn_indices"]

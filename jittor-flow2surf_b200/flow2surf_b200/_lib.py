@@ -1,0 +1,86 @@
+"""ctypes binding of libflow2surf_sm100.so (the C-ABI in include/flow2surf_b200.h).
+
+There is no fallback: if the library is missing or CUDA is unavailable the
+operators raise. Loading the library needs no GPU; calling a compute entry
+point does.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+LIBRARY_NAME = "libflow2surf_sm100.so"
+LIBRARY_PATH = Path(__file__).resolve().parent / LIBRARY_NAME
+
+F2S_OK = 0
+F2S_ERR_INVALID_ARGUMENT = 1
+F2S_ERR_UNSUPPORTED = 2
+F2S_ERR_CUDA = 3
+F2S_ERR_WORKSPACE = 4
+
+_p = ctypes.c_void_p
+_i = ctypes.c_int
+_i64 = ctypes.c_int64
+_f = ctypes.c_float
+_d = ctypes.c_double
+_sz = ctypes.c_size_t
+
+# name -> argtypes; every name here is declared in include/flow2surf_b200.h.
+SIGNATURES: dict[str, list] = {
+    "f2s_last_error": [],
+    "f2s_version": [],
+    "f2s_knn": [_p, _i, _i, _i, _i, _p, _p],
+}
+
+_RESTYPES = {"f2s_last_error": ctypes.c_char_p}
+
+_LIB = None
+
+
+class Flow2SurfError(RuntimeError):
+    """A C-ABI call returned a status other than F2S_OK."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(f"[status {status}] {message}")
+        self.status = status
+
+
+def lib() -> ctypes.CDLL:
+    global _LIB
+    if _LIB is None:
+        if not LIBRARY_PATH.exists():
+            raise RuntimeError(
+                f"{LIBRARY_NAME} is not built; run `python jittor-flow2surf_b200/build.py` "
+                "(or __graft_entry__.build())")
+        handle = ctypes.CDLL(str(LIBRARY_PATH))
+        for name, argtypes in SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.argtypes = argtypes
+            fn.restype = _RESTYPES.get(name, ctypes.c_int)
+        _LIB = handle
+    return _LIB
+
+
+def check(status: int) -> None:
+    if status != F2S_OK:
+        message = lib().f2s_last_error().decode("utf-8", "replace")
+        if status in (F2S_ERR_INVALID_ARGUMENT, F2S_ERR_UNSUPPORTED):
+            raise ValueError(message)
+        raise Flow2SurfError(status, message)
+
+
+def call(name: str, *args) -> None:
+    check(getattr(lib(), name)(*args))
+
+
+def ptr(tensor) -> int | None:
+    """Raw device pointer of a torch tensor (None for an empty one)."""
+    return tensor.data_ptr() if tensor is not None and tensor.numel() > 0 else None
+
+
+def stream_handle(stream=None) -> int | None:
+    import torch
+
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream

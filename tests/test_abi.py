@@ -1,0 +1,61 @@
+"""The C-ABI library loads and exports every entry point the header declares.
+
+No compute calls: these run without a GPU.
+"""
+
+import re
+from pathlib import Path
+
+import pytest
+
+from flow2surf_b200 import _lib
+
+HEADER = Path(__file__).resolve().parent.parent / "include" / "flow2surf_b200.h"
+
+
+def declared_functions():
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(f2s_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_header_declares_entry_points():
+    names = declared_functions()
+    assert "f2s_knn" in names and "f2s_last_error" in names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.lib()
+    for name in declared_functions():
+        assert hasattr(lib, name), f"{name} declared in the header but not exported"
+
+
+def test_python_signatures_cover_header():
+    assert set(declared_functions()) == set(_lib.SIGNATURES)
+
+
+def test_version_and_error_without_gpu():
+    lib = _lib.lib()
+    assert lib.f2s_version() >= 100
+    assert isinstance(lib.f2s_last_error(), bytes)
+
+
+def test_invalid_arguments_fail_before_any_device_work():
+    """Argument validation happens on the host and needs no GPU."""
+    lib = _lib.lib()
+    assert lib.f2s_knn(None, 1, 3, 8, 0, None, None) == _lib.F2S_ERR_INVALID_ARGUMENT
+    assert b"k must be >= 1" in lib.f2s_last_error()
+    assert lib.f2s_knn(None, 1, 3, 8, 33, None, None) == _lib.F2S_ERR_UNSUPPORTED
+    assert lib.f2s_knn(None, 1, 3, 4096, 8, None, None) == _lib.F2S_ERR_UNSUPPORTED
+    assert lib.f2s_knn(None, 1, 3, 8, 4, None, None) == _lib.F2S_ERR_INVALID_ARGUMENT
+    assert lib.f2s_knn(None, 0, 3, 8, 4, None, None) == _lib.F2S_OK
+
+
+def test_operator_rejects_cpu_tensors():
+    torch = pytest.importorskip("torch")
+    from flow2surf_b200 import knn_indices
+
+    with pytest.raises(ValueError):
+        knn_indices(torch.zeros(1, 3, 8), 4)
+    with pytest.raises(ValueError, match="k must be >= 1"):
+        knn_indices(torch.zeros(1, 3, 8), 0)
