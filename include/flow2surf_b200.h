@@ -62,6 +62,98 @@ int f2s_version(void);
 int f2s_knn(const float* features, int B, int C, int N, int k,
             int32_t* indices, void* stream);
 
+/*
+ * Offset-attention aggregate: column softmax over queries, then row
+ * normalisation over keys, then the value product, without ever storing the
+ * N x N matrix.
+ * Replaces offset_attention_aggregate (flow2surf/models/ops/attention.py:84-106;
+ * semantics of _aggregate_jittor, attention.py:15-19).
+ *   query (B, N, d), key (B, d, N), value (B, N, C) float32 -> out (B, N, C)
+ *   workspace: f2s_offset_attention_workspace_bytes() bytes (key transposed
+ *   point-major and one log-sum-exp per key).
+ * Limits: d <= 128, C <= 256.
+ */
+int f2s_offset_attention_workspace_bytes(int B, int N, int d, size_t* bytes);
+int f2s_offset_attention(const float* query, const float* key, const float* value,
+                         int B, int N, int d, int C, float* out,
+                         void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Normalised neighbour-message reduction with HPE geometry, fused into one
+ * kernel (hidden and per-edge contributions never reach HBM).
+ * Replaces reduce_neighbor_messages (flow2surf/models/ops/neighbor_reduce.py:244-337)
+ * with its no-grad CUDA branch hpe_hidden (hpe.py:35-43, hpe_hidden_forward.cu),
+ * project_hpe_output (hpe.py:46-50) and neighbor_reduce (neighbor_reduce_forward.cu).
+ *   content (B, 2C, N), geometry (B, N, K, D), indices (B, N, K) int32,
+ *   hpe_input_weight (H, D), hpe_input_bias (H), hpe_output_weight (C, H),
+ *   hpe_output_bias (C), hpe_norm_weight/bias (H), message_norm_weight/bias (C)
+ *   -> out (B, C, N).
+ *   workspace: f2s_neighbor_reduce_workspace_bytes() bytes.
+ * Limits: K <= 64, D <= 8, H <= 256, C <= 256.
+ */
+int f2s_neighbor_reduce_workspace_bytes(int B, int N, int C, size_t* bytes);
+int f2s_neighbor_reduce(const float* content, const float* geometry, const int32_t* indices,
+                        const float* hpe_input_weight, const float* hpe_input_bias,
+                        const float* hpe_output_weight, const float* hpe_output_bias,
+                        const float* hpe_norm_weight, const float* hpe_norm_bias,
+                        const float* message_norm_weight, const float* message_norm_bias,
+                        int B, int N, int K, int D, int H, int C, float* out,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Model (flow2surf/models/network.py:29-95)                                */
+/* ------------------------------------------------------------------------ */
+
+#define F2S_MAX_STAGES 6
+#define F2S_MAX_BLOCKS 16
+#define F2S_MAX_DECODER 4
+
+/* The architecture keys of build_model(cfg) (network.py:85-95). */
+typedef struct f2s_model_config {
+    int32_t k_neighbors;                     /* cfg["k_neighbors"]             */
+    int32_t feat_dim;                        /* cfg["feat_dim"]                */
+    int32_t num_blocks;                      /* cfg["num_blocks"]              */
+    int32_t alpha_dim;                       /* cfg["alpha_dim"]               */
+    int32_t ffn_ratio;                       /* cfg["ffn_ratio"]               */
+    int32_t num_stages;                      /* len(encoder_dims) + 1          */
+    int32_t stage_dims[F2S_MAX_STAGES];      /* encoder_dims + [feat_dim]      */
+    int32_t num_decoder;                     /* len(decoder_dims)              */
+    int32_t decoder_dims[F2S_MAX_DECODER];   /* cfg["decoder_dims"]            */
+} f2s_model_config;
+
+/*
+ * Layout of the packed parameter blob (float32). On success returns the
+ * number of segments (always > F2S_ERR_WORKSPACE, a valid config has at least
+ * 20) and, when the arrays are given, each segment's float offset and element
+ * count; *total_floats gets the blob size. On failure returns an f2s_status. Segment order (composed exactly as encoder.py:88-101 composes
+ * them):
+ *   alpha_emb.mlp.0.{weight,bias}, alpha_emb.mlp.2.{weight,bias},
+ *   input_embed.net.{0.weight, 0.bias, 1.weight, 1.bias, 3.weight, 3.bias},
+ *   per stage: [Wd; Wc - Wd] (2C_out x C_in), position_embed.net.0.{weight,bias},
+ *     position_embed.net.1.{weight,bias}, P W_out (C_out x H), P b_out,
+ *     norm.{weight,bias}   (P = projection.weight[:, 2 C_in:], W_out/b_out =
+ *     position_embed.net.3)
+ *   proj.0.weight, proj.1.{weight,bias},
+ *   per block: mod.1.{weight,bias}, qkv_conv.weight, proj.weight,
+ *     ff_gate.{weight,bias}, ff1.{weight,bias}, ff2.{weight,bias},
+ *   per decoder layer: net.{3i}.weight, net.{3i+1}.{weight,bias}; output weight.
+ */
+int f2s_model_param_segments(const f2s_model_config* cfg, int64_t* offsets, int64_t* sizes,
+                             int capacity, int64_t* total_floats);
+
+/* Workspace bytes f2s_model_forward needs for B patches of M points. */
+int f2s_model_workspace_bytes(const f2s_model_config* cfg, int B, int M, size_t* bytes);
+
+/*
+ * Flow2SurfNet forward: x (B, 3, M) float32 patch coordinates, alpha (B)
+ * float32 -> velocity (B, M, 3) float32.
+ * Replaces Flow2SurfNet.execute (network.py:75-82) under jt.no_grad().
+ * Limits: M <= F2S_KNN_MAX_POINTS, stage widths and feat_dim <= 256.
+ */
+int f2s_model_forward(const f2s_model_config* cfg, const float* params, const float* x,
+                      const float* alpha, int B, int M, float* velocity,
+                      void* workspace, size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

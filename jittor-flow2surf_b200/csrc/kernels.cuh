@@ -1,0 +1,83 @@
+// Internal launch functions shared by the C-ABI translation units.
+#pragma once
+
+#include "common.cuh"
+
+namespace f2s {
+
+// ---- knn.cu ----
+int knn_launch(const float* features, int B, int C, int N, int k, int32_t* indices,
+               cudaStream_t stream);
+
+// ---- gemm.cu ----
+// Y[r, n] = sum_k A[r, k] * W[n, k] for r < rows, n < cols (A row-major with
+// leading dimension lda, W row-major (cols x K)), followed by an epilogue.
+enum GemmEpilogue {
+    kEpiStore = 0,          // Y = acc (+ bias)
+    kEpiGatedResidual = 1,  // Y += gate[r / rows_per_patch, n] * (acc (+ bias))
+    kEpiSwiGlu = 2,         // Y = silu(acc_W + bias) * (acc_W2 + bias2)
+};
+
+struct GemmArgs {
+    const float* A;
+    int lda;
+    const float* W;
+    const float* bias;     // may be null
+    const float* W2;       // SwiGLU value weights
+    const float* bias2;    // SwiGLU value bias
+    float* Y;
+    int ldy;
+    const float* gate;     // gated residual: (patches, gate_stride) rows
+    int gate_stride;
+    int rows_per_patch;
+    int rows, cols, K;
+    GemmEpilogue epilogue;
+};
+int gemm_f32(const GemmArgs& args, cudaStream_t stream);
+
+// ---- rownorm.cu ----
+// h = LN(x) * (1 + scale[p]) + shift[p]; LN two-pass over C, eps 1e-6.
+int ln_modulate(const float* x, int ldx, float* h, int ldh, const float* mod, int mod_stride,
+                int scale_off, int shift_off, int rows, int rows_per_patch, int C,
+                cudaStream_t stream);
+// y = LeakyReLU_0.2(LN(y) * gamma + beta) in place (two-pass, eps 1e-6).
+int ln_affine_leaky(float* y, int ldy, const float* gamma, const float* beta, int rows, int C,
+                    cudaStream_t stream);
+// LN (no affine, eps 1e-6) of columns [0, d) and [d, 2d) of each row, in place.
+int qk_norm(float* qkv, int ld, int rows, int d, cudaStream_t stream);
+
+// ---- attention.cu ----
+// Offset attention over point-major q, k (rows B*N, leading dim ldqk, width d)
+// and v (ldv, width C); out = h - A when h is given, else A. colstats holds
+// B*N floats of scratch (per-key log-sum-exp over queries).
+int attention_f32(const float* q, const float* k, int ldqk, const float* v, int ldv,
+                  const float* h, int ldh, float* out, int ldo, float* colstats, int B, int N,
+                  int d, int C, cudaStream_t stream);
+
+// ---- edge.cu ----
+// Fused neighbour stage: per edge (i, j = idx[i, k]) the HPE hidden
+// GELU(LN(W_in g + b_in)) of g = [xyz_j - xyz_i, xyz_i] (or a given geometry
+// row), the composed projection W_po h + b_po, plus the content terms, LN,
+// affine, LeakyReLU and the max over k.
+struct EdgeArgs {
+    const float* content;   // (B*M, ldc): [0, cout) neighbour term, [cout, 2cout) centre term
+    int ldc;
+    const float* xyz4;      // (B*M, 4) point-major xyz (model path), or null
+    const float* geometry;  // (B*M*K, D) explicit geometry (operator path), or null
+    int D;
+    const int32_t* idx;     // (B*M, K) indices local to each patch
+    int B, M, K, H, cout;
+    const float* hpe_w;     // (H, D)
+    const float* hpe_b;
+    const float* hpe_ln_w;
+    const float* hpe_ln_b;
+    const float* contrib_w; // (cout, H)
+    const float* contrib_b;
+    const float* ln_w;
+    const float* ln_b;
+    float* out;             // (B*M, ldo) row-major, already offset to its column
+    int ldo;
+};
+int edge_stage_f32(const EdgeArgs& args, cudaStream_t stream);
+
+}  // namespace f2s

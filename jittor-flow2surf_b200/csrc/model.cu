@@ -1,0 +1,550 @@
+// Flow2SurfNet forward (flow2surf/models/network.py:75-82) as a sequence of
+// sm_100a kernels over point-major activations, plus the parameter-blob and
+// workspace layouts and the operator entry points that share its kernels.
+#include <cfloat>
+#include <vector>
+
+#include "kernels.cuh"
+
+namespace f2s {
+
+int transpose_batched(const float* in, float* out, int B, int rows, int cols,
+                      cudaStream_t stream);
+
+namespace {
+
+constexpr int kMaxStages = F2S_MAX_STAGES;
+constexpr int kMaxBlocks = F2S_MAX_BLOCKS;
+constexpr int kMaxDecoder = F2S_MAX_DECODER;
+
+// ---------------------------------------------------------------------------
+// Parameter blob: float32 segments, each 16-byte aligned, in a fixed order.
+// ---------------------------------------------------------------------------
+struct StageParams {
+    int64_t content_w, hpe_w, hpe_b, hpe_ln_w, hpe_ln_b, contrib_w, contrib_b, ln_w, ln_b;
+};
+struct BlockParams {
+    int64_t mod_w, mod_b, qkv_w, proj_w, gate_w, gate_b, ff1_w, ff1_b, ff2_w, ff2_b;
+};
+struct DecParams {
+    int64_t w, ln_w, ln_b;
+};
+
+struct Layout {
+    int64_t alpha_w1, alpha_b1, alpha_w2, alpha_b2;
+    int64_t in_w, in_b, in_ln_w, in_ln_b, in_out_w, in_out_b;
+    StageParams stage[kMaxStages];
+    int64_t proj_w, proj_ln_w, proj_ln_b;
+    BlockParams block[kMaxBlocks];
+    DecParams dec[kMaxDecoder];
+    int64_t dec_out_w;
+    std::vector<int64_t> offsets, sizes;
+    int64_t total = 0;
+
+    int64_t add(int64_t n) {
+        const int64_t off = total;
+        offsets.push_back(off);
+        sizes.push_back(n);
+        total += (n + 3) & ~int64_t(3);
+        return off;
+    }
+};
+
+struct Dims {
+    int K, C, NB, A, Hf, qk, S, ndec;
+    int sd[kMaxStages], si[kMaxStages], dd[kMaxDecoder];
+    int sum_stage, max_cout, max_dec;
+};
+
+int check_config(const f2s_model_config* cfg, Dims& d) {
+    F2S_REQUIRE(cfg != nullptr, "model config is null");
+    d.K = cfg->k_neighbors;
+    d.C = cfg->feat_dim;
+    d.NB = cfg->num_blocks;
+    d.A = cfg->alpha_dim;
+    F2S_REQUIRE(d.K >= 1, "k_neighbors must be >= 1, got %d", d.K);
+    F2S_LIMIT(d.K <= F2S_KNN_MAX_K, "k_neighbors %d exceeds %d", d.K, F2S_KNN_MAX_K);
+    F2S_REQUIRE(d.NB >= 0, "num_blocks must be >= 0, got %d", d.NB);
+    F2S_LIMIT(d.NB <= kMaxBlocks, "num_blocks %d exceeds %d", d.NB, kMaxBlocks);
+    F2S_REQUIRE(cfg->ffn_ratio >= 1, "ffn_ratio must be >= 1, got %d", cfg->ffn_ratio);
+    F2S_REQUIRE(d.A >= 1, "alpha_dim must be >= 1, got %d", d.A);
+    F2S_REQUIRE(d.C >= 4, "channels must be >= 4, got %d", d.C);
+    F2S_LIMIT(d.C <= 256, "feat_dim %d exceeds 256", d.C);
+    F2S_LIMIT(d.A <= 256, "alpha_dim %d exceeds 256", d.A);
+    d.qk = d.C / 4;
+    d.Hf = d.C * cfg->ffn_ratio;
+    d.S = cfg->num_stages;
+    F2S_REQUIRE(d.S >= 1 && d.S <= kMaxStages, "num_stages %d outside [1, %d]", d.S, kMaxStages);
+    F2S_REQUIRE(cfg->stage_dims[d.S - 1] == d.C, "last stage width must equal feat_dim");
+    d.sum_stage = 0;
+    d.max_cout = 0;
+    for (int s = 0; s < d.S; ++s) {
+        d.sd[s] = cfg->stage_dims[s];
+        d.si[s] = s == 0 ? cfg->stage_dims[0] : cfg->stage_dims[s - 1];
+        F2S_REQUIRE(d.sd[s] >= 1, "stage width must be >= 1");
+        F2S_LIMIT(d.sd[s] <= 256, "stage width %d exceeds 256", d.sd[s]);
+        d.sum_stage += d.sd[s];
+        d.max_cout = d.sd[s] > d.max_cout ? d.sd[s] : d.max_cout;
+    }
+    d.ndec = cfg->num_decoder;
+    F2S_REQUIRE(d.ndec >= 0 && d.ndec <= kMaxDecoder, "num_decoder %d outside [0, %d]", d.ndec,
+                kMaxDecoder);
+    d.max_dec = 0;
+    for (int i = 0; i < d.ndec; ++i) {
+        d.dd[i] = cfg->decoder_dims[i];
+        F2S_REQUIRE(d.dd[i] >= 1, "decoder width must be >= 1");
+        d.max_dec = d.dd[i] > d.max_dec ? d.dd[i] : d.max_dec;
+    }
+    return F2S_OK;
+}
+
+Layout make_layout(const Dims& d) {
+    Layout L;
+    const int A4 = 4 * d.A, S0 = d.sd[0];
+    L.alpha_w1 = L.add(A4);
+    L.alpha_b1 = L.add(A4);
+    L.alpha_w2 = L.add((int64_t)d.A * A4);
+    L.alpha_b2 = L.add(d.A);
+    L.in_w = L.add((int64_t)S0 * 3);
+    L.in_b = L.add(S0);
+    L.in_ln_w = L.add(S0);
+    L.in_ln_b = L.add(S0);
+    L.in_out_w = L.add((int64_t)S0 * S0);
+    L.in_out_b = L.add(S0);
+    for (int s = 0; s < d.S; ++s) {
+        const int cin = d.si[s], cout = d.sd[s], H = cin;
+        StageParams& p = L.stage[s];
+        p.content_w = L.add((int64_t)2 * cout * cin);
+        p.hpe_w = L.add((int64_t)H * 6);
+        p.hpe_b = L.add(H);
+        p.hpe_ln_w = L.add(H);
+        p.hpe_ln_b = L.add(H);
+        p.contrib_w = L.add((int64_t)cout * H);
+        p.contrib_b = L.add(cout);
+        p.ln_w = L.add(cout);
+        p.ln_b = L.add(cout);
+    }
+    L.proj_w = L.add((int64_t)d.C * d.sum_stage);
+    L.proj_ln_w = L.add(d.C);
+    L.proj_ln_b = L.add(d.C);
+    for (int i = 0; i < d.NB; ++i) {
+        BlockParams& p = L.block[i];
+        p.mod_w = L.add((int64_t)6 * d.C * d.A);
+        p.mod_b = L.add(6 * d.C);
+        p.qkv_w = L.add((int64_t)(d.C + 2 * d.qk) * d.C);
+        p.proj_w = L.add((int64_t)d.C * d.C);
+        p.gate_w = L.add((int64_t)d.Hf * d.C);
+        p.gate_b = L.add(d.Hf);
+        p.ff1_w = L.add((int64_t)d.Hf * d.C);
+        p.ff1_b = L.add(d.Hf);
+        p.ff2_w = L.add((int64_t)d.C * d.Hf);
+        p.ff2_b = L.add(d.C);
+    }
+    int in_dim = d.C;
+    for (int i = 0; i < d.ndec; ++i) {
+        L.dec[i].w = L.add((int64_t)d.dd[i] * in_dim);
+        L.dec[i].ln_w = L.add(d.dd[i]);
+        L.dec[i].ln_b = L.add(d.dd[i]);
+        in_dim = d.dd[i];
+    }
+    L.dec_out_w = L.add((int64_t)3 * in_dim);
+    return L;
+}
+
+// ---------------------------------------------------------------------------
+// Workspace carve-up (all regions 256-byte aligned).
+// ---------------------------------------------------------------------------
+struct Workspace {
+    float *xyz4, *feat0, *content, *cat, *x, *h, *qkv, *colstats, *offs, *ffh, *dec0, *dec1;
+    float *cond, *mod;
+    int32_t* idx;
+    size_t bytes;
+};
+
+Workspace carve(const Dims& d, int B, int M, char* base) {
+    Workspace w{};
+    size_t off = 0;
+    const size_t R = (size_t)B * M;
+    auto take = [&](size_t count) -> char* {
+        char* p = base ? base + off : nullptr;
+        off += (count * 4 + 255) & ~size_t(255);
+        return p;
+    };
+    w.xyz4 = (float*)take(R * 4);
+    w.feat0 = (float*)take(R * d.sd[0]);
+    w.idx = (int32_t*)take(R * d.K);
+    w.content = (float*)take(R * 2 * d.max_cout);
+    w.cat = (float*)take(R * d.sum_stage);
+    w.x = (float*)take(R * d.C);
+    w.h = (float*)take(R * d.C);
+    w.qkv = (float*)take(R * (d.C + 2 * d.qk));
+    w.colstats = (float*)take(R);
+    w.offs = (float*)take(R * d.C);
+    w.ffh = (float*)take(R * d.Hf);
+    w.dec0 = (float*)take(R * (d.max_dec > 0 ? d.max_dec : 1));
+    w.dec1 = (float*)take(R * (d.max_dec > 0 ? d.max_dec : 1));
+    w.cond = (float*)take((size_t)B * d.A);
+    w.mod = (float*)take((size_t)B * (d.NB > 0 ? d.NB : 1) * 6 * d.C);
+    w.bytes = off;
+    return w;
+}
+
+// ---------------------------------------------------------------------------
+// Small kernels: conditioning and the input embedding.
+// ---------------------------------------------------------------------------
+struct CondArgs {
+    const float* P;
+    int64_t w1, b1, w2, b2;
+    int64_t mod_w[kMaxBlocks], mod_b[kMaxBlocks];
+    int A, NB, C;
+};
+
+// AlphaEmbed (network.py:10-26) and every block's AdaLN modulation
+// Linear(SiLU(cond)) (transformer.py:51-54,77-83); one CTA per patch.
+__global__ void cond_mod_kernel(const CondArgs a, const float* __restrict__ alpha,
+                                float* __restrict__ cond, float* __restrict__ mod) {
+    extern __shared__ float sm[];
+    const int A = a.A, A4 = 4 * a.A;
+    float* t = sm;            // [A4]
+    float* sc = sm + A4;      // [A]
+    const int b = blockIdx.x;
+    const float e = 2.0f * alpha[b] - 1.0f;
+    for (int j = threadIdx.x; j < A4; j += blockDim.x)
+        t[j] = f2s_silu(fmaf(a.P[a.w1 + j], e, a.P[a.b1 + j]));
+    __syncthreads();
+    for (int i = threadIdx.x; i < A; i += blockDim.x) {
+        float v = a.P[a.b2 + i];
+        for (int j = 0; j < A4; ++j) v = fmaf(a.P[a.w2 + (int64_t)i * A4 + j], t[j], v);
+        cond[(size_t)b * A + i] = v;
+        sc[i] = f2s_silu(v);
+    }
+    __syncthreads();
+    const int n6 = 6 * a.C;
+    for (int blk = 0; blk < a.NB; ++blk) {
+        for (int n = threadIdx.x; n < n6; n += blockDim.x) {
+            float v = a.P[a.mod_b[blk] + n];
+            const float* w = a.P + a.mod_w[blk] + (int64_t)n * A;
+            for (int j = 0; j < A; ++j) v = fmaf(w[j], sc[j], v);
+            mod[((size_t)b * a.NB + blk) * n6 + n] = v;
+        }
+    }
+}
+
+// xyz (B, 3, M) -> point-major xyz4, and the input HPE (encoder.py:40-71,177):
+// Linear(3 -> S0), Jittor LayerNorm (var = max(E[x^2]-E[x]^2, 0), eps 1e-5),
+// erf GELU, Linear(S0 -> S0). One warp per point.
+__global__ void input_embed_kernel(const float* __restrict__ x, int B, int M,
+                                   const float* __restrict__ w, const float* __restrict__ bia,
+                                   const float* __restrict__ lnw, const float* __restrict__ lnb,
+                                   const float* __restrict__ ow, const float* __restrict__ ob,
+                                   int S0, float* __restrict__ xyz4, float* __restrict__ feat) {
+    extern __shared__ float sm[];
+    float* owT = sm;                         // [S0][S0] transposed (h-major)
+    float* hid = sm + (size_t)S0 * S0;       // [8][S0]
+    for (int i = threadIdx.x; i < S0 * S0; i += blockDim.x) {
+        const int c = i / S0, hh = i - c * S0;
+        owT[hh * S0 + c] = ow[i];
+    }
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int R = B * M;
+    const int p = blockIdx.x * 8 + warp;
+    if (p >= R) return;
+    const int b = p / M, m = p - b * M;
+    const float* xb = x + (size_t)b * 3 * M;
+    const float x0 = xb[m], x1 = xb[M + m], x2 = xb[2 * M + m];
+    if (lane == 0) *reinterpret_cast<float4*>(xyz4 + (size_t)p * 4) = make_float4(x0, x1, x2, 0.0f);
+    float* hw = hid + warp * S0;
+    float s = 0.0f, s2 = 0.0f;
+    for (int c = lane; c < S0; c += 32) {
+        float v = bia[c];
+        v = fmaf(w[c * 3 + 0], x0, v);
+        v = fmaf(w[c * 3 + 1], x1, v);
+        v = fmaf(w[c * 3 + 2], x2, v);
+        hw[c] = v;
+        s += v;
+        s2 = fmaf(v, v, s2);
+    }
+    const float mean = f2s_warp_sum(s) / (float)S0;
+    const float var = fmaxf(f2s_warp_sum(s2) / (float)S0 - mean * mean, 0.0f);
+    const float rstd = rsqrtf(var + 1e-5f);
+    for (int c = lane; c < S0; c += 32)
+        hw[c] = f2s_gelu_erf((hw[c] - mean) * rstd * lnw[c] + lnb[c]);
+    __syncwarp();
+    float* fr = feat + (size_t)p * S0;
+    for (int c = lane; c < S0; c += 32) {
+        float v = ob[c];
+        for (int hh = 0; hh < S0; ++hh) v = fmaf(owT[hh * S0 + c], hw[hh], v);
+        fr[c] = v;
+    }
+}
+
+GemmArgs gemm_args(const float* A, int lda, const float* W, const float* bias, float* Y, int ldy,
+                   int rows, int cols, int K) {
+    GemmArgs g{};
+    g.A = A;
+    g.lda = lda;
+    g.W = W;
+    g.bias = bias;
+    g.Y = Y;
+    g.ldy = ldy;
+    g.rows = rows;
+    g.cols = cols;
+    g.K = K;
+    g.rows_per_patch = 1;
+    g.epilogue = kEpiStore;
+    return g;
+}
+
+int forward(const Dims& d, const Layout& L, const float* P, const float* x_in, const float* alpha,
+            int B, int M, float* velocity, const Workspace& w, cudaStream_t st) {
+    const int R = B * M;
+    const int C = d.C;
+    // conditioning
+    {
+        CondArgs ca{};
+        ca.P = P;
+        ca.w1 = L.alpha_w1;
+        ca.b1 = L.alpha_b1;
+        ca.w2 = L.alpha_w2;
+        ca.b2 = L.alpha_b2;
+        for (int i = 0; i < d.NB; ++i) {
+            ca.mod_w[i] = L.block[i].mod_w;
+            ca.mod_b[i] = L.block[i].mod_b;
+        }
+        ca.A = d.A;
+        ca.NB = d.NB;
+        ca.C = C;
+        cond_mod_kernel<<<B, 256, sizeof(float) * 5 * d.A, st>>>(ca, alpha, w.cond, w.mod);
+        F2S_TRY(check_launch("cond_mod_kernel"));
+    }
+    // input embedding + xyz
+    {
+        const int S0 = d.sd[0];
+        const size_t smem = sizeof(float) * ((size_t)S0 * S0 + 8 * S0);
+        F2S_CUDA_TRY(cudaFuncSetAttribute(input_embed_kernel,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        input_embed_kernel<<<ceil_div(R, 8), 256, smem, st>>>(
+            x_in, B, M, P + L.in_w, P + L.in_b, P + L.in_ln_w, P + L.in_ln_b, P + L.in_out_w,
+            P + L.in_out_b, S0, w.xyz4, w.feat0);
+        F2S_TRY(check_launch("input_embed_kernel"));
+    }
+    F2S_TRY(knn_launch(x_in, B, 3, M, d.K, w.idx, st));
+    // neighbour stages
+    int col = 0;
+    const float* fin = w.feat0;
+    int ldin = d.sd[0];
+    for (int s = 0; s < d.S; ++s) {
+        const StageParams& sp = L.stage[s];
+        const int cin = d.si[s], cout = d.sd[s];
+        F2S_TRY(gemm_f32(gemm_args(fin, ldin, P + sp.content_w, nullptr, w.content, 2 * cout, R,
+                                   2 * cout, cin),
+                         st));
+        EdgeArgs ea{};
+        ea.content = w.content;
+        ea.ldc = 2 * cout;
+        ea.xyz4 = w.xyz4;
+        ea.D = 6;
+        ea.idx = w.idx;
+        ea.B = B;
+        ea.M = M;
+        ea.K = d.K;
+        ea.H = cin;
+        ea.cout = cout;
+        ea.hpe_w = P + sp.hpe_w;
+        ea.hpe_b = P + sp.hpe_b;
+        ea.hpe_ln_w = P + sp.hpe_ln_w;
+        ea.hpe_ln_b = P + sp.hpe_ln_b;
+        ea.contrib_w = P + sp.contrib_w;
+        ea.contrib_b = P + sp.contrib_b;
+        ea.ln_w = P + sp.ln_w;
+        ea.ln_b = P + sp.ln_b;
+        ea.out = w.cat + col;
+        ea.ldo = d.sum_stage;
+        F2S_TRY(edge_stage_f32(ea, st));
+        fin = w.cat + col;
+        ldin = d.sum_stage;
+        col += cout;
+    }
+    // projection head (encoder.py:118-123,184)
+    F2S_TRY(gemm_f32(gemm_args(w.cat, d.sum_stage, P + L.proj_w, nullptr, w.x, C, R, C,
+                               d.sum_stage),
+                     st));
+    F2S_TRY(ln_affine_leaky(w.x, C, P + L.proj_ln_w, P + L.proj_ln_b, R, C, st));
+    // trunk (transformer.py:75-89)
+    const int ld_qkv = C + 2 * d.qk;
+    const int mstride = d.NB * 6 * C;
+    for (int i = 0; i < d.NB; ++i) {
+        const BlockParams& bp = L.block[i];
+        const float* mod = w.mod + (size_t)i * 6 * C;
+        F2S_TRY(ln_modulate(w.x, C, w.h, C, mod, mstride, 0, C, R, M, C, st));
+        F2S_TRY(gemm_f32(gemm_args(w.h, C, P + bp.qkv_w, nullptr, w.qkv, ld_qkv, R, ld_qkv, C),
+                         st));
+        F2S_TRY(qk_norm(w.qkv, ld_qkv, R, d.qk, st));
+        F2S_TRY(attention_f32(w.qkv, w.qkv + d.qk, ld_qkv, w.qkv + 2 * d.qk, ld_qkv, w.h, C,
+                              w.offs, C, w.colstats, B, M, d.qk, C, st));
+        GemmArgs g = gemm_args(w.offs, C, P + bp.proj_w, nullptr, w.x, C, R, C, C);
+        g.epilogue = kEpiGatedResidual;
+        g.gate = mod + 2 * C;
+        g.gate_stride = mstride;
+        g.rows_per_patch = M;
+        F2S_TRY(gemm_f32(g, st));
+        F2S_TRY(ln_modulate(w.x, C, w.h, C, mod, mstride, 3 * C, 4 * C, R, M, C, st));
+        GemmArgs sw = gemm_args(w.h, C, P + bp.gate_w, P + bp.gate_b, w.ffh, d.Hf, R, d.Hf, C);
+        sw.epilogue = kEpiSwiGlu;
+        sw.W2 = P + bp.ff1_w;
+        sw.bias2 = P + bp.ff1_b;
+        F2S_TRY(gemm_f32(sw, st));
+        GemmArgs f2 = gemm_args(w.ffh, d.Hf, P + bp.ff2_w, P + bp.ff2_b, w.x, C, R, C, d.Hf);
+        f2.epilogue = kEpiGatedResidual;
+        f2.gate = mod + 5 * C;
+        f2.gate_stride = mstride;
+        f2.rows_per_patch = M;
+        F2S_TRY(gemm_f32(f2, st));
+    }
+    // decoder (decoder.py:8-32)
+    const float* cur = w.x;
+    int in_dim = C;
+    float* bufs[2] = {w.dec0, w.dec1};
+    for (int i = 0; i < d.ndec; ++i) {
+        float* out = bufs[i & 1];
+        F2S_TRY(gemm_f32(gemm_args(cur, in_dim, P + L.dec[i].w, nullptr, out, d.dd[i], R, d.dd[i],
+                                   in_dim),
+                         st));
+        F2S_TRY(ln_affine_leaky(out, d.dd[i], P + L.dec[i].ln_w, P + L.dec[i].ln_b, R, d.dd[i], st));
+        cur = out;
+        in_dim = d.dd[i];
+    }
+    return gemm_f32(gemm_args(cur, in_dim, P + L.dec_out_w, nullptr, velocity, 3, R, 3, in_dim),
+                    st);
+}
+
+}  // namespace
+}  // namespace f2s
+
+using namespace f2s;
+
+extern "C" int f2s_model_param_segments(const f2s_model_config* cfg, int64_t* offsets,
+                                        int64_t* sizes, int capacity, int64_t* total_floats) {
+    Dims d;
+    F2S_TRY(check_config(cfg, d));
+    const Layout L = make_layout(d);
+    const int n = (int)L.offsets.size();
+    if (offsets && sizes) {
+        F2S_REQUIRE(capacity >= n, "segment arrays hold %d entries, %d needed", capacity, n);
+        for (int i = 0; i < n; ++i) {
+            offsets[i] = L.offsets[i];
+            sizes[i] = L.sizes[i];
+        }
+    }
+    if (total_floats) *total_floats = L.total;
+    return n;
+}
+
+extern "C" int f2s_model_workspace_bytes(const f2s_model_config* cfg, int B, int M,
+                                         size_t* bytes) {
+    Dims d;
+    F2S_TRY(check_config(cfg, d));
+    F2S_REQUIRE(B >= 0 && M >= 0 && bytes != nullptr, "bad workspace query");
+    *bytes = carve(d, B, M, nullptr).bytes;
+    return F2S_OK;
+}
+
+extern "C" int f2s_model_forward(const f2s_model_config* cfg, const float* params,
+                                 const float* x, const float* alpha, int B, int M,
+                                 float* velocity, void* workspace, size_t workspace_bytes,
+                                 void* stream) {
+    Dims d;
+    F2S_TRY(check_config(cfg, d));
+    F2S_REQUIRE(B >= 0 && M >= 0, "bad shape B=%d M=%d", B, M);
+    if (B == 0 || M == 0) return F2S_OK;
+    F2S_LIMIT(M <= F2S_KNN_MAX_POINTS, "patch of %d points exceeds %d", M, F2S_KNN_MAX_POINTS);
+    F2S_LIMIT((int64_t)B * M < (1ll << 31) / 2048, "too many points in one call: B*M=%lld",
+              (long long)B * M);
+    F2S_REQUIRE(params && x && alpha && velocity && workspace, "model forward: null pointer");
+    const Layout L = make_layout(d);
+    const Workspace w = carve(d, B, M, static_cast<char*>(workspace));
+    if (workspace_bytes < w.bytes)
+        return fail(F2S_ERR_WORKSPACE, "model forward needs %zu workspace bytes, got %zu", w.bytes,
+                    workspace_bytes);
+    return forward(d, L, params, x, alpha, B, M, velocity, w, as_stream(stream));
+}
+
+extern "C" int f2s_neighbor_reduce_workspace_bytes(int B, int N, int C, size_t* bytes) {
+    F2S_REQUIRE(B >= 0 && N >= 0 && C >= 0 && bytes, "bad workspace query");
+    *bytes = (size_t)B * N * 3 * C * sizeof(float);
+    return F2S_OK;
+}
+
+extern "C" int f2s_neighbor_reduce(const float* content, const float* geometry,
+                                   const int32_t* indices, const float* hpe_input_weight,
+                                   const float* hpe_input_bias, const float* hpe_output_weight,
+                                   const float* hpe_output_bias, const float* hpe_norm_weight,
+                                   const float* hpe_norm_bias, const float* message_norm_weight,
+                                   const float* message_norm_bias, int B, int N, int K, int D,
+                                   int H, int C, float* out, void* workspace,
+                                   size_t workspace_bytes, void* stream) {
+    F2S_REQUIRE(B >= 0 && N >= 0 && K >= 1 && D >= 1 && H >= 1 && C >= 1,
+                "neighbor_reduce: bad shape B=%d N=%d K=%d D=%d H=%d C=%d", B, N, K, D, H, C);
+    if (B == 0 || N == 0) return F2S_OK;
+    F2S_REQUIRE(content && geometry && indices && hpe_input_weight && hpe_input_bias &&
+                    hpe_output_weight && hpe_output_bias && hpe_norm_weight && hpe_norm_bias &&
+                    message_norm_weight && message_norm_bias && out && workspace,
+                "neighbor_reduce: null pointer");
+    const size_t need = (size_t)B * N * 3 * C * sizeof(float);
+    if (workspace_bytes < need)
+        return fail(F2S_ERR_WORKSPACE, "neighbor_reduce needs %zu workspace bytes, got %zu", need,
+                    workspace_bytes);
+    cudaStream_t st = as_stream(stream);
+    float* content_pm = static_cast<float*>(workspace);       // (B*N, 2C)
+    float* out_pm = content_pm + (size_t)B * N * 2 * C;         // (B*N, C)
+    F2S_TRY(transpose_batched(content, content_pm, B, 2 * C, N, st));
+    EdgeArgs ea{};
+    ea.content = content_pm;
+    ea.ldc = 2 * C;
+    ea.geometry = geometry;
+    ea.D = D;
+    ea.idx = indices;
+    ea.B = B;
+    ea.M = N;
+    ea.K = K;
+    ea.H = H;
+    ea.cout = C;
+    ea.hpe_w = hpe_input_weight;
+    ea.hpe_b = hpe_input_bias;
+    ea.hpe_ln_w = hpe_norm_weight;
+    ea.hpe_ln_b = hpe_norm_bias;
+    ea.contrib_w = hpe_output_weight;
+    ea.contrib_b = hpe_output_bias;
+    ea.ln_w = message_norm_weight;
+    ea.ln_b = message_norm_bias;
+    ea.out = out_pm;
+    ea.ldo = C;
+    F2S_TRY(edge_stage_f32(ea, st));
+    return transpose_batched(out_pm, out, B, N, C, st);
+}
+
+extern "C" int f2s_offset_attention_workspace_bytes(int B, int N, int d, size_t* bytes) {
+    F2S_REQUIRE(B >= 0 && N >= 0 && d >= 0 && bytes, "bad workspace query");
+    *bytes = (size_t)B * N * (d + 1) * sizeof(float);
+    return F2S_OK;
+}
+
+extern "C" int f2s_offset_attention(const float* query, const float* key, const float* value,
+                                    int B, int N, int d, int C, float* out, void* workspace,
+                                    size_t workspace_bytes, void* stream) {
+    F2S_REQUIRE(B >= 0 && N >= 0 && d >= 1 && C >= 1,
+                "offset_attention: bad shape B=%d N=%d d=%d C=%d", B, N, d, C);
+    if (B == 0 || N == 0) return F2S_OK;
+    F2S_REQUIRE(query && key && value && out && workspace, "offset_attention: null pointer");
+    const size_t need = (size_t)B * N * (d + 1) * sizeof(float);
+    if (workspace_bytes < need)
+        return fail(F2S_ERR_WORKSPACE, "offset_attention needs %zu workspace bytes, got %zu",
+                    need, workspace_bytes);
+    cudaStream_t st = as_stream(stream);
+    float* key_pm = static_cast<float*>(workspace);           // (B*N, d)
+    float* colstats = key_pm + (size_t)B * N * d;             // (B*N)
+    F2S_TRY(transpose_batched(key, key_pm, B, d, N, st));
+    return attention_f32(query, key_pm, d, value, C, nullptr, 0, out, C, colstats, B, N, d, C,
+                         st);
+}

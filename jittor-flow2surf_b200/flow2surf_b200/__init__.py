@@ -5,6 +5,13 @@ the Flow2SurfNet model and patch_denoise, all computed by hand-written CUDA
 kernels in libflow2surf_sm100.so behind a C-ABI (include/flow2surf_b200.h).
 """
 
-from .ops import knn_indices
+from .network import Flow2SurfNet, build_model
+from .ops import knn_indices, offset_attention_aggregate, reduce_neighbor_messages
 
-__all__ = ["knn_indices"]
+__all__ = [
+    "Flow2SurfNet",
+    "build_model",
+    "knn_indices",
+    "offset_attention_aggregate",
+    "reduce_neighbor_messages",
+]

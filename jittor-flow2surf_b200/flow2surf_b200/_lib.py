@@ -31,6 +31,13 @@ SIGNATURES: dict[str, list] = {
     "f2s_last_error": [],
     "f2s_version": [],
     "f2s_knn": [_p, _i, _i, _i, _i, _p, _p],
+    "f2s_offset_attention_workspace_bytes": [_i, _i, _i, _p],
+    "f2s_offset_attention": [_p, _p, _p, _i, _i, _i, _i, _p, _p, _sz, _p],
+    "f2s_neighbor_reduce_workspace_bytes": [_i, _i, _i, _p],
+    "f2s_neighbor_reduce": [_p] * 11 + [_i] * 6 + [_p, _p, _sz, _p],
+    "f2s_model_param_segments": [_p, _p, _p, _i, _p],
+    "f2s_model_workspace_bytes": [_p, _i, _i, _p],
+    "f2s_model_forward": [_p, _p, _p, _p, _i, _i, _p, _p, _sz, _p],
 }
 
 _RESTYPES = {"f2s_last_error": ctypes.c_char_p}

@@ -8,6 +8,8 @@ CPU path -- a CPU tensor or a missing library raises.
 
 from __future__ import annotations
 
+import ctypes
+
 import torch
 
 from . import _lib
@@ -46,5 +48,89 @@ def knn_indices(features: torch.Tensor, k: int) -> torch.Tensor:
         return out
     features = _f32(features)
     _lib.call("f2s_knn", _lib.ptr(features), batch, channels, points, k, _lib.ptr(out),
+              _lib.stream_handle())
+    return out
+
+
+def _workspace(query: str, *dims) -> torch.Tensor:
+    size = ctypes.c_size_t()
+    _lib.check(getattr(_lib.lib(), query)(*dims, ctypes.byref(size)))
+    return torch.empty(size.value, dtype=torch.uint8, device="cuda")
+
+
+def offset_attention_aggregate(query: torch.Tensor, key: torch.Tensor,
+                               value: torch.Tensor) -> torch.Tensor:
+    """Aggregate values using normalized offset-attention weights.
+
+    query (B, N, d), key (B, d, N), value (B, N, C) -> (B, N, C): softmax of
+    query . key over the query axis, each row divided by its sum over keys
+    plus 1e-9, times value (flow2surf/models/ops/attention.py:15-19,84-106).
+    """
+    if query.dim() != 3 or key.dim() != 3 or value.dim() != 3:
+        raise ValueError("query, key, and value must be rank-3 tensors")
+    if (query.shape[0] != key.shape[0] or query.shape[0] != value.shape[0]
+            or query.shape[1] != key.shape[2] or query.shape[1] != value.shape[1]
+            or query.shape[2] != key.shape[1]):
+        raise ValueError(f"Incompatible attention shapes: {tuple(query.shape)}, "
+                         f"{tuple(key.shape)}, {tuple(value.shape)}")
+    _require_cuda(query, key, value)
+    batch, points, width = query.shape
+    channels = value.shape[2]
+    out = torch.empty((batch, points, channels), dtype=torch.float32, device=query.device)
+    if out.numel() == 0:
+        return out
+    query, key, value = _f32(query), _f32(key), _f32(value)
+    ws = _workspace("f2s_offset_attention_workspace_bytes", batch, points, width)
+    _lib.call("f2s_offset_attention", _lib.ptr(query), _lib.ptr(key), _lib.ptr(value), batch,
+              points, width, channels, _lib.ptr(out), _lib.ptr(ws), ws.numel(),
+              _lib.stream_handle())
+    return out
+
+
+def reduce_neighbor_messages(content, geometry, indices, hpe_input_weight, hpe_input_bias,
+                             hpe_output_weight, hpe_output_bias, hpe_norm_weight, hpe_norm_bias,
+                             message_norm_weight, message_norm_bias) -> torch.Tensor:
+    """Encode relative geometry and max-reduce normalized neighbor messages.
+
+    content  : (B, 2C, N), projected neighbor and center terms
+    geometry : (B, N, K, D), compact relative coordinates
+    indices  : (B, N, K)
+    output   : (B, C, N)
+
+    flow2surf/models/ops/neighbor_reduce.py:244-337, with the HPE hidden
+    layer, its output projection and the reduce fused in one kernel.
+    """
+    channels, hidden_channels = hpe_output_weight.shape
+    input_hidden_channels, input_channels = hpe_input_weight.shape
+    if content.shape[1] != 2 * channels:
+        raise ValueError(f"Expected {2 * channels} content channels, got {content.shape[1]}")
+    if input_hidden_channels != hidden_channels:
+        raise ValueError("HPE projections disagree on hidden width: "
+                         f"{input_hidden_channels} != {hidden_channels}")
+    if geometry.shape[-1] != input_channels:
+        raise ValueError(f"Expected {input_channels} geometry channels, got {geometry.shape[-1]}")
+    if tuple(geometry.shape[:3]) != tuple(indices.shape):
+        raise ValueError(f"Geometry shape {tuple(geometry.shape[:3])} does not match indices "
+                         f"{tuple(indices.shape)}")
+    if content.shape[0] != indices.shape[0] or content.shape[2] != indices.shape[1]:
+        raise ValueError(f"Content shape {tuple(content.shape)} does not match indices "
+                         f"{tuple(indices.shape)}")
+    tensors = (content, geometry, indices, hpe_input_weight, hpe_input_bias, hpe_output_weight,
+               hpe_output_bias, hpe_norm_weight, hpe_norm_bias, message_norm_weight,
+               message_norm_bias)
+    _require_cuda(*tensors)
+    batch, points, neighbors = indices.shape
+    out = torch.empty((batch, channels, points), dtype=torch.float32, device=content.device)
+    if out.numel() == 0:
+        return out
+    if indices.dtype != torch.int32:
+        raise ValueError(f"indices must be int32, got {indices.dtype}")
+    floats = [_f32(t) for t in tensors[:2]] + [_f32(t) for t in tensors[3:]]
+    indices = indices.contiguous()
+    ws = _workspace("f2s_neighbor_reduce_workspace_bytes", batch, points, channels)
+    args = [_lib.ptr(floats[0]), _lib.ptr(floats[1]), _lib.ptr(indices)]
+    args += [_lib.ptr(t) for t in floats[2:]]
+    _lib.call("f2s_neighbor_reduce", *args, batch, points, neighbors, input_channels,
+              hidden_channels, channels, _lib.ptr(out), _lib.ptr(ws), ws.numel(),
               _lib.stream_handle())
     return out

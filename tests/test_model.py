@@ -1,0 +1,115 @@
+"""Flow2SurfNet forward on the GPU against the oracle (flow2surf/models/*).
+
+Velocity tolerance: max-abs 1e-4 for the fp32 path.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from flow2surf_b200 import Flow2SurfNet, build_model
+from flow2surf_b200.synthetic import DEFAULT_CONFIG, random_parameters, sphere_cloud
+from oracle.model import OracleNet
+
+TINY_CONFIG = {
+    "k_neighbors": 8, "feat_dim": 32, "encoder_dims": [16, 24], "num_blocks": 2,
+    "alpha_dim": 8, "ffn_ratio": 2, "decoder_dims": [16, 8],
+}
+VELOCITY_ATOL = 1e-4
+
+
+def patches_from_cloud(cloud, count, size, seed):
+    rng = np.random.default_rng(seed)
+    centers = cloud[rng.choice(len(cloud), count, replace=False)]
+    out = []
+    for c in centers:
+        order = np.argsort(((cloud - c) ** 2).sum(1), kind="stable")[:size]
+        out.append((cloud[order] - c).T)
+    return np.ascontiguousarray(np.stack(out), dtype=np.float32)
+
+
+def gpu_forward(cfg, params, x, alpha):
+    model = build_model(cfg)
+    model.load_parameters(params)
+    v = model(torch.from_numpy(x).cuda(), torch.from_numpy(alpha).cuda())
+    return v.cpu().numpy()
+
+
+@pytest.mark.gpu
+def test_tiny_model_matches_reference_golden(cuda, golden):
+    fix = golden("model")
+    params = {k[len("param/"):]: v for k, v in fix.items() if k.startswith("param/")}
+    v = gpu_forward(TINY_CONFIG, params, fix["x"], fix["alpha"])
+    np.testing.assert_allclose(v, fix["velocity_f64"], rtol=0, atol=VELOCITY_ATOL)
+    ora = OracleNet(TINY_CONFIG, params)(fix["x"], fix["alpha"])
+    np.testing.assert_allclose(v, ora, rtol=0, atol=1e-5)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("k,points", [(32, 1024), (16, 1000)])
+def test_default_model_matches_oracle(cuda, k, points):
+    cfg = dict(DEFAULT_CONFIG, k_neighbors=k)
+    params = random_parameters(cfg, seed=0)
+    cloud = sphere_cloud(20000, seed=3)[0]
+    x = patches_from_cloud(cloud, 3, points, seed=k)
+    alpha = np.array([0.5, 0.791531, 0.997947], dtype=np.float32)
+    v = gpu_forward(cfg, params, x, alpha)
+    ref, inter = OracleNet(cfg, params)(x, alpha, return_intermediates=True)
+    err = np.abs(v - ref).max()
+    assert err < VELOCITY_ATOL, f"max abs velocity error {err}"
+    assert np.abs(ref).max() > 1e-2  # the comparison is not vacuous
+
+
+@pytest.mark.gpu
+def test_default_model_reference_golden(cuda, golden):
+    fix = golden("model_default")
+    params = random_parameters(DEFAULT_CONFIG, seed=int(fix["params_seed"]))
+    v = gpu_forward(DEFAULT_CONFIG, params, fix["x"], fix["alpha"])
+    np.testing.assert_allclose(v, fix["velocity_f64"], rtol=0, atol=VELOCITY_ATOL)
+
+
+@pytest.mark.gpu
+def test_fresh_model_predicts_zero_velocity(cuda):
+    """As constructed, the reference's model is a zero-velocity identity flow
+    (decoder.py:23-27)."""
+    model = build_model(DEFAULT_CONFIG)
+    x = torch.randn(2, 3, 256, device="cuda") * 0.1
+    v = model(x, torch.tensor([0.3, 0.7], device="cuda"))
+    assert v.shape == (2, 256, 3)
+    assert torch.count_nonzero(v).item() == 0
+
+
+@pytest.mark.gpu
+def test_batch_independence(cuda):
+    """Patches are independent: a batch gives the same bits as one at a time."""
+    params = random_parameters(TINY_CONFIG, seed=9)
+    rng = np.random.default_rng(1)
+    x = (0.2 * rng.normal(size=(5, 3, 100))).astype(np.float32)
+    alpha = rng.uniform(size=5).astype(np.float32)
+    full = gpu_forward(TINY_CONFIG, params, x, alpha)
+    for b in range(5):
+        one = gpu_forward(TINY_CONFIG, params, x[b:b + 1], alpha[b:b + 1])
+        np.testing.assert_array_equal(one[0], full[b])
+
+
+def test_constructor_validation_matches_reference():
+    with pytest.raises(ValueError, match="num_blocks"):
+        Flow2SurfNet(num_blocks=-1)
+    with pytest.raises(ValueError, match="ffn_ratio"):
+        Flow2SurfNet(ffn_ratio=0)
+    with pytest.raises(ValueError, match="alpha_dim"):
+        Flow2SurfNet(alpha_dim=0)
+
+
+def test_state_dict_round_trip():
+    model = build_model(DEFAULT_CONFIG)
+    params = random_parameters(DEFAULT_CONFIG, seed=4)
+    model.load_parameters(params)
+    sd = model.state_dict()
+    assert set(sd) == set(params)
+    for k in params:
+        np.testing.assert_array_equal(sd[k], params[k])
+    bad = dict(params)
+    bad.pop("blocks.0.proj.weight")
+    with pytest.raises(KeyError):
+        model.load_parameters(bad)
