@@ -154,6 +154,92 @@ int f2s_model_forward(const f2s_model_config* cfg, const float* params, const fl
                       const float* alpha, int B, int M, float* velocity,
                       void* workspace, size_t workspace_bytes, void* stream);
 
+/* ------------------------------------------------------------------------ */
+/* Patch-wise reverse flow (flow2surf/inference.py:19-198)                  */
+/* ------------------------------------------------------------------------ */
+
+/*
+ * Farthest-point sampling, bit-exact to _farthest_point_indices
+ * (inference.py:19-41) given its first index (the reference's
+ * rng.integers(N), drawn by the caller).
+ *   points (N, 3) float32 -> selected (count,) int32.
+ *   workspace: f2s_fps_workspace_bytes() bytes (used only when one CTA's
+ *   share of the cloud does not fit in shared memory, N > ~114k).
+ */
+int f2s_fps_workspace_bytes(int64_t N, size_t* bytes);
+int f2s_fps(const float* points, int64_t N, int64_t count, int64_t first, int32_t* selected,
+            void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Patch index and vote weights (build_patch_index + build_aggregation,
+ * inference.py:110-134): for each seed the k = patch_size nearest points by
+ * float64 squared distance, ascending (ties by index);
+ * radial = d / (d_max + 1e-8); weights = exp(-beta * radial^2).
+ *   seeds (P,) int32 -> neighbors (P, k) int32, radial (P, k) float64,
+ *   weights (P, k) float64.   Limit: k <= F2S_KNN_MAX_POINTS.
+ */
+int f2s_patch_index(const float* points, int64_t N, const int32_t* seeds, int P, int k,
+                    double beta, int32_t* neighbors, double* radial, double* weights,
+                    void* stream);
+
+/*
+ * Fusion structure (the grouping np.bincount performs, inference.py:128-132):
+ * offsets (N + 1,) int32, entries (P * k,) int32 -- for every point, the flat
+ * (patch * k + slot) positions voting for it in increasing order -- and
+ * weight_sum (N,) float64 summed in that order.
+ *   workspace: f2s_fusion_workspace_bytes() bytes.
+ */
+int f2s_fusion_workspace_bytes(int64_t N, size_t* bytes);
+int f2s_fusion_build(const int32_t* neighbors, const double* weights, int P, int k, int64_t N,
+                     int32_t* offsets, int32_t* entries, double* weight_sum,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Model input of every patch (inference.py:142-150):
+ * x[p, c, m] = points[neighbors[p, m], c] - points[seeds[p], c], x (P, 3, k).
+ */
+int f2s_gather_patches(const float* points, const int32_t* neighbors, const int32_t* seeds,
+                       int P, int k, float* x, void* stream);
+
+/*
+ * Centre-weighted fusion of the patch votes (P * k, 3) and the Euler update
+ * (aggregate_votes + update, inference.py:158-171,193-195):
+ * v = (float)(sum_f w_f vote_f / (weight_sum + 1e-8)) in float64 in entry
+ * order; out = points - alpha_step * v (float32, two roundings); points with
+ * weight_sum == 0 are copied. `velocity` (N, 3) may be NULL.
+ */
+int f2s_fuse_euler(const float* points, const float* votes, const int32_t* offsets,
+                   const int32_t* entries, const double* weights, const double* weight_sum,
+                   int64_t N, float alpha_step, float* out, float* velocity, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Nearest distances and Chamfer                                            */
+/* ------------------------------------------------------------------------ */
+
+/*
+ * Bidirectional nearest squared distances, bit-exact to the reference kernels
+ * nearest_first / nearest_second (flow2surf/training/cuda/nearest_distance_forward.cu:1-93)
+ * behind nearest_squared_distances (flow2surf/training/distances.py:70-87).
+ *   first (B, M, 3), second (B, N, 3) float32 ->
+ *   first_distance (B, M), second_index (B, M) int32,
+ *   second_distance (B, N), first_index (B, N) int32.
+ *   workspace: f2s_nearest_workspace_bytes() bytes (one 64-bit key per point).
+ */
+int f2s_nearest_workspace_bytes(int B, int M, int N, size_t* bytes);
+int f2s_nearest(const float* first, const float* second, int B, int M, int N,
+                float* first_distance, int32_t* second_index, float* second_distance,
+                int32_t* first_index, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Chamfer distance per batch item: mean of the float32 nearest squared
+ * distances pred -> target plus target -> pred, accumulated in float64
+ * (chamfer_distance, flow2surf/evaluation.py:24-28, with the kernel's
+ * distances). pred (B, M, 3), target (B, N, 3) -> chamfer (B,) float64.
+ *   workspace: f2s_nearest_workspace_bytes(B, M, N) bytes.
+ */
+int f2s_chamfer(const float* pred, const float* target, int B, int M, int N, double* chamfer,
+                void* workspace, size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,209 @@
+// Bidirectional nearest squared distances and the Chamfer distance.
+//
+// Reference semantics (flow2surf/training/cuda/nearest_distance_forward.cu:1-93):
+// for each query point, scan the other set in index order keeping the smallest
+// d = dx*dx + dy*dy + dz*dz (nvcc contracts it to fma(dz, dz, fma(dx, dx,
+// dy*dy)), dx = query - reference), starting from (FLT_MAX, index = N) and
+// replacing only on a strictly smaller distance (ties keep the lower index).
+// Chamfer: mean d(p -> q) + mean d(q -> p) (flow2surf/evaluation.py:24-28).
+//
+// B200 design: each thread keeps 4 queries in registers, the reference set
+// streams through shared memory as float4 tiles, and the reference set is split
+// across CTAs when the query count alone cannot fill 148 SMs. Each split's
+// (distance, index) winner is folded into a 64-bit key
+// (order-preserving distance bits << 32 | index) with atomicMin, which is
+// exactly the lexicographic rule above, so the split changes no result.
+#include <cfloat>
+
+#include "kernels.cuh"
+
+namespace f2s {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kQpt = 4;
+constexpr int kQueriesPerCta = kThreads * kQpt;
+constexpr int kTile = 1024;
+
+__device__ __forceinline__ unsigned long long dist_key(float d, int j) {
+    return ((unsigned long long)f2s_ordered_bits(d) << 32) | (unsigned)j;
+}
+
+__global__ void init_keys_kernel(unsigned long long* keys, int64_t count, int reference_count) {
+    const unsigned long long k0 = dist_key(FLT_MAX, reference_count);
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < count;
+         i += (int64_t)gridDim.x * blockDim.x)
+        keys[i] = k0;
+}
+
+__global__ void __launch_bounds__(kThreads)
+nearest_kernel(const float* __restrict__ query, const float* __restrict__ ref, int M, int N,
+               int ref_chunk, unsigned long long* __restrict__ keys) {
+    __shared__ float4 tile[kTile];
+    const int b = blockIdx.z;
+    const int q0 = blockIdx.x * kQueriesPerCta;
+    const int j_lo = blockIdx.y * ref_chunk;
+    const int j_hi = min(N, j_lo + ref_chunk);
+    const float* qb = query + (size_t)b * M * 3;
+    const float* rb = ref + (size_t)b * N * 3;
+    float qx[kQpt], qy[kQpt], qz[kQpt], best[kQpt];
+    int bj[kQpt];
+#pragma unroll
+    for (int t = 0; t < kQpt; ++t) {
+        const int i = q0 + threadIdx.x + kThreads * t;
+        const bool in = i < M;
+        qx[t] = in ? qb[3 * i] : 0.0f;
+        qy[t] = in ? qb[3 * i + 1] : 0.0f;
+        qz[t] = in ? qb[3 * i + 2] : 0.0f;
+        best[t] = INFINITY;
+        bj[t] = -1;
+    }
+    for (int t0 = j_lo; t0 < j_hi; t0 += kTile) {
+        const int count = min(kTile, j_hi - t0);
+        __syncthreads();
+        for (int j = threadIdx.x; j < count; j += kThreads) {
+            const float* p = rb + 3 * (size_t)(t0 + j);
+            tile[j] = make_float4(p[0], p[1], p[2], 0.0f);
+        }
+        __syncthreads();
+        for (int j = 0; j < count; ++j) {
+            const float4 r = tile[j];
+#pragma unroll
+            for (int t = 0; t < kQpt; ++t) {
+                const float dx = __fsub_rn(qx[t], r.x);
+                const float dy = __fsub_rn(qy[t], r.y);
+                const float dz = __fsub_rn(qz[t], r.z);
+                const float d = __fmaf_rn(dz, dz, __fmaf_rn(dx, dx, __fmul_rn(dy, dy)));
+                if (d < best[t]) {
+                    best[t] = d;
+                    bj[t] = t0 + j;
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < kQpt; ++t) {
+        const int i = q0 + threadIdx.x + kThreads * t;
+        if (i < M && bj[t] >= 0) atomicMin(&keys[(size_t)b * M + i], dist_key(best[t], bj[t]));
+    }
+}
+
+__global__ void unpack_kernel(const unsigned long long* __restrict__ keys, int64_t count,
+                              float* __restrict__ dist, int32_t* __restrict__ index) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < count;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const unsigned long long k = keys[i];
+        dist[i] = __uint_as_float((unsigned)(k >> 32) ^ 0x80000000u);
+        index[i] = (int32_t)(unsigned)(k & 0xffffffffu);
+    }
+}
+
+// chamfer[b] = mean_i d1[b, i] + mean_j d2[b, j], float64, fixed reduction order.
+__global__ void __launch_bounds__(1024)
+chamfer_reduce_kernel(const unsigned long long* __restrict__ k1, int M,
+                      const unsigned long long* __restrict__ k2, int N, double* __restrict__ out) {
+    __shared__ double red[32];
+    const int b = blockIdx.x;
+    double s1 = 0.0, s2 = 0.0;
+    for (int i = threadIdx.x; i < M; i += 1024)
+        s1 += (double)__uint_as_float((unsigned)(k1[(size_t)b * M + i] >> 32) ^ 0x80000000u);
+    for (int j = threadIdx.x; j < N; j += 1024)
+        s2 += (double)__uint_as_float((unsigned)(k2[(size_t)b * N + j] >> 32) ^ 0x80000000u);
+    double v = s1 / (double)M + s2 / (double)N;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        v = red[threadIdx.x];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (threadIdx.x == 0) out[b] = v;
+    }
+}
+
+int grid_1d(int64_t work) {
+    const int64_t blocks = (work + 255) / 256;
+    const int64_t cap = (int64_t)sm_count() * 16;
+    return (int)(blocks < 1 ? 1 : (blocks < cap ? blocks : cap));
+}
+
+// keys[b, i] = min over j of dist_key(d(query_i, ref_j), j), starting at (FLT_MAX, N).
+int one_way(const float* query, const float* ref, int B, int M, int N, unsigned long long* keys,
+            cudaStream_t st) {
+    const int64_t count = (int64_t)B * M;
+    init_keys_kernel<<<grid_1d(count), 256, 0, st>>>(keys, count, N);
+    F2S_TRY(check_launch("init_keys_kernel"));
+    const int qblocks = ceil_div(M, kQueriesPerCta);
+    const int64_t base = (int64_t)qblocks * B;
+    int splits = (int)((4ll * sm_count() + base - 1) / base);
+    const int max_splits = ceil_div(N, kTile);
+    splits = splits < 1 ? 1 : (splits > max_splits ? max_splits : splits);
+    const int ref_chunk = ceil_div(ceil_div(N, splits), kTile) * kTile;
+    dim3 grid(qblocks, ceil_div(N, ref_chunk), B);
+    F2S_LIMIT(grid.y <= 65535 && grid.z <= 65535, "nearest: grid too large");
+    nearest_kernel<<<grid, kThreads, 0, st>>>(query, ref, M, N, ref_chunk, keys);
+    return check_launch("nearest_kernel");
+}
+
+int check_sets(const float* first, const float* second, int B, int M, int N) {
+    F2S_REQUIRE(B >= 0, "batch must be >= 0");
+    F2S_REQUIRE(M >= 1 && N >= 1, "Point sets must be nonempty");
+    F2S_REQUIRE(first && second, "nearest: null pointer");
+    return F2S_OK;
+}
+
+}  // namespace
+}  // namespace f2s
+
+using namespace f2s;
+
+extern "C" int f2s_nearest_workspace_bytes(int B, int M, int N, size_t* bytes) {
+    F2S_REQUIRE(B >= 0 && M >= 0 && N >= 0 && bytes, "bad workspace query");
+    *bytes = (size_t)B * ((size_t)M + N) * sizeof(unsigned long long);
+    return F2S_OK;
+}
+
+extern "C" int f2s_nearest(const float* first, const float* second, int B, int M, int N,
+                           float* first_distance, int32_t* second_index, float* second_distance,
+                           int32_t* first_index, void* workspace, size_t workspace_bytes,
+                           void* stream) {
+    F2S_TRY(check_sets(first, second, B, M, N));
+    if (B == 0) return F2S_OK;
+    F2S_REQUIRE(first_distance && second_index && second_distance && first_index && workspace,
+                "nearest: null pointer");
+    const size_t need = (size_t)B * ((size_t)M + N) * sizeof(unsigned long long);
+    if (workspace_bytes < need)
+        return fail(F2S_ERR_WORKSPACE, "nearest needs %zu workspace bytes, got %zu", need,
+                    workspace_bytes);
+    cudaStream_t st = as_stream(stream);
+    unsigned long long* k1 = static_cast<unsigned long long*>(workspace);
+    unsigned long long* k2 = k1 + (size_t)B * M;
+    F2S_TRY(one_way(first, second, B, M, N, k1, st));
+    F2S_TRY(one_way(second, first, B, N, M, k2, st));
+    unpack_kernel<<<grid_1d((int64_t)B * M), 256, 0, st>>>(k1, (int64_t)B * M, first_distance,
+                                                           second_index);
+    F2S_TRY(check_launch("unpack_kernel"));
+    unpack_kernel<<<grid_1d((int64_t)B * N), 256, 0, st>>>(k2, (int64_t)B * N, second_distance,
+                                                           first_index);
+    return check_launch("unpack_kernel");
+}
+
+extern "C" int f2s_chamfer(const float* pred, const float* target, int B, int M, int N,
+                           double* chamfer, void* workspace, size_t workspace_bytes,
+                           void* stream) {
+    F2S_TRY(check_sets(pred, target, B, M, N));
+    if (B == 0) return F2S_OK;
+    F2S_REQUIRE(chamfer && workspace, "chamfer: null pointer");
+    const size_t need = (size_t)B * ((size_t)M + N) * sizeof(unsigned long long);
+    if (workspace_bytes < need)
+        return fail(F2S_ERR_WORKSPACE, "chamfer needs %zu workspace bytes, got %zu", need,
+                    workspace_bytes);
+    cudaStream_t st = as_stream(stream);
+    unsigned long long* k1 = static_cast<unsigned long long*>(workspace);
+    unsigned long long* k2 = k1 + (size_t)B * M;
+    F2S_TRY(one_way(pred, target, B, M, N, k1, st));
+    F2S_TRY(one_way(target, pred, B, N, M, k2, st));
+    chamfer_reduce_kernel<<<B, 1024, 0, st>>>(k1, M, k2, N, chamfer);
+    return check_launch("chamfer_reduce_kernel");
+}

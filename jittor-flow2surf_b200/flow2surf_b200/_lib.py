@@ -38,6 +38,16 @@ SIGNATURES: dict[str, list] = {
     "f2s_model_param_segments": [_p, _p, _p, _i, _p],
     "f2s_model_workspace_bytes": [_p, _i, _i, _p],
     "f2s_model_forward": [_p, _p, _p, _p, _i, _i, _p, _p, _sz, _p],
+    "f2s_fps_workspace_bytes": [_i64, _p],
+    "f2s_fps": [_p, _i64, _i64, _i64, _p, _p, _sz, _p],
+    "f2s_patch_index": [_p, _i64, _p, _i, _i, _d, _p, _p, _p, _p],
+    "f2s_fusion_workspace_bytes": [_i64, _p],
+    "f2s_fusion_build": [_p, _p, _i, _i, _i64, _p, _p, _p, _p, _sz, _p],
+    "f2s_gather_patches": [_p, _p, _p, _i, _i, _p, _p],
+    "f2s_fuse_euler": [_p, _p, _p, _p, _p, _p, _i64, _f, _p, _p, _p],
+    "f2s_nearest_workspace_bytes": [_i, _i, _i, _p],
+    "f2s_nearest": [_p, _p, _i, _i, _i, _p, _p, _p, _p, _p, _sz, _p],
+    "f2s_chamfer": [_p, _p, _i, _i, _i, _p, _p, _sz, _p],
 }
 
 _RESTYPES = {"f2s_last_error": ctypes.c_char_p}

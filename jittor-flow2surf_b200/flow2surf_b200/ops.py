@@ -134,3 +134,61 @@ def reduce_neighbor_messages(content, geometry, indices, hpe_input_weight, hpe_i
               hidden_channels, channels, _lib.ptr(out), _lib.ptr(ws), ws.numel(),
               _lib.stream_handle())
     return out
+
+
+def nearest_squared_distances(first: torch.Tensor, second: torch.Tensor):
+    """Return distances and indices from each 3D point set to the other.
+
+    Inputs are (B, M, 3) and (B, N, 3). Outputs are first distances and second
+    indices shaped (B, M), then second distances and first indices shaped
+    (B, N) (flow2surf/training/distances.py:70-87; CUDA semantics, ties to the
+    lower index).
+    """
+    if first.dim() != 3 or first.shape[2] != 3:
+        raise ValueError(f"Expected first shaped (B, M, 3), got {tuple(first.shape)}")
+    if second.dim() != 3 or second.shape[2] != 3:
+        raise ValueError(f"Expected second shaped (B, N, 3), got {tuple(second.shape)}")
+    if first.shape[0] != second.shape[0]:
+        raise ValueError(f"Batch sizes differ: {first.shape[0]} and {second.shape[0]}")
+    if first.shape[1] < 1 or second.shape[1] < 1:
+        raise ValueError("Point sets must be nonempty")
+    if first.dtype != second.dtype:
+        raise ValueError(f"Dtypes differ: {first.dtype} and {second.dtype}")
+    _require_cuda(first, second)
+    first, second = _f32(first), _f32(second)
+    B, M, _ = first.shape
+    N = second.shape[1]
+    dev = first.device
+    d1 = torch.empty((B, M), dtype=torch.float32, device=dev)
+    i2 = torch.empty((B, M), dtype=torch.int32, device=dev)
+    d2 = torch.empty((B, N), dtype=torch.float32, device=dev)
+    i1 = torch.empty((B, N), dtype=torch.int32, device=dev)
+    if B == 0:
+        return d1, i2, d2, i1
+    ws = _workspace("f2s_nearest_workspace_bytes", B, M, N)
+    _lib.call("f2s_nearest", _lib.ptr(first), _lib.ptr(second), B, M, N, _lib.ptr(d1),
+              _lib.ptr(i2), _lib.ptr(d2), _lib.ptr(i1), _lib.ptr(ws), ws.numel(),
+              _lib.stream_handle())
+    return d1, i2, d2, i1
+
+
+def chamfer_distances(pred: torch.Tensor, target: torch.Tensor) -> torch.Tensor:
+    """Per-item Chamfer distance (B,) float64 of (B, M, 3) and (B, N, 3) clouds:
+    mean squared nearest distance both ways (flow2surf/evaluation.py:24-28)."""
+    if pred.dim() != 3 or target.dim() != 3 or pred.shape[2] != 3 or target.shape[2] != 3:
+        raise ValueError("pred and target must be (B, M, 3) and (B, N, 3)")
+    if pred.shape[0] != target.shape[0]:
+        raise ValueError(f"Batch sizes differ: {pred.shape[0]} and {target.shape[0]}")
+    if pred.shape[1] < 1 or target.shape[1] < 1:
+        raise ValueError("Point sets must be nonempty")
+    _require_cuda(pred, target)
+    pred, target = _f32(pred), _f32(target)
+    B, M, _ = pred.shape
+    N = target.shape[1]
+    out = torch.empty(B, dtype=torch.float64, device=pred.device)
+    if B == 0:
+        return out
+    ws = _workspace("f2s_nearest_workspace_bytes", B, M, N)
+    _lib.call("f2s_chamfer", _lib.ptr(pred), _lib.ptr(target), B, M, N, _lib.ptr(out),
+              _lib.ptr(ws), ws.numel(), _lib.stream_handle())
+    return out
