@@ -1,0 +1,405 @@
+#!/usr/bin/env python
+"""Denoised points/s of the full reverse flow on B200.
+
+Workload (per GPU, weak scaling: each rank denoises its own cloud): a
+50,000-point synthetic cloud sampled area-uniform on a random union of 4
+ellipsoids and 2 boxes, normalised to the unit sphere, with rotation-invariant
+Laplace noise (sigma = 0.015 x bbox diagonal); 1,000-point patches at
+farthest-point seeds with ~3x overlap (seed_k = 3 -> 150 patches), the default
+configuration's architecture (K = 32, feat 192, 3 trunk blocks) with random
+weights (seed 0), the default schedule (3 Euler steps, alpha powers 1 / 6),
+centre-weighted fusion (beta = 5). One step = one full patch_denoise of the
+cloud: FPS seeds, patch index, fusion structure, 3 x (gather, model forward
+over all patches, fusion + Euler).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+`value` is timed on the device with CUDA events (cloud resident in HBM, L2
+flushed between steps); `e2e` is the same metric through the public
+patch_denoise with a pinned host array in and a host array out. The
+`reference` arm times the CPU restatement of the reference's path on the host
+cores (the reference's Jittor is not installed here).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from datetime import timedelta
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+for _p in (ROOT, ROOT / "jittor-flow2surf_b200"):
+    if str(_p) not in sys.path:
+        sys.path.insert(0, str(_p))
+
+METRIC = "denoised points/sec (full reverse flow)"
+UNIT = "points/s"
+DENOISE = dict(patch_size=1000, seed_k=3, num_steps=3, patch_agg_beta=5.0,
+               alpha_clean_power=1.0, alpha_noisy_power=6.0)
+L2_FLUSH_BYTES = 512 << 20
+
+
+def parse_args():
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawTextHelpFormatter)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    p.add_argument("--points", type=int, default=50_000)
+    p.add_argument("--seed-k", type=int, default=DENOISE["seed_k"])
+    p.add_argument("--cpu-sample-points", type=int, default=5_000,
+                   help="cloud size of the bounded CPU-baseline sample")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def workload_config(args, world: int) -> dict:
+    from flow2surf_b200.inference import patch_seed_count
+
+    patches = patch_seed_count(args.points, DENOISE["patch_size"], args.seed_k)
+    return {
+        "workload": (f"full reverse-flow denoise of one {args.points:,}-point synthetic cloud "
+                     f"per GPU ({patches} patches x {DENOISE['patch_size']} points, "
+                     f"{DENOISE['num_steps']} Euler steps)"),
+        "points_per_cloud": args.points,
+        "clouds": world,
+        "patch_size": DENOISE["patch_size"],
+        "seed_k": args.seed_k,
+        "patches": patches,
+        "num_steps": DENOISE["num_steps"],
+        "alpha_powers": [1, 6],
+        "patch_agg_beta": DENOISE["patch_agg_beta"],
+        "k_neighbors": 32,
+        "architecture": "configs/default.yaml (feat 192, encoder 64/128, 3 blocks, ffn x8)",
+        "weights": "random init, seed 0",
+        "l2": f"flushed between timed steps ({L2_FLUSH_BYTES >> 20} MiB write, untimed)",
+        "parallelism": f"shard by cloud, {world} GPU(s), no collective",
+    }
+
+
+def make_cloud(points: int, rank: int):
+    from flow2surf_b200.synthetic import mesh_cloud
+
+    return mesh_cloud(points, seed=4 + rank, sigma_fraction=0.015, noise_type="laplace")[0]
+
+
+def make_model():
+    from flow2surf_b200 import build_model
+    from flow2surf_b200.synthetic import DEFAULT_CONFIG, random_parameters
+
+    model = build_model(DEFAULT_CONFIG)
+    model.load_parameters(random_parameters(DEFAULT_CONFIG, seed=0))
+    return model
+
+
+# ---------------------------------------------------------------------------
+# CPU arms (the oracle restatement of the reference's path)
+# ---------------------------------------------------------------------------
+
+def cpu_sample(points: int, seed_k: int, steps: int = 1, warmup: int = 0):
+    """Time the CPU restatement on a bounded sample: a `points`-point cloud of
+    the same recipe at the same patch density. Returns (points/s, seconds)."""
+    import torch
+
+    from flow2surf_b200.synthetic import DEFAULT_CONFIG, random_parameters
+    from oracle import inference as oinf
+    from oracle.model_torch import TorchOracleNet
+
+    torch.set_num_threads(os.cpu_count())
+    cloud = make_cloud(points, 0)
+    net = TorchOracleNet(DEFAULT_CONFIG, random_parameters(DEFAULT_CONFIG, seed=0))
+    kw = dict(DENOISE, seed_k=seed_k)
+    patches = oinf.patch_seed_count(points, kw["patch_size"], seed_k)
+    chunks = max(1, (patches + 4) // 5)
+    times = []
+    for i in range(warmup + steps):
+        t0 = time.perf_counter()
+        oinf.patch_denoise(net, cloud, kw["patch_size"], seed_k, kw["num_steps"], chunks,
+                           rng=np.random.default_rng(0), patch_agg_beta=kw["patch_agg_beta"],
+                           alpha_clean_power=kw["alpha_clean_power"],
+                           alpha_noisy_power=kw["alpha_noisy_power"])
+        if i >= warmup:
+            times.append(time.perf_counter() - t0)
+    return points / statistics.mean(times), times
+
+
+def cpu_baseline_line(args) -> dict:
+    value, times = cpu_sample(args.cpu_sample_points, args.seed_k)
+    return {"value": value, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+            "sample": (f"CPU restatement (torch-CPU float32 oracle, all host threads; Jittor is not "
+                       f"installed) on a {args.cpu_sample_points:,}-point cloud of the same "
+                       f"recipe and patch density, one full denoise ({times[0]:.1f} s)")}
+
+
+def run_reference(args, rank: int, world: int) -> None:
+    if rank != 0:
+        return
+    sample = max(1000, min(args.cpu_sample_points, 2_000))
+    value, times = cpu_sample(sample, args.seed_k, steps=args.steps, warmup=min(args.warmup, 1))
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1e3 * statistics.mean(times),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "impl": "reference",
+        "config": workload_config(args, 1),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+                         "sample": (f"each step: one full denoise of a {sample:,}-point cloud "
+                                    "of the same recipe and patch density by the CPU "
+                                    "restatement (Jittor unavailable)")},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str):
+        self.gpu_id = gpu_id
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", self.gpu_id, f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.text = ""
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.text, _ = self.proc.communicate(timeout=10)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.text, _ = self.proc.communicate()
+
+    def summary(self) -> dict:
+        rows = []
+        for line in (getattr(self, "text", "") or "").splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), parts[5:9]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm_max = max(r[1] for r in rows)
+        loaded = [r for r in rows if r[0] >= 0.5 * sm_max] or rows
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i, v in enumerate(r[2]) if v == "Active"})
+        return {"sm_mhz": statistics.median(r[0] for r in loaded), "sm_max_mhz": sm_max,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def kernel_flops_per_point(tag: str, dims) -> float:
+    """Algorithmic FLOPs per patch point of one forward, by kernel class."""
+    C, Hf, qk, K = dims.feat_dim, dims.hidden, dims.qk_dim, dims.k
+    M = DENOISE["patch_size"]
+    nb = dims.num_blocks
+    if tag == "gemm_swiglu":
+        return nb * 2 * 2 * C * Hf
+    if tag == "gemm_ff2":
+        return nb * 2 * Hf * C
+    if tag == "gemm_qkv":
+        return nb * 2 * C * (C + 2 * qk)
+    if tag == "gemm_proj":
+        return nb * 2 * C * C
+    if tag == "attn_output":
+        return nb * 2 * M * (qk + C)
+    if tag == "attn_colstats":
+        return nb * 2 * M * qk
+    if tag == "edge_stage":
+        return sum(2 * K * (6 * h + h * c) for h, c in zip(dims.stage_inputs, dims.stage_dims))
+    if tag == "gemm_content":
+        return sum(2 * h * 2 * c for h, c in zip(dims.stage_inputs, dims.stage_dims))
+    if tag == "gemm_head":
+        return 2 * sum(dims.stage_dims) * C
+    return 0.0
+
+
+def load_traffic() -> dict:
+    """DRAM bytes per launch by kernel class from the committed ncu summary."""
+    path = ROOT / "profiles" / "traffic.txt"
+    out = {}
+    if path.exists():
+        for line in path.read_text().splitlines():
+            parts = line.split()
+            if len(parts) >= 2 and not line.startswith("#"):
+                try:
+                    out[parts[0]] = float(parts[1])
+                except ValueError:
+                    pass
+    return out
+
+
+def peaks() -> dict:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        d = json.loads(path.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d["bf16_tflops_sustained"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "source": "fallback"}
+
+
+def roofline(kernels: dict, forwards_points: float, dims) -> dict:
+    """The dominant kernel's achieved rate against its bound."""
+    tag, (ms, launches) = max(kernels.items(), key=lambda kv: kv[1][0])
+    pk = peaks()
+    flops = kernel_flops_per_point(tag, dims) * forwards_points
+    traffic = load_traffic().get(tag)
+    if flops > 0:
+        achieved = flops / (ms * 1e-3) / 1e12
+        peak = pk["bf16_tflops_sustained"]
+        return {"kernel": tag, "bound": "tensor", "achieved": achieved, "peak": peak,
+                "unit": "TFLOP/s", "frac": achieved / peak, "traffic": traffic,
+                "launches": launches, "avg_launch_ms": ms / launches,
+                "peak_source": f"{pk['source']} bf16 dense, sustained"}
+    return {"kernel": tag, "bound": "hbm", "achieved": None, "peak": pk["hbm_gbs"],
+            "unit": "GB/s", "frac": None, "traffic": traffic, "launches": launches,
+            "avg_launch_ms": ms / launches, "peak_source": f"{pk['source']} HBM copy"}
+
+
+def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
+    import torch
+    import torch.distributed as dist
+
+    from flow2surf_b200 import trace
+    from flow2surf_b200.inference import denoise_device, patch_denoise, patch_seed_count
+    from flow2surf_b200.params import model_dims
+    from flow2surf_b200.synthetic import DEFAULT_CONFIG
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    model = make_model()
+    cloud = make_cloud(args.points, rank)
+    points = torch.from_numpy(cloud).to(dev)
+    pinned = torch.from_numpy(cloud).pin_memory()
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    kw = dict(DENOISE, seed_k=args.seed_k)
+    steps, warmup = args.steps, args.warmup
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    def one_step():
+        return denoise_device(model, points, rng=np.random.default_rng(rank), **kw)
+
+    for _ in range(warmup):
+        one_step()
+    barrier()
+
+    # device-timed steps (value)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    stops = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    gpu_id = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    with ClockSampler(gpu_id) as clocks:
+        barrier()
+        with trace.recording() as rec:
+            for i in range(steps):
+                flush.fill_(i & 0xFF)
+                starts[i].record()
+                out = one_step()
+                stops[i].record()
+            barrier()
+    elapsed_ms = sum(s.elapsed_time(e) for s, e in zip(starts, stops))
+    total = torch.tensor([elapsed_ms], dtype=torch.float64, device=dev)
+
+    # end-to-end through the public API (value measured the same way, host in/out)
+    e2e_s = 0.0
+    for i in range(steps):
+        flush.fill_(i & 0xFF)
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        host_out = patch_denoise(model, pinned, num_chunks=8, rng=np.random.default_rng(rank),
+                                 device=dev, **kw)
+        e2e_s += time.perf_counter() - t0
+    barrier()
+    e2e = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(total, op=dist.ReduceOp.MAX)
+        dist.all_reduce(e2e, op=dist.ReduceOp.MAX)
+    if not np.all(np.isfinite(host_out)) or not torch.isfinite(out).all():
+        raise RuntimeError("non-finite denoised output")
+    if rank != 0:
+        return
+
+    ms_step = total.item() / steps
+    value = world * args.points / (ms_step * 1e-3)
+    e2e_value = world * args.points * steps / e2e.item()
+    dims = model_dims(DEFAULT_CONFIG)
+    patches = patch_seed_count(args.points, kw["patch_size"], args.seed_k)
+    forward_points = steps * kw["num_steps"] * patches * kw["patch_size"]
+    kernels = rec.kernels
+    total_kernel_ms = sum(ms for ms, _ in kernels.values()) or 1.0
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": steps,
+        "warmup": warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded mesh clouds, random-init "
+        "weights; no ShapeNet or checkpoints available)",
+        "config": workload_config(args, world),
+        "roofline": roofline(kernels, forward_points, dims),
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(cloud.nbytes),
+                "d2h_bytes_per_step": int(host_out.nbytes)},
+        "gpu_launches": rec.launches,
+        "clocks": clocks.summary(),
+        "kernels": {k: {"ms_per_step": ms / steps, "launches_per_step": n / steps,
+                        "share": ms / total_kernel_ms} for k, (ms, n) in
+                    sorted(kernels.items(), key=lambda kv: -kv[1][0])},
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline_line(args)
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        run_gpu(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -39,6 +39,19 @@ const char* f2s_last_error(void);
 /* ABI version: major * 10000 + minor * 100 + patch. */
 int f2s_version(void);
 
+/*
+ * Per-launch device timing (no counterpart in the reference, which has no
+ * profiling hooks). While enabled, every kernel launch of this library is
+ * bracketed by CUDA events on its stream; f2s_trace_collect waits for them,
+ * returns per-kernel-class totals (arrays of f2s_trace_tag_count() entries,
+ * milliseconds and launch counts) and clears the records.
+ * f2s_trace_enable(0|1) also clears them.
+ */
+int f2s_trace_enable(int on);
+int f2s_trace_tag_count(void);
+const char* f2s_trace_tag_name(int tag);
+int f2s_trace_collect(double* total_ms, int64_t* launches);
+
 /* ------------------------------------------------------------------------ */
 /* Operators (flow2surf/models/ops/__init__.py:3-11)                        */
 /* ------------------------------------------------------------------------ */

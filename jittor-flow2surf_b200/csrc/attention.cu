@@ -198,6 +198,7 @@ int launch_output(const float* q, const float* k, int ldqk, const float* v, int 
     F2S_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       (int)smem));
     const int tiles = ceil_div(N, TQ);
+    TraceScope trace(kTagAttnOutput, stream);
     kernel<<<B * tiles, 256, smem, stream>>>(q, k, ldqk, v, ldv, L, h, ldh, out, ldo, N, d, C,
                                              tiles);
     return check_launch("attn_output_kernel");
@@ -216,9 +217,12 @@ int attention_f32(const float* q, const float* k, int ldqk, const float* v, int 
     F2S_CUDA_TRY(cudaFuncSetAttribute(attn_colstats_kernel,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem1));
     const int key_tiles = ceil_div(N, TK);
+    {
+    TraceScope trace(kTagAttnColstats, stream);
     attn_colstats_kernel<<<B * key_tiles, 256, smem1, stream>>>(q, k, ldqk, N, d, key_tiles,
                                                                 colstats);
     F2S_TRY(check_launch("attn_colstats_kernel"));
+    }
     const int cj = ceil_div(C, 16);
     if (cj <= 4) return launch_output<4>(q, k, ldqk, v, ldv, colstats, h, ldh, out, ldo, B, N, d, C, stream);
     if (cj <= 8) return launch_output<8>(q, k, ldqk, v, ldv, colstats, h, ldh, out, ldo, B, N, d, C, stream);

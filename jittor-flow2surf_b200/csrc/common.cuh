@@ -23,6 +23,46 @@ inline int64_t ceil_div64(int64_t a, int64_t b) { return (a + b - 1) / b; }
 // Number of SMs on the current device (cached per device).
 int sm_count();
 
+// Per-launch device timing (CUDA events around each kernel launch), off by
+// default; f2s_trace_enable / f2s_trace_collect expose it through the C-ABI.
+enum TraceTag {
+    kTagKnn = 0,
+    kTagInputEmbed,
+    kTagCondition,
+    kTagGemmContent,
+    kTagEdge,
+    kTagGemmHead,
+    kTagRowNorm,
+    kTagGemmQkv,
+    kTagAttnColstats,
+    kTagAttnOutput,
+    kTagGemmProj,
+    kTagGemmSwiGlu,
+    kTagGemmFf2,
+    kTagGemmDecoder,
+    kTagFps,
+    kTagPatchIndex,
+    kTagFusionBuild,
+    kTagGather,
+    kTagFuseEuler,
+    kTagNearest,
+    kTagTranspose,
+    kTagCount
+};
+
+class TraceScope {
+  public:
+    TraceScope(int tag, cudaStream_t stream);
+    ~TraceScope();
+    TraceScope(const TraceScope&) = delete;
+    TraceScope& operator=(const TraceScope&) = delete;
+
+  private:
+    int tag_;
+    cudaStream_t stream_;
+    cudaEvent_t start_ = nullptr;
+};
+
 }  // namespace f2s
 
 #define F2S_REQUIRE(cond, ...)                                        \

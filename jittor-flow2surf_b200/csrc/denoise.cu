@@ -446,6 +446,7 @@ extern "C" int f2s_fps(const float* points, int64_t N, int64_t count, int64_t fi
             return fail(F2S_ERR_WORKSPACE, "fps needs %zu workspace bytes, got %zu",
                         (size_t)N * sizeof(float), workspace_bytes);
     }
+    TraceScope trace(kTagFps, as_stream(stream));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(cs);
     cfg.blockDim = dim3(kFpsThreads);
@@ -486,6 +487,7 @@ extern "C" int f2s_patch_index(const float* points, int64_t N, const int32_t* se
     const size_t smem = (size_t)kpow2 * (sizeof(unsigned long long) + sizeof(int));
     F2S_CUDA_TRY(cudaFuncSetAttribute(patch_index_kernel,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    TraceScope trace(kTagPatchIndex, as_stream(stream));
     patch_index_kernel<<<P, kPiThreads, smem, as_stream(stream)>>>(
         points, (int)N, seeds, k, kpow2, beta, neighbors, radial, weights);
     return check_launch("patch_index_kernel");
@@ -511,6 +513,7 @@ extern "C" int f2s_fusion_build(const int32_t* neighbors, const double* weights,
         return fail(F2S_ERR_WORKSPACE, "fusion_build needs %zu workspace bytes, got %zu", need,
                     workspace_bytes);
     cudaStream_t st = as_stream(stream);
+    TraceScope trace(kTagFusionBuild, st);
     int* counts = static_cast<int*>(workspace);
     int* cursor = counts + N;
     int* bad = cursor + N;
@@ -534,6 +537,7 @@ extern "C" int f2s_gather_patches(const float* points, const int32_t* neighbors,
     if (P == 0) return F2S_OK;
     F2S_REQUIRE(points && neighbors && seeds && x, "gather_patches: null pointer");
     const int64_t total = (int64_t)P * k;
+    TraceScope trace(kTagGather, as_stream(stream));
     gather_kernel<<<grid_for(total, 256), 256, 0, as_stream(stream)>>>(points, neighbors, seeds,
                                                                          P, k, x);
     return check_launch("gather_kernel");
@@ -548,6 +552,7 @@ extern "C" int f2s_fuse_euler(const float* points, const float* votes, const int
     F2S_LIMIT(N < (1ll << 31) - 1, "too many points");
     F2S_REQUIRE(points && votes && offsets && entries && weights && weight_sum && out,
                 "fuse_euler: null pointer");
+    TraceScope trace(kTagFuseEuler, as_stream(stream));
     fuse_euler_kernel<<<ceil_div((int)N, 256), 256, 0, as_stream(stream)>>>(
         points, votes, offsets, entries, weights, weight_sum, (int)N, alpha_step, out, velocity);
     return check_launch("fuse_euler_kernel");

@@ -177,6 +177,7 @@ int launch_edge(const EdgeArgs& a, cudaStream_t stream) {
     F2S_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       (int)smem));
     const int R = a.B * a.M;
+    TraceScope trace(kTagEdge, stream);
     kernel<<<ceil_div(R, ppc), 256, smem, stream>>>(a, ppc);
     return check_launch("edge_kernel");
 }

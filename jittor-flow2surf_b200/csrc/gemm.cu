@@ -110,6 +110,7 @@ int gemm_f32(const GemmArgs& g, cudaStream_t stream) {
     F2S_REQUIRE(g.epilogue != kEpiGatedResidual || (g.gate && g.rows_per_patch > 0),
                 "gemm: gated residual needs gate");
     dim3 grid(ceil_div(g.rows, BM), ceil_div(g.cols, BN));
+    TraceScope trace(g.tag, stream);
     F2S_LIMIT(grid.y <= 65535, "gemm: cols too large");
     switch (g.epilogue) {
         case kEpiStore: gemm_f32_kernel<kEpiStore><<<grid, 256, 0, stream>>>(g); break;

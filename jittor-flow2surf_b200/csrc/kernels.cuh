@@ -32,6 +32,7 @@ struct GemmArgs {
     int rows_per_patch;
     int rows, cols, K;
     GemmEpilogue epilogue;
+    int tag;               // TraceTag of this launch
 };
 int gemm_f32(const GemmArgs& args, cudaStream_t stream);
 

@@ -21,6 +21,9 @@
 // reference's k block-wide reductions.
 #include "common.cuh"
 
+using f2s::TraceScope;
+using f2s::kTagKnn;
+
 namespace {
 
 constexpr int kWarps = 8;
@@ -208,6 +211,7 @@ int launch_knn(const float* features, int B, int C, int N, int k, int actual_k, 
     const int tiles = f2s::ceil_div(N, kQueriesPerCta);
     const int64_t grid = (int64_t)B * tiles;
     F2S_LIMIT(grid < (1ll << 31), "knn grid too large: B=%d N=%d", B, N);
+    TraceScope trace(kTagKnn, stream);
     kernel<<<(unsigned)grid, kWarps * 32, smem, stream>>>(features, C, N, k, actual_k, tiles, out);
     return f2s::check_launch("knn_kernel");
 }

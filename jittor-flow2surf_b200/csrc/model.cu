@@ -293,6 +293,7 @@ GemmArgs gemm_args(const float* A, int lda, const float* W, const float* bias, f
     g.K = K;
     g.rows_per_patch = 1;
     g.epilogue = kEpiStore;
+    g.tag = kTagGemmContent;
     return g;
 }
 
@@ -315,6 +316,7 @@ int forward(const Dims& d, const Layout& L, const float* P, const float* x_in, c
         ca.A = d.A;
         ca.NB = d.NB;
         ca.C = C;
+        TraceScope trace(kTagCondition, st);
         cond_mod_kernel<<<B, 256, sizeof(float) * 5 * d.A, st>>>(ca, alpha, w.cond, w.mod);
         F2S_TRY(check_launch("cond_mod_kernel"));
     }
@@ -324,6 +326,7 @@ int forward(const Dims& d, const Layout& L, const float* P, const float* x_in, c
         const size_t smem = sizeof(float) * ((size_t)S0 * S0 + 8 * S0);
         F2S_CUDA_TRY(cudaFuncSetAttribute(input_embed_kernel,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        TraceScope trace(kTagInputEmbed, st);
         input_embed_kernel<<<ceil_div(R, 8), 256, smem, st>>>(
             x_in, B, M, P + L.in_w, P + L.in_b, P + L.in_ln_w, P + L.in_ln_b, P + L.in_out_w,
             P + L.in_out_b, S0, w.xyz4, w.feat0);
@@ -339,7 +342,7 @@ int forward(const Dims& d, const Layout& L, const float* P, const float* x_in, c
         const int cin = d.si[s], cout = d.sd[s];
         F2S_TRY(gemm_f32(gemm_args(fin, ldin, P + sp.content_w, nullptr, w.content, 2 * cout, R,
                                    2 * cout, cin),
-                         st));
+                         st));  // tag: gemm_content
         EdgeArgs ea{};
         ea.content = w.content;
         ea.ldc = 2 * cout;
@@ -367,9 +370,12 @@ int forward(const Dims& d, const Layout& L, const float* P, const float* x_in, c
         col += cout;
     }
     // projection head (encoder.py:118-123,184)
-    F2S_TRY(gemm_f32(gemm_args(w.cat, d.sum_stage, P + L.proj_w, nullptr, w.x, C, R, C,
-                               d.sum_stage),
-                     st));
+    {
+        GemmArgs g = gemm_args(w.cat, d.sum_stage, P + L.proj_w, nullptr, w.x, C, R, C,
+                               d.sum_stage);
+        g.tag = kTagGemmHead;
+        F2S_TRY(gemm_f32(g, st));
+    }
     F2S_TRY(ln_affine_leaky(w.x, C, P + L.proj_ln_w, P + L.proj_ln_b, R, C, st));
     // trunk (transformer.py:75-89)
     const int ld_qkv = C + 2 * d.qk;
@@ -378,8 +384,9 @@ int forward(const Dims& d, const Layout& L, const float* P, const float* x_in, c
         const BlockParams& bp = L.block[i];
         const float* mod = w.mod + (size_t)i * 6 * C;
         F2S_TRY(ln_modulate(w.x, C, w.h, C, mod, mstride, 0, C, R, M, C, st));
-        F2S_TRY(gemm_f32(gemm_args(w.h, C, P + bp.qkv_w, nullptr, w.qkv, ld_qkv, R, ld_qkv, C),
-                         st));
+        GemmArgs gq = gemm_args(w.h, C, P + bp.qkv_w, nullptr, w.qkv, ld_qkv, R, ld_qkv, C);
+        gq.tag = kTagGemmQkv;
+        F2S_TRY(gemm_f32(gq, st));
         F2S_TRY(qk_norm(w.qkv, ld_qkv, R, d.qk, st));
         F2S_TRY(attention_f32(w.qkv, w.qkv + d.qk, ld_qkv, w.qkv + 2 * d.qk, ld_qkv, w.h, C,
                               w.offs, C, w.colstats, B, M, d.qk, C, st));
@@ -388,18 +395,21 @@ int forward(const Dims& d, const Layout& L, const float* P, const float* x_in, c
         g.gate = mod + 2 * C;
         g.gate_stride = mstride;
         g.rows_per_patch = M;
+        g.tag = kTagGemmProj;
         F2S_TRY(gemm_f32(g, st));
         F2S_TRY(ln_modulate(w.x, C, w.h, C, mod, mstride, 3 * C, 4 * C, R, M, C, st));
         GemmArgs sw = gemm_args(w.h, C, P + bp.gate_w, P + bp.gate_b, w.ffh, d.Hf, R, d.Hf, C);
         sw.epilogue = kEpiSwiGlu;
         sw.W2 = P + bp.ff1_w;
         sw.bias2 = P + bp.ff1_b;
+        sw.tag = kTagGemmSwiGlu;
         F2S_TRY(gemm_f32(sw, st));
         GemmArgs f2 = gemm_args(w.ffh, d.Hf, P + bp.ff2_w, P + bp.ff2_b, w.x, C, R, C, d.Hf);
         f2.epilogue = kEpiGatedResidual;
         f2.gate = mod + 5 * C;
         f2.gate_stride = mstride;
         f2.rows_per_patch = M;
+        f2.tag = kTagGemmFf2;
         F2S_TRY(gemm_f32(f2, st));
     }
     // decoder (decoder.py:8-32)
@@ -408,15 +418,17 @@ int forward(const Dims& d, const Layout& L, const float* P, const float* x_in, c
     float* bufs[2] = {w.dec0, w.dec1};
     for (int i = 0; i < d.ndec; ++i) {
         float* out = bufs[i & 1];
-        F2S_TRY(gemm_f32(gemm_args(cur, in_dim, P + L.dec[i].w, nullptr, out, d.dd[i], R, d.dd[i],
-                                   in_dim),
-                         st));
+        GemmArgs gd = gemm_args(cur, in_dim, P + L.dec[i].w, nullptr, out, d.dd[i], R, d.dd[i],
+                                in_dim);
+        gd.tag = kTagGemmDecoder;
+        F2S_TRY(gemm_f32(gd, st));
         F2S_TRY(ln_affine_leaky(out, d.dd[i], P + L.dec[i].ln_w, P + L.dec[i].ln_b, R, d.dd[i], st));
         cur = out;
         in_dim = d.dd[i];
     }
-    return gemm_f32(gemm_args(cur, in_dim, P + L.dec_out_w, nullptr, velocity, 3, R, 3, in_dim),
-                    st);
+    GemmArgs go = gemm_args(cur, in_dim, P + L.dec_out_w, nullptr, velocity, 3, R, 3, in_dim);
+    go.tag = kTagGemmDecoder;
+    return gemm_f32(go, st);
 }
 
 }  // namespace

@@ -177,6 +177,7 @@ extern "C" int f2s_nearest(const float* first, const float* second, int B, int M
         return fail(F2S_ERR_WORKSPACE, "nearest needs %zu workspace bytes, got %zu", need,
                     workspace_bytes);
     cudaStream_t st = as_stream(stream);
+    TraceScope trace(kTagNearest, st);
     unsigned long long* k1 = static_cast<unsigned long long*>(workspace);
     unsigned long long* k2 = k1 + (size_t)B * M;
     F2S_TRY(one_way(first, second, B, M, N, k1, st));
@@ -200,6 +201,7 @@ extern "C" int f2s_chamfer(const float* pred, const float* target, int B, int M,
         return fail(F2S_ERR_WORKSPACE, "chamfer needs %zu workspace bytes, got %zu", need,
                     workspace_bytes);
     cudaStream_t st = as_stream(stream);
+    TraceScope trace(kTagNearest, st);
     unsigned long long* k1 = static_cast<unsigned long long*>(workspace);
     unsigned long long* k2 = k1 + (size_t)B * M;
     F2S_TRY(one_way(pred, target, B, M, N, k1, st));

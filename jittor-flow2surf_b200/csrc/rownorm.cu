@@ -71,6 +71,7 @@ int ln_modulate(const float* x, int ldx, float* h, int ldh, const float* mod, in
                 int scale_off, int shift_off, int rows, int rows_per_patch, int C,
                 cudaStream_t stream) {
     if (rows == 0) return F2S_OK;
+    TraceScope trace(kTagRowNorm, stream);
     ln_modulate_kernel<<<ceil_div(rows, kRowsPerCta), kRowsPerCta * 32, 0, stream>>>(
         x, ldx, h, ldh, mod, mod_stride, scale_off, shift_off, rows, rows_per_patch, C);
     return check_launch("ln_modulate_kernel");
@@ -79,6 +80,7 @@ int ln_modulate(const float* x, int ldx, float* h, int ldh, const float* mod, in
 int ln_affine_leaky(float* y, int ldy, const float* gamma, const float* beta, int rows, int C,
                     cudaStream_t stream) {
     if (rows == 0) return F2S_OK;
+    TraceScope trace(kTagRowNorm, stream);
     ln_affine_leaky_kernel<<<ceil_div(rows, kRowsPerCta), kRowsPerCta * 32, 0, stream>>>(
         y, ldy, gamma, beta, rows, C);
     return check_launch("ln_affine_leaky_kernel");
@@ -86,6 +88,7 @@ int ln_affine_leaky(float* y, int ldy, const float* gamma, const float* beta, in
 
 int qk_norm(float* qkv, int ld, int rows, int d, cudaStream_t stream) {
     if (rows == 0) return F2S_OK;
+    TraceScope trace(kTagRowNorm, stream);
     qk_norm_kernel<<<ceil_div(rows, kRowsPerCta), kRowsPerCta * 32, 0, stream>>>(qkv, ld, rows,
                                                                                  d);
     return check_launch("qk_norm_kernel");

@@ -35,6 +35,7 @@ int transpose_batched(const float* in, float* out, int B, int rows, int cols,
     F2S_LIMIT(B <= 65535, "transpose: batch %d too large", B);
     dim3 grid(ceil_div(cols, 32), ceil_div(rows, 32), B);
     F2S_LIMIT(grid.y <= 65535, "transpose: too many rows");
+    TraceScope trace(kTagTranspose, stream);
     transpose_kernel<<<grid, dim3(32, 8), 0, stream>>>(in, out, rows, cols, grid.x);
     return check_launch("transpose_kernel");
 }

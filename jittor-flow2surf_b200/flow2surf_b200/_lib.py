@@ -30,6 +30,10 @@ _sz = ctypes.c_size_t
 SIGNATURES: dict[str, list] = {
     "f2s_last_error": [],
     "f2s_version": [],
+    "f2s_trace_enable": [_i],
+    "f2s_trace_tag_count": [],
+    "f2s_trace_tag_name": [_i],
+    "f2s_trace_collect": [_p, _p],
     "f2s_knn": [_p, _i, _i, _i, _i, _p, _p],
     "f2s_offset_attention_workspace_bytes": [_i, _i, _i, _p],
     "f2s_offset_attention": [_p, _p, _p, _i, _i, _i, _i, _p, _p, _sz, _p],
@@ -50,7 +54,7 @@ SIGNATURES: dict[str, list] = {
     "f2s_chamfer": [_p, _p, _i, _i, _i, _p, _p, _sz, _p],
 }
 
-_RESTYPES = {"f2s_last_error": ctypes.c_char_p}
+_RESTYPES = {"f2s_last_error": ctypes.c_char_p, "f2s_trace_tag_name": ctypes.c_char_p}
 
 _LIB = None
 

@@ -202,8 +202,11 @@ def patch_denoise(model, pc_noisy, patch_size, seed_k, num_steps, num_chunks, rn
     """
     if num_chunks < 1:
         raise ValueError(f"num_chunks must be >= 1, got {num_chunks}")
-    host = np.ascontiguousarray(np.asarray(pc_noisy), dtype=np.float32)
-    points = torch.from_numpy(host).to(device)
+    if isinstance(pc_noisy, torch.Tensor):   # e.g. a pinned host tensor: asynchronous copy
+        points = pc_noisy.to(device=device, dtype=torch.float32, non_blocking=True)
+    else:
+        host = np.ascontiguousarray(np.asarray(pc_noisy), dtype=np.float32)
+        points = torch.from_numpy(host).to(device)
     out = denoise_device(model, points, patch_size, seed_k, num_steps, rng=rng,
                          patch_seed_idx=patch_seed_idx, patch_agg_beta=patch_agg_beta,
                          alpha_clean_power=alpha_clean_power,

@@ -155,3 +155,18 @@ def test_chamfer_oracle_matches_reference(golden):
     d2, _ = native.nearest_one_way(fix["target"][None], fix["pred"][None])
     kernel_form = float(d1.astype(np.float64).mean() + d2.astype(np.float64).mean())
     assert abs(kernel_form - float(fix["chamfer"])) < 1e-5
+
+
+def test_torch_cpu_oracle_matches_numpy_oracle(golden):
+    """The torch-CPU restatement (timed as the CPU baseline) computes the same
+    model as the NumPy oracle."""
+    from oracle.model_torch import TorchOracleNet
+
+    fix = golden("model")
+    params = _params(fix)
+    got = TorchOracleNet(TINY_CONFIG, params, dtype=__import__("torch").float64)(
+        fix["x"], fix["alpha"])
+    want = OracleNet(TINY_CONFIG, params)(fix["x"], fix["alpha"])
+    # the torch restatement returns float32 velocities
+    np.testing.assert_allclose(got, want, rtol=1e-7, atol=1e-9)
+    np.testing.assert_allclose(got, fix["velocity_f64"], rtol=0, atol=1e-5)
