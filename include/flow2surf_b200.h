@@ -253,6 +253,26 @@ int f2s_nearest(const float* first, const float* second, int B, int M, int N,
 int f2s_chamfer(const float* pred, const float* target, int B, int M, int N, double* chamfer,
                 void* workspace, size_t workspace_bytes, void* stream);
 
+/*
+ * f2s_chamfer for callers that cannot allocate device memory. No counterpart
+ * in the reference: it exists for code that must not call cudaMalloc -- an
+ * out-of-memory handler, a host that forbids device allocation once running,
+ * or work that must not risk the device synchronisation cudaMalloc/cudaFree
+ * can cause. Same inputs, outputs and results as f2s_chamfer, but the
+ * distance keys live in a built-in device array of
+ * F2S_CHAMFER_STATIC_MAX_POINTS 64-bit entries (16 MiB, held by every GPU
+ * that loads this library until the process exits) instead of a workspace.
+ *   Requires B * (M + N) <= F2S_CHAMFER_STATIC_MAX_POINTS, else
+ *   F2S_ERR_UNSUPPORTED. Allocates nothing.
+ *   The first call on each device looks up the array's device address (with
+ *   that device current); make that first call before any stream capture.
+ *   All calls share the one array: calls that overlap on the GPU (other
+ *   streams, other host threads) race and must be serialised by the caller.
+ */
+#define F2S_CHAMFER_STATIC_MAX_POINTS (1 << 21)
+int f2s_chamfer_static(const float* pred, const float* target, int B, int M, int N,
+                       double* chamfer, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

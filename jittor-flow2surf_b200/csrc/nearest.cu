@@ -209,3 +209,62 @@ extern "C" int f2s_chamfer(const float* pred, const float* target, int B, int M,
     chamfer_reduce_kernel<<<B, 1024, 0, st>>>(k1, M, k2, N, chamfer);
     return check_launch("chamfer_reduce_kernel");
 }
+
+// ---------------------------------------------------------------------------
+// Chamfer without any allocation, for callers that cannot call cudaMalloc:
+// code running inside a caching allocator's out-of-memory handler, a host
+// that forbids device allocation after start-up, or a caller in the middle of
+// other work that must not synchronise the device (cudaMalloc/cudaFree can).
+// The 64-bit distance keys live in one file-scope device array of
+// F2S_CHAMFER_STATIC_MAX_POINTS entries (16 MiB), which every GPU that loads
+// this library keeps until the process exits.
+// ---------------------------------------------------------------------------
+#include <mutex>
+
+static __device__ __align__(256) unsigned long long
+    g_chamfer_scratch[F2S_CHAMFER_STATIC_MAX_POINTS];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mutex;
+unsigned long long* g_scratch_address[kMaxDevices] = {nullptr};
+
+// The device address of g_chamfer_scratch on the current device. In host code
+// the array's name is only a host-side stand-in, so the address is looked up
+// once per device (with that device current) and cached.
+int chamfer_scratch(unsigned long long** out) {
+    int dev = 0;
+    F2S_CUDA_TRY(cudaGetDevice(&dev));
+    F2S_LIMIT(dev >= 0 && dev < kMaxDevices, "device ordinal %d beyond %d", dev, kMaxDevices);
+    std::lock_guard<std::mutex> lock(g_scratch_mutex);
+    if (g_scratch_address[dev] == nullptr) {
+        void* ptr = nullptr;
+        F2S_CUDA_TRY(cudaGetSymbolAddress(&ptr, g_chamfer_scratch));
+        g_scratch_address[dev] = static_cast<unsigned long long*>(ptr);
+    }
+    *out = g_scratch_address[dev];
+    return F2S_OK;
+}
+}  // namespace
+
+extern "C" int f2s_chamfer_static(const float* pred, const float* target, int B, int M, int N,
+                                  double* chamfer, void* stream) {
+    F2S_TRY(check_sets(pred, target, B, M, N));
+    if (B == 0) return F2S_OK;
+    F2S_REQUIRE(chamfer != nullptr, "chamfer: null pointer");
+    const int64_t keys = (int64_t)B * ((int64_t)M + N);
+    F2S_LIMIT(keys <= F2S_CHAMFER_STATIC_MAX_POINTS,
+              "chamfer_static: B*(M+N) = %lld points exceed the built-in scratch of %d; use "
+              "f2s_chamfer with a caller workspace",
+              (long long)keys, F2S_CHAMFER_STATIC_MAX_POINTS);
+    unsigned long long* k1 = nullptr;
+    F2S_TRY(chamfer_scratch(&k1));
+    unsigned long long* k2 = k1 + (size_t)B * M;
+    cudaStream_t st = as_stream(stream);
+    // one_way() rewrites every key it uses with its starting value first, so
+    // whatever an earlier call left in the array does not matter.
+    F2S_TRY(one_way(pred, target, B, M, N, k1, st));
+    F2S_TRY(one_way(target, pred, B, N, M, k2, st));
+    chamfer_reduce_kernel<<<B, 1024, 0, st>>>(k1, M, k2, N, chamfer);
+    return check_launch("chamfer_reduce_kernel");
+}
