@@ -113,6 +113,29 @@ int f2s_neighbor_reduce(const float* content, const float* geometry, const int32
                         int B, int N, int K, int D, int H, int C, float* out,
                         void* workspace, size_t workspace_bytes, void* stream);
 
+/*
+ * Point-wise linear map y = x W^T + b over rows of points: the 1x1
+ * Conv1d / Linear of the reference's modules (e.g. transformer.py:37-48 via
+ * Jittor's conv/linear) with point-major activations.
+ *   x (rows, ldx >= K), weight (cols, K), bias (cols) or NULL -> y (rows, ldy) fp32.
+ *   precision F2S_PRECISION_FP32: fp32 CUDA-core kernel;
+ *   F2S_PRECISION_TF32: tcgen05 tensor cores reading fp32 x/weight as tf32;
+ *   F2S_PRECISION_BF16: tcgen05 tensor cores, x and weight are bf16.
+ * Rows (ldx, ldy) must be 16-byte pitched for the tensor-core precisions.
+ */
+#define F2S_PRECISION_FP32 0
+#define F2S_PRECISION_TF32 1
+#define F2S_PRECISION_BF16 2
+int f2s_linear(const void* x, int ldx, const void* weight, const float* bias, float* y, int ldy,
+               int rows, int cols, int K, int precision, void* stream);
+
+/*
+ * The library's device error word: non-zero when a tensor-core kernel gave up
+ * on a bounded wait (it then returned without finishing its tile). Copies it
+ * to *value (synchronising `stream`) and clears it when `reset` is non-zero.
+ */
+int f2s_device_error(int* value, int reset, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Model (flow2surf/models/network.py:29-95)                                */
 /* ------------------------------------------------------------------------ */

@@ -36,6 +36,32 @@ struct GemmArgs {
 };
 int gemm_f32(const GemmArgs& args, cudaStream_t stream);
 
+// ---- tc_gemm.cu ----
+// The same contraction on tcgen05 tensor cores (TMA-fed, TMEM accumulators).
+// A, W, W2 are bf16 or (tf32 = true) fp32; Y is fp32 or (y_bf16) bf16.
+struct TcGemmOp {
+    const void* A;
+    int lda;
+    const void* W;           // cols x K, K contiguous
+    const void* W2;          // SwiGLU value weights (cols x K)
+    const float* bias;
+    const float* bias2;
+    void* Y;
+    int ldy;
+    bool y_bf16;
+    const float* gate;       // gated residual
+    int gate_stride;
+    int rows_per_patch;
+    int rows, cols, K;
+    int bn;                  // N tile: multiple of 32, <= 256 (<= 128 for SwiGLU)
+    bool tf32;
+    GemmEpilogue epilogue;
+    int tag;
+};
+int tc_gemm(const TcGemmOp& op, cudaStream_t stream);
+// N tile with the least padding for `cols` output columns.
+int tc_pick_bn(int cols, bool swiglu);
+
 // ---- rownorm.cu ----
 // h = LN(x) * (1 + scale[p]) + shift[p]; LN two-pass over C, eps 1e-6.
 int ln_modulate(const float* x, int ldx, float* h, int ldh, const float* mod, int mod_stride,

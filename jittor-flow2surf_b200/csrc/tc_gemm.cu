@@ -1,0 +1,441 @@
+// Tensor-core (tcgen05 / TMEM / TMA) GEMM for the point-wise contractions,
+// Y (rows x cols) = A (rows x K) * W^T (W: cols x K), both K-major, with the
+// model's epilogues fused: bias, gated residual x += g * (acc + b), and SwiGLU
+// silu(acc_gate + b) * (acc_value + b2) from two weight matrices sharing A.
+//
+// Structure (one CTA per SM, persistent over 128 x BN output tiles):
+//   warp 0      TMA producer: A and W tiles (128-byte swizzle) into a ring of
+//               shared-memory stages, each completing on a "full" mbarrier;
+//   warp 1      allocates TMEM; lane 0 issues tcgen05.mma (M = 128, N = BN,
+//               K = 32 bytes per instruction) into one of two TMEM
+//               accumulators and commits stage releases / accumulator-ready;
+//   warps 2-5   epilogue: each thread owns one accumulator row (TMEM lane),
+//               reads 32 columns at a time with tcgen05.ld, applies the
+//               epilogue and stores; then frees the accumulator buffer, so the
+//               MMAs of the next tile overlap this epilogue.
+// Operands are bf16 (kind::f16) or fp32 read as tf32 (kind::tf32).
+#include <mutex>
+
+#include "kernels.cuh"
+#include "tc_common.cuh"
+
+namespace f2s {
+
+// Library-wide device error word of the tensor-core kernels (bounded waits
+// that ran out). Read and cleared through f2s_device_error().
+__device__ int g_tc_error = 0;
+
+namespace {
+
+constexpr int kThreads = 192;
+constexpr int kTileM = 128;
+constexpr int kStageBudget = 200 * 1024;
+
+struct TcGemmArgs {
+    int rows, cols, K;
+    int bn;
+    int k_blocks;
+    int stages;
+    int acc_cols;       // TMEM columns of one accumulator buffer
+    uint32_t idesc;
+    const float* bias;
+    const float* bias2;
+    void* Y;
+    int ldy;
+    int y_bf16;
+    const float* gate;
+    int gate_stride;
+    int rows_per_patch;
+    int* err;
+};
+
+__device__ __forceinline__ float epi_value(float v, const float* bias, int col) {
+    return bias ? v + bias[col] : v;
+}
+
+template <bool kTf32, int kEpi>
+__global__ void __launch_bounds__(kThreads, 1)
+tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+               const __grid_constant__ CUtensorMap map_b2, const TcGemmArgs g) {
+    constexpr bool kDual = kEpi == kEpiSwiGlu;
+    extern __shared__ __align__(1024) unsigned char tc_smem_raw[];
+    // 1024-byte alignment of the tile region (SWIZZLE_128B atoms)
+    unsigned char* smem = reinterpret_cast<unsigned char*>(
+        (reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
+    const int S = g.stages;
+    const uint32_t a_bytes = kTileM * 128;
+    const uint32_t b_bytes = (uint32_t)g.bn * 128;
+    const uint32_t stage_bytes = a_bytes + b_bytes * (kDual ? 2 : 1);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)S * stage_bytes);
+    uint64_t* empty = full + S;
+    uint64_t* tfull = empty + S;      // [2]
+    uint64_t* tempty = tfull + 2;     // [2]
+    uint64_t* mma_done = tempty + 2;  // [1]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n_tiles_n = (g.cols + g.bn - 1) / g.bn;
+    const int n_tiles = ((g.rows + kTileM - 1) / kTileM) * n_tiles_n;
+    uint32_t tmem_cols = 32;
+    while (tmem_cols < (uint32_t)(2 * g.acc_cols)) tmem_cols <<= 1;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            tc::mbar_init(&full[s], 1);
+            tc::mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            tc::mbar_init(&tfull[b], 1);
+            tc::mbar_init(&tempty[b], 128);
+        }
+        tc::mbar_init(mma_done, 1);
+        tc::fence_barrier_init();
+        tc::prefetch_tensormap(&map_a);
+        tc::prefetch_tensormap(&map_b);
+        if (kDual) tc::prefetch_tensormap(&map_b2);
+    }
+    if (warp == 1) tc::tmem_alloc(tmem_slot, tmem_cols);
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t pending = 0;        // stages whose last load may still be in flight
+            uint32_t pending_phase = 0;  // the phase each of those loads completes
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
+                const int m0 = (tile / n_tiles_n) * kTileM;
+                const int n0 = (tile % n_tiles_n) * g.bn;
+                for (int kb = 0; kb < g.k_blocks; ++kb) {
+                    if (!tc::mbar_wait(&empty[stage], phase ^ 1u, g.err)) {
+                        ok = false;
+                        break;
+                    }
+                    pending &= ~(1u << stage);
+                    unsigned char* st = smem + (size_t)stage * stage_bytes;
+                    tc::mbar_arrive_expect_tx(&full[stage], stage_bytes);
+                    const int k0 = kb * (kTf32 ? 32 : 64);
+                    tc::tma_load_2d(st, &map_a, &full[stage], k0, m0);
+                    tc::tma_load_2d(st + a_bytes, &map_b, &full[stage], k0, n0);
+                    if (kDual) tc::tma_load_2d(st + a_bytes + b_bytes, &map_b2, &full[stage], k0, n0);
+                    pending |= 1u << stage;
+                    pending_phase = (pending_phase & ~(1u << stage)) | (phase << stage);
+                    if (++stage == S) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            if (!ok) {
+                // let the copies already issued land before the CTA exits
+                for (int s = 0; s < S; ++s) {
+                    if (!(pending & (1u << s))) continue;
+                    const uint32_t ph = (pending_phase >> s) & 1u;
+                    for (uint32_t i = 0; i < tc::kSpinLimit; ++i)
+                        if (tc::mbar_try_wait(&full[s], ph)) break;
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            int iter = 0;
+            bool ok = true;
+            constexpr int kSteps = 4;  // 128 bytes of K per stage / 32 bytes per instruction
+            for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x, ++iter) {
+                const int buf = iter & 1;
+                const uint32_t tph = (uint32_t)(iter >> 1) & 1u;
+                if (!tc::mbar_wait(&tempty[buf], tph ^ 1u, g.err)) {
+                    ok = false;
+                    break;
+                }
+                tc::tc_fence_after();
+                const uint32_t d = tmem_base + (uint32_t)(buf * g.acc_cols);
+                for (int kb = 0; kb < g.k_blocks; ++kb) {
+                    if (!tc::mbar_wait(&full[stage], phase, g.err)) {
+                        ok = false;
+                        break;
+                    }
+                    tc::tc_fence_after();
+                    const uint32_t st = tc::smem_u32(smem + (size_t)stage * stage_bytes);
+#pragma unroll
+                    for (int k = 0; k < kSteps; ++k) {
+                        const uint64_t a = tc::sw128_desc(st + k * 32);
+                        const uint64_t b = tc::sw128_desc(st + a_bytes + k * 32);
+                        const uint32_t acc = (kb | k) ? 1u : 0u;
+                        tc::umma<kTf32>(d, a, b, g.idesc, acc);
+                        if (kDual) {
+                            const uint64_t b2 = tc::sw128_desc(st + a_bytes + b_bytes + k * 32);
+                            tc::umma<kTf32>(d + (uint32_t)g.bn, a, b2, g.idesc, acc);
+                        }
+                    }
+                    tc::umma_commit(&empty[stage]);
+                    if (++stage == S) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (ok) tc::umma_commit(&tfull[buf]);
+            }
+            // every MMA this thread issued has completed before TMEM is freed
+            tc::umma_commit(mma_done);
+            tc::mbar_wait(mma_done, 0, g.err);
+        }
+        __syncwarp();
+    } else {
+        // ---------------- epilogue (warps 2..5) ----------------
+        const int quarter = warp & 3;
+        const int row_in_tile = quarter * 32 + lane;
+        int iter = 0;
+        for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++iter) {
+            const int buf = iter & 1;
+            const uint32_t tph = (uint32_t)(iter >> 1) & 1u;
+            if (!tc::mbar_wait(&tfull[buf], tph, g.err)) break;
+            tc::tc_fence_after();
+            const int m0 = (tile / n_tiles_n) * kTileM;
+            const int n0 = (tile % n_tiles_n) * g.bn;
+            const int row = m0 + row_in_tile;
+            const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) +
+                                   (uint32_t)(buf * g.acc_cols);
+            for (int c0 = 0; c0 < g.bn; c0 += 32) {
+                float v[32];
+                float v2[32];
+                tc::tmem_ld32(t_row + (uint32_t)c0, v);
+                if constexpr (kDual) tc::tmem_ld32(t_row + (uint32_t)(g.bn + c0), v2);
+                if (row >= g.rows) continue;
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    const int col = n0 + c0 + i;
+                    if (col >= g.cols) continue;
+                    float out = epi_value(v[i], g.bias, col);
+                    if constexpr (kDual) out = f2s_silu(out) * epi_value(v2[i], g.bias2, col);
+                    const size_t o = (size_t)row * g.ldy + col;
+                    if (kEpi == kEpiGatedResidual) {
+                        const float gt =
+                            g.gate[(size_t)(row / g.rows_per_patch) * g.gate_stride + col];
+                        float* y = static_cast<float*>(g.Y) + o;
+                        *y = *y + gt * out;
+                    } else if (g.y_bf16) {
+                        static_cast<__nv_bfloat16*>(g.Y)[o] = __float2bfloat16_rn(out);
+                    } else {
+                        static_cast<float*>(g.Y)[o] = out;
+                    }
+                }
+            }
+            tc::tc_fence_before();
+            tc::mbar_arrive(&tempty[buf]);
+        }
+    }
+
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tmem_base, tmem_cols);
+    }
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+int* device_error_word() {
+    static int* addr[64] = {nullptr};
+    static std::mutex mu;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!addr[dev]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_tc_error) != cudaSuccess) return nullptr;
+        addr[dev] = static_cast<int*>(p);
+    }
+    return addr[dev];
+}
+
+template <bool kTf32, int kEpi>
+int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb2,
+              const TcGemmArgs& g, size_t smem, int grid, cudaStream_t st) {
+    auto kernel = tc_gemm_kernel<kTf32, kEpi>;
+    F2S_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    kernel<<<grid, kThreads, smem, st>>>(ma, mb, mb2, g);
+    return check_launch("tc_gemm_kernel");
+}
+
+}  // namespace
+
+int make_tensor_map_2d(CUtensorMap* map, const void* base, bool fp32, int64_t rows, int64_t cols,
+                       int64_t ld, int box_rows, int box_cols) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return fail(F2S_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    const int64_t elem = fp32 ? 4 : 2;
+    F2S_REQUIRE(((uintptr_t)base & 15) == 0, "tensor map base must be 16-byte aligned");
+    F2S_REQUIRE((ld * elem) % 16 == 0, "tensor map row pitch must be a multiple of 16 bytes");
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)(ld * elem)};
+    const cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = enc(map, fp32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                           2, const_cast<void*>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(F2S_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return F2S_OK;
+}
+
+// Y = A W^T (+ epilogue) on tcgen05. A: rows x K (lda), W: cols x K (K
+// contiguous), W2 the SwiGLU value weights. `tf32`: A/W are fp32 and the MMA
+// runs kind::tf32; otherwise bf16 and kind::f16. bn: N tile (multiple of 32,
+// <= 256; <= 128 for SwiGLU).
+int tc_gemm(const TcGemmOp& op, cudaStream_t st) {
+    if (op.rows == 0 || op.cols == 0) return F2S_OK;
+    F2S_REQUIRE(op.A && op.W && op.Y && op.K > 0, "tc_gemm: bad operands");
+    const bool dual = op.epilogue == kEpiSwiGlu;
+    F2S_REQUIRE(!dual || op.W2, "tc_gemm: SwiGLU needs W2");
+    F2S_REQUIRE(op.epilogue != kEpiGatedResidual || (op.gate && op.rows_per_patch > 0 && !op.y_bf16),
+                "tc_gemm: gated residual needs a gate and an fp32 output");
+    int bn = op.bn;
+    F2S_REQUIRE(bn >= 32 && bn <= 256 && bn % 32 == 0 && (!dual || bn <= 128),
+                "tc_gemm: bad N tile %d", bn);
+    int* err = device_error_word();
+    if (!err) return fail(F2S_ERR_CUDA, "tc_gemm: device error word unavailable");
+    CUtensorMap ma, mb, mb2;
+    const int bk = op.tf32 ? 32 : 64;
+    F2S_TRY(make_tensor_map_2d(&ma, op.A, op.tf32, op.rows, op.K, op.lda, kTileM, bk));
+    F2S_TRY(make_tensor_map_2d(&mb, op.W, op.tf32, op.cols, op.K, op.K, bn, bk));
+    if (dual) F2S_TRY(make_tensor_map_2d(&mb2, op.W2, op.tf32, op.cols, op.K, op.K, bn, bk));
+    else mb2 = mb;
+
+    TcGemmArgs g{};
+    g.rows = op.rows;
+    g.cols = op.cols;
+    g.K = op.K;
+    g.bn = bn;
+    g.k_blocks = ceil_div(op.K, bk);
+    g.acc_cols = bn * (dual ? 2 : 1);
+    g.idesc = tc::make_idesc(kTileM, bn, op.tf32 ? 2u : 1u);
+    g.bias = op.bias;
+    g.bias2 = op.bias2;
+    g.Y = op.Y;
+    g.ldy = op.ldy;
+    g.y_bf16 = op.y_bf16 ? 1 : 0;
+    g.gate = op.gate;
+    g.gate_stride = op.gate_stride;
+    g.rows_per_patch = op.rows_per_patch > 0 ? op.rows_per_patch : 1;
+    g.err = err;
+    const size_t stage_bytes = (size_t)kTileM * 128 + (size_t)bn * 128 * (dual ? 2 : 1);
+    int stages = (int)(kStageBudget / stage_bytes);
+    stages = stages > 8 ? 8 : stages;
+    F2S_LIMIT(stages >= 2, "tc_gemm: tile too large for shared memory");
+    g.stages = stages;
+    const size_t smem = 1024 + stages * stage_bytes + (2 * stages + 5) * 8 + 16;
+    const int tiles = ceil_div(op.rows, kTileM) * ceil_div(op.cols, bn);
+    const int grid = tiles < sm_count() ? tiles : sm_count();
+    TraceScope trace(op.tag, st);
+    if (op.tf32) {
+        switch (op.epilogue) {
+            case kEpiStore: return launch_tc<true, kEpiStore>(ma, mb, mb2, g, smem, grid, st);
+            case kEpiGatedResidual: return launch_tc<true, kEpiGatedResidual>(ma, mb, mb2, g, smem, grid, st);
+            case kEpiSwiGlu: return launch_tc<true, kEpiSwiGlu>(ma, mb, mb2, g, smem, grid, st);
+        }
+    } else {
+        switch (op.epilogue) {
+            case kEpiStore: return launch_tc<false, kEpiStore>(ma, mb, mb2, g, smem, grid, st);
+            case kEpiGatedResidual: return launch_tc<false, kEpiGatedResidual>(ma, mb, mb2, g, smem, grid, st);
+            case kEpiSwiGlu: return launch_tc<false, kEpiSwiGlu>(ma, mb, mb2, g, smem, grid, st);
+        }
+    }
+    return fail(F2S_ERR_INVALID_ARGUMENT, "tc_gemm: bad epilogue");
+}
+
+int tc_pick_bn(int cols, bool swiglu) {
+    static const int kCandidates[] = {256, 192, 128, 96, 64, 32};
+    int best = 32, best_waste = 1 << 30;
+    for (int bn : kCandidates) {
+        if (swiglu && bn > 128) continue;
+        const int waste = ceil_div(cols, bn) * bn - cols;
+        if (waste < best_waste) {
+            best = bn;
+            best_waste = waste;
+        }
+    }
+    return best;
+}
+
+}  // namespace f2s
+
+extern "C" int f2s_linear(const void* x, int ldx, const void* weight, const float* bias, float* y,
+                          int ldy, int rows, int cols, int K, int precision, void* stream) {
+    F2S_REQUIRE(rows >= 0 && cols >= 1 && K >= 1 && ldx >= K && ldy >= cols,
+                "linear: bad shape rows=%d cols=%d K=%d ldx=%d ldy=%d", rows, cols, K, ldx, ldy);
+    if (rows == 0) return F2S_OK;
+    F2S_REQUIRE(x && weight && y, "linear: null pointer");
+    cudaStream_t st = f2s::as_stream(stream);
+    if (precision == F2S_PRECISION_FP32) {
+        f2s::GemmArgs g{};
+        g.A = static_cast<const float*>(x);
+        g.lda = ldx;
+        g.W = static_cast<const float*>(weight);
+        g.bias = bias;
+        g.Y = y;
+        g.ldy = ldy;
+        g.rows = rows;
+        g.cols = cols;
+        g.K = K;
+        g.rows_per_patch = 1;
+        g.epilogue = f2s::kEpiStore;
+        g.tag = f2s::kTagGemmContent;
+        return f2s::gemm_f32(g, st);
+    }
+    F2S_REQUIRE(precision == F2S_PRECISION_TF32 || precision == F2S_PRECISION_BF16,
+                "linear: unknown precision %d", precision);
+    f2s::TcGemmOp op{};
+    op.A = x;
+    op.lda = ldx;
+    op.W = weight;
+    op.bias = bias;
+    op.Y = y;
+    op.ldy = ldy;
+    op.rows = rows;
+    op.cols = cols;
+    op.K = K;
+    op.bn = f2s::tc_pick_bn(cols, false);
+    op.tf32 = precision == F2S_PRECISION_TF32;
+    op.epilogue = f2s::kEpiStore;
+    op.rows_per_patch = 1;
+    op.tag = f2s::kTagGemmContent;
+    return f2s::tc_gemm(op, st);
+}
+
+extern "C" int f2s_device_error(int* value, int reset, void* stream) {
+    F2S_REQUIRE(value != nullptr, "device_error: null pointer");
+    int* word = f2s::device_error_word();
+    if (!word) return f2s::fail(F2S_ERR_CUDA, "device error word unavailable");
+    cudaStream_t st = f2s::as_stream(stream);
+    F2S_CUDA_TRY(cudaMemcpyAsync(value, word, sizeof(int), cudaMemcpyDeviceToHost, st));
+    F2S_CUDA_TRY(cudaStreamSynchronize(st));
+    if (reset) F2S_CUDA_TRY(cudaMemsetAsync(word, 0, sizeof(int), st));
+    return F2S_OK;
+}

@@ -53,6 +53,8 @@ SIGNATURES: dict[str, list] = {
     "f2s_nearest": [_p, _p, _i, _i, _i, _p, _p, _p, _p, _p, _sz, _p],
     "f2s_chamfer": [_p, _p, _i, _i, _i, _p, _p, _sz, _p],
     "f2s_chamfer_static": [_p, _p, _i, _i, _i, _p, _p],
+    "f2s_linear": [_p, _i, _p, _p, _p, _i, _i, _i, _i, _i, _p],
+    "f2s_device_error": [_p, _i, _p],
 }
 
 _RESTYPES = {"f2s_last_error": ctypes.c_char_p, "f2s_trace_tag_name": ctypes.c_char_p}
