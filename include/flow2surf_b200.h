@@ -155,6 +155,11 @@ typedef struct f2s_model_config {
     int32_t stage_dims[F2S_MAX_STAGES];      /* encoder_dims + [feat_dim]      */
     int32_t num_decoder;                     /* len(decoder_dims)              */
     int32_t decoder_dims[F2S_MAX_DECODER];   /* cfg["decoder_dims"]            */
+    int32_t precision;                       /* trunk and decoder contractions:
+                                                F2S_PRECISION_FP32 (CUDA cores) or
+                                                F2S_PRECISION_TF32 (tcgen05)   */
+    int32_t encoder_precision;               /* neighbour stages and projection
+                                                head, same choices             */
 } f2s_model_config;
 
 /*

@@ -106,5 +106,9 @@ struct EdgeArgs {
     int ldo;
 };
 int edge_stage_f32(const EdgeArgs& args, cudaStream_t stream);
+// The stage on tcgen05 tensor cores; `contrib_w` is the composed (cout x H)
+// projection in fp32 (tf32 = true) or bf16. F2S_ERR_UNSUPPORTED for shapes it
+// does not cover.
+int edge_stage_tc(const EdgeArgs& args, const void* contrib_w, bool tf32, cudaStream_t stream);
 
 }  // namespace f2s

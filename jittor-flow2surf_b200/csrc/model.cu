@@ -54,6 +54,8 @@ struct Dims {
     int K, C, NB, A, Hf, qk, S, ndec;
     int sd[kMaxStages], si[kMaxStages], dd[kMaxDecoder];
     int sum_stage, max_cout, max_dec;
+    int precision;      // trunk + decoder
+    int enc_precision;  // neighbour stages + projection head
 };
 
 int check_config(const f2s_model_config* cfg, Dims& d) {
@@ -86,6 +88,11 @@ int check_config(const f2s_model_config* cfg, Dims& d) {
         d.sum_stage += d.sd[s];
         d.max_cout = d.sd[s] > d.max_cout ? d.sd[s] : d.max_cout;
     }
+    d.precision = cfg->precision;
+    d.enc_precision = cfg->encoder_precision;
+    for (int p : {d.precision, d.enc_precision})
+        F2S_REQUIRE(p == F2S_PRECISION_FP32 || p == F2S_PRECISION_TF32,
+                    "model precision %d is not one of F2S_PRECISION_FP32 / F2S_PRECISION_TF32", p);
     d.ndec = cfg->num_decoder;
     F2S_REQUIRE(d.ndec >= 0 && d.ndec <= kMaxDecoder, "num_decoder %d outside [0, %d]", d.ndec,
                 kMaxDecoder);
@@ -297,6 +304,32 @@ GemmArgs gemm_args(const float* A, int lda, const float* W, const float* bias, f
     return g;
 }
 
+// One dense contraction of the forward at the configured precision: the fp32
+// CUDA-core kernel, or the tcgen05 kernel reading the fp32 operands as tf32.
+int linear_op(const GemmArgs& g, int precision, cudaStream_t st) {
+    if (precision == F2S_PRECISION_FP32) return gemm_f32(g, st);
+    TcGemmOp op{};
+    op.A = g.A;
+    op.lda = g.lda;
+    op.W = g.W;
+    op.W2 = g.W2;
+    op.bias = g.bias;
+    op.bias2 = g.bias2;
+    op.Y = g.Y;
+    op.ldy = g.ldy;
+    op.gate = g.gate;
+    op.gate_stride = g.gate_stride;
+    op.rows_per_patch = g.rows_per_patch;
+    op.rows = g.rows;
+    op.cols = g.cols;
+    op.K = g.K;
+    op.bn = tc_pick_bn(g.cols, g.epilogue == kEpiSwiGlu);
+    op.tf32 = true;
+    op.epilogue = g.epilogue;
+    op.tag = g.tag;
+    return tc_gemm(op, st);
+}
+
 int forward(const Dims& d, const Layout& L, const float* P, const float* x_in, const float* alpha,
             int B, int M, float* velocity, const Workspace& w, cudaStream_t st) {
     const int R = B * M;
@@ -340,9 +373,9 @@ int forward(const Dims& d, const Layout& L, const float* P, const float* x_in, c
     for (int s = 0; s < d.S; ++s) {
         const StageParams& sp = L.stage[s];
         const int cin = d.si[s], cout = d.sd[s];
-        F2S_TRY(gemm_f32(gemm_args(fin, ldin, P + sp.content_w, nullptr, w.content, 2 * cout, R,
-                                   2 * cout, cin),
-                         st));  // tag: gemm_content
+        F2S_TRY(linear_op(gemm_args(fin, ldin, P + sp.content_w, nullptr, w.content, 2 * cout, R,
+                                    2 * cout, cin),
+                          d.enc_precision, st));  // tag: gemm_content
         EdgeArgs ea{};
         ea.content = w.content;
         ea.ldc = 2 * cout;
@@ -364,7 +397,12 @@ int forward(const Dims& d, const Layout& L, const float* P, const float* x_in, c
         ea.ln_b = P + sp.ln_b;
         ea.out = w.cat + col;
         ea.ldo = d.sum_stage;
-        F2S_TRY(edge_stage_f32(ea, st));
+        int edge_status = F2S_ERR_UNSUPPORTED;
+        if (d.enc_precision == F2S_PRECISION_TF32)
+            edge_status = edge_stage_tc(ea, P + sp.contrib_w, true, st);
+        // shapes the tensor-core kernel does not take run on the CUDA-core kernel
+        if (edge_status == F2S_ERR_UNSUPPORTED) edge_status = edge_stage_f32(ea, st);
+        F2S_TRY(edge_status);
         fin = w.cat + col;
         ldin = d.sum_stage;
         col += cout;
@@ -374,7 +412,7 @@ int forward(const Dims& d, const Layout& L, const float* P, const float* x_in, c
         GemmArgs g = gemm_args(w.cat, d.sum_stage, P + L.proj_w, nullptr, w.x, C, R, C,
                                d.sum_stage);
         g.tag = kTagGemmHead;
-        F2S_TRY(gemm_f32(g, st));
+        F2S_TRY(linear_op(g, d.enc_precision, st));
     }
     F2S_TRY(ln_affine_leaky(w.x, C, P + L.proj_ln_w, P + L.proj_ln_b, R, C, st));
     // trunk (transformer.py:75-89)
@@ -386,7 +424,7 @@ int forward(const Dims& d, const Layout& L, const float* P, const float* x_in, c
         F2S_TRY(ln_modulate(w.x, C, w.h, C, mod, mstride, 0, C, R, M, C, st));
         GemmArgs gq = gemm_args(w.h, C, P + bp.qkv_w, nullptr, w.qkv, ld_qkv, R, ld_qkv, C);
         gq.tag = kTagGemmQkv;
-        F2S_TRY(gemm_f32(gq, st));
+        F2S_TRY(linear_op(gq, d.precision, st));
         F2S_TRY(qk_norm(w.qkv, ld_qkv, R, d.qk, st));
         F2S_TRY(attention_f32(w.qkv, w.qkv + d.qk, ld_qkv, w.qkv + 2 * d.qk, ld_qkv, w.h, C,
                               w.offs, C, w.colstats, B, M, d.qk, C, st));
@@ -396,21 +434,21 @@ int forward(const Dims& d, const Layout& L, const float* P, const float* x_in, c
         g.gate_stride = mstride;
         g.rows_per_patch = M;
         g.tag = kTagGemmProj;
-        F2S_TRY(gemm_f32(g, st));
+        F2S_TRY(linear_op(g, d.precision, st));
         F2S_TRY(ln_modulate(w.x, C, w.h, C, mod, mstride, 3 * C, 4 * C, R, M, C, st));
         GemmArgs sw = gemm_args(w.h, C, P + bp.gate_w, P + bp.gate_b, w.ffh, d.Hf, R, d.Hf, C);
         sw.epilogue = kEpiSwiGlu;
         sw.W2 = P + bp.ff1_w;
         sw.bias2 = P + bp.ff1_b;
         sw.tag = kTagGemmSwiGlu;
-        F2S_TRY(gemm_f32(sw, st));
+        F2S_TRY(linear_op(sw, d.precision, st));
         GemmArgs f2 = gemm_args(w.ffh, d.Hf, P + bp.ff2_w, P + bp.ff2_b, w.x, C, R, C, d.Hf);
         f2.epilogue = kEpiGatedResidual;
         f2.gate = mod + 5 * C;
         f2.gate_stride = mstride;
         f2.rows_per_patch = M;
         f2.tag = kTagGemmFf2;
-        F2S_TRY(gemm_f32(f2, st));
+        F2S_TRY(linear_op(f2, d.precision, st));
     }
     // decoder (decoder.py:8-32)
     const float* cur = w.x;
@@ -421,14 +459,14 @@ int forward(const Dims& d, const Layout& L, const float* P, const float* x_in, c
         GemmArgs gd = gemm_args(cur, in_dim, P + L.dec[i].w, nullptr, out, d.dd[i], R, d.dd[i],
                                 in_dim);
         gd.tag = kTagGemmDecoder;
-        F2S_TRY(gemm_f32(gd, st));
+        F2S_TRY(linear_op(gd, d.precision, st));
         F2S_TRY(ln_affine_leaky(out, d.dd[i], P + L.dec[i].ln_w, P + L.dec[i].ln_b, R, d.dd[i], st));
         cur = out;
         in_dim = d.dd[i];
     }
     GemmArgs go = gemm_args(cur, in_dim, P + L.dec_out_w, nullptr, velocity, 3, R, 3, in_dim);
     go.tag = kTagGemmDecoder;
-    return gemm_f32(go, st);
+    return linear_op(go, d.precision, st);
 }
 
 }  // namespace

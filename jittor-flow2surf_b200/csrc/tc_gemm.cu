@@ -192,42 +192,61 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     } else {
         // ---------------- epilogue (warps 2..5) ----------------
         const int quarter = warp & 3;
-        const int row_in_tile = quarter * 32 + lane;
+        float* stage_buf = reinterpret_cast<float*>(smem + (size_t)S * stage_bytes + 256) +
+                           (warp - 2) * 32 * 33;
         int iter = 0;
         for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++iter) {
             const int buf = iter & 1;
             const uint32_t tph = (uint32_t)(iter >> 1) & 1u;
-            if (!tc::mbar_wait(&tfull[buf], tph, g.err)) break;
+            // one lane waits, the warp follows it (tcgen05.ld is warp-collective)
+            int ready = 0;
+            if (lane == 0) ready = tc::mbar_wait(&tfull[buf], tph, g.err) ? 1 : 0;
+            if (!__shfl_sync(0xffffffffu, ready, 0)) break;
             tc::tc_fence_after();
             const int m0 = (tile / n_tiles_n) * kTileM;
             const int n0 = (tile % n_tiles_n) * g.bn;
-            const int row = m0 + row_in_tile;
+            const int row0 = m0 + quarter * 32;  // first of this warp's 32 rows
             const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) +
                                    (uint32_t)(buf * g.acc_cols);
             for (int c0 = 0; c0 < g.bn; c0 += 32) {
+                // thread = row in TMEM; through the staging buffer, lane = column
+                // for coalesced global access
                 float v[32];
-                float v2[32];
                 tc::tmem_ld32(t_row + (uint32_t)c0, v);
-                if constexpr (kDual) tc::tmem_ld32(t_row + (uint32_t)(g.bn + c0), v2);
-                if (row >= g.rows) continue;
+                if constexpr (kDual) {
+                    float v2[32];
+                    tc::tmem_ld32(t_row + (uint32_t)(g.bn + c0), v2);
 #pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const int col = n0 + c0 + i;
-                    if (col >= g.cols) continue;
-                    float out = epi_value(v[i], g.bias, col);
-                    if constexpr (kDual) out = f2s_silu(out) * epi_value(v2[i], g.bias2, col);
-                    const size_t o = (size_t)row * g.ldy + col;
-                    if (kEpi == kEpiGatedResidual) {
-                        const float gt =
-                            g.gate[(size_t)(row / g.rows_per_patch) * g.gate_stride + col];
-                        float* y = static_cast<float*>(g.Y) + o;
-                        *y = *y + gt * out;
-                    } else if (g.y_bf16) {
-                        static_cast<__nv_bfloat16*>(g.Y)[o] = __float2bfloat16_rn(out);
-                    } else {
-                        static_cast<float*>(g.Y)[o] = out;
+                    for (int i = 0; i < 32; ++i) {
+                        const int col = min(n0 + c0 + i, g.cols - 1);
+                        v[i] = f2s_silu(epi_value(v[i], g.bias, col)) *
+                               epi_value(v2[i], g.bias2, col);
                     }
                 }
+#pragma unroll
+                for (int i = 0; i < 32; ++i) stage_buf[lane * 33 + i] = v[i];
+                __syncwarp();
+                const int col = n0 + c0 + lane;
+                if (col < g.cols) {
+                    const float b = (!kDual && g.bias) ? g.bias[col] : 0.0f;
+                    for (int r = 0; r < 32; ++r) {
+                        const int row = row0 + r;
+                        if (row >= g.rows) break;
+                        const float out = stage_buf[r * 33 + lane] + b;
+                        const size_t o = (size_t)row * g.ldy + col;
+                        if (kEpi == kEpiGatedResidual) {
+                            const float gt =
+                                g.gate[(size_t)(row / g.rows_per_patch) * g.gate_stride + col];
+                            float* y = static_cast<float*>(g.Y) + o;
+                            *y = *y + gt * out;
+                        } else if (g.y_bf16) {
+                            static_cast<__nv_bfloat16*>(g.Y)[o] = __float2bfloat16_rn(out);
+                        } else {
+                            static_cast<float*>(g.Y)[o] = out;
+                        }
+                    }
+                }
+                __syncwarp();
             }
             tc::tc_fence_before();
             tc::mbar_arrive(&tempty[buf]);
@@ -261,7 +280,18 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-int* device_error_word() {
+template <bool kTf32, int kEpi>
+int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb2,
+              const TcGemmArgs& g, size_t smem, int grid, cudaStream_t st) {
+    auto kernel = tc_gemm_kernel<kTf32, kEpi>;
+    F2S_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    kernel<<<grid, kThreads, smem, st>>>(ma, mb, mb2, g);
+    return check_launch("tc_gemm_kernel");
+}
+
+}  // namespace
+
+int* tc_error_word() {
     static int* addr[64] = {nullptr};
     static std::mutex mu;
     int dev = 0;
@@ -274,17 +304,6 @@ int* device_error_word() {
     }
     return addr[dev];
 }
-
-template <bool kTf32, int kEpi>
-int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb2,
-              const TcGemmArgs& g, size_t smem, int grid, cudaStream_t st) {
-    auto kernel = tc_gemm_kernel<kTf32, kEpi>;
-    F2S_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    kernel<<<grid, kThreads, smem, st>>>(ma, mb, mb2, g);
-    return check_launch("tc_gemm_kernel");
-}
-
-}  // namespace
 
 int make_tensor_map_2d(CUtensorMap* map, const void* base, bool fp32, int64_t rows, int64_t cols,
                        int64_t ld, int box_rows, int box_cols) {
@@ -319,7 +338,7 @@ int tc_gemm(const TcGemmOp& op, cudaStream_t st) {
     int bn = op.bn;
     F2S_REQUIRE(bn >= 32 && bn <= 256 && bn % 32 == 0 && (!dual || bn <= 128),
                 "tc_gemm: bad N tile %d", bn);
-    int* err = device_error_word();
+    int* err = tc_error_word();
     if (!err) return fail(F2S_ERR_CUDA, "tc_gemm: device error word unavailable");
     CUtensorMap ma, mb, mb2;
     const int bk = op.tf32 ? 32 : 64;
@@ -350,7 +369,9 @@ int tc_gemm(const TcGemmOp& op, cudaStream_t st) {
     stages = stages > 8 ? 8 : stages;
     F2S_LIMIT(stages >= 2, "tc_gemm: tile too large for shared memory");
     g.stages = stages;
-    const size_t smem = 1024 + stages * stage_bytes + (2 * stages + 5) * 8 + 16;
+    // tiles, then barriers + TMEM slot (< 256 bytes for <= 8 stages), then the
+    // four epilogue warps' 32 x 33 staging buffers
+    const size_t smem = 1024 + stages * stage_bytes + 256 + 4 * 32 * 33 * sizeof(float);
     const int tiles = ceil_div(op.rows, kTileM) * ceil_div(op.cols, bn);
     const int grid = tiles < sm_count() ? tiles : sm_count();
     TraceScope trace(op.tag, st);
@@ -431,7 +452,7 @@ extern "C" int f2s_linear(const void* x, int ldx, const void* weight, const floa
 
 extern "C" int f2s_device_error(int* value, int reset, void* stream) {
     F2S_REQUIRE(value != nullptr, "device_error: null pointer");
-    int* word = f2s::device_error_word();
+    int* word = f2s::tc_error_word();
     if (!word) return f2s::fail(F2S_ERR_CUDA, "device error word unavailable");
     cudaStream_t st = f2s::as_stream(stream);
     F2S_CUDA_TRY(cudaMemcpyAsync(value, word, sizeof(int), cudaMemcpyDeviceToHost, st));

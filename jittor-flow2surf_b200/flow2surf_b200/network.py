@@ -33,11 +33,23 @@ class ModelConfig(ctypes.Structure):
         ("stage_dims", ctypes.c_int32 * MAX_STAGES),
         ("num_decoder", ctypes.c_int32),
         ("decoder_dims", ctypes.c_int32 * MAX_DECODER),
+        ("precision", ctypes.c_int32),
+        ("encoder_precision", ctypes.c_int32),
     ]
 
 
-def model_config(cfg: dict) -> ModelConfig:
+PRECISIONS = {"fp32": 0, "tf32": 1}
+"""Arithmetic of the dense contractions: fp32 CUDA-core kernels, or tcgen05
+tensor cores reading the fp32 operands as tf32."""
+
+
+def model_config(cfg: dict, precision: str = "fp32",
+                 encoder_precision: str | None = None) -> ModelConfig:
     d = model_dims(cfg)
+    encoder_precision = encoder_precision or precision
+    for p in (precision, encoder_precision):
+        if p not in PRECISIONS:
+            raise ValueError(f"precision must be one of {sorted(PRECISIONS)}, got {p!r}")
     if len(d.stage_dims) > MAX_STAGES or len(d.decoder_dims) > MAX_DECODER:
         raise ValueError("too many encoder or decoder layers for the kernels")
     c = ModelConfig()
@@ -49,6 +61,8 @@ def model_config(cfg: dict) -> ModelConfig:
     c.num_decoder = len(d.decoder_dims)
     for i, v in enumerate(d.decoder_dims):
         c.decoder_dims[i] = v
+    c.precision = PRECISIONS[precision]
+    c.encoder_precision = PRECISIONS[encoder_precision]
     return c
 
 
@@ -143,12 +157,15 @@ class Flow2SurfNet:
 
     def __init__(self, k: int = 32, feat_dim: int = 128, num_blocks: int = 3,
                  encoder_dims=(64, 64), alpha_dim: int = 192, ffn_ratio: int = 4,
-                 decoder_dims=(128, 64), seed: int = 0):
+                 decoder_dims=(128, 64), seed: int = 0, precision: str = "fp32",
+                 encoder_precision: str | None = None):
         self.cfg = {"k_neighbors": k, "feat_dim": feat_dim, "num_blocks": num_blocks,
                     "encoder_dims": list(encoder_dims), "alpha_dim": alpha_dim,
                     "ffn_ratio": ffn_ratio, "decoder_dims": list(decoder_dims)}
         model_dims(self.cfg)  # validates like the reference constructor
-        self._config = model_config(self.cfg)
+        self.precision = precision
+        self.encoder_precision = encoder_precision or precision
+        self._config = model_config(self.cfg, precision, self.encoder_precision)
         self._params = reference_init(self.cfg, seed)
         self._blob = None
         self._workspace = None
@@ -223,8 +240,12 @@ class Flow2SurfNet:
     execute = __call__
 
 
-def build_model(cfg: dict) -> Flow2SurfNet:
-    """flow2surf/models/network.py:85-95."""
+def build_model(cfg: dict, precision: str | None = None,
+                encoder_precision: str | None = None) -> Flow2SurfNet:
+    """flow2surf/models/network.py:85-95; `precision` (or cfg["precision"],
+    default "fp32") selects the arithmetic of the trunk and decoder
+    contractions, `encoder_precision` (default: the same) that of the
+    neighbour stages and projection head."""
     return Flow2SurfNet(
         k=cfg["k_neighbors"],
         feat_dim=cfg["feat_dim"],
@@ -233,4 +254,6 @@ def build_model(cfg: dict) -> Flow2SurfNet:
         alpha_dim=cfg["alpha_dim"],
         ffn_ratio=cfg["ffn_ratio"],
         decoder_dims=cfg["decoder_dims"],
+        precision=precision or cfg.get("precision", "fp32"),
+        encoder_precision=encoder_precision or cfg.get("encoder_precision"),
     )
