@@ -126,6 +126,10 @@ int f2s_neighbor_reduce(const float* content, const float* geometry, const int32
 #define F2S_PRECISION_FP32 0
 #define F2S_PRECISION_TF32 1
 #define F2S_PRECISION_BF16 2
+/* Operands split as x = hi + lo (both bf16) and contracted as
+ * hi*hi + hi*lo + lo*hi on tensor cores: close to fp32 accuracy. Accepted by
+ * the model's encoder_precision only. */
+#define F2S_PRECISION_BF16X3 3
 int f2s_linear(const void* x, int ldx, const void* weight, const float* bias, float* y, int ldy,
                int rows, int cols, int K, int precision, void* stream);
 
@@ -159,7 +163,10 @@ typedef struct f2s_model_config {
                                                 F2S_PRECISION_FP32 (CUDA cores) or
                                                 F2S_PRECISION_TF32 (tcgen05)   */
     int32_t encoder_precision;               /* neighbour stages and projection
-                                                head, same choices             */
+                                                head: the choices above or
+                                                F2S_PRECISION_BF16X3 (edge
+                                                contraction on split-bf16
+                                                tensor cores, the rest fp32) */
 } f2s_model_config;
 
 /*

@@ -96,7 +96,7 @@ __global__ void __launch_bounds__(256)
 attn_output_kernel(const float* __restrict__ q, const float* __restrict__ k, int ldqk,
                    const float* __restrict__ v, int ldv, const float* __restrict__ L,
                    const float* __restrict__ h, int ldh, float* __restrict__ out, int ldo,
-                   int N, int d, int C, int query_tiles) {
+                   int N, int d, int C, int query_tiles, bool round_tf32) {
     extern __shared__ __align__(16) float sm[];
     const int dp = d + 1;
     float* Qs = sm;                    // [TQ][dp]
@@ -182,7 +182,8 @@ attn_output_kernel(const float* __restrict__ q, const float* __restrict__ k, int
             const int c = tx + 16 * j;
             if (c >= C) continue;
             const float a = acc[i][j] * inv;
-            out[(base + r) * ldo + c] = h ? h[(base + r) * ldh + c] - a : a;
+            const float o = h ? h[(base + r) * ldh + c] - a : a;
+            out[(base + r) * ldo + c] = round_tf32 ? f2s_round_tf32(o) : o;
         }
     }
 }
@@ -190,7 +191,7 @@ attn_output_kernel(const float* __restrict__ q, const float* __restrict__ k, int
 template <int CJ>
 int launch_output(const float* q, const float* k, int ldqk, const float* v, int ldv,
                   const float* L, const float* h, int ldh, float* out, int ldo, int B, int N,
-                  int d, int C, cudaStream_t stream) {
+                  int d, int C, bool round_tf32, cudaStream_t stream) {
     const int dp = d + 1;
     const size_t smem = sizeof(float) * ((size_t)TQ * dp + TK * dp + (size_t)TK * C +
                                          TQ * (TK + 1) + TK);
@@ -200,7 +201,7 @@ int launch_output(const float* q, const float* k, int ldqk, const float* v, int 
     const int tiles = ceil_div(N, TQ);
     TraceScope trace(kTagAttnOutput, stream);
     kernel<<<B * tiles, 256, smem, stream>>>(q, k, ldqk, v, ldv, L, h, ldh, out, ldo, N, d, C,
-                                             tiles);
+                                             tiles, round_tf32);
     return check_launch("attn_output_kernel");
 }
 
@@ -208,7 +209,7 @@ int launch_output(const float* q, const float* k, int ldqk, const float* v, int 
 
 int attention_f32(const float* q, const float* k, int ldqk, const float* v, int ldv,
                   const float* h, int ldh, float* out, int ldo, float* colstats, int B, int N,
-                  int d, int C, cudaStream_t stream) {
+                  int d, int C, bool round_tf32, cudaStream_t stream) {
     if (B == 0 || N == 0) return F2S_OK;
     F2S_LIMIT(d >= 1 && d <= 128, "attention: query/key width %d outside [1, 128]", d);
     F2S_LIMIT(C >= 1 && C <= 256, "attention: value width %d outside [1, 256]", C);
@@ -224,10 +225,10 @@ int attention_f32(const float* q, const float* k, int ldqk, const float* v, int 
     F2S_TRY(check_launch("attn_colstats_kernel"));
     }
     const int cj = ceil_div(C, 16);
-    if (cj <= 4) return launch_output<4>(q, k, ldqk, v, ldv, colstats, h, ldh, out, ldo, B, N, d, C, stream);
-    if (cj <= 8) return launch_output<8>(q, k, ldqk, v, ldv, colstats, h, ldh, out, ldo, B, N, d, C, stream);
-    if (cj <= 12) return launch_output<12>(q, k, ldqk, v, ldv, colstats, h, ldh, out, ldo, B, N, d, C, stream);
-    return launch_output<16>(q, k, ldqk, v, ldv, colstats, h, ldh, out, ldo, B, N, d, C, stream);
+    if (cj <= 4) return launch_output<4>(q, k, ldqk, v, ldv, colstats, h, ldh, out, ldo, B, N, d, C, round_tf32, stream);
+    if (cj <= 8) return launch_output<8>(q, k, ldqk, v, ldv, colstats, h, ldh, out, ldo, B, N, d, C, round_tf32, stream);
+    if (cj <= 12) return launch_output<12>(q, k, ldqk, v, ldv, colstats, h, ldh, out, ldo, B, N, d, C, round_tf32, stream);
+    return launch_output<16>(q, k, ldqk, v, ldv, colstats, h, ldh, out, ldo, B, N, d, C, round_tf32, stream);
 }
 
 }  // namespace f2s

@@ -120,3 +120,12 @@ __device__ __forceinline__ float f2s_gelu_erf(float x) {
 __device__ __forceinline__ float f2s_silu(float x) { return x / (1.0f + expf(-x)); }
 
 __device__ __forceinline__ float f2s_leaky(float x) { return x > 0.0f ? x : 0.2f * x; }
+
+// Round to the nearest tf32 value (10-bit mantissa, ties away from zero).
+// Tensor cores read an fp32 operand as tf32 by dropping the low 13 mantissa
+// bits; rounding first makes that error unbiased and half as large.
+__device__ __forceinline__ float f2s_round_tf32(float x) {
+    uint32_t u = __float_as_uint(x);
+    if ((u & 0x7f800000u) != 0x7f800000u) u = (u + 0x1000u) & 0xffffe000u;
+    return __uint_as_float(u);
+}

@@ -22,6 +22,7 @@
 //      is a register butterfly across lanes that leaves lane = channel, so the
 //      output row is stored coalesced.
 #include <cfloat>
+#include <cstring>
 
 #include "kernels.cuh"
 #include "tc_common.cuh"
@@ -47,6 +48,7 @@ struct EdgeTcArgs {
     const float* hpe_ln_w;
     const float* hpe_ln_b;
     const float* contrib_b;
+    const float* contrib_w;  // fp32 (cout x H): converted in-kernel for the bf16 modes
     const float* ln_w;
     const float* ln_b;
     float* out;
@@ -65,20 +67,33 @@ __device__ __forceinline__ void fence_proxy_async() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-template <bool kTf32>
+// Operand modes of the edge contraction.
+enum EdgeMode : int {
+    kModeTf32 = 0,   // fp32 hidden rows and weights read as tf32
+    kModeBf16 = 1,   // bf16 hidden rows and weights
+    kModeSplit = 2,  // x = hi + lo with hi, lo bf16; hi*hi + hi*lo + lo*hi (3 MMAs)
+};
+
+template <int kMode>
 __global__ void __launch_bounds__(kThreads, 1)
 edge_tc_kernel(const __grid_constant__ CUtensorMap map_w, const EdgeTcArgs a) {
     extern __shared__ __align__(1024) unsigned char edge_smem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>(
         (reinterpret_cast<uintptr_t>(edge_smem_raw) + 1023) & ~uintptr_t(1023));
+    constexpr bool kTf32 = kMode == kModeTf32;
+    constexpr bool kSplit = kMode == kModeSplit;
     constexpr int kElem = kTf32 ? 4 : 2;
     constexpr int kBk = 128 / kElem;   // K elements per 128-byte row
     constexpr int kPer = 16 / kElem;   // elements per 16-byte chunk
     const int H = a.H, cout = a.cout, K = a.K;
     const int kblocks = (H + kBk - 1) / kBk;
-    unsigned char* sA = smem;                                     // kblocks x 16 KB
-    unsigned char* sB = sA + (size_t)kblocks * kRows * 128;       // kblocks x cout x 128
-    float* sW = reinterpret_cast<float*>(sB + (size_t)kblocks * cout * 128);  // H x 6
+    const size_t a_bytes = (size_t)kblocks * kRows * 128;
+    const size_t b_bytes = (size_t)kblocks * cout * 128;
+    unsigned char* sA = smem;                     // kblocks x 16 KB
+    unsigned char* sAlo = sA + a_bytes;           // split mode: low halves
+    unsigned char* sB = sAlo + (kSplit ? a_bytes : 0);
+    unsigned char* sBlo = sB + b_bytes;
+    float* sW = reinterpret_cast<float*>(sBlo + (kSplit ? b_bytes : 0));  // H x 6
     float* sHb = sW + H * 6;
     float* sHg = sHb + H;
     float* sHs = sHg + H;
@@ -121,11 +136,36 @@ edge_tc_kernel(const __grid_constant__ CUtensorMap map_w, const EdgeTcArgs a) {
     const uint32_t tmem_base = *tmem_slot;
 
     bool ok = true;
-    if (tid == 0) {
-        tc::mbar_arrive_expect_tx(&bars[0], (uint32_t)(kblocks * cout * 128));
-        for (int kb = 0; kb < kblocks; ++kb)
-            tc::tma_load_2d(sB + (size_t)kb * cout * 128, &map_w, &bars[0], kb * kBk, 0);
-        ok = tc::mbar_wait(&bars[0], 0, a.err);
+    if constexpr (kTf32) {
+        if (tid == 0) {
+            tc::mbar_arrive_expect_tx(&bars[0], (uint32_t)(kblocks * cout * 128));
+            for (int kb = 0; kb < kblocks; ++kb)
+                tc::tma_load_2d(sB + (size_t)kb * cout * 128, &map_w, &bars[0], kb * kBk, 0);
+            ok = tc::mbar_wait(&bars[0], 0, a.err);
+        }
+    } else {
+        // bf16 weights (and their residuals in split mode), swizzled like TMA would
+        const int chunks_per_row = H / 8;
+        for (int t = tid; t < cout * chunks_per_row; t += kThreads) {
+            const int n = t / chunks_per_row, q = t - n * chunks_per_row;
+            const float4 w0 = *reinterpret_cast<const float4*>(a.contrib_w + (size_t)n * H + q * 8);
+            const float4 w1 = *reinterpret_cast<const float4*>(a.contrib_w + (size_t)n * H + q * 8 + 4);
+            const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+            uint32_t hi[4], lo[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const __nv_bfloat162 h2 = __floats2bfloat162_rn(w[2 * e], w[2 * e + 1]);
+                const __nv_bfloat162 l2 = __floats2bfloat162_rn(
+                    w[2 * e] - __bfloat162float(h2.x), w[2 * e + 1] - __bfloat162float(h2.y));
+                hi[e] = *reinterpret_cast<const uint32_t*>(&h2);
+                lo[e] = *reinterpret_cast<const uint32_t*>(&l2);
+            }
+            const size_t off = (size_t)(q / 8) * cout * 128 + sw128_offset(n, q % 8);
+            *reinterpret_cast<uint4*>(sB + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+            if (kSplit) *reinterpret_cast<uint4*>(sBlo + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+        }
+        fence_proxy_async();
+        __syncthreads();
     }
 
     const int hper = H / kParts;
@@ -200,13 +240,22 @@ edge_tc_kernel(const __grid_constant__ CUtensorMap map_w, const EdgeTcArgs a) {
                     if constexpr (kTf32) {
                         *reinterpret_cast<float4*>(dst) = make_float4(o[0], o[1], o[2], o[3]);
                     } else {
-                        uint32_t w[4];
+                        uint32_t w[4], wl[4];
 #pragma unroll
                         for (int e = 0; e < 4; ++e) {
-                            __nv_bfloat162 b2 = __floats2bfloat162_rn(o[2 * e], o[2 * e + 1]);
-                            w[e] = *reinterpret_cast<uint32_t*>(&b2);
+                            const __nv_bfloat162 b2 = __floats2bfloat162_rn(o[2 * e], o[2 * e + 1]);
+                            w[e] = *reinterpret_cast<const uint32_t*>(&b2);
+                            if (kSplit) {
+                                const __nv_bfloat162 l2 = __floats2bfloat162_rn(
+                                    o[2 * e] - __bfloat162float(b2.x),
+                                    o[2 * e + 1] - __bfloat162float(b2.y));
+                                wl[e] = *reinterpret_cast<const uint32_t*>(&l2);
+                            }
                         }
                         *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+                        if (kSplit)
+                            *reinterpret_cast<uint4*>(dst + (sAlo - sA)) =
+                                make_uint4(wl[0], wl[1], wl[2], wl[3]);
                     }
                 }
             }
@@ -219,13 +268,20 @@ edge_tc_kernel(const __grid_constant__ CUtensorMap map_w, const EdgeTcArgs a) {
             tc::tc_fence_after();
             if (ok) {
                 const uint32_t a0 = tc::smem_u32(sA), b0 = tc::smem_u32(sB);
+                const uint32_t a_lo = tc::smem_u32(sAlo), b_lo = tc::smem_u32(sBlo);
                 for (int kb = 0; kb < kblocks; ++kb)
 #pragma unroll
                     for (int k = 0; k < 4; ++k) {
                         if ((kb * kBk + k * (32 / kElem)) >= H) break;
-                        const uint64_t da = tc::sw128_desc(a0 + kb * kRows * 128 + k * 32);
-                        const uint64_t db = tc::sw128_desc(b0 + kb * cout * 128 + k * 32);
+                        const uint32_t ao = kb * kRows * 128 + k * 32;
+                        const uint32_t bo = kb * cout * 128 + k * 32;
+                        const uint64_t da = tc::sw128_desc(a0 + ao);
+                        const uint64_t db = tc::sw128_desc(b0 + bo);
                         tc::umma<kTf32>(tmem_base, da, db, a.idesc, (kb | k) ? 1u : 0u);
+                        if (kSplit) {
+                            tc::umma<false>(tmem_base, da, tc::sw128_desc(b_lo + bo), a.idesc, 1u);
+                            tc::umma<false>(tmem_base, tc::sw128_desc(a_lo + ao), db, a.idesc, 1u);
+                        }
                     }
             }
             tc::umma_commit(&bars[1]);
@@ -334,23 +390,32 @@ edge_tc_kernel(const __grid_constant__ CUtensorMap map_w, const EdgeTcArgs a) {
 
 }  // namespace
 
-// Tensor-core edge stage; returns F2S_ERR_UNSUPPORTED for shapes it does not
-// cover (the caller then uses the CUDA-core kernel).
-int edge_stage_tc(const EdgeArgs& e, const void* contrib_w, bool tf32, cudaStream_t st) {
+// Tensor-core edge stage at `precision` (F2S_PRECISION_TF32, _BF16 or
+// _BF16X3); returns F2S_ERR_UNSUPPORTED for shapes it does not cover (the
+// caller then uses the CUDA-core kernel).
+int edge_stage_tc(const EdgeArgs& e, int precision, cudaStream_t st) {
     if (e.B == 0 || e.M == 0) return F2S_OK;
     int log2K = 0;
     while ((1 << log2K) < e.K) ++log2K;
     if (e.geometry != nullptr || e.xyz4 == nullptr || e.D != 6 || e.H > kParts * kMaxPer ||
         e.H % 32 != 0 || e.cout % 32 != 0 || e.cout > 256 || (1 << log2K) != e.K || e.K > 32 ||
-        ((uintptr_t)e.content & 15) != 0 || e.ldc % 4 != 0)
+        ((uintptr_t)e.content & 15) != 0 || e.ldc % 4 != 0 || ((uintptr_t)e.contrib_w & 15) != 0)
         return fail(F2S_ERR_UNSUPPORTED, "edge stage shape outside the tensor-core kernel");
+    const int mode = precision == F2S_PRECISION_TF32   ? kModeTf32
+                     : precision == F2S_PRECISION_BF16 ? kModeBf16
+                                                       : kModeSplit;
+    F2S_REQUIRE(precision == F2S_PRECISION_TF32 || precision == F2S_PRECISION_BF16 ||
+                    precision == F2S_PRECISION_BF16X3,
+                "edge_tc: precision %d", precision);
     int* err = tc_error_word();
     if (!err) return fail(F2S_ERR_CUDA, "edge_tc: device error word unavailable");
+    const bool tf32 = mode == kModeTf32;
     const int elem = tf32 ? 4 : 2;
     const int bk = 128 / elem;
     const int kblocks = ceil_div(e.H, bk);
     CUtensorMap map;
-    F2S_TRY(make_tensor_map_2d(&map, contrib_w, tf32, e.cout, e.H, e.H, e.cout, bk));
+    if (tf32) F2S_TRY(make_tensor_map_2d(&map, e.contrib_w, true, e.cout, e.H, e.H, e.cout, bk));
+    else memset(&map, 0, sizeof(map));
     EdgeTcArgs a{};
     a.content = e.content;
     a.ldc = e.ldc;
@@ -368,13 +433,16 @@ int edge_stage_tc(const EdgeArgs& e, const void* contrib_w, bool tf32, cudaStrea
     a.hpe_ln_w = e.hpe_ln_w;
     a.hpe_ln_b = e.hpe_ln_b;
     a.contrib_b = e.contrib_b;
+    a.contrib_w = e.contrib_w;
     a.ln_w = e.ln_w;
     a.ln_b = e.ln_b;
     a.out = e.out;
     a.ldo = e.ldo;
     a.idesc = tc::make_idesc(kRows, e.cout, tf32 ? 2u : 1u);
     a.err = err;
-    const size_t smem = 1024 + (size_t)kblocks * kRows * 128 + (size_t)kblocks * e.cout * 128 +
+    const size_t copies = mode == kModeSplit ? 2 : 1;
+    const size_t smem = 1024 + copies * ((size_t)kblocks * kRows * 128 +
+                                         (size_t)kblocks * e.cout * 128) +
                         sizeof(float) * ((size_t)e.H * 9 + (size_t)e.cout * 3 + 2 * kParts * kRows) +
                         sizeof(int) * kRows + 64;
     F2S_LIMIT(smem <= 227 * 1024, "edge_tc: %zu bytes of shared memory", smem);
@@ -382,16 +450,15 @@ int edge_stage_tc(const EdgeArgs& e, const void* contrib_w, bool tf32, cudaStrea
     const int tiles = ceil_div(R, a.ppt);
     const int grid = tiles < sm_count() ? tiles : sm_count();
     TraceScope trace(kTagEdge, st);
-    if (tf32) {
-        F2S_CUDA_TRY(cudaFuncSetAttribute(edge_tc_kernel<true>,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        edge_tc_kernel<true><<<grid, kThreads, smem, st>>>(map, a);
-    } else {
-        F2S_CUDA_TRY(cudaFuncSetAttribute(edge_tc_kernel<false>,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        edge_tc_kernel<false><<<grid, kThreads, smem, st>>>(map, a);
-    }
-    return check_launch("edge_tc_kernel");
+    auto launch = [&](auto kernel) -> int {
+        F2S_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)smem));
+        kernel<<<grid, kThreads, smem, st>>>(map, a);
+        return check_launch("edge_tc_kernel");
+    };
+    if (mode == kModeTf32) return launch(edge_tc_kernel<kModeTf32>);
+    if (mode == kModeBf16) return launch(edge_tc_kernel<kModeBf16>);
+    return launch(edge_tc_kernel<kModeSplit>);
 }
 
 }  // namespace f2s

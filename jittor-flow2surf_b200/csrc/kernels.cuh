@@ -33,6 +33,7 @@ struct GemmArgs {
     int rows, cols, K;
     GemmEpilogue epilogue;
     int tag;               // TraceTag of this launch
+    bool round_tf32;       // tensor-core path: round fp32 outputs to the nearest tf32
 };
 int gemm_f32(const GemmArgs& args, cudaStream_t stream);
 
@@ -55,6 +56,7 @@ struct TcGemmOp {
     int rows, cols, K;
     int bn;                  // N tile: multiple of 32, <= 256 (<= 128 for SwiGLU)
     bool tf32;
+    bool round_tf32;         // round fp32 outputs to the nearest tf32
     GemmEpilogue epilogue;
     int tag;
 };
@@ -64,12 +66,13 @@ int tc_pick_bn(int cols, bool swiglu);
 
 // ---- rownorm.cu ----
 // h = LN(x) * (1 + scale[p]) + shift[p]; LN two-pass over C, eps 1e-6.
+// round_tf32: round the output to the nearest tf32 (it feeds a tf32 GEMM).
 int ln_modulate(const float* x, int ldx, float* h, int ldh, const float* mod, int mod_stride,
                 int scale_off, int shift_off, int rows, int rows_per_patch, int C,
-                cudaStream_t stream);
+                bool round_tf32, cudaStream_t stream);
 // y = LeakyReLU_0.2(LN(y) * gamma + beta) in place (two-pass, eps 1e-6).
 int ln_affine_leaky(float* y, int ldy, const float* gamma, const float* beta, int rows, int C,
-                    cudaStream_t stream);
+                    bool round_tf32, cudaStream_t stream);
 // LN (no affine, eps 1e-6) of columns [0, d) and [d, 2d) of each row, in place.
 int qk_norm(float* qkv, int ld, int rows, int d, cudaStream_t stream);
 
@@ -79,7 +82,7 @@ int qk_norm(float* qkv, int ld, int rows, int d, cudaStream_t stream);
 // B*N floats of scratch (per-key log-sum-exp over queries).
 int attention_f32(const float* q, const float* k, int ldqk, const float* v, int ldv,
                   const float* h, int ldh, float* out, int ldo, float* colstats, int B, int N,
-                  int d, int C, cudaStream_t stream);
+                  int d, int C, bool round_tf32, cudaStream_t stream);
 
 // ---- edge.cu ----
 // Fused neighbour stage: per edge (i, j = idx[i, k]) the HPE hidden
@@ -106,9 +109,9 @@ struct EdgeArgs {
     int ldo;
 };
 int edge_stage_f32(const EdgeArgs& args, cudaStream_t stream);
-// The stage on tcgen05 tensor cores; `contrib_w` is the composed (cout x H)
-// projection in fp32 (tf32 = true) or bf16. F2S_ERR_UNSUPPORTED for shapes it
+// The stage on tcgen05 tensor cores at F2S_PRECISION_TF32, _BF16 or _BF16X3
+// (args.contrib_w is fp32 in every case). F2S_ERR_UNSUPPORTED for shapes it
 // does not cover.
-int edge_stage_tc(const EdgeArgs& args, const void* contrib_w, bool tf32, cudaStream_t stream);
+int edge_stage_tc(const EdgeArgs& args, int precision, cudaStream_t stream);
 
 }  // namespace f2s

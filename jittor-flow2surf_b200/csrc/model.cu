@@ -56,6 +56,7 @@ struct Dims {
     int sum_stage, max_cout, max_dec;
     int precision;      // trunk + decoder
     int enc_precision;  // neighbour stages + projection head
+    int enc_gemm_precision;
 };
 
 int check_config(const f2s_model_config* cfg, Dims& d) {
@@ -90,9 +91,16 @@ int check_config(const f2s_model_config* cfg, Dims& d) {
     }
     d.precision = cfg->precision;
     d.enc_precision = cfg->encoder_precision;
-    for (int p : {d.precision, d.enc_precision})
-        F2S_REQUIRE(p == F2S_PRECISION_FP32 || p == F2S_PRECISION_TF32,
-                    "model precision %d is not one of F2S_PRECISION_FP32 / F2S_PRECISION_TF32", p);
+    F2S_REQUIRE(d.precision == F2S_PRECISION_FP32 || d.precision == F2S_PRECISION_TF32,
+                "trunk precision %d is not F2S_PRECISION_FP32 or F2S_PRECISION_TF32",
+                d.precision);
+    F2S_REQUIRE(d.enc_precision == F2S_PRECISION_FP32 || d.enc_precision == F2S_PRECISION_TF32 ||
+                    d.enc_precision == F2S_PRECISION_BF16X3,
+                "encoder precision %d is not F2S_PRECISION_FP32, _TF32 or _BF16X3",
+                d.enc_precision);
+    // the encoder's plain GEMMs have no split-bf16 form: fp32 CUDA cores there
+    d.enc_gemm_precision =
+        d.enc_precision == F2S_PRECISION_TF32 ? F2S_PRECISION_TF32 : F2S_PRECISION_FP32;
     d.ndec = cfg->num_decoder;
     F2S_REQUIRE(d.ndec >= 0 && d.ndec <= kMaxDecoder, "num_decoder %d outside [0, %d]", d.ndec,
                 kMaxDecoder);
@@ -325,6 +333,7 @@ int linear_op(const GemmArgs& g, int precision, cudaStream_t st) {
     op.K = g.K;
     op.bn = tc_pick_bn(g.cols, g.epilogue == kEpiSwiGlu);
     op.tf32 = true;
+    op.round_tf32 = g.round_tf32;
     op.epilogue = g.epilogue;
     op.tag = g.tag;
     return tc_gemm(op, st);
@@ -375,7 +384,7 @@ int forward(const Dims& d, const Layout& L, const float* P, const float* x_in, c
         const int cin = d.si[s], cout = d.sd[s];
         F2S_TRY(linear_op(gemm_args(fin, ldin, P + sp.content_w, nullptr, w.content, 2 * cout, R,
                                     2 * cout, cin),
-                          d.enc_precision, st));  // tag: gemm_content
+                          d.enc_gemm_precision, st));  // tag: gemm_content
         EdgeArgs ea{};
         ea.content = w.content;
         ea.ldc = 2 * cout;
@@ -398,8 +407,8 @@ int forward(const Dims& d, const Layout& L, const float* P, const float* x_in, c
         ea.out = w.cat + col;
         ea.ldo = d.sum_stage;
         int edge_status = F2S_ERR_UNSUPPORTED;
-        if (d.enc_precision == F2S_PRECISION_TF32)
-            edge_status = edge_stage_tc(ea, P + sp.contrib_w, true, st);
+        if (d.enc_precision != F2S_PRECISION_FP32)
+            edge_status = edge_stage_tc(ea, d.enc_precision, st);
         // shapes the tensor-core kernel does not take run on the CUDA-core kernel
         if (edge_status == F2S_ERR_UNSUPPORTED) edge_status = edge_stage_f32(ea, st);
         F2S_TRY(edge_status);
@@ -412,22 +421,24 @@ int forward(const Dims& d, const Layout& L, const float* P, const float* x_in, c
         GemmArgs g = gemm_args(w.cat, d.sum_stage, P + L.proj_w, nullptr, w.x, C, R, C,
                                d.sum_stage);
         g.tag = kTagGemmHead;
-        F2S_TRY(linear_op(g, d.enc_precision, st));
+        F2S_TRY(linear_op(g, d.enc_gemm_precision, st));
     }
-    F2S_TRY(ln_affine_leaky(w.x, C, P + L.proj_ln_w, P + L.proj_ln_b, R, C, st));
+    F2S_TRY(ln_affine_leaky(w.x, C, P + L.proj_ln_w, P + L.proj_ln_b, R, C, false, st));
     // trunk (transformer.py:75-89)
     const int ld_qkv = C + 2 * d.qk;
+    // operands of tf32 contractions are rounded to the nearest tf32 where made
+    const bool tf32_trunk = d.precision == F2S_PRECISION_TF32;
     const int mstride = d.NB * 6 * C;
     for (int i = 0; i < d.NB; ++i) {
         const BlockParams& bp = L.block[i];
         const float* mod = w.mod + (size_t)i * 6 * C;
-        F2S_TRY(ln_modulate(w.x, C, w.h, C, mod, mstride, 0, C, R, M, C, st));
+        F2S_TRY(ln_modulate(w.x, C, w.h, C, mod, mstride, 0, C, R, M, C, tf32_trunk, st));
         GemmArgs gq = gemm_args(w.h, C, P + bp.qkv_w, nullptr, w.qkv, ld_qkv, R, ld_qkv, C);
         gq.tag = kTagGemmQkv;
         F2S_TRY(linear_op(gq, d.precision, st));
         F2S_TRY(qk_norm(w.qkv, ld_qkv, R, d.qk, st));
         F2S_TRY(attention_f32(w.qkv, w.qkv + d.qk, ld_qkv, w.qkv + 2 * d.qk, ld_qkv, w.h, C,
-                              w.offs, C, w.colstats, B, M, d.qk, C, st));
+                              w.offs, C, w.colstats, B, M, d.qk, C, tf32_trunk, st));
         GemmArgs g = gemm_args(w.offs, C, P + bp.proj_w, nullptr, w.x, C, R, C, C);
         g.epilogue = kEpiGatedResidual;
         g.gate = mod + 2 * C;
@@ -435,12 +446,13 @@ int forward(const Dims& d, const Layout& L, const float* P, const float* x_in, c
         g.rows_per_patch = M;
         g.tag = kTagGemmProj;
         F2S_TRY(linear_op(g, d.precision, st));
-        F2S_TRY(ln_modulate(w.x, C, w.h, C, mod, mstride, 3 * C, 4 * C, R, M, C, st));
+        F2S_TRY(ln_modulate(w.x, C, w.h, C, mod, mstride, 3 * C, 4 * C, R, M, C, tf32_trunk, st));
         GemmArgs sw = gemm_args(w.h, C, P + bp.gate_w, P + bp.gate_b, w.ffh, d.Hf, R, d.Hf, C);
         sw.epilogue = kEpiSwiGlu;
         sw.W2 = P + bp.ff1_w;
         sw.bias2 = P + bp.ff1_b;
         sw.tag = kTagGemmSwiGlu;
+        sw.round_tf32 = tf32_trunk;
         F2S_TRY(linear_op(sw, d.precision, st));
         GemmArgs f2 = gemm_args(w.ffh, d.Hf, P + bp.ff2_w, P + bp.ff2_b, w.x, C, R, C, d.Hf);
         f2.epilogue = kEpiGatedResidual;
@@ -460,7 +472,8 @@ int forward(const Dims& d, const Layout& L, const float* P, const float* x_in, c
                                 in_dim);
         gd.tag = kTagGemmDecoder;
         F2S_TRY(linear_op(gd, d.precision, st));
-        F2S_TRY(ln_affine_leaky(out, d.dd[i], P + L.dec[i].ln_w, P + L.dec[i].ln_b, R, d.dd[i], st));
+        F2S_TRY(ln_affine_leaky(out, d.dd[i], P + L.dec[i].ln_w, P + L.dec[i].ln_b, R, d.dd[i],
+                                tf32_trunk, st));
         cur = out;
         in_dim = d.dd[i];
     }
@@ -596,5 +609,5 @@ extern "C" int f2s_offset_attention(const float* query, const float* key, const 
     float* colstats = key_pm + (size_t)B * N * d;             // (B*N)
     F2S_TRY(transpose_batched(key, key_pm, B, d, N, st));
     return attention_f32(query, key_pm, d, value, C, nullptr, 0, out, C, colstats, B, N, d, C,
-                         st);
+                         false, st);
 }

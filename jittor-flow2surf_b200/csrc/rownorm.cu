@@ -23,7 +23,7 @@ __device__ __forceinline__ void row_stats(const float* x, int C, int lane, float
 __global__ void ln_modulate_kernel(const float* __restrict__ x, int ldx, float* __restrict__ h,
                                    int ldh, const float* __restrict__ mod, int mod_stride,
                                    int scale_off, int shift_off, int rows, int rows_per_patch,
-                                   int C) {
+                                   int C, bool round_tf32) {
     const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (row >= rows) return;
@@ -32,22 +32,27 @@ __global__ void ln_modulate_kernel(const float* __restrict__ x, int ldx, float* 
     row_stats(xr, C, lane, mean, rstd);
     const float* m = mod + (size_t)(row / rows_per_patch) * mod_stride;
     float* hr = h + (size_t)row * ldh;
-    for (int c = lane; c < C; c += 32)
-        hr[c] = (xr[c] - mean) * rstd * (1.0f + m[scale_off + c]) + m[shift_off + c];
+    for (int c = lane; c < C; c += 32) {
+        const float v = (xr[c] - mean) * rstd * (1.0f + m[scale_off + c]) + m[shift_off + c];
+        hr[c] = round_tf32 ? f2s_round_tf32(v) : v;
+    }
 }
 
 // Affine ChannelLayerNorm + LeakyReLU(0.2) (encoder.py:118-123, decoder.py:18-22).
 __global__ void ln_affine_leaky_kernel(float* __restrict__ y, int ldy,
                                        const float* __restrict__ gamma,
-                                       const float* __restrict__ beta, int rows, int C) {
+                                       const float* __restrict__ beta, int rows, int C,
+                                       bool round_tf32) {
     const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (row >= rows) return;
     float* yr = y + (size_t)row * ldy;
     float mean, rstd;
     row_stats(yr, C, lane, mean, rstd);
-    for (int c = lane; c < C; c += 32)
-        yr[c] = f2s_leaky((yr[c] - mean) * rstd * gamma[c] + beta[c]);
+    for (int c = lane; c < C; c += 32) {
+        const float v = f2s_leaky((yr[c] - mean) * rstd * gamma[c] + beta[c]);
+        yr[c] = round_tf32 ? f2s_round_tf32(v) : v;
+    }
 }
 
 // qk_norm on the query and key blocks of qkv (transformer.py:59-63).
@@ -69,20 +74,20 @@ constexpr int kRowsPerCta = 8;
 
 int ln_modulate(const float* x, int ldx, float* h, int ldh, const float* mod, int mod_stride,
                 int scale_off, int shift_off, int rows, int rows_per_patch, int C,
-                cudaStream_t stream) {
+                bool round_tf32, cudaStream_t stream) {
     if (rows == 0) return F2S_OK;
     TraceScope trace(kTagRowNorm, stream);
     ln_modulate_kernel<<<ceil_div(rows, kRowsPerCta), kRowsPerCta * 32, 0, stream>>>(
-        x, ldx, h, ldh, mod, mod_stride, scale_off, shift_off, rows, rows_per_patch, C);
+        x, ldx, h, ldh, mod, mod_stride, scale_off, shift_off, rows, rows_per_patch, C, round_tf32);
     return check_launch("ln_modulate_kernel");
 }
 
 int ln_affine_leaky(float* y, int ldy, const float* gamma, const float* beta, int rows, int C,
-                    cudaStream_t stream) {
+                    bool round_tf32, cudaStream_t stream) {
     if (rows == 0) return F2S_OK;
     TraceScope trace(kTagRowNorm, stream);
     ln_affine_leaky_kernel<<<ceil_div(rows, kRowsPerCta), kRowsPerCta * 32, 0, stream>>>(
-        y, ldy, gamma, beta, rows, C);
+        y, ldy, gamma, beta, rows, C, round_tf32);
     return check_launch("ln_affine_leaky_kernel");
 }
 

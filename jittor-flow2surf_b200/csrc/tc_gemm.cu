@@ -46,6 +46,7 @@ struct TcGemmArgs {
     const float* gate;
     int gate_stride;
     int rows_per_patch;
+    int round_tf32;
     int* err;
 };
 
@@ -242,7 +243,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                         } else if (g.y_bf16) {
                             static_cast<__nv_bfloat16*>(g.Y)[o] = __float2bfloat16_rn(out);
                         } else {
-                            static_cast<float*>(g.Y)[o] = out;
+                            static_cast<float*>(g.Y)[o] = g.round_tf32 ? f2s_round_tf32(out) : out;
                         }
                     }
                 }
@@ -363,6 +364,7 @@ int tc_gemm(const TcGemmOp& op, cudaStream_t st) {
     g.gate = op.gate;
     g.gate_stride = op.gate_stride;
     g.rows_per_patch = op.rows_per_patch > 0 ? op.rows_per_patch : 1;
+    g.round_tf32 = op.round_tf32 ? 1 : 0;
     g.err = err;
     const size_t stage_bytes = (size_t)kTileM * 128 + (size_t)bn * 128 * (dual ? 2 : 1);
     int stages = (int)(kStageBudget / stage_bytes);

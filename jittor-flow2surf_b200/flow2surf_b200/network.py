@@ -38,9 +38,10 @@ class ModelConfig(ctypes.Structure):
     ]
 
 
-PRECISIONS = {"fp32": 0, "tf32": 1}
-"""Arithmetic of the dense contractions: fp32 CUDA-core kernels, or tcgen05
-tensor cores reading the fp32 operands as tf32."""
+PRECISIONS = {"fp32": 0, "tf32": 1, "bf16x3": 3}
+"""Arithmetic of the dense contractions: fp32 CUDA-core kernels, tcgen05
+tensor cores reading the fp32 operands as tf32, or (encoder only) tensor cores
+on operands split into two bf16 halves (hi*hi + hi*lo + lo*hi)."""
 
 
 def model_config(cfg: dict, precision: str = "fp32",
@@ -71,11 +72,25 @@ def _w2(w):
     return np.asarray(w).reshape(w.shape[0], w.shape[1])
 
 
-def composed_segments(cfg: dict, p: dict) -> list[np.ndarray]:
+def round_tf32(a) -> np.ndarray:
+    """Nearest tf32 value (10-bit mantissa, ties away from zero) of each
+    element, as float32: tensor cores read fp32 operands by dropping the low
+    13 mantissa bits, so operands rounded first carry unbiased error."""
+    u = np.ascontiguousarray(a, dtype=np.float32).view(np.uint32).copy()
+    finite = (u & 0x7F800000) != 0x7F800000
+    u[finite] = (u[finite] + 0x1000) & 0xFFFFE000
+    return u.view(np.float32)
+
+
+def composed_segments(cfg: dict, p: dict, trunk_tf32: bool = False,
+                      encoder_tf32: bool = False) -> list[np.ndarray]:
     """Parameter segments in blob order, with the reference's exact
-    factorisations (flow2surf/models/encoder.py:88-101)."""
+    factorisations (flow2surf/models/encoder.py:88-101). Weights that a tf32
+    tensor-core contraction reads are rounded to the nearest tf32."""
     d = model_dims(cfg)
     f32 = lambda a: np.asarray(a, dtype=np.float32)  # noqa: E731
+    enc = round_tf32 if encoder_tf32 else f32
+    trk = round_tf32 if trunk_tf32 else f32
     segs = [p["alpha_emb.mlp.0.weight"], p["alpha_emb.mlp.0.bias"],
             p["alpha_emb.mlp.2.weight"], p["alpha_emb.mlp.2.bias"]]
     pre = "local_encoder.input_embed.net"
@@ -89,28 +104,30 @@ def composed_segments(cfg: dict, p: dict) -> list[np.ndarray]:
         pos64 = pos.astype(np.float64)
         contrib_w = pos64 @ np.asarray(p[f"{pre}.position_embed.net.3.weight"], np.float64)
         contrib_b = pos64 @ np.asarray(p[f"{pre}.position_embed.net.3.bias"], np.float64)
-        segs += [content, p[f"{pre}.position_embed.net.0.weight"],
+        segs += [enc(content), p[f"{pre}.position_embed.net.0.weight"],
                  p[f"{pre}.position_embed.net.0.bias"], p[f"{pre}.position_embed.net.1.weight"],
-                 p[f"{pre}.position_embed.net.1.bias"], contrib_w, contrib_b,
+                 p[f"{pre}.position_embed.net.1.bias"], enc(contrib_w), contrib_b,
                  p[f"{pre}.norm.weight"], p[f"{pre}.norm.bias"]]
-    segs += [_w2(p["local_encoder.proj.0.weight"]), p["local_encoder.proj.1.weight"],
+    segs += [enc(_w2(p["local_encoder.proj.0.weight"])), p["local_encoder.proj.1.weight"],
              p["local_encoder.proj.1.bias"]]
     for i in range(d.num_blocks):
         pre = f"blocks.{i}"
-        segs += [p[f"{pre}.mod.1.weight"], p[f"{pre}.mod.1.bias"], _w2(p[f"{pre}.qkv_conv.weight"]),
-                 _w2(p[f"{pre}.proj.weight"]), _w2(p[f"{pre}.ff_gate.weight"]),
-                 p[f"{pre}.ff_gate.bias"], _w2(p[f"{pre}.ff1.weight"]), p[f"{pre}.ff1.bias"],
-                 _w2(p[f"{pre}.ff2.weight"]), p[f"{pre}.ff2.bias"]]
+        segs += [p[f"{pre}.mod.1.weight"], p[f"{pre}.mod.1.bias"],
+                 trk(_w2(p[f"{pre}.qkv_conv.weight"])), trk(_w2(p[f"{pre}.proj.weight"])),
+                 trk(_w2(p[f"{pre}.ff_gate.weight"])), p[f"{pre}.ff_gate.bias"],
+                 trk(_w2(p[f"{pre}.ff1.weight"])), p[f"{pre}.ff1.bias"],
+                 trk(_w2(p[f"{pre}.ff2.weight"])), p[f"{pre}.ff2.bias"]]
     layer = 0
     for _ in d.decoder_dims:
-        segs += [_w2(p[f"decoder.net.{layer}.weight"]), p[f"decoder.net.{layer + 1}.weight"],
+        segs += [trk(_w2(p[f"decoder.net.{layer}.weight"])), p[f"decoder.net.{layer + 1}.weight"],
                  p[f"decoder.net.{layer + 1}.bias"]]
         layer += 3
-    segs.append(_w2(p[f"decoder.net.{layer}.weight"]))
+    segs.append(trk(_w2(p[f"decoder.net.{layer}.weight"])))
     return [f32(s) for s in segs]
 
 
-def pack_parameters(cfg: dict, params: dict) -> np.ndarray:
+def pack_parameters(cfg: dict, params: dict, trunk_tf32: bool = False,
+                    encoder_tf32: bool = False) -> np.ndarray:
     """Host float32 blob laid out as f2s_model_param_segments reports."""
     c = model_config(cfg)
     total = ctypes.c_int64()
@@ -120,7 +137,7 @@ def pack_parameters(cfg: dict, params: dict) -> np.ndarray:
     offsets = (ctypes.c_int64 * n)()
     sizes = (ctypes.c_int64 * n)()
     _lib.lib().f2s_model_param_segments(ctypes.byref(c), offsets, sizes, n, ctypes.byref(total))
-    segs = composed_segments(cfg, params)
+    segs = composed_segments(cfg, params, trunk_tf32, encoder_tf32)
     if len(segs) != n:
         raise RuntimeError(f"blob layout mismatch: {len(segs)} segments vs {n}")
     blob = np.zeros(total.value, dtype=np.float32)
@@ -193,7 +210,9 @@ class Flow2SurfNet:
 
     def device_blob(self, device) -> torch.Tensor:
         if self._blob is None or self._blob.device != torch.device(device):
-            host = pack_parameters(self.cfg, self._params)
+            host = pack_parameters(self.cfg, self._params,
+                                   trunk_tf32=self.precision == "tf32",
+                                   encoder_tf32=self.encoder_precision == "tf32")
             self._blob = torch.from_numpy(host).to(device)
         return self._blob
 

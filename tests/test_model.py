@@ -28,8 +28,8 @@ def patches_from_cloud(cloud, count, size, seed):
     return np.ascontiguousarray(np.stack(out), dtype=np.float32)
 
 
-def gpu_forward(cfg, params, x, alpha):
-    model = build_model(cfg)
+def gpu_forward(cfg, params, x, alpha, precision="fp32", encoder_precision=None):
+    model = build_model(cfg, precision=precision, encoder_precision=encoder_precision)
     model.load_parameters(params)
     v = model(torch.from_numpy(x).cuda(), torch.from_numpy(alpha).cuda())
     return v.cpu().numpy()
@@ -58,6 +58,28 @@ def test_default_model_matches_oracle(cuda, k, points):
     err = np.abs(v - ref).max()
     assert err < VELOCITY_ATOL, f"max abs velocity error {err}"
     assert np.abs(ref).max() > 1e-2  # the comparison is not vacuous
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("k", [32, 16])
+@pytest.mark.parametrize("precision,encoder_precision,max_abs,rel_norm", [
+    ("tf32", "bf16x3", VELOCITY_ATOL, 1e-3),   # tensor cores, within the fp32/tf32 bound
+    ("tf32", "tf32", None, 2e-3),              # all-tf32: normwise relative bound
+    ("fp32", "bf16x3", VELOCITY_ATOL, 1e-4),
+])
+def test_tensor_core_model_matches_oracle(cuda, k, precision, encoder_precision, max_abs,
+                                          rel_norm):
+    cfg = dict(DEFAULT_CONFIG, k_neighbors=k)
+    params = random_parameters(cfg, seed=0)
+    cloud = sphere_cloud(20000, seed=3)[0]
+    x = patches_from_cloud(cloud, 4, 1024 if k == 32 else 1000, seed=k + 1)
+    alpha = np.array([0.5, 0.791531, 0.997947, 1.0], dtype=np.float32)
+    v = gpu_forward(cfg, params, x, alpha, precision, encoder_precision)
+    ref = OracleNet(cfg, params)(x, alpha)
+    rel = np.linalg.norm(v - ref) / np.linalg.norm(ref)
+    assert rel < rel_norm, f"normwise relative error {rel}"
+    if max_abs is not None:
+        assert np.abs(v - ref).max() < max_abs, f"max abs error {np.abs(v - ref).max()}"
 
 
 @pytest.mark.gpu
