@@ -58,8 +58,10 @@ def parse_args():
     p.add_argument("--cpu-sample-points", type=int, default=5_000,
                    help="cloud size of the bounded CPU-baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--precision", choices=["fp32", "tf32"], default="fp32",
-                   help="arithmetic of the model's dense contractions")
+    p.add_argument("--precision", choices=["fp32", "tf32"], default="tf32",
+                   help="arithmetic of the trunk and decoder contractions")
+    p.add_argument("--encoder-precision", choices=["fp32", "tf32", "bf16x3"], default="bf16x3",
+                   help="arithmetic of the neighbour-stage contractions")
     return p.parse_args()
 
 
@@ -93,11 +95,11 @@ def make_cloud(points: int, rank: int):
     return mesh_cloud(points, seed=4 + rank, sigma_fraction=0.015, noise_type="laplace")[0]
 
 
-def make_model(precision: str = "fp32"):
+def make_model(precision: str = "fp32", encoder_precision: str | None = None):
     from flow2surf_b200 import build_model
     from flow2surf_b200.synthetic import DEFAULT_CONFIG, random_parameters
 
-    model = build_model(DEFAULT_CONFIG, precision=precision)
+    model = build_model(DEFAULT_CONFIG, precision=precision, encoder_precision=encoder_precision)
     model.load_parameters(random_parameters(DEFAULT_CONFIG, seed=0))
     return model
 
@@ -296,7 +298,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
-    model = make_model(args.precision)
+    model = make_model(args.precision, args.encoder_precision)
     cloud = make_cloud(args.points, rank)
     points = torch.from_numpy(cloud).to(dev)
     pinned = torch.from_numpy(cloud).pin_memory()
@@ -362,7 +364,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": steps,
         "warmup": warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": args.precision, "data": "synthetic (seeded mesh clouds, random-init "
+        "vs_baseline": None, "dtype": f"trunk {args.precision}, encoder {args.encoder_precision}", "data": "synthetic (seeded mesh clouds, random-init "
         "weights; no ShapeNet or checkpoints available)",
         "config": workload_config(args, world),
         "roofline": roofline(kernels, forward_points, dims),

@@ -1,0 +1,539 @@
+// Offset attention on tcgen05 tensor cores (two passes, N x N never stored).
+//
+// Semantics as attention.cu (flow2surf/models/ops/attention.py:15-19):
+// S = Q K^T, column softmax over queries, rows divided by (sum + 1e-9), times V.
+//
+//   prep     q, k (optionally LayerNorm'd, transformer.py:59-63) split into
+//            bf16 hi + lo halves, padded to 64 channels (one 128-byte swizzle
+//            row); V transposed per patch to (C x N) fp32 rounded to tf32.
+//   pass 1   CTA = (patch, 128 keys): S^T = K Q^T per 128-query tile with
+//            three bf16 MMAs (hi hi + hi lo + lo hi, ~16-bit mantissa), keys
+//            on TMEM lanes; each thread keeps an online max / sum over its
+//            key's query columns -> L_j = log-sum-exp over queries.
+//   pass 2   CTA = (patch, 128 queries), 64-key tiles: S = Q K^T (split bf16)
+//            into TMEM; softmax threads write P = exp(S - L) (masked, tf32)
+//            into shared memory in the swizzled A-operand layout and keep the
+//            row sums; O += P V (tf32 MMA, O resident in TMEM, 192 columns);
+//            finally out = h - O / (sum + 1e-9).
+// Warp 4 lane 0 issues every TMA copy and MMA; warps 0-3 (one thread per
+// TMEM lane) do the exponentials. All waits are bounded.
+#include <cfloat>
+
+#include "kernels.cuh"
+#include "tc_common.cuh"
+
+namespace f2s {
+namespace {
+
+constexpr int kRows = 128;        // keys (pass 1) / queries (pass 2) per CTA
+constexpr int kDPad = 64;         // padded q/k width: 64 bf16 = 128 bytes
+constexpr int kKeyTile = 64;      // keys per pass-2 tile
+constexpr int kThreads = 160;     // warps 0-3 softmax/epilogue, warp 4 TMA + MMA
+constexpr unsigned kFull = 0xffffffffu;
+
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                            int c0, int c1, int c2) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(tc::smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(tc::smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+        : "memory");
+}
+
+__device__ __forceinline__ uint32_t sw128_offset(int row, int chunk) {
+    return (uint32_t)((row >> 3) * 1024 + (row & 7) * 128 + ((chunk ^ (row & 7)) << 4));
+}
+
+__device__ __forceinline__ void fence_proxy_async() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void named_sync_softmax() {
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------
+// prep: q, k -> padded bf16 hi/lo rows; V -> V^T (C x N per patch), tf32
+// ---------------------------------------------------------------------------
+__global__ void qk_split_kernel(const float* __restrict__ q, const float* __restrict__ k, int ldqk,
+                                int rows, int d, bool normalize, __nv_bfloat16* __restrict__ hi,
+                                __nv_bfloat16* __restrict__ lo) {
+    const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    for (int part = 0; part < 2; ++part) {
+        const float* src = (part == 0 ? q : k) + (size_t)row * ldqk;
+        float mean = 0.0f, rstd = 1.0f;
+        if (normalize) {  // ChannelLayerNorm, no affine, eps 1e-6 (layers.py:20-27)
+            float s = 0.0f;
+            for (int c = lane; c < d; c += 32) s += src[c];
+            mean = f2s_warp_sum(s) / (float)d;
+            float qq = 0.0f;
+            for (int c = lane; c < d; c += 32) {
+                const float t = src[c] - mean;
+                qq = fmaf(t, t, qq);
+            }
+            rstd = rsqrtf(f2s_warp_sum(qq) / (float)d + 1e-6f);
+        }
+        __nv_bfloat16* h = hi + (size_t)row * 2 * kDPad + part * kDPad;
+        __nv_bfloat16* l = lo + (size_t)row * 2 * kDPad + part * kDPad;
+        for (int c = lane; c < kDPad; c += 32) {
+            const float v = c < d ? (src[c] - mean) * rstd : 0.0f;
+            const __nv_bfloat16 vh = __float2bfloat16_rn(v);
+            h[c] = vh;
+            l[c] = __float2bfloat16_rn(v - __bfloat162float(vh));
+        }
+    }
+}
+
+// V (rows = b*N + n, ldv) -> vT[b][c][n] (pitch n_pad), rounded to tf32.
+__global__ void v_transpose_kernel(const float* __restrict__ v, int ldv, int N, int C, int n_pad,
+                                   float* __restrict__ vT) {
+    __shared__ float tile[32][33];
+    const int b = blockIdx.z;
+    const int n0 = blockIdx.x * 32, c0 = blockIdx.y * 32;
+    for (int y = threadIdx.y; y < 32; y += 8) {
+        const int n = n0 + y, c = c0 + threadIdx.x;
+        if (n < N && c < C) tile[y][threadIdx.x] = v[((size_t)b * N + n) * ldv + c];
+    }
+    __syncthreads();
+    for (int y = threadIdx.y; y < 32; y += 8) {
+        const int c = c0 + y, n = n0 + threadIdx.x;
+        if (c < C && n < n_pad)
+            vT[((size_t)b * C + c) * n_pad + n] = n < N ? f2s_round_tf32(tile[threadIdx.x][y]) : 0.0f;
+    }
+}
+
+struct AttnArgs {
+    int N, C, n_pad;
+    int tiles;        // key tiles (pass 1: of 128) / query tiles (pass 2: of 128) per patch
+    float* colstats;  // (B*N) per-key log-sum-exp
+    const float* h;   // pass 2: offset input (nullptr: plain aggregate)
+    int ldh;
+    float* out;
+    int ldo;
+    int round_tf32;
+    uint32_t idesc_s;   // bf16, M = 128, N = 128 (pass 1) / 64 (pass 2)
+    uint32_t idesc_pv;  // tf32, M = 128, N = C
+    int* err;
+};
+
+// ---------------------------------------------------------------------------
+// pass 1: per-key log-sum-exp over all queries
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kThreads, 1)
+attn_tc_colstats_kernel(const __grid_constant__ CUtensorMap map_hi,
+                        const __grid_constant__ CUtensorMap map_lo, const AttnArgs a) {
+    extern __shared__ __align__(1024) unsigned char attn_smem_raw[];
+    unsigned char* smem = reinterpret_cast<unsigned char*>(
+        (reinterpret_cast<uintptr_t>(attn_smem_raw) + 1023) & ~uintptr_t(1023));
+    constexpr uint32_t kTileBytes = kRows * 128;  // 128 rows x 64 bf16
+    unsigned char* sK = smem;                      // hi, lo
+    unsigned char* sQ = smem + 2 * kTileBytes;     // 2 stages x (hi, lo)
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sQ + 4 * kTileBytes);
+    uint64_t* k_full = bars;         // [1]
+    uint64_t* q_full = bars + 1;     // [2]
+    uint64_t* q_empty = bars + 3;    // [2]
+    uint64_t* s_full = bars + 5;     // [2]
+    uint64_t* s_empty = bars + 7;    // [2]
+    uint64_t* done = bars + 9;       // [1]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
+
+    const int b = blockIdx.x / a.tiles;
+    const int key0 = (blockIdx.x - b * a.tiles) * kRows;
+    const int nq = (a.N + kRows - 1) / kRows;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < 10; ++i) tc::mbar_init(&bars[i], i == 7 || i == 8 ? 128 : 1);
+        tc::fence_barrier_init();
+    }
+    if (warp == 0) tc::tmem_alloc(tmem_slot, 256);
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 4) {
+        if (lane == 0) {
+            bool ok = true;
+            tc::mbar_arrive_expect_tx(k_full, 2 * kTileBytes);
+            tma_load_3d(sK, &map_hi, k_full, kDPad, key0, b);
+            tma_load_3d(sK + kTileBytes, &map_lo, k_full, kDPad, key0, b);
+            auto load_q = [&](int j) {
+                const int s = j & 1;
+                tc::mbar_arrive_expect_tx(&q_full[s], 2 * kTileBytes);
+                tma_load_3d(sQ + (2 * s) * kTileBytes, &map_hi, &q_full[s], 0, j * kRows, b);
+                tma_load_3d(sQ + (2 * s + 1) * kTileBytes, &map_lo, &q_full[s], 0, j * kRows, b);
+            };
+            load_q(0);
+            if (nq > 1) load_q(1);
+            ok = tc::mbar_wait(k_full, 0, a.err);
+            const uint32_t k_hi = tc::smem_u32(sK), k_lo = k_hi + kTileBytes;
+            for (int j = 0; j < nq && ok; ++j) {
+                const int s = j & 1;
+                const uint32_t ph = (uint32_t)(j >> 1) & 1u;
+                if (!tc::mbar_wait(&q_full[s], ph, a.err) ||
+                    !tc::mbar_wait(&s_empty[s], ph ^ 1u, a.err)) {
+                    ok = false;
+                    break;
+                }
+                tc::tc_fence_after();
+                const uint32_t q_hi = tc::smem_u32(sQ + (2 * s) * kTileBytes), q_lo = q_hi + kTileBytes;
+                const uint32_t d = tmem + (uint32_t)(s * 128);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk) {  // 64 channels, 16 per MMA
+                    const uint32_t o = kk * 32;
+                    tc::umma<false>(d, tc::sw128_desc(k_hi + o), tc::sw128_desc(q_hi + o), a.idesc_s,
+                                    kk ? 1u : 0u);
+                    tc::umma<false>(d, tc::sw128_desc(k_hi + o), tc::sw128_desc(q_lo + o), a.idesc_s, 1u);
+                    tc::umma<false>(d, tc::sw128_desc(k_lo + o), tc::sw128_desc(q_hi + o), a.idesc_s, 1u);
+                }
+                tc::umma_commit(&s_full[s]);
+                tc::umma_commit(&q_empty[s]);
+                if (j + 2 < nq) {
+                    if (!tc::mbar_wait(&q_empty[s], ph, a.err)) {
+                        ok = false;
+                        break;
+                    }
+                    load_q(j + 2);
+                }
+            }
+            tc::umma_commit(done);
+            tc::mbar_wait(done, 0, a.err);
+        }
+        __syncwarp();
+    } else {
+        // one thread per key (TMEM lane): online max / sum over query columns
+        const int row = warp * 32 + lane;
+        float m = -FLT_MAX, s = 0.0f;
+        for (int j = 0; j < nq; ++j) {
+            const int sb = j & 1;
+            const uint32_t ph = (uint32_t)(j >> 1) & 1u;
+            int ready = 0;
+            if (lane == 0) ready = tc::mbar_wait(&s_full[sb], ph, a.err) ? 1 : 0;
+            if (!__shfl_sync(kFull, ready, 0)) break;
+            tc::tc_fence_after();
+            const int valid = min(kRows, a.N - j * kRows);
+            const uint32_t t = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(sb * 128);
+            for (int c0 = 0; c0 < kRows; c0 += 32) {
+                float v[32];
+                tc::tmem_ld32(t + (uint32_t)c0, v);
+                float tmax = -FLT_MAX;
+#pragma unroll
+                for (int i = 0; i < 32; ++i)
+                    if (c0 + i < valid) tmax = fmaxf(tmax, v[i]);
+                if (tmax > m) {
+                    s *= __expf(m - tmax);
+                    m = tmax;
+                }
+#pragma unroll
+                for (int i = 0; i < 32; ++i)
+                    if (c0 + i < valid) s += __expf(v[i] - m);
+            }
+            tc::tc_fence_before();
+            tc::mbar_arrive(&s_empty[sb]);
+        }
+        const int key = key0 + row;
+        if (key < a.N) a.colstats[(size_t)b * a.N + key] = m + __logf(s);
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tmem, 256);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// pass 2: out = h - (sum_j p_ij V_j) / (sum_j p_ij + 1e-9), p_ij = exp(S_ij - L_j)
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kThreads, 1)
+attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
+                      const __grid_constant__ CUtensorMap map_qlo,
+                      const __grid_constant__ CUtensorMap map_khi,
+                      const __grid_constant__ CUtensorMap map_klo,
+                      const __grid_constant__ CUtensorMap map_vt, const AttnArgs a) {
+    extern __shared__ __align__(1024) unsigned char attn_smem_raw[];
+    unsigned char* smem = reinterpret_cast<unsigned char*>(
+        (reinterpret_cast<uintptr_t>(attn_smem_raw) + 1023) & ~uintptr_t(1023));
+    const int C = a.C;
+    constexpr uint32_t kQBytes = kRows * 128;        // 128 queries x 64 bf16
+    constexpr uint32_t kKBytes = kKeyTile * 128;     // 64 keys x 64 bf16
+    const uint32_t v_bytes = (uint32_t)C * 128;      // one K-block: C rows x 32 fp32 keys
+    constexpr uint32_t kPBytes = kRows * 128;        // one K-block: 128 queries x 32 fp32 keys
+    unsigned char* sQ = smem;                                  // hi, lo
+    unsigned char* sK = sQ + 2 * kQBytes;                      // 2 stages x (hi, lo)
+    unsigned char* sV = sK + 4 * kKBytes;                      // 2 stages x 2 K-blocks
+    unsigned char* sP = sV + 4 * v_bytes;                      // 2 K-blocks
+    float* sL = reinterpret_cast<float*>(sP + 2 * kPBytes);    // 2 stages x 64
+    int* sFlag = reinterpret_cast<int*>(sL + 2 * kKeyTile);    // softmax go / stop
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sFlag + 2);
+    uint64_t* q_full = bars;        // [1]
+    uint64_t* kv_full = bars + 1;   // [2]
+    uint64_t* kv_empty = bars + 3;  // [2]
+    uint64_t* s_full = bars + 5;    // [2]
+    uint64_t* s_empty = bars + 7;   // [2]  (128 arrivals)
+    uint64_t* p_full = bars + 9;    // [1]  (128 arrivals)
+    uint64_t* pv_done = bars + 10;  // [1]
+    uint64_t* done = bars + 11;     // [1]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+
+    const int b = blockIdx.x / a.tiles;
+    const int q0 = (blockIdx.x - b * a.tiles) * kRows;
+    const int nk = (a.N + kKeyTile - 1) / kKeyTile;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // TMEM: S double buffer at columns [0, 128), O at [256, 256 + C)
+    constexpr uint32_t kOCol = 256;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < 12; ++i)
+            tc::mbar_init(&bars[i], (i == 7 || i == 8 || i == 9) ? 128 : 1);
+        tc::fence_barrier_init();
+    }
+    if (warp == 0) tc::tmem_alloc(tmem_slot, 512);
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 4) {
+        if (lane == 0) {
+            bool ok = true;
+            auto load_kv = [&](int i) {
+                const int s = i & 1;
+                tc::mbar_arrive_expect_tx(&kv_full[s], 2 * kKBytes + 2 * v_bytes);
+                tma_load_3d(sK + (2 * s) * kKBytes, &map_khi, &kv_full[s], kDPad, i * kKeyTile, b);
+                tma_load_3d(sK + (2 * s + 1) * kKBytes, &map_klo, &kv_full[s], kDPad, i * kKeyTile, b);
+                tma_load_3d(sV + (2 * s) * v_bytes, &map_vt, &kv_full[s], i * kKeyTile, 0, b);
+                tma_load_3d(sV + (2 * s + 1) * v_bytes, &map_vt, &kv_full[s], i * kKeyTile + 32, 0, b);
+            };
+            tc::mbar_arrive_expect_tx(q_full, 2 * kQBytes);
+            tma_load_3d(sQ, &map_qhi, q_full, 0, q0, b);
+            tma_load_3d(sQ + kQBytes, &map_qlo, q_full, 0, q0, b);
+            load_kv(0);
+            if (nk > 1) load_kv(1);
+            ok = tc::mbar_wait(q_full, 0, a.err);
+            const uint32_t q_hi = tc::smem_u32(sQ), q_lo = q_hi + kQBytes;
+            auto issue_s = [&](int i) -> bool {
+                const int s = i & 1;
+                const uint32_t ph = (uint32_t)(i >> 1) & 1u;
+                if (!tc::mbar_wait(&kv_full[s], ph, a.err) ||
+                    !tc::mbar_wait(&s_empty[s], ph ^ 1u, a.err))
+                    return false;
+                tc::tc_fence_after();
+                const uint32_t k_hi = tc::smem_u32(sK + (2 * s) * kKBytes), k_lo = k_hi + kKBytes;
+                const uint32_t d = tmem + (uint32_t)(s * 64);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk) {
+                    const uint32_t o = kk * 32;
+                    tc::umma<false>(d, tc::sw128_desc(q_hi + o), tc::sw128_desc(k_hi + o), a.idesc_s,
+                                    kk ? 1u : 0u);
+                    tc::umma<false>(d, tc::sw128_desc(q_hi + o), tc::sw128_desc(k_lo + o), a.idesc_s, 1u);
+                    tc::umma<false>(d, tc::sw128_desc(q_lo + o), tc::sw128_desc(k_hi + o), a.idesc_s, 1u);
+                }
+                tc::umma_commit(&s_full[s]);
+                return true;
+            };
+            if (ok) ok = issue_s(0);
+            const uint32_t p0 = tc::smem_u32(sP);
+            for (int i = 0; i < nk && ok; ++i) {
+                const int s = i & 1;
+                if (i + 1 < nk && !issue_s(i + 1)) {
+                    ok = false;
+                    break;
+                }
+                // P_i written by the softmax threads
+                if (!tc::mbar_wait(p_full, (uint32_t)i & 1u, a.err)) {
+                    ok = false;
+                    break;
+                }
+                tc::tc_fence_after();
+                const uint32_t v0 = tc::smem_u32(sV + (2 * s) * v_bytes);
+#pragma unroll
+                for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk) {  // 8 keys (32 bytes) per tf32 MMA
+                        const uint32_t o = kk * 32;
+                        tc::umma<true>(tmem + kOCol, tc::sw128_desc(p0 + kb * kPBytes + o),
+                                       tc::sw128_desc(v0 + kb * v_bytes + o), a.idesc_pv,
+                                       (i | kb | kk) ? 1u : 0u);
+                    }
+                tc::umma_commit(pv_done);
+                tc::umma_commit(&kv_empty[s]);
+                if (i + 2 < nk) {
+                    if (!tc::mbar_wait(&kv_empty[s], (uint32_t)(i >> 1) & 1u, a.err)) {
+                        ok = false;
+                        break;
+                    }
+                    load_kv(i + 2);
+                }
+            }
+            tc::umma_commit(done);
+            tc::mbar_wait(done, 0, a.err);
+        }
+        __syncwarp();
+    } else {
+        // one thread per query row; thread 0 does every wait and publishes
+        // the outcome, so the four softmax warps always take the same path
+        const int row = warp * 32 + lane;
+        const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+        float den = 0.0f;
+        bool ok = true;
+        for (int i = 0; i < nk; ++i) {
+            const int s = i & 1;
+            const uint32_t ph = (uint32_t)(i >> 1) & 1u;
+            if (row < kKeyTile) {  // this key tile's log-sum-exp values
+                const int key = i * kKeyTile + row;
+                sL[s * kKeyTile + row] = key < a.N ? a.colstats[(size_t)b * a.N + key] : 0.0f;
+            }
+            if (row == 0) {
+                bool go = tc::mbar_wait(&s_full[s], ph, a.err);
+                // the previous P must have been consumed before it is overwritten
+                if (go && i > 0) go = tc::mbar_wait(pv_done, (uint32_t)(i - 1) & 1u, a.err);
+                sFlag[0] = go ? 1 : 0;
+            }
+            named_sync_softmax();
+            if (!sFlag[0]) {
+                ok = false;
+                break;
+            }
+            tc::tc_fence_after();
+            float p[64];
+            tc::tmem_ld32(tmem + lane_base + (uint32_t)(s * 64), *reinterpret_cast<float(*)[32]>(p));
+            tc::tmem_ld32(tmem + lane_base + (uint32_t)(s * 64 + 32),
+                          *reinterpret_cast<float(*)[32]>(p + 32));
+            tc::tc_fence_before();
+            tc::mbar_arrive(&s_empty[s]);
+            const int valid = min(kKeyTile, a.N - i * kKeyTile);
+#pragma unroll
+            for (int j = 0; j < 64; ++j) {
+                const float e = j < valid ? __expf(p[j] - sL[s * kKeyTile + j]) : 0.0f;
+                p[j] = e;
+                den += e;
+            }
+#pragma unroll
+            for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+                for (int ch = 0; ch < 8; ++ch) {
+                    const int j = kb * 32 + ch * 4;
+                    *reinterpret_cast<float4*>(sP + kb * kPBytes + sw128_offset(row, ch)) =
+                        make_float4(f2s_round_tf32(p[j]), f2s_round_tf32(p[j + 1]),
+                                    f2s_round_tf32(p[j + 2]), f2s_round_tf32(p[j + 3]));
+                }
+            fence_proxy_async();
+            tc::mbar_arrive(p_full);
+        }
+        // wait for the last P V product, then write h - O / (den + 1e-9)
+        if (ok) {
+            if (row == 0) sFlag[1] = tc::mbar_wait(pv_done, (uint32_t)(nk - 1) & 1u, a.err) ? 1 : 0;
+            named_sync_softmax();
+            ok = sFlag[1] != 0;
+        }
+        if (ok) {
+            tc::tc_fence_after();
+            const float inv = 1.0f / (den + 1e-9f);
+            const int qrow = q0 + row;
+            const size_t grow = (size_t)b * a.N + qrow;
+            for (int c0 = 0; c0 < C; c0 += 32) {
+                float o[32];
+                tc::tmem_ld32(tmem + lane_base + kOCol + (uint32_t)c0, o);
+                if (qrow < a.N) {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        const float av = o[i] * inv;
+                        const float r = a.h ? a.h[grow * a.ldh + c0 + i] - av : av;
+                        a.out[grow * a.ldo + c0 + i] = a.round_tf32 ? f2s_round_tf32(r) : r;
+                    }
+                }
+            }
+        }
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tmem, 512);
+    }
+}
+
+}  // namespace
+
+int attention_tc_workspace_floats(int B, int N, int C) {
+    const int n_pad = (N + 3) & ~3;
+    // qk hi + lo (bf16: 2 x B*N*128 halves = B*N*128 floats), vT, colstats
+    return B * N * 128 + B * C * n_pad + B * N;
+}
+
+// q, k: (B*N rows, ldqk), width d (<= 64); v (ldv), width C (multiple of 32,
+// <= 256); out = h - A (or A). workspace: attention_tc_workspace_floats floats.
+int attention_tc(const float* q, const float* k, int ldqk, const float* v, int ldv,
+                 const float* h, int ldh, float* out, int ldo, float* workspace, int B, int N,
+                 int d, int C, bool normalize_qk, bool round_tf32, cudaStream_t st) {
+    if (B == 0 || N == 0) return F2S_OK;
+    if (d > kDPad || C % 32 != 0 || C > 256 || C < 32)
+        return fail(F2S_ERR_UNSUPPORTED, "attention shape outside the tensor-core kernel");
+    int* err = tc_error_word();
+    if (!err) return fail(F2S_ERR_CUDA, "attention_tc: device error word unavailable");
+    const int n_pad = (N + 3) & ~3;
+    __nv_bfloat16* qk_hi = reinterpret_cast<__nv_bfloat16*>(workspace);
+    __nv_bfloat16* qk_lo = qk_hi + (size_t)B * N * 2 * kDPad;
+    float* vT = workspace + (size_t)B * N * 128;
+    float* colstats = vT + (size_t)B * C * n_pad;
+    {
+        TraceScope trace(kTagRowNorm, st);
+        qk_split_kernel<<<ceil_div(B * N, 8), 256, 0, st>>>(q, k, ldqk, B * N, d, normalize_qk,
+                                                             qk_hi, qk_lo);
+        F2S_TRY(check_launch("qk_split_kernel"));
+        dim3 grid(ceil_div(n_pad, 32), ceil_div(C, 32), B);
+        v_transpose_kernel<<<grid, dim3(32, 8), 0, st>>>(v, ldv, N, C, n_pad, vT);
+        F2S_TRY(check_launch("v_transpose_kernel"));
+    }
+    CUtensorMap map_hi_q, map_lo_q, map_hi_k, map_lo_k, map_vt;
+    const int64_t row_bytes = 2 * kDPad * 2;  // q and k halves: 256 bytes per point
+    // pass 1 reads 128-row boxes of both q and k; pass 2 reads 128-row q and 64-row k boxes
+    F2S_TRY(make_tensor_map_3d(&map_hi_q, qk_hi, false, 2 * kDPad, N, B, row_bytes, row_bytes * N, kDPad, kRows));
+    F2S_TRY(make_tensor_map_3d(&map_lo_q, qk_lo, false, 2 * kDPad, N, B, row_bytes, row_bytes * N, kDPad, kRows));
+    F2S_TRY(make_tensor_map_3d(&map_hi_k, qk_hi, false, 2 * kDPad, N, B, row_bytes, row_bytes * N, kDPad, kKeyTile));
+    F2S_TRY(make_tensor_map_3d(&map_lo_k, qk_lo, false, 2 * kDPad, N, B, row_bytes, row_bytes * N, kDPad, kKeyTile));
+    F2S_TRY(make_tensor_map_3d(&map_vt, vT, true, N, C, B, (int64_t)n_pad * 4, (int64_t)n_pad * 4 * C, 32, C));
+
+    AttnArgs a{};
+    a.N = N;
+    a.C = C;
+    a.n_pad = n_pad;
+    a.colstats = colstats;
+    a.h = h;
+    a.ldh = ldh;
+    a.out = out;
+    a.ldo = ldo;
+    a.round_tf32 = round_tf32 ? 1 : 0;
+    a.err = err;
+    {
+        TraceScope trace(kTagAttnColstats, st);
+        a.tiles = ceil_div(N, kRows);
+        a.idesc_s = tc::make_idesc(kRows, kRows, 1u);
+        const size_t smem = 1024 + 6 * kRows * 128 + 128;
+        F2S_CUDA_TRY(cudaFuncSetAttribute(attn_tc_colstats_kernel,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        attn_tc_colstats_kernel<<<B * a.tiles, kThreads, smem, st>>>(map_hi_q, map_lo_q, a);
+        F2S_TRY(check_launch("attn_tc_colstats_kernel"));
+    }
+    {
+        TraceScope trace(kTagAttnOutput, st);
+        a.tiles = ceil_div(N, kRows);
+        a.idesc_s = tc::make_idesc(kRows, kKeyTile, 1u);
+        a.idesc_pv = tc::make_idesc(kRows, C, 2u);
+        const size_t smem = 1024 + 2 * kRows * 128 + 4 * kKeyTile * 128 + 4 * (size_t)C * 128 +
+                            2 * kRows * 128 + 2 * kKeyTile * 4 + 8 + 128;
+        F2S_LIMIT(smem <= 227 * 1024, "attention_tc: %zu bytes of shared memory", smem);
+        F2S_CUDA_TRY(cudaFuncSetAttribute(attn_tc_output_kernel,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        attn_tc_output_kernel<<<B * a.tiles, kThreads, smem, st>>>(map_hi_q, map_lo_q, map_hi_k,
+                                                                   map_lo_k, map_vt, a);
+        F2S_TRY(check_launch("attn_tc_output_kernel"));
+    }
+    return F2S_OK;
+}
+
+}  // namespace f2s

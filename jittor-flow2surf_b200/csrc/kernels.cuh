@@ -84,6 +84,16 @@ int attention_f32(const float* q, const float* k, int ldqk, const float* v, int 
                   const float* h, int ldh, float* out, int ldo, float* colstats, int B, int N,
                   int d, int C, bool round_tf32, cudaStream_t stream);
 
+// ---- attention_tc.cu ----
+// The same on tcgen05 tensor cores: q, k (width d <= 64, LayerNorm'd first
+// when normalize_qk) contracted as split bf16, P V as tf32. workspace holds
+// attention_tc_workspace_floats(B, N, C) floats. F2S_ERR_UNSUPPORTED for
+// shapes it does not cover.
+int attention_tc_workspace_floats(int B, int N, int C);
+int attention_tc(const float* q, const float* k, int ldqk, const float* v, int ldv,
+                 const float* h, int ldh, float* out, int ldo, float* workspace, int B, int N,
+                 int d, int C, bool normalize_qk, bool round_tf32, cudaStream_t stream);
+
 // ---- edge.cu ----
 // Fused neighbour stage: per edge (i, j = idx[i, k]) the HPE hidden
 // GELU(LN(W_in g + b_in)) of g = [xyz_j - xyz_i, xyz_i] (or a given geometry

@@ -171,7 +171,7 @@ Layout make_layout(const Dims& d) {
 // ---------------------------------------------------------------------------
 struct Workspace {
     float *xyz4, *feat0, *content, *cat, *x, *h, *qkv, *colstats, *offs, *ffh, *dec0, *dec1;
-    float *cond, *mod;
+    float *cond, *mod, *attn;
     int32_t* idx;
     size_t bytes;
 };
@@ -200,6 +200,7 @@ Workspace carve(const Dims& d, int B, int M, char* base) {
     w.dec1 = (float*)take(R * (d.max_dec > 0 ? d.max_dec : 1));
     w.cond = (float*)take((size_t)B * d.A);
     w.mod = (float*)take((size_t)B * (d.NB > 0 ? d.NB : 1) * 6 * d.C);
+    w.attn = (float*)take((size_t)attention_tc_workspace_floats(B, M, d.C));
     w.bytes = off;
     return w;
 }
@@ -436,9 +437,17 @@ int forward(const Dims& d, const Layout& L, const float* P, const float* x_in, c
         GemmArgs gq = gemm_args(w.h, C, P + bp.qkv_w, nullptr, w.qkv, ld_qkv, R, ld_qkv, C);
         gq.tag = kTagGemmQkv;
         F2S_TRY(linear_op(gq, d.precision, st));
-        F2S_TRY(qk_norm(w.qkv, ld_qkv, R, d.qk, st));
-        F2S_TRY(attention_f32(w.qkv, w.qkv + d.qk, ld_qkv, w.qkv + 2 * d.qk, ld_qkv, w.h, C,
-                              w.offs, C, w.colstats, B, M, d.qk, C, tf32_trunk, st));
+        int attn_status = F2S_ERR_UNSUPPORTED;
+        if (tf32_trunk)  // q, k LayerNorm inside the tensor-core path's prep kernel
+            attn_status = attention_tc(w.qkv, w.qkv + d.qk, ld_qkv, w.qkv + 2 * d.qk, ld_qkv,
+                                       w.h, C, w.offs, C, w.attn, B, M, d.qk, C, true, true, st);
+        if (attn_status == F2S_ERR_UNSUPPORTED) {
+            F2S_TRY(qk_norm(w.qkv, ld_qkv, R, d.qk, st));
+            attn_status = attention_f32(w.qkv, w.qkv + d.qk, ld_qkv, w.qkv + 2 * d.qk, ld_qkv,
+                                        w.h, C, w.offs, C, w.colstats, B, M, d.qk, C, tf32_trunk,
+                                        st);
+        }
+        F2S_TRY(attn_status);
         GemmArgs g = gemm_args(w.offs, C, P + bp.proj_w, nullptr, w.x, C, R, C, C);
         g.epilogue = kEpiGatedResidual;
         g.gate = mod + 2 * C;

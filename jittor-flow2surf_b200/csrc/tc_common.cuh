@@ -196,6 +196,13 @@ __host__ __device__ constexpr uint32_t make_idesc(int M, int N, uint32_t ab_form
 int make_tensor_map_2d(CUtensorMap* map, const void* base, bool fp32, int64_t rows,
                        int64_t cols, int64_t ld, int box_rows, int box_cols);
 
+// 3-D tensor (d0 innermost, element strides given in bytes for dims 1, 2),
+// boxes of (box0 x box1 x 1), 128-byte swizzle: out-of-range rows of a patch
+// (dim 1) read as zeros without touching the next patch (dim 2).
+int make_tensor_map_3d(CUtensorMap* map, const void* base, bool fp32, int64_t d0, int64_t d1,
+                       int64_t d2, int64_t stride1_bytes, int64_t stride2_bytes, int box0,
+                       int box1);
+
 // Device address of the library's error word (per device, cached).
 int* tc_error_word();
 
