@@ -9,10 +9,12 @@
 //   warp 1      allocates TMEM; lane 0 issues tcgen05.mma (M = 128, N = BN,
 //               K = 32 bytes per instruction) into one of two TMEM
 //               accumulators and commits stage releases / accumulator-ready;
-//   warps 2-5   epilogue: each thread owns one accumulator row (TMEM lane),
-//               reads 32 columns at a time with tcgen05.ld, applies the
-//               epilogue and stores; then frees the accumulator buffer, so the
-//               MMAs of the next tile overlap this epilogue.
+//   warps 2-9   epilogue: two warps per TMEM lane quarter, each taking every
+//               other 32-column chunk; a chunk is read with tcgen05.ld (thread
+//               = accumulator row), transposed through shared memory (lane =
+//               column, so bias / gate loads and stores are coalesced), the
+//               epilogue applied and stored; then the accumulator buffer is
+//               freed, so the MMAs of the next tile overlap this epilogue.
 // Operands are bf16 (kind::f16) or fp32 read as tf32 (kind::tf32).
 #include <mutex>
 
@@ -27,9 +29,10 @@ __device__ int g_tc_error = 0;
 
 namespace {
 
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;
+constexpr int kEpilogueThreads = 256;
 constexpr int kTileM = 128;
-constexpr int kStageBudget = 200 * 1024;
+constexpr size_t kSmemLimit = 227 * 1024;
 
 struct TcGemmArgs {
     int rows, cols, K;
@@ -87,7 +90,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         }
         for (int b = 0; b < 2; ++b) {
             tc::mbar_init(&tfull[b], 1);
-            tc::mbar_init(&tempty[b], 128);
+            tc::mbar_init(&tempty[b], kEpilogueThreads);
         }
         tc::mbar_init(mma_done, 1);
         tc::fence_barrier_init();
@@ -191,10 +194,14 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         }
         __syncwarp();
     } else {
-        // ---------------- epilogue (warps 2..5) ----------------
+        // ---------------- epilogue (warps 2..9) ----------------
+        // two warps per TMEM lane quarter, taking alternate 32-column chunks
         const int quarter = warp & 3;
+        const int ew = warp - 2;
+        const int chunk_half = ew >> 2;
         float* stage_buf = reinterpret_cast<float*>(smem + (size_t)S * stage_bytes + 256) +
-                           (warp - 2) * 32 * 33;
+                           ew * (kDual ? 2 : 1) * 32 * 33;
+        float* stage_buf2 = stage_buf + 32 * 33;  // SwiGLU value accumulator
         int iter = 0;
         for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++iter) {
             const int buf = iter & 1;
@@ -209,35 +216,40 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             const int row0 = m0 + quarter * 32;  // first of this warp's 32 rows
             const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) +
                                    (uint32_t)(buf * g.acc_cols);
-            for (int c0 = 0; c0 < g.bn; c0 += 32) {
+            for (int c0 = chunk_half * 32; c0 < g.bn; c0 += 64) {
                 // thread = row in TMEM; through the staging buffer, lane = column
-                // for coalesced global access
+                // for coalesced global access and one bias / gate load per lane
                 float v[32];
                 tc::tmem_ld32(t_row + (uint32_t)c0, v);
-                if constexpr (kDual) {
-                    float v2[32];
-                    tc::tmem_ld32(t_row + (uint32_t)(g.bn + c0), v2);
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        const int col = min(n0 + c0 + i, g.cols - 1);
-                        v[i] = f2s_silu(epi_value(v[i], g.bias, col)) *
-                               epi_value(v2[i], g.bias2, col);
-                    }
-                }
 #pragma unroll
                 for (int i = 0; i < 32; ++i) stage_buf[lane * 33 + i] = v[i];
+                if constexpr (kDual) {
+                    tc::tmem_ld32(t_row + (uint32_t)(g.bn + c0), v);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) stage_buf2[lane * 33 + i] = v[i];
+                }
                 __syncwarp();
                 const int col = n0 + c0 + lane;
                 if (col < g.cols) {
-                    const float b = (!kDual && g.bias) ? g.bias[col] : 0.0f;
-                    for (int r = 0; r < 32; ++r) {
+                    const float b = g.bias ? g.bias[col] : 0.0f;
+                    const float b2 = (kDual && g.bias2) ? g.bias2[col] : 0.0f;
+                    int patch = -1;
+                    float gt = 0.0f;
+                    const int r_end = min(32, g.rows - row0);
+                    for (int r = 0; r < r_end; ++r) {
                         const int row = row0 + r;
-                        if (row >= g.rows) break;
-                        const float out = stage_buf[r * 33 + lane] + b;
+                        float out = stage_buf[r * 33 + lane] + b;
+                        if constexpr (kDual) {
+                            const float u = stage_buf2[r * 33 + lane] + b2;
+                            out = f2s_silu(out) * u;
+                        }
                         const size_t o = (size_t)row * g.ldy + col;
-                        if (kEpi == kEpiGatedResidual) {
-                            const float gt =
-                                g.gate[(size_t)(row / g.rows_per_patch) * g.gate_stride + col];
+                        if constexpr (kEpi == kEpiGatedResidual) {
+                            const int p = row / g.rows_per_patch;
+                            if (p != patch) {
+                                patch = p;
+                                gt = g.gate[(size_t)p * g.gate_stride + col];
+                            }
                             float* y = static_cast<float*>(g.Y) + o;
                             *y = *y + gt * out;
                         } else if (g.y_bf16) {
@@ -387,13 +399,14 @@ int tc_gemm(const TcGemmOp& op, cudaStream_t st) {
     g.round_tf32 = op.round_tf32 ? 1 : 0;
     g.err = err;
     const size_t stage_bytes = (size_t)kTileM * 128 + (size_t)bn * 128 * (dual ? 2 : 1);
-    int stages = (int)(kStageBudget / stage_bytes);
+    const size_t stage_buf_bytes = (size_t)(kEpilogueThreads / 32) * (dual ? 2 : 1) * 32 * 33 * sizeof(float);
+    int stages = (int)((kSmemLimit - 1024 - 256 - stage_buf_bytes) / stage_bytes);
     stages = stages > 8 ? 8 : stages;
     F2S_LIMIT(stages >= 2, "tc_gemm: tile too large for shared memory");
     g.stages = stages;
     // tiles, then barriers + TMEM slot (< 256 bytes for <= 8 stages), then the
-    // four epilogue warps' 32 x 33 staging buffers
-    const size_t smem = 1024 + stages * stage_bytes + 256 + 4 * 32 * 33 * sizeof(float);
+    // eight epilogue warps' 32 x 33 staging buffers (two each for SwiGLU)
+    const size_t smem = 1024 + stages * stage_bytes + 256 + stage_buf_bytes;
     const int tiles = ceil_div(op.rows, kTileM) * ceil_div(op.cols, bn);
     const int grid = tiles < sm_count() ? tiles : sm_count();
     TraceScope trace(op.tag, st);
