@@ -157,6 +157,7 @@ attn_tc_colstats_kernel(const __grid_constant__ CUtensorMap map_hi,
     if (warp == 4) {
         if (lane == 0) {
             bool ok = true;
+            int q_issued = 0, q_landed = 0;  // Q tiles loaded / seen complete
             tc::mbar_arrive_expect_tx(k_full, 2 * kTileBytes);
             tma_load_3d(sK, &map_hi, k_full, kDPad, key0, b);
             tma_load_3d(sK + kTileBytes, &map_lo, k_full, kDPad, key0, b);
@@ -165,16 +166,22 @@ attn_tc_colstats_kernel(const __grid_constant__ CUtensorMap map_hi,
                 tc::mbar_arrive_expect_tx(&q_full[s], 2 * kTileBytes);
                 tma_load_3d(sQ + (2 * s) * kTileBytes, &map_hi, &q_full[s], 0, j * kRows, b);
                 tma_load_3d(sQ + (2 * s + 1) * kTileBytes, &map_lo, &q_full[s], 0, j * kRows, b);
+                q_issued = j + 1;
             };
             load_q(0);
             if (nq > 1) load_q(1);
             ok = tc::mbar_wait(k_full, 0, a.err);
+            if (!ok) tc::mbar_drain(k_full, 0);
             const uint32_t k_hi = tc::smem_u32(sK), k_lo = k_hi + kTileBytes;
             for (int j = 0; j < nq && ok; ++j) {
                 const int s = j & 1;
                 const uint32_t ph = (uint32_t)(j >> 1) & 1u;
-                if (!tc::mbar_wait(&q_full[s], ph, a.err) ||
-                    !tc::mbar_wait(&s_empty[s], ph ^ 1u, a.err)) {
+                if (!tc::mbar_wait(&q_full[s], ph, a.err)) {
+                    ok = false;
+                    break;
+                }
+                q_landed = j + 1;
+                if (!tc::mbar_wait(&s_empty[s], ph ^ 1u, a.err)) {
                     ok = false;
                     break;
                 }
@@ -199,8 +206,11 @@ attn_tc_colstats_kernel(const __grid_constant__ CUtensorMap map_hi,
                     load_q(j + 2);
                 }
             }
+            // Q copies still in flight land before the CTA exits
+            for (int j = q_landed; j < q_issued; ++j)
+                tc::mbar_drain(&q_full[j & 1], (uint32_t)(j >> 1) & 1u);
             tc::umma_commit(done);
-            tc::mbar_wait(done, 0, a.err);
+            tc::mbar_drain(done, 0);
         }
         __syncwarp();
     } else {
@@ -300,6 +310,7 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
     if (warp == 4) {
         if (lane == 0) {
             bool ok = true;
+            int kv_issued = 0, kv_landed = 0;  // K/V tiles loaded / seen complete
             auto load_kv = [&](int i) {
                 const int s = i & 1;
                 tc::mbar_arrive_expect_tx(&kv_full[s], 2 * kKBytes + 2 * v_bytes);
@@ -307,6 +318,7 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
                 tma_load_3d(sK + (2 * s + 1) * kKBytes, &map_klo, &kv_full[s], kDPad, i * kKeyTile, b);
                 tma_load_3d(sV + (2 * s) * v_bytes, &map_vt, &kv_full[s], i * kKeyTile, 0, b);
                 tma_load_3d(sV + (2 * s + 1) * v_bytes, &map_vt, &kv_full[s], i * kKeyTile + 32, 0, b);
+                kv_issued = i + 1;
             };
             tc::mbar_arrive_expect_tx(q_full, 2 * kQBytes);
             tma_load_3d(sQ, &map_qhi, q_full, 0, q0, b);
@@ -314,13 +326,14 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
             load_kv(0);
             if (nk > 1) load_kv(1);
             ok = tc::mbar_wait(q_full, 0, a.err);
+            if (!ok) tc::mbar_drain(q_full, 0);
             const uint32_t q_hi = tc::smem_u32(sQ), q_lo = q_hi + kQBytes;
             auto issue_s = [&](int i) -> bool {
                 const int s = i & 1;
                 const uint32_t ph = (uint32_t)(i >> 1) & 1u;
-                if (!tc::mbar_wait(&kv_full[s], ph, a.err) ||
-                    !tc::mbar_wait(&s_empty[s], ph ^ 1u, a.err))
-                    return false;
+                if (!tc::mbar_wait(&kv_full[s], ph, a.err)) return false;
+                kv_landed = i + 1;
+                if (!tc::mbar_wait(&s_empty[s], ph ^ 1u, a.err)) return false;
                 tc::tc_fence_after();
                 const uint32_t k_hi = tc::smem_u32(sK + (2 * s) * kKBytes), k_lo = k_hi + kKBytes;
                 const uint32_t d = tmem + (uint32_t)(s * 64);
@@ -369,8 +382,11 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
                     load_kv(i + 2);
                 }
             }
+            // K/V copies still in flight land before the CTA exits
+            for (int i = kv_landed; i < kv_issued; ++i)
+                tc::mbar_drain(&kv_full[i & 1], (uint32_t)(i >> 1) & 1u);
             tc::umma_commit(done);
-            tc::mbar_wait(done, 0, a.err);
+            tc::mbar_drain(done, 0);
         }
         __syncwarp();
     } else {

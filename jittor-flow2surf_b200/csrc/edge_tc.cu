@@ -6,21 +6,29 @@
 // a tcgen05 MMA with the hidden rows as the A operand. Nothing per edge
 // reaches HBM.
 //
-// Persistent CTA of 512 threads; W_po resident in shared memory (TMA,
-// 128-byte swizzle, K-major), every per-channel parameter staged in shared
-// memory; per tile of 128 edge rows (128 / K points):
-//   1. hidden: 4 threads per edge row gather xyz_i, xyz_j and evaluate
-//      W_in g + b_in, the HPE LayerNorm (E[h^2] - E[h]^2, eps 1e-5) and GELU
-//      for a quarter of the H channels, writing them straight into shared
-//      memory in the swizzled layout the MMA reads (generic-proxy writes
-//      fenced for the async proxy);
-//   2. one thread issues the MMAs (M = 128, N = C_out) into TMEM;
-//   3. 16 warps = 4 TMEM lane quarters x 4 column groups: the message
-//      content[j] + content[i] + (acc + b_po) is formed once and written back
-//      to TMEM, the two-pass LayerNorm (eps 1e-6) reads only TMEM, and after
-//      the affine + LeakyReLU the max over each point's K edge rows (K lanes)
-//      is a register butterfly across lanes that leaves lane = channel, so the
-//      output row is stored coalesced.
+// Persistent CTA of 17 warps, specialised and pipelined over tiles of 128
+// edge rows (128 / K points); W_po resident in shared memory (TMA or an
+// in-kernel bf16 conversion, 128-byte swizzle, K-major):
+//   warps 0-7   hidden producers, two lanes per edge row: gather xyz_i,
+//               xyz_j; the HPE LayerNorm statistics (E[h^2] - E[h]^2, eps
+//               1e-5) of h = W_in g + b_in come from the Gram matrix of W_in
+//               (computed once per CTA) in O(36) instead of a pass over H;
+//               once the A buffer is free (one or two buffers, whatever
+//               shared memory holds) evaluate h with the LayerNorm and GELU,
+//               write the row into the swizzled buffer and arrive on its
+//               "full" barrier;
+//   warps 8-15  epilogue, two warps per TMEM lane quarter splitting the
+//               output channels: the message content[j] + content[i] +
+//               (acc + b_po) is formed once and written back to TMEM, the
+//               two-pass LayerNorm (eps 1e-6) reads only TMEM, and after the
+//               affine + LeakyReLU the max over each point's K edge rows (K
+//               lanes) is a register butterfly across lanes that leaves
+//               lane = channel, so the output row is stored coalesced;
+//   warp 16     allocates TMEM; one lane issues the MMAs (M = 128, N = C_out)
+//               into one of two TMEM accumulators and commits "A free" and
+//               "accumulator ready".
+// So the hidden rows of tile t + 1 are computed while the epilogue of tile t
+// runs, and the MMAs overlap both.
 #include <cfloat>
 #include <cstring>
 
@@ -30,11 +38,16 @@
 namespace f2s {
 namespace {
 
-constexpr int kThreads = 512;
 constexpr int kRows = 128;
-constexpr int kParts = 4;    // threads per row in phase 1, column groups in phase 3
-constexpr int kMaxPer = 32;  // hidden channels per thread: H <= 128
+constexpr int kProducerWarps = 8;
+constexpr int kEpilogueWarps = 8;
+constexpr int kEpiWarp0 = kProducerWarps;
+constexpr int kMmaWarp = kProducerWarps + kEpilogueWarps;
+constexpr int kThreads = (kMmaWarp + 1) * 32;
+constexpr int kProducerThreads = kProducerWarps * 32;
+constexpr int kEpilogueThreads = kEpilogueWarps * 32;
 constexpr unsigned kFull = 0xffffffffu;
+constexpr int kEpiBarrier = 1;  // named barrier of the epilogue warps
 
 struct EdgeTcArgs {
     const float* content;
@@ -42,7 +55,8 @@ struct EdgeTcArgs {
     const float* xyz4;
     const int32_t* idx;
     int B, M, K, log2K, H, cout;
-    int ppt;  // points per tile (128 / K)
+    int ppt;     // points per tile (128 / K)
+    int a_bufs;  // hidden-row buffers (1 or 2)
     const float* hpe_w;
     const float* hpe_b;
     const float* hpe_ln_w;
@@ -67,6 +81,49 @@ __device__ __forceinline__ void fence_proxy_async() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+__device__ __forceinline__ void epi_barrier() {
+    asm volatile("bar.sync %0, %1;" ::"n"(kEpiBarrier), "n"(kEpilogueThreads) : "memory");
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float lo_elem, float hi_elem) {
+    const __nv_bfloat162 b = __floats2bfloat162_rn(lo_elem, hi_elem);
+    return *reinterpret_cast<const uint32_t*>(&b);
+}
+
+// HPE input projection of one channel: b + W g with the channel's
+// parameters packed {w0..w5, b, 0}; same operation order as edge.cu.
+__device__ __forceinline__ float hpe_pre(const float* prm, const float (&g)[6]) {
+    const float4 w0 = *reinterpret_cast<const float4*>(prm);
+    const float4 w1 = *reinterpret_cast<const float4*>(prm + 4);
+    float v = w1.z;
+    v = fmaf(g[0], w0.x, v);
+    v = fmaf(g[1], w0.y, v);
+    v = fmaf(g[2], w0.z, v);
+    v = fmaf(g[3], w0.w, v);
+    v = fmaf(g[4], w1.x, v);
+    v = fmaf(g[5], w1.y, v);
+    return v;
+}
+
+// GELU(x) = x * Phi(x) with Phi from the erf approximation of Abramowitz and
+// Stegun, Handbook of Mathematical Functions, eq. 7.1.26 (after Hastings):
+//   erf(z) = 1 - t (a1 + t (a2 + t (a3 + t (a4 + t a5)))) exp(-z^2),
+//   t = 1 / (1 + p z), z >= 0, |error| <= 1.5e-7,
+// so with z = |x| / sqrt(2) and q = (1 - erf(z)) / 2, Phi(x) = q for x < 0 and
+// 1 - q otherwise (no cancellation in the negative tail). The coefficients
+// below carry the factor 1/2. The error is far below the operand rounding of
+// the tensor-core contraction the hidden rows feed (2^-18 relative at best).
+__device__ __forceinline__ float gelu_as(float x) {
+    const float z = fabsf(x) * 0.70710678118654752f;
+    const float t = __fdividef(1.0f, fmaf(0.3275911f, z, 1.0f));
+    float q = fmaf(t, 0.5307027145f, -0.7265760135f);
+    q = fmaf(t, q, 0.7107068705f);
+    q = fmaf(t, q, -0.142248368f);
+    q = fmaf(t, q, 0.127414796f);
+    q = q * t * __expf(-z * z);
+    return x * (x < 0.0f ? q : 1.0f - q);
+}
+
 // Operand modes of the edge contraction.
 enum EdgeMode : int {
     kModeTf32 = 0,   // fp32 hidden rows and weights read as tf32
@@ -87,63 +144,83 @@ edge_tc_kernel(const __grid_constant__ CUtensorMap map_w, const EdgeTcArgs a) {
     constexpr int kPer = 16 / kElem;   // elements per 16-byte chunk
     const int H = a.H, cout = a.cout, K = a.K;
     const int kblocks = (H + kBk - 1) / kBk;
-    const size_t a_bytes = (size_t)kblocks * kRows * 128;
+    const size_t a_bytes = (size_t)kblocks * kRows * 128;  // one operand copy of a tile
+    const size_t a_buf_bytes = a_bytes * (kSplit ? 2 : 1);  // + low halves
     const size_t b_bytes = (size_t)kblocks * cout * 128;
-    unsigned char* sA = smem;                     // kblocks x 16 KB
-    unsigned char* sAlo = sA + a_bytes;           // split mode: low halves
-    unsigned char* sB = sAlo + (kSplit ? a_bytes : 0);
+    unsigned char* sA = smem;                               // a_bufs x a_buf_bytes
+    unsigned char* sB = sA + (size_t)a.a_bufs * a_buf_bytes;
     unsigned char* sBlo = sB + b_bytes;
-    float* sW = reinterpret_cast<float*>(sBlo + (kSplit ? b_bytes : 0));  // H x 6
-    float* sHb = sW + H * 6;
-    float* sHg = sHb + H;
-    float* sHs = sHg + H;
-    float* sCb = sHs + H;                                         // cout
-    float* sLg = sCb + cout;
-    float* sLs = sLg + cout;
-    float* sStat = sLs + cout;                                    // [2][kParts][128]
-    int* sJ = reinterpret_cast<int*>(sStat + 2 * kParts * kRows); // [128]
+    // per hidden channel c: {w0..w5, b, 0} at hp_off(c), {gain, shift} at
+    // hn_off(c); the upper half of the channels is shifted by 16 / 8 bytes so
+    // the two lanes of a row (one per half) read different banks
+    float* sHp = reinterpret_cast<float*>(sBlo + (kSplit ? b_bytes : 0));
+    float* sHn = sHp + H * 8 + 4;
+    // LayerNorm moments of the pre-activations as functions of g:
+    // sum = bsum + wsum . g, sum of squares = bsq + g . (2 u + G g)
+    float* sGram = sHn + H * 2 + 4;  // G[36], u[6], wsum[6], bsum, bsq (16-byte aligned)
+    float* sCb = sGram + 52;                                              // cout
+    float* sLn = sCb + cout;                                              // cout x {gain, shift}
+    float* sStat = sLn + cout * 2;                                        // [2][2][128]
     uint64_t* bars = reinterpret_cast<uint64_t*>(
-        (reinterpret_cast<uintptr_t>(sJ + kRows) + 7) & ~uintptr_t(7));  // [0] weights, [1] mma
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2);
-    int* sFlag = reinterpret_cast<int*>(tmem_slot + 1);
+        (reinterpret_cast<uintptr_t>(sStat + 4 * kRows) + 7) & ~uintptr_t(7));
+    uint64_t* a_full = bars;        // [2]
+    uint64_t* a_empty = bars + 2;   // [2]
+    uint64_t* t_full = bars + 4;    // [2]
+    uint64_t* t_empty = bars + 6;   // [2]
+    uint64_t* w_bar = bars + 8;
+    uint64_t* mma_done = bars + 9;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
+    int* sEpiFail = reinterpret_cast<int*>(tmem_slot + 1);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int R = a.B * a.M;
     const int n_tiles = (R + a.ppt - 1) / a.ppt;
     uint32_t tmem_cols = 32;
-    while (tmem_cols < (uint32_t)cout) tmem_cols <<= 1;
+    while (tmem_cols < (uint32_t)(2 * cout)) tmem_cols <<= 1;
 
-    for (int i = tid; i < H * 6; i += kThreads) sW[i] = a.hpe_w[i];
-    for (int i = tid; i < H; i += kThreads) {
-        sHb[i] = a.hpe_b[i];
-        sHg[i] = a.hpe_ln_w[i];
-        sHs[i] = a.hpe_ln_b[i];
+    const int hh = H >> 1;
+    for (int c = tid; c < H; c += kThreads) {
+        const float* w = a.hpe_w + (size_t)c * 6;
+        float* d = sHp + c * 8 + (c >= hh ? 4 : 0);
+        d[0] = w[0]; d[1] = w[1]; d[2] = w[2]; d[3] = w[3]; d[4] = w[4]; d[5] = w[5];
+        d[6] = a.hpe_b[c];
+        d[7] = 0.0f;
+        float* n = sHn + c * 2 + (c >= hh ? 2 : 0);
+        n[0] = a.hpe_ln_w[c];
+        n[1] = a.hpe_ln_b[c];
     }
-    for (int i = tid; i < cout; i += kThreads) {
-        sCb[i] = a.contrib_b[i];
-        sLg[i] = a.ln_w[i];
-        sLs[i] = a.ln_b[i];
+    if (tid < 50) {
+        // 50 sums over the hidden channels, in double
+        double acc = 0.0;
+        for (int c = 0; c < H; ++c) {
+            const float* w = a.hpe_w + (size_t)c * 6;
+            const double b = a.hpe_b[c];
+            if (tid < 36) acc += (double)w[tid / 6] * (double)w[tid % 6];
+            else if (tid < 42) acc += (double)w[tid - 36] * b;
+            else if (tid < 48) acc += (double)w[tid - 42];
+            else if (tid == 48) acc += b;
+            else acc += b * b;
+        }
+        sGram[tid] = (float)acc;
+    }
+    for (int c = tid; c < cout; c += kThreads) {
+        sCb[c] = a.contrib_b[c];
+        sLn[2 * c] = a.ln_w[c];
+        sLn[2 * c + 1] = a.ln_b[c];
     }
     if (tid == 0) {
-        tc::mbar_init(&bars[0], 1);
-        tc::mbar_init(&bars[1], 1);
+        for (int b = 0; b < 2; ++b) {
+            tc::mbar_init(&a_full[b], kProducerThreads);
+            tc::mbar_init(&a_empty[b], 1);
+            tc::mbar_init(&t_full[b], 1);
+            tc::mbar_init(&t_empty[b], kEpilogueThreads);
+        }
+        tc::mbar_init(w_bar, 1);
+        tc::mbar_init(mma_done, 1);
+        *sEpiFail = 0;
         tc::fence_barrier_init();
     }
-    if (warp == 0) tc::tmem_alloc(tmem_slot, tmem_cols);
-    tc::tc_fence_before();
-    __syncthreads();
-    tc::tc_fence_after();
-    const uint32_t tmem_base = *tmem_slot;
-
-    bool ok = true;
-    if constexpr (kTf32) {
-        if (tid == 0) {
-            tc::mbar_arrive_expect_tx(&bars[0], (uint32_t)(kblocks * cout * 128));
-            for (int kb = 0; kb < kblocks; ++kb)
-                tc::tma_load_2d(sB + (size_t)kb * cout * 128, &map_w, &bars[0], kb * kBk, 0);
-            ok = tc::mbar_wait(&bars[0], 0, a.err);
-        }
-    } else {
+    if constexpr (!kTf32) {
         // bf16 weights (and their residuals in split mode), swizzled like TMA would
         const int chunks_per_row = H / 8;
         for (int t = tid; t < cout * chunks_per_row; t += kThreads) {
@@ -155,35 +232,35 @@ edge_tc_kernel(const __grid_constant__ CUtensorMap map_w, const EdgeTcArgs a) {
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
                 const __nv_bfloat162 h2 = __floats2bfloat162_rn(w[2 * e], w[2 * e + 1]);
-                const __nv_bfloat162 l2 = __floats2bfloat162_rn(
-                    w[2 * e] - __bfloat162float(h2.x), w[2 * e + 1] - __bfloat162float(h2.y));
                 hi[e] = *reinterpret_cast<const uint32_t*>(&h2);
-                lo[e] = *reinterpret_cast<const uint32_t*>(&l2);
+                lo[e] = pack_bf16(w[2 * e] - __bfloat162float(h2.x),
+                                  w[2 * e + 1] - __bfloat162float(h2.y));
             }
             const size_t off = (size_t)(q / 8) * cout * 128 + sw128_offset(n, q % 8);
             *reinterpret_cast<uint4*>(sB + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
             if (kSplit) *reinterpret_cast<uint4*>(sBlo + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
         }
         fence_proxy_async();
-        __syncthreads();
     }
+    if (warp == kMmaWarp) tc::tmem_alloc(tmem_slot, tmem_cols);
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
 
-    const int hper = H / kParts;
-    uint32_t mma_phase = 0;
-
-    for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
-        // one thread decides whether to go on; every thread follows it
-        if (tid == 0) *sFlag = *reinterpret_cast<volatile int*>(a.err) != tc::kTcOk;
-        __syncthreads();
-        if (*sFlag) break;
-        const int p0 = tile * a.ppt;
-        // ---- 1. hidden rows -> A operand --------------------------------
-        {
-            const int row = tid & (kRows - 1);
-            const int part = tid >> 7;
+    if (warp < kProducerWarps) {
+        // ---------------- hidden producers ----------------
+        const int row = (warp << 4) + (lane >> 1);
+        const int half = lane & 1;
+        const int ch0 = half * hh;
+        const float* hp = sHp + ch0 * 8 + half * 4;  // this lane's half of the records
+        const float* hn = sHn + ch0 * 2 + half * 2;
+        int it = 0;
+        for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
+            const int p0 = tile * a.ppt;
             const int pl = row >> a.log2K;
             const int p = p0 + pl;
-            const bool valid = pl < a.ppt && p < R;
+            const bool valid = p < R;
             float g[6] = {0, 0, 0, 0, 0, 0};
             if (valid) {
                 const int kk = row - (pl << a.log2K);
@@ -193,119 +270,92 @@ edge_tc_kernel(const __grid_constant__ CUtensorMap map_w, const EdgeTcArgs a) {
                 const float4 xj = *reinterpret_cast<const float4*>(a.xyz4 + (size_t)jrow * 4);
                 g[0] = xj.x - xi.x; g[1] = xj.y - xi.y; g[2] = xj.z - xi.z;
                 g[3] = xi.x; g[4] = xi.y; g[5] = xi.z;
-                if (part == 0) sJ[row] = jrow;
-            } else if (part == 0) {
-                sJ[row] = -1;
             }
-            const int ch0 = part * hper;
-            float pre[kMaxPer];
-            float s = 0.0f, s2 = 0.0f;
+            // LayerNorm moments of the pre-activations W_in g + b_in from the
+            // Gram matrix of W_in: no pass over the H channels
+            float s = sGram[48], s2 = sGram[49];
 #pragma unroll
-            for (int i = 0; i < kMaxPer; ++i) {
-                if (i < hper) {
-                    const int c = ch0 + i;
-                    float v = sHb[c];
+            for (int d = 0; d < 6; ++d) {
+                float t = 2.0f * sGram[36 + d];
 #pragma unroll
-                    for (int d = 0; d < 6; ++d) v = fmaf(g[d], sW[c * 6 + d], v);
-                    pre[i] = v;
-                    s += v;
-                    s2 = fmaf(v, v, s2);
-                }
+                for (int e = 0; e < 6; ++e) t = fmaf(sGram[d * 6 + e], g[e], t);
+                s2 = fmaf(t, g[d], s2);
+                s = fmaf(sGram[42 + d], g[d], s);
             }
-            sStat[part * kRows + row] = s;
-            sStat[(kParts + part) * kRows + row] = s2;
-            __syncthreads();
-            float ts = 0.0f, ts2 = 0.0f;
-#pragma unroll
-            for (int q = 0; q < kParts; ++q) {
-                ts += sStat[q * kRows + row];
-                ts2 += sStat[(kParts + q) * kRows + row];
-            }
-            const float mean = ts / (float)H;
-            const float var = fmaxf(ts2 / (float)H - mean * mean, 0.0f);
+            const float mean = s / (float)H;
+            const float var = fmaxf(s2 / (float)H - mean * mean, 0.0f);
             const float rstd = rsqrtf(var + 1e-5f);
+            // wait until the MMAs of the tile that last used this buffer are done
+            const int abuf = a.a_bufs == 2 ? (it & 1) : 0;
+            const uint32_t round = a.a_bufs == 2 ? (uint32_t)(it >> 1) : (uint32_t)it;
+            int ready = 0;
+            if (lane == 0) ready = tc::mbar_wait(&a_empty[abuf], (round & 1u) ^ 1u, a.err) ? 1 : 0;
+            if (!__shfl_sync(kFull, ready, 0)) break;
+            unsigned char* dA = sA + (size_t)abuf * a_buf_bytes;
+            // pre-activation, GELU(LN), packed as the MMA reads it
+            for (int i0 = 0; i0 < hh; i0 += kPer) {
+                float o[kPer];
 #pragma unroll
-            for (int i0 = 0; i0 < kMaxPer; i0 += kPer) {
-                if (i0 < hper) {
-                    float o[kPer];
+                for (int e = 0; e < kPer; ++e) {
+                    const float v = hpe_pre(hp + (i0 + e) * 8, g);
+                    const float2 gs = *reinterpret_cast<const float2*>(hn + 2 * (i0 + e));
+                    o[e] = valid ? gelu_as((v - mean) * rstd * gs.x + gs.y) : 0.0f;
+                }
+                const int c = ch0 + i0;
+                unsigned char* dst =
+                    dA + (size_t)(c / kBk) * kRows * 128 + sw128_offset(row, (c % kBk) / kPer);
+                if constexpr (kTf32) {
+                    *reinterpret_cast<float4*>(dst) = make_float4(o[0], o[1], o[2], o[3]);
+                } else {
+                    uint32_t hi[4], lo[4];
 #pragma unroll
-                    for (int e = 0; e < kPer; ++e) {
-                        const int c = ch0 + i0 + e;
-                        o[e] = valid ? f2s_gelu_erf((pre[i0 + e] - mean) * rstd * sHg[c] + sHs[c])
-                                     : 0.0f;
-                    }
-                    const int c = ch0 + i0;
-                    unsigned char* dst = sA + (size_t)(c / kBk) * kRows * 128 +
-                                         sw128_offset(row, (c % kBk) / kPer);
-                    if constexpr (kTf32) {
-                        *reinterpret_cast<float4*>(dst) = make_float4(o[0], o[1], o[2], o[3]);
-                    } else {
-                        uint32_t w[4], wl[4];
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const __nv_bfloat162 b2 = __floats2bfloat162_rn(o[2 * e], o[2 * e + 1]);
-                            w[e] = *reinterpret_cast<const uint32_t*>(&b2);
-                            if (kSplit) {
-                                const __nv_bfloat162 l2 = __floats2bfloat162_rn(
-                                    o[2 * e] - __bfloat162float(b2.x),
-                                    o[2 * e + 1] - __bfloat162float(b2.y));
-                                wl[e] = *reinterpret_cast<const uint32_t*>(&l2);
-                            }
-                        }
-                        *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+                    for (int e = 0; e < 4; ++e) {
+                        const __nv_bfloat162 h2 = __floats2bfloat162_rn(o[2 * e], o[2 * e + 1]);
+                        hi[e] = *reinterpret_cast<const uint32_t*>(&h2);
                         if (kSplit)
-                            *reinterpret_cast<uint4*>(dst + (sAlo - sA)) =
-                                make_uint4(wl[0], wl[1], wl[2], wl[3]);
+                            lo[e] = pack_bf16(o[2 * e] - __bfloat162float(h2.x),
+                                              o[2 * e + 1] - __bfloat162float(h2.y));
                     }
+                    *reinterpret_cast<uint4*>(dst) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                    if (kSplit)
+                        *reinterpret_cast<uint4*>(dst + a_bytes) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
                 }
             }
+            fence_proxy_async();
+            tc::mbar_arrive(&a_full[abuf]);
         }
-        fence_proxy_async();
-        tc::tc_fence_before();
-        __syncthreads();
-        // ---- 2. MMA -------------------------------------------------------
-        if (tid == 0) {
+    } else if (warp < kMmaWarp) {
+        // ---------------- epilogue ----------------
+        const int quarter = warp & 3;
+        const int cpart = (warp - kEpiWarp0) >> 2;
+        const int erow = quarter * 32 + lane;  // TMEM lane = edge row
+        const int nchunks = cout / 32;
+        int it = 0;
+        for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
+            const int tbuf = it & 1;
+            const uint32_t tph = (uint32_t)(it >> 1) & 1u;
+            int ready = 0;
+            if (lane == 0) ready = tc::mbar_wait(&t_full[tbuf], tph, a.err) ? 1 : 0;
+            ready = __shfl_sync(kFull, ready, 0);
+            if (!ready && lane == 0) *reinterpret_cast<volatile int*>(sEpiFail) = 1;
+            epi_barrier();  // every epilogue warp takes the same decision
+            if (*reinterpret_cast<volatile int*>(sEpiFail)) break;
             tc::tc_fence_after();
-            if (ok) {
-                const uint32_t a0 = tc::smem_u32(sA), b0 = tc::smem_u32(sB);
-                const uint32_t a_lo = tc::smem_u32(sAlo), b_lo = tc::smem_u32(sBlo);
-                for (int kb = 0; kb < kblocks; ++kb)
-#pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        if ((kb * kBk + k * (32 / kElem)) >= H) break;
-                        const uint32_t ao = kb * kRows * 128 + k * 32;
-                        const uint32_t bo = kb * cout * 128 + k * 32;
-                        const uint64_t da = tc::sw128_desc(a0 + ao);
-                        const uint64_t db = tc::sw128_desc(b0 + bo);
-                        tc::umma<kTf32>(tmem_base, da, db, a.idesc, (kb | k) ? 1u : 0u);
-                        if (kSplit) {
-                            tc::umma<false>(tmem_base, da, tc::sw128_desc(b_lo + bo), a.idesc, 1u);
-                            tc::umma<false>(tmem_base, tc::sw128_desc(a_lo + ao), db, a.idesc, 1u);
-                        }
-                    }
-            }
-            tc::umma_commit(&bars[1]);
-            *sFlag = tc::mbar_wait(&bars[1], mma_phase, a.err) ? 0 : 1;
-        }
-        __syncthreads();
-        if (*sFlag) break;
-        mma_phase ^= 1u;
-        tc::tc_fence_after();
-        // ---- 3. message LayerNorm, LeakyReLU, max over k --------------------
-        {
-            const int quarter = warp & 3;
-            const int cpart = warp >> 2;
-            const int erow = quarter * 32 + lane;  // TMEM lane = edge row
-            const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16);
-            const int ej = sJ[erow];
+            const int p0 = tile * a.ppt;
             const int ep = p0 + (erow >> a.log2K);
+            int ej = -1;
+            if (ep < R) {
+                const int kk = erow & (K - 1);
+                ej = (ep / a.M) * a.M + a.idx[(size_t)ep * K + kk];
+            }
+            const uint32_t taddr =
+                tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(tbuf * cout);
             const float* cj = a.content + (size_t)(ej < 0 ? 0 : ej) * a.ldc;
             // centre terms: one point per K consecutive lanes, mostly a broadcast
             const float* ci = a.content + (size_t)(ej < 0 ? 0 : ep) * a.ldc + cout;
-            const int nchunks = cout / 32;
             // pass 1: message = content[j] + content[i] + (acc + b_po) -> TMEM
             float sum = 0.0f;
-            for (int ch = cpart; ch < nchunks; ch += kParts) {
+            for (int ch = cpart; ch < nchunks; ch += 2) {
                 const int cb = ch * 32;
                 float v[32];
                 tc::tmem_ld32(taddr + (uint32_t)cb, v);
@@ -313,23 +363,21 @@ edge_tc_kernel(const __grid_constant__ CUtensorMap map_w, const EdgeTcArgs a) {
                 for (int i = 0; i < 32; i += 4) {
                     const float4 nj = *reinterpret_cast<const float4*>(cj + cb + i);
                     const float4 ni = *reinterpret_cast<const float4*>(ci + cb + i);
-                    v[i + 0] = nj.x + ni.x + (v[i + 0] + sCb[cb + i + 0]);
-                    v[i + 1] = nj.y + ni.y + (v[i + 1] + sCb[cb + i + 1]);
-                    v[i + 2] = nj.z + ni.z + (v[i + 2] + sCb[cb + i + 2]);
-                    v[i + 3] = nj.w + ni.w + (v[i + 3] + sCb[cb + i + 3]);
+                    const float4 bb = *reinterpret_cast<const float4*>(sCb + cb + i);
+                    v[i + 0] = nj.x + ni.x + (v[i + 0] + bb.x);
+                    v[i + 1] = nj.y + ni.y + (v[i + 1] + bb.y);
+                    v[i + 2] = nj.z + ni.z + (v[i + 2] + bb.z);
+                    v[i + 3] = nj.w + ni.w + (v[i + 3] + bb.w);
                     sum += (v[i] + v[i + 1]) + (v[i + 2] + v[i + 3]);
                 }
                 tc::tmem_st32(taddr + (uint32_t)cb, v);
             }
             sStat[cpart * kRows + erow] = sum;
-            __syncthreads();
-            float tot = 0.0f;
-#pragma unroll
-            for (int q = 0; q < kParts; ++q) tot += sStat[q * kRows + erow];
-            const float mean = tot / (float)cout;
+            epi_barrier();
+            const float mean = (sStat[erow] + sStat[kRows + erow]) / (float)cout;
             // pass 2: centred second moment
             float q2 = 0.0f;
-            for (int ch = cpart; ch < nchunks; ch += kParts) {
+            for (int ch = cpart; ch < nchunks; ch += 2) {
                 float v[32];
                 tc::tmem_ld32(taddr + (uint32_t)(ch * 32), v);
 #pragma unroll
@@ -338,21 +386,25 @@ edge_tc_kernel(const __grid_constant__ CUtensorMap map_w, const EdgeTcArgs a) {
                     q2 = fmaf(d, d, q2);
                 }
             }
-            sStat[(kParts + cpart) * kRows + erow] = q2;
-            __syncthreads();
-            float totq = 0.0f;
-#pragma unroll
-            for (int q = 0; q < kParts; ++q) totq += sStat[(kParts + q) * kRows + erow];
-            const float rstd = rsqrtf(totq / (float)cout + 1e-6f);
+            sStat[(2 + cpart) * kRows + erow] = q2;
+            epi_barrier();
+            const float rstd =
+                rsqrtf((sStat[2 * kRows + erow] + sStat[3 * kRows + erow]) / (float)cout + 1e-6f);
             // pass 3: affine + LeakyReLU, then max over the K lanes of each point
-            for (int ch = cpart; ch < nchunks; ch += kParts) {
+            for (int ch = cpart; ch < nchunks; ch += 2) {
                 const int cb = ch * 32;
                 float y[32];
                 tc::tmem_ld32(taddr + (uint32_t)cb, y);
+                if (ej >= 0) {
 #pragma unroll
-                for (int i = 0; i < 32; ++i)
-                    y[i] = ej >= 0 ? f2s_leaky((y[i] - mean) * rstd * sLg[cb + i] + sLs[cb + i])
-                                   : -FLT_MAX;
+                    for (int i = 0; i < 32; ++i) {
+                        const float2 gs = *reinterpret_cast<const float2*>(sLn + 2 * (cb + i));
+                        y[i] = f2s_leaky((y[i] - mean) * rstd * gs.x + gs.y);
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) y[i] = -FLT_MAX;
+                }
                 int off = 0;
 #pragma unroll
                 for (int s = 0; s < 5; ++s) {
@@ -377,15 +429,71 @@ edge_tc_kernel(const __grid_constant__ CUtensorMap map_w, const EdgeTcArgs a) {
                         if (i < nv) o[i] = y[i];
                 }
             }
+            tc::tc_fence_before();
+            tc::mbar_arrive(&t_empty[tbuf]);
         }
-        tc::tc_fence_before();
+    } else {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            bool ok = true;
+            if constexpr (kTf32) {
+                tc::mbar_arrive_expect_tx(w_bar, (uint32_t)(kblocks * cout * 128));
+                for (int kb = 0; kb < kblocks; ++kb)
+                    tc::tma_load_2d(sB + (size_t)kb * cout * 128, &map_w, w_bar, kb * kBk, 0);
+                ok = tc::mbar_wait(w_bar, 0, a.err);
+                if (!ok) tc::mbar_drain(w_bar, 0);  // the weight copies land before the CTA exits
+            }
+            int it = 0;
+            for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x, ++it) {
+                const int abuf = a.a_bufs == 2 ? (it & 1) : 0;
+                const uint32_t round = a.a_bufs == 2 ? (uint32_t)(it >> 1) : (uint32_t)it;
+                const int tbuf = it & 1;
+                const uint32_t tph = (uint32_t)(it >> 1) & 1u;
+                if (!tc::mbar_wait(&t_empty[tbuf], tph ^ 1u, a.err)) break;
+                if (!tc::mbar_wait(&a_full[abuf], round & 1u, a.err)) break;
+                tc::tc_fence_after();
+                const uint32_t d = tmem_base + (uint32_t)(tbuf * cout);
+                const uint32_t a0 = tc::smem_u32(sA + (size_t)abuf * a_buf_bytes);
+                const uint32_t b0 = tc::smem_u32(sB), b_lo = tc::smem_u32(sBlo);
+                for (int kb = 0; kb < kblocks; ++kb)
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        if ((kb * kBk + k * (32 / kElem)) >= H) break;
+                        const uint32_t ao = kb * kRows * 128 + k * 32;
+                        const uint32_t bo = kb * cout * 128 + k * 32;
+                        const uint64_t da = tc::sw128_desc(a0 + ao);
+                        const uint64_t db = tc::sw128_desc(b0 + bo);
+                        tc::umma<kTf32>(d, da, db, a.idesc, (kb | k) ? 1u : 0u);
+                        if (kSplit) {
+                            tc::umma<false>(d, da, tc::sw128_desc(b_lo + bo), a.idesc, 1u);
+                            tc::umma<false>(d, tc::sw128_desc(a0 + (uint32_t)a_bytes + ao), db,
+                                            a.idesc, 1u);
+                        }
+                    }
+                tc::umma_commit(&a_empty[abuf]);
+                tc::umma_commit(&t_full[tbuf]);
+            }
+            // every MMA this thread issued has completed before TMEM is freed
+            tc::umma_commit(mma_done);
+            tc::mbar_drain(mma_done, 0);
+        }
+        __syncwarp();
     }
     tc::tc_fence_before();
     __syncthreads();
-    if (warp == 0) {
+    if (warp == kMmaWarp) {
         tc::tc_fence_after();
         tc::tmem_dealloc(tmem_base, tmem_cols);
     }
+}
+
+// Shared memory of the kernel for `bufs` hidden-row buffers.
+size_t edge_tc_smem(int mode, int H, int cout, int bufs) {
+    const int elem = mode == kModeTf32 ? 4 : 2;
+    const size_t kblocks = (size_t)ceil_div(H, 128 / elem);
+    const size_t copies = mode == kModeSplit ? 2 : 1;
+    return 1024 + copies * kblocks * 128 * ((size_t)bufs * kRows + cout) +
+           sizeof(float) * ((size_t)H * 10 + 60 + (size_t)cout * 3 + 4 * kRows) + 128;
 }
 
 }  // namespace
@@ -397,25 +505,31 @@ int edge_stage_tc(const EdgeArgs& e, int precision, cudaStream_t st) {
     if (e.B == 0 || e.M == 0) return F2S_OK;
     int log2K = 0;
     while ((1 << log2K) < e.K) ++log2K;
-    if (e.geometry != nullptr || e.xyz4 == nullptr || e.D != 6 || e.H > kParts * kMaxPer ||
+    if (e.geometry != nullptr || e.xyz4 == nullptr || e.D != 6 || e.H > 128 ||
         e.H % 32 != 0 || e.cout % 32 != 0 || e.cout > 256 || (1 << log2K) != e.K || e.K > 32 ||
         ((uintptr_t)e.content & 15) != 0 || e.ldc % 4 != 0 || ((uintptr_t)e.contrib_w & 15) != 0)
         return fail(F2S_ERR_UNSUPPORTED, "edge stage shape outside the tensor-core kernel");
-    const int mode = precision == F2S_PRECISION_TF32   ? kModeTf32
-                     : precision == F2S_PRECISION_BF16 ? kModeBf16
-                                                       : kModeSplit;
     F2S_REQUIRE(precision == F2S_PRECISION_TF32 || precision == F2S_PRECISION_BF16 ||
                     precision == F2S_PRECISION_BF16X3,
                 "edge_tc: precision %d", precision);
+    const int mode = precision == F2S_PRECISION_TF32   ? kModeTf32
+                     : precision == F2S_PRECISION_BF16 ? kModeBf16
+                                                       : kModeSplit;
     int* err = tc_error_word();
     if (!err) return fail(F2S_ERR_CUDA, "edge_tc: device error word unavailable");
     const bool tf32 = mode == kModeTf32;
-    const int elem = tf32 ? 4 : 2;
-    const int bk = 128 / elem;
-    const int kblocks = ceil_div(e.H, bk);
+    const int bk = tf32 ? 32 : 64;
     CUtensorMap map;
     if (tf32) F2S_TRY(make_tensor_map_2d(&map, e.contrib_w, true, e.cout, e.H, e.H, e.cout, bk));
     else memset(&map, 0, sizeof(map));
+    constexpr size_t kSmemLimit = 227 * 1024;
+    int bufs = 2;
+    size_t smem = edge_tc_smem(mode, e.H, e.cout, bufs);
+    if (smem > kSmemLimit) {
+        bufs = 1;
+        smem = edge_tc_smem(mode, e.H, e.cout, bufs);
+    }
+    F2S_LIMIT(smem <= kSmemLimit, "edge_tc: %zu bytes of shared memory", smem);
     EdgeTcArgs a{};
     a.content = e.content;
     a.ldc = e.ldc;
@@ -428,6 +542,7 @@ int edge_stage_tc(const EdgeArgs& e, int precision, cudaStream_t st) {
     a.H = e.H;
     a.cout = e.cout;
     a.ppt = kRows / e.K;
+    a.a_bufs = bufs;
     a.hpe_w = e.hpe_w;
     a.hpe_b = e.hpe_b;
     a.hpe_ln_w = e.hpe_ln_w;
@@ -440,12 +555,6 @@ int edge_stage_tc(const EdgeArgs& e, int precision, cudaStream_t st) {
     a.ldo = e.ldo;
     a.idesc = tc::make_idesc(kRows, e.cout, tf32 ? 2u : 1u);
     a.err = err;
-    const size_t copies = mode == kModeSplit ? 2 : 1;
-    const size_t smem = 1024 + copies * ((size_t)kblocks * kRows * 128 +
-                                         (size_t)kblocks * e.cout * 128) +
-                        sizeof(float) * ((size_t)e.H * 9 + (size_t)e.cout * 3 + 2 * kParts * kRows) +
-                        sizeof(int) * kRows + 64;
-    F2S_LIMIT(smem <= 227 * 1024, "edge_tc: %zu bytes of shared memory", smem);
     const int R = e.B * e.M;
     const int tiles = ceil_div(R, a.ppt);
     const int grid = tiles < sm_count() ? tiles : sm_count();

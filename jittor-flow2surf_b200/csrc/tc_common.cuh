@@ -14,7 +14,12 @@
 namespace f2s {
 namespace tc {
 
-constexpr uint32_t kSpinLimit = 1u << 26;
+// Polls of a bounded wait. Each poll is a try_wait that may park the thread
+// for up to kSuspendHintNs (it wakes as soon as the phase completes), and
+// polls past the first 256 also sleep, so a wait ends after between roughly
+// 0.3 s (hint ignored) and 4.5 s (hint honoured) when nothing arrives.
+constexpr uint32_t kSpinLimit = 1u << 22;
+constexpr uint32_t kSuspendHintNs = 1000;
 
 // Error codes written to the kernel's error word.
 enum TcError : int { kTcOk = 0, kTcWaitTimeout = 1 };
@@ -46,10 +51,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     uint32_t done;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(done)
-        : "r"(smem_u32(bar)), "r"(parity)
+        : "r"(smem_u32(bar)), "r"(parity), "n"(kSuspendHintNs)
         : "memory");
     return done != 0;
 }
@@ -59,10 +64,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
     for (uint32_t i = 0; i < kSpinLimit; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 1023u) == 1023u && *reinterpret_cast<volatile int*>(err) != kTcOk) return false;
+        if ((i & 63u) == 63u && *reinterpret_cast<volatile int*>(err) != kTcOk) return false;
         if (i > 256) __nanosleep(64);
     }
     atomicExch(err, kTcWaitTimeout);
+    return false;
+}
+
+// Bounded wait that ignores the error word: used on the way out for copies
+// and MMAs already in flight, which must complete before the CTA releases its
+// shared or tensor memory. False when the phase did not complete in time.
+__device__ __forceinline__ bool mbar_drain(uint64_t* bar, uint32_t parity) {
+    for (uint32_t i = 0; i < kSpinLimit; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (i > 256) __nanosleep(64);
+    }
     return false;
 }
 

@@ -137,12 +137,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             }
             if (!ok) {
                 // let the copies already issued land before the CTA exits
-                for (int s = 0; s < S; ++s) {
-                    if (!(pending & (1u << s))) continue;
-                    const uint32_t ph = (pending_phase >> s) & 1u;
-                    for (uint32_t i = 0; i < tc::kSpinLimit; ++i)
-                        if (tc::mbar_try_wait(&full[s], ph)) break;
-                }
+                for (int s = 0; s < S; ++s)
+                    if (pending & (1u << s)) tc::mbar_drain(&full[s], (pending_phase >> s) & 1u);
             }
         }
     } else if (warp == 1) {
@@ -190,7 +186,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             }
             // every MMA this thread issued has completed before TMEM is freed
             tc::umma_commit(mma_done);
-            tc::mbar_wait(mma_done, 0, g.err);
+            tc::mbar_drain(mma_done, 0);
         }
         __syncwarp();
     } else {
