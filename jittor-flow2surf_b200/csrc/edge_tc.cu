@@ -6,29 +6,30 @@
 // a tcgen05 MMA with the hidden rows as the A operand. Nothing per edge
 // reaches HBM.
 //
-// Persistent CTA of 17 warps, specialised and pipelined over tiles of 128
+// Persistent CTA of 16 warps, specialised and pipelined over tiles of 128
 // edge rows (128 / K points); W_po resident in shared memory (TMA or an
 // in-kernel bf16 conversion, 128-byte swizzle, K-major):
-//   warps 0-7   hidden producers, two lanes per edge row: gather xyz_i,
-//               xyz_j; the HPE LayerNorm statistics (E[h^2] - E[h]^2, eps
-//               1e-5) of h = W_in g + b_in come from the Gram matrix of W_in
-//               (computed once per CTA) in O(36) instead of a pass over H;
-//               once the A buffer is free (one or two buffers, whatever
-//               shared memory holds) evaluate h with the LayerNorm and GELU,
-//               write the row into the swizzled buffer and arrive on its
-//               "full" barrier;
+//   warps 0-7   hidden producers, two lanes per edge row. The geometry g =
+//               [xyz_j - xyz_i, xyz_i] of the next tile is loaded while this
+//               tile is processed; the HPE LayerNorm statistics (E[h^2] -
+//               E[h]^2, eps 1e-5) of h = W_in g + b_in come from the Gram
+//               matrix of W_in (computed once per CTA) in O(36) instead of a
+//               pass over H. Once the A buffer is free (one or two buffers,
+//               whatever shared memory holds) they evaluate h with the
+//               LayerNorm and GELU and write the rows into the swizzled
+//               buffer; then one lane issues the MMAs (M = 128, N = C_out)
+//               into one of two TMEM accumulators and commits "A free" and
+//               "accumulator ready". Warp 0 owns the TMEM allocation.
 //   warps 8-15  epilogue, two warps per TMEM lane quarter splitting the
 //               output channels: the message content[j] + content[i] +
 //               (acc + b_po) is formed once and written back to TMEM, the
 //               two-pass LayerNorm (eps 1e-6) reads only TMEM, and after the
 //               affine + LeakyReLU the max over each point's K edge rows (K
 //               lanes) is a register butterfly across lanes that leaves
-//               lane = channel, so the output row is stored coalesced;
-//   warp 16     allocates TMEM; one lane issues the MMAs (M = 128, N = C_out)
-//               into one of two TMEM accumulators and commits "A free" and
-//               "accumulator ready".
+//               lane = channel, so the output row is stored coalesced.
 // So the hidden rows of tile t + 1 are computed while the epilogue of tile t
-// runs, and the MMAs overlap both.
+// runs, and the MMAs overlap both. Each role has one polling lane per wait;
+// the role's other warps wait on a named barrier and issue nothing.
 #include <cfloat>
 #include <cstring>
 
@@ -42,12 +43,12 @@ constexpr int kRows = 128;
 constexpr int kProducerWarps = 8;
 constexpr int kEpilogueWarps = 8;
 constexpr int kEpiWarp0 = kProducerWarps;
-constexpr int kMmaWarp = kProducerWarps + kEpilogueWarps;
-constexpr int kThreads = (kMmaWarp + 1) * 32;
+constexpr int kThreads = (kProducerWarps + kEpilogueWarps) * 32;
 constexpr int kProducerThreads = kProducerWarps * 32;
 constexpr int kEpilogueThreads = kEpilogueWarps * 32;
 constexpr unsigned kFull = 0xffffffffu;
-constexpr int kEpiBarrier = 1;  // named barrier of the epilogue warps
+constexpr int kEpiBarrier = 1;   // named barrier of the epilogue warps
+constexpr int kProdBarrier = 2;  // named barrier of the producer warps
 
 struct EdgeTcArgs {
     const float* content;
@@ -85,6 +86,10 @@ __device__ __forceinline__ void epi_barrier() {
     asm volatile("bar.sync %0, %1;" ::"n"(kEpiBarrier), "n"(kEpilogueThreads) : "memory");
 }
 
+__device__ __forceinline__ void prod_barrier() {
+    asm volatile("bar.sync %0, %1;" ::"n"(kProdBarrier), "n"(kProducerThreads) : "memory");
+}
+
 __device__ __forceinline__ uint32_t pack_bf16(float lo_elem, float hi_elem) {
     const __nv_bfloat162 b = __floats2bfloat162_rn(lo_elem, hi_elem);
     return *reinterpret_cast<const uint32_t*>(&b);
@@ -105,23 +110,37 @@ __device__ __forceinline__ float hpe_pre(const float* prm, const float (&g)[6]) 
     return v;
 }
 
+__device__ __forceinline__ float rcp_approx(float x) {
+    float r;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
+
+__device__ __forceinline__ float ex2_approx(float x) {
+    float r;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
+
 // GELU(x) = x * Phi(x) with Phi from the erf approximation of Abramowitz and
 // Stegun, Handbook of Mathematical Functions, eq. 7.1.26 (after Hastings):
 //   erf(z) = 1 - t (a1 + t (a2 + t (a3 + t (a4 + t a5)))) exp(-z^2),
-//   t = 1 / (1 + p z), z >= 0, |error| <= 1.5e-7,
-// so with z = |x| / sqrt(2) and q = (1 - erf(z)) / 2, Phi(x) = q for x < 0 and
-// 1 - q otherwise (no cancellation in the negative tail). The coefficients
-// below carry the factor 1/2. The error is far below the operand rounding of
-// the tensor-core contraction the hidden rows feed (2^-18 relative at best).
+//   t = 1 / (1 + p z), z >= 0, |error| <= 1.5e-7.
+// With z = |x| / sqrt(2) and q = (1 - erf(z)) / 2, Phi(x) = q for x < 0 and
+// 1 - q otherwise, so GELU(x) = max(x, 0) - |x| q for every x (no select, no
+// cancellation in the negative tail). The constants fold in 1/2, 1/sqrt(2)
+// and log2(e) / 2 (exp(-x^2 / 2) = 2^(-x^2 log2(e) / 2)). Within 3.5e-7 of
+// the exact GELU in float32, far below the operand rounding of the
+// tensor-core contraction the hidden rows feed (2^-18 relative at best).
 __device__ __forceinline__ float gelu_as(float x) {
-    const float z = fabsf(x) * 0.70710678118654752f;
-    const float t = __fdividef(1.0f, fmaf(0.3275911f, z, 1.0f));
+    const float ax = fabsf(x);
+    const float t = rcp_approx(fmaf(0.23164189f, ax, 1.0f));  // p / sqrt(2)
     float q = fmaf(t, 0.5307027145f, -0.7265760135f);
     q = fmaf(t, q, 0.7107068705f);
     q = fmaf(t, q, -0.142248368f);
     q = fmaf(t, q, 0.127414796f);
-    q = q * t * __expf(-z * z);
-    return x * (x < 0.0f ? q : 1.0f - q);
+    const float e = ex2_approx(x * (x * -0.72134752f));
+    return fmaf(-ax, q * t * e, fmaxf(x, 0.0f));
 }
 
 // Operand modes of the edge contraction.
@@ -159,18 +178,22 @@ edge_tc_kernel(const __grid_constant__ CUtensorMap map_w, const EdgeTcArgs a) {
     // sum = bsum + wsum . g, sum of squares = bsq + g . (2 u + G g)
     float* sGram = sHn + H * 2 + 4;  // G[36], u[6], wsum[6], bsum, bsq (16-byte aligned)
     float* sCb = sGram + 52;                                              // cout
-    float* sLn = sCb + cout;                                              // cout x {gain, shift}
-    float* sStat = sLn + cout * 2;                                        // [2][2][128]
+    float* sLn = sCb + cout;      // cout x {|gain|, shift}
+    float* sSgn = sLn + cout * 2;  // cout: sign of the gain (+1 / -1)
+    float* sStat = sSgn + cout;    // [2][2][128]
     uint64_t* bars = reinterpret_cast<uint64_t*>(
         (reinterpret_cast<uintptr_t>(sStat + 4 * kRows) + 7) & ~uintptr_t(7));
-    uint64_t* a_full = bars;        // [2]
     uint64_t* a_empty = bars + 2;   // [2]
     uint64_t* t_full = bars + 4;    // [2]
     uint64_t* t_empty = bars + 6;   // [2]
     uint64_t* w_bar = bars + 8;
     uint64_t* mma_done = bars + 9;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
+    // failure flags of the epilogue and (per tile parity) producer warps:
+    // written by the role's one polling lane before the role's named barrier,
+    // read by every warp of the role after it
     int* sEpiFail = reinterpret_cast<int*>(tmem_slot + 1);
+    int* sProdFail = sEpiFail + 1;  // [2]
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int R = a.B * a.M;
@@ -205,12 +228,12 @@ edge_tc_kernel(const __grid_constant__ CUtensorMap map_w, const EdgeTcArgs a) {
     }
     for (int c = tid; c < cout; c += kThreads) {
         sCb[c] = a.contrib_b[c];
-        sLn[2 * c] = a.ln_w[c];
+        sLn[2 * c] = fabsf(a.ln_w[c]);
         sLn[2 * c + 1] = a.ln_b[c];
+        sSgn[c] = a.ln_w[c] < 0.0f ? -1.0f : 1.0f;
     }
     if (tid == 0) {
         for (int b = 0; b < 2; ++b) {
-            tc::mbar_init(&a_full[b], kProducerThreads);
             tc::mbar_init(&a_empty[b], 1);
             tc::mbar_init(&t_full[b], 1);
             tc::mbar_init(&t_empty[b], kEpilogueThreads);
@@ -218,6 +241,7 @@ edge_tc_kernel(const __grid_constant__ CUtensorMap map_w, const EdgeTcArgs a) {
         tc::mbar_init(w_bar, 1);
         tc::mbar_init(mma_done, 1);
         *sEpiFail = 0;
+        sProdFail[0] = sProdFail[1] = 0;
         tc::fence_barrier_init();
     }
     if constexpr (!kTf32) {
@@ -242,34 +266,53 @@ edge_tc_kernel(const __grid_constant__ CUtensorMap map_w, const EdgeTcArgs a) {
         }
         fence_proxy_async();
     }
-    if (warp == kMmaWarp) tc::tmem_alloc(tmem_slot, tmem_cols);
+    if (warp == 0) tc::tmem_alloc(tmem_slot, tmem_cols);
+    if constexpr (kTf32) {
+        if (tid == 0) {
+            tc::mbar_arrive_expect_tx(w_bar, (uint32_t)(kblocks * cout * 128));
+            for (int kb = 0; kb < kblocks; ++kb)
+                tc::tma_load_2d(sB + (size_t)kb * cout * 128, &map_w, w_bar, kb * kBk, 0);
+        }
+    }
     tc::tc_fence_before();
     __syncthreads();
     tc::tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
     if (warp < kProducerWarps) {
-        // ---------------- hidden producers ----------------
+        // ---------------- hidden producers + MMA issue ----------------
         const int row = (warp << 4) + (lane >> 1);
         const int half = lane & 1;
         const int ch0 = half * hh;
         const float* hp = sHp + ch0 * 8 + half * 4;  // this lane's half of the records
         const float* hn = sHn + ch0 * 2 + half * 2;
+        const int pl = row >> a.log2K;
+        const int kk = row & (K - 1);
+        // geometry of the first tile; later tiles' loads are issued one tile ahead
+        bool valid = false;
+        float4 xi = make_float4(0.f, 0.f, 0.f, 0.f), xj = xi;
+        {
+            const int p = blockIdx.x * a.ppt + pl;
+            if (blockIdx.x < n_tiles && p < R) {
+                valid = true;
+                xi = *reinterpret_cast<const float4*>(a.xyz4 + (size_t)p * 4);
+                const int jrow = (p / a.M) * a.M + a.idx[(size_t)p * K + kk];
+                xj = *reinterpret_cast<const float4*>(a.xyz4 + (size_t)jrow * 4);
+            }
+        }
+        bool weights_ready = !kTf32;
         int it = 0;
         for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
-            const int p0 = tile * a.ppt;
-            const int pl = row >> a.log2K;
-            const int p = p0 + pl;
-            const bool valid = p < R;
-            float g[6] = {0, 0, 0, 0, 0, 0};
+            const float g[6] = {xj.x - xi.x, xj.y - xi.y, xj.z - xi.z, xi.x, xi.y, xi.z};
+            const bool cur_valid = valid;
+            // next tile: neighbour index and centre point now, the neighbour
+            // point after the wait below
+            const int np = (tile + gridDim.x) * a.ppt + pl;
+            valid = tile + (int)gridDim.x < n_tiles && np < R;
+            int nidx = 0;
             if (valid) {
-                const int kk = row - (pl << a.log2K);
-                const int b = p / a.M;
-                const int jrow = b * a.M + a.idx[(size_t)p * K + kk];
-                const float4 xi = *reinterpret_cast<const float4*>(a.xyz4 + (size_t)p * 4);
-                const float4 xj = *reinterpret_cast<const float4*>(a.xyz4 + (size_t)jrow * 4);
-                g[0] = xj.x - xi.x; g[1] = xj.y - xi.y; g[2] = xj.z - xi.z;
-                g[3] = xi.x; g[4] = xi.y; g[5] = xi.z;
+                nidx = a.idx[(size_t)np * K + kk];
+                xi = *reinterpret_cast<const float4*>(a.xyz4 + (size_t)np * 4);
             }
             // LayerNorm moments of the pre-activations W_in g + b_in from the
             // Gram matrix of W_in: no pass over the H channels
@@ -288,9 +331,13 @@ edge_tc_kernel(const __grid_constant__ CUtensorMap map_w, const EdgeTcArgs a) {
             // wait until the MMAs of the tile that last used this buffer are done
             const int abuf = a.a_bufs == 2 ? (it & 1) : 0;
             const uint32_t round = a.a_bufs == 2 ? (uint32_t)(it >> 1) : (uint32_t)it;
-            int ready = 0;
-            if (lane == 0) ready = tc::mbar_wait(&a_empty[abuf], (round & 1u) ^ 1u, a.err) ? 1 : 0;
-            if (!__shfl_sync(kFull, ready, 0)) break;
+            // one lane polls, the other producer warps wait on the named barrier
+            volatile int* fail = sProdFail + (it & 1);
+            if (tid == 0 && !tc::mbar_wait(&a_empty[abuf], (round & 1u) ^ 1u, a.err)) *fail = 1;
+            prod_barrier();
+            if (*fail) break;
+            if (valid) xj = *reinterpret_cast<const float4*>(
+                           a.xyz4 + (size_t)((np / a.M) * a.M + nidx) * 4);
             unsigned char* dA = sA + (size_t)abuf * a_buf_bytes;
             // pre-activation, GELU(LN), packed as the MMA reads it
             for (int i0 = 0; i0 < hh; i0 += kPer) {
@@ -299,7 +346,7 @@ edge_tc_kernel(const __grid_constant__ CUtensorMap map_w, const EdgeTcArgs a) {
                 for (int e = 0; e < kPer; ++e) {
                     const float v = hpe_pre(hp + (i0 + e) * 8, g);
                     const float2 gs = *reinterpret_cast<const float2*>(hn + 2 * (i0 + e));
-                    o[e] = valid ? gelu_as((v - mean) * rstd * gs.x + gs.y) : 0.0f;
+                    o[e] = cur_valid ? gelu_as((v - mean) * rstd * gs.x + gs.y) : 0.0f;
                 }
                 const int c = ch0 + i0;
                 unsigned char* dst =
@@ -322,9 +369,54 @@ edge_tc_kernel(const __grid_constant__ CUtensorMap map_w, const EdgeTcArgs a) {
                 }
             }
             fence_proxy_async();
-            tc::mbar_arrive(&a_full[abuf]);
+            prod_barrier();  // the whole A tile is written
+            if (tid == 0) {
+                // issue the tile's MMAs once its accumulator buffer is free; a
+                // failure stops the producers at the next tile's decision
+                const int tbuf = it & 1;
+                const uint32_t tph = (uint32_t)(it >> 1) & 1u;
+                bool ok = true;
+                if (!weights_ready) {
+                    ok = tc::mbar_wait(w_bar, 0, a.err);
+                    if (!ok) tc::mbar_drain(w_bar, 0);
+                    weights_ready = true;
+                }
+                ok = ok && tc::mbar_wait(&t_empty[tbuf], tph ^ 1u, a.err);
+                if (ok) {
+                    tc::tc_fence_after();
+                    const uint32_t d = tmem_base + (uint32_t)(tbuf * cout);
+                    const uint32_t a0 = tc::smem_u32(dA);
+                    const uint32_t b0 = tc::smem_u32(sB), b_lo = tc::smem_u32(sBlo);
+                    for (int kb = 0; kb < kblocks; ++kb)
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) {
+                            if ((kb * kBk + k * (32 / kElem)) >= H) break;
+                            const uint32_t ao = kb * kRows * 128 + k * 32;
+                            const uint32_t bo = kb * cout * 128 + k * 32;
+                            const uint64_t da = tc::sw128_desc(a0 + ao);
+                            const uint64_t db = tc::sw128_desc(b0 + bo);
+                            tc::umma<kTf32>(d, da, db, a.idesc, (kb | k) ? 1u : 0u);
+                            if (kSplit) {
+                                tc::umma<false>(d, da, tc::sw128_desc(b_lo + bo), a.idesc, 1u);
+                                tc::umma<false>(d, tc::sw128_desc(a0 + (uint32_t)a_bytes + ao),
+                                                db, a.idesc, 1u);
+                            }
+                        }
+                    tc::umma_commit(&a_empty[abuf]);
+                    tc::umma_commit(&t_full[tbuf]);
+                } else {
+                    reinterpret_cast<volatile int*>(sProdFail)[(it + 1) & 1] = 1;
+                }
+            }
         }
-    } else if (warp < kMmaWarp) {
+        if (tid == 0) {
+            // the weight copies and every MMA issued complete before the CTA
+            // releases its shared and tensor memory
+            if (!weights_ready) tc::mbar_drain(w_bar, 0);
+            tc::umma_commit(mma_done);
+            tc::mbar_drain(mma_done, 0);
+        }
+    } else {
         // ---------------- epilogue ----------------
         const int quarter = warp & 3;
         const int cpart = (warp - kEpiWarp0) >> 2;
@@ -334,11 +426,12 @@ edge_tc_kernel(const __grid_constant__ CUtensorMap map_w, const EdgeTcArgs a) {
         for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
             const int tbuf = it & 1;
             const uint32_t tph = (uint32_t)(it >> 1) & 1u;
-            int ready = 0;
-            if (lane == 0) ready = tc::mbar_wait(&t_full[tbuf], tph, a.err) ? 1 : 0;
-            ready = __shfl_sync(kFull, ready, 0);
-            if (!ready && lane == 0) *reinterpret_cast<volatile int*>(sEpiFail) = 1;
-            epi_barrier();  // every epilogue warp takes the same decision
+            // one lane polls, the other epilogue warps wait on the named
+            // barrier; the flag is next written after two more barriers of
+            // this tile, so every warp reads this tile's decision
+            if (warp == kEpiWarp0 && lane == 0 && !tc::mbar_wait(&t_full[tbuf], tph, a.err))
+                *reinterpret_cast<volatile int*>(sEpiFail) = 1;
+            epi_barrier();
             if (*reinterpret_cast<volatile int*>(sEpiFail)) break;
             tc::tc_fence_after();
             const int p0 = tile * a.ppt;
@@ -390,16 +483,25 @@ edge_tc_kernel(const __grid_constant__ CUtensorMap map_w, const EdgeTcArgs a) {
             epi_barrier();
             const float rstd =
                 rsqrtf((sStat[2 * kRows + erow] + sStat[3 * kRows + erow]) / (float)cout + 1e-6f);
-            // pass 3: affine + LeakyReLU, then max over the K lanes of each point
+            const float nmr = -mean * rstd;
+            // pass 3: max over the K lanes of each point of the normalised value,
+            // then the affine + LeakyReLU once per point and channel. Both are
+            // monotone (and rounding is monotone), so they commute exactly with
+            // the max; a negative gain reverses the order, which the sign
+            // folded into the normalised value undoes (|g| s n + b with s n
+            // maximised).
             for (int ch = cpart; ch < nchunks; ch += 2) {
                 const int cb = ch * 32;
                 float y[32];
                 tc::tmem_ld32(taddr + (uint32_t)cb, y);
                 if (ej >= 0) {
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        const float2 gs = *reinterpret_cast<const float2*>(sLn + 2 * (cb + i));
-                        y[i] = f2s_leaky((y[i] - mean) * rstd * gs.x + gs.y);
+                    for (int i = 0; i < 32; i += 4) {
+                        const float4 sg = *reinterpret_cast<const float4*>(sSgn + cb + i);
+                        y[i + 0] = fmaf(y[i + 0], rstd, nmr) * sg.x;
+                        y[i + 1] = fmaf(y[i + 1], rstd, nmr) * sg.y;
+                        y[i + 2] = fmaf(y[i + 2], rstd, nmr) * sg.z;
+                        y[i + 3] = fmaf(y[i + 3], rstd, nmr) * sg.w;
                     }
                 } else {
 #pragma unroll
@@ -425,63 +527,22 @@ edge_tc_kernel(const __grid_constant__ CUtensorMap map_w, const EdgeTcArgs a) {
                     const int nv = 32 >> a.log2K;
                     float* o = a.out + (size_t)ep * a.ldo + cb + off;
 #pragma unroll
-                    for (int i = 0; i < 32; ++i)
-                        if (i < nv) o[i] = y[i];
+                    for (int i = 0; i < 32; ++i) {
+                        if (i < nv) {
+                            const float2 gs = *reinterpret_cast<const float2*>(sLn + 2 * (cb + off + i));
+                            const float t = fmaf(y[i], gs.x, gs.y);
+                            o[i] = fmaxf(t, 0.2f * t);  // LeakyReLU(0.2)
+                        }
+                    }
                 }
             }
             tc::tc_fence_before();
             tc::mbar_arrive(&t_empty[tbuf]);
         }
-    } else {
-        // ---------------- MMA issuer ----------------
-        if (lane == 0) {
-            bool ok = true;
-            if constexpr (kTf32) {
-                tc::mbar_arrive_expect_tx(w_bar, (uint32_t)(kblocks * cout * 128));
-                for (int kb = 0; kb < kblocks; ++kb)
-                    tc::tma_load_2d(sB + (size_t)kb * cout * 128, &map_w, w_bar, kb * kBk, 0);
-                ok = tc::mbar_wait(w_bar, 0, a.err);
-                if (!ok) tc::mbar_drain(w_bar, 0);  // the weight copies land before the CTA exits
-            }
-            int it = 0;
-            for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x, ++it) {
-                const int abuf = a.a_bufs == 2 ? (it & 1) : 0;
-                const uint32_t round = a.a_bufs == 2 ? (uint32_t)(it >> 1) : (uint32_t)it;
-                const int tbuf = it & 1;
-                const uint32_t tph = (uint32_t)(it >> 1) & 1u;
-                if (!tc::mbar_wait(&t_empty[tbuf], tph ^ 1u, a.err)) break;
-                if (!tc::mbar_wait(&a_full[abuf], round & 1u, a.err)) break;
-                tc::tc_fence_after();
-                const uint32_t d = tmem_base + (uint32_t)(tbuf * cout);
-                const uint32_t a0 = tc::smem_u32(sA + (size_t)abuf * a_buf_bytes);
-                const uint32_t b0 = tc::smem_u32(sB), b_lo = tc::smem_u32(sBlo);
-                for (int kb = 0; kb < kblocks; ++kb)
-#pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        if ((kb * kBk + k * (32 / kElem)) >= H) break;
-                        const uint32_t ao = kb * kRows * 128 + k * 32;
-                        const uint32_t bo = kb * cout * 128 + k * 32;
-                        const uint64_t da = tc::sw128_desc(a0 + ao);
-                        const uint64_t db = tc::sw128_desc(b0 + bo);
-                        tc::umma<kTf32>(d, da, db, a.idesc, (kb | k) ? 1u : 0u);
-                        if (kSplit) {
-                            tc::umma<false>(d, da, tc::sw128_desc(b_lo + bo), a.idesc, 1u);
-                            tc::umma<false>(d, tc::sw128_desc(a0 + (uint32_t)a_bytes + ao), db,
-                                            a.idesc, 1u);
-                        }
-                    }
-                tc::umma_commit(&a_empty[abuf]);
-                tc::umma_commit(&t_full[tbuf]);
-            }
-            // every MMA this thread issued has completed before TMEM is freed
-            tc::umma_commit(mma_done);
-            tc::mbar_drain(mma_done, 0);
-        }
-        __syncwarp();
     }
     tc::tc_fence_before();
     __syncthreads();
-    if (warp == kMmaWarp) {
+    if (warp == 0) {
         tc::tc_fence_after();
         tc::tmem_dealloc(tmem_base, tmem_cols);
     }
@@ -493,7 +554,7 @@ size_t edge_tc_smem(int mode, int H, int cout, int bufs) {
     const size_t kblocks = (size_t)ceil_div(H, 128 / elem);
     const size_t copies = mode == kModeSplit ? 2 : 1;
     return 1024 + copies * kblocks * 128 * ((size_t)bufs * kRows + cout) +
-           sizeof(float) * ((size_t)H * 10 + 60 + (size_t)cout * 3 + 4 * kRows) + 128;
+           sizeof(float) * ((size_t)H * 10 + 60 + (size_t)cout * 4 + 4 * kRows) + 128;
 }
 
 }  // namespace

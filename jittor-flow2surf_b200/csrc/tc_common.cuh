@@ -16,8 +16,8 @@ namespace tc {
 
 // Polls of a bounded wait. Each poll is a try_wait that may park the thread
 // for up to kSuspendHintNs (it wakes as soon as the phase completes), and
-// polls past the first 256 also sleep, so a wait ends after between roughly
-// 0.3 s (hint ignored) and 4.5 s (hint honoured) when nothing arrives.
+// polls past the first 64 also sleep, so a wait ends after between roughly
+// 0.15 s (hint ignored) and 4.3 s (hint honoured) when nothing arrives.
 constexpr uint32_t kSpinLimit = 1u << 22;
 constexpr uint32_t kSuspendHintNs = 1000;
 
@@ -65,7 +65,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
     for (uint32_t i = 0; i < kSpinLimit; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
         if ((i & 63u) == 63u && *reinterpret_cast<volatile int*>(err) != kTcOk) return false;
-        if (i > 256) __nanosleep(64);
+        if (i >= 64) __nanosleep(32);
     }
     atomicExch(err, kTcWaitTimeout);
     return false;
@@ -77,7 +77,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
 __device__ __forceinline__ bool mbar_drain(uint64_t* bar, uint32_t parity) {
     for (uint32_t i = 0; i < kSpinLimit; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
-        if (i > 256) __nanosleep(64);
+        if (i >= 64) __nanosleep(32);
     }
     return false;
 }

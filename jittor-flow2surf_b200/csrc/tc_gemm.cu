@@ -76,6 +76,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     uint64_t* tempty = tfull + 2;     // [2]
     uint64_t* mma_done = tempty + 2;  // [1]
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+    // per tile parity: set by the one polling epilogue lane when its wait
+    // failed, read by every epilogue warp after their named barrier
+    int* epi_fail = reinterpret_cast<int*>(tmem_slot + 1);  // [2]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_tiles_n = (g.cols + g.bn - 1) / g.bn;
@@ -93,6 +96,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             tc::mbar_init(&tempty[b], kEpilogueThreads);
         }
         tc::mbar_init(mma_done, 1);
+        epi_fail[0] = epi_fail[1] = 0;
         tc::fence_barrier_init();
         tc::prefetch_tensormap(&map_a);
         tc::prefetch_tensormap(&map_b);
@@ -202,10 +206,11 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++iter) {
             const int buf = iter & 1;
             const uint32_t tph = (uint32_t)(iter >> 1) & 1u;
-            // one lane waits, the warp follows it (tcgen05.ld is warp-collective)
-            int ready = 0;
-            if (lane == 0) ready = tc::mbar_wait(&tfull[buf], tph, g.err) ? 1 : 0;
-            if (!__shfl_sync(0xffffffffu, ready, 0)) break;
+            // one lane polls, the other epilogue warps wait on the named barrier
+            volatile int* fail = epi_fail + (iter & 1);
+            if (ew == 0 && lane == 0 && !tc::mbar_wait(&tfull[buf], tph, g.err)) *fail = 1;
+            asm volatile("bar.sync 1, %0;" ::"n"(kEpilogueThreads) : "memory");
+            if (*fail) break;
             tc::tc_fence_after();
             const int m0 = (tile / n_tiles_n) * kTileM;
             const int n0 = (tile % n_tiles_n) * g.bn;
