@@ -260,6 +260,29 @@ int f2s_fuse_euler(const float* points, const float* votes, const int32_t* offse
                    const int32_t* entries, const double* weights, const double* weight_sum,
                    int64_t N, float alpha_step, float* out, float* velocity, void* stream);
 
+/*
+ * Patch-sharded fusion, for one cloud whose patches are split across GPUs
+ * (no counterpart in the reference, which runs one process; it splits the
+ * bincount sum of aggregate_votes, inference.py:158-171, by patch):
+ * vote_sum (N, 3) float64 = sum, in entry order, of w_f * vote_f over the
+ * entries f whose patch p = f / k lies in [patch_begin, patch_end). Only those
+ * patches' votes are read. Summing the ranks' vote_sum (an all-reduce) and
+ * calling f2s_euler_from_sum gives f2s_fuse_euler's result; with a single
+ * range [0, P) it is bit-identical.
+ */
+int f2s_fuse_partial(const float* votes, const int32_t* offsets, const int32_t* entries,
+                     const double* weights, int64_t N, int k, int patch_begin, int patch_end,
+                     double* vote_sum, void* stream);
+
+/*
+ * Second half of f2s_fuse_euler from summed votes: v = (float)(vote_sum /
+ * (weight_sum + 1e-8)), out = points - alpha_step * v; uncovered points are
+ * copied. `velocity` (N, 3) may be NULL.
+ */
+int f2s_euler_from_sum(const float* points, const double* vote_sum, const double* weight_sum,
+                       const int32_t* offsets, int64_t N, float alpha_step, float* out,
+                       float* velocity, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Nearest distances and Chamfer                                            */
 /* ------------------------------------------------------------------------ */

@@ -119,6 +119,26 @@ __device__ __forceinline__ float f2s_gelu_erf(float x) {
 
 __device__ __forceinline__ float f2s_silu(float x) { return x / (1.0f + expf(-x)); }
 
+// Approximate reciprocal / base-2 exponential (the hardware's approximate
+// instructions, denormals flushed): for tensor-core paths whose operands are
+// rounded far more coarsely than these results.
+__device__ __forceinline__ float f2s_rcp_approx(float x) {
+    float r;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
+
+__device__ __forceinline__ float f2s_ex2_approx(float x) {
+    float r;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
+
+// silu(x) = x / (1 + 2^(-x log2 e)) on the approximate instructions.
+__device__ __forceinline__ float f2s_silu_approx(float x) {
+    return x * f2s_rcp_approx(1.0f + f2s_ex2_approx(-1.44269504088896341f * x));
+}
+
 __device__ __forceinline__ float f2s_leaky(float x) { return x > 0.0f ? x : 0.2f * x; }
 
 // Round to the nearest tf32 value (10-bit mantissa, ties away from zero).

@@ -409,6 +409,55 @@ __global__ void fuse_euler_kernel(const float* __restrict__ pts, const float* __
     }
 }
 
+// Patch-sharded form of the same fusion, for one cloud whose patches are
+// split across GPUs: the weighted vote sums of the entries whose patch lies in
+// [patch_begin, patch_end), in entry order, float64 (N, 3). Summed over the
+// ranks (an all-reduce) they give the sums fuse_euler_kernel forms; with one
+// rank the result is the same sum bit for bit.
+__global__ void fuse_partial_kernel(const float* __restrict__ votes,
+                                    const int32_t* __restrict__ offsets,
+                                    const int32_t* __restrict__ entries,
+                                    const double* __restrict__ wts, int N, int k,
+                                    int patch_begin, int patch_end, double* __restrict__ vsum) {
+    const int n = blockIdx.x * blockDim.x + threadIdx.x;
+    if (n >= N) return;
+    const int a = offsets[n], b = offsets[n + 1];
+    const int f_begin = patch_begin * k, f_end = patch_end * k;
+    double s0 = 0.0, s1 = 0.0, s2 = 0.0;
+    for (int i = a; i < b; ++i) {
+        const int f = entries[i];
+        if (f < f_begin || f >= f_end) continue;
+        const double w = wts[f];
+        s0 = __dadd_rn(s0, __dmul_rn(w, (double)votes[3 * (size_t)f]));
+        s1 = __dadd_rn(s1, __dmul_rn(w, (double)votes[3 * (size_t)f + 1]));
+        s2 = __dadd_rn(s2, __dmul_rn(w, (double)votes[3 * (size_t)f + 2]));
+    }
+    vsum[3 * (size_t)n] = s0;
+    vsum[3 * (size_t)n + 1] = s1;
+    vsum[3 * (size_t)n + 2] = s2;
+}
+
+// Normalisation and Euler update from summed votes (the second half of
+// fuse_euler_kernel).
+__global__ void euler_from_sum_kernel(const float* __restrict__ pts,
+                                      const double* __restrict__ vsum,
+                                      const double* __restrict__ wsum,
+                                      const int32_t* __restrict__ offsets, int N,
+                                      float alpha_step, float* __restrict__ out,
+                                      float* __restrict__ velocity) {
+    const int n = blockIdx.x * blockDim.x + threadIdx.x;
+    if (n >= N) return;
+    const double den = __dadd_rn(wsum[n], 1e-8);
+    const bool covered = offsets[n + 1] > offsets[n] && wsum[n] != 0.0;
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+        const float v = (float)__ddiv_rn(vsum[3 * (size_t)n + c], den);
+        const float x = pts[3 * n + c];
+        out[3 * n + c] = covered ? __fsub_rn(x, __fmul_rn(alpha_step, v)) : x;
+        if (velocity) velocity[3 * n + c] = v;
+    }
+}
+
 int grid_for(int64_t work, int threads) {
     const int64_t blocks = (work + threads - 1) / threads;
     const int64_t cap = (int64_t)sm_count() * 32;
@@ -556,4 +605,34 @@ extern "C" int f2s_fuse_euler(const float* points, const float* votes, const int
     fuse_euler_kernel<<<ceil_div((int)N, 256), 256, 0, as_stream(stream)>>>(
         points, votes, offsets, entries, weights, weight_sum, (int)N, alpha_step, out, velocity);
     return check_launch("fuse_euler_kernel");
+}
+
+extern "C" int f2s_fuse_partial(const float* votes, const int32_t* offsets,
+                                const int32_t* entries, const double* weights, int64_t N, int k,
+                                int patch_begin, int patch_end, double* vote_sum, void* stream) {
+    F2S_REQUIRE(N >= 0 && k >= 1 && 0 <= patch_begin && patch_begin <= patch_end,
+                "fuse_partial: bad size N=%lld k=%d patches [%d, %d)", (long long)N, k,
+                patch_begin, patch_end);
+    if (N == 0) return F2S_OK;
+    F2S_LIMIT(N < (1ll << 31) - 1 && (int64_t)patch_end * k < (1ll << 31) - 1, "too many points");
+    F2S_REQUIRE(offsets && entries && weights && vote_sum && (votes || patch_begin == patch_end),
+                "fuse_partial: null pointer");
+    f2s::TraceScope trace(f2s::kTagFuseEuler, f2s::as_stream(stream));
+    f2s::fuse_partial_kernel<<<f2s::ceil_div((int)N, 256), 256, 0, f2s::as_stream(stream)>>>(
+        votes, offsets, entries, weights, (int)N, k, patch_begin, patch_end, vote_sum);
+    return f2s::check_launch("fuse_partial_kernel");
+}
+
+extern "C" int f2s_euler_from_sum(const float* points, const double* vote_sum,
+                                  const double* weight_sum, const int32_t* offsets, int64_t N,
+                                  float alpha_step, float* out, float* velocity, void* stream) {
+    F2S_REQUIRE(N >= 0, "euler_from_sum: bad size");
+    if (N == 0) return F2S_OK;
+    F2S_LIMIT(N < (1ll << 31) - 1, "too many points");
+    F2S_REQUIRE(points && vote_sum && weight_sum && offsets && out,
+                "euler_from_sum: null pointer");
+    f2s::TraceScope trace(f2s::kTagFuseEuler, f2s::as_stream(stream));
+    f2s::euler_from_sum_kernel<<<f2s::ceil_div((int)N, 256), 256, 0, f2s::as_stream(stream)>>>(
+        points, vote_sum, weight_sum, offsets, (int)N, alpha_step, out, velocity);
+    return f2s::check_launch("euler_from_sum_kernel");
 }

@@ -110,18 +110,6 @@ __device__ __forceinline__ float hpe_pre(const float* prm, const float (&g)[6]) 
     return v;
 }
 
-__device__ __forceinline__ float rcp_approx(float x) {
-    float r;
-    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
-    return r;
-}
-
-__device__ __forceinline__ float ex2_approx(float x) {
-    float r;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
-    return r;
-}
-
 // GELU(x) = x * Phi(x) with Phi from the erf approximation of Abramowitz and
 // Stegun, Handbook of Mathematical Functions, eq. 7.1.26 (after Hastings):
 //   erf(z) = 1 - t (a1 + t (a2 + t (a3 + t (a4 + t a5)))) exp(-z^2),
@@ -134,12 +122,12 @@ __device__ __forceinline__ float ex2_approx(float x) {
 // tensor-core contraction the hidden rows feed (2^-18 relative at best).
 __device__ __forceinline__ float gelu_as(float x) {
     const float ax = fabsf(x);
-    const float t = rcp_approx(fmaf(0.23164189f, ax, 1.0f));  // p / sqrt(2)
+    const float t = f2s_rcp_approx(fmaf(0.23164189f, ax, 1.0f));  // p / sqrt(2)
     float q = fmaf(t, 0.5307027145f, -0.7265760135f);
     q = fmaf(t, q, 0.7107068705f);
     q = fmaf(t, q, -0.142248368f);
     q = fmaf(t, q, 0.127414796f);
-    const float e = ex2_approx(x * (x * -0.72134752f));
+    const float e = f2s_ex2_approx(x * (x * -0.72134752f));
     return fmaf(-ax, q * t * e, fmaxf(x, 0.0f));
 }
 

@@ -234,29 +234,49 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                 if (col < g.cols) {
                     const float b = g.bias ? g.bias[col] : 0.0f;
                     const float b2 = (kDual && g.bias2) ? g.bias2[col] : 0.0f;
-                    int patch = -1;
-                    float gt = 0.0f;
                     const int r_end = min(32, g.rows - row0);
-                    for (int r = 0; r < r_end; ++r) {
-                        const int row = row0 + r;
-                        float out = stage_buf[r * 33 + lane] + b;
-                        if constexpr (kDual) {
-                            const float u = stage_buf2[r * 33 + lane] + b2;
-                            out = f2s_silu(out) * u;
-                        }
-                        const size_t o = (size_t)row * g.ldy + col;
+                    // gated residual: patch of the current row and the row
+                    // where the next patch starts
+                    int patch = row0 / g.rows_per_patch;
+                    int next_patch_row = (patch + 1) * g.rows_per_patch;
+                    float gt = 0.0f;
+                    if constexpr (kEpi == kEpiGatedResidual)
+                        gt = g.gate[(size_t)patch * g.gate_stride + col];
+                    // eight rows at a time: all loads of a group are issued
+                    // before its stores (rows are distinct, but the compiler
+                    // cannot tell that the residual loads do not alias them)
+                    for (int r0 = 0; r0 < r_end; r0 += 8) {
+                        float yv[8];
                         if constexpr (kEpi == kEpiGatedResidual) {
-                            const int p = row / g.rows_per_patch;
-                            if (p != patch) {
-                                patch = p;
-                                gt = g.gate[(size_t)p * g.gate_stride + col];
+#pragma unroll
+                            for (int j = 0; j < 8; ++j)
+                                yv[j] = r0 + j < r_end
+                                            ? static_cast<const float*>(g.Y)[(size_t)(row0 + r0 + j) * g.ldy + col]
+                                            : 0.0f;
+                        }
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            const int r = r0 + j;
+                            if (r >= r_end) break;
+                            const int row = row0 + r;
+                            float out = stage_buf[r * 33 + lane] + b;
+                            if constexpr (kDual) {
+                                const float u = stage_buf2[r * 33 + lane] + b2;
+                                out = f2s_silu_approx(out) * u;
                             }
-                            float* y = static_cast<float*>(g.Y) + o;
-                            *y = *y + gt * out;
-                        } else if (g.y_bf16) {
-                            static_cast<__nv_bfloat16*>(g.Y)[o] = __float2bfloat16_rn(out);
-                        } else {
-                            static_cast<float*>(g.Y)[o] = g.round_tf32 ? f2s_round_tf32(out) : out;
+                            const size_t o = (size_t)row * g.ldy + col;
+                            if constexpr (kEpi == kEpiGatedResidual) {
+                                if (row >= next_patch_row) {
+                                    patch = row / g.rows_per_patch;
+                                    next_patch_row = (patch + 1) * g.rows_per_patch;
+                                    gt = g.gate[(size_t)patch * g.gate_stride + col];
+                                }
+                                static_cast<float*>(g.Y)[o] = fmaf(gt, out, yv[j]);
+                            } else if (g.y_bf16) {
+                                static_cast<__nv_bfloat16*>(g.Y)[o] = __float2bfloat16_rn(out);
+                            } else {
+                                static_cast<float*>(g.Y)[o] = g.round_tf32 ? f2s_round_tf32(out) : out;
+                            }
                         }
                     }
                 }

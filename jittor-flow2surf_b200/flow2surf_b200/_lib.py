@@ -49,6 +49,8 @@ SIGNATURES: dict[str, list] = {
     "f2s_fusion_build": [_p, _p, _i, _i, _i64, _p, _p, _p, _p, _sz, _p],
     "f2s_gather_patches": [_p, _p, _p, _i, _i, _p, _p],
     "f2s_fuse_euler": [_p, _p, _p, _p, _p, _p, _i64, _f, _p, _p, _p],
+    "f2s_fuse_partial": [_p, _p, _p, _p, _i64, _i, _i, _i, _p, _p],
+    "f2s_euler_from_sum": [_p, _p, _p, _p, _i64, _f, _p, _p, _p],
     "f2s_nearest_workspace_bytes": [_i, _i, _i, _p],
     "f2s_nearest": [_p, _p, _i, _i, _i, _p, _p, _p, _p, _p, _sz, _p],
     "f2s_chamfer": [_p, _p, _i, _i, _i, _p, _p, _sz, _p],

@@ -130,15 +130,19 @@ class _Runner:
             self.workspace = torch.empty(model.workspace_bytes(self.chunk, k), dtype=torch.uint8,
                                          device=dev)
 
-    def predict(self, points: torch.Tensor, alpha_value: float) -> torch.Tensor:
-        """Per-patch votes (P, k, 3) (inference.py:141-153)."""
+    def predict(self, points: torch.Tensor, alpha_value: float, begin: int = 0,
+                end: int | None = None) -> torch.Tensor:
+        """Per-patch votes (P, k, 3) of patches [begin, end) (inference.py:141-153)."""
         plan = self.plan
-        P, k = plan.num_patches, plan.patch_size
-        _lib.call("f2s_gather_patches", _lib.ptr(points), _lib.ptr(plan.neighbors),
-                  _lib.ptr(plan.seeds), P, k, _lib.ptr(self.x), _lib.stream_handle())
+        k = plan.patch_size
+        end = plan.num_patches if end is None else end
+        if end > begin:
+            _lib.call("f2s_gather_patches", _lib.ptr(points), _lib.ptr(plan.neighbors[begin]),
+                      _lib.ptr(plan.seeds[begin:]), end - begin, k, _lib.ptr(self.x[begin]),
+                      _lib.stream_handle())
         self.alpha.fill_(alpha_value)
-        for start in range(0, P, self.chunk):
-            stop = min(P, start + self.chunk)
+        for start in range(begin, end, self.chunk):
+            stop = min(end, start + self.chunk)
             if self.workspace is not None:
                 self.model.forward_into(self.x[start:stop], self.alpha[start:stop],
                                         self.votes[start:stop], self.workspace)
@@ -156,11 +160,58 @@ class _Runner:
                   _lib.stream_handle())
 
 
+def shard_range(num_patches: int, rank: int, world_size: int) -> tuple[int, int]:
+    """Contiguous patch range [begin, end) of `rank` when one cloud's patches
+    are split across `world_size` GPUs: a fixed split, so the result depends
+    only on the world size."""
+    if world_size < 1 or not 0 <= rank < world_size:
+        raise ValueError(f"bad rank {rank} of world size {world_size}")
+    base, extra = divmod(num_patches, world_size)
+    begin = rank * base + min(rank, extra)
+    return begin, begin + base + (1 if rank < extra else 0)
+
+
+class _ShardedRunner(_Runner):
+    """One cloud across the ranks of a process group: every rank holds the
+    whole cloud and plan, runs the model on its own patch range, forms the
+    weighted vote sums of those patches, and one all-reduce (NCCL over NVLink)
+    per Euler step adds them; the update is then identical on every rank."""
+
+    def __init__(self, model, plan: DenoisePlan, workspace_budget: int, group):
+        import torch.distributed as dist
+        super().__init__(model, plan, workspace_budget)
+        self.dist, self.group = dist, group
+        self.begin, self.end = shard_range(plan.num_patches, dist.get_rank(group),
+                                           dist.get_world_size(group))
+        self.vote_sum = torch.empty((plan.num_points, 3), dtype=torch.float64,
+                                    device=plan.seeds.device)
+
+    def step(self, points: torch.Tensor, out: torch.Tensor, alpha_current: float,
+             alpha_step: float) -> None:
+        plan = self.plan
+        votes = self.predict(points, alpha_current, self.begin, self.end)
+        stream = _lib.stream_handle()
+        _lib.call("f2s_fuse_partial", _lib.ptr(votes), _lib.ptr(plan.offsets),
+                  _lib.ptr(plan.entries), _lib.ptr(plan.weights), plan.num_points,
+                  plan.patch_size, self.begin, self.end, _lib.ptr(self.vote_sum), stream)
+        self.dist.all_reduce(self.vote_sum, group=self.group)
+        _lib.call("f2s_euler_from_sum", _lib.ptr(points), _lib.ptr(self.vote_sum),
+                  _lib.ptr(plan.weight_sum), _lib.ptr(plan.offsets), plan.num_points,
+                  ctypes.c_float(alpha_step), _lib.ptr(out), None, stream)
+
+
 def denoise_device(model, points: torch.Tensor, patch_size, seed_k, num_steps, rng=None,
                    patch_seed_idx=None, patch_agg_beta=4.0, alpha_clean_power=1.0,
-                   alpha_noisy_power=1.0, workspace_budget=DEFAULT_WORKSPACE_BUDGET):
+                   alpha_noisy_power=1.0, workspace_budget=DEFAULT_WORKSPACE_BUDGET,
+                   process_group=None):
     """patch_denoise on a cloud already on the GPU ((N, 3) float32 CUDA
-    tensor); returns the denoised cloud as a new CUDA tensor."""
+    tensor); returns the denoised cloud as a new CUDA tensor.
+
+    With `process_group` (an initialised torch.distributed group, one GPU per
+    rank), every rank passes the same cloud and seeds and the patches are
+    split across the ranks (`shard_range`); every rank returns the same
+    result. The per-step sum then adds the ranks' partial float64 sums, which
+    can differ from the one-GPU order in the last bit of a float64 sum."""
     if rng is None:
         rng = np.random.default_rng(0)
     num_points = points.shape[0]
@@ -179,7 +230,10 @@ def denoise_device(model, points: torch.Tensor, patch_size, seed_k, num_steps, r
         seeds = torch.from_numpy(seed_idx.astype(np.int32)).to(points.device)
     plan = build_plan(points, patch_size, seeds, patch_agg_beta)
     alphas = alpha_schedule(num_steps, alpha_clean_power, alpha_noisy_power)
-    runner = _Runner(model, plan, workspace_budget)
+    if process_group is not None and torch.distributed.get_world_size(process_group) > 1:
+        runner = _ShardedRunner(model, plan, workspace_budget, process_group)
+    else:
+        runner = _Runner(model, plan, workspace_budget)
     current = points.clone()
     spare = torch.empty_like(current)
     for step in range(num_steps - 1, -1, -1):
