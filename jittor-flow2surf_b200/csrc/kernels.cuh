@@ -45,6 +45,8 @@ struct TcGemmOp {
     int lda;
     const void* W;           // cols x K, K contiguous
     const void* W2;          // SwiGLU value weights (cols x K)
+    const void* A_lo;        // 3xTF32: low parts of A (rows x K, lda) and W (cols x K);
+    const void* W_lo;        //   A and W then hold the tf32-rounded high parts
     const float* bias;
     const float* bias2;
     void* Y;
@@ -61,6 +63,9 @@ struct TcGemmOp {
     int tag;
 };
 int tc_gemm(const TcGemmOp& op, cudaStream_t stream);
+// hi = x rounded to the nearest tf32, lo = x - hi; hi and lo are (rows, K)
+// with leading dimension K: the operand split of the 3xTF32 GEMM.
+int split_tf32(const float* x, int ldx, int rows, int K, float* hi, float* lo, cudaStream_t stream);
 // N tile with the least padding for `cols` output columns.
 int tc_pick_bn(int cols, bool swiglu);
 

@@ -54,6 +54,8 @@ struct Dims {
     int K, C, NB, A, Hf, qk, S, ndec;
     int sd[kMaxStages], si[kMaxStages], dd[kMaxDecoder];
     int sum_stage, max_cout, max_dec;
+    int max_gemm_in;    // widest K of the encoder GEMMs (content, projection head)
+    int max_gemm_w;     // largest weight matrix of the encoder GEMMs
     int precision;      // trunk + decoder
     int enc_precision;  // neighbour stages + projection head
     int enc_gemm_precision;
@@ -98,9 +100,17 @@ int check_config(const f2s_model_config* cfg, Dims& d) {
                     d.enc_precision == F2S_PRECISION_BF16X3,
                 "encoder precision %d is not F2S_PRECISION_FP32, _TF32 or _BF16X3",
                 d.enc_precision);
-    // the encoder's plain GEMMs have no split-bf16 form: fp32 CUDA cores there
-    d.enc_gemm_precision =
-        d.enc_precision == F2S_PRECISION_TF32 ? F2S_PRECISION_TF32 : F2S_PRECISION_FP32;
+    // the encoder's plain GEMMs (content, projection head): tf32 with a tf32
+    // encoder, 3xTF32 (denoted F2S_PRECISION_BF16X3 here) with a split-bf16
+    // one, fp32 CUDA cores with an fp32 one
+    d.enc_gemm_precision = d.enc_precision;
+    d.max_gemm_in = d.sum_stage;
+    d.max_gemm_w = d.C * d.sum_stage;
+    for (int s = 0; s < d.S; ++s) {
+        d.max_gemm_in = d.si[s] > d.max_gemm_in ? d.si[s] : d.max_gemm_in;
+        const int wsize = 2 * d.sd[s] * d.si[s];
+        d.max_gemm_w = wsize > d.max_gemm_w ? wsize : d.max_gemm_w;
+    }
     d.ndec = cfg->num_decoder;
     F2S_REQUIRE(d.ndec >= 0 && d.ndec <= kMaxDecoder, "num_decoder %d outside [0, %d]", d.ndec,
                 kMaxDecoder);
@@ -172,6 +182,7 @@ Layout make_layout(const Dims& d) {
 struct Workspace {
     float *xyz4, *feat0, *content, *cat, *x, *h, *qkv, *colstats, *offs, *ffh, *dec0, *dec1;
     float *cond, *mod, *attn;
+    float *split_a, *split_w;  // 3xTF32 operand halves (split-bf16 encoder only)
     int32_t* idx;
     size_t bytes;
 };
@@ -201,6 +212,9 @@ Workspace carve(const Dims& d, int B, int M, char* base) {
     w.cond = (float*)take((size_t)B * d.A);
     w.mod = (float*)take((size_t)B * (d.NB > 0 ? d.NB : 1) * 6 * d.C);
     w.attn = (float*)take((size_t)attention_tc_workspace_floats(B, M, d.C));
+    const bool split = d.enc_gemm_precision == F2S_PRECISION_BF16X3;
+    w.split_a = split ? (float*)take(R * 2 * d.max_gemm_in) : nullptr;
+    w.split_w = split ? (float*)take((size_t)2 * d.max_gemm_w) : nullptr;
     w.bytes = off;
     return w;
 }
@@ -314,9 +328,47 @@ GemmArgs gemm_args(const float* A, int lda, const float* W, const float* bias, f
 }
 
 // One dense contraction of the forward at the configured precision: the fp32
-// CUDA-core kernel, or the tcgen05 kernel reading the fp32 operands as tf32.
-int linear_op(const GemmArgs& g, int precision, cudaStream_t st) {
+// CUDA-core kernel, the tcgen05 kernel reading the fp32 operands as tf32, or
+// (F2S_PRECISION_BF16X3 here) the 3xTF32 tcgen05 kernel on operands split
+// into split_a (2 x rows x K floats) and split_w (2 x cols x K).
+int linear_op(const GemmArgs& g, int precision, cudaStream_t st, float* split_a = nullptr,
+              float* split_w = nullptr) {
     if (precision == F2S_PRECISION_FP32) return gemm_f32(g, st);
+    if (precision == F2S_PRECISION_BF16X3) {
+        // the split operands are K-contiguous; TMA rows need 16-byte pitches
+        if (g.K % 4 != 0 || g.epilogue != kEpiStore || !split_a || !split_w)
+            return gemm_f32(g, st);
+        float* a_hi = split_a;
+        float* a_lo = split_a + (size_t)g.rows * g.K;
+        float* w_hi = split_w;
+        float* w_lo = split_w + (size_t)g.cols * g.K;
+        {
+            TraceScope trace(g.tag, st);
+            F2S_TRY(split_tf32(g.A, g.lda, g.rows, g.K, a_hi, a_lo, st));
+        }
+        {
+            TraceScope trace(g.tag, st);
+            F2S_TRY(split_tf32(g.W, g.K, g.cols, g.K, w_hi, w_lo, st));
+        }
+        TcGemmOp op{};
+        op.A = a_hi;
+        op.A_lo = a_lo;
+        op.lda = g.K;
+        op.W = w_hi;
+        op.W_lo = w_lo;
+        op.bias = g.bias;
+        op.Y = g.Y;
+        op.ldy = g.ldy;
+        op.rows_per_patch = 1;
+        op.rows = g.rows;
+        op.cols = g.cols;
+        op.K = g.K;
+        op.bn = tc_pick_bn(g.cols, false);
+        op.tf32 = true;
+        op.epilogue = kEpiStore;
+        op.tag = g.tag;
+        return tc_gemm(op, st);
+    }
     TcGemmOp op{};
     op.A = g.A;
     op.lda = g.lda;
@@ -385,7 +437,7 @@ int forward(const Dims& d, const Layout& L, const float* P, const float* x_in, c
         const int cin = d.si[s], cout = d.sd[s];
         F2S_TRY(linear_op(gemm_args(fin, ldin, P + sp.content_w, nullptr, w.content, 2 * cout, R,
                                     2 * cout, cin),
-                          d.enc_gemm_precision, st));  // tag: gemm_content
+                          d.enc_gemm_precision, st, w.split_a, w.split_w));  // tag: gemm_content
         EdgeArgs ea{};
         ea.content = w.content;
         ea.ldc = 2 * cout;
@@ -422,7 +474,7 @@ int forward(const Dims& d, const Layout& L, const float* P, const float* x_in, c
         GemmArgs g = gemm_args(w.cat, d.sum_stage, P + L.proj_w, nullptr, w.x, C, R, C,
                                d.sum_stage);
         g.tag = kTagGemmHead;
-        F2S_TRY(linear_op(g, d.enc_gemm_precision, st));
+        F2S_TRY(linear_op(g, d.enc_gemm_precision, st, w.split_a, w.split_w));
     }
     F2S_TRY(ln_affine_leaky(w.x, C, P + L.proj_ln_w, P + L.proj_ln_b, R, C, false, st));
     // trunk (transformer.py:75-89)

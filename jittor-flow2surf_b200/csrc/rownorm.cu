@@ -19,7 +19,40 @@ __device__ __forceinline__ void row_stats(const float* x, int C, int lane, float
     rstd = rsqrtf(f2s_warp_sum(q) / (float)C + 1e-6f);
 }
 
+// Rows of up to 256 channels held in registers: lane `l` owns the float2
+// pairs (l + 32 i) for i < kPairs, so a row is read from HBM once with
+// coalesced 8-byte loads.
+constexpr int kPairs = 4;
+
+__device__ __forceinline__ void row_load(const float* x, int C, int lane, float2 (&v)[kPairs]) {
+#pragma unroll
+    for (int i = 0; i < kPairs; ++i) {
+        const int c = 2 * (lane + 32 * i);
+        v[i] = c < C ? *reinterpret_cast<const float2*>(x + c) : make_float2(0.0f, 0.0f);
+    }
+}
+
+__device__ __forceinline__ void row_stats_reg(const float2 (&v)[kPairs], int C, int lane,
+                                              float& mean, float& rstd) {
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kPairs; ++i) s += v[i].x + v[i].y;
+    mean = f2s_warp_sum(s) / (float)C;
+    float q = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kPairs; ++i) {
+        if (2 * (lane + 32 * i) < C) {
+            const float d0 = v[i].x - mean, d1 = v[i].y - mean;
+            q = fmaf(d0, d0, q);
+            q = fmaf(d1, d1, q);
+        }
+    }
+    rstd = rsqrtf(f2s_warp_sum(q) / (float)C + 1e-6f);
+}
+
 // AdaLN-Zero modulate(norm(x), shift, scale) (transformer.py:10-12,85,88).
+// kPaired: C even, C <= 256, 8-byte aligned rows (the register path).
+template <bool kPaired>
 __global__ void ln_modulate_kernel(const float* __restrict__ x, int ldx, float* __restrict__ h,
                                    int ldh, const float* __restrict__ mod, int mod_stride,
                                    int scale_off, int shift_off, int rows, int rows_per_patch,
@@ -28,17 +61,38 @@ __global__ void ln_modulate_kernel(const float* __restrict__ x, int ldx, float* 
     const int lane = threadIdx.x & 31;
     if (row >= rows) return;
     const float* xr = x + (size_t)row * ldx;
-    float mean, rstd;
-    row_stats(xr, C, lane, mean, rstd);
     const float* m = mod + (size_t)(row / rows_per_patch) * mod_stride;
     float* hr = h + (size_t)row * ldh;
-    for (int c = lane; c < C; c += 32) {
-        const float v = (xr[c] - mean) * rstd * (1.0f + m[scale_off + c]) + m[shift_off + c];
-        hr[c] = round_tf32 ? f2s_round_tf32(v) : v;
+    float mean, rstd;
+    if constexpr (kPaired) {
+        float2 v[kPairs];
+        row_load(xr, C, lane, v);
+        row_stats_reg(v, C, lane, mean, rstd);
+#pragma unroll
+        for (int i = 0; i < kPairs; ++i) {
+            const int c = 2 * (lane + 32 * i);
+            if (c < C) {
+                float a = (v[i].x - mean) * rstd * (1.0f + m[scale_off + c]) + m[shift_off + c];
+                float b = (v[i].y - mean) * rstd * (1.0f + m[scale_off + c + 1]) +
+                          m[shift_off + c + 1];
+                if (round_tf32) {
+                    a = f2s_round_tf32(a);
+                    b = f2s_round_tf32(b);
+                }
+                *reinterpret_cast<float2*>(hr + c) = make_float2(a, b);
+            }
+        }
+    } else {
+        row_stats(xr, C, lane, mean, rstd);
+        for (int c = lane; c < C; c += 32) {
+            const float v = (xr[c] - mean) * rstd * (1.0f + m[scale_off + c]) + m[shift_off + c];
+            hr[c] = round_tf32 ? f2s_round_tf32(v) : v;
+        }
     }
 }
 
 // Affine ChannelLayerNorm + LeakyReLU(0.2) (encoder.py:118-123, decoder.py:18-22).
+template <bool kPaired>
 __global__ void ln_affine_leaky_kernel(float* __restrict__ y, int ldy,
                                        const float* __restrict__ gamma,
                                        const float* __restrict__ beta, int rows, int C,
@@ -48,10 +102,29 @@ __global__ void ln_affine_leaky_kernel(float* __restrict__ y, int ldy,
     if (row >= rows) return;
     float* yr = y + (size_t)row * ldy;
     float mean, rstd;
-    row_stats(yr, C, lane, mean, rstd);
-    for (int c = lane; c < C; c += 32) {
-        const float v = f2s_leaky((yr[c] - mean) * rstd * gamma[c] + beta[c]);
-        yr[c] = round_tf32 ? f2s_round_tf32(v) : v;
+    if constexpr (kPaired) {
+        float2 v[kPairs];
+        row_load(yr, C, lane, v);
+        row_stats_reg(v, C, lane, mean, rstd);
+#pragma unroll
+        for (int i = 0; i < kPairs; ++i) {
+            const int c = 2 * (lane + 32 * i);
+            if (c < C) {
+                float a = f2s_leaky((v[i].x - mean) * rstd * gamma[c] + beta[c]);
+                float b = f2s_leaky((v[i].y - mean) * rstd * gamma[c + 1] + beta[c + 1]);
+                if (round_tf32) {
+                    a = f2s_round_tf32(a);
+                    b = f2s_round_tf32(b);
+                }
+                *reinterpret_cast<float2*>(yr + c) = make_float2(a, b);
+            }
+        }
+    } else {
+        row_stats(yr, C, lane, mean, rstd);
+        for (int c = lane; c < C; c += 32) {
+            const float v = f2s_leaky((yr[c] - mean) * rstd * gamma[c] + beta[c]);
+            yr[c] = round_tf32 ? f2s_round_tf32(v) : v;
+        }
     }
 }
 
@@ -77,7 +150,10 @@ int ln_modulate(const float* x, int ldx, float* h, int ldh, const float* mod, in
                 bool round_tf32, cudaStream_t stream) {
     if (rows == 0) return F2S_OK;
     TraceScope trace(kTagRowNorm, stream);
-    ln_modulate_kernel<<<ceil_div(rows, kRowsPerCta), kRowsPerCta * 32, 0, stream>>>(
+    const bool paired = C % 2 == 0 && C <= 64 * kPairs && ldx % 2 == 0 && ldh % 2 == 0 &&
+                        ((uintptr_t)x & 7) == 0 && ((uintptr_t)h & 7) == 0;
+    auto kernel = paired ? ln_modulate_kernel<true> : ln_modulate_kernel<false>;
+    kernel<<<ceil_div(rows, kRowsPerCta), kRowsPerCta * 32, 0, stream>>>(
         x, ldx, h, ldh, mod, mod_stride, scale_off, shift_off, rows, rows_per_patch, C, round_tf32);
     return check_launch("ln_modulate_kernel");
 }
@@ -86,7 +162,9 @@ int ln_affine_leaky(float* y, int ldy, const float* gamma, const float* beta, in
                     bool round_tf32, cudaStream_t stream) {
     if (rows == 0) return F2S_OK;
     TraceScope trace(kTagRowNorm, stream);
-    ln_affine_leaky_kernel<<<ceil_div(rows, kRowsPerCta), kRowsPerCta * 32, 0, stream>>>(
+    const bool paired = C % 2 == 0 && C <= 64 * kPairs && ldy % 2 == 0 && ((uintptr_t)y & 7) == 0;
+    auto kernel = paired ? ln_affine_leaky_kernel<true> : ln_affine_leaky_kernel<false>;
+    kernel<<<ceil_div(rows, kRowsPerCta), kRowsPerCta * 32, 0, stream>>>(
         y, ldy, gamma, beta, rows, C, round_tf32);
     return check_launch("ln_affine_leaky_kernel");
 }

@@ -15,7 +15,9 @@
 //               column, so bias / gate loads and stores are coalesced), the
 //               epilogue applied and stored; then the accumulator buffer is
 //               freed, so the MMAs of the next tile overlap this epilogue.
-// Operands are bf16 (kind::f16) or fp32 read as tf32 (kind::tf32).
+// Operands are bf16 (kind::f16) or fp32 read as tf32 (kind::tf32), or
+// (3xTF32) pairs x = hi + lo of tf32 values with the products hi*hi + hi*lo +
+// lo*hi accumulated, which leaves only the lo*lo term (2^-22 relative) out.
 #include <mutex>
 
 #include "kernels.cuh"
@@ -57,11 +59,14 @@ __device__ __forceinline__ float epi_value(float v, const float* bias, int col) 
     return bias ? v + bias[col] : v;
 }
 
-template <bool kTf32, int kEpi>
+// kSplit (with kTf32): map_a2 / map_b2 hold the low parts of A / W.
+template <bool kTf32, int kEpi, bool kSplit>
 __global__ void __launch_bounds__(kThreads, 1)
-tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-               const __grid_constant__ CUtensorMap map_b2, const TcGemmArgs g) {
+tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_a2,
+               const __grid_constant__ CUtensorMap map_b, const __grid_constant__ CUtensorMap map_b2,
+               const TcGemmArgs g) {
     constexpr bool kDual = kEpi == kEpiSwiGlu;
+    static_assert(!(kSplit && (kDual || !kTf32)), "3xTF32 runs the single-matrix tf32 form");
     extern __shared__ __align__(1024) unsigned char tc_smem_raw[];
     // 1024-byte alignment of the tile region (SWIZZLE_128B atoms)
     unsigned char* smem = reinterpret_cast<unsigned char*>(
@@ -69,7 +74,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     const int S = g.stages;
     const uint32_t a_bytes = kTileM * 128;
     const uint32_t b_bytes = (uint32_t)g.bn * 128;
-    const uint32_t stage_bytes = a_bytes + b_bytes * (kDual ? 2 : 1);
+    // stage: A (A_lo), then W (W2 for SwiGLU, W_lo for 3xTF32)
+    const uint32_t a_stage = a_bytes * (kSplit ? 2 : 1);
+    const uint32_t stage_bytes = a_stage + b_bytes * ((kDual || kSplit) ? 2 : 1);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)S * stage_bytes);
     uint64_t* empty = full + S;
     uint64_t* tfull = empty + S;      // [2]
@@ -100,7 +107,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         tc::fence_barrier_init();
         tc::prefetch_tensormap(&map_a);
         tc::prefetch_tensormap(&map_b);
-        if (kDual) tc::prefetch_tensormap(&map_b2);
+        if (kSplit) tc::prefetch_tensormap(&map_a2);
+        if (kDual || kSplit) tc::prefetch_tensormap(&map_b2);
     }
     if (warp == 1) tc::tmem_alloc(tmem_slot, tmem_cols);
     tc::tc_fence_before();
@@ -129,8 +137,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                     tc::mbar_arrive_expect_tx(&full[stage], stage_bytes);
                     const int k0 = kb * (kTf32 ? 32 : 64);
                     tc::tma_load_2d(st, &map_a, &full[stage], k0, m0);
-                    tc::tma_load_2d(st + a_bytes, &map_b, &full[stage], k0, n0);
-                    if (kDual) tc::tma_load_2d(st + a_bytes + b_bytes, &map_b2, &full[stage], k0, n0);
+                    if (kSplit) tc::tma_load_2d(st + a_bytes, &map_a2, &full[stage], k0, m0);
+                    tc::tma_load_2d(st + a_stage, &map_b, &full[stage], k0, n0);
+                    if (kDual || kSplit)
+                        tc::tma_load_2d(st + a_stage + b_bytes, &map_b2, &full[stage], k0, n0);
                     pending |= 1u << stage;
                     pending_phase = (pending_phase & ~(1u << stage)) | (phase << stage);
                     if (++stage == S) {
@@ -172,12 +182,18 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
 #pragma unroll
                     for (int k = 0; k < kSteps; ++k) {
                         const uint64_t a = tc::sw128_desc(st + k * 32);
-                        const uint64_t b = tc::sw128_desc(st + a_bytes + k * 32);
+                        const uint64_t b = tc::sw128_desc(st + a_stage + k * 32);
                         const uint32_t acc = (kb | k) ? 1u : 0u;
                         tc::umma<kTf32>(d, a, b, g.idesc, acc);
                         if (kDual) {
-                            const uint64_t b2 = tc::sw128_desc(st + a_bytes + b_bytes + k * 32);
+                            const uint64_t b2 = tc::sw128_desc(st + a_stage + b_bytes + k * 32);
                             tc::umma<kTf32>(d + (uint32_t)g.bn, a, b2, g.idesc, acc);
+                        }
+                        if (kSplit) {
+                            const uint64_t a_lo = tc::sw128_desc(st + a_bytes + k * 32);
+                            const uint64_t b_lo = tc::sw128_desc(st + a_stage + b_bytes + k * 32);
+                            tc::umma<kTf32>(d, a, b_lo, g.idesc, 1u);
+                            tc::umma<kTf32>(d, a_lo, b, g.idesc, 1u);
                         }
                     }
                     tc::umma_commit(&empty[stage]);
@@ -314,12 +330,12 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-template <bool kTf32, int kEpi>
-int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb2,
-              const TcGemmArgs& g, size_t smem, int grid, cudaStream_t st) {
-    auto kernel = tc_gemm_kernel<kTf32, kEpi>;
+template <bool kTf32, int kEpi, bool kSplit = false>
+int launch_tc(const CUtensorMap& ma, const CUtensorMap& ma2, const CUtensorMap& mb,
+              const CUtensorMap& mb2, const TcGemmArgs& g, size_t smem, int grid, cudaStream_t st) {
+    auto kernel = tc_gemm_kernel<kTf32, kEpi, kSplit>;
     F2S_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    kernel<<<grid, kThreads, smem, st>>>(ma, mb, mb2, g);
+    kernel<<<grid, kThreads, smem, st>>>(ma, ma2, mb, mb2, g);
     return check_launch("tc_gemm_kernel");
 }
 
@@ -386,7 +402,10 @@ int tc_gemm(const TcGemmOp& op, cudaStream_t st) {
     if (op.rows == 0 || op.cols == 0) return F2S_OK;
     F2S_REQUIRE(op.A && op.W && op.Y && op.K > 0, "tc_gemm: bad operands");
     const bool dual = op.epilogue == kEpiSwiGlu;
+    const bool split = op.A_lo != nullptr;
     F2S_REQUIRE(!dual || op.W2, "tc_gemm: SwiGLU needs W2");
+    F2S_REQUIRE(!split || (op.W_lo && op.tf32 && op.epilogue == kEpiStore),
+                "tc_gemm: 3xTF32 needs W_lo, tf32 operands and the plain epilogue");
     F2S_REQUIRE(op.epilogue != kEpiGatedResidual || (op.gate && op.rows_per_patch > 0 && !op.y_bf16),
                 "tc_gemm: gated residual needs a gate and an fp32 output");
     int bn = op.bn;
@@ -394,12 +413,15 @@ int tc_gemm(const TcGemmOp& op, cudaStream_t st) {
                 "tc_gemm: bad N tile %d", bn);
     int* err = tc_error_word();
     if (!err) return fail(F2S_ERR_CUDA, "tc_gemm: device error word unavailable");
-    CUtensorMap ma, mb, mb2;
+    CUtensorMap ma, ma2, mb, mb2;
     const int bk = op.tf32 ? 32 : 64;
     F2S_TRY(make_tensor_map_2d(&ma, op.A, op.tf32, op.rows, op.K, op.lda, kTileM, bk));
     F2S_TRY(make_tensor_map_2d(&mb, op.W, op.tf32, op.cols, op.K, op.K, bn, bk));
     if (dual) F2S_TRY(make_tensor_map_2d(&mb2, op.W2, op.tf32, op.cols, op.K, op.K, bn, bk));
+    else if (split) F2S_TRY(make_tensor_map_2d(&mb2, op.W_lo, true, op.cols, op.K, op.K, bn, bk));
     else mb2 = mb;
+    if (split) F2S_TRY(make_tensor_map_2d(&ma2, op.A_lo, true, op.rows, op.K, op.lda, kTileM, bk));
+    else ma2 = ma;
 
     TcGemmArgs g{};
     g.rows = op.rows;
@@ -419,7 +441,8 @@ int tc_gemm(const TcGemmOp& op, cudaStream_t st) {
     g.rows_per_patch = op.rows_per_patch > 0 ? op.rows_per_patch : 1;
     g.round_tf32 = op.round_tf32 ? 1 : 0;
     g.err = err;
-    const size_t stage_bytes = (size_t)kTileM * 128 + (size_t)bn * 128 * (dual ? 2 : 1);
+    const size_t stage_bytes =
+        (size_t)kTileM * 128 * (split ? 2 : 1) + (size_t)bn * 128 * ((dual || split) ? 2 : 1);
     const size_t stage_buf_bytes = (size_t)(kEpilogueThreads / 32) * (dual ? 2 : 1) * 32 * 33 * sizeof(float);
     int stages = (int)((kSmemLimit - 1024 - 256 - stage_buf_bytes) / stage_bytes);
     stages = stages > 8 ? 8 : stages;
@@ -431,20 +454,47 @@ int tc_gemm(const TcGemmOp& op, cudaStream_t st) {
     const int tiles = ceil_div(op.rows, kTileM) * ceil_div(op.cols, bn);
     const int grid = tiles < sm_count() ? tiles : sm_count();
     TraceScope trace(op.tag, st);
+    if (split) return launch_tc<true, kEpiStore, true>(ma, ma2, mb, mb2, g, smem, grid, st);
     if (op.tf32) {
         switch (op.epilogue) {
-            case kEpiStore: return launch_tc<true, kEpiStore>(ma, mb, mb2, g, smem, grid, st);
-            case kEpiGatedResidual: return launch_tc<true, kEpiGatedResidual>(ma, mb, mb2, g, smem, grid, st);
-            case kEpiSwiGlu: return launch_tc<true, kEpiSwiGlu>(ma, mb, mb2, g, smem, grid, st);
+            case kEpiStore: return launch_tc<true, kEpiStore>(ma, ma2, mb, mb2, g, smem, grid, st);
+            case kEpiGatedResidual: return launch_tc<true, kEpiGatedResidual>(ma, ma2, mb, mb2, g, smem, grid, st);
+            case kEpiSwiGlu: return launch_tc<true, kEpiSwiGlu>(ma, ma2, mb, mb2, g, smem, grid, st);
         }
     } else {
         switch (op.epilogue) {
-            case kEpiStore: return launch_tc<false, kEpiStore>(ma, mb, mb2, g, smem, grid, st);
-            case kEpiGatedResidual: return launch_tc<false, kEpiGatedResidual>(ma, mb, mb2, g, smem, grid, st);
-            case kEpiSwiGlu: return launch_tc<false, kEpiSwiGlu>(ma, mb, mb2, g, smem, grid, st);
+            case kEpiStore: return launch_tc<false, kEpiStore>(ma, ma2, mb, mb2, g, smem, grid, st);
+            case kEpiGatedResidual: return launch_tc<false, kEpiGatedResidual>(ma, ma2, mb, mb2, g, smem, grid, st);
+            case kEpiSwiGlu: return launch_tc<false, kEpiSwiGlu>(ma, ma2, mb, mb2, g, smem, grid, st);
         }
     }
     return fail(F2S_ERR_INVALID_ARGUMENT, "tc_gemm: bad epilogue");
+}
+
+namespace {
+// hi = x rounded to the nearest tf32, lo = x - hi (exact), both (rows, K).
+__global__ void split_tf32_kernel(const float* __restrict__ x, int ldx, int rows, int K,
+                                  float* __restrict__ hi, float* __restrict__ lo) {
+    const int64_t total = (int64_t)rows * K;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = i / K, c = i - r * K;
+        const float v = x[r * ldx + c];
+        const float h = f2s_round_tf32(v);
+        hi[i] = h;
+        lo[i] = v - h;
+    }
+}
+}  // namespace
+
+int split_tf32(const float* x, int ldx, int rows, int K, float* hi, float* lo, cudaStream_t st) {
+    if (rows == 0 || K == 0) return F2S_OK;
+    const int64_t total = (int64_t)rows * K;
+    int64_t blocks = (total + 255) / 256;
+    const int64_t cap = (int64_t)sm_count() * 16;
+    blocks = blocks < cap ? blocks : cap;
+    split_tf32_kernel<<<(int)blocks, 256, 0, st>>>(x, ldx, rows, K, hi, lo);
+    return check_launch("split_tf32_kernel");
 }
 
 int tc_pick_bn(int cols, bool swiglu) {
