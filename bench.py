@@ -62,7 +62,32 @@ def parse_args():
                    help="arithmetic of the trunk and decoder contractions")
     p.add_argument("--encoder-precision", choices=["fp32", "tf32", "bf16x3"], default="bf16x3",
                    help="arithmetic of the neighbour-stage contractions")
+    p.add_argument("--profile-forward", type=int, default=0, metavar="B",
+                   help="instead of the benchmark: two model forwards on B synthetic "
+                        "1000-point patches and exit (a small case for ncu captures)")
     return p.parse_args()
+
+
+def profile_forward(args) -> None:
+    """Two forwards of the default architecture on B patches: the first warms
+    up, the second is the one an ncu capture skips to (-s <launches of one
+    forward>)."""
+    import torch
+
+    from flow2surf_b200 import build_model
+    from flow2surf_b200.synthetic import DEFAULT_CONFIG, random_parameters
+
+    B = args.profile_forward
+    model = build_model(DEFAULT_CONFIG, precision=args.precision,
+                        encoder_precision=args.encoder_precision)
+    model.load_parameters(random_parameters(DEFAULT_CONFIG, seed=0))
+    gen = torch.Generator().manual_seed(0)
+    x = (torch.randn(B, 3, DENOISE["patch_size"], generator=gen) * 0.3).cuda()
+    alpha = torch.full((B,), 0.5).cuda()
+    for _ in range(2):
+        v = model(x, alpha)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_forward": B, "checksum": float(v.abs().sum())}), flush=True)
 
 
 def workload_config(args, world: int) -> dict:
@@ -388,6 +413,9 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference(args, rank, world)
+        return
+    if args.profile_forward > 0:
+        profile_forward(args)
         return
     if world > 1:
         import torch

@@ -11,10 +11,14 @@
 //            on TMEM lanes; each thread keeps an online max / sum over its
 //            key's query columns -> L_j = log-sum-exp over queries.
 //   pass 2   CTA = (patch, 128 queries), 64-key tiles: S = Q K^T (split bf16)
-//            into TMEM; softmax threads write P = exp(S - L) (masked, tf32)
-//            into shared memory in the swizzled A-operand layout and keep the
-//            row sums; O += P V (tf32 MMA, O resident in TMEM, 192 columns);
-//            finally out = h - O / (sum + 1e-9).
+//            into TMEM (double-buffered); softmax threads compute P = exp(S -
+//            L) = 2^(S log2 e - L log2 e) (masked; the patch's L held in
+//            shared memory) while the previous P V product runs, then write P
+//            (tf32) into shared memory in the swizzled A-operand layout and
+//            keep the row sums; O += P V (tf32 MMA, O resident in TMEM, 192
+//            columns); finally out = h - O / (sum + 1e-9). K tiles are loaded
+//            three deep and refilled once their S product completes, V^T tiles
+//            two deep.
 // Warp 4 lane 0 issues every TMA copy and MMA; warps 0-3 (one thread per
 // TMEM lane) do the exponentials. All waits are bounded.
 #include <cfloat>
@@ -28,6 +32,7 @@ namespace {
 constexpr int kRows = 128;        // keys (pass 1) / queries (pass 2) per CTA
 constexpr int kDPad = 64;         // padded q/k width: 64 bf16 = 128 bytes
 constexpr int kKeyTile = 64;      // keys per pass-2 tile
+constexpr int kKStages = 3;       // pass-2 K tiles in flight
 constexpr int kThreads = 160;     // warps 0-3 softmax/epilogue, warp 4 TMA + MMA
 constexpr unsigned kFull = 0xffffffffu;
 
@@ -113,6 +118,7 @@ struct AttnArgs {
     float* out;
     int ldo;
     int round_tf32;
+    int vec4;           // pass 2: h / out rows 16-byte aligned
     uint32_t idesc_s;   // bf16, M = 128, N = 128 (pass 1) / 64 (pass 2)
     uint32_t idesc_pv;  // tf32, M = 128, N = C
     int* err;
@@ -273,32 +279,38 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
     const uint32_t v_bytes = (uint32_t)C * 128;      // one K-block: C rows x 32 fp32 keys
     constexpr uint32_t kPBytes = kRows * 128;        // one K-block: 128 queries x 32 fp32 keys
     unsigned char* sQ = smem;                                  // hi, lo
-    unsigned char* sK = sQ + 2 * kQBytes;                      // 2 stages x (hi, lo)
-    unsigned char* sV = sK + 4 * kKBytes;                      // 2 stages x 2 K-blocks
+    unsigned char* sK = sQ + 2 * kQBytes;                      // kKStages x (hi, lo)
+    unsigned char* sV = sK + 2 * kKStages * kKBytes;           // 2 stages x 2 K-blocks
     unsigned char* sP = sV + 4 * v_bytes;                      // 2 K-blocks
-    float* sL = reinterpret_cast<float*>(sP + 2 * kPBytes);    // 2 stages x 64
-    int* sFlag = reinterpret_cast<int*>(sL + 2 * kKeyTile);    // softmax go / stop
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sFlag + 2);
+    const int nk = (a.N + kKeyTile - 1) / kKeyTile;
+    // the patch's per-key log-sum-exp values times log2(e), nk * 64 of them
+    float* sL = reinterpret_cast<float*>(sP + 2 * kPBytes);
+    // softmax go / stop decisions: [0, 2) S ready, [2, 4) P free (by tile
+    // parity), [4] output ready; written by thread 0 before a named barrier
+    int* sFlag = reinterpret_cast<int*>(sL + nk * kKeyTile);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(
+        (reinterpret_cast<uintptr_t>(sFlag + 5) + 7) & ~uintptr_t(7));
     uint64_t* q_full = bars;        // [1]
-    uint64_t* kv_full = bars + 1;   // [2]
-    uint64_t* kv_empty = bars + 3;  // [2]
-    uint64_t* s_full = bars + 5;    // [2]
-    uint64_t* s_empty = bars + 7;   // [2]  (128 arrivals)
-    uint64_t* p_full = bars + 9;    // [1]  (128 arrivals)
-    uint64_t* pv_done = bars + 10;  // [1]
-    uint64_t* done = bars + 11;     // [1]
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+    uint64_t* k_full = bars + 1;    // [kKStages]
+    uint64_t* k_empty = bars + 4;   // [kKStages]
+    uint64_t* v_full = bars + 7;    // [2]
+    uint64_t* v_empty = bars + 9;   // [2]
+    uint64_t* s_full = bars + 11;   // [2]
+    uint64_t* s_empty = bars + 13;  // [2]  (128 arrivals)
+    uint64_t* p_full = bars + 15;   // [1]  (128 arrivals)
+    uint64_t* pv_done = bars + 16;  // [1]
+    uint64_t* done = bars + 17;     // [1]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
 
     const int b = blockIdx.x / a.tiles;
     const int q0 = (blockIdx.x - b * a.tiles) * kRows;
-    const int nk = (a.N + kKeyTile - 1) / kKeyTile;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // TMEM: S double buffer at columns [0, 128), O at [256, 256 + C)
     constexpr uint32_t kOCol = 256;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < 12; ++i)
-            tc::mbar_init(&bars[i], (i == 7 || i == 8 || i == 9) ? 128 : 1);
+        for (int i = 0; i < 18; ++i)
+            tc::mbar_init(&bars[i], (i == 13 || i == 14 || i == 15) ? 128 : 1);
         tc::fence_barrier_init();
     }
     if (warp == 0) tc::tmem_alloc(tmem_slot, 512);
@@ -310,32 +322,40 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
     if (warp == 4) {
         if (lane == 0) {
             bool ok = true;
-            int kv_issued = 0, kv_landed = 0;  // K/V tiles loaded / seen complete
-            auto load_kv = [&](int i) {
-                const int s = i & 1;
-                tc::mbar_arrive_expect_tx(&kv_full[s], 2 * kKBytes + 2 * v_bytes);
-                tma_load_3d(sK + (2 * s) * kKBytes, &map_khi, &kv_full[s], kDPad, i * kKeyTile, b);
-                tma_load_3d(sK + (2 * s + 1) * kKBytes, &map_klo, &kv_full[s], kDPad, i * kKeyTile, b);
-                tma_load_3d(sV + (2 * s) * v_bytes, &map_vt, &kv_full[s], i * kKeyTile, 0, b);
-                tma_load_3d(sV + (2 * s + 1) * v_bytes, &map_vt, &kv_full[s], i * kKeyTile + 32, 0, b);
-                kv_issued = i + 1;
+            // K tiles run kKStages deep and are refilled as soon as their S
+            // product completes; V tiles two deep, refilled once the P V
+            // product before the current one completes
+            int k_issued = 0, k_landed = 0, v_issued = 0, v_landed = 0;
+            auto load_k = [&](int i) {
+                const int ks = i % kKStages;
+                tc::mbar_arrive_expect_tx(&k_full[ks], 2 * kKBytes);
+                tma_load_3d(sK + (2 * ks) * kKBytes, &map_khi, &k_full[ks], kDPad, i * kKeyTile, b);
+                tma_load_3d(sK + (2 * ks + 1) * kKBytes, &map_klo, &k_full[ks], kDPad, i * kKeyTile, b);
+                k_issued = i + 1;
+            };
+            auto load_v = [&](int i) {
+                const int vs = i & 1;
+                tc::mbar_arrive_expect_tx(&v_full[vs], 2 * v_bytes);
+                tma_load_3d(sV + (2 * vs) * v_bytes, &map_vt, &v_full[vs], i * kKeyTile, 0, b);
+                tma_load_3d(sV + (2 * vs + 1) * v_bytes, &map_vt, &v_full[vs], i * kKeyTile + 32, 0, b);
+                v_issued = i + 1;
             };
             tc::mbar_arrive_expect_tx(q_full, 2 * kQBytes);
             tma_load_3d(sQ, &map_qhi, q_full, 0, q0, b);
             tma_load_3d(sQ + kQBytes, &map_qlo, q_full, 0, q0, b);
-            load_kv(0);
-            if (nk > 1) load_kv(1);
+            for (int i = 0; i < kKStages && i < nk; ++i) load_k(i);
+            for (int i = 0; i < 2 && i < nk; ++i) load_v(i);
             ok = tc::mbar_wait(q_full, 0, a.err);
             if (!ok) tc::mbar_drain(q_full, 0);
             const uint32_t q_hi = tc::smem_u32(sQ), q_lo = q_hi + kQBytes;
             auto issue_s = [&](int i) -> bool {
+                const int ks = i % kKStages;
+                if (!tc::mbar_wait(&k_full[ks], (uint32_t)(i / kKStages) & 1u, a.err)) return false;
+                k_landed = i + 1;
                 const int s = i & 1;
-                const uint32_t ph = (uint32_t)(i >> 1) & 1u;
-                if (!tc::mbar_wait(&kv_full[s], ph, a.err)) return false;
-                kv_landed = i + 1;
-                if (!tc::mbar_wait(&s_empty[s], ph ^ 1u, a.err)) return false;
+                if (!tc::mbar_wait(&s_empty[s], ((uint32_t)(i >> 1) & 1u) ^ 1u, a.err)) return false;
                 tc::tc_fence_after();
-                const uint32_t k_hi = tc::smem_u32(sK + (2 * s) * kKBytes), k_lo = k_hi + kKBytes;
+                const uint32_t k_hi = tc::smem_u32(sK + (2 * ks) * kKBytes), k_lo = k_hi + kKBytes;
                 const uint32_t d = tmem + (uint32_t)(s * 64);
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk) {
@@ -346,23 +366,33 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
                     tc::umma<false>(d, tc::sw128_desc(q_lo + o), tc::sw128_desc(k_hi + o), a.idesc_s, 1u);
                 }
                 tc::umma_commit(&s_full[s]);
+                tc::umma_commit(&k_empty[ks]);
                 return true;
             };
             if (ok) ok = issue_s(0);
             const uint32_t p0 = tc::smem_u32(sP);
             for (int i = 0; i < nk && ok; ++i) {
-                const int s = i & 1;
                 if (i + 1 < nk && !issue_s(i + 1)) {
                     ok = false;
                     break;
                 }
-                // P_i written by the softmax threads
-                if (!tc::mbar_wait(p_full, (uint32_t)i & 1u, a.err)) {
+                // S_i is done with its K tile: refill that stage with tile i + kKStages
+                if (i + kKStages < nk) {
+                    if (!tc::mbar_wait(&k_empty[i % kKStages], (uint32_t)(i / kKStages) & 1u, a.err)) {
+                        ok = false;
+                        break;
+                    }
+                    load_k(i + kKStages);
+                }
+                // P_i written by the softmax threads, V_i landed
+                if (!tc::mbar_wait(p_full, (uint32_t)i & 1u, a.err) ||
+                    !tc::mbar_wait(&v_full[i & 1], (uint32_t)(i >> 1) & 1u, a.err)) {
                     ok = false;
                     break;
                 }
+                v_landed = i + 1;
                 tc::tc_fence_after();
-                const uint32_t v0 = tc::smem_u32(sV + (2 * s) * v_bytes);
+                const uint32_t v0 = tc::smem_u32(sV + (2 * (i & 1)) * v_bytes);
 #pragma unroll
                 for (int kb = 0; kb < 2; ++kb)
 #pragma unroll
@@ -373,18 +403,21 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
                                        (i | kb | kk) ? 1u : 0u);
                     }
                 tc::umma_commit(pv_done);
-                tc::umma_commit(&kv_empty[s]);
-                if (i + 2 < nk) {
-                    if (!tc::mbar_wait(&kv_empty[s], (uint32_t)(i >> 1) & 1u, a.err)) {
+                tc::umma_commit(&v_empty[i & 1]);
+                // P V_{i-1} is done with its V tile: refill that stage with tile i + 1
+                if (i >= 1 && i + 1 < nk) {
+                    if (!tc::mbar_wait(&v_empty[(i - 1) & 1], (uint32_t)((i - 1) >> 1) & 1u, a.err)) {
                         ok = false;
                         break;
                     }
-                    load_kv(i + 2);
+                    load_v(i + 1);
                 }
             }
-            // K/V copies still in flight land before the CTA exits
-            for (int i = kv_landed; i < kv_issued; ++i)
-                tc::mbar_drain(&kv_full[i & 1], (uint32_t)(i >> 1) & 1u);
+            // K / V copies still in flight land before the CTA exits
+            for (int i = k_landed; i < k_issued; ++i)
+                tc::mbar_drain(&k_full[i % kKStages], (uint32_t)(i / kKStages) & 1u);
+            for (int i = v_landed; i < v_issued; ++i)
+                tc::mbar_drain(&v_full[i & 1], (uint32_t)(i >> 1) & 1u);
             tc::umma_commit(done);
             tc::mbar_drain(done, 0);
         }
@@ -394,23 +427,17 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
         // the outcome, so the four softmax warps always take the same path
         const int row = warp * 32 + lane;
         const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+        constexpr float kLog2e = 1.44269504088896341f;
+        for (int j = row; j < nk * kKeyTile; j += kRows)
+            sL[j] = j < a.N ? a.colstats[(size_t)b * a.N + j] * kLog2e : 0.0f;
         float den = 0.0f;
         bool ok = true;
         for (int i = 0; i < nk; ++i) {
             const int s = i & 1;
             const uint32_t ph = (uint32_t)(i >> 1) & 1u;
-            if (row < kKeyTile) {  // this key tile's log-sum-exp values
-                const int key = i * kKeyTile + row;
-                sL[s * kKeyTile + row] = key < a.N ? a.colstats[(size_t)b * a.N + key] : 0.0f;
-            }
-            if (row == 0) {
-                bool go = tc::mbar_wait(&s_full[s], ph, a.err);
-                // the previous P must have been consumed before it is overwritten
-                if (go && i > 0) go = tc::mbar_wait(pv_done, (uint32_t)(i - 1) & 1u, a.err);
-                sFlag[0] = go ? 1 : 0;
-            }
+            if (row == 0) sFlag[s] = tc::mbar_wait(&s_full[s], ph, a.err) ? 1 : 0;
             named_sync_softmax();
-            if (!sFlag[0]) {
+            if (!sFlag[s]) {
                 ok = false;
                 break;
             }
@@ -421,12 +448,31 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
                           *reinterpret_cast<float(*)[32]>(p + 32));
             tc::tc_fence_before();
             tc::mbar_arrive(&s_empty[s]);
+            // p = exp(S - L) = 2^(S log2 e - L log2 e), computed while the
+            // previous tile's P V product may still run
             const int valid = min(kKeyTile, a.N - i * kKeyTile);
+            const float* Lt = sL + i * kKeyTile;
 #pragma unroll
-            for (int j = 0; j < 64; ++j) {
-                const float e = j < valid ? __expf(p[j] - sL[s * kKeyTile + j]) : 0.0f;
-                p[j] = e;
-                den += e;
+            for (int j = 0; j < 64; j += 4) {
+                const float4 l4 = *reinterpret_cast<const float4*>(Lt + j);
+                const float lj[4] = {l4.x, l4.y, l4.z, l4.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float pe =
+                        j + e < valid ? f2s_ex2_approx(fmaf(p[j + e], kLog2e, -lj[e])) : 0.0f;
+                    p[j + e] = pe;
+                    den += pe;
+                }
+            }
+            // the previous P must have been consumed before it is overwritten
+            if (i > 0) {
+                if (row == 0)
+                    sFlag[2 + s] = tc::mbar_wait(pv_done, (uint32_t)(i - 1) & 1u, a.err) ? 1 : 0;
+                named_sync_softmax();
+                if (!sFlag[2 + s]) {
+                    ok = false;
+                    break;
+                }
             }
 #pragma unroll
             for (int kb = 0; kb < 2; ++kb)
@@ -442,9 +488,9 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
         }
         // wait for the last P V product, then write h - O / (den + 1e-9)
         if (ok) {
-            if (row == 0) sFlag[1] = tc::mbar_wait(pv_done, (uint32_t)(nk - 1) & 1u, a.err) ? 1 : 0;
+            if (row == 0) sFlag[4] = tc::mbar_wait(pv_done, (uint32_t)(nk - 1) & 1u, a.err) ? 1 : 0;
             named_sync_softmax();
-            ok = sFlag[1] != 0;
+            ok = sFlag[4] != 0;
         }
         if (ok) {
             tc::tc_fence_after();
@@ -455,11 +501,29 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
                 float o[32];
                 tc::tmem_ld32(tmem + lane_base + kOCol + (uint32_t)c0, o);
                 if (qrow < a.N) {
+                    if (a.vec4) {  // 16-byte rows: float4 loads and stores
+                        float* dst = a.out + grow * a.ldo + c0;
+                        const float* hr = a.h ? a.h + grow * a.ldh + c0 : nullptr;
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        const float av = o[i] * inv;
-                        const float r = a.h ? a.h[grow * a.ldh + c0 + i] - av : av;
-                        a.out[grow * a.ldo + c0 + i] = a.round_tf32 ? f2s_round_tf32(r) : r;
+                        for (int i = 0; i < 32; i += 4) {
+                            const float4 hv = hr ? *reinterpret_cast<const float4*>(hr + i)
+                                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+                            float4 r = make_float4(hv.x - o[i] * inv, hv.y - o[i + 1] * inv,
+                                                   hv.z - o[i + 2] * inv, hv.w - o[i + 3] * inv);
+                            if (!hr) r = make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv,
+                                                     o[i + 3] * inv);
+                            if (a.round_tf32)
+                                r = make_float4(f2s_round_tf32(r.x), f2s_round_tf32(r.y),
+                                                f2s_round_tf32(r.z), f2s_round_tf32(r.w));
+                            *reinterpret_cast<float4*>(dst + i) = r;
+                        }
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) {
+                            const float av = o[i] * inv;
+                            const float r = a.h ? a.h[grow * a.ldh + c0 + i] - av : av;
+                            a.out[grow * a.ldo + c0 + i] = a.round_tf32 ? f2s_round_tf32(r) : r;
+                        }
                     }
                 }
             }
@@ -524,6 +588,8 @@ int attention_tc(const float* q, const float* k, int ldqk, const float* v, int l
     a.out = out;
     a.ldo = ldo;
     a.round_tf32 = round_tf32 ? 1 : 0;
+    a.vec4 = ldo % 4 == 0 && ((uintptr_t)out & 15) == 0 &&
+             (!h || (ldh % 4 == 0 && ((uintptr_t)h & 15) == 0));
     a.err = err;
     {
         TraceScope trace(kTagAttnColstats, st);
@@ -540,8 +606,9 @@ int attention_tc(const float* q, const float* k, int ldqk, const float* v, int l
         a.tiles = ceil_div(N, kRows);
         a.idesc_s = tc::make_idesc(kRows, kKeyTile, 1u);
         a.idesc_pv = tc::make_idesc(kRows, C, 2u);
-        const size_t smem = 1024 + 2 * kRows * 128 + 4 * kKeyTile * 128 + 4 * (size_t)C * 128 +
-                            2 * kRows * 128 + 2 * kKeyTile * 4 + 8 + 128;
+        const size_t smem = 1024 + 2 * kRows * 128 + 2 * kKStages * kKeyTile * 128 + 4 * (size_t)C * 128 +
+                            2 * kRows * 128 + (size_t)ceil_div(N, kKeyTile) * kKeyTile * 4 + 32 +
+                            8 + 18 * 8 + 16;
         F2S_LIMIT(smem <= 227 * 1024, "attention_tc: %zu bytes of shared memory", smem);
         F2S_CUDA_TRY(cudaFuncSetAttribute(attn_tc_output_kernel,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
