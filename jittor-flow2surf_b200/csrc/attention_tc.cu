@@ -45,6 +45,21 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
         : "memory");
 }
 
+// 3-D TMA tile store from shared memory (bulk group; no multicast).
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int c0, int c1,
+                                             int c2) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+            reinterpret_cast<uint64_t>(map)),
+        "r"(tc::smem_u32(src)), "r"(c0), "r"(c1), "r"(c2)
+        : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit_and_wait_read() {
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+
 __device__ __forceinline__ uint32_t sw128_offset(int row, int chunk) {
     return (uint32_t)((row >> 3) * 1024 + (row & 7) * 128 + ((chunk ^ (row & 7)) << 4));
 }
@@ -119,6 +134,7 @@ struct AttnArgs {
     int ldo;
     int round_tf32;
     int vec4;           // pass 2: h / out rows 16-byte aligned
+    int tma_epi;        // pass 2: h / out tiles by TMA (16-byte pitches and bases)
     uint32_t idesc_s;   // bf16, M = 128, N = 128 (pass 1) / 64 (pass 2)
     uint32_t idesc_pv;  // tf32, M = 128, N = C
     int* err;
@@ -269,7 +285,9 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
                       const __grid_constant__ CUtensorMap map_qlo,
                       const __grid_constant__ CUtensorMap map_khi,
                       const __grid_constant__ CUtensorMap map_klo,
-                      const __grid_constant__ CUtensorMap map_vt, const AttnArgs a) {
+                      const __grid_constant__ CUtensorMap map_vt,
+                      const __grid_constant__ CUtensorMap map_h,
+                      const __grid_constant__ CUtensorMap map_out, const AttnArgs a) {
     extern __shared__ __align__(1024) unsigned char attn_smem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>(
         (reinterpret_cast<uintptr_t>(attn_smem_raw) + 1023) & ~uintptr_t(1023));
@@ -286,10 +304,11 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
     // the patch's per-key log-sum-exp values times log2(e), nk * 64 of them
     float* sL = reinterpret_cast<float*>(sP + 2 * kPBytes);
     // softmax go / stop decisions: [0, 2) S ready, [2, 4) P free (by tile
-    // parity), [4] output ready; written by thread 0 before a named barrier
+    // parity), [4] output ready, [5] h tile landed; written by thread 0
+    // before a named barrier
     int* sFlag = reinterpret_cast<int*>(sL + nk * kKeyTile);
     uint64_t* bars = reinterpret_cast<uint64_t*>(
-        (reinterpret_cast<uintptr_t>(sFlag + 5) + 7) & ~uintptr_t(7));
+        (reinterpret_cast<uintptr_t>(sFlag + 6) + 7) & ~uintptr_t(7));
     uint64_t* q_full = bars;        // [1]
     uint64_t* k_full = bars + 1;    // [kKStages]
     uint64_t* k_empty = bars + 4;   // [kKStages]
@@ -300,7 +319,8 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
     uint64_t* p_full = bars + 15;   // [1]  (128 arrivals)
     uint64_t* pv_done = bars + 16;  // [1]
     uint64_t* done = bars + 17;     // [1]
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
+    uint64_t* h_full = bars + 18;   // [1]  epilogue: h tile
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 19);
 
     const int b = blockIdx.x / a.tiles;
     const int q0 = (blockIdx.x - b * a.tiles) * kRows;
@@ -309,7 +329,7 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
     constexpr uint32_t kOCol = 256;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < 18; ++i)
+        for (int i = 0; i < 19; ++i)
             tc::mbar_init(&bars[i], (i == 13 || i == 14 || i == 15) ? 128 : 1);
         tc::fence_barrier_init();
     }
@@ -492,7 +512,56 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
             named_sync_softmax();
             ok = sFlag[4] != 0;
         }
-        if (ok) {
+        if (ok && a.tma_epi) {
+            // the tile through shared memory: h (C / 32 boxes of 128 rows x
+            // 32 floats, 128-byte swizzle) lands by TMA in the V buffers, which
+            // the finished P V products no longer read; h - O / (den + 1e-9)
+            // in place; one TMA store per box (rows past N are clipped)
+            constexpr uint32_t kBox = kRows * 128;
+            const int nbox = C / 32;
+            if (row == 0) {
+                bool go = true;
+                if (a.h) {
+                    tc::mbar_arrive_expect_tx(h_full, nbox * kBox);
+                    for (int j = 0; j < nbox; ++j)
+                        tma_load_3d(sV + j * kBox, &map_h, h_full, j * 32, q0, b);
+                    go = tc::mbar_wait(h_full, 0, a.err);
+                    if (!go) tc::mbar_drain(h_full, 0);
+                }
+                sFlag[5] = go ? 1 : 0;
+            }
+            named_sync_softmax();
+            const bool go = sFlag[5] != 0;
+            if (go) {
+                tc::tc_fence_after();
+                const float inv = 1.0f / (den + 1e-9f);
+                for (int c0 = 0; c0 < C; c0 += 32) {
+                    float o[32];
+                    tc::tmem_ld32(tmem + lane_base + kOCol + (uint32_t)c0, o);
+                    unsigned char* box = sV + (c0 / 32) * kBox;
+#pragma unroll
+                    for (int ch = 0; ch < 8; ++ch) {
+                        float4* cell = reinterpret_cast<float4*>(box + sw128_offset(row, ch));
+                        const float4 hv = a.h ? *cell : make_float4(0.f, 0.f, 0.f, 0.f);
+                        const float* oc = o + ch * 4;
+                        float4 r = a.h ? make_float4(hv.x - oc[0] * inv, hv.y - oc[1] * inv,
+                                                     hv.z - oc[2] * inv, hv.w - oc[3] * inv)
+                                       : make_float4(oc[0] * inv, oc[1] * inv, oc[2] * inv,
+                                                     oc[3] * inv);
+                        if (a.round_tf32)
+                            r = make_float4(f2s_round_tf32(r.x), f2s_round_tf32(r.y),
+                                            f2s_round_tf32(r.z), f2s_round_tf32(r.w));
+                        *cell = r;
+                    }
+                }
+                fence_proxy_async();
+            }
+            named_sync_softmax();
+            if (row == 0 && go) {
+                for (int j = 0; j < nbox; ++j) tma_store_3d(&map_out, sV + j * kBox, j * 32, q0, b);
+                bulk_commit_and_wait_read();
+            }
+        } else if (ok) {
             tc::tc_fence_after();
             const float inv = 1.0f / (den + 1e-9f);
             const int qrow = q0 + row;
@@ -590,6 +659,18 @@ int attention_tc(const float* q, const float* k, int ldqk, const float* v, int l
     a.round_tf32 = round_tf32 ? 1 : 0;
     a.vec4 = ldo % 4 == 0 && ((uintptr_t)out & 15) == 0 &&
              (!h || (ldh % 4 == 0 && ((uintptr_t)h & 15) == 0));
+    a.tma_epi = a.vec4;
+    CUtensorMap map_h, map_out;
+    if (a.tma_epi) {
+        F2S_TRY(make_tensor_map_3d(&map_out, out, true, C, N, B, (int64_t)ldo * 4,
+                                   (int64_t)ldo * 4 * N, 32, kRows));
+        if (h) F2S_TRY(make_tensor_map_3d(&map_h, h, true, C, N, B, (int64_t)ldh * 4,
+                                          (int64_t)ldh * 4 * N, 32, kRows));
+        else map_h = map_out;
+    } else {
+        map_out = map_vt;
+        map_h = map_vt;
+    }
     a.err = err;
     {
         TraceScope trace(kTagAttnColstats, st);
@@ -608,12 +689,12 @@ int attention_tc(const float* q, const float* k, int ldqk, const float* v, int l
         a.idesc_pv = tc::make_idesc(kRows, C, 2u);
         const size_t smem = 1024 + 2 * kRows * 128 + 2 * kKStages * kKeyTile * 128 + 4 * (size_t)C * 128 +
                             2 * kRows * 128 + (size_t)ceil_div(N, kKeyTile) * kKeyTile * 4 + 32 +
-                            8 + 18 * 8 + 16;
+                            8 + 19 * 8 + 16;
         F2S_LIMIT(smem <= 227 * 1024, "attention_tc: %zu bytes of shared memory", smem);
         F2S_CUDA_TRY(cudaFuncSetAttribute(attn_tc_output_kernel,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        attn_tc_output_kernel<<<B * a.tiles, kThreads, smem, st>>>(map_hi_q, map_lo_q, map_hi_k,
-                                                                   map_lo_k, map_vt, a);
+        attn_tc_output_kernel<<<B * a.tiles, kThreads, smem, st>>>(
+            map_hi_q, map_lo_q, map_hi_k, map_lo_k, map_vt, map_h, map_out, a);
         F2S_TRY(check_launch("attn_tc_output_kernel"));
     }
     return F2S_OK;
