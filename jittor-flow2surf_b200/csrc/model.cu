@@ -363,7 +363,7 @@ int linear_op(const GemmArgs& g, int precision, cudaStream_t st, float* split_a 
         op.rows = g.rows;
         op.cols = g.cols;
         op.K = g.K;
-        op.bn = tc_pick_bn(g.cols, false);
+        op.bn = tc_pick_bn(g.cols, true);  // N tile <= 128: two stages of four operand tiles fit
         op.tf32 = true;
         op.epilogue = kEpiStore;
         op.tag = g.tag;

@@ -52,11 +52,56 @@ struct TcGemmArgs {
     int gate_stride;
     int rows_per_patch;
     int round_tf32;
+    int tma_epi;        // fp32 output written by TMA store / reduce-add boxes
     int* err;
 };
 
-__device__ __forceinline__ float epi_value(float v, const float* bias, int col) {
-    return bias ? v + bias[col] : v;
+constexpr uint32_t kEpiBox = 32 * 128;  // one 32-row x 32-column fp32 box, 128-byte swizzle
+
+__device__ __forceinline__ uint32_t sw128_offset(int row, int chunk) {
+    return (uint32_t)((row >> 3) * 1024 + (row & 7) * 128 + ((chunk ^ (row & 7)) << 4));
+}
+
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int c0, int c1) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(tc::smem_u32(src)), "r"(c0), "r"(c1)
+                 : "memory");
+}
+
+// global += box, element by element in L2 (each element once: deterministic)
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, const void* src, int c0,
+                                                  int c1) {
+    asm volatile(
+        "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+            reinterpret_cast<uint64_t>(map)),
+        "r"(tc::smem_u32(src)), "r"(c0), "r"(c1)
+        : "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_shared() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+
+template <int kPending>
+__device__ __forceinline__ void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(kPending) : "memory");
+}
+
+// 32 consecutive values of a per-column vector from `col0` (zeros past `cols`;
+// cols is a multiple of 4 on the TMA path).
+__device__ __forceinline__ void load_cols32(const float* v, int col0, int cols, float (&out)[32]) {
+#pragma unroll
+    for (int i = 0; i < 32; i += 4) {
+        const float4 x = v && col0 + i < cols ? __ldg(reinterpret_cast<const float4*>(v + col0 + i))
+                                              : make_float4(0.f, 0.f, 0.f, 0.f);
+        out[i] = x.x;
+        out[i + 1] = x.y;
+        out[i + 2] = x.z;
+        out[i + 3] = x.w;
+    }
 }
 
 // kSplit (with kTf32): map_a2 / map_b2 hold the low parts of A / W.
@@ -64,7 +109,7 @@ template <bool kTf32, int kEpi, bool kSplit>
 __global__ void __launch_bounds__(kThreads, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_a2,
                const __grid_constant__ CUtensorMap map_b, const __grid_constant__ CUtensorMap map_b2,
-               const TcGemmArgs g) {
+               const __grid_constant__ CUtensorMap map_y, const TcGemmArgs g) {
     constexpr bool kDual = kEpi == kEpiSwiGlu;
     static_assert(!(kSplit && (kDual || !kTf32)), "3xTF32 runs the single-matrix tf32 form");
     extern __shared__ __align__(1024) unsigned char tc_smem_raw[];
@@ -215,10 +260,14 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         const int quarter = warp & 3;
         const int ew = warp - 2;
         const int chunk_half = ew >> 2;
-        float* stage_buf = reinterpret_cast<float*>(smem + (size_t)S * stage_bytes + 256) +
-                           ew * (kDual ? 2 : 1) * 32 * 33;
+        unsigned char* epi_smem = smem + (size_t)S * stage_bytes + 1024;  // 1024-byte aligned
+        // TMA path: two swizzled 32 x 32 boxes per warp, alternating
+        unsigned char* boxes = epi_smem + (size_t)ew * 2 * kEpiBox;
+        // transposing path: 32 x 33 staging buffers (two for SwiGLU)
+        float* stage_buf = reinterpret_cast<float*>(epi_smem) + ew * (kDual ? 2 : 1) * 32 * 33;
         float* stage_buf2 = stage_buf + 32 * 33;  // SwiGLU value accumulator
         int iter = 0;
+        int boxes_sent = 0;
         for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++iter) {
             const int buf = iter & 1;
             const uint32_t tph = (uint32_t)(iter >> 1) & 1u;
@@ -233,6 +282,55 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             const int row0 = m0 + quarter * 32;  // first of this warp's 32 rows
             const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) +
                                    (uint32_t)(buf * g.acc_cols);
+            if (g.tma_epi) {
+                // thread = row: the epilogue in registers, one swizzled box per
+                // 32 columns, written to global memory by one TMA store (or
+                // reduce-add for the residual, so y is never read here)
+                const int row = min(row0 + lane, g.rows - 1);
+                for (int c0 = chunk_half * 32; c0 < g.bn; c0 += 64) {
+                    const int col0 = n0 + c0;
+                    float v[32];
+                    tc::tmem_ld32(t_row + (uint32_t)c0, v);
+                    if (col0 >= g.cols) continue;  // warp-uniform
+                    float b[32];
+                    load_cols32(g.bias, col0, g.cols, b);
+                    if constexpr (kDual) {
+                        float u[32], b2[32];
+                        tc::tmem_ld32(t_row + (uint32_t)(g.bn + c0), u);
+                        load_cols32(g.bias2, col0, g.cols, b2);
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) v[i] = f2s_silu_approx(v[i] + b[i]) * (u[i] + b2[i]);
+                    } else if constexpr (kEpi == kEpiGatedResidual) {
+                        float gt[32];
+                        load_cols32(g.gate + (size_t)(row / g.rows_per_patch) * g.gate_stride, col0,
+                                    g.cols, gt);
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) v[i] = gt[i] * (v[i] + b[i]);
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) {
+                            v[i] += b[i];
+                            if (g.round_tf32) v[i] = f2s_round_tf32(v[i]);
+                        }
+                    }
+                    unsigned char* box = boxes + (boxes_sent & 1) * kEpiBox;
+                    // the box's previous store must have read it
+                    if (lane == 0 && boxes_sent >= 2) bulk_wait_read<1>();
+                    __syncwarp();
+#pragma unroll
+                    for (int ch = 0; ch < 8; ++ch)
+                        *reinterpret_cast<float4*>(box + sw128_offset(lane, ch)) =
+                            make_float4(v[4 * ch], v[4 * ch + 1], v[4 * ch + 2], v[4 * ch + 3]);
+                    fence_proxy_async_shared();
+                    __syncwarp();
+                    if (lane == 0) {
+                        if constexpr (kEpi == kEpiGatedResidual) tma_reduce_add_2d(&map_y, box, col0, row0);
+                        else tma_store_2d(&map_y, box, col0, row0);
+                        bulk_commit();
+                    }
+                    ++boxes_sent;
+                }
+            } else {
             for (int c0 = chunk_half * 32; c0 < g.bn; c0 += 64) {
                 // thread = row in TMEM; through the staging buffer, lane = column
                 // for coalesced global access and one bias / gate load per lane
@@ -298,9 +396,13 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                 }
                 __syncwarp();
             }
+            }
             tc::tc_fence_before();
             tc::mbar_arrive(&tempty[buf]);
         }
+        // every box store has read its shared memory before the CTA exits
+        if (lane == 0) bulk_wait_read<0>();
+        __syncwarp();
     }
 
     tc::tc_fence_before();
@@ -332,10 +434,11 @@ EncodeTiledFn encode_fn() {
 
 template <bool kTf32, int kEpi, bool kSplit = false>
 int launch_tc(const CUtensorMap& ma, const CUtensorMap& ma2, const CUtensorMap& mb,
-              const CUtensorMap& mb2, const TcGemmArgs& g, size_t smem, int grid, cudaStream_t st) {
+              const CUtensorMap& mb2, const CUtensorMap& my, const TcGemmArgs& g, size_t smem,
+              int grid, cudaStream_t st) {
     auto kernel = tc_gemm_kernel<kTf32, kEpi, kSplit>;
     F2S_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    kernel<<<grid, kThreads, smem, st>>>(ma, ma2, mb, mb2, g);
+    kernel<<<grid, kThreads, smem, st>>>(ma, ma2, mb, mb2, my, g);
     return check_launch("tc_gemm_kernel");
 }
 
@@ -441,31 +544,44 @@ int tc_gemm(const TcGemmOp& op, cudaStream_t st) {
     g.rows_per_patch = op.rows_per_patch > 0 ? op.rows_per_patch : 1;
     g.round_tf32 = op.round_tf32 ? 1 : 0;
     g.err = err;
+    // fp32 output with 16-byte rows, columns and per-column vectors: the
+    // epilogue writes 32 x 32 boxes by TMA (store, or reduce-add for the residual)
+    auto aligned16 = [](const void* p) { return ((uintptr_t)p & 15) == 0; };
+    g.tma_epi = !op.y_bf16 && op.ldy % 4 == 0 && op.cols % 4 == 0 && aligned16(op.Y) &&
+                aligned16(op.bias) && aligned16(op.bias2) &&
+                (op.epilogue != kEpiGatedResidual || (aligned16(op.gate) && op.gate_stride % 4 == 0));
+    CUtensorMap my;
+    if (g.tma_epi) F2S_TRY(make_tensor_map_2d(&my, op.Y, true, op.rows, op.cols, op.ldy, 32, 32));
+    else my = ma;
     const size_t stage_bytes =
         (size_t)kTileM * 128 * (split ? 2 : 1) + (size_t)bn * 128 * ((dual || split) ? 2 : 1);
-    const size_t stage_buf_bytes = (size_t)(kEpilogueThreads / 32) * (dual ? 2 : 1) * 32 * 33 * sizeof(float);
-    int stages = (int)((kSmemLimit - 1024 - 256 - stage_buf_bytes) / stage_bytes);
+    // epilogue region: the transposing path's 32 x 33 buffers or the TMA
+    // path's two 4 KB boxes per warp, whichever is larger
+    size_t stage_buf_bytes = (size_t)(kEpilogueThreads / 32) * (dual ? 2 : 1) * 32 * 33 * sizeof(float);
+    const size_t box_bytes = (size_t)(kEpilogueThreads / 32) * 2 * kEpiBox;
+    stage_buf_bytes = stage_buf_bytes > box_bytes ? stage_buf_bytes : box_bytes;
+    int stages = (int)((kSmemLimit - 1024 - 1024 - stage_buf_bytes) / stage_bytes);
     stages = stages > 8 ? 8 : stages;
     F2S_LIMIT(stages >= 2, "tc_gemm: tile too large for shared memory");
     g.stages = stages;
-    // tiles, then barriers + TMEM slot (< 256 bytes for <= 8 stages), then the
-    // eight epilogue warps' 32 x 33 staging buffers (two each for SwiGLU)
-    const size_t smem = 1024 + stages * stage_bytes + 256 + stage_buf_bytes;
+    // alignment slack, tiles, barriers + TMEM slot (< 1 KB, keeping the
+    // epilogue region 1024-byte aligned for its swizzled boxes), epilogue region
+    const size_t smem = 1024 + stages * stage_bytes + 1024 + stage_buf_bytes;
     const int tiles = ceil_div(op.rows, kTileM) * ceil_div(op.cols, bn);
     const int grid = tiles < sm_count() ? tiles : sm_count();
     TraceScope trace(op.tag, st);
-    if (split) return launch_tc<true, kEpiStore, true>(ma, ma2, mb, mb2, g, smem, grid, st);
+    if (split) return launch_tc<true, kEpiStore, true>(ma, ma2, mb, mb2, my, g, smem, grid, st);
     if (op.tf32) {
         switch (op.epilogue) {
-            case kEpiStore: return launch_tc<true, kEpiStore>(ma, ma2, mb, mb2, g, smem, grid, st);
-            case kEpiGatedResidual: return launch_tc<true, kEpiGatedResidual>(ma, ma2, mb, mb2, g, smem, grid, st);
-            case kEpiSwiGlu: return launch_tc<true, kEpiSwiGlu>(ma, ma2, mb, mb2, g, smem, grid, st);
+            case kEpiStore: return launch_tc<true, kEpiStore>(ma, ma2, mb, mb2, my, g, smem, grid, st);
+            case kEpiGatedResidual: return launch_tc<true, kEpiGatedResidual>(ma, ma2, mb, mb2, my, g, smem, grid, st);
+            case kEpiSwiGlu: return launch_tc<true, kEpiSwiGlu>(ma, ma2, mb, mb2, my, g, smem, grid, st);
         }
     } else {
         switch (op.epilogue) {
-            case kEpiStore: return launch_tc<false, kEpiStore>(ma, ma2, mb, mb2, g, smem, grid, st);
-            case kEpiGatedResidual: return launch_tc<false, kEpiGatedResidual>(ma, ma2, mb, mb2, g, smem, grid, st);
-            case kEpiSwiGlu: return launch_tc<false, kEpiSwiGlu>(ma, ma2, mb, mb2, g, smem, grid, st);
+            case kEpiStore: return launch_tc<false, kEpiStore>(ma, ma2, mb, mb2, my, g, smem, grid, st);
+            case kEpiGatedResidual: return launch_tc<false, kEpiGatedResidual>(ma, ma2, mb, mb2, my, g, smem, grid, st);
+            case kEpiSwiGlu: return launch_tc<false, kEpiSwiGlu>(ma, ma2, mb, mb2, my, g, smem, grid, st);
         }
     }
     return fail(F2S_ERR_INVALID_ARGUMENT, "tc_gemm: bad epilogue");
