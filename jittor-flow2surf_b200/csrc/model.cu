@@ -262,7 +262,8 @@ __global__ void cond_mod_kernel(const CondArgs a, const float* __restrict__ alph
 
 // xyz (B, 3, M) -> point-major xyz4, and the input HPE (encoder.py:40-71,177):
 // Linear(3 -> S0), Jittor LayerNorm (var = max(E[x^2]-E[x]^2, 0), eps 1e-5),
-// erf GELU, Linear(S0 -> S0). One warp per point.
+// erf GELU, Linear(S0 -> S0). One warp per point; persistent CTAs load the
+// output weights into shared memory once and loop over groups of 8 points.
 __global__ void input_embed_kernel(const float* __restrict__ x, int B, int M,
                                    const float* __restrict__ w, const float* __restrict__ bia,
                                    const float* __restrict__ lnw, const float* __restrict__ lnb,
@@ -278,8 +279,7 @@ __global__ void input_embed_kernel(const float* __restrict__ x, int B, int M,
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int R = B * M;
-    const int p = blockIdx.x * 8 + warp;
-    if (p >= R) return;
+    for (int p = blockIdx.x * 8 + warp; p < R; p += gridDim.x * 8) {
     const int b = p / M, m = p - b * M;
     const float* xb = x + (size_t)b * 3 * M;
     const float x0 = xb[m], x1 = xb[M + m], x2 = xb[2 * M + m];
@@ -306,6 +306,8 @@ __global__ void input_embed_kernel(const float* __restrict__ x, int B, int M,
         float v = ob[c];
         for (int hh = 0; hh < S0; ++hh) v = fmaf(owT[hh * S0 + c], hw[hh], v);
         fr[c] = v;
+    }
+    __syncwarp();  // hw is rewritten for the next point
     }
 }
 
@@ -422,7 +424,9 @@ int forward(const Dims& d, const Layout& L, const float* P, const float* x_in, c
         F2S_CUDA_TRY(cudaFuncSetAttribute(input_embed_kernel,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
         TraceScope trace(kTagInputEmbed, st);
-        input_embed_kernel<<<ceil_div(R, 8), 256, smem, st>>>(
+        const int groups = ceil_div(R, 8);
+        const int grid = groups < 4 * sm_count() ? groups : 4 * sm_count();
+        input_embed_kernel<<<grid, 256, smem, st>>>(
             x_in, B, M, P + L.in_w, P + L.in_b, P + L.in_ln_w, P + L.in_ln_b, P + L.in_out_w,
             P + L.in_out_b, S0, w.xyz4, w.feat0);
         F2S_TRY(check_launch("input_embed_kernel"));

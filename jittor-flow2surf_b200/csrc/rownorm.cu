@@ -72,9 +72,10 @@ __global__ void ln_modulate_kernel(const float* __restrict__ x, int ldx, float* 
         for (int i = 0; i < kPairs; ++i) {
             const int c = 2 * (lane + 32 * i);
             if (c < C) {
-                float a = (v[i].x - mean) * rstd * (1.0f + m[scale_off + c]) + m[shift_off + c];
-                float b = (v[i].y - mean) * rstd * (1.0f + m[scale_off + c + 1]) +
-                          m[shift_off + c + 1];
+                const float2 sc = *reinterpret_cast<const float2*>(m + scale_off + c);
+                const float2 sh = *reinterpret_cast<const float2*>(m + shift_off + c);
+                float a = (v[i].x - mean) * rstd * (1.0f + sc.x) + sh.x;
+                float b = (v[i].y - mean) * rstd * (1.0f + sc.y) + sh.y;
                 if (round_tf32) {
                     a = f2s_round_tf32(a);
                     b = f2s_round_tf32(b);
@@ -151,7 +152,9 @@ int ln_modulate(const float* x, int ldx, float* h, int ldh, const float* mod, in
     if (rows == 0) return F2S_OK;
     TraceScope trace(kTagRowNorm, stream);
     const bool paired = C % 2 == 0 && C <= 64 * kPairs && ldx % 2 == 0 && ldh % 2 == 0 &&
-                        ((uintptr_t)x & 7) == 0 && ((uintptr_t)h & 7) == 0;
+                        ((uintptr_t)x & 7) == 0 && ((uintptr_t)h & 7) == 0 &&
+                        ((uintptr_t)mod & 7) == 0 && mod_stride % 2 == 0 && scale_off % 2 == 0 &&
+                        shift_off % 2 == 0;
     auto kernel = paired ? ln_modulate_kernel<true> : ln_modulate_kernel<false>;
     kernel<<<ceil_div(rows, kRowsPerCta), kRowsPerCta * 32, 0, stream>>>(
         x, ldx, h, ldh, mod, mod_stride, scale_off, shift_off, rows, rows_per_patch, C, round_tf32);
