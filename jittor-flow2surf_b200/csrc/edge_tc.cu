@@ -69,8 +69,11 @@ struct EdgeTcArgs {
     float* out;
     int ldo;
     uint32_t idesc;
+    uint32_t idesc_pre;  // tf32, M = 128, N = H: the pre-activation MMA
     int* err;
 };
+
+constexpr uint32_t kUBytes = kRows * 32;  // one 128 x 8 tf32 operand in the interleaved layout
 
 // Byte offset of 16-byte chunk `chunk` of row `row` inside a K-block of
 // 128-byte rows in the 128-byte-swizzle layout (8-row atoms of 1024 bytes).
@@ -95,19 +98,11 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo_elem, float hi_elem) {
     return *reinterpret_cast<const uint32_t*>(&b);
 }
 
-// HPE input projection of one channel: b + W g with the channel's
-// parameters packed {w0..w5, b, 0}; same operation order as edge.cu.
-__device__ __forceinline__ float hpe_pre(const float* prm, const float (&g)[6]) {
-    const float4 w0 = *reinterpret_cast<const float4*>(prm);
-    const float4 w1 = *reinterpret_cast<const float4*>(prm + 4);
-    float v = w1.z;
-    v = fmaf(g[0], w0.x, v);
-    v = fmaf(g[1], w0.y, v);
-    v = fmaf(g[2], w0.z, v);
-    v = fmaf(g[3], w0.w, v);
-    v = fmaf(g[4], w1.x, v);
-    v = fmaf(g[5], w1.y, v);
-    return v;
+// Byte offset of 16-byte chunk `chunk` of row `row` in the interleaved
+// (no-swizzle) K-major layout of 32-byte rows: 8-row core matrices of 128
+// bytes, the two K chunks 128 bytes apart, 8-row groups 256 bytes apart.
+__device__ __forceinline__ uint32_t interleaved_offset(int row, int chunk) {
+    return (uint32_t)((row >> 3) * 256 + chunk * 128 + (row & 7) * 16);
 }
 
 // GELU(x) = x * Phi(x) with Phi from the erf approximation of Abramowitz and
@@ -157,14 +152,15 @@ edge_tc_kernel(const __grid_constant__ CUtensorMap map_w, const EdgeTcArgs a) {
     unsigned char* sA = smem;                               // a_bufs x a_buf_bytes
     unsigned char* sB = sA + (size_t)a.a_bufs * a_buf_bytes;
     unsigned char* sBlo = sB + b_bytes;
-    // per hidden channel c: {w0..w5, b, 0} at hp_off(c), {gain, shift} at
-    // hn_off(c); the upper half of the channels is shifted by 16 / 8 bytes so
-    // the two lanes of a row (one per half) read different banks
-    float* sHp = reinterpret_cast<float*>(sBlo + (kSplit ? b_bytes : 0));
-    float* sHn = sHp + H * 8 + 4;
+    // the pre-activation contraction h = [W_in | b_in] [g ; 1] as a K = 8 tf32
+    // MMA in the interleaved (no-swizzle) K-major layout: A_u = 128 rows of
+    // [g0..g5, 1, 0], B_w = H rows of [w0..w5, b, 0], each as tf32 hi and lo
+    unsigned char* sU = sBlo + (kSplit ? b_bytes : 0);  // 2 x 4 KB
+    unsigned char* sWu = sU + 2 * kUBytes;               // 2 x H x 32 bytes
+    float* sHn = reinterpret_cast<float*>(sWu + 2 * (size_t)H * 32);  // H x {gain, shift}
     // LayerNorm moments of the pre-activations as functions of g:
     // sum = bsum + wsum . g, sum of squares = bsq + g . (2 u + G g)
-    float* sGram = sHn + H * 2 + 4;  // G[36], u[6], wsum[6], bsum, bsq (16-byte aligned)
+    float* sGram = sHn + H * 2;  // G[36], u[6], wsum[6], bsum, bsq (16-byte aligned)
     float* sCb = sGram + 52;                                              // cout
     float* sLn = sCb + cout;      // cout x {|gain|, shift}
     float* sSgn = sLn + cout * 2;  // cout: sign of the gain (+1 / -1)
@@ -176,7 +172,8 @@ edge_tc_kernel(const __grid_constant__ CUtensorMap map_w, const EdgeTcArgs a) {
     uint64_t* t_empty = bars + 6;   // [2]
     uint64_t* w_bar = bars + 8;
     uint64_t* mma_done = bars + 9;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
+    uint64_t* pre_full = bars + 10;  // pre-activation MMA of the tile done
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
     // failure flags of the epilogue and (per tile parity) producer warps:
     // written by the role's one polling lane before the role's named barrier,
     // read by every warp of the role after it
@@ -186,19 +183,31 @@ edge_tc_kernel(const __grid_constant__ CUtensorMap map_w, const EdgeTcArgs a) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int R = a.B * a.M;
     const int n_tiles = (R + a.ppt - 1) / a.ppt;
+    // TMEM: two accumulators (columns [0, 2 C_out)), the pre-activations
+    // (columns [2 C_out, 2 C_out + H))
     uint32_t tmem_cols = 32;
-    while (tmem_cols < (uint32_t)(2 * cout)) tmem_cols <<= 1;
+    while (tmem_cols < (uint32_t)(2 * cout + H)) tmem_cols <<= 1;
+    const uint32_t pre_col = (uint32_t)(2 * cout);
 
     const int hh = H >> 1;
     for (int c = tid; c < H; c += kThreads) {
         const float* w = a.hpe_w + (size_t)c * 6;
-        float* d = sHp + c * 8 + (c >= hh ? 4 : 0);
-        d[0] = w[0]; d[1] = w[1]; d[2] = w[2]; d[3] = w[3]; d[4] = w[4]; d[5] = w[5];
-        d[6] = a.hpe_b[c];
-        d[7] = 0.0f;
-        float* n = sHn + c * 2 + (c >= hh ? 2 : 0);
-        n[0] = a.hpe_ln_w[c];
-        n[1] = a.hpe_ln_b[c];
+        const float row8[8] = {w[0], w[1], w[2], w[3], w[4], w[5], a.hpe_b[c], 0.0f};
+        float hi[8], lo[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            hi[e] = f2s_round_tf32(row8[e]);
+            lo[e] = row8[e] - hi[e];
+        }
+        for (int ch = 0; ch < 2; ++ch) {
+            const uint32_t off = interleaved_offset(c, ch);
+            *reinterpret_cast<float4*>(sWu + off) =
+                make_float4(hi[4 * ch], hi[4 * ch + 1], hi[4 * ch + 2], hi[4 * ch + 3]);
+            *reinterpret_cast<float4*>(sWu + (size_t)H * 32 + off) =
+                make_float4(lo[4 * ch], lo[4 * ch + 1], lo[4 * ch + 2], lo[4 * ch + 3]);
+        }
+        sHn[2 * c] = a.hpe_ln_w[c];
+        sHn[2 * c + 1] = a.hpe_ln_b[c];
     }
     if (tid < 50) {
         // 50 sums over the hidden channels, in double
@@ -228,6 +237,7 @@ edge_tc_kernel(const __grid_constant__ CUtensorMap map_w, const EdgeTcArgs a) {
         }
         tc::mbar_init(w_bar, 1);
         tc::mbar_init(mma_done, 1);
+        tc::mbar_init(pre_full, 1);
         *sEpiFail = 0;
         sProdFail[0] = sProdFail[1] = 0;
         tc::fence_barrier_init();
@@ -252,8 +262,8 @@ edge_tc_kernel(const __grid_constant__ CUtensorMap map_w, const EdgeTcArgs a) {
             *reinterpret_cast<uint4*>(sB + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
             if (kSplit) *reinterpret_cast<uint4*>(sBlo + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
         }
-        fence_proxy_async();
     }
+    fence_proxy_async();  // the split B_w (and bf16 W_po) for the tensor cores
     if (warp == 0) tc::tmem_alloc(tmem_slot, tmem_cols);
     if constexpr (kTf32) {
         if (tid == 0) {
@@ -269,11 +279,12 @@ edge_tc_kernel(const __grid_constant__ CUtensorMap map_w, const EdgeTcArgs a) {
 
     if (warp < kProducerWarps) {
         // ---------------- hidden producers + MMA issue ----------------
-        const int row = (warp << 4) + (lane >> 1);
-        const int half = lane & 1;
+        // thread = edge row (TMEM lane) for one half of the hidden channels
+        const int quarter = warp & 3;
+        const int half = warp >> 2;
+        const int row = quarter * 32 + lane;
         const int ch0 = half * hh;
-        const float* hp = sHp + ch0 * 8 + half * 4;  // this lane's half of the records
-        const float* hn = sHn + ch0 * 2 + half * 2;
+        const uint32_t t_lane = (uint32_t)(quarter * 32) << 16;
         const int pl = row >> a.log2K;
         const int kk = row & (K - 1);
         // geometry of the first tile; later tiles' loads are issued one tile ahead
@@ -293,6 +304,43 @@ edge_tc_kernel(const __grid_constant__ CUtensorMap map_w, const EdgeTcArgs a) {
         for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
             const float g[6] = {xj.x - xi.x, xj.y - xi.y, xj.z - xi.z, xi.x, xi.y, xi.z};
             const bool cur_valid = valid;
+            // u = [g, 1, 0] of this row as tf32 hi / lo (the lanes of one half)
+            if (half == 0) {
+                const float u8[8] = {g[0], g[1], g[2], g[3], g[4], g[5], 1.0f, 0.0f};
+                float hi[8], lo[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    hi[e] = f2s_round_tf32(u8[e]);
+                    lo[e] = u8[e] - hi[e];
+                }
+#pragma unroll
+                for (int ch = 0; ch < 2; ++ch) {
+                    const uint32_t off = interleaved_offset(row, ch);
+                    *reinterpret_cast<float4*>(sU + off) =
+                        make_float4(hi[4 * ch], hi[4 * ch + 1], hi[4 * ch + 2], hi[4 * ch + 3]);
+                    *reinterpret_cast<float4*>(sU + kUBytes + off) =
+                        make_float4(lo[4 * ch], lo[4 * ch + 1], lo[4 * ch + 2], lo[4 * ch + 3]);
+                }
+                fence_proxy_async();
+            }
+            // the previous tile's pre-activations have been read (tcgen05.ld
+            // waited) by every producer thread before this barrier
+            tc::tc_fence_before();
+            prod_barrier();
+            if (tid == 0) {
+                // pre = [W_in | b_in] [g ; 1] in 3xTF32: hi hi + hi lo + lo hi
+                tc::tc_fence_after();
+                const uint32_t u0 = tc::smem_u32(sU), w0 = tc::smem_u32(sWu);
+                const uint64_t du = tc::interleaved_desc(u0, 128, 256);
+                const uint64_t du_lo = tc::interleaved_desc(u0 + kUBytes, 128, 256);
+                const uint64_t dw = tc::interleaved_desc(w0, 128, 256);
+                const uint64_t dw_lo = tc::interleaved_desc(w0 + (uint32_t)H * 32, 128, 256);
+                const uint32_t dpre = tmem_base + pre_col;
+                tc::umma<true>(dpre, du, dw, a.idesc_pre, 0u);
+                tc::umma<true>(dpre, du, dw_lo, a.idesc_pre, 1u);
+                tc::umma<true>(dpre, du_lo, dw, a.idesc_pre, 1u);
+                tc::umma_commit(pre_full);
+            }
             // next tile: neighbour index and centre point now, the neighbour
             // point after the wait below
             const int np = (tile + gridDim.x) * a.ppt + pl;
@@ -316,44 +364,54 @@ edge_tc_kernel(const __grid_constant__ CUtensorMap map_w, const EdgeTcArgs a) {
             const float mean = s / (float)H;
             const float var = fmaxf(s2 / (float)H - mean * mean, 0.0f);
             const float rstd = rsqrtf(var + 1e-5f);
-            // wait until the MMAs of the tile that last used this buffer are done
+            // wait until the MMAs of the tile that last used this A buffer are
+            // done and this tile's pre-activations are in TMEM; one lane polls,
+            // the other producer warps wait on the named barrier
             const int abuf = a.a_bufs == 2 ? (it & 1) : 0;
             const uint32_t round = a.a_bufs == 2 ? (uint32_t)(it >> 1) : (uint32_t)it;
-            // one lane polls, the other producer warps wait on the named barrier
             volatile int* fail = sProdFail + (it & 1);
-            if (tid == 0 && !tc::mbar_wait(&a_empty[abuf], (round & 1u) ^ 1u, a.err)) *fail = 1;
+            if (tid == 0 && !(tc::mbar_wait(&a_empty[abuf], (round & 1u) ^ 1u, a.err) &&
+                              tc::mbar_wait(pre_full, (uint32_t)it & 1u, a.err)))
+                *fail = 1;
             prod_barrier();
             if (*fail) break;
+            tc::tc_fence_after();
             if (valid) xj = *reinterpret_cast<const float4*>(
                            a.xyz4 + (size_t)((np / a.M) * a.M + nidx) * 4);
             unsigned char* dA = sA + (size_t)abuf * a_buf_bytes;
-            // pre-activation, GELU(LN), packed as the MMA reads it
-            for (int i0 = 0; i0 < hh; i0 += kPer) {
-                float o[kPer];
+            // GELU(LN(pre)), packed as the main MMA reads it
+            for (int c0 = 0; c0 < hh; c0 += 32) {
+                float v[32];
+                tc::tmem_ld32(tmem_base + t_lane + pre_col + (uint32_t)(ch0 + c0), v);
 #pragma unroll
-                for (int e = 0; e < kPer; ++e) {
-                    const float v = hpe_pre(hp + (i0 + e) * 8, g);
-                    const float2 gs = *reinterpret_cast<const float2*>(hn + 2 * (i0 + e));
-                    o[e] = cur_valid ? gelu_as((v - mean) * rstd * gs.x + gs.y) : 0.0f;
-                }
-                const int c = ch0 + i0;
-                unsigned char* dst =
-                    dA + (size_t)(c / kBk) * kRows * 128 + sw128_offset(row, (c % kBk) / kPer);
-                if constexpr (kTf32) {
-                    *reinterpret_cast<float4*>(dst) = make_float4(o[0], o[1], o[2], o[3]);
-                } else {
-                    uint32_t hi[4], lo[4];
+                for (int i0 = 0; i0 < 32; i0 += kPer) {
+                    float o[kPer];
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const __nv_bfloat162 h2 = __floats2bfloat162_rn(o[2 * e], o[2 * e + 1]);
-                        hi[e] = *reinterpret_cast<const uint32_t*>(&h2);
-                        if (kSplit)
-                            lo[e] = pack_bf16(o[2 * e] - __bfloat162float(h2.x),
-                                              o[2 * e + 1] - __bfloat162float(h2.y));
+                    for (int e = 0; e < kPer; e += 2) {
+                        const float4 gs = *reinterpret_cast<const float4*>(sHn + 2 * (ch0 + c0 + i0 + e));
+                        o[e] = cur_valid ? gelu_as((v[i0 + e] - mean) * rstd * gs.x + gs.y) : 0.0f;
+                        o[e + 1] = cur_valid ? gelu_as((v[i0 + e + 1] - mean) * rstd * gs.z + gs.w) : 0.0f;
                     }
-                    *reinterpret_cast<uint4*>(dst) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-                    if (kSplit)
-                        *reinterpret_cast<uint4*>(dst + a_bytes) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                    const int c = ch0 + c0 + i0;
+                    unsigned char* dst =
+                        dA + (size_t)(c / kBk) * kRows * 128 + sw128_offset(row, (c % kBk) / kPer);
+                    if constexpr (kTf32) {
+                        *reinterpret_cast<float4*>(dst) = make_float4(o[0], o[1], o[2], o[3]);
+                    } else {
+                        uint32_t hi[4], lo[4];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const __nv_bfloat162 h2 = __floats2bfloat162_rn(o[2 * e], o[2 * e + 1]);
+                            hi[e] = *reinterpret_cast<const uint32_t*>(&h2);
+                            if (kSplit)
+                                lo[e] = pack_bf16(o[2 * e] - __bfloat162float(h2.x),
+                                                  o[2 * e + 1] - __bfloat162float(h2.y));
+                        }
+                        *reinterpret_cast<uint4*>(dst) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                        if (kSplit)
+                            *reinterpret_cast<uint4*>(dst + a_bytes) =
+                                make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                    }
                 }
             }
             fence_proxy_async();
@@ -541,8 +599,9 @@ size_t edge_tc_smem(int mode, int H, int cout, int bufs) {
     const int elem = mode == kModeTf32 ? 4 : 2;
     const size_t kblocks = (size_t)ceil_div(H, 128 / elem);
     const size_t copies = mode == kModeSplit ? 2 : 1;
-    return 1024 + copies * kblocks * 128 * ((size_t)bufs * kRows + cout) +
-           sizeof(float) * ((size_t)H * 10 + 60 + (size_t)cout * 4 + 4 * kRows) + 128;
+    return 1024 + copies * kblocks * 128 * ((size_t)bufs * kRows + cout) + 2 * (size_t)kUBytes +
+           2 * (size_t)H * 32 + sizeof(float) * ((size_t)H * 2 + 52 + (size_t)cout * 4 + 4 * kRows) +
+           128;
 }
 
 }  // namespace
@@ -554,8 +613,10 @@ int edge_stage_tc(const EdgeArgs& e, int precision, cudaStream_t st) {
     if (e.B == 0 || e.M == 0) return F2S_OK;
     int log2K = 0;
     while ((1 << log2K) < e.K) ++log2K;
-    if (e.geometry != nullptr || e.xyz4 == nullptr || e.D != 6 || e.H > 128 ||
-        e.H % 32 != 0 || e.cout % 32 != 0 || e.cout > 256 || (1 << log2K) != e.K || e.K > 32 ||
+    // H: a multiple of 64 (each producer half reads 32-column TMEM chunks);
+    // TMEM holds two C_out accumulators and the H pre-activations
+    if (e.geometry != nullptr || e.xyz4 == nullptr || e.D != 6 || e.H > 128 || e.H % 64 != 0 ||
+        e.cout % 32 != 0 || e.cout > 256 || 2 * e.cout + e.H > 512 || (1 << log2K) != e.K || e.K > 32 ||
         ((uintptr_t)e.content & 15) != 0 || e.ldc % 4 != 0 || ((uintptr_t)e.contrib_w & 15) != 0)
         return fail(F2S_ERR_UNSUPPORTED, "edge stage shape outside the tensor-core kernel");
     F2S_REQUIRE(precision == F2S_PRECISION_TF32 || precision == F2S_PRECISION_BF16 ||
@@ -603,6 +664,7 @@ int edge_stage_tc(const EdgeArgs& e, int precision, cudaStream_t st) {
     a.out = e.out;
     a.ldo = e.ldo;
     a.idesc = tc::make_idesc(kRows, e.cout, tf32 ? 2u : 1u);
+    a.idesc_pre = tc::make_idesc(kRows, e.H, 2u);
     a.err = err;
     const int R = e.B * e.M;
     const int tiles = ceil_div(R, a.ppt);

@@ -197,6 +197,19 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
     return d;
 }
 
+// Shared-memory matrix descriptor of a K-major tile in the interleaved
+// (no-swizzle) layout: 8-row x 16-byte core matrices stored contiguously,
+// `lbo` bytes between the core matrices of one row group along K, `sbo` bytes
+// between 8-row groups.
+__device__ __forceinline__ uint64_t interleaved_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t)1u << 46;  // descriptor version (sm_100); layout type 0 = no swizzle
+    return d;
+}
+
 // Instruction descriptor: fp32 accumulate, A/B format (1 = bf16, 2 = tf32),
 // both K-major, M x N.
 __host__ __device__ constexpr uint32_t make_idesc(int M, int N, uint32_t ab_format) {
