@@ -554,6 +554,19 @@ edge_tc_kernel(const __grid_constant__ CUtensorMap map_w, const EdgeTcArgs a) {
                     for (int i = 0; i < 32; ++i) y[i] = -FLT_MAX;
                 }
                 int off = 0;
+                if (K == 32) {
+                    // one point per warp: a warp-wide max per channel, lane c
+                    // keeps channel c
+                    float mine = 0.0f;
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        float r;
+                        asm("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(y[i]));
+                        mine = lane == i ? r : mine;
+                    }
+                    y[0] = mine;
+                    off = lane;
+                } else
 #pragma unroll
                 for (int s = 0; s < 5; ++s) {
                     if (s < a.log2K) {
