@@ -57,33 +57,47 @@ __global__ void ln_modulate_kernel(const float* __restrict__ x, int ldx, float* 
                                    int ldh, const float* __restrict__ mod, int mod_stride,
                                    int scale_off, int shift_off, int rows, int rows_per_patch,
                                    int C, bool round_tf32) {
-    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
-    if (row >= rows) return;
-    const float* xr = x + (size_t)row * ldx;
-    const float* m = mod + (size_t)(row / rows_per_patch) * mod_stride;
-    float* hr = h + (size_t)row * ldh;
-    float mean, rstd;
     if constexpr (kPaired) {
-        float2 v[kPairs];
-        row_load(xr, C, lane, v);
-        row_stats_reg(v, C, lane, mean, rstd);
+        // two rows per warp, both loaded before either is reduced
+        const int row0 = (blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * 2;
+        if (row0 >= rows) return;
+        float2 v[2][kPairs];
 #pragma unroll
-        for (int i = 0; i < kPairs; ++i) {
-            const int c = 2 * (lane + 32 * i);
-            if (c < C) {
-                const float2 sc = *reinterpret_cast<const float2*>(m + scale_off + c);
-                const float2 sh = *reinterpret_cast<const float2*>(m + shift_off + c);
-                float a = (v[i].x - mean) * rstd * (1.0f + sc.x) + sh.x;
-                float b = (v[i].y - mean) * rstd * (1.0f + sc.y) + sh.y;
-                if (round_tf32) {
-                    a = f2s_round_tf32(a);
-                    b = f2s_round_tf32(b);
+        for (int q = 0; q < 2; ++q) {
+            if (row0 + q < rows) row_load(x + (size_t)(row0 + q) * ldx, C, lane, v[q]);
+        }
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+            const int row = row0 + q;
+            if (row >= rows) break;
+            float mean, rstd;
+            row_stats_reg(v[q], C, lane, mean, rstd);
+            const float* m = mod + (size_t)(row / rows_per_patch) * mod_stride;
+            float* hr = h + (size_t)row * ldh;
+#pragma unroll
+            for (int i = 0; i < kPairs; ++i) {
+                const int c = 2 * (lane + 32 * i);
+                if (c < C) {
+                    const float2 sc = *reinterpret_cast<const float2*>(m + scale_off + c);
+                    const float2 sh = *reinterpret_cast<const float2*>(m + shift_off + c);
+                    float a = (v[q][i].x - mean) * rstd * (1.0f + sc.x) + sh.x;
+                    float b = (v[q][i].y - mean) * rstd * (1.0f + sc.y) + sh.y;
+                    if (round_tf32) {
+                        a = f2s_round_tf32(a);
+                        b = f2s_round_tf32(b);
+                    }
+                    *reinterpret_cast<float2*>(hr + c) = make_float2(a, b);
                 }
-                *reinterpret_cast<float2*>(hr + c) = make_float2(a, b);
             }
         }
     } else {
+        const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+        if (row >= rows) return;
+        const float* xr = x + (size_t)row * ldx;
+        const float* m = mod + (size_t)(row / rows_per_patch) * mod_stride;
+        float* hr = h + (size_t)row * ldh;
+        float mean, rstd;
         row_stats(xr, C, lane, mean, rstd);
         for (int c = lane; c < C; c += 32) {
             const float v = (xr[c] - mean) * rstd * (1.0f + m[scale_off + c]) + m[shift_off + c];
@@ -156,7 +170,8 @@ int ln_modulate(const float* x, int ldx, float* h, int ldh, const float* mod, in
                         ((uintptr_t)mod & 7) == 0 && mod_stride % 2 == 0 && scale_off % 2 == 0 &&
                         shift_off % 2 == 0;
     auto kernel = paired ? ln_modulate_kernel<true> : ln_modulate_kernel<false>;
-    kernel<<<ceil_div(rows, kRowsPerCta), kRowsPerCta * 32, 0, stream>>>(
+    const int rows_per_cta = paired ? 2 * kRowsPerCta : kRowsPerCta;
+    kernel<<<ceil_div(rows, rows_per_cta), kRowsPerCta * 32, 0, stream>>>(
         x, ldx, h, ldh, mod, mod_stride, scale_off, shift_off, rows, rows_per_patch, C, round_tf32);
     return check_launch("ln_modulate_kernel");
 }
