@@ -299,52 +299,58 @@ edge_tc_kernel(const __grid_constant__ CUtensorMap map_w, const EdgeTcArgs a) {
                 xj = *reinterpret_cast<const float4*>(a.xyz4 + (size_t)jrow * 4);
             }
         }
+        // u = [g, 1, 0] of this row as tf32 hi / lo (the lanes of one half)
+        auto write_u = [&](const float4& pi, const float4& pj) {
+            const float u8[8] = {pj.x - pi.x, pj.y - pi.y, pj.z - pi.z, pi.x, pi.y, pi.z, 1.0f, 0.0f};
+            float hi[8], lo[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                hi[e] = f2s_round_tf32(u8[e]);
+                lo[e] = u8[e] - hi[e];
+            }
+#pragma unroll
+            for (int ch = 0; ch < 2; ++ch) {
+                const uint32_t off = interleaved_offset(row, ch);
+                *reinterpret_cast<float4*>(sU + off) =
+                    make_float4(hi[4 * ch], hi[4 * ch + 1], hi[4 * ch + 2], hi[4 * ch + 3]);
+                *reinterpret_cast<float4*>(sU + kUBytes + off) =
+                    make_float4(lo[4 * ch], lo[4 * ch + 1], lo[4 * ch + 2], lo[4 * ch + 3]);
+            }
+        };
+        // pre = [W_in | b_in] [g ; 1] in 3xTF32 (hi hi + hi lo + lo hi) into TMEM
+        auto issue_pre = [&]() {
+            const uint32_t u0 = tc::smem_u32(sU), w0 = tc::smem_u32(sWu);
+            const uint64_t du = tc::interleaved_desc(u0, 128, 256);
+            const uint64_t du_lo = tc::interleaved_desc(u0 + kUBytes, 128, 256);
+            const uint64_t dw = tc::interleaved_desc(w0, 128, 256);
+            const uint64_t dw_lo = tc::interleaved_desc(w0 + (uint32_t)H * 32, 128, 256);
+            const uint32_t dpre = tmem_base + pre_col;
+            tc::umma<true>(dpre, du, dw, a.idesc_pre, 0u);
+            tc::umma<true>(dpre, du, dw_lo, a.idesc_pre, 1u);
+            tc::umma<true>(dpre, du_lo, dw, a.idesc_pre, 1u);
+            tc::umma_commit(pre_full);
+        };
+        // the first tile's pre-activations; later tiles' are issued with the
+        // previous tile's main MMAs
+        if (half == 0) {
+            write_u(xi, xj);
+            fence_proxy_async();
+        }
+        prod_barrier();
+        if (tid == 0 && blockIdx.x < n_tiles) {
+            tc::tc_fence_after();
+            issue_pre();
+        }
         bool weights_ready = !kTf32;
         int it = 0;
         for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
             const float g[6] = {xj.x - xi.x, xj.y - xi.y, xj.z - xi.z, xi.x, xi.y, xi.z};
             const bool cur_valid = valid;
-            // u = [g, 1, 0] of this row as tf32 hi / lo (the lanes of one half)
-            if (half == 0) {
-                const float u8[8] = {g[0], g[1], g[2], g[3], g[4], g[5], 1.0f, 0.0f};
-                float hi[8], lo[8];
-#pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    hi[e] = f2s_round_tf32(u8[e]);
-                    lo[e] = u8[e] - hi[e];
-                }
-#pragma unroll
-                for (int ch = 0; ch < 2; ++ch) {
-                    const uint32_t off = interleaved_offset(row, ch);
-                    *reinterpret_cast<float4*>(sU + off) =
-                        make_float4(hi[4 * ch], hi[4 * ch + 1], hi[4 * ch + 2], hi[4 * ch + 3]);
-                    *reinterpret_cast<float4*>(sU + kUBytes + off) =
-                        make_float4(lo[4 * ch], lo[4 * ch + 1], lo[4 * ch + 2], lo[4 * ch + 3]);
-                }
-                fence_proxy_async();
-            }
-            // the previous tile's pre-activations have been read (tcgen05.ld
-            // waited) by every producer thread before this barrier
-            tc::tc_fence_before();
-            prod_barrier();
-            if (tid == 0) {
-                // pre = [W_in | b_in] [g ; 1] in 3xTF32: hi hi + hi lo + lo hi
-                tc::tc_fence_after();
-                const uint32_t u0 = tc::smem_u32(sU), w0 = tc::smem_u32(sWu);
-                const uint64_t du = tc::interleaved_desc(u0, 128, 256);
-                const uint64_t du_lo = tc::interleaved_desc(u0 + kUBytes, 128, 256);
-                const uint64_t dw = tc::interleaved_desc(w0, 128, 256);
-                const uint64_t dw_lo = tc::interleaved_desc(w0 + (uint32_t)H * 32, 128, 256);
-                const uint32_t dpre = tmem_base + pre_col;
-                tc::umma<true>(dpre, du, dw, a.idesc_pre, 0u);
-                tc::umma<true>(dpre, du, dw_lo, a.idesc_pre, 1u);
-                tc::umma<true>(dpre, du_lo, dw, a.idesc_pre, 1u);
-                tc::umma_commit(pre_full);
-            }
+            const bool has_next = tile + (int)gridDim.x < n_tiles;
             // next tile: neighbour index and centre point now, the neighbour
             // point after the wait below
             const int np = (tile + gridDim.x) * a.ppt + pl;
-            valid = tile + (int)gridDim.x < n_tiles && np < R;
+            valid = has_next && np < R;
             int nidx = 0;
             if (valid) {
                 nidx = a.idx[(size_t)np * K + kk];
@@ -414,8 +420,11 @@ edge_tc_kernel(const __grid_constant__ CUtensorMap map_w, const EdgeTcArgs a) {
                     }
                 }
             }
+            // the next tile's u rows (its geometry has landed by now)
+            if (half == 0 && has_next) write_u(xi, xj);
             fence_proxy_async();
-            prod_barrier();  // the whole A tile is written
+            tc::tc_fence_before();  // this tile's pre-activations have been read
+            prod_barrier();  // the whole A tile (and the next u) is written
             if (tid == 0) {
                 // issue the tile's MMAs once its accumulator buffer is free; a
                 // failure stops the producers at the next tile's decision
@@ -450,6 +459,7 @@ edge_tc_kernel(const __grid_constant__ CUtensorMap map_w, const EdgeTcArgs a) {
                         }
                     tc::umma_commit(&a_empty[abuf]);
                     tc::umma_commit(&t_full[tbuf]);
+                    if (has_next) issue_pre();
                 } else {
                     reinterpret_cast<volatile int*>(sProdFail)[(it + 1) & 1] = 1;
                 }
