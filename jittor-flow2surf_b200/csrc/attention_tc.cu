@@ -45,7 +45,7 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
         : "memory");
 }
 
-// 3-D TMA tile store from shared memory (bulk group; no multicast).
+// 3-D TMA tile store from shared memory (bulk group, this CTA only).
 __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int c0, int c1,
                                              int c2) {
     asm volatile(

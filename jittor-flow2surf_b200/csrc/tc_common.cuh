@@ -82,7 +82,7 @@ __device__ __forceinline__ bool mbar_drain(uint64_t* bar, uint32_t parity) {
     return false;
 }
 
-// 2-D TMA tile load into shared memory, completing on `bar` (no multicast).
+// 2-D TMA tile load into this CTA's shared memory, completing on `bar`.
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar,
                                             int c0, int c1) {
     asm volatile(
