@@ -62,6 +62,10 @@ def parse_args():
                    help="arithmetic of the trunk and decoder contractions")
     p.add_argument("--encoder-precision", choices=["fp32", "tf32", "bf16x3"], default="bf16x3",
                    help="arithmetic of the neighbour-stage contractions")
+    p.add_argument("--one-cloud", action="store_true",
+                   help="all ranks denoise one cloud of --points, its patches split across "
+                        "the GPUs with one NCCL all-reduce of the vote sums per Euler step "
+                        "(strong scaling) instead of one cloud per GPU")
     p.add_argument("--profile-forward", type=int, default=0, metavar="B",
                    help="instead of the benchmark: two model forwards on B synthetic "
                         "1000-point patches and exit (a small case for ncu captures)")
@@ -94,12 +98,13 @@ def workload_config(args, world: int) -> dict:
     from flow2surf_b200.inference import patch_seed_count
 
     patches = patch_seed_count(args.points, DENOISE["patch_size"], args.seed_k)
+    where = f"split by patch across {world} GPU(s)" if args.one_cloud else "per GPU"
     return {
         "workload": (f"full reverse-flow denoise of one {args.points:,}-point synthetic cloud "
-                     f"per GPU ({patches} patches x {DENOISE['patch_size']} points, "
+                     f"{where} ({patches} patches x {DENOISE['patch_size']} points, "
                      f"{DENOISE['num_steps']} Euler steps)"),
         "points_per_cloud": args.points,
-        "clouds": world,
+        "clouds": 1 if args.one_cloud else world,
         "patch_size": DENOISE["patch_size"],
         "seed_k": args.seed_k,
         "patches": patches,
@@ -110,7 +115,9 @@ def workload_config(args, world: int) -> dict:
         "architecture": "configs/default.yaml (feat 192, encoder 64/128, 3 blocks, ffn x8)",
         "weights": "random init, seed 0",
         "l2": f"flushed between timed steps ({L2_FLUSH_BYTES >> 20} MiB write, untimed)",
-        "parallelism": f"shard by cloud, {world} GPU(s), no collective",
+        "parallelism": (f"one cloud sharded by patch over {world} GPU(s), NCCL all-reduce of "
+                        "the float64 vote sums (24 bytes per point) per Euler step"
+                        if args.one_cloud else f"shard by cloud, {world} GPU(s), no collective"),
     }
 
 
@@ -317,14 +324,18 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
     import torch.distributed as dist
 
     from flow2surf_b200 import trace
-    from flow2surf_b200.inference import denoise_device, patch_denoise, patch_seed_count
+    from flow2surf_b200.inference import (denoise_device, patch_denoise, patch_seed_count,
+                                          shard_range)
     from flow2surf_b200.params import model_dims
     from flow2surf_b200.synthetic import DEFAULT_CONFIG
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     model = make_model(args.precision, args.encoder_precision)
-    cloud = make_cloud(args.points, rank)
+    shard = args.one_cloud and world > 1
+    group = dist.group.WORLD if shard else None
+    cloud_seed = 0 if args.one_cloud else rank
+    cloud = make_cloud(args.points, cloud_seed)
     points = torch.from_numpy(cloud).to(dev)
     pinned = torch.from_numpy(cloud).pin_memory()
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
@@ -337,7 +348,8 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
         torch.cuda.synchronize(dev)
 
     def one_step():
-        return denoise_device(model, points, rng=np.random.default_rng(rank), **kw)
+        return denoise_device(model, points, rng=np.random.default_rng(cloud_seed),
+                              process_group=group, **kw)
 
     for _ in range(warmup):
         one_step()
@@ -365,8 +377,9 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
         flush.fill_(i & 0xFF)
         torch.cuda.synchronize(dev)
         t0 = time.perf_counter()
-        host_out = patch_denoise(model, pinned, num_chunks=8, rng=np.random.default_rng(rank),
-                                 device=dev, **kw)
+        host_out = patch_denoise(model, pinned, num_chunks=8,
+                                 rng=np.random.default_rng(cloud_seed), device=dev,
+                                 process_group=group, **kw)
         e2e_s += time.perf_counter() - t0
     barrier()
     e2e = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
@@ -379,16 +392,21 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
         return
 
     ms_step = total.item() / steps
-    value = world * args.points / (ms_step * 1e-3)
-    e2e_value = world * args.points * steps / e2e.item()
+    clouds = 1 if args.one_cloud else world
+    value = clouds * args.points / (ms_step * 1e-3)
+    e2e_value = clouds * args.points * steps / e2e.item()
     dims = model_dims(DEFAULT_CONFIG)
     patches = patch_seed_count(args.points, kw["patch_size"], args.seed_k)
+    if shard:  # rank 0's share, which its kernel trace covers
+        begin, end = shard_range(patches, rank, world)
+        patches = end - begin
     forward_points = steps * kw["num_steps"] * patches * kw["patch_size"]
     kernels = rec.kernels
     total_kernel_ms = sum(ms for ms, _ in kernels.values()) or 1.0
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": steps,
-        "warmup": warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+        "warmup": warmup, "ms_per_step": ms_step, "higher_is_better": True,
+        "scaling": "strong" if args.one_cloud else "weak",
         "vs_baseline": None, "dtype": f"trunk {args.precision}, encoder {args.encoder_precision}", "data": "synthetic (seeded mesh clouds, random-init "
         "weights; no ShapeNet or checkpoints available)",
         "config": workload_config(args, world),

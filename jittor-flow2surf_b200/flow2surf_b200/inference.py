@@ -246,13 +246,15 @@ def denoise_device(model, points: torch.Tensor, patch_size, seed_k, num_steps, r
 
 def patch_denoise(model, pc_noisy, patch_size, seed_k, num_steps, num_chunks, rng=None,
                   patch_seed_idx=None, patch_agg_beta=4.0, alpha_clean_power=1.0,
-                  alpha_noisy_power=1.0, device="cuda"):
+                  alpha_noisy_power=1.0, device="cuda", process_group=None):
     """Denoise one normalized point cloud by patch-wise reverse integration.
 
     Drop-in for flow2surf/inference.py:68-198: `pc_noisy` is a host (N, 3)
     array and so is the result (float32). `num_chunks` is validated as the
     reference does; the GPU batches patches by a memory budget instead, which
     does not change any result because patches are independent.
+    `process_group` splits the cloud's patches across the group's GPUs
+    (see `denoise_device`).
     """
     if num_chunks < 1:
         raise ValueError(f"num_chunks must be >= 1, got {num_chunks}")
@@ -264,5 +266,5 @@ def patch_denoise(model, pc_noisy, patch_size, seed_k, num_steps, num_chunks, rn
     out = denoise_device(model, points, patch_size, seed_k, num_steps, rng=rng,
                          patch_seed_idx=patch_seed_idx, patch_agg_beta=patch_agg_beta,
                          alpha_clean_power=alpha_clean_power,
-                         alpha_noisy_power=alpha_noisy_power)
+                         alpha_noisy_power=alpha_noisy_power, process_group=process_group)
     return out.cpu().numpy()
