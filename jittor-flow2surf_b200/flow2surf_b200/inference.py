@@ -21,6 +21,7 @@ from .flow import alpha_schedule
 
 # Device memory the model's per-chunk workspace may take.
 DEFAULT_WORKSPACE_BUDGET = 24 << 30
+MAX_ROWS_PER_FORWARD = 1 << 20   # f2s_model_forward takes B * M below this per call
 
 
 def make_rng(seed, *parts):
@@ -126,7 +127,9 @@ class _Runner:
         self.workspace = None
         if hasattr(model, "workspace_bytes"):
             per_patch = max(1, model.workspace_bytes(1, k))
-            self.chunk = max(1, min(P, workspace_budget // per_patch))
+            # also within the forward's row limit (B * M < 2^20 per call)
+            row_cap = max(1, (MAX_ROWS_PER_FORWARD - 1) // k)
+            self.chunk = max(1, min(P, workspace_budget // per_patch, row_cap))
             self.workspace = torch.empty(model.workspace_bytes(self.chunk, k), dtype=torch.uint8,
                                          device=dev)
 
