@@ -78,49 +78,73 @@ __device__ __forceinline__ void named_sync_softmax() {
 __global__ void qk_split_kernel(const float* __restrict__ q, const float* __restrict__ k, int ldqk,
                                 int rows, int d, bool normalize, __nv_bfloat16* __restrict__ hi,
                                 __nv_bfloat16* __restrict__ lo) {
+    // half-warp per (row, part): lane l of the half owns padded channels
+    // [4l, 4l + 4) of the 64, loaded as one float4 (d <= 64, 16-byte rows)
     const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (row >= rows) return;
-    for (int part = 0; part < 2; ++part) {
-        const float* src = (part == 0 ? q : k) + (size_t)row * ldqk;
-        float mean = 0.0f, rstd = 1.0f;
-        if (normalize) {  // ChannelLayerNorm, no affine, eps 1e-6 (layers.py:20-27)
-            float s = 0.0f;
-            for (int c = lane; c < d; c += 32) s += src[c];
-            mean = f2s_warp_sum(s) / (float)d;
-            float qq = 0.0f;
-            for (int c = lane; c < d; c += 32) {
-                const float t = src[c] - mean;
-                qq = fmaf(t, t, qq);
-            }
-            rstd = rsqrtf(f2s_warp_sum(qq) / (float)d + 1e-6f);
-        }
-        __nv_bfloat16* h = hi + (size_t)row * 2 * kDPad + part * kDPad;
-        __nv_bfloat16* l = lo + (size_t)row * 2 * kDPad + part * kDPad;
-        for (int c = lane; c < kDPad; c += 32) {
-            const float v = c < d ? (src[c] - mean) * rstd : 0.0f;
-            const __nv_bfloat16 vh = __float2bfloat16_rn(v);
-            h[c] = vh;
-            l[c] = __float2bfloat16_rn(v - __bfloat162float(vh));
-        }
+    const int part = lane >> 4, l = lane & 15;
+    const int c0 = 4 * l;
+    const float* src = (part == 0 ? q : k) + (size_t)row * ldqk;
+    float v[4];
+    {
+        float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (c0 + 3 < d) x = *reinterpret_cast<const float4*>(src + c0);
+        else
+            for (int e = 0; e < 4; ++e)
+                if (c0 + e < d) (&x.x)[e] = src[c0 + e];
+        v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
     }
+    if (normalize) {  // ChannelLayerNorm, no affine, eps 1e-6 (layers.py:20-27)
+        float s = (v[0] + v[1]) + (v[2] + v[3]);
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        const float mean = s / (float)d;
+        float qq = 0.0f;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const float t = c0 + e < d ? v[e] - mean : 0.0f;
+            qq = fmaf(t, t, qq);
+        }
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) qq += __shfl_xor_sync(0xffffffffu, qq, o);
+        const float rstd = rsqrtf(qq / (float)d + 1e-6f);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) v[e] = c0 + e < d ? (v[e] - mean) * rstd : 0.0f;
+    }
+    uint32_t h[2], lw[2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+        const __nv_bfloat162 hb = __floats2bfloat162_rn(v[2 * e], v[2 * e + 1]);
+        const __nv_bfloat162 lb = __floats2bfloat162_rn(v[2 * e] - __bfloat162float(hb.x),
+                                                        v[2 * e + 1] - __bfloat162float(hb.y));
+        h[e] = *reinterpret_cast<const uint32_t*>(&hb);
+        lw[e] = *reinterpret_cast<const uint32_t*>(&lb);
+    }
+    const size_t o = (size_t)row * 2 * kDPad + part * kDPad + c0;
+    *reinterpret_cast<uint2*>(hi + o) = make_uint2(h[0], h[1]);
+    *reinterpret_cast<uint2*>(lo + o) = make_uint2(lw[0], lw[1]);
 }
 
-// V (rows = b*N + n, ldv) -> vT[b][c][n] (pitch n_pad), rounded to tf32.
+// V (rows = b*N + n, ldv) -> vT[b][c][n] (pitch n_pad), rounded to tf32;
+// 64 x 64 tiles through shared memory, 16 values per thread.
 __global__ void v_transpose_kernel(const float* __restrict__ v, int ldv, int N, int C, int n_pad,
                                    float* __restrict__ vT) {
-    __shared__ float tile[32][33];
+    __shared__ float tile[64][65];
     const int b = blockIdx.z;
-    const int n0 = blockIdx.x * 32, c0 = blockIdx.y * 32;
-    for (int y = threadIdx.y; y < 32; y += 8) {
-        const int n = n0 + y, c = c0 + threadIdx.x;
-        if (n < N && c < C) tile[y][threadIdx.x] = v[((size_t)b * N + n) * ldv + c];
+    const int n0 = blockIdx.x * 64, c0 = blockIdx.y * 64;
+    const int tx = threadIdx.x & 63, ty = threadIdx.x >> 6;  // 64 x 4
+#pragma unroll
+    for (int y = ty; y < 64; y += 4) {
+        const int n = n0 + y, c = c0 + tx;
+        if (n < N && c < C) tile[y][tx] = v[((size_t)b * N + n) * ldv + c];
     }
     __syncthreads();
-    for (int y = threadIdx.y; y < 32; y += 8) {
-        const int c = c0 + y, n = n0 + threadIdx.x;
+#pragma unroll
+    for (int y = ty; y < 64; y += 4) {
+        const int c = c0 + y, n = n0 + tx;
         if (c < C && n < n_pad)
-            vT[((size_t)b * C + c) * n_pad + n] = n < N ? f2s_round_tf32(tile[threadIdx.x][y]) : 0.0f;
+            vT[((size_t)b * C + c) * n_pad + n] = n < N ? f2s_round_tf32(tile[tx][y]) : 0.0f;
     }
 }
 
@@ -620,7 +644,8 @@ int attention_tc(const float* q, const float* k, int ldqk, const float* v, int l
                  const float* h, int ldh, float* out, int ldo, float* workspace, int B, int N,
                  int d, int C, bool normalize_qk, bool round_tf32, cudaStream_t st) {
     if (B == 0 || N == 0) return F2S_OK;
-    if (d > kDPad || C % 32 != 0 || C > 256 || C < 32)
+    if (d > kDPad || C % 32 != 0 || C > 256 || C < 32 || ldqk % 4 != 0 ||
+        ((uintptr_t)q & 15) != 0 || ((uintptr_t)k & 15) != 0)
         return fail(F2S_ERR_UNSUPPORTED, "attention shape outside the tensor-core kernel");
     int* err = tc_error_word();
     if (!err) return fail(F2S_ERR_CUDA, "attention_tc: device error word unavailable");
@@ -634,8 +659,8 @@ int attention_tc(const float* q, const float* k, int ldqk, const float* v, int l
         qk_split_kernel<<<ceil_div(B * N, 8), 256, 0, st>>>(q, k, ldqk, B * N, d, normalize_qk,
                                                              qk_hi, qk_lo);
         F2S_TRY(check_launch("qk_split_kernel"));
-        dim3 grid(ceil_div(n_pad, 32), ceil_div(C, 32), B);
-        v_transpose_kernel<<<grid, dim3(32, 8), 0, st>>>(v, ldv, N, C, n_pad, vT);
+        dim3 grid(ceil_div(n_pad, 64), ceil_div(C, 64), B);
+        v_transpose_kernel<<<grid, 256, 0, st>>>(v, ldv, N, C, n_pad, vT);
         F2S_TRY(check_launch("v_transpose_kernel"));
     }
     CUtensorMap map_hi_q, map_lo_q, map_hi_k, map_lo_k, map_vt;
