@@ -9,6 +9,7 @@ state-dict names; they are composed and packed once into a device blob
 from __future__ import annotations
 
 import ctypes
+import pickle
 
 import numpy as np
 import torch
@@ -165,6 +166,23 @@ def reference_init(cfg: dict, seed: int = 0) -> dict:
     return p
 
 
+class _ArrayUnpickler(pickle.Unpickler):
+    """Unpickler for parameter files: dicts, lists and NumPy arrays only."""
+
+    _ALLOWED = {
+        ("collections", "OrderedDict"), ("builtins", "dict"), ("builtins", "list"),
+        ("numpy", "ndarray"), ("numpy", "dtype"),
+        ("numpy.core.multiarray", "_reconstruct"), ("numpy._core.multiarray", "_reconstruct"),
+        ("numpy.core.multiarray", "scalar"), ("numpy._core.multiarray", "scalar"),
+        ("numpy.core.numeric", "_frombuffer"), ("numpy._core.numeric", "_frombuffer"),
+    }
+
+    def find_class(self, module, name):
+        if (module, name) in self._ALLOWED or (module == "numpy" and name.startswith("dtype")):
+            return super().find_class(module, name)
+        raise pickle.UnpicklingError(f"refusing to load {module}.{name} from a parameter file")
+
+
 class Flow2SurfNet:
     """Predict patch velocities (flow2surf/models/network.py:29-82).
 
@@ -204,6 +222,29 @@ class Flow2SurfNet:
         self._blob = None
 
     load_state_dict = load_parameters
+
+    def save(self, path) -> None:
+        """Write the parameters as the reference's Module.save does: a pickled
+        {state-dict name: float32 array} dict (flow2surf/training/checkpoint.py:72-74)."""
+        with open(path, "wb") as f:
+            pickle.dump({k: np.ascontiguousarray(v) for k, v in self._params.items()}, f,
+                        protocol=pickle.HIGHEST_PROTOCOL)
+
+    def load(self, path) -> None:
+        """Load a checkpoint the reference wrote with model.save (loaded there by
+        model.load, predict.py:46): a pickled dict of parameter arrays keyed by
+        state-dict name; `.npz` archives are taken too. The unpickler accepts
+        only dicts, lists and NumPy arrays, so a checkpoint file cannot run code."""
+        path = str(path)
+        if path.endswith(".npz"):
+            with np.load(path, allow_pickle=False) as z:
+                params = {k: z[k] for k in z.files}
+        else:
+            with open(path, "rb") as f:
+                params = _ArrayUnpickler(f).load()
+        if not isinstance(params, dict):
+            raise ValueError(f"{path}: expected a dict of parameter arrays, got {type(params)}")
+        self.load_parameters({str(k): np.asarray(v) for k, v in params.items()})
 
     def eval(self):
         return self
