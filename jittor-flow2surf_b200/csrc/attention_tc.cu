@@ -319,14 +319,12 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
     constexpr uint32_t kQBytes = kRows * 128;        // 128 queries x 64 bf16
     constexpr uint32_t kKBytes = kKeyTile * 128;     // 64 keys x 64 bf16
     const uint32_t v_bytes = (uint32_t)C * 128;      // one K-block: C rows x 32 fp32 keys
-    constexpr uint32_t kPBytes = kRows * 128;        // one K-block: 128 queries x 32 fp32 keys
     unsigned char* sQ = smem;                                  // hi, lo
     unsigned char* sK = sQ + 2 * kQBytes;                      // kKStages x (hi, lo)
     unsigned char* sV = sK + 2 * kKStages * kKBytes;           // 2 stages x 2 K-blocks
-    unsigned char* sP = sV + 4 * v_bytes;                      // 2 K-blocks
     const int nk = (a.N + kKeyTile - 1) / kKeyTile;
     // the patch's per-key log-sum-exp values times log2(e), nk * 64 of them
-    float* sL = reinterpret_cast<float*>(sP + 2 * kPBytes);
+    float* sL = reinterpret_cast<float*>(sV + 4 * v_bytes);
     // softmax go / stop decisions: [0, 2) S ready, [2, 4) P free (by tile
     // parity), [4] output ready, [5] h tile landed; written by thread 0
     // before a named barrier
@@ -341,19 +339,21 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
     uint64_t* s_full = bars + 11;   // [2]
     uint64_t* s_empty = bars + 13;  // [2]  (128 arrivals)
     uint64_t* p_full = bars + 15;   // [1]  (128 arrivals)
-    uint64_t* pv_done = bars + 16;  // [1]
-    uint64_t* done = bars + 17;     // [1]
-    uint64_t* h_full = bars + 18;   // [1]  epilogue: h tile
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 19);
+    uint64_t* pv_done = bars + 16;  // [2]  by P buffer
+    uint64_t* done = bars + 18;     // [1]
+    uint64_t* h_full = bars + 19;   // [1]  epilogue: h tile
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
 
     const int b = blockIdx.x / a.tiles;
     const int q0 = (blockIdx.x - b * a.tiles) * kRows;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    // TMEM: S double buffer at columns [0, 128), O at [256, 256 + C)
+    // TMEM: S double buffer at columns [0, 128), P (tf32, the P V product's A
+    // operand) double buffer at [128, 256), O at [256, 256 + C)
+    constexpr uint32_t kPCol = 128;
     constexpr uint32_t kOCol = 256;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < 19; ++i)
+        for (int i = 0; i < 20; ++i)
             tc::mbar_init(&bars[i], (i == 13 || i == 14 || i == 15) ? 128 : 1);
         tc::fence_barrier_init();
     }
@@ -414,7 +414,6 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
                 return true;
             };
             if (ok) ok = issue_s(0);
-            const uint32_t p0 = tc::smem_u32(sP);
             for (int i = 0; i < nk && ok; ++i) {
                 if (i + 1 < nk && !issue_s(i + 1)) {
                     ok = false;
@@ -437,16 +436,16 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
                 v_landed = i + 1;
                 tc::tc_fence_after();
                 const uint32_t v0 = tc::smem_u32(sV + (2 * (i & 1)) * v_bytes);
+                const uint32_t pa = tmem + kPCol + (uint32_t)((i & 1) * kKeyTile);
 #pragma unroll
                 for (int kb = 0; kb < 2; ++kb)
 #pragma unroll
-                    for (int kk = 0; kk < 4; ++kk) {  // 8 keys (32 bytes) per tf32 MMA
-                        const uint32_t o = kk * 32;
-                        tc::umma<true>(tmem + kOCol, tc::sw128_desc(p0 + kb * kPBytes + o),
-                                       tc::sw128_desc(v0 + kb * v_bytes + o), a.idesc_pv,
-                                       (i | kb | kk) ? 1u : 0u);
+                    for (int kk = 0; kk < 4; ++kk) {  // 8 keys (32 bytes of V^T) per tf32 MMA
+                        tc::umma_tmem_a_tf32(tmem + kOCol, pa + (uint32_t)(kb * 32 + kk * 8),
+                                             tc::sw128_desc(v0 + kb * v_bytes + kk * 32),
+                                             a.idesc_pv, (i | kb | kk) ? 1u : 0u);
                     }
-                tc::umma_commit(pv_done);
+                tc::umma_commit(&pv_done[i & 1]);
                 tc::umma_commit(&v_empty[i & 1]);
                 // P V_{i-1} is done with its V tile: refill that stage with tile i + 1
                 if (i >= 1 && i + 1 < nk) {
@@ -508,31 +507,31 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
                     den += pe;
                 }
             }
-            // the previous P must have been consumed before it is overwritten
-            if (i > 0) {
+            // P buffer i & 1 was last read by the P V product of tile i - 2
+            if (i > 1) {
                 if (row == 0)
-                    sFlag[2 + s] = tc::mbar_wait(pv_done, (uint32_t)(i - 1) & 1u, a.err) ? 1 : 0;
+                    sFlag[2 + s] =
+                        tc::mbar_wait(&pv_done[s], (uint32_t)((i - 2) >> 1) & 1u, a.err) ? 1 : 0;
                 named_sync_softmax();
                 if (!sFlag[2 + s]) {
                     ok = false;
                     break;
                 }
+                tc::tc_fence_after();
             }
 #pragma unroll
-            for (int kb = 0; kb < 2; ++kb)
-#pragma unroll
-                for (int ch = 0; ch < 8; ++ch) {
-                    const int j = kb * 32 + ch * 4;
-                    *reinterpret_cast<float4*>(sP + kb * kPBytes + sw128_offset(row, ch)) =
-                        make_float4(f2s_round_tf32(p[j]), f2s_round_tf32(p[j + 1]),
-                                    f2s_round_tf32(p[j + 2]), f2s_round_tf32(p[j + 3]));
-                }
-            fence_proxy_async();
+            for (int j = 0; j < 64; ++j) p[j] = f2s_round_tf32(p[j]);
+            const uint32_t pt = tmem + lane_base + kPCol + (uint32_t)(s * kKeyTile);
+            tc::tmem_st32(pt, *reinterpret_cast<float(*)[32]>(p));
+            tc::tmem_st32(pt + 32, *reinterpret_cast<float(*)[32]>(p + 32));
+            tc::tc_fence_before();
             tc::mbar_arrive(p_full);
         }
         // wait for the last P V product, then write h - O / (den + 1e-9)
         if (ok) {
-            if (row == 0) sFlag[4] = tc::mbar_wait(pv_done, (uint32_t)(nk - 1) & 1u, a.err) ? 1 : 0;
+            if (row == 0)
+                sFlag[4] = tc::mbar_wait(&pv_done[(nk - 1) & 1], (uint32_t)((nk - 1) >> 1) & 1u,
+                                         a.err) ? 1 : 0;
             named_sync_softmax();
             ok = sFlag[4] != 0;
         }
@@ -713,8 +712,7 @@ int attention_tc(const float* q, const float* k, int ldqk, const float* v, int l
         a.idesc_s = tc::make_idesc(kRows, kKeyTile, 1u);
         a.idesc_pv = tc::make_idesc(kRows, C, 2u);
         const size_t smem = 1024 + 2 * kRows * 128 + 2 * kKStages * kKeyTile * 128 + 4 * (size_t)C * 128 +
-                            2 * kRows * 128 + (size_t)ceil_div(N, kKeyTile) * kKeyTile * 4 + 32 +
-                            8 + 19 * 8 + 16;
+                            (size_t)ceil_div(N, kKeyTile) * kKeyTile * 4 + 32 + 8 + 20 * 8 + 16;
         F2S_LIMIT(smem <= 227 * 1024, "attention_tc: %zu bytes of shared memory", smem);
         F2S_CUDA_TRY(cudaFuncSetAttribute(attn_tc_output_kernel,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));

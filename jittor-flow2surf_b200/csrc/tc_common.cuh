@@ -136,6 +136,17 @@ __device__ __forceinline__ void umma(uint32_t d_tmem, uint64_t a_desc, uint64_t 
     }
 }
 
+// The same with the A operand in tensor memory (M = 128 rows on the lanes, K
+// consecutive 32-bit columns from `a_tmem`), tf32 operands.
+__device__ __forceinline__ void umma_tmem_a_tf32(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                                 uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 // Arrive on `bar` once every tcgen05 operation this thread issued completes.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
     asm volatile(
