@@ -150,6 +150,7 @@ __global__ void v_transpose_kernel(const float* __restrict__ v, int ldv, int N, 
 
 struct AttnArgs {
     int N, C, n_pad;
+    int d_steps;      // 16-channel MMA steps covering the d real q/k channels (the padding is 0)
     int tiles;        // key tiles (pass 1: of 128) / query tiles (pass 2: of 128) per patch
     float* colstats;  // (B*N) per-key log-sum-exp
     const float* h;   // pass 2: offset input (nullptr: plain aggregate)
@@ -235,7 +236,7 @@ attn_tc_colstats_kernel(const __grid_constant__ CUtensorMap map_hi,
                 const uint32_t q_hi = tc::smem_u32(sQ + (2 * s) * kTileBytes), q_lo = q_hi + kTileBytes;
                 const uint32_t d = tmem + (uint32_t)(s * 128);
 #pragma unroll
-                for (int kk = 0; kk < 4; ++kk) {  // 64 channels, 16 per MMA
+                for (int kk = 0; kk < a.d_steps; ++kk) {  // 16 channels per MMA
                     const uint32_t o = kk * 32;
                     tc::umma<false>(d, tc::sw128_desc(k_hi + o), tc::sw128_desc(q_hi + o), a.idesc_s,
                                     kk ? 1u : 0u);
@@ -402,7 +403,7 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
                 const uint32_t k_hi = tc::smem_u32(sK + (2 * ks) * kKBytes), k_lo = k_hi + kKBytes;
                 const uint32_t d = tmem + (uint32_t)(s * 64);
 #pragma unroll
-                for (int kk = 0; kk < 4; ++kk) {
+                for (int kk = 0; kk < a.d_steps; ++kk) {  // 16 channels per MMA
                     const uint32_t o = kk * 32;
                     tc::umma<false>(d, tc::sw128_desc(q_hi + o), tc::sw128_desc(k_hi + o), a.idesc_s,
                                     kk ? 1u : 0u);
@@ -418,14 +419,6 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
                 if (i + 1 < nk && !issue_s(i + 1)) {
                     ok = false;
                     break;
-                }
-                // S_i is done with its K tile: refill that stage with tile i + kKStages
-                if (i + kKStages < nk) {
-                    if (!tc::mbar_wait(&k_empty[i % kKStages], (uint32_t)(i / kKStages) & 1u, a.err)) {
-                        ok = false;
-                        break;
-                    }
-                    load_k(i + kKStages);
                 }
                 // P_i written by the softmax threads, V_i landed
                 if (!tc::mbar_wait(p_full, (uint32_t)i & 1u, a.err) ||
@@ -447,6 +440,16 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
                     }
                 tc::umma_commit(&pv_done[i & 1]);
                 tc::umma_commit(&v_empty[i & 1]);
+                // S_i is done with its K tile (issued before P V_i, so waiting here
+                // never holds P V_i back): refill that stage with tile i + kKStages
+                if (i + kKStages < nk) {
+                    if (!tc::mbar_wait(&k_empty[i % kKStages], (uint32_t)(i / kKStages) & 1u, a.err)) {
+                        ok = false;
+                        break;
+                    }
+                    load_k(i + kKStages);
+                }
+
                 // P V_{i-1} is done with its V tile: refill that stage with tile i + 1
                 if (i >= 1 && i + 1 < nk) {
                     if (!tc::mbar_wait(&v_empty[(i - 1) & 1], (uint32_t)((i - 1) >> 1) & 1u, a.err)) {
@@ -674,6 +677,7 @@ int attention_tc(const float* q, const float* k, int ldqk, const float* v, int l
     AttnArgs a{};
     a.N = N;
     a.C = C;
+    a.d_steps = ceil_div(d, 16);
     a.n_pad = n_pad;
     a.colstats = colstats;
     a.h = h;

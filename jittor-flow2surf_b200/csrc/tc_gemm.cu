@@ -43,6 +43,7 @@ struct TcGemmArgs {
     int stages;
     int acc_cols;       // TMEM columns of one accumulator buffer
     uint32_t idesc;
+    uint32_t idesc_dual;  // SwiGLU: N = 2 BN over the adjacent W / W2 tiles
     const float* bias;
     const float* bias2;
     void* Y;
@@ -229,11 +230,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                         const uint64_t a = tc::sw128_desc(st + k * 32);
                         const uint64_t b = tc::sw128_desc(st + a_stage + k * 32);
                         const uint32_t acc = (kb | k) ? 1u : 0u;
-                        tc::umma<kTf32>(d, a, b, g.idesc, acc);
-                        if (kDual) {
-                            const uint64_t b2 = tc::sw128_desc(st + a_stage + b_bytes + k * 32);
-                            tc::umma<kTf32>(d + (uint32_t)g.bn, a, b2, g.idesc, acc);
-                        }
+                        // SwiGLU: W and W2 tiles are adjacent swizzled row blocks,
+                        // so one N = 2 BN instruction fills both accumulators
+                        // (an MMA costs the same time for any N up to 128)
+                        tc::umma<kTf32>(d, a, b, kDual ? g.idesc_dual : g.idesc, acc);
                         if (kSplit) {
                             const uint64_t a_lo = tc::sw128_desc(st + a_bytes + k * 32);
                             const uint64_t b_lo = tc::sw128_desc(st + a_stage + b_bytes + k * 32);
@@ -534,6 +534,7 @@ int tc_gemm(const TcGemmOp& op, cudaStream_t st) {
     g.k_blocks = ceil_div(op.K, bk);
     g.acc_cols = bn * (dual ? 2 : 1);
     g.idesc = tc::make_idesc(kTileM, bn, op.tf32 ? 2u : 1u);
+    g.idesc_dual = tc::make_idesc(kTileM, 2 * bn, op.tf32 ? 2u : 1u);
     g.bias = op.bias;
     g.bias2 = op.bias2;
     g.Y = op.Y;
@@ -614,13 +615,24 @@ int split_tf32(const float* x, int ldx, int rows, int K, float* hi, float* lo, c
 }
 
 int tc_pick_bn(int cols, bool swiglu) {
-    static const int kCandidates[] = {256, 192, 128, 96, 64, 32};
+    // One tcgen05 MMA (M = 128) takes about 64 ns for every N up to ~176 and
+    // about 0.36 ns per column beyond (measured on B200: 64 ns at N <= 128,
+    // 93 ns at N = 256): minimise N tiles x that time, larger tiles on ties.
+    // On ties, the least padding, then the larger tile. SwiGLU tiles pair W
+    // and W2 in one N = 2 BN instruction, so BN <= 128.
+    static const int kCandidates[] = {256, 224, 192, 160, 128, 96, 64, 32};
     int best = 32, best_waste = 1 << 30;
+    double best_cost = 1e30;
     for (int bn : kCandidates) {
         if (swiglu && bn > 128) continue;
-        const int waste = ceil_div(cols, bn) * bn - cols;
-        if (waste < best_waste) {
+        const int n_eff = swiglu ? 2 * bn : bn;
+        const double per_mma = 0.3625 * n_eff > 64.0 ? 0.3625 * n_eff : 64.0;
+        const int tiles = ceil_div(cols, bn);
+        const double cost = tiles * per_mma;
+        const int waste = tiles * bn - cols;
+        if (cost < best_cost - 1e-9 || (cost < best_cost + 1e-9 && waste < best_waste)) {
             best = bn;
+            best_cost = cost;
             best_waste = waste;
         }
     }
