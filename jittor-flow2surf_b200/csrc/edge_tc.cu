@@ -442,21 +442,23 @@ edge_tc_kernel(const __grid_constant__ CUtensorMap map_w, const EdgeTcArgs a) {
                     const uint32_t d = tmem_base + (uint32_t)(tbuf * cout);
                     const uint32_t a0 = tc::smem_u32(dA);
                     const uint32_t b0 = tc::smem_u32(sB), b_lo = tc::smem_u32(sBlo);
-                    for (int kb = 0; kb < kblocks; ++kb)
+                    for (int kb = 0; kb < kblocks; ++kb) {
+                        // the K block's descriptors once; K step k adds 32 bytes
+                        // = 2 in the start-address field (address >> 4)
+                        const uint64_t da0 = tc::sw128_desc(a0 + kb * kRows * 128);
+                        const uint64_t db0 = tc::sw128_desc(b0 + kb * cout * 128);
+                        const uint64_t dal0 = tc::sw128_desc(a0 + (uint32_t)a_bytes + kb * kRows * 128);
+                        const uint64_t dbl0 = tc::sw128_desc(b_lo + kb * cout * 128);
 #pragma unroll
                         for (int k = 0; k < 4; ++k) {
                             if ((kb * kBk + k * (32 / kElem)) >= H) break;
-                            const uint32_t ao = kb * kRows * 128 + k * 32;
-                            const uint32_t bo = kb * cout * 128 + k * 32;
-                            const uint64_t da = tc::sw128_desc(a0 + ao);
-                            const uint64_t db = tc::sw128_desc(b0 + bo);
-                            tc::umma<kTf32>(d, da, db, a.idesc, (kb | k) ? 1u : 0u);
+                            tc::umma<kTf32>(d, da0 + 2 * k, db0 + 2 * k, a.idesc, (kb | k) ? 1u : 0u);
                             if (kSplit) {
-                                tc::umma<false>(d, da, tc::sw128_desc(b_lo + bo), a.idesc, 1u);
-                                tc::umma<false>(d, tc::sw128_desc(a0 + (uint32_t)a_bytes + ao),
-                                                db, a.idesc, 1u);
+                                tc::umma<false>(d, da0 + 2 * k, dbl0 + 2 * k, a.idesc, 1u);
+                                tc::umma<false>(d, dal0 + 2 * k, db0 + 2 * k, a.idesc, 1u);
                             }
                         }
+                    }
                     tc::umma_commit(&a_empty[abuf]);
                     tc::umma_commit(&t_full[tbuf]);
                     if (has_next) issue_pre();

@@ -225,20 +225,22 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                     }
                     tc::tc_fence_after();
                     const uint32_t st = tc::smem_u32(smem + (size_t)stage * stage_bytes);
+                    // the stage's descriptors once; K step k adds 32 bytes = 2 in
+                    // the start-address field (address >> 4)
+                    const uint64_t a0 = tc::sw128_desc(st);
+                    const uint64_t b0 = tc::sw128_desc(st + a_stage);
+                    const uint64_t a_lo0 = kSplit ? tc::sw128_desc(st + a_bytes) : 0;
+                    const uint64_t b_lo0 = kSplit ? tc::sw128_desc(st + a_stage + b_bytes) : 0;
+                    const uint32_t idesc = kDual ? g.idesc_dual : g.idesc;
 #pragma unroll
                     for (int k = 0; k < kSteps; ++k) {
-                        const uint64_t a = tc::sw128_desc(st + k * 32);
-                        const uint64_t b = tc::sw128_desc(st + a_stage + k * 32);
                         const uint32_t acc = (kb | k) ? 1u : 0u;
                         // SwiGLU: W and W2 tiles are adjacent swizzled row blocks,
                         // so one N = 2 BN instruction fills both accumulators
-                        // (an MMA costs the same time for any N up to 128)
-                        tc::umma<kTf32>(d, a, b, kDual ? g.idesc_dual : g.idesc, acc);
+                        tc::umma<kTf32>(d, a0 + 2 * k, b0 + 2 * k, idesc, acc);
                         if (kSplit) {
-                            const uint64_t a_lo = tc::sw128_desc(st + a_bytes + k * 32);
-                            const uint64_t b_lo = tc::sw128_desc(st + a_stage + b_bytes + k * 32);
-                            tc::umma<kTf32>(d, a, b_lo, g.idesc, 1u);
-                            tc::umma<kTf32>(d, a_lo, b, g.idesc, 1u);
+                            tc::umma<kTf32>(d, a0 + 2 * k, b_lo0 + 2 * k, g.idesc, 1u);
+                            tc::umma<kTf32>(d, a_lo0 + 2 * k, b0 + 2 * k, g.idesc, 1u);
                         }
                     }
                     tc::umma_commit(&empty[stage]);
