@@ -33,7 +33,11 @@ constexpr int kRows = 128;        // keys (pass 1) / queries (pass 2) per CTA
 constexpr int kDPad = 64;         // padded q/k width: 64 bf16 = 128 bytes
 constexpr int kKeyTile = 64;      // keys per pass-2 tile
 constexpr int kKStages = 3;       // pass-2 K tiles in flight
-constexpr int kThreads = 160;     // warps 0-3 softmax/epilogue, warp 4 TMA + MMA
+constexpr int kThreads = 160;     // pass 1: warps 0-3 statistics, warp 4 TMA + MMA
+// pass 2: warps 0-7 softmax / epilogue (two per TMEM lane quarter, one half of
+// each key tile and of the output columns each), warp 8 TMA + MMA
+constexpr int kOutWarps = 8;
+constexpr int kOutThreads = (kOutWarps + 1) * 32;
 constexpr unsigned kFull = 0xffffffffu;
 
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar,
@@ -70,6 +74,10 @@ __device__ __forceinline__ void fence_proxy_async() {
 
 __device__ __forceinline__ void named_sync_softmax() {
     asm volatile("bar.sync 1, 128;" ::: "memory");
+}
+
+__device__ __forceinline__ void named_sync_out() {
+    asm volatile("bar.sync 1, %0;" ::"n"(kOutWarps * 32) : "memory");
 }
 
 // ---------------------------------------------------------------------------
@@ -305,7 +313,7 @@ attn_tc_colstats_kernel(const __grid_constant__ CUtensorMap map_hi,
 // ---------------------------------------------------------------------------
 // pass 2: out = h - (sum_j p_ij V_j) / (sum_j p_ij + 1e-9), p_ij = exp(S_ij - L_j)
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kOutThreads, 1)
 attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
                       const __grid_constant__ CUtensorMap map_qlo,
                       const __grid_constant__ CUtensorMap map_khi,
@@ -330,8 +338,9 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
     // parity), [4] output ready, [5] h tile landed; written by thread 0
     // before a named barrier
     int* sFlag = reinterpret_cast<int*>(sL + nk * kKeyTile);
+    float* sDen = reinterpret_cast<float*>(sFlag + 8);  // [2][128] partial row sums
     uint64_t* bars = reinterpret_cast<uint64_t*>(
-        (reinterpret_cast<uintptr_t>(sFlag + 6) + 7) & ~uintptr_t(7));
+        (reinterpret_cast<uintptr_t>(sDen + 2 * kRows) + 7) & ~uintptr_t(7));
     uint64_t* q_full = bars;        // [1]
     uint64_t* k_full = bars + 1;    // [kKStages]
     uint64_t* k_empty = bars + 4;   // [kKStages]
@@ -355,7 +364,7 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < 20; ++i)
-            tc::mbar_init(&bars[i], (i == 13 || i == 14 || i == 15) ? 128 : 1);
+            tc::mbar_init(&bars[i], (i == 13 || i == 14 || i == 15) ? kOutWarps * 32 : 1);
         tc::fence_barrier_init();
     }
     if (warp == 0) tc::tmem_alloc(tmem_slot, 512);
@@ -364,7 +373,7 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
     tc::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == 4) {
+    if (warp == kOutWarps) {
         if (lane == 0) {
             bool ok = true;
             // K tiles run kKStages deep and are refilled as soon as their S
@@ -469,75 +478,78 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
         }
         __syncwarp();
     } else {
-        // one thread per query row; thread 0 does every wait and publishes
-        // the outcome, so the four softmax warps always take the same path
-        const int row = warp * 32 + lane;
-        const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+        // one thread per (query row, half of the key tile / output columns);
+        // thread 0 does every wait and publishes the outcome, so the eight
+        // softmax warps always take the same path
+        const int quarter = warp & 3, half = warp >> 2;
+        const int row = quarter * 32 + lane;
+        const int stid = threadIdx.x;  // 0 .. 255
+        const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
         constexpr float kLog2e = 1.44269504088896341f;
-        for (int j = row; j < nk * kKeyTile; j += kRows)
+        for (int j = stid; j < nk * kKeyTile; j += kOutWarps * 32)
             sL[j] = j < a.N ? a.colstats[(size_t)b * a.N + j] * kLog2e : 0.0f;
         float den = 0.0f;
         bool ok = true;
+        const int k0 = half * 32;  // this thread's keys within a tile
         for (int i = 0; i < nk; ++i) {
             const int s = i & 1;
             const uint32_t ph = (uint32_t)(i >> 1) & 1u;
-            if (row == 0) sFlag[s] = tc::mbar_wait(&s_full[s], ph, a.err) ? 1 : 0;
-            named_sync_softmax();
+            if (stid == 0) sFlag[s] = tc::mbar_wait(&s_full[s], ph, a.err) ? 1 : 0;
+            named_sync_out();
             if (!sFlag[s]) {
                 ok = false;
                 break;
             }
             tc::tc_fence_after();
-            float p[64];
-            tc::tmem_ld32(tmem + lane_base + (uint32_t)(s * 64), *reinterpret_cast<float(*)[32]>(p));
-            tc::tmem_ld32(tmem + lane_base + (uint32_t)(s * 64 + 32),
-                          *reinterpret_cast<float(*)[32]>(p + 32));
+            float p[32];
+            tc::tmem_ld32(tmem + lane_base + (uint32_t)(s * 64 + k0), p);
             tc::tc_fence_before();
             tc::mbar_arrive(&s_empty[s]);
             // p = exp(S - L) = 2^(S log2 e - L log2 e), computed while the
             // previous tile's P V product may still run
-            const int valid = min(kKeyTile, a.N - i * kKeyTile);
-            const float* Lt = sL + i * kKeyTile;
+            const int valid = min(kKeyTile, a.N - i * kKeyTile) - k0;
+            const float* Lt = sL + i * kKeyTile + k0;
 #pragma unroll
-            for (int j = 0; j < 64; j += 4) {
+            for (int j = 0; j < 32; j += 4) {
                 const float4 l4 = *reinterpret_cast<const float4*>(Lt + j);
                 const float lj[4] = {l4.x, l4.y, l4.z, l4.w};
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
                     const float pe =
                         j + e < valid ? f2s_ex2_approx(fmaf(p[j + e], kLog2e, -lj[e])) : 0.0f;
-                    p[j + e] = pe;
+                    p[j + e] = f2s_round_tf32(pe);
                     den += pe;
                 }
             }
             // P buffer i & 1 was last read by the P V product of tile i - 2
             if (i > 1) {
-                if (row == 0)
+                if (stid == 0)
                     sFlag[2 + s] =
                         tc::mbar_wait(&pv_done[s], (uint32_t)((i - 2) >> 1) & 1u, a.err) ? 1 : 0;
-                named_sync_softmax();
+                named_sync_out();
                 if (!sFlag[2 + s]) {
                     ok = false;
                     break;
                 }
                 tc::tc_fence_after();
             }
-#pragma unroll
-            for (int j = 0; j < 64; ++j) p[j] = f2s_round_tf32(p[j]);
-            const uint32_t pt = tmem + lane_base + kPCol + (uint32_t)(s * kKeyTile);
-            tc::tmem_st32(pt, *reinterpret_cast<float(*)[32]>(p));
-            tc::tmem_st32(pt + 32, *reinterpret_cast<float(*)[32]>(p + 32));
+            tc::tmem_st32(tmem + lane_base + kPCol + (uint32_t)(s * kKeyTile + k0), p);
             tc::tc_fence_before();
             tc::mbar_arrive(p_full);
         }
-        // wait for the last P V product, then write h - O / (den + 1e-9)
+        // wait for the last P V product, then write h - O / (den + 1e-9); the
+        // row sum adds the two halves' partial sums
         if (ok) {
-            if (row == 0)
+            sDen[half * kRows + row] = den;
+            if (stid == 0)
                 sFlag[4] = tc::mbar_wait(&pv_done[(nk - 1) & 1], (uint32_t)((nk - 1) >> 1) & 1u,
                                          a.err) ? 1 : 0;
-            named_sync_softmax();
+            named_sync_out();
             ok = sFlag[4] != 0;
+            den = sDen[row] + sDen[kRows + row];
         }
+        const int cw = C / 2;          // this thread's output columns [c_begin, c_begin + cw)
+        const int c_begin = half * cw;
         if (ok && a.tma_epi) {
             // the tile through shared memory: h (C / 32 boxes of 128 rows x
             // 32 floats, 128-byte swizzle) lands by TMA in the V buffers, which
@@ -545,7 +557,7 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
             // in place; one TMA store per box (rows past N are clipped)
             constexpr uint32_t kBox = kRows * 128;
             const int nbox = C / 32;
-            if (row == 0) {
+            if (stid == 0) {
                 bool go = true;
                 if (a.h) {
                     tc::mbar_arrive_expect_tx(h_full, nbox * kBox);
@@ -556,12 +568,12 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
                 }
                 sFlag[5] = go ? 1 : 0;
             }
-            named_sync_softmax();
+            named_sync_out();
             const bool go = sFlag[5] != 0;
             if (go) {
                 tc::tc_fence_after();
                 const float inv = 1.0f / (den + 1e-9f);
-                for (int c0 = 0; c0 < C; c0 += 32) {
+                for (int c0 = c_begin; c0 < c_begin + cw; c0 += 32) {
                     float o[32];
                     tc::tmem_ld32(tmem + lane_base + kOCol + (uint32_t)c0, o);
                     unsigned char* box = sV + (c0 / 32) * kBox;
@@ -582,8 +594,8 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
                 }
                 fence_proxy_async();
             }
-            named_sync_softmax();
-            if (row == 0 && go) {
+            named_sync_out();
+            if (stid == 0 && go) {
                 for (int j = 0; j < nbox; ++j) tma_store_3d(&map_out, sV + j * kBox, j * 32, q0, b);
                 bulk_commit_and_wait_read();
             }
@@ -592,7 +604,7 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
             const float inv = 1.0f / (den + 1e-9f);
             const int qrow = q0 + row;
             const size_t grow = (size_t)b * a.N + qrow;
-            for (int c0 = 0; c0 < C; c0 += 32) {
+            for (int c0 = c_begin; c0 < c_begin + cw; c0 += 32) {
                 float o[32];
                 tc::tmem_ld32(tmem + lane_base + kOCol + (uint32_t)c0, o);
                 if (qrow < a.N) {
@@ -646,7 +658,7 @@ int attention_tc(const float* q, const float* k, int ldqk, const float* v, int l
                  const float* h, int ldh, float* out, int ldo, float* workspace, int B, int N,
                  int d, int C, bool normalize_qk, bool round_tf32, cudaStream_t st) {
     if (B == 0 || N == 0) return F2S_OK;
-    if (d > kDPad || C % 32 != 0 || C > 256 || C < 32 || ldqk % 4 != 0 ||
+    if (d > kDPad || C % 64 != 0 || C > 256 || ldqk % 4 != 0 ||
         ((uintptr_t)q & 15) != 0 || ((uintptr_t)k & 15) != 0)
         return fail(F2S_ERR_UNSUPPORTED, "attention shape outside the tensor-core kernel");
     int* err = tc_error_word();
@@ -716,11 +728,12 @@ int attention_tc(const float* q, const float* k, int ldqk, const float* v, int l
         a.idesc_s = tc::make_idesc(kRows, kKeyTile, 1u);
         a.idesc_pv = tc::make_idesc(kRows, C, 2u);
         const size_t smem = 1024 + 2 * kRows * 128 + 2 * kKStages * kKeyTile * 128 + 4 * (size_t)C * 128 +
-                            (size_t)ceil_div(N, kKeyTile) * kKeyTile * 4 + 32 + 8 + 20 * 8 + 16;
+                            (size_t)ceil_div(N, kKeyTile) * kKeyTile * 4 + 32 + 2 * kRows * 4 + 8 +
+                            20 * 8 + 16;
         F2S_LIMIT(smem <= 227 * 1024, "attention_tc: %zu bytes of shared memory", smem);
         F2S_CUDA_TRY(cudaFuncSetAttribute(attn_tc_output_kernel,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        attn_tc_output_kernel<<<B * a.tiles, kThreads, smem, st>>>(
+        attn_tc_output_kernel<<<B * a.tiles, kOutThreads, smem, st>>>(
             map_hi_q, map_lo_q, map_hi_k, map_lo_k, map_vt, map_h, map_out, a);
         F2S_TRY(check_launch("attn_tc_output_kernel"));
     }
