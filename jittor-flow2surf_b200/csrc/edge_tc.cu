@@ -11,25 +11,35 @@
 // in-kernel bf16 conversion, 128-byte swizzle, K-major):
 //   warps 0-7   hidden producers, two lanes per edge row. The geometry g =
 //               [xyz_j - xyz_i, xyz_i] of the next tile is loaded while this
-//               tile is processed; the HPE LayerNorm statistics (E[h^2] -
-//               E[h]^2, eps 1e-5) of h = W_in g + b_in come from the Gram
-//               matrix of W_in (computed once per CTA) in O(36) instead of a
-//               pass over H. Once the A buffer is free (one or two buffers,
-//               whatever shared memory holds) they evaluate h with the
-//               LayerNorm and GELU and write the rows into the swizzled
-//               buffer; then one lane issues the MMAs (M = 128, N = C_out)
-//               into one of two TMEM accumulators and commits "A free" and
-//               "accumulator ready". Warp 0 owns the TMEM allocation.
+//               tile is processed. The HPE LayerNorm (eps 1e-5) rides on the
+//               pre-activation MMA: the per-channel mean of h = W_in g + b_in
+//               is linear in g, so with column-centred weights the centred,
+//               scaled and shifted h is one K = 8 product [gamma W~ | gamma b~
+//               | beta] . [rstd g | rstd | 1], and the variance is a quadratic
+//               form in g (the centred rows' 6 x 6 moment matrix, computed
+//               once per CTA): O(36) per edge row, no pass over H. Once the A
+//               buffer is free (one or two buffers, whatever shared memory
+//               holds) they apply GELU to the normalised pre-activations and
+//               write the rows into the swizzled buffer; then one lane issues
+//               the MMAs (M = 128, N = C_out) into one of two TMEM
+//               accumulators and commits "A free" and "accumulator ready".
+//               Warp 0 owns the TMEM allocation.
 //   warps 8-15  epilogue, two warps per TMEM lane quarter splitting the
 //               output channels: the message content[j] + content[i] +
-//               (acc + b_po) is formed once and written back to TMEM, the
-//               two-pass LayerNorm (eps 1e-6) reads only TMEM, and after the
+//               (acc + b_po) is formed once from content rows staged in
+//               shared memory by coalesced asynchronous copies (a chunk or a
+//               tile ahead; the rows two grid rounds ahead are prefetched into
+//               L2) and written back to TMEM with its moments about a
+//               per-warp shift (one pass, the channel halves combined
+//               pairwise); the LayerNorm (eps 1e-6) then reads only TMEM, and
+//               after the
 //               affine + LeakyReLU the max over each point's K edge rows (K
 //               lanes) is a register butterfly across lanes that leaves
 //               lane = channel, so the output row is stored coalesced.
 // So the hidden rows of tile t + 1 are computed while the epilogue of tile t
 // runs, and the MMAs overlap both. Each role has one polling lane per wait;
 // the role's other warps wait on a named barrier and issue nothing.
+#include <algorithm>
 #include <cfloat>
 #include <cstring>
 
@@ -58,6 +68,8 @@ struct EdgeTcArgs {
     int B, M, K, log2K, H, cout;
     int ppt;     // points per tile (128 / K)
     int a_bufs;  // hidden-row buffers (1 or 2)
+    int stage_bufs;   // content staging buffers per epilogue warp (1 .. 4)
+    int stage_bytes;  // bytes of one staging buffer: 32 neighbour rows + the warp's centre rows
     const float* hpe_w;
     const float* hpe_b;
     const float* hpe_ln_w;
@@ -83,6 +95,34 @@ __device__ __forceinline__ uint32_t sw128_offset(int row, int chunk) {
 
 __device__ __forceinline__ void fence_proxy_async() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// 16-byte global -> shared copy through L2 only (the content rows are read
+// once per tile), tracked per thread by commit groups.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+// Bring `bytes` (a multiple of 16) at a 16-byte aligned global address into L2.
+__device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ float4 lds128(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(addr)
+                 : "memory");
+    return v;
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// wait until at most `pending` (0 .. 3) of this thread's groups are in flight
+__device__ __forceinline__ void cp_async_wait(int pending) {
+    switch (pending) {
+        case 0: asm volatile("cp.async.wait_group 0;" ::: "memory"); break;
+        case 1: asm volatile("cp.async.wait_group 1;" ::: "memory"); break;
+        case 2: asm volatile("cp.async.wait_group 2;" ::: "memory"); break;
+        default: asm volatile("cp.async.wait_group 3;" ::: "memory"); break;
+    }
 }
 
 __device__ __forceinline__ void epi_barrier() {
@@ -152,15 +192,16 @@ edge_tc_kernel(const __grid_constant__ CUtensorMap map_w, const EdgeTcArgs a) {
     unsigned char* sA = smem;                               // a_bufs x a_buf_bytes
     unsigned char* sB = sA + (size_t)a.a_bufs * a_buf_bytes;
     unsigned char* sBlo = sB + b_bytes;
-    // the pre-activation contraction h = [W_in | b_in] [g ; 1] as a K = 8 tf32
-    // MMA in the interleaved (no-swizzle) K-major layout: A_u = 128 rows of
-    // [g0..g5, 1, 0], B_w = H rows of [w0..w5, b, 0], each as tf32 hi and lo
+    // the normalised pre-activations LN(W_in g + b_in) as a K = 8 tf32 MMA in
+    // the interleaved (no-swizzle) K-major layout: A_u = 128 rows of
+    // [rstd g0..g5, rstd, 1], B_w = H rows of [gamma W~ (6), gamma b~, beta]
+    // (column-centred weights), each as tf32 hi and lo
     unsigned char* sU = sBlo + (kSplit ? b_bytes : 0);  // 2 x 4 KB
     unsigned char* sWu = sU + 2 * kUBytes;               // 2 x H x 32 bytes
-    float* sHn = reinterpret_cast<float*>(sWu + 2 * (size_t)H * 32);  // H x {gain, shift}
+    float* sHn = reinterpret_cast<float*>(sWu + 2 * (size_t)H * 32);  // H x 2 floats of set-up scratch
     // LayerNorm moments of the pre-activations as functions of g:
     // sum = bsum + wsum . g, sum of squares = bsq + g . (2 u + G g)
-    float* sGram = sHn + H * 2;  // G[36], u[6], wsum[6], bsum, bsq (16-byte aligned)
+    float* sGram = sHn + H * 2;  // moments of the centred HPE rows: G[36], a[6], c (16-byte aligned)
     float* sCb = sGram + 52;                                              // cout
     float* sLn = sCb + cout;      // cout x {|gain|, shift}
     float* sSgn = sLn + cout * 2;  // cout: sign of the gain (+1 / -1)
@@ -179,6 +220,11 @@ edge_tc_kernel(const __grid_constant__ CUtensorMap map_w, const EdgeTcArgs a) {
     // read by every warp of the role after it
     int* sEpiFail = reinterpret_cast<int*>(tmem_slot + 1);
     int* sProdFail = sEpiFail + 1;  // [2]
+    // content staging of the epilogue warps: per warp `stage_bufs` buffers of
+    // 32 neighbour rows x 32 channels (128-byte rows, 16-byte chunks swizzled
+    // by row & 7) followed by the warp's centre rows (same swizzle by point)
+    unsigned char* sStage = reinterpret_cast<unsigned char*>(
+        (reinterpret_cast<uintptr_t>(sProdFail + 2) + 127) & ~uintptr_t(127));
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int R = a.B * a.M;
@@ -190,9 +236,30 @@ edge_tc_kernel(const __grid_constant__ CUtensorMap map_w, const EdgeTcArgs a) {
     const uint32_t pre_col = (uint32_t)(2 * cout);
 
     const int hh = H >> 1;
+    // The HPE LayerNorm is folded into the pre-activation contraction. The
+    // mean over the hidden channels of h = W_in g + b_in is linear in g, so
+    // with column-centred weights W~ = W_in - mean_c(W_in), b~ = b_in -
+    // mean_c(b_in), h - mean(h) = W~ g + b~ and
+    //   LN(h)_c = gamma_c rstd (W~_c g + b~_c) + beta_c
+    //           = [gamma_c W~_c | gamma_c b~_c | beta_c] . [rstd g | rstd | 1],
+    // a K = 8 row product whose u row carries the per-edge 1/std; the variance
+    // is g^T G g + 2 a.g + c with G, a, c the moments of the centred rows.
+    double* sMean = reinterpret_cast<double*>(sHn);  // 7 column means (sHn is 8-byte aligned)
+    if (tid < 7) {
+        double acc = 0.0;
+        for (int c = 0; c < H; ++c)
+            acc += tid < 6 ? (double)a.hpe_w[(size_t)c * 6 + tid] : (double)a.hpe_b[c];
+        sMean[tid] = acc / (double)H;
+    }
+    __syncthreads();
     for (int c = tid; c < H; c += kThreads) {
         const float* w = a.hpe_w + (size_t)c * 6;
-        const float row8[8] = {w[0], w[1], w[2], w[3], w[4], w[5], a.hpe_b[c], 0.0f};
+        const double gamma = a.hpe_ln_w[c];
+        float row8[8];
+#pragma unroll
+        for (int e = 0; e < 6; ++e) row8[e] = (float)(gamma * ((double)w[e] - sMean[e]));
+        row8[6] = (float)(gamma * ((double)a.hpe_b[c] - sMean[6]));
+        row8[7] = a.hpe_ln_b[c];
         float hi[8], lo[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
@@ -206,22 +273,24 @@ edge_tc_kernel(const __grid_constant__ CUtensorMap map_w, const EdgeTcArgs a) {
             *reinterpret_cast<float4*>(sWu + (size_t)H * 32 + off) =
                 make_float4(lo[4 * ch], lo[4 * ch + 1], lo[4 * ch + 2], lo[4 * ch + 3]);
         }
-        sHn[2 * c] = a.hpe_ln_w[c];
-        sHn[2 * c + 1] = a.hpe_ln_b[c];
     }
-    if (tid < 50) {
-        // 50 sums over the hidden channels, in double
+    if (tid < 43) {
+        // moments of the centred rows over the hidden channels, in double:
+        // G (36), a (6), c
         double acc = 0.0;
         for (int c = 0; c < H; ++c) {
             const float* w = a.hpe_w + (size_t)c * 6;
-            const double b = a.hpe_b[c];
-            if (tid < 36) acc += (double)w[tid / 6] * (double)w[tid % 6];
-            else if (tid < 42) acc += (double)w[tid - 36] * b;
-            else if (tid < 48) acc += (double)w[tid - 42];
-            else if (tid == 48) acc += b;
-            else acc += b * b;
+            const double bt = (double)a.hpe_b[c] - sMean[6];
+            if (tid < 36) {
+                const int d = tid / 6, e = tid % 6;
+                acc += ((double)w[d] - sMean[d]) * ((double)w[e] - sMean[e]);
+            } else if (tid < 42) {
+                acc += ((double)w[tid - 36] - sMean[tid - 36]) * bt;
+            } else {
+                acc += bt * bt;
+            }
         }
-        sGram[tid] = (float)acc;
+        sGram[tid] = (float)(acc / (double)H);
     }
     for (int c = tid; c < cout; c += kThreads) {
         sCb[c] = a.contrib_b[c];
@@ -299,9 +368,21 @@ edge_tc_kernel(const __grid_constant__ CUtensorMap map_w, const EdgeTcArgs a) {
                 xj = *reinterpret_cast<const float4*>(a.xyz4 + (size_t)jrow * 4);
             }
         }
-        // u = [g, 1, 0] of this row as tf32 hi / lo (the lanes of one half)
+        // u = [rstd g, rstd, 1] of this row as tf32 hi / lo (the lanes of one
+        // half), rstd = 1 / sqrt(var + 1e-5) of the row's pre-activations
         auto write_u = [&](const float4& pi, const float4& pj) {
-            const float u8[8] = {pj.x - pi.x, pj.y - pi.y, pj.z - pi.z, pi.x, pi.y, pi.z, 1.0f, 0.0f};
+            const float g[6] = {pj.x - pi.x, pj.y - pi.y, pj.z - pi.z, pi.x, pi.y, pi.z};
+            float var = sGram[42];
+#pragma unroll
+            for (int d = 0; d < 6; ++d) {
+                float t = 2.0f * sGram[36 + d];
+#pragma unroll
+                for (int e = 0; e < 6; ++e) t = fmaf(sGram[d * 6 + e], g[e], t);
+                var = fmaf(t, g[d], var);
+            }
+            const float rstd = rsqrtf(fmaxf(var, 0.0f) + 1e-5f);
+            const float u8[8] = {rstd * g[0], rstd * g[1], rstd * g[2], rstd * g[3],
+                                 rstd * g[4], rstd * g[5], rstd,        1.0f};
             float hi[8], lo[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
@@ -317,7 +398,8 @@ edge_tc_kernel(const __grid_constant__ CUtensorMap map_w, const EdgeTcArgs a) {
                     make_float4(lo[4 * ch], lo[4 * ch + 1], lo[4 * ch + 2], lo[4 * ch + 3]);
             }
         };
-        // pre = [W_in | b_in] [g ; 1] in 3xTF32 (hi hi + hi lo + lo hi) into TMEM
+        // pre = LN(W_in g + b_in) as the row product above, in 3xTF32 (hi hi +
+        // hi lo + lo hi), into TMEM
         auto issue_pre = [&]() {
             const uint32_t u0 = tc::smem_u32(sU), w0 = tc::smem_u32(sWu);
             const uint64_t du = tc::interleaved_desc(u0, 128, 256);
@@ -344,8 +426,6 @@ edge_tc_kernel(const __grid_constant__ CUtensorMap map_w, const EdgeTcArgs a) {
         bool weights_ready = !kTf32;
         int it = 0;
         for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
-            const float g[6] = {xj.x - xi.x, xj.y - xi.y, xj.z - xi.z, xi.x, xi.y, xi.z};
-            const bool cur_valid = valid;
             const bool has_next = tile + (int)gridDim.x < n_tiles;
             // next tile: neighbour index and centre point now, the neighbour
             // point after the wait below
@@ -356,20 +436,6 @@ edge_tc_kernel(const __grid_constant__ CUtensorMap map_w, const EdgeTcArgs a) {
                 nidx = a.idx[(size_t)np * K + kk];
                 xi = *reinterpret_cast<const float4*>(a.xyz4 + (size_t)np * 4);
             }
-            // LayerNorm moments of the pre-activations W_in g + b_in from the
-            // Gram matrix of W_in: no pass over the H channels
-            float s = sGram[48], s2 = sGram[49];
-#pragma unroll
-            for (int d = 0; d < 6; ++d) {
-                float t = 2.0f * sGram[36 + d];
-#pragma unroll
-                for (int e = 0; e < 6; ++e) t = fmaf(sGram[d * 6 + e], g[e], t);
-                s2 = fmaf(t, g[d], s2);
-                s = fmaf(sGram[42 + d], g[d], s);
-            }
-            const float mean = s / (float)H;
-            const float var = fmaxf(s2 / (float)H - mean * mean, 0.0f);
-            const float rstd = rsqrtf(var + 1e-5f);
             // wait until the MMAs of the tile that last used this A buffer are
             // done and this tile's pre-activations are in TMEM; one lane polls,
             // the other producer warps wait on the named barrier
@@ -385,7 +451,9 @@ edge_tc_kernel(const __grid_constant__ CUtensorMap map_w, const EdgeTcArgs a) {
             if (valid) xj = *reinterpret_cast<const float4*>(
                            a.xyz4 + (size_t)((np / a.M) * a.M + nidx) * 4);
             unsigned char* dA = sA + (size_t)abuf * a_buf_bytes;
-            // GELU(LN(pre)), packed as the main MMA reads it
+            // GELU of the normalised pre-activations, packed as the main MMA
+            // reads it (rows past the end hold finite values the epilogue
+            // ignores)
             for (int c0 = 0; c0 < hh; c0 += 32) {
                 float v[32];
                 tc::tmem_ld32(tmem_base + t_lane + pre_col + (uint32_t)(ch0 + c0), v);
@@ -393,11 +461,7 @@ edge_tc_kernel(const __grid_constant__ CUtensorMap map_w, const EdgeTcArgs a) {
                 for (int i0 = 0; i0 < 32; i0 += kPer) {
                     float o[kPer];
 #pragma unroll
-                    for (int e = 0; e < kPer; e += 2) {
-                        const float4 gs = *reinterpret_cast<const float4*>(sHn + 2 * (ch0 + c0 + i0 + e));
-                        o[e] = cur_valid ? gelu_as((v[i0 + e] - mean) * rstd * gs.x + gs.y) : 0.0f;
-                        o[e + 1] = cur_valid ? gelu_as((v[i0 + e + 1] - mean) * rstd * gs.z + gs.w) : 0.0f;
-                    }
+                    for (int e = 0; e < kPer; ++e) o[e] = gelu_as(v[i0 + e]);
                     const int c = ch0 + c0 + i0;
                     unsigned char* dst =
                         dA + (size_t)(c / kBk) * kRows * 128 + sw128_offset(row, (c % kBk) / kPer);
@@ -480,10 +544,75 @@ edge_tc_kernel(const __grid_constant__ CUtensorMap map_w, const EdgeTcArgs a) {
         const int cpart = (warp - kEpiWarp0) >> 2;
         const int erow = quarter * 32 + lane;  // TMEM lane = edge row
         const int nchunks = cout / 32;
+        const int kk = erow & (K - 1);
+        const int ptw = lane >> a.log2K;    // point of this lane's edge row within the warp
+        const int ppw = 32 >> a.log2K;      // points whose edge rows the warp holds
+        // this warp's 32-channel chunks of a tile: cpart, cpart + 2, ...
+        const int nmine = (nchunks - cpart + 1) >> 1;
+        const int nbuf = a.stage_bufs < nmine ? a.stage_bufs : nmine;
+        const uint32_t stage =
+            tc::smem_u32(sStage) + (uint32_t)((warp - kEpiWarp0) * a.stage_bufs * a.stage_bytes);
+        // neighbour row of this lane's edge row in tile t (-1 past the end)
+        auto neighbour_row = [&](int t) -> int {
+            const int p = t * a.ppt + (erow >> a.log2K);
+            if (t >= n_tiles || p >= R) return -1;
+            return (p / a.M) * a.M + a.idx[(size_t)p * K + kk];
+        };
+        int jcur = neighbour_row(blockIdx.x);
+        int jnext = neighbour_row(blockIdx.x + gridDim.x);
         int it = 0;
+        // Stage this warp's k-th chunk of tile `tile_s` (the current tile, or
+        // the next one when `next`) into buffer b with coalesced 16-byte
+        // copies: eight lanes per 128-byte row segment, four rows per
+        // instruction, so a warp instruction touches 4 lines instead of 32.
+        // One commit group per chunk (empty past the last tile), so `nbuf`
+        // groups are always in flight before a wait.
+        auto issue = [&](int tile_s, bool next, int k, int b) {
+            if (tile_s < n_tiles) {
+                const int ch = cpart + 2 * k;
+                const int jl = max(next ? jnext : jcur, 0);
+                const uint32_t buf = stage + (uint32_t)(b * a.stage_bytes);
+                const int q = lane & 7;
+                const float* src = a.content + ch * 32 + q * 4;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const int r = 4 * i + (lane >> 3);
+                    const int j = __shfl_sync(kFull, jl, r);
+                    cp_async16(buf + (uint32_t)(r * 128 + ((q ^ (r & 7)) << 4)), src + (size_t)j * a.ldc);
+                }
+                const int pbase = tile_s * a.ppt + ((quarter * 32) >> a.log2K);
+                for (int i = lane; i < ppw * 8; i += 32) {
+                    const int pt = i >> 3, qq = i & 7;
+                    const int p = pbase + pt < R ? pbase + pt : 0;
+                    cp_async16(buf + (uint32_t)(4096 + pt * 128 + ((qq ^ (pt & 7)) << 4)),
+                               a.content + (size_t)p * a.ldc + cout + ch * 32 + qq * 4);
+                }
+            }
+            cp_async_commit();
+        };
+        // The content rows of a patch are first read by the tiles of that
+        // patch in the same grid round, from DRAM when the matrix exceeds L2;
+        // each CTA brings the rows of its points two rounds ahead into L2 (the
+        // points of a round span a patch or more, so a patch's rows are in L2
+        // before its tiles gather them).
+        auto prefetch_rows = [&](int t) {
+            if (t < n_tiles) {
+                const int p = t * a.ppt;
+                const int n = min(a.ppt, R - p);
+                prefetch_l2(a.content + (size_t)p * a.ldc, (uint32_t)(n * a.ldc * 4));
+            }
+        };
+        if (warp == kEpiWarp0 && lane == 0) {
+            prefetch_rows(blockIdx.x);
+            prefetch_rows(blockIdx.x + gridDim.x);
+        }
+        if (nmine > 0)
+            for (int k = 0; k < nbuf; ++k) issue(blockIdx.x, false, k, k);
+        int cons = 0;  // buffer of the next chunk to consume
         for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
             const int tbuf = it & 1;
             const uint32_t tph = (uint32_t)(it >> 1) & 1u;
+            if (warp == kEpiWarp0 && lane == 0) prefetch_rows(tile + 2 * (int)gridDim.x);
             // one lane polls, the other epilogue warps wait on the named
             // barrier; the flag is next written after two more barriers of
             // this tile, so every warp reads this tile's decision
@@ -492,55 +621,70 @@ edge_tc_kernel(const __grid_constant__ CUtensorMap map_w, const EdgeTcArgs a) {
             epi_barrier();
             if (*reinterpret_cast<volatile int*>(sEpiFail)) break;
             tc::tc_fence_after();
-            const int p0 = tile * a.ppt;
-            const int ep = p0 + (erow >> a.log2K);
-            int ej = -1;
-            if (ep < R) {
-                const int kk = erow & (K - 1);
-                ej = (ep / a.M) * a.M + a.idx[(size_t)ep * K + kk];
-            }
+            const int ep = tile * a.ppt + (erow >> a.log2K);
+            const int ej = jcur;
             const uint32_t taddr =
                 tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(tbuf * cout);
-            const float* cj = a.content + (size_t)(ej < 0 ? 0 : ej) * a.ldc;
-            // centre terms: one point per K consecutive lanes, mostly a broadcast
-            const float* ci = a.content + (size_t)(ej < 0 ? 0 : ep) * a.ldc + cout;
-            // pass 1: message = content[j] + content[i] + (acc + b_po) -> TMEM
-            float sum = 0.0f;
-            for (int ch = cpart; ch < nchunks; ch += 2) {
-                const int cb = ch * 32;
+            // pass 1: message = content[j] + content[i] + (acc + b_po) -> TMEM,
+            // content rows from the staging buffers, with the moments of this
+            // warp's channels taken about the mean of its first chunk (one
+            // pass; the two channel halves are combined below)
+            float shift = 0.0f, s1 = 0.0f, s2 = 0.0f;
+            for (int k = 0; k < nmine; ++k) {
+                const int cb = (cpart + 2 * k) * 32;
+                uint32_t r[32];
+                tc::tmem_ld32_issue(taddr + (uint32_t)cb, r);
+                cp_async_wait(nbuf - 1);
+                __syncwarp();  // every lane's copies of this chunk have landed
+                const uint32_t buf = stage + (uint32_t)(cons * a.stage_bytes);
+                const uint32_t rj = buf + (uint32_t)(lane * 128);
+                const uint32_t ri = buf + (uint32_t)(4096 + ptw * 128);
+                tc::tmem_ld32_wait(r);
                 float v[32];
-                tc::tmem_ld32(taddr + (uint32_t)cb, v);
+                float csum = 0.0f;
 #pragma unroll
                 for (int i = 0; i < 32; i += 4) {
-                    const float4 nj = *reinterpret_cast<const float4*>(cj + cb + i);
-                    const float4 ni = *reinterpret_cast<const float4*>(ci + cb + i);
+                    const float4 nj = lds128(rj + (uint32_t)(((i >> 2) ^ (lane & 7)) << 4));
+                    const float4 ni = lds128(ri + (uint32_t)(((i >> 2) ^ (ptw & 7)) << 4));
                     const float4 bb = *reinterpret_cast<const float4*>(sCb + cb + i);
-                    v[i + 0] = nj.x + ni.x + (v[i + 0] + bb.x);
-                    v[i + 1] = nj.y + ni.y + (v[i + 1] + bb.y);
-                    v[i + 2] = nj.z + ni.z + (v[i + 2] + bb.z);
-                    v[i + 3] = nj.w + ni.w + (v[i + 3] + bb.w);
-                    sum += (v[i] + v[i + 1]) + (v[i + 2] + v[i + 3]);
+                    v[i + 0] = nj.x + ni.x + (__uint_as_float(r[i + 0]) + bb.x);
+                    v[i + 1] = nj.y + ni.y + (__uint_as_float(r[i + 1]) + bb.y);
+                    v[i + 2] = nj.z + ni.z + (__uint_as_float(r[i + 2]) + bb.z);
+                    v[i + 3] = nj.w + ni.w + (__uint_as_float(r[i + 3]) + bb.w);
+                    if (k == 0) csum += (v[i] + v[i + 1]) + (v[i + 2] + v[i + 3]);
                 }
-                tc::tmem_st32(taddr + (uint32_t)cb, v);
-            }
-            sStat[cpart * kRows + erow] = sum;
-            epi_barrier();
-            const float mean = (sStat[erow] + sStat[kRows + erow]) / (float)cout;
-            // pass 2: centred second moment
-            float q2 = 0.0f;
-            for (int ch = cpart; ch < nchunks; ch += 2) {
-                float v[32];
-                tc::tmem_ld32(taddr + (uint32_t)(ch * 32), v);
+                tc::tmem_st32_async(taddr + (uint32_t)cb, v);
+                if (k == 0) shift = csum * (1.0f / 32.0f);
 #pragma unroll
                 for (int i = 0; i < 32; ++i) {
-                    const float d = v[i] - mean;
-                    q2 = fmaf(d, d, q2);
+                    const float d = v[i] - shift;
+                    s1 += d;
+                    s2 = fmaf(d, d, s2);
                 }
+                __syncwarp();  // the buffer has been read: refill it
+                const int kn = k + nbuf;
+                if (kn < nmine) issue(tile, false, kn, cons);
+                else issue(tile + (int)gridDim.x, true, kn - nmine, cons);
+                cons = cons + 1 == nbuf ? 0 : cons + 1;
             }
-            sStat[(2 + cpart) * kRows + erow] = q2;
+            {
+                // this half's mean and centred sum of squares (Chan et al.'s
+                // pairwise update combines the halves)
+                const float n_p = (float)(32 * nmine);
+                const float m_p = nmine > 0 ? shift + s1 / n_p : 0.0f;
+                const float q_p = nmine > 0 ? fmaxf(s2 - s1 * (s1 / n_p), 0.0f) : 0.0f;
+                sStat[(2 * cpart) * kRows + erow] = m_p;
+                sStat[(2 * cpart + 1) * kRows + erow] = q_p;
+            }
+            tc::tmem_st_wait();  // the messages are in TMEM before pass 3 reads them
             epi_barrier();
-            const float rstd =
-                rsqrtf((sStat[2 * kRows + erow] + sStat[3 * kRows + erow]) / (float)cout + 1e-6f);
+            const float n0 = (float)(32 * ((nchunks + 1) >> 1)), n1 = (float)(32 * (nchunks >> 1));
+            const float m0 = sStat[erow], q0 = sStat[kRows + erow];
+            const float m1 = sStat[2 * kRows + erow], q1 = sStat[3 * kRows + erow];
+            const float dm = m1 - m0;
+            const float mean = m0 + dm * (n1 / (float)cout);
+            const float m2 = q0 + q1 + dm * dm * (n0 * n1 / (float)cout);
+            const float rstd = rsqrtf(m2 / (float)cout + 1e-6f);
             const float nmr = -mean * rstd;
             // pass 3: max over the K lanes of each point of the normalised value,
             // then the affine + LeakyReLU once per point and channel. Both are
@@ -609,7 +753,10 @@ edge_tc_kernel(const __grid_constant__ CUtensorMap map_w, const EdgeTcArgs a) {
             }
             tc::tc_fence_before();
             tc::mbar_arrive(&t_empty[tbuf]);
+            jcur = jnext;
+            jnext = neighbour_row(tile + 2 * (int)gridDim.x);
         }
+        cp_async_wait(0);  // no copy into shared memory outlives the loop
     }
     tc::tc_fence_before();
     __syncthreads();
@@ -619,14 +766,15 @@ edge_tc_kernel(const __grid_constant__ CUtensorMap map_w, const EdgeTcArgs a) {
     }
 }
 
-// Shared memory of the kernel for `bufs` hidden-row buffers.
-size_t edge_tc_smem(int mode, int H, int cout, int bufs) {
+// Shared memory of the kernel for `bufs` hidden-row buffers and `stage_bufs`
+// content staging buffers of `stage_bytes` per epilogue warp.
+size_t edge_tc_smem(int mode, int H, int cout, int bufs, int stage_bufs, int stage_bytes) {
     const int elem = mode == kModeTf32 ? 4 : 2;
     const size_t kblocks = (size_t)ceil_div(H, 128 / elem);
     const size_t copies = mode == kModeSplit ? 2 : 1;
     return 1024 + copies * kblocks * 128 * ((size_t)bufs * kRows + cout) + 2 * (size_t)kUBytes +
            2 * (size_t)H * 32 + sizeof(float) * ((size_t)H * 2 + 52 + (size_t)cout * 4 + 4 * kRows) +
-           128;
+           128 + 128 + (size_t)kEpilogueWarps * stage_bufs * stage_bytes;
 }
 
 }  // namespace
@@ -657,14 +805,22 @@ int edge_stage_tc(const EdgeArgs& e, int precision, cudaStream_t st) {
     CUtensorMap map;
     if (tf32) F2S_TRY(make_tensor_map_2d(&map, e.contrib_w, true, e.cout, e.H, e.H, e.cout, bk));
     else memset(&map, 0, sizeof(map));
+    // shared memory: as many content staging buffers per epilogue warp as
+    // the warp has chunks per tile (at most 4), then two hidden-row buffers
+    // if they still fit
     constexpr size_t kSmemLimit = 227 * 1024;
-    int bufs = 2;
-    size_t smem = edge_tc_smem(mode, e.H, e.cout, bufs);
-    if (smem > kSmemLimit) {
-        bufs = 1;
-        smem = edge_tc_smem(mode, e.H, e.cout, bufs);
-    }
-    F2S_LIMIT(smem <= kSmemLimit, "edge_tc: %zu bytes of shared memory", smem);
+    const int stage_bytes = 4096 + (32 / e.K) * 128;
+    const int stage_max = std::min((e.cout / 32 + 1) / 2, 4);
+    int bufs = 0, stage_bufs = 0;
+    size_t smem = 0;
+    for (int sb = stage_max; sb >= 1 && bufs == 0; --sb)
+        for (int ab = 2; ab >= 1 && bufs == 0; --ab)
+            if (edge_tc_smem(mode, e.H, e.cout, ab, sb, stage_bytes) <= kSmemLimit) {
+                bufs = ab;
+                stage_bufs = sb;
+                smem = edge_tc_smem(mode, e.H, e.cout, ab, sb, stage_bytes);
+            }
+    if (bufs == 0) return fail(F2S_ERR_UNSUPPORTED, "edge_tc: shape needs more shared memory");
     EdgeTcArgs a{};
     a.content = e.content;
     a.ldc = e.ldc;
@@ -678,6 +834,8 @@ int edge_stage_tc(const EdgeArgs& e, int precision, cudaStream_t st) {
     a.cout = e.cout;
     a.ppt = kRows / e.K;
     a.a_bufs = bufs;
+    a.stage_bufs = stage_bufs;
+    a.stage_bytes = stage_bytes;
     a.hpe_w = e.hpe_w;
     a.hpe_b = e.hpe_b;
     a.hpe_ln_w = e.hpe_ln_w;
