@@ -311,6 +311,103 @@ __global__ void input_embed_kernel(const float* __restrict__ x, int B, int M,
     }
 }
 
+// The same input embedding with one point per lane: the S0 hidden values of
+// the lane's point stay in registers and every weight is a warp-wide
+// broadcast read from shared memory (a float4 per four multiply-adds), so
+// the S0 x S0 output projection runs at the FMA rate. S0 <= S, channels past
+// S0 predicated off. Per output channel the projection accumulates in the
+// same order as input_embed_kernel (ob[c] + sum over hh = 0, 1, ...).
+template <int S>
+__global__ void __launch_bounds__(256, 1)
+input_embed_lane_kernel(const float* __restrict__ x, int B, int M, const float* __restrict__ w,
+                        const float* __restrict__ bia, const float* __restrict__ lnw,
+                        const float* __restrict__ lnb, const float* __restrict__ ow,
+                        const float* __restrict__ ob, int S0, float* __restrict__ xyz4,
+                        float* __restrict__ feat) {
+    extern __shared__ __align__(16) float sm[];
+    float* sOw = sm;                    // [S][S]: row c = output channel, zero-padded
+    float* sW = sOw + S * S;            // [S][4]: w0, w1, w2, bias
+    float* sLn = sW + 4 * S;            // [S][2]: gain, shift
+    float* sOb = sLn + 2 * S;           // [S]
+    for (int i = threadIdx.x; i < S * S; i += blockDim.x) {
+        const int c = i / S, hh = i - c * S;
+        sOw[i] = (c < S0 && hh < S0) ? ow[c * S0 + hh] : 0.0f;
+    }
+    for (int c = threadIdx.x; c < S; c += blockDim.x) {
+        const bool on = c < S0;
+        sW[4 * c + 0] = on ? w[c * 3 + 0] : 0.0f;
+        sW[4 * c + 1] = on ? w[c * 3 + 1] : 0.0f;
+        sW[4 * c + 2] = on ? w[c * 3 + 2] : 0.0f;
+        sW[4 * c + 3] = on ? bia[c] : 0.0f;
+        sLn[2 * c] = on ? lnw[c] : 0.0f;
+        sLn[2 * c + 1] = on ? lnb[c] : 0.0f;
+        sOb[c] = on ? ob[c] : 0.0f;
+    }
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int R = B * M;
+    for (int p0 = (blockIdx.x * 8 + warp) * 32; p0 < R; p0 += gridDim.x * 8 * 32) {
+        const int p = p0 + lane;
+        const bool ok = p < R;
+        float x0 = 0.0f, x1 = 0.0f, x2 = 0.0f;
+        if (ok) {
+            const int b = p / M, m = p - b * M;
+            const float* xb = x + (size_t)b * 3 * M;
+            x0 = xb[m];
+            x1 = xb[M + m];
+            x2 = xb[2 * M + m];
+            *reinterpret_cast<float4*>(xyz4 + (size_t)p * 4) = make_float4(x0, x1, x2, 0.0f);
+        }
+        float h[S];
+        float s = 0.0f, s2 = 0.0f;
+#pragma unroll
+        for (int c = 0; c < S; ++c) {
+            const float4 wc = *reinterpret_cast<const float4*>(sW + 4 * c);
+            float v = wc.w;
+            v = fmaf(wc.x, x0, v);
+            v = fmaf(wc.y, x1, v);
+            v = fmaf(wc.z, x2, v);
+            h[c] = v;
+            if (c < S0) {
+                s += v;
+                s2 = fmaf(v, v, s2);
+            }
+        }
+        const float mean = s / (float)S0;
+        const float var = fmaxf(s2 / (float)S0 - mean * mean, 0.0f);
+        const float rstd = rsqrtf(var + 1e-5f);
+#pragma unroll
+        for (int c = 0; c < S; ++c) {
+            const float2 g = *reinterpret_cast<const float2*>(sLn + 2 * c);
+            h[c] = f2s_gelu_erf((h[c] - mean) * rstd * g.x + g.y);  // padded channels: gain 0
+        }
+        if (!ok) continue;
+        float* fr = feat + (size_t)p * S0;
+        for (int c = 0; c < S0; c += 4) {
+            float o[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float* wr = sOw + (c + e) * S;
+                float v = sOb[c + e];
+#pragma unroll
+                for (int hh = 0; hh < S; hh += 4) {
+                    const float4 q = *reinterpret_cast<const float4*>(wr + hh);
+                    v = fmaf(q.x, h[hh], v);
+                    v = fmaf(q.y, h[hh + 1], v);
+                    v = fmaf(q.z, h[hh + 2], v);
+                    v = fmaf(q.w, h[hh + 3], v);
+                }
+                o[e] = v;
+            }
+            if (c + 4 <= S0 && (S0 & 3) == 0) {
+                *reinterpret_cast<float4*>(fr + c) = make_float4(o[0], o[1], o[2], o[3]);
+            } else {
+                for (int e = 0; e < 4 && c + e < S0; ++e) fr[c + e] = o[e];
+            }
+        }
+    }
+}
+
 GemmArgs gemm_args(const float* A, int lda, const float* W, const float* bias, float* Y, int ldy,
                    int rows, int cols, int K) {
     GemmArgs g{};
@@ -418,7 +515,25 @@ int forward(const Dims& d, const Layout& L, const float* P, const float* x_in, c
         F2S_TRY(check_launch("cond_mod_kernel"));
     }
     // input embedding + xyz
-    {
+    if (d.sd[0] <= 64) {
+        const int S0 = d.sd[0];
+        TraceScope trace(kTagInputEmbed, st);
+        const int warps = ceil_div(R, 32);
+        const int blocks = ceil_div(warps, 8);
+        const int grid = blocks < 4 * sm_count() ? blocks : 4 * sm_count();
+        auto launch = [&](auto kernel, int S) -> int {
+            const size_t smem = sizeof(float) * ((size_t)S * S + 7 * (size_t)S);
+            F2S_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              (int)smem));
+            kernel<<<grid, 256, smem, st>>>(x_in, B, M, P + L.in_w, P + L.in_b, P + L.in_ln_w,
+                                            P + L.in_ln_b, P + L.in_out_w, P + L.in_out_b, S0,
+                                            w.xyz4, w.feat0);
+            return check_launch("input_embed_lane_kernel");
+        };
+        if (S0 <= 16) F2S_TRY(launch(input_embed_lane_kernel<16>, 16));
+        else if (S0 <= 32) F2S_TRY(launch(input_embed_lane_kernel<32>, 32));
+        else F2S_TRY(launch(input_embed_lane_kernel<64>, 64));
+    } else {
         const int S0 = d.sd[0];
         const size_t smem = sizeof(float) * ((size_t)S0 * S0 + 8 * S0);
         F2S_CUDA_TRY(cudaFuncSetAttribute(input_embed_kernel,
