@@ -13,11 +13,17 @@
 //   - one CTA per (patch, 64 queries); the patch's features and per-point
 //     squared norms are staged once in shared memory;
 //   - one warp per query: each lane holds ceil(N/32) keys in registers;
-//   - the k-th smallest key is found exactly by a 4-pass, 8-bit radix select
-//     over a per-warp shared-memory histogram; keys below it and the
-//     lowest-index ties are compacted in index order with ballots; the <= 32
-//     survivors are sorted by a warp bitonic network and written coalesced.
-// Work per query is O(N/32 + 4*256/32 + k log^2 k) lane steps instead of the
+//   - a candidate filter: the k-th smallest of the 64 minima of half-lane
+//     slot groups bounds the k-th key from above; the (typically ~50) keys at
+//     or below it are compacted with ballots and sorted as (key, index)
+//     pairs by a 64-wide warp bitonic network, whose first k are the answer;
+//   - when more than 64 keys pass, the k-th smallest key is found exactly by
+//     a 4-pass, 8-bit radix select over a per-warp shared-memory histogram;
+//     keys below it and the lowest-index ties are compacted in index order
+//     with ballots; the <= 32 survivors are sorted by a warp bitonic network
+//     and written coalesced.
+// Work per query is O(N/32 + log^2 64) lane steps on the filter path (plus
+// 4*256/32 on the radix path) instead of the
 // reference's k block-wide reductions.
 #include "common.cuh"
 
@@ -46,6 +52,38 @@ __device__ __forceinline__ uint64_t warp_bitonic_sort_u64(uint64_t v, int lane) 
     return v;
 }
 
+// Ascending bitonic sort of 64 values held two per lane (element lane and
+// element 32 + lane).
+template <typename T>
+__device__ __forceinline__ void warp_bitonic_sort64(T& v0, T& v1, int lane) {
+#pragma unroll
+    for (int size = 2; size <= 64; size <<= 1) {
+#pragma unroll
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            if (stride == 32) {  // elements lane and 32 + lane; size 64 sorts ascending
+                const T lo = v1 < v0 ? v1 : v0;
+                const T hi = v1 < v0 ? v0 : v1;
+                v0 = lo;
+                v1 = hi;
+            } else {
+                const bool lower = (lane & stride) == 0;
+                {
+                    const T other = __shfl_xor_sync(kFull, v0, stride);
+                    const bool asc = (lane & size) == 0;  // element index lane
+                    const T lo = other < v0 ? other : v0, hi = other < v0 ? v0 : other;
+                    v0 = (lower == asc) ? lo : hi;
+                }
+                {
+                    const T other = __shfl_xor_sync(kFull, v1, stride);
+                    const bool asc = ((32 + lane) & size) == 0;  // element index 32 + lane
+                    const T lo = other < v1 ? other : v1, hi = other < v1 ? v1 : other;
+                    v1 = (lower == asc) ? lo : hi;
+                }
+            }
+        }
+    }
+}
+
 // CFIX = 3 specialises the channel loop for xyz; CFIX = 0 takes C at run time.
 template <int SLOTS, int CFIX>
 __global__ void __launch_bounds__(kWarps * 32)
@@ -57,7 +95,7 @@ knn_kernel(const float* __restrict__ features, int C_runtime, int N, int k, int 
     float* s_norm = reinterpret_cast<float*>(smem_raw);
     uint32_t* s_hist = reinterpret_cast<uint32_t*>(s_norm + n_pad);
     uint64_t* s_list = reinterpret_cast<uint64_t*>(s_hist + kWarps * 256);
-    float* s_feat = reinterpret_cast<float*>(s_list + kWarps * 32);
+    float* s_feat = reinterpret_cast<float*>(s_list + kWarps * 64);
 
     const int b = blockIdx.x / tiles_per_patch;
     const int tile = blockIdx.x - b * tiles_per_patch;
@@ -79,7 +117,8 @@ knn_kernel(const float* __restrict__ features, int C_runtime, int N, int k, int 
     const int lane = threadIdx.x & 31;
     const unsigned lanes_below = (1u << lane) - 1u;
     uint32_t* hist = s_hist + warp * 256;
-    uint64_t* list = s_list + warp * 32;
+    uint64_t* list = s_list + warp * 64;  // selected keys (32) or filter candidates (64)
+    uint64_t* cl = list;
 
     const int q_begin = tile * kQueriesPerCta;
     const int q_end = min(N, q_begin + kQueriesPerCta);
@@ -111,6 +150,48 @@ knn_kernel(const float* __restrict__ features, int C_runtime, int N, int k, int 
                 kk = f2s_ordered_bits(d);
             }
             key[r] = kk;
+        }
+
+        // Candidate filter. Each lane's slots form two groups; the
+        // actual_k-th smallest of the 64 group minima is a key T with at
+        // least actual_k distinct elements at or below it, so every selected
+        // element has key <= T (ties at T included). Typically ~5% of the
+        // keys pass; up to 64 candidates are sorted as (key, index) pairs,
+        // which is the final order, and more fall back to the radix select.
+        {
+            uint32_t g0 = 0xffffffffu, g1 = 0xffffffffu;
+#pragma unroll
+            for (int r = 0; r < SLOTS; ++r) {
+                const int j = r * 32 + lane;
+                const uint32_t kv = (j < N && j != q) ? key[r] : 0xffffffffu;
+                if (r < SLOTS / 2) g0 = kv < g0 ? kv : g0;
+                else g1 = kv < g1 ? kv : g1;
+            }
+            warp_bitonic_sort64<uint32_t>(g0, g1, lane);
+            const int src = actual_k - 1;  // element index of the threshold (< 32)
+            const uint32_t T = __shfl_sync(kFull, g0, src);
+            int c = 0;
+#pragma unroll
+            for (int r = 0; r < SLOTS; ++r) {
+                const int j = r * 32 + lane;
+                const bool cand = j < N && j != q && key[r] <= T;
+                const unsigned m = __ballot_sync(kFull, cand);
+                const int pos = c + __popc(m & lanes_below);
+                if (cand && pos < 64) cl[pos] = ((uint64_t)key[r] << 32) | (uint32_t)j;
+                c += __popc(m);
+            }
+            if (c <= 64) {
+                __syncwarp();
+                uint64_t v0 = lane < c ? cl[lane] : ~0ull;
+                uint64_t v1 = lane + 32 < c ? cl[lane + 32] : ~0ull;
+                __syncwarp();
+                warp_bitonic_sort64<uint64_t>(v0, v1, lane);
+                const int idx = (int)(uint32_t)(v0 & 0xffffffffu);
+                const int last = __shfl_sync(kFull, idx, actual_k - 1);
+                if (lane < k) out[((size_t)b * N + q) * k + lane] = lane < actual_k ? idx : last;
+                continue;
+            }
+            __syncwarp();
         }
 
         // Exact radix select of the actual_k-th smallest key among valid ones.
@@ -203,7 +284,7 @@ template <int SLOTS, int CFIX>
 int launch_knn(const float* features, int B, int C, int N, int k, int actual_k, int32_t* out,
                cudaStream_t stream) {
     const int n_pad = (N + 3) & ~3;
-    const size_t smem = (size_t)n_pad * 4 + (size_t)kWarps * 256 * 4 + (size_t)kWarps * 32 * 8 +
+    const size_t smem = (size_t)n_pad * 4 + (size_t)kWarps * 256 * 4 + (size_t)kWarps * 64 * 8 +
                         (size_t)C * N * 4;
     auto kernel = knn_kernel<SLOTS, CFIX>;
     if (smem > 48 * 1024)
