@@ -152,7 +152,8 @@ knn_kernel(const float* __restrict__ features, int C_runtime, int N, int k, int 
             key[r] = kk;
         }
 
-        // Candidate filter. Each lane's slots form two groups; the
+        // Candidate filter. Each lane's slots form two groups (even and odd
+        // slots); the
         // actual_k-th smallest of the 64 group minima is a key T with at
         // least actual_k distinct elements at or below it, so every selected
         // element has key <= T (ties at T included). Typically ~5% of the
@@ -164,7 +165,9 @@ knn_kernel(const float* __restrict__ features, int C_runtime, int N, int k, int 
             for (int r = 0; r < SLOTS; ++r) {
                 const int j = r * 32 + lane;
                 const uint32_t kv = (j < N && j != q) ? key[r] : 0xffffffffu;
-                if (r < SLOTS / 2) g0 = kv < g0 ? kv : g0;
+                // even / odd slots: both groups sample every part of the index
+                // range (patch points are stored in radial order)
+                if ((r & 1) == 0) g0 = kv < g0 ? kv : g0;
                 else g1 = kv < g1 ? kv : g1;
             }
             warp_bitonic_sort64<uint32_t>(g0, g1, lane);
