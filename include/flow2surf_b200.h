@@ -134,9 +134,12 @@ int f2s_linear(const void* x, int ldx, const void* weight, const float* bias, fl
                int rows, int cols, int K, int precision, void* stream);
 
 /*
- * The library's device error word: non-zero when a tensor-core kernel gave up
- * on a bounded wait (it then returned without finishing its tile). Copies it
- * to *value (synchronising `stream`) and clears it when `reset` is non-zero.
+ * The library's device error word: 1 when a tensor-core kernel gave up on a
+ * bounded wait (it then returned without finishing its tile), 2 when an fp16
+ * intermediate of the tf32 trunk (the FFN hidden rows, which keep tf32's
+ * 10-bit mantissa in half the bytes) was out of the fp16 range; 0 otherwise.
+ * Copies it to *value (synchronising `stream`) and clears it when `reset` is
+ * non-zero. The Python denoise entry points check it after every denoise.
  */
 int f2s_device_error(int* value, int reset, void* stream);
 

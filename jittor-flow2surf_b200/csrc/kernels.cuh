@@ -34,6 +34,11 @@ struct GemmArgs {
     GemmEpilogue epilogue;
     int tag;               // TraceTag of this launch
     bool round_tf32;       // tensor-core path: round fp32 outputs to the nearest tf32
+    // tensor-core path only: Y written as fp16 (y_fp16); A read as fp16 with the
+    // fp16 copy W16 of W (fp16_operands), the MMA then kind::f16
+    bool y_fp16;
+    bool fp16_operands;
+    const void* W16;
 };
 int gemm_f32(const GemmArgs& args, cudaStream_t stream);
 
@@ -52,12 +57,14 @@ struct TcGemmOp {
     void* Y;
     int ldy;
     bool y_bf16;
+    bool y_fp16;             // fp16 output (TMA epilogue; out-of-range values set the error word)
     const float* gate;       // gated residual
     int gate_stride;
     int rows_per_patch;
     int rows, cols, K;
     int bn;                  // N tile: multiple of 32, <= 256 (<= 128 for SwiGLU)
     bool tf32;
+    bool fp16;               // !tf32: operands are fp16 (kind::f16, F16) rather than bf16
     bool round_tf32;         // round fp32 outputs to the nearest tf32
     GemmEpilogue epilogue;
     int tag;

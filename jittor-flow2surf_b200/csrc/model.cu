@@ -1,6 +1,8 @@
 // Flow2SurfNet forward (flow2surf/models/network.py:75-82) as a sequence of
 // sm_100a kernels over point-major activations, plus the parameter-blob and
 // workspace layouts and the operator entry points that share its kernels.
+#include <cuda_fp16.h>
+
 #include <cfloat>
 #include <vector>
 
@@ -183,6 +185,9 @@ struct Workspace {
     float *xyz4, *feat0, *content, *cat, *x, *h, *qkv, *colstats, *offs, *ffh, *dec0, *dec1;
     float *cond, *mod, *attn;
     float *split_a, *split_w;  // 3xTF32 operand halves (split-bf16 encoder only)
+    // tf32 trunk: the FFN hidden rows (w.ffh) are fp16, and ff2 reads the fp16
+    // copy of its weights made at the start of every forward
+    __half* ff2_w16;
     int32_t* idx;
     size_t bytes;
 };
@@ -215,6 +220,8 @@ Workspace carve(const Dims& d, int B, int M, char* base) {
     const bool split = d.enc_gemm_precision == F2S_PRECISION_BF16X3;
     w.split_a = split ? (float*)take(R * 2 * d.max_gemm_in) : nullptr;
     w.split_w = split ? (float*)take((size_t)2 * d.max_gemm_w) : nullptr;
+    const bool tf32_trunk = d.precision == F2S_PRECISION_TF32;
+    w.ff2_w16 = tf32_trunk ? (__half*)take(((size_t)(d.NB > 0 ? d.NB : 1) * d.C * d.Hf + 1) / 2) : nullptr;
     w.bytes = off;
     return w;
 }
@@ -408,6 +415,13 @@ input_embed_lane_kernel(const float* __restrict__ x, int B, int M, const float* 
     }
 }
 
+// fp16 copy (round to nearest) of n floats.
+__global__ void to_half_kernel(const float* __restrict__ src, __half* __restrict__ dst, int64_t n) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x)
+        dst[i] = __float2half_rn(src[i]);
+}
+
 GemmArgs gemm_args(const float* A, int lda, const float* W, const float* bias, float* Y, int ldy,
                    int rows, int cols, int K) {
     GemmArgs g{};
@@ -484,7 +498,10 @@ int linear_op(const GemmArgs& g, int precision, cudaStream_t st, float* split_a 
     op.cols = g.cols;
     op.K = g.K;
     op.bn = tc_pick_bn(g.cols, g.epilogue == kEpiSwiGlu);
-    op.tf32 = true;
+    op.tf32 = !g.fp16_operands;
+    op.fp16 = g.fp16_operands;
+    if (g.fp16_operands) op.W = g.W16;
+    op.y_fp16 = g.y_fp16;
     op.round_tf32 = g.round_tf32;
     op.epilogue = g.epilogue;
     op.tag = g.tag;
@@ -601,6 +618,17 @@ int forward(const Dims& d, const Layout& L, const float* P, const float* x_in, c
     // operands of tf32 contractions are rounded to the nearest tf32 where made
     const bool tf32_trunk = d.precision == F2S_PRECISION_TF32;
     const int mstride = d.NB * 6 * C;
+    // fp16 FFN hidden rows (tf32 trunk; 16-byte fp16 rows)
+    const bool ffn_fp16 = tf32_trunk && d.Hf % 8 == 0 && w.ff2_w16 != nullptr;
+    if (ffn_fp16) {
+        TraceScope trace(kTagGemmFf2, st);
+        for (int i = 0; i < d.NB; ++i) {
+            const int64_t n = (int64_t)C * d.Hf;
+            to_half_kernel<<<(unsigned)((n + 255) / 256 < 1024 ? (n + 255) / 256 : 1024), 256, 0, st>>>(
+                P + L.block[i].ff2_w, w.ff2_w16 + (size_t)i * n, n);
+            F2S_TRY(check_launch("to_half_kernel"));
+        }
+    }
     for (int i = 0; i < d.NB; ++i) {
         const BlockParams& bp = L.block[i];
         const float* mod = w.mod + (size_t)i * 6 * C;
@@ -633,6 +661,10 @@ int forward(const Dims& d, const Layout& L, const float* P, const float* x_in, c
         sw.bias2 = P + bp.ff1_b;
         sw.tag = kTagGemmSwiGlu;
         sw.round_tf32 = tf32_trunk;
+        // the tf32 trunk keeps the FFN hidden rows in fp16 (the same 10-bit
+        // mantissa as the tf32 operand ff2 reads, half the bytes each way) and
+        // runs ff2 as kind::f16 on them
+        sw.y_fp16 = ffn_fp16;
         F2S_TRY(linear_op(sw, d.precision, st));
         GemmArgs f2 = gemm_args(w.ffh, d.Hf, P + bp.ff2_w, P + bp.ff2_b, w.x, C, R, C, d.Hf);
         f2.epilogue = kEpiGatedResidual;
@@ -640,6 +672,8 @@ int forward(const Dims& d, const Layout& L, const float* P, const float* x_in, c
         f2.gate_stride = mstride;
         f2.rows_per_patch = M;
         f2.tag = kTagGemmFf2;
+        f2.fp16_operands = ffn_fp16;
+        f2.W16 = ffn_fp16 ? (const void*)(w.ff2_w16 + (size_t)i * C * d.Hf) : nullptr;
         F2S_TRY(linear_op(f2, d.precision, st));
     }
     // decoder (decoder.py:8-32)

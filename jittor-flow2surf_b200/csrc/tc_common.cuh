@@ -22,7 +22,9 @@ constexpr uint32_t kSpinLimit = 1u << 22;
 constexpr uint32_t kSuspendHintNs = 1000;
 
 // Error codes written to the kernel's error word.
-enum TcError : int { kTcOk = 0, kTcWaitTimeout = 1 };
+// Device error word values: a bounded wait ran out; an fp16 output of a
+// tensor-core GEMM was out of the fp16 range (or not finite).
+enum TcError : int { kTcOk = 0, kTcWaitTimeout = 1, kTcFp16Range = 2 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -290,6 +292,12 @@ __host__ __device__ constexpr uint32_t make_idesc(int M, int N, uint32_t ab_form
 // fp32, loaded as boxes of (box_cols x box_rows) with 128-byte swizzle.
 int make_tensor_map_2d(CUtensorMap* map, const void* base, bool fp32, int64_t rows,
                        int64_t cols, int64_t ld, int box_rows, int box_cols);
+
+// Element types of the typed form: fp32, bf16, fp16.
+enum TmaType : int { kTmaF32 = 0, kTmaBF16 = 1, kTmaF16 = 2 };
+// The same with an explicit element type and swizzle span (128 or 64 bytes).
+int make_tensor_map_2d_typed(CUtensorMap* map, const void* base, TmaType type, int swizzle_bytes,
+                             int64_t rows, int64_t cols, int64_t ld, int box_rows, int box_cols);
 
 // 3-D tensor (d0 innermost, element strides given in bytes for dims 1, 2),
 // boxes of (box0 x box1 x 1), 128-byte swizzle: out-of-range rows of a patch

@@ -18,6 +18,8 @@
 // Operands are bf16 (kind::f16) or fp32 read as tf32 (kind::tf32), or
 // (3xTF32) pairs x = hi + lo of tf32 values with the products hi*hi + hi*lo +
 // lo*hi accumulated, which leaves only the lo*lo term (2^-22 relative) out.
+#include <cuda_fp16.h>
+
 #include <mutex>
 
 #include "kernels.cuh"
@@ -49,6 +51,7 @@ struct TcGemmArgs {
     void* Y;
     int ldy;
     int y_bf16;
+    int y_fp16;         // fp16 boxes (32 x 32, 64-byte swizzle) on the TMA path
     const float* gate;
     int gate_stride;
     int rows_per_patch;
@@ -61,6 +64,17 @@ constexpr uint32_t kEpiBox = 32 * 128;  // one 32-row x 32-column fp32 box, 128-
 
 __device__ __forceinline__ uint32_t sw128_offset(int row, int chunk) {
     return (uint32_t)((row >> 3) * 1024 + (row & 7) * 128 + ((chunk ^ (row & 7)) << 4));
+}
+
+// Byte offset of 16-byte chunk `chunk` (0..3) of row `row` in a box of
+// 64-byte rows with the 64-byte swizzle (box base 512-byte aligned).
+__device__ __forceinline__ uint32_t sw64_offset(int row, int chunk) {
+    return (uint32_t)(row * 64 + ((chunk ^ ((row >> 1) & 3)) << 4));
+}
+
+__device__ __forceinline__ uint32_t pack_half2(float a, float b) {
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
 }
 
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int c0, int c1) {
@@ -319,10 +333,24 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                     // the box's previous store must have read it
                     if (lane == 0 && boxes_sent >= 2) bulk_wait_read<1>();
                     __syncwarp();
+                    if (g.y_fp16) {
+                        // fp16 values keep tf32's 10-bit mantissa; a value the
+                        // format cannot hold is reported, not clamped
+                        bool out_of_range = false;
 #pragma unroll
-                    for (int ch = 0; ch < 8; ++ch)
-                        *reinterpret_cast<float4*>(box + sw128_offset(lane, ch)) =
-                            make_float4(v[4 * ch], v[4 * ch + 1], v[4 * ch + 2], v[4 * ch + 3]);
+                        for (int i = 0; i < 32; ++i) out_of_range |= !(fabsf(v[i]) < 65504.0f);
+                        if (out_of_range) atomicExch(g.err, tc::kTcFp16Range);
+#pragma unroll
+                        for (int ch = 0; ch < 4; ++ch)
+                            *reinterpret_cast<uint4*>(box + sw64_offset(lane, ch)) = make_uint4(
+                                pack_half2(v[8 * ch], v[8 * ch + 1]), pack_half2(v[8 * ch + 2], v[8 * ch + 3]),
+                                pack_half2(v[8 * ch + 4], v[8 * ch + 5]), pack_half2(v[8 * ch + 6], v[8 * ch + 7]));
+                    } else {
+#pragma unroll
+                        for (int ch = 0; ch < 8; ++ch)
+                            *reinterpret_cast<float4*>(box + sw128_offset(lane, ch)) =
+                                make_float4(v[4 * ch], v[4 * ch + 1], v[4 * ch + 2], v[4 * ch + 3]);
+                    }
                     fence_proxy_async_shared();
                     __syncwarp();
                     if (lane == 0) {
@@ -460,23 +488,34 @@ int* tc_error_word() {
     return addr[dev];
 }
 
-int make_tensor_map_2d(CUtensorMap* map, const void* base, bool fp32, int64_t rows, int64_t cols,
-                       int64_t ld, int box_rows, int box_cols) {
+int make_tensor_map_2d_typed(CUtensorMap* map, const void* base, TmaType type, int swizzle_bytes,
+                             int64_t rows, int64_t cols, int64_t ld, int box_rows, int box_cols) {
     EncodeTiledFn enc = encode_fn();
     if (!enc) return fail(F2S_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
-    const int64_t elem = fp32 ? 4 : 2;
+    const int64_t elem = type == kTmaF32 ? 4 : 2;
     F2S_REQUIRE(((uintptr_t)base & 15) == 0, "tensor map base must be 16-byte aligned");
     F2S_REQUIRE((ld * elem) % 16 == 0, "tensor map row pitch must be a multiple of 16 bytes");
+    F2S_REQUIRE(swizzle_bytes == 128 || swizzle_bytes == 64, "tensor map swizzle %d", swizzle_bytes);
+    F2S_REQUIRE(box_cols * elem <= swizzle_bytes, "tensor map box row wider than its swizzle span");
     const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
     const cuuint64_t strides[1] = {(cuuint64_t)(ld * elem)};
     const cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
     const cuuint32_t estr[2] = {1, 1};
-    const CUresult r = enc(map, fp32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
-                           2, const_cast<void*>(base), dims, strides, box, estr,
-                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+    const CUtensorMapDataType dt = type == kTmaF32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                   : type == kTmaBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                      : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    const CUresult r = enc(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           swizzle_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(F2S_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
     return F2S_OK;
+}
+
+int make_tensor_map_2d(CUtensorMap* map, const void* base, bool fp32, int64_t rows, int64_t cols,
+                       int64_t ld, int box_rows, int box_cols) {
+    return make_tensor_map_2d_typed(map, base, fp32 ? kTmaF32 : kTmaBF16, 128, rows, cols, ld,
+                                    box_rows, box_cols);
 }
 
 int make_tensor_map_3d(CUtensorMap* map, const void* base, bool fp32, int64_t d0, int64_t d1,
@@ -518,11 +557,14 @@ int tc_gemm(const TcGemmOp& op, cudaStream_t st) {
                 "tc_gemm: bad N tile %d", bn);
     int* err = tc_error_word();
     if (!err) return fail(F2S_ERR_CUDA, "tc_gemm: device error word unavailable");
+    F2S_REQUIRE(!(op.fp16 && op.tf32), "tc_gemm: fp16 operands run kind::f16, not tf32");
+    F2S_REQUIRE(!(op.y_fp16 && op.y_bf16), "tc_gemm: one output type");
     CUtensorMap ma, ma2, mb, mb2;
     const int bk = op.tf32 ? 32 : 64;
-    F2S_TRY(make_tensor_map_2d(&ma, op.A, op.tf32, op.rows, op.K, op.lda, kTileM, bk));
-    F2S_TRY(make_tensor_map_2d(&mb, op.W, op.tf32, op.cols, op.K, op.K, bn, bk));
-    if (dual) F2S_TRY(make_tensor_map_2d(&mb2, op.W2, op.tf32, op.cols, op.K, op.K, bn, bk));
+    const TmaType ot = op.tf32 ? kTmaF32 : op.fp16 ? kTmaF16 : kTmaBF16;
+    F2S_TRY(make_tensor_map_2d_typed(&ma, op.A, ot, 128, op.rows, op.K, op.lda, kTileM, bk));
+    F2S_TRY(make_tensor_map_2d_typed(&mb, op.W, ot, 128, op.cols, op.K, op.K, bn, bk));
+    if (dual) F2S_TRY(make_tensor_map_2d_typed(&mb2, op.W2, ot, 128, op.cols, op.K, op.K, bn, bk));
     else if (split) F2S_TRY(make_tensor_map_2d(&mb2, op.W_lo, true, op.cols, op.K, op.K, bn, bk));
     else mb2 = mb;
     if (split) F2S_TRY(make_tensor_map_2d(&ma2, op.A_lo, true, op.rows, op.K, op.lda, kTileM, bk));
@@ -535,13 +577,16 @@ int tc_gemm(const TcGemmOp& op, cudaStream_t st) {
     g.bn = bn;
     g.k_blocks = ceil_div(op.K, bk);
     g.acc_cols = bn * (dual ? 2 : 1);
-    g.idesc = tc::make_idesc(kTileM, bn, op.tf32 ? 2u : 1u);
-    g.idesc_dual = tc::make_idesc(kTileM, 2 * bn, op.tf32 ? 2u : 1u);
+    // operand format of the instruction descriptor: 0 fp16, 1 bf16 (kind::f16), 2 tf32
+    const uint32_t fmt = op.tf32 ? 2u : op.fp16 ? 0u : 1u;
+    g.idesc = tc::make_idesc(kTileM, bn, fmt);
+    g.idesc_dual = tc::make_idesc(kTileM, 2 * bn, fmt);
     g.bias = op.bias;
     g.bias2 = op.bias2;
     g.Y = op.Y;
     g.ldy = op.ldy;
     g.y_bf16 = op.y_bf16 ? 1 : 0;
+    g.y_fp16 = op.y_fp16 ? 1 : 0;
     g.gate = op.gate;
     g.gate_stride = op.gate_stride;
     g.rows_per_patch = op.rows_per_patch > 0 ? op.rows_per_patch : 1;
@@ -550,11 +595,15 @@ int tc_gemm(const TcGemmOp& op, cudaStream_t st) {
     // fp32 output with 16-byte rows, columns and per-column vectors: the
     // epilogue writes 32 x 32 boxes by TMA (store, or reduce-add for the residual)
     auto aligned16 = [](const void* p) { return ((uintptr_t)p & 15) == 0; };
-    g.tma_epi = !op.y_bf16 && op.ldy % 4 == 0 && op.cols % 4 == 0 && aligned16(op.Y) &&
+    g.tma_epi = !op.y_bf16 && op.ldy % (op.y_fp16 ? 8 : 4) == 0 && op.cols % 4 == 0 && aligned16(op.Y) &&
                 aligned16(op.bias) && aligned16(op.bias2) &&
                 (op.epilogue != kEpiGatedResidual || (aligned16(op.gate) && op.gate_stride % 4 == 0));
+    F2S_REQUIRE(!op.y_fp16 || (g.tma_epi && op.epilogue != kEpiGatedResidual),
+                "tc_gemm: fp16 output needs the TMA epilogue (16-byte rows and vectors), no residual");
     CUtensorMap my;
-    if (g.tma_epi) F2S_TRY(make_tensor_map_2d(&my, op.Y, true, op.rows, op.cols, op.ldy, 32, 32));
+    if (g.tma_epi)
+        F2S_TRY(make_tensor_map_2d_typed(&my, op.Y, op.y_fp16 ? kTmaF16 : kTmaF32, op.y_fp16 ? 64 : 128,
+                                         op.rows, op.cols, op.ldy, 32, 32));
     else my = ma;
     const size_t stage_bytes =
         (size_t)kTileM * 128 * (split ? 2 : 1) + (size_t)bn * 128 * ((dual || split) ? 2 : 1);

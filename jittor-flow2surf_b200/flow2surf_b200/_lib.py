@@ -100,6 +100,22 @@ def call(name: str, *args) -> None:
     check(getattr(lib(), name)(*args))
 
 
+DEVICE_ERRORS = {
+    1: "a tensor-core kernel gave up on a bounded wait",
+    2: "an fp16 intermediate of the tf32 trunk (the FFN hidden rows) was out of the fp16 range",
+}
+
+
+def check_device_error(stream=None) -> None:
+    """Raise when the library's device error word is set (it is then
+    cleared); synchronises `stream`."""
+    value = ctypes.c_int(0)
+    check(lib().f2s_device_error(ctypes.byref(value), 1, stream_handle(stream)))
+    if value.value:
+        raise Flow2SurfError(F2S_ERR_CUDA, "device error %d: %s" % (
+            value.value, DEVICE_ERRORS.get(value.value, "unknown")))
+
+
 def ptr(tensor) -> int | None:
     """Raw device pointer of a torch tensor (None for an empty one)."""
     return tensor.data_ptr() if tensor is not None and tensor.numel() > 0 else None

@@ -244,6 +244,7 @@ def denoise_device(model, points: torch.Tensor, patch_size, seed_k, num_steps, r
         alpha_previous = float(alphas[step - 1]) if step > 0 else 0.0
         runner.step(current, spare, alpha_current, alpha_current - alpha_previous)
         current, spare = spare, current
+    _lib.check_device_error()
     return current
 
 
