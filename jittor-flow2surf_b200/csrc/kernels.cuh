@@ -39,6 +39,7 @@ struct GemmArgs {
     bool y_fp16;
     bool fp16_operands;
     const void* W16;
+    const void* W2_16;     // fp16 copy of W2 (SwiGLU)
 };
 int gemm_f32(const GemmArgs& args, cudaStream_t stream);
 
@@ -82,6 +83,11 @@ int tc_pick_bn(int cols, bool swiglu);
 int ln_modulate(const float* x, int ldx, float* h, int ldh, const float* mod, int mod_stride,
                 int scale_off, int shift_off, int rows, int rows_per_patch, int C,
                 bool round_tf32, cudaStream_t stream);
+// The same with h in fp16 (C even, <= 256); values out of the fp16 range set
+// the device error word to 2. F2S_ERR_UNSUPPORTED outside that shape.
+int ln_modulate_f16(const float* x, int ldx, void* h, int ldh, const float* mod, int mod_stride,
+                    int scale_off, int shift_off, int rows, int rows_per_patch, int C,
+                    cudaStream_t stream);
 // y = LeakyReLU_0.2(LN(y) * gamma + beta) in place (two-pass, eps 1e-6).
 int ln_affine_leaky(float* y, int ldy, const float* gamma, const float* beta, int rows, int C,
                     bool round_tf32, cudaStream_t stream);

@@ -185,9 +185,11 @@ struct Workspace {
     float *xyz4, *feat0, *content, *cat, *x, *h, *qkv, *colstats, *offs, *ffh, *dec0, *dec1;
     float *cond, *mod, *attn;
     float *split_a, *split_w;  // 3xTF32 operand halves (split-bf16 encoder only)
-    // tf32 trunk: the FFN hidden rows (w.ffh) are fp16, and ff2 reads the fp16
-    // copy of its weights made at the start of every forward
-    __half* ff2_w16;
+    // tf32 trunk: the FFN input (w.h after the second modulation) and hidden
+    // rows (w.ffh) are fp16, and the FFN GEMMs read fp16 copies of their
+    // weights made at the start of every forward: per block gate, value
+    // (Hf x C each) and ff2 (C x Hf)
+    __half* ffn_w16;
     int32_t* idx;
     size_t bytes;
 };
@@ -221,7 +223,8 @@ Workspace carve(const Dims& d, int B, int M, char* base) {
     w.split_a = split ? (float*)take(R * 2 * d.max_gemm_in) : nullptr;
     w.split_w = split ? (float*)take((size_t)2 * d.max_gemm_w) : nullptr;
     const bool tf32_trunk = d.precision == F2S_PRECISION_TF32;
-    w.ff2_w16 = tf32_trunk ? (__half*)take(((size_t)(d.NB > 0 ? d.NB : 1) * d.C * d.Hf + 1) / 2) : nullptr;
+    w.ffn_w16 = tf32_trunk ? (__half*)take(((size_t)(d.NB > 0 ? d.NB : 1) * 3 * d.C * d.Hf + 1) / 2)
+                           : nullptr;
     w.bytes = off;
     return w;
 }
@@ -500,7 +503,10 @@ int linear_op(const GemmArgs& g, int precision, cudaStream_t st, float* split_a 
     op.bn = tc_pick_bn(g.cols, g.epilogue == kEpiSwiGlu);
     op.tf32 = !g.fp16_operands;
     op.fp16 = g.fp16_operands;
-    if (g.fp16_operands) op.W = g.W16;
+    if (g.fp16_operands) {
+        op.W = g.W16;
+        op.W2 = g.W2_16;
+    }
     op.y_fp16 = g.y_fp16;
     op.round_tf32 = g.round_tf32;
     op.epilogue = g.epilogue;
@@ -618,15 +624,20 @@ int forward(const Dims& d, const Layout& L, const float* P, const float* x_in, c
     // operands of tf32 contractions are rounded to the nearest tf32 where made
     const bool tf32_trunk = d.precision == F2S_PRECISION_TF32;
     const int mstride = d.NB * 6 * C;
-    // fp16 FFN hidden rows (tf32 trunk; 16-byte fp16 rows)
-    const bool ffn_fp16 = tf32_trunk && d.Hf % 8 == 0 && w.ff2_w16 != nullptr;
+    // fp16 FFN operands (tf32 trunk; 16-byte fp16 rows, the register LN path)
+    const bool ffn_fp16 = tf32_trunk && d.Hf % 8 == 0 && C % 8 == 0 && C <= 256 &&
+                          w.ffn_w16 != nullptr;
+    const int64_t ffn_n = (int64_t)C * d.Hf;  // elements of one FFN weight matrix
     if (ffn_fp16) {
-        TraceScope trace(kTagGemmFf2, st);
+        TraceScope trace(kTagGemmSwiGlu, st);
         for (int i = 0; i < d.NB; ++i) {
-            const int64_t n = (int64_t)C * d.Hf;
-            to_half_kernel<<<(unsigned)((n + 255) / 256 < 1024 ? (n + 255) / 256 : 1024), 256, 0, st>>>(
-                P + L.block[i].ff2_w, w.ff2_w16 + (size_t)i * n, n);
-            F2S_TRY(check_launch("to_half_kernel"));
+            const int64_t srcs[3] = {L.block[i].gate_w, L.block[i].ff1_w, L.block[i].ff2_w};
+            for (int m = 0; m < 3; ++m) {
+                to_half_kernel<<<(unsigned)((ffn_n + 255) / 256 < 1024 ? (ffn_n + 255) / 256 : 1024),
+                                 256, 0, st>>>(P + srcs[m], w.ffn_w16 + (size_t)(3 * i + m) * ffn_n,
+                                               ffn_n);
+                F2S_TRY(check_launch("to_half_kernel"));
+            }
         }
     }
     for (int i = 0; i < d.NB; ++i) {
@@ -654,17 +665,23 @@ int forward(const Dims& d, const Layout& L, const float* P, const float* x_in, c
         g.rows_per_patch = M;
         g.tag = kTagGemmProj;
         F2S_TRY(linear_op(g, d.precision, st));
-        F2S_TRY(ln_modulate(w.x, C, w.h, C, mod, mstride, 3 * C, 4 * C, R, M, C, tf32_trunk, st));
+        if (ffn_fp16)
+            F2S_TRY(ln_modulate_f16(w.x, C, w.h, C, mod, mstride, 3 * C, 4 * C, R, M, C, st));
+        else
+            F2S_TRY(ln_modulate(w.x, C, w.h, C, mod, mstride, 3 * C, 4 * C, R, M, C, tf32_trunk, st));
         GemmArgs sw = gemm_args(w.h, C, P + bp.gate_w, P + bp.gate_b, w.ffh, d.Hf, R, d.Hf, C);
         sw.epilogue = kEpiSwiGlu;
         sw.W2 = P + bp.ff1_w;
         sw.bias2 = P + bp.ff1_b;
         sw.tag = kTagGemmSwiGlu;
         sw.round_tf32 = tf32_trunk;
-        // the tf32 trunk keeps the FFN hidden rows in fp16 (the same 10-bit
-        // mantissa as the tf32 operand ff2 reads, half the bytes each way) and
-        // runs ff2 as kind::f16 on them
+        // the tf32 trunk keeps the FFN input and hidden rows in fp16 (the same
+        // 10-bit mantissa as the tf32 operands they replace, half the bytes
+        // each way) and runs both FFN GEMMs as kind::f16 on them
         sw.y_fp16 = ffn_fp16;
+        sw.fp16_operands = ffn_fp16;
+        sw.W16 = ffn_fp16 ? (const void*)(w.ffn_w16 + (size_t)(3 * i) * ffn_n) : nullptr;
+        sw.W2_16 = ffn_fp16 ? (const void*)(w.ffn_w16 + (size_t)(3 * i + 1) * ffn_n) : nullptr;
         F2S_TRY(linear_op(sw, d.precision, st));
         GemmArgs f2 = gemm_args(w.ffh, d.Hf, P + bp.ff2_w, P + bp.ff2_b, w.x, C, R, C, d.Hf);
         f2.epilogue = kEpiGatedResidual;
@@ -673,7 +690,7 @@ int forward(const Dims& d, const Layout& L, const float* P, const float* x_in, c
         f2.rows_per_patch = M;
         f2.tag = kTagGemmFf2;
         f2.fp16_operands = ffn_fp16;
-        f2.W16 = ffn_fp16 ? (const void*)(w.ff2_w16 + (size_t)i * C * d.Hf) : nullptr;
+        f2.W16 = ffn_fp16 ? (const void*)(w.ffn_w16 + (size_t)(3 * i + 2) * ffn_n) : nullptr;
         F2S_TRY(linear_op(f2, d.precision, st));
     }
     // decoder (decoder.py:8-32)

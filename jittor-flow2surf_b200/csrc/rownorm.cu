@@ -1,7 +1,10 @@
 // Row-wise channel LayerNorms of the point-major activations (one warp per
 // point). All follow ChannelLayerNorm (flow2surf/models/layers.py:20-27):
 // two-pass mean / variance over channels, eps 1e-6.
+#include <cuda_fp16.h>
+
 #include "kernels.cuh"
+#include "tc_common.cuh"
 
 namespace f2s {
 namespace {
@@ -52,11 +55,13 @@ __device__ __forceinline__ void row_stats_reg(const float2 (&v)[kPairs], int C, 
 
 // AdaLN-Zero modulate(norm(x), shift, scale) (transformer.py:10-12,85,88).
 // kPaired: C even, C <= 256, 8-byte aligned rows (the register path).
-template <bool kPaired>
-__global__ void ln_modulate_kernel(const float* __restrict__ x, int ldx, float* __restrict__ h,
+// kHalf (paired only): h is fp16, values out of its range set *err.
+template <bool kPaired, bool kHalf = false>
+__global__ void ln_modulate_kernel(const float* __restrict__ x, int ldx, void* __restrict__ h_out,
                                    int ldh, const float* __restrict__ mod, int mod_stride,
                                    int scale_off, int shift_off, int rows, int rows_per_patch,
-                                   int C, bool round_tf32) {
+                                   int C, bool round_tf32, int* err) {
+    float* h = static_cast<float*>(h_out);
     const int lane = threadIdx.x & 31;
     if constexpr (kPaired) {
         // two rows per warp, both loaded before either is reduced
@@ -75,6 +80,8 @@ __global__ void ln_modulate_kernel(const float* __restrict__ x, int ldx, float* 
             row_stats_reg(v[q], C, lane, mean, rstd);
             const float* m = mod + (size_t)(row / rows_per_patch) * mod_stride;
             float* hr = h + (size_t)row * ldh;
+            __half* hr16 = static_cast<__half*>(h_out) + (size_t)row * ldh;
+            bool out_of_range = false;
 #pragma unroll
             for (int i = 0; i < kPairs; ++i) {
                 const int c = 2 * (lane + 32 * i);
@@ -83,13 +90,19 @@ __global__ void ln_modulate_kernel(const float* __restrict__ x, int ldx, float* 
                     const float2 sh = *reinterpret_cast<const float2*>(m + shift_off + c);
                     float a = (v[q][i].x - mean) * rstd * (1.0f + sc.x) + sh.x;
                     float b = (v[q][i].y - mean) * rstd * (1.0f + sc.y) + sh.y;
-                    if (round_tf32) {
-                        a = f2s_round_tf32(a);
-                        b = f2s_round_tf32(b);
+                    if constexpr (kHalf) {
+                        out_of_range |= !(fabsf(a) < 65504.0f) || !(fabsf(b) < 65504.0f);
+                        *reinterpret_cast<__half2*>(hr16 + c) = __floats2half2_rn(a, b);
+                    } else {
+                        if (round_tf32) {
+                            a = f2s_round_tf32(a);
+                            b = f2s_round_tf32(b);
+                        }
+                        *reinterpret_cast<float2*>(hr + c) = make_float2(a, b);
                     }
-                    *reinterpret_cast<float2*>(hr + c) = make_float2(a, b);
                 }
             }
+            if (kHalf && out_of_range) atomicExch(err, 2);
         }
     } else {
         const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -172,7 +185,25 @@ int ln_modulate(const float* x, int ldx, float* h, int ldh, const float* mod, in
     auto kernel = paired ? ln_modulate_kernel<true> : ln_modulate_kernel<false>;
     const int rows_per_cta = paired ? 2 * kRowsPerCta : kRowsPerCta;
     kernel<<<ceil_div(rows, rows_per_cta), kRowsPerCta * 32, 0, stream>>>(
-        x, ldx, h, ldh, mod, mod_stride, scale_off, shift_off, rows, rows_per_patch, C, round_tf32);
+        x, ldx, h, ldh, mod, mod_stride, scale_off, shift_off, rows, rows_per_patch, C, round_tf32,
+        nullptr);
+    return check_launch("ln_modulate_kernel");
+}
+
+int ln_modulate_f16(const float* x, int ldx, void* h, int ldh, const float* mod, int mod_stride,
+                    int scale_off, int shift_off, int rows, int rows_per_patch, int C,
+                    cudaStream_t stream) {
+    if (rows == 0) return F2S_OK;
+    const bool paired = C % 2 == 0 && C <= 64 * kPairs && ldx % 2 == 0 && ldh % 2 == 0 &&
+                        ((uintptr_t)x & 7) == 0 && ((uintptr_t)h & 3) == 0 &&
+                        ((uintptr_t)mod & 7) == 0 && mod_stride % 2 == 0 && scale_off % 2 == 0 &&
+                        shift_off % 2 == 0;
+    if (!paired) return fail(F2S_ERR_UNSUPPORTED, "ln_modulate_f16: shape outside the register path");
+    int* err = tc_error_word();
+    if (!err) return fail(F2S_ERR_CUDA, "ln_modulate_f16: device error word unavailable");
+    TraceScope trace(kTagRowNorm, stream);
+    ln_modulate_kernel<true, true><<<ceil_div(rows, 2 * kRowsPerCta), kRowsPerCta * 32, 0, stream>>>(
+        x, ldx, h, ldh, mod, mod_stride, scale_off, shift_off, rows, rows_per_patch, C, false, err);
     return check_launch("ln_modulate_kernel");
 }
 
