@@ -72,10 +72,6 @@ __device__ __forceinline__ void fence_proxy_async() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-__device__ __forceinline__ void named_sync_softmax() {
-    asm volatile("bar.sync 1, 128;" ::: "memory");
-}
-
 __device__ __forceinline__ void named_sync_out() {
     asm volatile("bar.sync 1, %0;" ::"n"(kOutWarps * 32) : "memory");
 }

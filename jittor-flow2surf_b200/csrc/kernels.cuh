@@ -40,6 +40,9 @@ struct GemmArgs {
     bool fp16_operands;
     const void* W16;
     const void* W2_16;     // fp16 copy of W2 (SwiGLU)
+    // F2S_PRECISION_BF16X3: A already split (A = tf32 high parts, A_lo the
+    // remainders, both with leading dimension lda); null to split here
+    const float* A_lo;
 };
 int gemm_f32(const GemmArgs& args, cudaStream_t stream);
 

@@ -185,6 +185,8 @@ struct Workspace {
     float *xyz4, *feat0, *content, *cat, *x, *h, *qkv, *colstats, *offs, *ffh, *dec0, *dec1;
     float *cond, *mod, *attn;
     float *split_a, *split_w;  // 3xTF32 operand halves (split-bf16 encoder only)
+    // split-bf16 encoder: feat0 holds tf32 high parts, feat0_lo the remainders
+    float* feat0_lo;
     // tf32 trunk: the FFN input (w.h after the second modulation) and hidden
     // rows (w.ffh) are fp16, and the FFN GEMMs read fp16 copies of their
     // weights made at the start of every forward: per block gate, value
@@ -222,6 +224,7 @@ Workspace carve(const Dims& d, int B, int M, char* base) {
     const bool split = d.enc_gemm_precision == F2S_PRECISION_BF16X3;
     w.split_a = split ? (float*)take(R * 2 * d.max_gemm_in) : nullptr;
     w.split_w = split ? (float*)take((size_t)2 * d.max_gemm_w) : nullptr;
+    w.feat0_lo = split ? (float*)take(R * d.sd[0]) : nullptr;
     const bool tf32_trunk = d.precision == F2S_PRECISION_TF32;
     w.ffn_w16 = tf32_trunk ? (__half*)take(((size_t)(d.NB > 0 ? d.NB : 1) * 3 * d.C * d.Hf + 1) / 2)
                            : nullptr;
@@ -333,7 +336,7 @@ input_embed_lane_kernel(const float* __restrict__ x, int B, int M, const float* 
                         const float* __restrict__ bia, const float* __restrict__ lnw,
                         const float* __restrict__ lnb, const float* __restrict__ ow,
                         const float* __restrict__ ob, int S0, float* __restrict__ xyz4,
-                        float* __restrict__ feat) {
+                        float* __restrict__ feat, float* __restrict__ feat_lo) {
     extern __shared__ __align__(16) float sm[];
     float* sOw = sm;                    // [S][S]: row c = output channel, zero-padded
     float* sW = sOw + S * S;            // [S][4]: w0, w1, w2, bias
@@ -393,6 +396,7 @@ input_embed_lane_kernel(const float* __restrict__ x, int B, int M, const float* 
         }
         if (!ok) continue;
         float* fr = feat + (size_t)p * S0;
+        float* fl = feat_lo ? feat_lo + (size_t)p * S0 : nullptr;
         for (int c = 0; c < S0; c += 4) {
             float o[4];
 #pragma unroll
@@ -409,10 +413,25 @@ input_embed_lane_kernel(const float* __restrict__ x, int B, int M, const float* 
                 }
                 o[e] = v;
             }
+            float lo[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            if (fl) {
+                // tf32 high part here, the remainder in feat_lo (the operand
+                // split of the 3xTF32 GEMM that reads the features)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float hi = f2s_round_tf32(o[e]);
+                    lo[e] = o[e] - hi;
+                    o[e] = hi;
+                }
+            }
             if (c + 4 <= S0 && (S0 & 3) == 0) {
                 *reinterpret_cast<float4*>(fr + c) = make_float4(o[0], o[1], o[2], o[3]);
+                if (fl) *reinterpret_cast<float4*>(fl + c) = make_float4(lo[0], lo[1], lo[2], lo[3]);
             } else {
-                for (int e = 0; e < 4 && c + e < S0; ++e) fr[c + e] = o[e];
+                for (int e = 0; e < 4 && c + e < S0; ++e) {
+                    fr[c + e] = o[e];
+                    if (fl) fl[c + e] = lo[e];
+                }
             }
         }
     }
@@ -452,15 +471,19 @@ int linear_op(const GemmArgs& g, int precision, cudaStream_t st, float* split_a 
     if (precision == F2S_PRECISION_FP32) return gemm_f32(g, st);
     if (precision == F2S_PRECISION_BF16X3) {
         // the split operands are K-contiguous; TMA rows need 16-byte pitches
-        if (g.K % 4 != 0 || g.epilogue != kEpiStore || !split_a || !split_w)
+        if (g.K % 4 != 0 || g.epilogue != kEpiStore || !split_a || !split_w) {
+            if (g.A_lo) return fail(F2S_ERR_INVALID_ARGUMENT, "pre-split operand on the fp32 path");
             return gemm_f32(g, st);
-        float* a_hi = split_a;
-        float* a_lo = split_a + (size_t)g.rows * g.K;
+        }
+        const float* a_hi = g.A_lo ? g.A : split_a;
+        const float* a_lo = g.A_lo ? g.A_lo : split_a + (size_t)g.rows * g.K;
         float* w_hi = split_w;
         float* w_lo = split_w + (size_t)g.cols * g.K;
-        {
+        if (!g.A_lo) {
             TraceScope trace(g.tag, st);
-            F2S_TRY(split_tf32(g.A, g.lda, g.rows, g.K, a_hi, a_lo, st));
+            F2S_TRY(split_tf32(g.A, g.lda, g.rows, g.K, split_a, split_a + (size_t)g.rows * g.K, st));
+        } else if (g.lda % 4 != 0 || ((uintptr_t)g.A & 15) != 0 || ((uintptr_t)g.A_lo & 15) != 0) {
+            return fail(F2S_ERR_INVALID_ARGUMENT, "pre-split operand rows must be 16-byte aligned");
         }
         {
             TraceScope trace(g.tag, st);
@@ -469,7 +492,7 @@ int linear_op(const GemmArgs& g, int precision, cudaStream_t st, float* split_a 
         TcGemmOp op{};
         op.A = a_hi;
         op.A_lo = a_lo;
-        op.lda = g.K;
+        op.lda = g.A_lo ? g.lda : g.K;
         op.W = w_hi;
         op.W_lo = w_lo;
         op.bias = g.bias;
@@ -550,7 +573,7 @@ int forward(const Dims& d, const Layout& L, const float* P, const float* x_in, c
                                               (int)smem));
             kernel<<<grid, 256, smem, st>>>(x_in, B, M, P + L.in_w, P + L.in_b, P + L.in_ln_w,
                                             P + L.in_ln_b, P + L.in_out_w, P + L.in_out_b, S0,
-                                            w.xyz4, w.feat0);
+                                            w.xyz4, w.feat0, w.feat0_lo);
             return check_launch("input_embed_lane_kernel");
         };
         if (S0 <= 16) F2S_TRY(launch(input_embed_lane_kernel<16>, 16));
@@ -570,16 +593,21 @@ int forward(const Dims& d, const Layout& L, const float* P, const float* x_in, c
         F2S_TRY(check_launch("input_embed_kernel"));
     }
     F2S_TRY(knn_launch(x_in, B, 3, M, d.K, w.idx, st));
-    // neighbour stages
+    // neighbour stages; with the split encoder the first stage's input
+    // arrives already split (fin = tf32 high parts, fin_lo = remainders); the
+    // edge stages write plain fp32 rows (a second output there costs the
+    // register-bound edge kernel more than the split kernel it saves)
     int col = 0;
     const float* fin = w.feat0;
+    const float* fin_lo = d.sd[0] <= 64 ? w.feat0_lo : nullptr;
     int ldin = d.sd[0];
     for (int s = 0; s < d.S; ++s) {
         const StageParams& sp = L.stage[s];
         const int cin = d.si[s], cout = d.sd[s];
-        F2S_TRY(linear_op(gemm_args(fin, ldin, P + sp.content_w, nullptr, w.content, 2 * cout, R,
-                                    2 * cout, cin),
-                          d.enc_gemm_precision, st, w.split_a, w.split_w));  // tag: gemm_content
+        GemmArgs gc = gemm_args(fin, ldin, P + sp.content_w, nullptr, w.content, 2 * cout, R,
+                                2 * cout, cin);  // tag: gemm_content
+        gc.A_lo = fin_lo;
+        F2S_TRY(linear_op(gc, d.enc_gemm_precision, st, w.split_a, w.split_w));
         EdgeArgs ea{};
         ea.content = w.content;
         ea.ldc = 2 * cout;
@@ -608,6 +636,7 @@ int forward(const Dims& d, const Layout& L, const float* P, const float* x_in, c
         if (edge_status == F2S_ERR_UNSUPPORTED) edge_status = edge_stage_f32(ea, st);
         F2S_TRY(edge_status);
         fin = w.cat + col;
+        fin_lo = nullptr;
         ldin = d.sum_stage;
         col += cout;
     }

@@ -135,3 +135,29 @@ def test_state_dict_round_trip():
     bad.pop("blocks.0.proj.weight")
     with pytest.raises(KeyError):
         model.load_parameters(bad)
+
+
+@pytest.mark.gpu
+def test_fp16_ffn_range_is_reported(cuda):
+    """The tf32 trunk keeps the FFN input and hidden rows in fp16; a value
+    outside the fp16 range sets the device error word (2), which the denoise
+    entry points turn into an exception, instead of passing an infinity on."""
+    from flow2surf_b200 import _lib
+
+    params = random_parameters(DEFAULT_CONFIG, seed=0)
+    cloud = sphere_cloud(4000, seed=3)[0]
+    x = patches_from_cloud(cloud, 2, 1000, seed=1)
+    alpha = np.array([0.5, 0.9], dtype=np.float32)
+    _lib.check_device_error()  # clear whatever an earlier test left
+    gpu_forward(DEFAULT_CONFIG, params, x, alpha, precision="tf32", encoder_precision="bf16x3")
+    _lib.check_device_error()  # in range: no error
+    big = dict(params)
+    for name in ("blocks.0.ff_gate.weight", "blocks.0.ff1.weight"):
+        big[name] = (params[name] * 1e6).astype(np.float32)
+    gpu_forward(DEFAULT_CONFIG, big, x, alpha, precision="tf32", encoder_precision="bf16x3")
+    with pytest.raises(_lib.Flow2SurfError, match="fp16"):
+        _lib.check_device_error()
+    _lib.check_device_error()  # the word was cleared
+    # the fp32 trunk keeps fp32 rows: no range limit there
+    gpu_forward(DEFAULT_CONFIG, big, x, alpha, precision="fp32")
+    _lib.check_device_error()
