@@ -21,6 +21,8 @@
 //            two deep.
 // Warp 4 lane 0 issues every TMA copy and MMA; warps 0-3 (one thread per
 // TMEM lane) do the exponentials. All waits are bounded.
+#include <cuda_fp16.h>
+
 #include <cfloat>
 
 #include "kernels.cuh"
@@ -32,6 +34,7 @@ namespace {
 constexpr int kRows = 128;        // keys (pass 1) / queries (pass 2) per CTA
 constexpr int kDPad = 64;         // padded q/k width: 64 bf16 = 128 bytes
 constexpr int kKeyTile = 64;      // keys per pass-2 tile
+constexpr float kPScale = 32768.0f;  // 2^15: fp16 P = p * kPScale (p <= 1)
 constexpr int kKStages = 3;       // pass-2 K tiles in flight
 constexpr int kThreads = 160;     // pass 1: warps 0-3 statistics, warp 4 TMA + MMA
 // pass 2: warps 0-7 softmax / epilogue (two per TMEM lane quarter, one half of
@@ -130,10 +133,12 @@ __global__ void qk_split_kernel(const float* __restrict__ q, const float* __rest
     *reinterpret_cast<uint2*>(lo + o) = make_uint2(lw[0], lw[1]);
 }
 
-// V (rows = b*N + n, ldv) -> vT[b][c][n] (pitch n_pad), rounded to tf32;
-// 64 x 64 tiles through shared memory, 16 values per thread.
+// V (rows = b*N + n, ldv) -> vT[b][c][n] (pitch n_pad) in fp16 (rounded to
+// nearest: the 10-bit mantissa of the tf32 operand it replaces; a value out of
+// the fp16 range sets *err); 64 x 64 tiles through shared memory, 16 values
+// per thread.
 __global__ void v_transpose_kernel(const float* __restrict__ v, int ldv, int N, int C, int n_pad,
-                                   float* __restrict__ vT) {
+                                   __half* __restrict__ vT, int* err) {
     __shared__ float tile[64][65];
     const int b = blockIdx.z;
     const int n0 = blockIdx.x * 64, c0 = blockIdx.y * 64;
@@ -144,12 +149,17 @@ __global__ void v_transpose_kernel(const float* __restrict__ v, int ldv, int N, 
         if (n < N && c < C) tile[y][tx] = v[((size_t)b * N + n) * ldv + c];
     }
     __syncthreads();
+    bool out_of_range = false;
 #pragma unroll
     for (int y = ty; y < 64; y += 4) {
         const int c = c0 + y, n = n0 + tx;
-        if (c < C && n < n_pad)
-            vT[((size_t)b * C + c) * n_pad + n] = n < N ? f2s_round_tf32(tile[tx][y]) : 0.0f;
+        if (c < C && n < n_pad) {
+            const float x = n < N ? tile[tx][y] : 0.0f;
+            out_of_range |= !(fabsf(x) < 65504.0f);
+            vT[((size_t)b * C + c) * n_pad + n] = __float2half_rn(x);
+        }
     }
+    if (out_of_range) atomicExch(err, tc::kTcFp16Range);
 }
 
 struct AttnArgs {
@@ -165,7 +175,7 @@ struct AttnArgs {
     int vec4;           // pass 2: h / out rows 16-byte aligned
     int tma_epi;        // pass 2: h / out tiles by TMA (16-byte pitches and bases)
     uint32_t idesc_s;   // bf16, M = 128, N = 128 (pass 1) / 64 (pass 2)
-    uint32_t idesc_pv;  // tf32, M = 128, N = C
+    uint32_t idesc_pv;  // fp16 (kind::f16), M = 128, N = C
     int* err;
 };
 
@@ -323,10 +333,10 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
     const int C = a.C;
     constexpr uint32_t kQBytes = kRows * 128;        // 128 queries x 64 bf16
     constexpr uint32_t kKBytes = kKeyTile * 128;     // 64 keys x 64 bf16
-    const uint32_t v_bytes = (uint32_t)C * 128;      // one K-block: C rows x 32 fp32 keys
+    const uint32_t v_bytes = (uint32_t)C * 128;      // one key tile of V^T: C rows x 64 fp16 keys
     unsigned char* sQ = smem;                                  // hi, lo
     unsigned char* sK = sQ + 2 * kQBytes;                      // kKStages x (hi, lo)
-    unsigned char* sV = sK + 2 * kKStages * kKBytes;           // 2 stages x 2 K-blocks
+    unsigned char* sV = sK + 2 * kKStages * kKBytes;           // 2 stages (4 x v_bytes: the epilogue's h tile)
     const int nk = (a.N + kKeyTile - 1) / kKeyTile;
     // the patch's per-key log-sum-exp values times log2(e), nk * 64 of them
     float* sL = reinterpret_cast<float*>(sV + 4 * v_bytes);
@@ -353,8 +363,9 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
     const int b = blockIdx.x / a.tiles;
     const int q0 = (blockIdx.x - b * a.tiles) * kRows;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    // TMEM: S double buffer at columns [0, 128), P (tf32, the P V product's A
-    // operand) double buffer at [128, 256), O at [256, 256 + C)
+    // TMEM: S double buffer at columns [0, 128), P (fp16, two keys per column:
+    // the P V product's A operand) double buffer at [128, 192), O at
+    // [256, 256 + C)
     constexpr uint32_t kPCol = 128;
     constexpr uint32_t kOCol = 256;
 
@@ -385,9 +396,8 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
             };
             auto load_v = [&](int i) {
                 const int vs = i & 1;
-                tc::mbar_arrive_expect_tx(&v_full[vs], 2 * v_bytes);
-                tma_load_3d(sV + (2 * vs) * v_bytes, &map_vt, &v_full[vs], i * kKeyTile, 0, b);
-                tma_load_3d(sV + (2 * vs + 1) * v_bytes, &map_vt, &v_full[vs], i * kKeyTile + 32, 0, b);
+                tc::mbar_arrive_expect_tx(&v_full[vs], v_bytes);
+                tma_load_3d(sV + vs * v_bytes, &map_vt, &v_full[vs], i * kKeyTile, 0, b);
                 v_issued = i + 1;
             };
             tc::mbar_arrive_expect_tx(q_full, 2 * kQBytes);
@@ -433,16 +443,13 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
                 }
                 v_landed = i + 1;
                 tc::tc_fence_after();
-                const uint32_t v0 = tc::smem_u32(sV + (2 * (i & 1)) * v_bytes);
-                const uint32_t pa = tmem + kPCol + (uint32_t)((i & 1) * kKeyTile);
+                const uint32_t v0 = tc::smem_u32(sV + (i & 1) * v_bytes);
+                const uint32_t pa = tmem + kPCol + (uint32_t)((i & 1) * (kKeyTile / 2));
 #pragma unroll
-                for (int kb = 0; kb < 2; ++kb)
-#pragma unroll
-                    for (int kk = 0; kk < 4; ++kk) {  // 8 keys (32 bytes of V^T) per tf32 MMA
-                        tc::umma_tmem_a_tf32(tmem + kOCol, pa + (uint32_t)(kb * 32 + kk * 8),
-                                             tc::sw128_desc(v0 + kb * v_bytes + kk * 32),
-                                             a.idesc_pv, (i | kb | kk) ? 1u : 0u);
-                    }
+                for (int kk = 0; kk < 4; ++kk)  // 16 keys (8 TMEM columns, 32 bytes of V^T) per MMA
+                    tc::umma_tmem_a_f16(tmem + kOCol, pa + (uint32_t)(kk * 8),
+                                        tc::sw128_desc(v0 + kk * 32), a.idesc_pv,
+                                        (i | kk) ? 1u : 0u);
                 tc::umma_commit(&pv_done[i & 1]);
                 tc::umma_commit(&v_empty[i & 1]);
                 // S_i is done with its K tile (issued before P V_i, so waiting here
@@ -513,9 +520,20 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
                 for (int e = 0; e < 4; ++e) {
                     const float pe =
                         j + e < valid ? f2s_ex2_approx(fmaf(p[j + e], kLog2e, -lj[e])) : 0.0f;
-                    p[j + e] = f2s_round_tf32(pe);
+                    p[j + e] = pe;
                     den += pe;
                 }
+            }
+            // P in fp16, two keys per TMEM column (the lower key in the low
+            // half), scaled by 2^15: p <= 1 (column-normalised), so p 2^15 stays
+            // below the fp16 maximum and p down to ~2e-9 keeps the full 11-bit
+            // significand instead of falling into the subnormals; the
+            // epilogue divides the 2^15 out
+            uint32_t ph16[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                const __half2 h2 = __floats2half2_rn(p[2 * j] * kPScale, p[2 * j + 1] * kPScale);
+                ph16[j] = *reinterpret_cast<const uint32_t*>(&h2);
             }
             // P buffer i & 1 was last read by the P V product of tile i - 2
             if (i > 1) {
@@ -529,7 +547,7 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
                 }
                 tc::tc_fence_after();
             }
-            tc::tmem_st32(tmem + lane_base + kPCol + (uint32_t)(s * kKeyTile + k0), p);
+            tc::tmem_st16(tmem + lane_base + kPCol + (uint32_t)(s * (kKeyTile / 2) + k0 / 2), ph16);
             tc::tc_fence_before();
             tc::mbar_arrive(p_full);
         }
@@ -568,7 +586,7 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
             const bool go = sFlag[5] != 0;
             if (go) {
                 tc::tc_fence_after();
-                const float inv = 1.0f / (den + 1e-9f);
+                const float inv = (1.0f / kPScale) / (den + 1e-9f);  // O holds 2^15 sum p v
                 for (int c0 = c_begin; c0 < c_begin + cw; c0 += 32) {
                     float o[32];
                     tc::tmem_ld32(tmem + lane_base + kOCol + (uint32_t)c0, o);
@@ -597,7 +615,7 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
             }
         } else if (ok) {
             tc::tc_fence_after();
-            const float inv = 1.0f / (den + 1e-9f);
+            const float inv = (1.0f / kPScale) / (den + 1e-9f);  // O holds 2^15 sum p v
             const int qrow = q0 + row;
             const size_t grow = (size_t)b * a.N + qrow;
             for (int c0 = c_begin; c0 < c_begin + cw; c0 += 32) {
@@ -643,9 +661,9 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
 }  // namespace
 
 int attention_tc_workspace_floats(int B, int N, int C) {
-    const int n_pad = (N + 3) & ~3;
-    // qk hi + lo (bf16: 2 x B*N*128 halves = B*N*128 floats), vT, colstats
-    return B * N * 128 + B * C * n_pad + B * N;
+    const int n_pad = (N + 7) & ~7;
+    // qk hi + lo (bf16: 2 x B*N*128 halves = B*N*128 floats), vT (fp16), colstats
+    return B * N * 128 + (B * C * n_pad + 1) / 2 + B * N;
 }
 
 // q, k: (B*N rows, ldqk), width d (<= 64); v (ldv), width C (multiple of 32,
@@ -659,18 +677,18 @@ int attention_tc(const float* q, const float* k, int ldqk, const float* v, int l
         return fail(F2S_ERR_UNSUPPORTED, "attention shape outside the tensor-core kernel");
     int* err = tc_error_word();
     if (!err) return fail(F2S_ERR_CUDA, "attention_tc: device error word unavailable");
-    const int n_pad = (N + 3) & ~3;
+    const int n_pad = (N + 7) & ~7;  // 16-byte fp16 rows of V^T
     __nv_bfloat16* qk_hi = reinterpret_cast<__nv_bfloat16*>(workspace);
     __nv_bfloat16* qk_lo = qk_hi + (size_t)B * N * 2 * kDPad;
-    float* vT = workspace + (size_t)B * N * 128;
-    float* colstats = vT + (size_t)B * C * n_pad;
+    __half* vT = reinterpret_cast<__half*>(workspace + (size_t)B * N * 128);
+    float* colstats = workspace + (size_t)B * N * 128 + ((size_t)B * C * n_pad + 1) / 2;
     {
         TraceScope trace(kTagRowNorm, st);
         qk_split_kernel<<<ceil_div(B * N, 8), 256, 0, st>>>(q, k, ldqk, B * N, d, normalize_qk,
                                                              qk_hi, qk_lo);
         F2S_TRY(check_launch("qk_split_kernel"));
         dim3 grid(ceil_div(n_pad, 64), ceil_div(C, 64), B);
-        v_transpose_kernel<<<grid, 256, 0, st>>>(v, ldv, N, C, n_pad, vT);
+        v_transpose_kernel<<<grid, 256, 0, st>>>(v, ldv, N, C, n_pad, vT, err);
         F2S_TRY(check_launch("v_transpose_kernel"));
     }
     CUtensorMap map_hi_q, map_lo_q, map_hi_k, map_lo_k, map_vt;
@@ -680,7 +698,8 @@ int attention_tc(const float* q, const float* k, int ldqk, const float* v, int l
     F2S_TRY(make_tensor_map_3d(&map_lo_q, qk_lo, false, 2 * kDPad, N, B, row_bytes, row_bytes * N, kDPad, kRows));
     F2S_TRY(make_tensor_map_3d(&map_hi_k, qk_hi, false, 2 * kDPad, N, B, row_bytes, row_bytes * N, kDPad, kKeyTile));
     F2S_TRY(make_tensor_map_3d(&map_lo_k, qk_lo, false, 2 * kDPad, N, B, row_bytes, row_bytes * N, kDPad, kKeyTile));
-    F2S_TRY(make_tensor_map_3d(&map_vt, vT, true, N, C, B, (int64_t)n_pad * 4, (int64_t)n_pad * 4 * C, 32, C));
+    F2S_TRY(make_tensor_map_3d_typed(&map_vt, vT, kTmaF16, N, C, B, (int64_t)n_pad * 2,
+                                     (int64_t)n_pad * 2 * C, kKeyTile, C));
 
     AttnArgs a{};
     a.N = N;
@@ -722,7 +741,7 @@ int attention_tc(const float* q, const float* k, int ldqk, const float* v, int l
         TraceScope trace(kTagAttnOutput, st);
         a.tiles = ceil_div(N, kRows);
         a.idesc_s = tc::make_idesc(kRows, kKeyTile, 1u);
-        a.idesc_pv = tc::make_idesc(kRows, C, 2u);
+        a.idesc_pv = tc::make_idesc(kRows, C, 0u);
         const size_t smem = 1024 + 2 * kRows * 128 + 2 * kKStages * kKeyTile * 128 + 4 * (size_t)C * 128 +
                             (size_t)ceil_div(N, kKeyTile) * kKeyTile * 4 + 32 + 2 * kRows * 4 + 8 +
                             20 * 8 + 16;

@@ -149,6 +149,16 @@ __device__ __forceinline__ void umma_tmem_a_tf32(uint32_t d_tmem, uint32_t a_tme
         : "memory");
 }
 
+// kind::f16 MMA with A (128 rows x 16 fp16, two per 32-bit column) in TMEM.
+__device__ __forceinline__ void umma_tmem_a_f16(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                                uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 // Arrive on `bar` once every tcgen05 operation this thread issued completes.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
     asm volatile(
@@ -231,6 +241,18 @@ __device__ __forceinline__ void tmem_st_wait() {
     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
+// Store 16 consecutive 32-bit columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+        "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
+        "r"(v[15])
+        : "memory");
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
 // Store 32 consecutive fp32 columns of this thread's TMEM lane.
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
     asm volatile(
@@ -298,6 +320,10 @@ enum TmaType : int { kTmaF32 = 0, kTmaBF16 = 1, kTmaF16 = 2 };
 // The same with an explicit element type and swizzle span (128 or 64 bytes).
 int make_tensor_map_2d_typed(CUtensorMap* map, const void* base, TmaType type, int swizzle_bytes,
                              int64_t rows, int64_t cols, int64_t ld, int box_rows, int box_cols);
+// The 3-D form below with an explicit element type (128-byte swizzle).
+int make_tensor_map_3d_typed(CUtensorMap* map, const void* base, TmaType type, int64_t d0,
+                             int64_t d1, int64_t d2, int64_t stride1_bytes, int64_t stride2_bytes,
+                             int box0, int box1);
 
 // 3-D tensor (d0 innermost, element strides given in bytes for dims 1, 2),
 // boxes of (box0 x box1 x 1), 128-byte swizzle: out-of-range rows of a patch

@@ -521,6 +521,13 @@ int make_tensor_map_2d(CUtensorMap* map, const void* base, bool fp32, int64_t ro
 int make_tensor_map_3d(CUtensorMap* map, const void* base, bool fp32, int64_t d0, int64_t d1,
                        int64_t d2, int64_t stride1_bytes, int64_t stride2_bytes, int box0,
                        int box1) {
+    return make_tensor_map_3d_typed(map, base, fp32 ? kTmaF32 : kTmaBF16, d0, d1, d2,
+                                    stride1_bytes, stride2_bytes, box0, box1);
+}
+
+int make_tensor_map_3d_typed(CUtensorMap* map, const void* base, TmaType type, int64_t d0,
+                             int64_t d1, int64_t d2, int64_t stride1_bytes, int64_t stride2_bytes,
+                             int box0, int box1) {
     EncodeTiledFn enc = encode_fn();
     if (!enc) return fail(F2S_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
     F2S_REQUIRE(((uintptr_t)base & 15) == 0, "tensor map base must be 16-byte aligned");
@@ -530,8 +537,10 @@ int make_tensor_map_3d(CUtensorMap* map, const void* base, bool fp32, int64_t d0
     const cuuint64_t strides[2] = {(cuuint64_t)stride1_bytes, (cuuint64_t)stride2_bytes};
     const cuuint32_t box[3] = {(cuuint32_t)box0, (cuuint32_t)box1, 1};
     const cuuint32_t estr[3] = {1, 1, 1};
-    const CUresult r = enc(map, fp32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
-                           3, const_cast<void*>(base), dims, strides, box, estr,
+    const CUtensorMapDataType dt = type == kTmaF32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                   : type == kTmaBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                      : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    const CUresult r = enc(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr,
                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(F2S_ERR_CUDA, "cuTensorMapEncodeTiled (3-D) failed (%d)", (int)r);
