@@ -36,7 +36,8 @@ constexpr int kDPad = 64;         // padded q/k width: 64 bf16 = 128 bytes
 constexpr int kKeyTile = 64;      // keys per pass-2 tile
 constexpr float kPScale = 32768.0f;  // 2^15: fp16 P = p * kPScale (p <= 1)
 constexpr int kKStages = 3;       // pass-2 K tiles in flight
-constexpr int kThreads = 160;     // pass 1: warps 0-3 statistics, warp 4 TMA + MMA
+constexpr int kStatWarps = 8;     // pass 1: two statistics warps per TMEM lane quarter
+constexpr int kThreads = (kStatWarps + 1) * 32;  // pass 1: + one TMA / MMA warp
 // pass 2: warps 0-7 softmax / epilogue (two per TMEM lane quarter, one half of
 // each key tile and of the output columns each), warp 8 TMA + MMA
 constexpr int kOutWarps = 8;
@@ -199,6 +200,7 @@ attn_tc_colstats_kernel(const __grid_constant__ CUtensorMap map_hi,
     uint64_t* s_empty = bars + 7;    // [2]
     uint64_t* done = bars + 9;       // [1]
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
+    float* sPart = reinterpret_cast<float*>(bars + 12);  // [2][128] (max, sum) of the second half
 
     const int b = blockIdx.x / a.tiles;
     const int key0 = (blockIdx.x - b * a.tiles) * kRows;
@@ -206,7 +208,8 @@ attn_tc_colstats_kernel(const __grid_constant__ CUtensorMap map_hi,
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < 10; ++i) tc::mbar_init(&bars[i], i == 7 || i == 8 ? 128 : 1);
+        for (int i = 0; i < 10; ++i)
+            tc::mbar_init(&bars[i], i == 7 || i == 8 ? kStatWarps * 32 : 1);
         tc::fence_barrier_init();
     }
     if (warp == 0) tc::tmem_alloc(tmem_slot, 256);
@@ -215,7 +218,7 @@ attn_tc_colstats_kernel(const __grid_constant__ CUtensorMap map_hi,
     tc::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == 4) {
+    if (warp == kStatWarps) {
         if (lane == 0) {
             bool ok = true;
             int q_issued = 0, q_landed = 0;  // Q tiles loaded / seen complete
@@ -275,38 +278,64 @@ attn_tc_colstats_kernel(const __grid_constant__ CUtensorMap map_hi,
         }
         __syncwarp();
     } else {
-        // one thread per key (TMEM lane): online max / sum over query columns
-        const int row = warp * 32 + lane;
+        // one thread per (key = TMEM lane, half of the query columns): online
+        // max / sum, the two halves combined at the end
+        const int quarter = warp & 3, half = warp >> 2;
+        const int row = quarter * 32 + lane;
         float m = -FLT_MAX, s = 0.0f;
+        bool ok = true;
         for (int j = 0; j < nq; ++j) {
             const int sb = j & 1;
             const uint32_t ph = (uint32_t)(j >> 1) & 1u;
             int ready = 0;
             if (lane == 0) ready = tc::mbar_wait(&s_full[sb], ph, a.err) ? 1 : 0;
-            if (!__shfl_sync(kFull, ready, 0)) break;
+            if (!__shfl_sync(kFull, ready, 0)) {
+                ok = false;
+                break;
+            }
             tc::tc_fence_after();
             const int valid = min(kRows, a.N - j * kRows);
-            const uint32_t t = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(sb * 128);
-            for (int c0 = 0; c0 < kRows; c0 += 32) {
+            const uint32_t t = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(sb * 128);
+            for (int c0 = half * 64; c0 < half * 64 + 64; c0 += 32) {
                 float v[32];
                 tc::tmem_ld32(t + (uint32_t)c0, v);
-                float tmax = -FLT_MAX;
 #pragma unroll
                 for (int i = 0; i < 32; ++i)
-                    if (c0 + i < valid) tmax = fmaxf(tmax, v[i]);
+                    if (c0 + i >= valid) v[i] = -FLT_MAX;
+                // tree max, then four partial sums: short dependency chains
+                float mx[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                    mx[i] = fmaxf(fmaxf(v[i], v[i + 8]), fmaxf(v[i + 16], v[i + 24]));
+                const float tmax = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                                         fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
                 if (tmax > m) {
                     s *= __expf(m - tmax);
                     m = tmax;
                 }
+                float ps[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
                 for (int i = 0; i < 32; ++i)
-                    if (c0 + i < valid) s += __expf(v[i] - m);
+                    if (c0 + i < valid) ps[i & 3] += __expf(v[i] - m);
+                s += (ps[0] + ps[1]) + (ps[2] + ps[3]);
             }
             tc::tc_fence_before();
             tc::mbar_arrive(&s_empty[sb]);
         }
-        const int key = key0 + row;
-        if (key < a.N) a.colstats[(size_t)b * a.N + key] = m + __logf(s);
+        // the second half's (max, sum) through shared memory to the first
+        if (half == 1) {
+            sPart[row] = m;
+            sPart[kRows + row] = s;
+        }
+        asm volatile("bar.sync 1, %0;" ::"n"(kStatWarps * 32) : "memory");
+        if (half == 0 && ok) {
+            const float m1 = sPart[row], s1 = sPart[kRows + row];
+            const float mm = fmaxf(m, m1);
+            const float st = (s > 0.0f ? s * __expf(m - mm) : 0.0f) +
+                             (s1 > 0.0f ? s1 * __expf(m1 - mm) : 0.0f);
+            const int key = key0 + row;
+            if (key < a.N) a.colstats[(size_t)b * a.N + key] = mm + __logf(st);
+        }
     }
     tc::tc_fence_before();
     __syncthreads();
@@ -731,7 +760,7 @@ int attention_tc(const float* q, const float* k, int ldqk, const float* v, int l
         TraceScope trace(kTagAttnColstats, st);
         a.tiles = ceil_div(N, kRows);
         a.idesc_s = tc::make_idesc(kRows, kRows, 1u);
-        const size_t smem = 1024 + 6 * kRows * 128 + 128;
+        const size_t smem = 1024 + 6 * kRows * 128 + 96 + 2 * kRows * 4 + 32;
         F2S_CUDA_TRY(cudaFuncSetAttribute(attn_tc_colstats_kernel,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
         attn_tc_colstats_kernel<<<B * a.tiles, kThreads, smem, st>>>(map_hi_q, map_lo_q, a);
