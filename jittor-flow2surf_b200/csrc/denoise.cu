@@ -125,6 +125,11 @@ fps_kernel(const float* __restrict__ pts, int N, int count, int first, int slice
 // r = d / (d_max + 1e-8) (inference.py:110-122) and vote weights
 // w = exp(-beta r r) (:124-127). One CTA per seed: exact 8-pass radix select
 // of the k-th 64-bit key, ordered compaction, bitonic sort in shared memory.
+// The histogram passes walk the points with the block's stride, so a warp's
+// coordinate loads are coalesced (the ordered compaction keeps contiguous
+// per-thread ranges); the distances from one seed share their high bytes, so
+// the histogram adds of a warp mostly hit one bin and are aggregated per
+// distinct bin (__match_any_sync) before the shared-memory atomic.
 // ---------------------------------------------------------------------------
 constexpr int kPiThreads = 1024;
 
@@ -176,19 +181,25 @@ patch_index_kernel(const float* __restrict__ pts, int N, const int32_t* __restri
     const int tid = threadIdx.x;
     const int sp = seeds[s];
     const double sx = pts[3 * sp], sy = pts[3 * sp + 1], sz = pts[3 * sp + 2];
-    const int chunk = (N + kPiThreads - 1) / kPiThreads;
-    const int lo = min(N, tid * chunk), hi = min(N, lo + chunk);
-
+    const unsigned lanes_below = (1u << (tid & 31)) - 1u;
     unsigned long long prefix = 0ull, mask = 0ull;
     unsigned need = (unsigned)k;
     for (int pass = 0; pass < 8; ++pass) {
         const int shift = 56 - 8 * pass;
         if (tid < 256) hist[tid] = 0u;
         __syncthreads();
-        for (int n = lo; n < hi; ++n) {
-            const unsigned long long key =
-                (unsigned long long)__double_as_longlong(sqdist64(pts + 3 * n, sx, sy, sz));
-            if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255ull], 1u);
+        // the same trip count in every thread, so whole warps vote together
+        for (int base = 0; base < N; base += kPiThreads) {
+            const int n = base + tid;
+            unsigned long long key = 0ull;
+            if (n < N) key = (unsigned long long)__double_as_longlong(sqdist64(pts + 3 * n, sx, sy, sz));
+            const bool act = n < N && (key & mask) == prefix;
+            const unsigned bin = (unsigned)((key >> shift) & 255ull);
+            const unsigned am = __ballot_sync(0xffffffffu, act);
+            if (act) {
+                const unsigned peers = __match_any_sync(am, bin);
+                if ((peers & lanes_below) == 0u) atomicAdd(&hist[bin], (unsigned)__popc(peers));
+            }
         }
         __syncthreads();
         if (tid < 32) {
@@ -233,6 +244,8 @@ patch_index_kernel(const float* __restrict__ pts, int N, const int32_t* __restri
     const unsigned long long T = prefix;
     const unsigned n_less = (unsigned)k - need;
 
+    const int chunk = (N + kPiThreads - 1) / kPiThreads;
+    const int lo = min(N, tid * chunk), hi = min(N, lo + chunk);
     unsigned cl = 0u, ce = 0u;
     for (int n = lo; n < hi; ++n) {
         const unsigned long long key =
