@@ -206,8 +206,9 @@ edge_tc_kernel(const __grid_constant__ CUtensorMap map_w, const EdgeTcArgs a) {
     float* sLn = sCb + cout;      // cout x {|gain|, shift}
     float* sSgn = sLn + cout * 2;  // cout: sign of the gain (+1 / -1)
     float* sStat = sSgn + cout;    // [2][2][128]
+    float* sRed = sStat + 4 * kRows;  // [8 epilogue warps][32]: per-channel maxima (K = 32)
     uint64_t* bars = reinterpret_cast<uint64_t*>(
-        (reinterpret_cast<uintptr_t>(sStat + 4 * kRows) + 7) & ~uintptr_t(7));
+        (reinterpret_cast<uintptr_t>(sRed + kEpilogueWarps * 32) + 7) & ~uintptr_t(7));
     uint64_t* a_empty = bars + 2;   // [2]
     uint64_t* t_full = bars + 4;    // [2]
     uint64_t* t_empty = bars + 6;   // [2]
@@ -711,16 +712,21 @@ edge_tc_kernel(const __grid_constant__ CUtensorMap map_w, const EdgeTcArgs a) {
                 }
                 int off = 0;
                 if (K == 32) {
-                    // one point per warp: a warp-wide max per channel, lane c
-                    // keeps channel c
-                    float mine = 0.0f;
+                    // one point per warp: a warp-wide max per channel; lane 0
+                    // writes the 32 maxima to the warp's slots and lane c reads
+                    // channel c back
+                    float* red = sRed + (warp - kEpiWarp0) * 32;
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        float r;
-                        asm("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(y[i]));
-                        mine = lane == i ? r : mine;
+                    for (int i = 0; i < 32; i += 4) {
+                        float r[4];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e)
+                            asm("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(r[e]) : "f"(y[i + e]));
+                        if (lane == 0) *reinterpret_cast<float4*>(red + i) = make_float4(r[0], r[1], r[2], r[3]);
                     }
-                    y[0] = mine;
+                    __syncwarp();
+                    y[0] = red[lane];
+                    __syncwarp();  // read before the next chunk's maxima overwrite the slots
                     off = lane;
                 } else
 #pragma unroll
@@ -773,7 +779,8 @@ size_t edge_tc_smem(int mode, int H, int cout, int bufs, int stage_bufs, int sta
     const size_t kblocks = (size_t)ceil_div(H, 128 / elem);
     const size_t copies = mode == kModeSplit ? 2 : 1;
     return 1024 + copies * kblocks * 128 * ((size_t)bufs * kRows + cout) + 2 * (size_t)kUBytes +
-           2 * (size_t)H * 32 + sizeof(float) * ((size_t)H * 2 + 52 + (size_t)cout * 4 + 4 * kRows) +
+           2 * (size_t)H * 32 +
+           sizeof(float) * ((size_t)H * 2 + 52 + (size_t)cout * 4 + 4 * kRows + kEpilogueWarps * 32) +
            128 + 128 + (size_t)kEpilogueWarps * stage_bufs * stage_bytes;
 }
 
