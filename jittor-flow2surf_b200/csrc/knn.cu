@@ -163,8 +163,7 @@ knn_kernel(const float* __restrict__ features, int C_runtime, int N, int k, int 
             uint32_t g0 = 0xffffffffu, g1 = 0xffffffffu;
 #pragma unroll
             for (int r = 0; r < SLOTS; ++r) {
-                const int j = r * 32 + lane;
-                const uint32_t kv = (j < N && j != q) ? key[r] : 0xffffffffu;
+                const uint32_t kv = key[r];  // 0xffffffff for the query itself and slots past N
                 // even / odd slots: both groups sample every part of the index
                 // range (patch points are stored in radial order)
                 if ((r & 1) == 0) g0 = kv < g0 ? kv : g0;
@@ -174,10 +173,13 @@ knn_kernel(const float* __restrict__ features, int C_runtime, int N, int k, int 
             const int src = actual_k - 1;  // element index of the threshold (< 32)
             const uint32_t T = __shfl_sync(kFull, g0, src);
             int c = 0;
+            // below the all-ones key the threshold already excludes the slots
+            // that are not candidates; only T = 0xffffffff needs the check
+            const bool check_valid = T == 0xffffffffu;
 #pragma unroll
             for (int r = 0; r < SLOTS; ++r) {
                 const int j = r * 32 + lane;
-                const bool cand = j < N && j != q && key[r] <= T;
+                const bool cand = key[r] <= T && (!check_valid || (j < N && j != q));
                 const unsigned m = __ballot_sync(kFull, cand);
                 const int pos = c + __popc(m & lanes_below);
                 if (cand && pos < 64) cl[pos] = ((uint64_t)key[r] << 32) | (uint32_t)j;
