@@ -102,7 +102,7 @@ __global__ void ln_modulate_kernel(const float* __restrict__ x, int ldx, void* _
                     }
                 }
             }
-            if (kHalf && out_of_range) atomicExch(err, 2);
+            if (kHalf && out_of_range) atomicExch(err, tc::kTcFp16Range);
         }
     } else {
         const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
