@@ -45,6 +45,7 @@ UNIT = "points/s"
 DENOISE = dict(patch_size=1000, seed_k=3, num_steps=3, patch_agg_beta=5.0,
                alpha_clean_power=1.0, alpha_noisy_power=6.0)
 L2_FLUSH_BYTES = 512 << 20
+TRACED_STEPS = 5
 
 
 def parse_args():
@@ -55,8 +56,8 @@ def parse_args():
     p.add_argument("--impl", choices=["b200", "reference"], default="b200")
     p.add_argument("--points", type=int, default=50_000)
     p.add_argument("--seed-k", type=int, default=DENOISE["seed_k"])
-    p.add_argument("--cpu-sample-points", type=int, default=5_000,
-                   help="cloud size of the bounded CPU-baseline sample")
+    p.add_argument("--cpu-sample-patches", type=int, default=10,
+                   help="patches of the cloud in the bounded CPU-baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--precision", choices=["fp32", "tf32"], default="tf32",
                    help="arithmetic of the trunk and decoder contractions")
@@ -140,9 +141,44 @@ def make_model(precision: str = "fp32", encoder_precision: str | None = None):
 # CPU arms (the oracle restatement of the reference's path)
 # ---------------------------------------------------------------------------
 
-def cpu_sample(points: int, seed_k: int, steps: int = 1, warmup: int = 0):
-    """Time the CPU restatement on a bounded sample: a `points`-point cloud of
-    the same recipe at the same patch density. Returns (points/s, seconds)."""
+CPU_SAMPLE_PATCHES = 15   # patches of the cloud per reference-arm step (10 steps cover all 150)
+
+
+def cpu_denoise_sample(cloud: np.ndarray, net, seed_k: int, sample: int, offset: int) -> float:
+    """Seconds the CPU restatement of the reference's patch_denoise
+    (flow2surf/inference.py:68-198) spends on a bounded sample of the full
+    denoise of `cloud`: `sample` of its P patches (a contiguous window from
+    `offset`, wrapping) through everything that scales with the patches (patch
+    index, aggregation weights, and for each of the 3 Euler steps the model
+    forward, the vote fusion and the update), plus the cloud's farthest-point
+    seeds (all P of them, a serial per-cloud cost) charged pro rata sample / P."""
+    from oracle import inference as oinf
+
+    kw = DENOISE
+    N = len(cloud)
+    P = oinf.patch_seed_count(N, kw["patch_size"], seed_k)
+    sample = min(sample, P)
+    t0 = time.perf_counter()
+    seeds = oinf.patch_seed_indices(cloud, kw["patch_size"], seed_k, np.random.default_rng(0))
+    t_fps = time.perf_counter() - t0
+    t1 = time.perf_counter()
+    sel = seeds[(offset + np.arange(sample)) % P]
+    nbr, radial = oinf.build_patch_index(cloud, sel, kw["patch_size"])
+    point_idx, w, wsum, uncovered = oinf.build_aggregation(nbr, radial, kw["patch_agg_beta"], N)
+    alphas = oinf.alpha_schedule(kw["num_steps"], kw["alpha_clean_power"],
+                                 kw["alpha_noisy_power"])
+    chunk = (P + 7) // 8  # the reference's num_chunks = 8 batching
+    current = cloud.copy()
+    for step in range(kw["num_steps"] - 1, -1, -1):
+        a = float(alphas[step])
+        a_prev = float(alphas[step - 1]) if step > 0 else 0.0
+        votes = oinf.predict_velocity(net, current, nbr, sel, a, chunk)
+        velocity = oinf.aggregate_votes(votes, point_idx, w, wsum, N)
+        current = oinf.euler_update(current, velocity, a - a_prev, uncovered)
+    return t_fps * sample / P + (time.perf_counter() - t1)
+
+
+def cpu_sampler(points: int, seed_k: int):
     import torch
 
     from flow2surf_b200.synthetic import DEFAULT_CONFIG, random_parameters
@@ -152,44 +188,47 @@ def cpu_sample(points: int, seed_k: int, steps: int = 1, warmup: int = 0):
     torch.set_num_threads(os.cpu_count())
     cloud = make_cloud(points, 0)
     net = TorchOracleNet(DEFAULT_CONFIG, random_parameters(DEFAULT_CONFIG, seed=0))
-    kw = dict(DENOISE, seed_k=seed_k)
-    patches = oinf.patch_seed_count(points, kw["patch_size"], seed_k)
-    chunks = max(1, (patches + 4) // 5)
-    times = []
-    for i in range(warmup + steps):
-        t0 = time.perf_counter()
-        oinf.patch_denoise(net, cloud, kw["patch_size"], seed_k, kw["num_steps"], chunks,
-                           rng=np.random.default_rng(0), patch_agg_beta=kw["patch_agg_beta"],
-                           alpha_clean_power=kw["alpha_clean_power"],
-                           alpha_noisy_power=kw["alpha_noisy_power"])
-        if i >= warmup:
-            times.append(time.perf_counter() - t0)
-    return points / statistics.mean(times), times
+    P = oinf.patch_seed_count(points, DENOISE["patch_size"], seed_k)
+    return cloud, net, P
+
+
+def cpu_sample_text(sample: int, patches: int, points: int) -> str:
+    return (f"CPU restatement of the reference's path (torch-CPU float32 model, NumPy/SciPy "
+            f"patch index and fusion; Jittor is not installed), all {os.cpu_count()} host "
+            f"threads, on the {points:,}-point cloud itself: {sample} of its {patches} patches "
+            f"per step through the patch index, weights and 3 Euler steps of forward, fusion "
+            f"and update, FPS charged pro rata; points/s = points x {sample}/{patches} / time")
 
 
 def cpu_baseline_line(args) -> dict:
-    value, times = cpu_sample(args.cpu_sample_points, args.seed_k)
+    cloud, net, P = cpu_sampler(args.points, args.seed_k)
+    sample = max(1, min(args.cpu_sample_patches, P))
+    seconds = cpu_denoise_sample(cloud, net, args.seed_k, sample, 0)
+    value = args.points * sample / P / seconds
     return {"value": value, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
-            "sample": (f"CPU restatement (torch-CPU float32 oracle, all host threads; Jittor is not "
-                       f"installed) on a {args.cpu_sample_points:,}-point cloud of the same "
-                       f"recipe and patch density, one full denoise ({times[0]:.1f} s)")}
+            "sample": cpu_sample_text(sample, P, args.points) + f" ({seconds:.1f} s, one sample)"}
 
 
 def run_reference(args, rank: int, world: int) -> None:
     if rank != 0:
         return
-    sample = max(1000, min(args.cpu_sample_points, 2_000))
-    value, times = cpu_sample(sample, args.seed_k, steps=args.steps, warmup=min(args.warmup, 1))
+    cloud, net, P = cpu_sampler(args.points, args.seed_k)
+    sample = min(CPU_SAMPLE_PATCHES, P)
+    times = []
+    for i in range(args.warmup + args.steps):
+        seconds = cpu_denoise_sample(cloud, net, args.seed_k, sample, (i * sample) % P)
+        if i >= args.warmup:
+            times.append(seconds)
+    value = args.points * sample / P / statistics.mean(times)
+    ms_step = 1e3 * args.points / value     # one full denoise of the cloud at this rate
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": 1e3 * statistics.mean(times),
+        "warmup": args.warmup, "ms_per_step": ms_step,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic", "impl": "reference",
         "config": workload_config(args, 1),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
-                         "sample": (f"each step: one full denoise of a {sample:,}-point cloud "
-                                    "of the same recipe and patch density by the CPU "
-                                    "restatement (Jittor unavailable)")},
+                         "sample": cpu_sample_text(sample, P, args.points)},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -361,15 +400,23 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
     gpu_id = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
     with ClockSampler(gpu_id) as clocks:
         barrier()
-        with trace.recording() as rec:
-            for i in range(steps):
-                flush.fill_(i & 0xFF)
-                starts[i].record()
-                out = one_step()
-                stops[i].record()
-            barrier()
+        for i in range(steps):
+            flush.fill_(i & 0xFF)
+            starts[i].record()
+            out = one_step()
+            stops[i].record()
+        barrier()
     elapsed_ms = sum(s.elapsed_time(e) for s, e in zip(starts, stops))
     total = torch.tensor([elapsed_ms], dtype=torch.float64, device=dev)
+
+    # per-kernel breakdown: a separate pass of the same steps with a CUDA-event
+    # pair around every launch (the events cost the timed steps above nothing)
+    traced_steps = min(steps, TRACED_STEPS)
+    with trace.recording() as rec:
+        for i in range(traced_steps):
+            flush.fill_(i & 0xFF)
+            one_step()
+        barrier()
 
     # end-to-end through the public API (value measured the same way, host in/out)
     e2e_s = 0.0
@@ -400,7 +447,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
     if shard:  # rank 0's share, which its kernel trace covers
         begin, end = shard_range(patches, rank, world)
         patches = end - begin
-    forward_points = steps * kw["num_steps"] * patches * kw["patch_size"]
+    forward_points = traced_steps * kw["num_steps"] * patches * kw["patch_size"]
     kernels = rec.kernels
     total_kernel_ms = sum(ms for ms, _ in kernels.values()) or 1.0
     line = {
@@ -413,9 +460,11 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
         "roofline": roofline(kernels, forward_points, dims),
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(cloud.nbytes),
                 "d2h_bytes_per_step": int(host_out.nbytes)},
-        "gpu_launches": rec.launches,
+        "gpu_launches": rec.launches * steps // traced_steps,
         "clocks": clocks.summary(),
-        "kernels": {k: {"ms_per_step": ms / steps, "launches_per_step": n / steps,
+        "kernel_breakdown": (f"separate traced pass of {traced_steps} steps (CUDA events "
+                             "around every launch on its stream); value is timed untraced"),
+        "kernels": {k: {"ms_per_step": ms / traced_steps, "launches_per_step": n / traced_steps,
                         "share": ms / total_kernel_ms} for k, (ms, n) in
                     sorted(kernels.items(), key=lambda kv: -kv[1][0])},
     }

@@ -58,12 +58,12 @@ int f2s_trace_collect(double* total_ms, int64_t* launches);
 
 /*
  * k nearest non-self neighbours in feature space.
- * Replaces knn_indices (flow2surf/models/ops/knn.py:55-86) and its kernel
+ * Replaces knn_indices (flow2surf/models/ops/knn.py:35-66) and its kernel
  * global_knn (flow2surf/models/ops/cuda/knn_global.cu:1-57, keys from
  * flow2surf/models/ops/cuda/knn.cuh:7-17).
  *   features : (B, C, N) float32
  *   indices  : (B, N, k) int32, ascending (distance, index); when k > N-1 the
- *              last real neighbour is repeated (knn.py:83-85); N <= 1 gives 0.
+ *              last real neighbour is repeated (knn.py:63-65); N <= 1 gives 0.
  * Distances are the reference kernel's fp32 expression, bit for bit.
  * Limits: 1 <= k <= 32 (F2S_KNN_MAX_K), N <= 2048 (F2S_KNN_MAX_POINTS) and
  * C*N*4 <= F2S_KNN_MAX_FEATURE_BYTES (one patch's features are staged in
@@ -143,6 +143,15 @@ int f2s_linear(const void* x, int ldx, const void* weight, const float* bias, fl
  */
 int f2s_device_error(int* value, int reset, void* stream);
 
+/*
+ * Self-test of the failure path above (no counterpart in the reference): one
+ * thread waits on an mbarrier that nothing arrives on, bounded by `polls`
+ * (1 .. 2^20; each poll parks the thread for at most ~1 us), gives up and
+ * sets the device error word to 1, as a tensor-core kernel does when a wait
+ * runs out. Nothing faults or hangs; the context stays usable.
+ */
+int f2s_selftest_wait_timeout(int polls, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Model (flow2surf/models/network.py:29-95)                                */
 /* ------------------------------------------------------------------------ */
@@ -204,6 +213,24 @@ int f2s_model_workspace_bytes(const f2s_model_config* cfg, int B, int M, size_t*
 int f2s_model_forward(const f2s_model_config* cfg, const float* params, const float* x,
                       const float* alpha, int B, int M, float* velocity,
                       void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * The transformer trunk alone: AlphaEmbed and the num_blocks AdaLN-Zero
+ * blocks (offset attention + SwiGLU FFN) of the model above
+ * (flow2surf/models/network.py:75-80, transformer.py:75-89), in place on the
+ * residual stream; the cfg->precision arithmetic (fp32 CUDA cores or tf32
+ * tensor cores). For the trunk micro-benchmark and for callers that run the
+ * encoder elsewhere.
+ *   params : the same blob as f2s_model_forward (only the alpha embedding and
+ *            block segments are read)
+ *   x      : (B, M, feat_dim) float32 POINT-MAJOR (the reference's (B, C, M)
+ *            transposed), 16-byte aligned; updated in place
+ *   alpha  : (B,) float32
+ *   workspace: f2s_model_workspace_bytes(cfg, B, M) bytes.
+ */
+int f2s_trunk_forward(const f2s_model_config* cfg, const float* params, float* x,
+                      const float* alpha, int B, int M, void* workspace, size_t workspace_bytes,
+                      void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* Patch-wise reverse flow (flow2surf/inference.py:19-198)                  */
@@ -325,8 +352,13 @@ int f2s_chamfer(const float* pred, const float* target, int B, int M, int N, dou
  * that loads this library until the process exits) instead of a workspace.
  *   Requires B * (M + N) <= F2S_CHAMFER_STATIC_MAX_POINTS, else
  *   F2S_ERR_UNSUPPORTED. Allocates nothing.
- *   The first call on each device looks up the array's device address (with
- *   that device current); make that first call before any stream capture.
+ *   The first call on each device (with that device current) looks up the
+ *   array's device address; under CUDA's lazy module loading (the default)
+ *   that first call is also what loads the library's module on the device,
+ *   which reserves the array, and it loads the entry's kernels. So make one
+ *   call per device before the phase in which nothing may be allocated, and
+ *   before any stream capture: a call with B = 0 (any non-null pointers,
+ *   M, N >= 1) does only this set-up.
  *   All calls share the one array: calls that overlap on the GPU (other
  *   streams, other host threads) race and must be serialised by the caller.
  */

@@ -29,9 +29,11 @@ int check_launch(const char* what) {
 }
 
 int sm_count() {
+    static std::mutex cache_mutex;
     static int cached[64] = {0};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    std::lock_guard<std::mutex> lock(cache_mutex);
     if (cached[dev] == 0) {
         int n = 0;
         if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)

@@ -537,11 +537,11 @@ int linear_op(const GemmArgs& g, int precision, cudaStream_t st, float* split_a 
     return tc_gemm(op, st);
 }
 
-int forward(const Dims& d, const Layout& L, const float* P, const float* x_in, const float* alpha,
-            int B, int M, float* velocity, const Workspace& w, cudaStream_t st) {
-    const int R = B * M;
+// AlphaEmbed (network.py:10-26, :75-76) and every block's AdaLN modulation
+// (transformer.py:48-54) into w.cond, w.mod.
+int condition(const Dims& d, const Layout& L, const float* P, const float* alpha, int B,
+              const Workspace& w, cudaStream_t st) {
     const int C = d.C;
-    // conditioning
     {
         CondArgs ca{};
         ca.P = P;
@@ -560,6 +560,17 @@ int forward(const Dims& d, const Layout& L, const float* P, const float* x_in, c
         cond_mod_kernel<<<B, 256, sizeof(float) * 5 * d.A, st>>>(ca, alpha, w.cond, w.mod);
         F2S_TRY(check_launch("cond_mod_kernel"));
     }
+    return F2S_OK;
+}
+
+int trunk(const Dims& d, const Layout& L, const float* P, int B, int M, float* x,
+          const Workspace& w, cudaStream_t st);
+
+int forward(const Dims& d, const Layout& L, const float* P, const float* x_in, const float* alpha,
+            int B, int M, float* velocity, const Workspace& w, cudaStream_t st) {
+    const int R = B * M;
+    const int C = d.C;
+    F2S_TRY(condition(d, L, P, alpha, B, w, st));
     // input embedding + xyz
     if (d.sd[0] <= 64) {
         const int S0 = d.sd[0];
@@ -648,7 +659,34 @@ int forward(const Dims& d, const Layout& L, const float* P, const float* x_in, c
         F2S_TRY(linear_op(g, d.enc_gemm_precision, st, w.split_a, w.split_w));
     }
     F2S_TRY(ln_affine_leaky(w.x, C, P + L.proj_ln_w, P + L.proj_ln_b, R, C, false, st));
-    // trunk (transformer.py:75-89)
+    F2S_TRY(trunk(d, L, P, B, M, w.x, w, st));
+    // decoder (decoder.py:8-32)
+    const bool tf32_trunk = d.precision == F2S_PRECISION_TF32;
+    const float* cur = w.x;
+    int in_dim = C;
+    float* bufs[2] = {w.dec0, w.dec1};
+    for (int i = 0; i < d.ndec; ++i) {
+        float* out = bufs[i & 1];
+        GemmArgs gd = gemm_args(cur, in_dim, P + L.dec[i].w, nullptr, out, d.dd[i], R, d.dd[i],
+                                in_dim);
+        gd.tag = kTagGemmDecoder;
+        F2S_TRY(linear_op(gd, d.precision, st));
+        F2S_TRY(ln_affine_leaky(out, d.dd[i], P + L.dec[i].ln_w, P + L.dec[i].ln_b, R, d.dd[i],
+                                tf32_trunk, st));
+        cur = out;
+        in_dim = d.dd[i];
+    }
+    GemmArgs go = gemm_args(cur, in_dim, P + L.dec_out_w, nullptr, velocity, 3, R, 3, in_dim);
+    go.tag = kTagGemmDecoder;
+    return linear_op(go, d.precision, st);
+}
+
+// The AdaLN-Zero blocks (transformer.py:75-89) on the point-major residual
+// stream x (B*M rows of C), in place; w.mod holds the blocks' modulation.
+int trunk(const Dims& d, const Layout& L, const float* P, int B, int M, float* x,
+          const Workspace& w, cudaStream_t st) {
+    const int R = B * M;
+    const int C = d.C;
     const int ld_qkv = C + 2 * d.qk;
     // operands of tf32 contractions are rounded to the nearest tf32 where made
     const bool tf32_trunk = d.precision == F2S_PRECISION_TF32;
@@ -672,7 +710,7 @@ int forward(const Dims& d, const Layout& L, const float* P, const float* x_in, c
     for (int i = 0; i < d.NB; ++i) {
         const BlockParams& bp = L.block[i];
         const float* mod = w.mod + (size_t)i * 6 * C;
-        F2S_TRY(ln_modulate(w.x, C, w.h, C, mod, mstride, 0, C, R, M, C, tf32_trunk, st));
+        F2S_TRY(ln_modulate(x, C, w.h, C, mod, mstride, 0, C, R, M, C, tf32_trunk, st));
         GemmArgs gq = gemm_args(w.h, C, P + bp.qkv_w, nullptr, w.qkv, ld_qkv, R, ld_qkv, C);
         gq.tag = kTagGemmQkv;
         F2S_TRY(linear_op(gq, d.precision, st));
@@ -687,7 +725,7 @@ int forward(const Dims& d, const Layout& L, const float* P, const float* x_in, c
                                         st);
         }
         F2S_TRY(attn_status);
-        GemmArgs g = gemm_args(w.offs, C, P + bp.proj_w, nullptr, w.x, C, R, C, C);
+        GemmArgs g = gemm_args(w.offs, C, P + bp.proj_w, nullptr, x, C, R, C, C);
         g.epilogue = kEpiGatedResidual;
         g.gate = mod + 2 * C;
         g.gate_stride = mstride;
@@ -695,9 +733,9 @@ int forward(const Dims& d, const Layout& L, const float* P, const float* x_in, c
         g.tag = kTagGemmProj;
         F2S_TRY(linear_op(g, d.precision, st));
         if (ffn_fp16)
-            F2S_TRY(ln_modulate_f16(w.x, C, w.h, C, mod, mstride, 3 * C, 4 * C, R, M, C, st));
+            F2S_TRY(ln_modulate_f16(x, C, w.h, C, mod, mstride, 3 * C, 4 * C, R, M, C, st));
         else
-            F2S_TRY(ln_modulate(w.x, C, w.h, C, mod, mstride, 3 * C, 4 * C, R, M, C, tf32_trunk, st));
+            F2S_TRY(ln_modulate(x, C, w.h, C, mod, mstride, 3 * C, 4 * C, R, M, C, tf32_trunk, st));
         GemmArgs sw = gemm_args(w.h, C, P + bp.gate_w, P + bp.gate_b, w.ffh, d.Hf, R, d.Hf, C);
         sw.epilogue = kEpiSwiGlu;
         sw.W2 = P + bp.ff1_w;
@@ -712,7 +750,7 @@ int forward(const Dims& d, const Layout& L, const float* P, const float* x_in, c
         sw.W16 = ffn_fp16 ? (const void*)(w.ffn_w16 + (size_t)(3 * i) * ffn_n) : nullptr;
         sw.W2_16 = ffn_fp16 ? (const void*)(w.ffn_w16 + (size_t)(3 * i + 1) * ffn_n) : nullptr;
         F2S_TRY(linear_op(sw, d.precision, st));
-        GemmArgs f2 = gemm_args(w.ffh, d.Hf, P + bp.ff2_w, P + bp.ff2_b, w.x, C, R, C, d.Hf);
+        GemmArgs f2 = gemm_args(w.ffh, d.Hf, P + bp.ff2_w, P + bp.ff2_b, x, C, R, C, d.Hf);
         f2.epilogue = kEpiGatedResidual;
         f2.gate = mod + 5 * C;
         f2.gate_stride = mstride;
@@ -722,24 +760,7 @@ int forward(const Dims& d, const Layout& L, const float* P, const float* x_in, c
         f2.W16 = ffn_fp16 ? (const void*)(w.ffn_w16 + (size_t)(3 * i + 2) * ffn_n) : nullptr;
         F2S_TRY(linear_op(f2, d.precision, st));
     }
-    // decoder (decoder.py:8-32)
-    const float* cur = w.x;
-    int in_dim = C;
-    float* bufs[2] = {w.dec0, w.dec1};
-    for (int i = 0; i < d.ndec; ++i) {
-        float* out = bufs[i & 1];
-        GemmArgs gd = gemm_args(cur, in_dim, P + L.dec[i].w, nullptr, out, d.dd[i], R, d.dd[i],
-                                in_dim);
-        gd.tag = kTagGemmDecoder;
-        F2S_TRY(linear_op(gd, d.precision, st));
-        F2S_TRY(ln_affine_leaky(out, d.dd[i], P + L.dec[i].ln_w, P + L.dec[i].ln_b, R, d.dd[i],
-                                tf32_trunk, st));
-        cur = out;
-        in_dim = d.dd[i];
-    }
-    GemmArgs go = gemm_args(cur, in_dim, P + L.dec_out_w, nullptr, velocity, 3, R, 3, in_dim);
-    go.tag = kTagGemmDecoder;
-    return linear_op(go, d.precision, st);
+    return F2S_OK;
 }
 
 }  // namespace
@@ -791,6 +812,28 @@ extern "C" int f2s_model_forward(const f2s_model_config* cfg, const float* param
         return fail(F2S_ERR_WORKSPACE, "model forward needs %zu workspace bytes, got %zu", w.bytes,
                     workspace_bytes);
     return forward(d, L, params, x, alpha, B, M, velocity, w, as_stream(stream));
+}
+
+extern "C" int f2s_trunk_forward(const f2s_model_config* cfg, const float* params, float* x,
+                                 const float* alpha, int B, int M, void* workspace,
+                                 size_t workspace_bytes, void* stream) {
+    Dims d;
+    F2S_TRY(check_config(cfg, d));
+    F2S_REQUIRE(B >= 0 && M >= 0, "bad shape B=%d M=%d", B, M);
+    if (B == 0 || M == 0) return F2S_OK;
+    F2S_LIMIT(M <= F2S_KNN_MAX_POINTS, "patch of %d points exceeds %d", M, F2S_KNN_MAX_POINTS);
+    F2S_LIMIT((int64_t)B * M < (1ll << 31) / 2048, "too many points in one call: B*M=%lld",
+              (long long)B * M);
+    F2S_REQUIRE(params && x && alpha && workspace, "trunk forward: null pointer");
+    F2S_REQUIRE(((uintptr_t)x & 15) == 0, "trunk forward: x must be 16-byte aligned");
+    const Layout L = make_layout(d);
+    const Workspace w = carve(d, B, M, static_cast<char*>(workspace));
+    if (workspace_bytes < w.bytes)
+        return fail(F2S_ERR_WORKSPACE, "trunk forward needs %zu workspace bytes, got %zu", w.bytes,
+                    workspace_bytes);
+    cudaStream_t st = as_stream(stream);
+    F2S_TRY(condition(d, L, params, alpha, B, w, st));
+    return trunk(d, L, params, B, M, x, w, st);
 }
 
 extern "C" int f2s_neighbor_reduce_workspace_bytes(int B, int N, int C, size_t* bytes) {

@@ -231,7 +231,11 @@ unsigned long long* g_scratch_address[kMaxDevices] = {nullptr};
 
 // The device address of g_chamfer_scratch on the current device. In host code
 // the array's name is only a host-side stand-in, so the address is looked up
-// once per device (with that device current) and cached.
+// once per device (with that device current) and cached. With CUDA's lazy
+// module loading (the default) that first look-up is also what loads this
+// file's module on the device and so reserves the array; the kernels the
+// entry launches are loaded here too (cudaFuncGetAttributes loads a
+// function), so later calls load and reserve nothing.
 int chamfer_scratch(unsigned long long** out) {
     int dev = 0;
     F2S_CUDA_TRY(cudaGetDevice(&dev));
@@ -240,6 +244,10 @@ int chamfer_scratch(unsigned long long** out) {
     if (g_scratch_address[dev] == nullptr) {
         void* ptr = nullptr;
         F2S_CUDA_TRY(cudaGetSymbolAddress(&ptr, g_chamfer_scratch));
+        cudaFuncAttributes attr;
+        F2S_CUDA_TRY(cudaFuncGetAttributes(&attr, init_keys_kernel));
+        F2S_CUDA_TRY(cudaFuncGetAttributes(&attr, nearest_kernel));
+        F2S_CUDA_TRY(cudaFuncGetAttributes(&attr, chamfer_reduce_kernel));
         g_scratch_address[dev] = static_cast<unsigned long long*>(ptr);
     }
     *out = g_scratch_address[dev];
@@ -250,6 +258,10 @@ int chamfer_scratch(unsigned long long** out) {
 extern "C" int f2s_chamfer_static(const float* pred, const float* target, int B, int M, int N,
                                   double* chamfer, void* stream) {
     F2S_TRY(check_sets(pred, target, B, M, N));
+    // the per-device set-up comes first, so that a call with B = 0 does it and
+    // nothing else: the way to prepare a device before allocation is ruled out
+    unsigned long long* k1 = nullptr;
+    F2S_TRY(chamfer_scratch(&k1));
     if (B == 0) return F2S_OK;
     F2S_REQUIRE(chamfer != nullptr, "chamfer: null pointer");
     const int64_t keys = (int64_t)B * ((int64_t)M + N);
@@ -257,10 +269,9 @@ extern "C" int f2s_chamfer_static(const float* pred, const float* target, int B,
               "chamfer_static: B*(M+N) = %lld points exceed the built-in scratch of %d; use "
               "f2s_chamfer with a caller workspace",
               (long long)keys, F2S_CHAMFER_STATIC_MAX_POINTS);
-    unsigned long long* k1 = nullptr;
-    F2S_TRY(chamfer_scratch(&k1));
     unsigned long long* k2 = k1 + (size_t)B * M;
     cudaStream_t st = as_stream(stream);
+    TraceScope trace(kTagNearest, st);
     // one_way() rewrites every key it uses with its starting value first, so
     // whatever an earlier call left in the array does not matter.
     F2S_TRY(one_way(pred, target, B, M, N, k1, st));

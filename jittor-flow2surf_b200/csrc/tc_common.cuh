@@ -62,9 +62,11 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Bounded wait for the phase of `parity` to complete; false (and *err set)
-// when it does not within kSpinLimit polls or another thread already failed.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
-    for (uint32_t i = 0; i < kSpinLimit; ++i) {
+// when it does not within `limit` polls (kSpinLimit unless given) or another
+// thread already failed.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err,
+                                          uint32_t limit = kSpinLimit) {
+    for (uint32_t i = 0; i < limit; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
         if ((i & 63u) == 63u && *reinterpret_cast<volatile int*>(err) != kTcOk) return false;
         if (i >= 64) __nanosleep(32);

@@ -769,6 +769,29 @@ extern "C" int f2s_linear(const void* x, int ldx, const void* weight, const floa
     return f2s::tc_gemm(op, st);
 }
 
+namespace f2s {
+namespace {
+// One thread waits, with a bound of `polls`, on an mbarrier that expects one
+// arrival that never comes: the bounded-wait path of every tensor-core kernel
+// (give up, record kTcWaitTimeout in the error word, return) without a real
+// pipeline behind it.
+__global__ void wait_timeout_kernel(int* err, uint32_t polls) {
+    __shared__ uint64_t bar;
+    tc::mbar_init(&bar, 1);
+    tc::fence_barrier_init();
+    tc::mbar_wait(&bar, 0, err, polls);
+}
+}  // namespace
+}  // namespace f2s
+
+extern "C" int f2s_selftest_wait_timeout(int polls, void* stream) {
+    F2S_REQUIRE(polls >= 1 && polls <= (1 << 20), "selftest: polls %d outside [1, 2^20]", polls);
+    int* word = f2s::tc_error_word();
+    if (!word) return f2s::fail(F2S_ERR_CUDA, "device error word unavailable");
+    f2s::wait_timeout_kernel<<<1, 1, 0, f2s::as_stream(stream)>>>(word, (uint32_t)polls);
+    return f2s::check_launch("wait_timeout_kernel");
+}
+
 extern "C" int f2s_device_error(int* value, int reset, void* stream) {
     F2S_REQUIRE(value != nullptr, "device_error: null pointer");
     int* word = f2s::tc_error_word();

@@ -42,6 +42,7 @@ SIGNATURES: dict[str, list] = {
     "f2s_model_param_segments": [_p, _p, _p, _i, _p],
     "f2s_model_workspace_bytes": [_p, _i, _i, _p],
     "f2s_model_forward": [_p, _p, _p, _p, _i, _i, _p, _p, _sz, _p],
+    "f2s_trunk_forward": [_p, _p, _p, _p, _i, _i, _p, _sz, _p],
     "f2s_fps_workspace_bytes": [_i64, _p],
     "f2s_fps": [_p, _i64, _i64, _i64, _p, _p, _sz, _p],
     "f2s_patch_index": [_p, _i64, _p, _i, _i, _d, _p, _p, _p, _p],
@@ -57,6 +58,7 @@ SIGNATURES: dict[str, list] = {
     "f2s_chamfer_static": [_p, _p, _i, _i, _i, _p, _p],
     "f2s_linear": [_p, _i, _p, _p, _p, _i, _i, _i, _i, _i, _p],
     "f2s_device_error": [_p, _i, _p],
+    "f2s_selftest_wait_timeout": [_i, _p],
 }
 
 _RESTYPES = {"f2s_last_error": ctypes.c_char_p, "f2s_trace_tag_name": ctypes.c_char_p}

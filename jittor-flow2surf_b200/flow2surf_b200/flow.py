@@ -1,21 +1,6 @@
-"""Conditional-flow mathematics (flow2surf/flow.py:1-52), host-side NumPy."""
+"""Integration schedule of the reverse flow (flow2surf/flow.py:24-52), host-side NumPy."""
 
 import numpy as np
-
-
-def flow_state(clean, noisy, alpha):
-    """Interpolate from clean alpha=0 to noisy alpha=1 (flow.py:6-11)."""
-    return clean + alpha * (noisy - clean)
-
-
-def flow_velocity(clean, noisy):
-    """dX_alpha/dalpha for the linear clean-to-noisy path (flow.py:14-16)."""
-    return noisy - clean
-
-
-def reconstruct_clean(x_alpha, velocity, alpha):
-    """x_alpha - alpha * velocity, the implied clean endpoint (flow.py:19-21)."""
-    return x_alpha - alpha * velocity
 
 
 def alpha_schedule(num_steps, clean_power, noisy_power):

@@ -225,7 +225,8 @@ class Flow2SurfNet:
 
     def save(self, path) -> None:
         """Write the parameters as the reference's Module.save does: a pickled
-        {state-dict name: float32 array} dict (flow2surf/training/checkpoint.py:72-74)."""
+        {state-dict name: float32 array} dict (flow2surf/training/optimization.py:41-42,
+        flow2surf/training/checkpoint.py:151-153)."""
         with open(path, "wb") as f:
             pickle.dump({k: np.ascontiguousarray(v) for k, v in self._params.items()}, f,
                         protocol=pickle.HIGHEST_PROTOCOL)
@@ -281,6 +282,27 @@ class Flow2SurfNet:
                   _lib.ptr(x_alpha), _lib.ptr(alpha), batch, points, _lib.ptr(out),
                   _lib.ptr(ws), ws.numel(), _lib.stream_handle())
         return out
+
+    def trunk_(self, x: torch.Tensor, alpha: torch.Tensor,
+               workspace: torch.Tensor | None = None) -> torch.Tensor:
+        """The AdaLN-Zero blocks alone (transformer.py:75-89, with the
+        AlphaEmbed conditioning of network.py:75-80), in place on a
+        point-major residual stream x (B, M, feat_dim) float32 CUDA tensor
+        (the reference's (B, C, M) transposed); alpha (B,)."""
+        if x.dim() != 3 or x.shape[2] != self.cfg["feat_dim"]:
+            raise ValueError(f"x must be (B, M, {self.cfg['feat_dim']}), got {tuple(x.shape)}")
+        if alpha.dim() != 1 or alpha.shape[0] != x.shape[0]:
+            raise ValueError(f"alpha must be (B,), got {tuple(alpha.shape)}")
+        if not x.is_cuda or not alpha.is_cuda or x.dtype != torch.float32 or \
+                not x.is_contiguous():
+            raise ValueError("trunk_ takes contiguous float32 CUDA tensors (no CPU path)")
+        alpha = alpha.to(torch.float32).contiguous()
+        batch, points, _ = x.shape
+        ws = workspace if workspace is not None else self._workspace_for(batch, points, x.device)
+        blob = self.device_blob(x.device)
+        _lib.call("f2s_trunk_forward", ctypes.byref(self._config), _lib.ptr(blob), _lib.ptr(x),
+                  _lib.ptr(alpha), batch, points, _lib.ptr(ws), ws.numel(), _lib.stream_handle())
+        return x
 
     def __call__(self, x_alpha: torch.Tensor, alpha: torch.Tensor) -> torch.Tensor:
         if x_alpha.dim() != 3 or x_alpha.shape[1] != 3:

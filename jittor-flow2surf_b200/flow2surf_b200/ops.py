@@ -33,7 +33,7 @@ def knn_indices(features: torch.Tensor, k: int) -> torch.Tensor:
     features : (B, C, N) float32
     output   : (B, N, k) int32
 
-    flow2surf/models/ops/knn.py:55-86: k < 1 raises; N <= 1 gives zeros; when
+    flow2surf/models/ops/knn.py:35-66: k < 1 raises; N <= 1 gives zeros; when
     k > N-1 the last real neighbour is repeated. Ties are broken by the lower
     index and distances are the reference kernel's fp32 expression bit for bit.
     """

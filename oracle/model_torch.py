@@ -82,16 +82,50 @@ class TorchOracleNet:
         msg = _cln(msg, 1e-6, p[f"{pre}.norm.weight"], p[f"{pre}.norm.bias"])
         return _leaky(msg).amax(dim=2)
 
+    def _condition(self, alpha):
+        """AlphaEmbed (network.py:10-26)."""
+        p = self.p
+        e = 2.0 * torch.from_numpy(np.asarray(alpha)).to(self.dtype)[:, None] - 1.0
+        cond = torch.nn.functional.silu(e @ p["alpha_emb.mlp.0.weight"].T +
+                                        p["alpha_emb.mlp.0.bias"])
+        return cond @ p["alpha_emb.mlp.2.weight"].T + p["alpha_emb.mlp.2.bias"]
+
+    def _trunk(self, x, cond):
+        """AdaLN-Zero blocks (transformer.py:75-89) on point-major x (B, M, C)."""
+        p = self.p
+        C = x.shape[-1]
+        qk = C // 4
+        for i in range(self.num_blocks):
+            pre = f"blocks.{i}"
+            mod = torch.nn.functional.silu(cond) @ p[f"{pre}.mod.1.weight"].T + \
+                p[f"{pre}.mod.1.bias"]
+            s1, b1, g1, s2, b2, g2 = [mod[:, None, j * C:(j + 1) * C] for j in range(6)]
+            h = _cln(x) * (1.0 + s1) + b1
+            qkv = h @ self._w(f"{pre}.qkv_conv.weight").T
+            q, k, v = _cln(qkv[..., :qk]), _cln(qkv[..., qk:2 * qk]), qkv[..., 2 * qk:]
+            col = torch.softmax(q @ k.transpose(1, 2), dim=1)
+            wts = col / (col.sum(dim=-1, keepdim=True) + 1e-9)
+            x = x + g1 * ((h - wts @ v) @ self._w(f"{pre}.proj.weight").T)
+            h = _cln(x) * (1.0 + s2) + b2
+            gate = h @ self._w(f"{pre}.ff_gate.weight").T + p[f"{pre}.ff_gate.bias"]
+            val = h @ self._w(f"{pre}.ff1.weight").T + p[f"{pre}.ff1.bias"]
+            x = x + g2 * ((torch.nn.functional.silu(gate) * val) @
+                          self._w(f"{pre}.ff2.weight").T + p[f"{pre}.ff2.bias"])
+        return x
+
+    def trunk(self, x: np.ndarray, alpha: np.ndarray) -> np.ndarray:
+        """The trunk alone on a point-major (B, M, C) residual stream."""
+        with torch.no_grad():
+            xt = torch.from_numpy(np.asarray(x, dtype=np.float32)).to(self.dtype)
+            return self._trunk(xt, self._condition(alpha)).to(torch.float32).numpy()
+
     def forward(self, x_alpha: np.ndarray, alpha: np.ndarray) -> np.ndarray:
         p = self.p
         with torch.no_grad():
             x32 = np.asarray(x_alpha, dtype=np.float32)
             idx = torch.from_numpy(native.knn(x32, self.k).astype(np.int64))
             xyz = torch.from_numpy(np.ascontiguousarray(x32.transpose(0, 2, 1))).to(self.dtype)
-            e = 2.0 * torch.from_numpy(np.asarray(alpha)).to(self.dtype)[:, None] - 1.0
-            cond = torch.nn.functional.silu(e @ p["alpha_emb.mlp.0.weight"].T +
-                                            p["alpha_emb.mlp.0.bias"])
-            cond = cond @ p["alpha_emb.mlp.2.weight"].T + p["alpha_emb.mlp.2.bias"]
+            cond = self._condition(alpha)
             f = self._hpe("local_encoder.input_embed", xyz)
             outs = []
             for s in range(len(self.stage_dims)):
@@ -100,24 +134,7 @@ class TorchOracleNet:
             x = torch.cat(outs, -1) @ self._w("local_encoder.proj.0.weight").T
             x = _leaky(_cln(x, 1e-6, p["local_encoder.proj.1.weight"],
                             p["local_encoder.proj.1.bias"]))
-            C = x.shape[-1]
-            qk = C // 4
-            for i in range(self.num_blocks):
-                pre = f"blocks.{i}"
-                mod = torch.nn.functional.silu(cond) @ p[f"{pre}.mod.1.weight"].T + \
-                    p[f"{pre}.mod.1.bias"]
-                s1, b1, g1, s2, b2, g2 = [mod[:, None, j * C:(j + 1) * C] for j in range(6)]
-                h = _cln(x) * (1.0 + s1) + b1
-                qkv = h @ self._w(f"{pre}.qkv_conv.weight").T
-                q, k, v = _cln(qkv[..., :qk]), _cln(qkv[..., qk:2 * qk]), qkv[..., 2 * qk:]
-                col = torch.softmax(q @ k.transpose(1, 2), dim=1)
-                wts = col / (col.sum(dim=-1, keepdim=True) + 1e-9)
-                x = x + g1 * ((h - wts @ v) @ self._w(f"{pre}.proj.weight").T)
-                h = _cln(x) * (1.0 + s2) + b2
-                gate = h @ self._w(f"{pre}.ff_gate.weight").T + p[f"{pre}.ff_gate.bias"]
-                val = h @ self._w(f"{pre}.ff1.weight").T + p[f"{pre}.ff1.bias"]
-                x = x + g2 * ((torch.nn.functional.silu(gate) * val) @
-                              self._w(f"{pre}.ff2.weight").T + p[f"{pre}.ff2.bias"])
+            x = self._trunk(x, cond)
             layer = 0
             for _ in self.decoder_dims:
                 x = x @ self._w(f"decoder.net.{layer}.weight").T

@@ -35,7 +35,7 @@ def _ptr(a: np.ndarray):
 
 
 def knn(features: np.ndarray, k: int) -> np.ndarray:
-    """knn_indices restated (flow2surf/models/ops/knn.py:55-86 + knn_global.cu).
+    """knn_indices restated (flow2surf/models/ops/knn.py:35-66 + knn_global.cu).
 
     features (B, C, N) float32 -> (B, N, k) int32.
     """

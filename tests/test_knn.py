@@ -1,5 +1,5 @@
 """knn_indices on the GPU against the bit-exact oracle
-(flow2surf/models/ops/knn.py:55-86, flow2surf/models/ops/cuda/knn_global.cu)."""
+(flow2surf/models/ops/knn.py:35-66, flow2surf/models/ops/cuda/knn_global.cu)."""
 
 import numpy as np
 import pytest

@@ -161,3 +161,28 @@ def test_fp16_ffn_range_is_reported(cuda):
     # the fp32 trunk keeps fp32 rows: no range limit there
     gpu_forward(DEFAULT_CONFIG, big, x, alpha, precision="fp32")
     _lib.check_device_error()
+
+
+@pytest.mark.gpu
+def test_bounded_wait_that_runs_out_is_reported(cuda):
+    """Every tensor-core kernel bounds its mbarrier waits; a wait that runs out
+    sets device error word 1 and returns instead of hanging. The self-test
+    entry waits on a barrier nothing arrives on (a few thousand polls, no copy
+    or MMA in flight); the word reads 1, is cleared, and the next forward runs
+    clean."""
+    import ctypes
+
+    from flow2surf_b200 import _lib
+
+    _lib.check_device_error()  # start from a clear word
+    _lib.call("f2s_selftest_wait_timeout", 4096, _lib.stream_handle())
+    value = ctypes.c_int(0)
+    _lib.call("f2s_device_error", ctypes.byref(value), 1, _lib.stream_handle())
+    assert value.value == 1
+    params = random_parameters(DEFAULT_CONFIG, seed=0)
+    cloud = sphere_cloud(4000, seed=3)[0]
+    x = patches_from_cloud(cloud, 2, 1000, seed=1)
+    alpha = np.array([0.5, 0.9], dtype=np.float32)
+    v = gpu_forward(DEFAULT_CONFIG, params, x, alpha, precision="tf32", encoder_precision="bf16x3")
+    _lib.check_device_error()
+    assert np.isfinite(v).all()

@@ -170,3 +170,29 @@ def test_torch_cpu_oracle_matches_numpy_oracle(golden):
     # the torch restatement returns float32 velocities
     np.testing.assert_allclose(got, want, rtol=1e-7, atol=1e-9)
     np.testing.assert_allclose(got, fix["velocity_f64"], rtol=0, atol=1e-5)
+
+
+def test_torch_float32_oracle_tracks_float64_oracle_on_default_model():
+    """The float32 torch-CPU restatement is the checker of the large GPU
+    parity tests (whole 50k-point denoise steps, the 64-patch trunk): on the
+    default architecture it stays within 1e-6 of the float64 NumPy oracle,
+    two orders below the 1e-4 velocity tolerance."""
+    import torch
+
+    from flow2surf_b200.synthetic import DEFAULT_CONFIG, random_parameters
+    from oracle.model_torch import TorchOracleNet
+
+    params = random_parameters(DEFAULT_CONFIG, seed=0)
+    rng = np.random.default_rng(11)
+    x = (0.1 * rng.normal(size=(2, 3, 300))).astype(np.float32)
+    alpha = np.array([0.5, 0.997947], dtype=np.float32)
+    ref = OracleNet(DEFAULT_CONFIG, params)
+    want, inter = ref(x, alpha, return_intermediates=True)
+    got = TorchOracleNet(DEFAULT_CONFIG, params)(x, alpha)
+    assert np.abs(got - want).max() < 1e-6
+    assert np.abs(want).max() > 1e-2
+    # the trunk alone, on the encoded stream
+    trunk = TorchOracleNet(DEFAULT_CONFIG, params, dtype=torch.float32).trunk(
+        inter["encoded"].astype(np.float32), alpha)
+    want_t = inter[f"block{DEFAULT_CONFIG['num_blocks'] - 1}"]
+    assert np.abs(trunk - want_t).max() < 1e-5 * max(1.0, np.abs(want_t).max())

@@ -3,7 +3,9 @@
 Some callers cannot call cudaMalloc (an out-of-memory handler, a host that
 forbids device allocation once running, work that must not synchronise the
 device), so this variant keeps its scratch in a built-in device array instead
-of a caller workspace. It must give what f2s_chamfer gives. This file sorts
+of a caller workspace. It must give what f2s_chamfer gives, bit for bit (the
+same kernels run on the same inputs), and once a device has been set up by a
+first call it must not change the device memory in use. This file sorts
 last so that, if it fails, a run that stops at the first failure has already
 run every other test.
 """
@@ -17,7 +19,6 @@ import torch
 from flow2surf_b200 import _lib
 from flow2surf_b200.synthetic import mesh_cloud
 
-CHAMFER_ATOL = 1e-5
 STATIC_MAX_POINTS = 1 << 21
 
 
@@ -41,9 +42,17 @@ def without_allocation(pred, target, out):
     return out.cpu().numpy()
 
 
+def set_up_device(out):
+    """The B = 0 call: only the per-device set-up (module load, scratch address)."""
+    one = torch.zeros((1, 1, 3), device="cuda")
+    _lib.call("f2s_chamfer_static", one.data_ptr(), one.data_ptr(), 0, 1, 1, out.data_ptr(),
+              _lib.stream_handle())
+
+
 @pytest.mark.gpu
 def test_chamfer_static_matches_workspace_entry_twice(cuda):
     out = torch.empty(4, dtype=torch.float64, device="cuda")
+    set_up_device(out)
     rng = np.random.default_rng(0)
     # first call: four 30k/25k pairs; second call: two larger, differently
     # shaped pairs, so stale keys of the first call would show up if not reset
@@ -56,8 +65,30 @@ def test_chamfer_static_matches_workspace_entry_twice(cuda):
     for pred, target in ((first_pred, first_target), (second_pred, second_target)):
         got = without_allocation(pred, target, out[:pred.shape[0]])
         want = with_workspace(pred, target)
-        np.testing.assert_allclose(got, want, rtol=0, atol=CHAMFER_ATOL)
+        np.testing.assert_array_equal(got, want)
         assert np.all(want > 0)
+
+
+@pytest.mark.gpu
+def test_chamfer_static_allocates_nothing_after_set_up(cuda):
+    rng = np.random.default_rng(1)
+    pred = torch.from_numpy(rng.normal(size=(2, 20_000, 3)).astype(np.float32)).cuda()
+    target = torch.from_numpy(rng.normal(size=(2, 15_000, 3)).astype(np.float32)).cuda()
+    out = torch.empty(2, dtype=torch.float64, device="cuda")
+    set_up_device(out)
+    B, M, N = 2, 20_000, 15_000
+    call = lambda: _lib.call("f2s_chamfer_static", pred.data_ptr(), target.data_ptr(), B, M, N,
+                             out.data_ptr(), _lib.stream_handle())
+    call()
+    torch.cuda.synchronize()
+    free_before, _ = torch.cuda.mem_get_info()
+    allocated_before = torch.cuda.memory_allocated()
+    call()
+    torch.cuda.synchronize()
+    free_after, _ = torch.cuda.mem_get_info()
+    assert torch.cuda.memory_allocated() == allocated_before
+    assert free_after == free_before
+    np.testing.assert_array_equal(out.cpu().numpy(), with_workspace(pred, target))
 
 
 @pytest.mark.gpu
