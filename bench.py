@@ -239,7 +239,11 @@ def run_reference(args, rank: int, world: int) -> None:
 # ---------------------------------------------------------------------------
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    """nvidia-smi clocks and throttle reasons sampled during the timed region.
+
+    nvidia-smi's start-up (NVML initialisation) is heavy; `__enter__` returns
+    only once the first sample has arrived, so that start-up does not overlap
+    the timed steps."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -248,8 +252,16 @@ class ClockSampler:
     def __init__(self, gpu_id: str):
         self.gpu_id = gpu_id
         self.proc = None
+        self.lines: list[str] = []
+        self.text = ""
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line)
 
     def __enter__(self):
+        import threading
+
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", self.gpu_id, f"--query-gpu={self.FIELDS}",
@@ -257,21 +269,29 @@ class ClockSampler:
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
+            return self
+        self.reader = threading.Thread(target=self._read, daemon=True)
+        self.reader.start()
+        deadline = time.time() + 15.0
+        while not self.lines and time.time() < deadline and self.proc.poll() is None:
+            time.sleep(0.02)
         return self
 
     def __exit__(self, *exc):
-        self.text = ""
         if self.proc is not None:
+            time.sleep(0.25)  # one more sample after the last timed step
             self.proc.terminate()
             try:
-                self.text, _ = self.proc.communicate(timeout=10)
+                self.proc.wait(timeout=10)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
-                self.text, _ = self.proc.communicate()
+                self.proc.wait()
+            self.reader.join(timeout=5)
+        self.text = "".join(self.lines)
 
     def summary(self) -> dict:
         rows = []
-        for line in (getattr(self, "text", "") or "").splitlines():
+        for line in self.text.splitlines():
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 9:
                 continue

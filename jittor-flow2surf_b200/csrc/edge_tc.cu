@@ -145,6 +145,15 @@ __device__ __forceinline__ uint32_t interleaved_offset(int row, int chunk) {
     return (uint32_t)((row >> 3) * 256 + chunk * 128 + (row & 7) * 16);
 }
 
+// Packed fp32x2 arithmetic of sm_100 (one instruction, two lanes of fp32,
+// each rounded as the scalar operation is): the per-edge CUDA-core work of
+// this kernel is issue-bound, so pairs of channels go through one issue slot.
+__device__ __forceinline__ float2 f2(float v) { return make_float2(v, v); }
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+__device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
+
+
 // GELU(x) = x * Phi(x) with Phi from the erf approximation of Abramowitz and
 // Stegun, Handbook of Mathematical Functions, eq. 7.1.26 (after Hastings):
 //   erf(z) = 1 - t (a1 + t (a2 + t (a3 + t (a4 + t a5)))) exp(-z^2),
@@ -155,15 +164,20 @@ __device__ __forceinline__ uint32_t interleaved_offset(int row, int chunk) {
 // and log2(e) / 2 (exp(-x^2 / 2) = 2^(-x^2 log2(e) / 2)). Within 3.5e-7 of
 // the exact GELU in float32, far below the operand rounding of the
 // tensor-core contraction the hidden rows feed (2^-18 relative at best).
-__device__ __forceinline__ float gelu_as(float x) {
-    const float ax = fabsf(x);
-    const float t = f2s_rcp_approx(fmaf(0.23164189f, ax, 1.0f));  // p / sqrt(2)
-    float q = fmaf(t, 0.5307027145f, -0.7265760135f);
-    q = fmaf(t, q, 0.7107068705f);
-    q = fmaf(t, q, -0.142248368f);
-    q = fmaf(t, q, 0.127414796f);
-    const float e = f2s_ex2_approx(x * (x * -0.72134752f));
-    return fmaf(-ax, q * t * e, fmaxf(x, 0.0f));
+// Applied to two values at once; the polynomial's coefficients are negated
+// so that the final step is max(x, 0) + |x| (-q t e).
+__device__ __forceinline__ float2 gelu_as2(float2 x) {
+    const float2 ax = make_float2(fabsf(x.x), fabsf(x.y));
+    const float2 den = fma2(f2(0.23164189f), ax, f2(1.0f));
+    const float2 t = make_float2(f2s_rcp_approx(den.x), f2s_rcp_approx(den.y));
+    float2 q = fma2(t, f2(-0.5307027145f), f2(0.7265760135f));
+    q = fma2(t, q, f2(-0.7107068705f));
+    q = fma2(t, q, f2(0.142248368f));
+    q = fma2(t, q, f2(-0.127414796f));
+    const float2 s = mul2(x, mul2(x, f2(-0.72134752f)));
+    const float2 e = make_float2(f2s_ex2_approx(s.x), f2s_ex2_approx(s.y));
+    const float2 nqte = mul2(mul2(q, t), e);
+    return fma2(ax, nqte, make_float2(fmaxf(x.x, 0.0f), fmaxf(x.y, 0.0f)));
 }
 
 // Operand modes of the edge contraction.
@@ -460,23 +474,28 @@ edge_tc_kernel(const __grid_constant__ CUtensorMap map_w, const EdgeTcArgs a) {
                 tc::tmem_ld32(tmem_base + t_lane + pre_col + (uint32_t)(ch0 + c0), v);
 #pragma unroll
                 for (int i0 = 0; i0 < 32; i0 += kPer) {
-                    float o[kPer];
+                    float2 o[kPer / 2];
 #pragma unroll
-                    for (int e = 0; e < kPer; ++e) o[e] = gelu_as(v[i0 + e]);
+                    for (int e = 0; e < kPer / 2; ++e)
+                        o[e] = gelu_as2(make_float2(v[i0 + 2 * e], v[i0 + 2 * e + 1]));
                     const int c = ch0 + c0 + i0;
                     unsigned char* dst =
                         dA + (size_t)(c / kBk) * kRows * 128 + sw128_offset(row, (c % kBk) / kPer);
                     if constexpr (kTf32) {
-                        *reinterpret_cast<float4*>(dst) = make_float4(o[0], o[1], o[2], o[3]);
+                        *reinterpret_cast<float4*>(dst) = make_float4(o[0].x, o[0].y, o[1].x, o[1].y);
                     } else {
                         uint32_t hi[4], lo[4];
 #pragma unroll
                         for (int e = 0; e < 4; ++e) {
-                            const __nv_bfloat162 h2 = __floats2bfloat162_rn(o[2 * e], o[2 * e + 1]);
+                            const __nv_bfloat162 h2 = __floats2bfloat162_rn(o[e].x, o[e].y);
                             hi[e] = *reinterpret_cast<const uint32_t*>(&h2);
-                            if (kSplit)
-                                lo[e] = pack_bf16(o[2 * e] - __bfloat162float(h2.x),
-                                                  o[2 * e + 1] - __bfloat162float(h2.y));
+                            if (kSplit) {
+                                // o - hi exactly (Sterbenz), then rounded to bf16
+                                const float2 hf = make_float2(__uint_as_float(hi[e] << 16),
+                                                              __uint_as_float(hi[e] & 0xffff0000u));
+                                const float2 r = fma2(hf, f2(-1.0f), o[e]);
+                                lo[e] = pack_bf16(r.x, r.y);
+                            }
                         }
                         *reinterpret_cast<uint4*>(dst) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
                         if (kSplit)
@@ -641,27 +660,33 @@ edge_tc_kernel(const __grid_constant__ CUtensorMap map_w, const EdgeTcArgs a) {
                 const uint32_t rj = buf + (uint32_t)(lane * 128);
                 const uint32_t ri = buf + (uint32_t)(4096 + ptw * 128);
                 tc::tmem_ld32_wait(r);
-                float v[32];
-                float csum = 0.0f;
+                float2 v2[16];
+                float2 csum = f2(0.0f);
 #pragma unroll
                 for (int i = 0; i < 32; i += 4) {
                     const float4 nj = lds128(rj + (uint32_t)(((i >> 2) ^ (lane & 7)) << 4));
                     const float4 ni = lds128(ri + (uint32_t)(((i >> 2) ^ (ptw & 7)) << 4));
                     const float4 bb = *reinterpret_cast<const float4*>(sCb + cb + i);
-                    v[i + 0] = nj.x + ni.x + (__uint_as_float(r[i + 0]) + bb.x);
-                    v[i + 1] = nj.y + ni.y + (__uint_as_float(r[i + 1]) + bb.y);
-                    v[i + 2] = nj.z + ni.z + (__uint_as_float(r[i + 2]) + bb.z);
-                    v[i + 3] = nj.w + ni.w + (__uint_as_float(r[i + 3]) + bb.w);
-                    if (k == 0) csum += (v[i] + v[i + 1]) + (v[i + 2] + v[i + 3]);
+                    const float2 a0 = make_float2(__uint_as_float(r[i + 0]), __uint_as_float(r[i + 1]));
+                    const float2 a1 = make_float2(__uint_as_float(r[i + 2]), __uint_as_float(r[i + 3]));
+                    v2[i / 2] = add2(add2(make_float2(nj.x, nj.y), make_float2(ni.x, ni.y)),
+                                     add2(a0, make_float2(bb.x, bb.y)));
+                    v2[i / 2 + 1] = add2(add2(make_float2(nj.z, nj.w), make_float2(ni.z, ni.w)),
+                                         add2(a1, make_float2(bb.z, bb.w)));
+                    if (k == 0) csum = add2(csum, add2(v2[i / 2], v2[i / 2 + 1]));
                 }
-                tc::tmem_st32_async(taddr + (uint32_t)cb, v);
-                if (k == 0) shift = csum * (1.0f / 32.0f);
+                tc::tmem_st32_async(taddr + (uint32_t)cb, *reinterpret_cast<const float(*)[32]>(v2));
+                if (k == 0) shift = (csum.x + csum.y) * (1.0f / 32.0f);
+                const float2 nshift = f2(-shift);
+                float2 s1p = f2(0.0f), s2p = f2(0.0f);
 #pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const float d = v[i] - shift;
-                    s1 += d;
-                    s2 = fmaf(d, d, s2);
+                for (int i = 0; i < 16; ++i) {
+                    const float2 d = add2(v2[i], nshift);
+                    s1p = add2(s1p, d);
+                    s2p = fma2(d, d, s2p);
                 }
+                s1 += s1p.x + s1p.y;
+                s2 += s2p.x + s2p.y;
                 __syncwarp();  // the buffer has been read: refill it
                 const int kn = k + nbuf;
                 if (kn < nmine) issue(tile, false, kn, cons);
@@ -698,13 +723,18 @@ edge_tc_kernel(const __grid_constant__ CUtensorMap map_w, const EdgeTcArgs a) {
                 float y[32];
                 tc::tmem_ld32(taddr + (uint32_t)cb, y);
                 if (ej >= 0) {
+                    const float2 rstd2 = f2(rstd), nmr2 = f2(nmr);
 #pragma unroll
                     for (int i = 0; i < 32; i += 4) {
                         const float4 sg = *reinterpret_cast<const float4*>(sSgn + cb + i);
-                        y[i + 0] = fmaf(y[i + 0], rstd, nmr) * sg.x;
-                        y[i + 1] = fmaf(y[i + 1], rstd, nmr) * sg.y;
-                        y[i + 2] = fmaf(y[i + 2], rstd, nmr) * sg.z;
-                        y[i + 3] = fmaf(y[i + 3], rstd, nmr) * sg.w;
+                        const float2 y0 = mul2(fma2(make_float2(y[i], y[i + 1]), rstd2, nmr2),
+                                               make_float2(sg.x, sg.y));
+                        const float2 y1 = mul2(fma2(make_float2(y[i + 2], y[i + 3]), rstd2, nmr2),
+                                               make_float2(sg.z, sg.w));
+                        y[i + 0] = y0.x;
+                        y[i + 1] = y0.y;
+                        y[i + 2] = y1.x;
+                        y[i + 3] = y1.y;
                     }
                 } else {
 #pragma unroll
