@@ -144,5 +144,9 @@ int edge_stage_f32(const EdgeArgs& args, cudaStream_t stream);
 // (args.contrib_w is fp32 in every case). F2S_ERR_UNSUPPORTED for shapes it
 // does not cover.
 int edge_stage_tc(const EdgeArgs& args, int precision, cudaStream_t stream);
+// The split-bf16 stage on the kernel whose warps each take both the hidden-row
+// and the epilogue work (edge_tcu.cu); F2S_ERR_UNSUPPORTED for shapes it does
+// not cover.
+int edge_stage_unified(const EdgeArgs& args, cudaStream_t stream);
 
 }  // namespace f2s

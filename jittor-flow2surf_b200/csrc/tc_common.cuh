@@ -75,6 +75,21 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
     return false;
 }
 
+// Bounded wait without the sleeps: each poll is a try_wait that parks the
+// thread until the phase completes or the suspend hint runs out, so a waiter
+// wakes as soon as the phase completes. For waits on the steady-state path
+// of a pipeline whose stages hand over every few microseconds; the bound
+// (kSpinLimit polls, at least ~0.15 s) and the error word behave as in
+// mbar_wait.
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, int* err) {
+    for (uint32_t i = 0; i < kSpinLimit; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 63u) == 63u && *reinterpret_cast<volatile int*>(err) != kTcOk) return false;
+    }
+    atomicExch(err, kTcWaitTimeout);
+    return false;
+}
+
 // Bounded wait that ignores the error word: used on the way out for copies
 // and MMAs already in flight, which must complete before the CTA releases its
 // shared or tensor memory. False when the phase did not complete in time.
@@ -274,6 +289,66 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) 
         "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
         : "memory");
     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// N consecutive 32-bit columns of this thread's TMEM lane (N = 2, 8, 16),
+// loaded and waited for.
+template <int N>
+__device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&r)[N]) {
+    static_assert(N == 2 || N == 8 || N == 16, "tmem_ld: 2, 8 or 16 columns");
+    if constexpr (N == 2) {
+        asm volatile("tcgen05.ld.sync.aligned.32x32b.x2.b32 {%0,%1}, [%2];"
+                     : "=r"(r[0]), "=r"(r[1])
+                     : "r"(taddr));
+        asm volatile("tcgen05.wait::ld.sync.aligned;" : "+r"(r[0]), "+r"(r[1])::"memory");
+    } else if constexpr (N == 8) {
+        asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                     : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                       "=r"(r[6]), "=r"(r[7])
+                     : "r"(taddr));
+        asm volatile("tcgen05.wait::ld.sync.aligned;"
+                     : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
+                       "+r"(r[6]), "+r"(r[7])::"memory");
+    } else {
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+            "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+            : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+              "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+              "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+            : "r"(taddr));
+        asm volatile("tcgen05.wait::ld.sync.aligned;"
+                     : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
+                       "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]),
+                       "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])::"memory");
+    }
+}
+
+// N consecutive 32-bit columns of this thread's TMEM lane (N = 2, 8, 16),
+// stored without waiting: tmem_st_wait() before the columns are read back or
+// signalled as written.
+template <int N>
+__device__ __forceinline__ void tmem_st_async(uint32_t taddr, const uint32_t (&v)[N]) {
+    static_assert(N == 2 || N == 8 || N == 16, "tmem_st_async: 2, 8 or 16 columns");
+    if constexpr (N == 2) {
+        asm volatile("tcgen05.st.sync.aligned.32x32b.x2.b32 [%0], {%1,%2};" ::"r"(taddr),
+                     "r"(v[0]), "r"(v[1])
+                     : "memory");
+    } else if constexpr (N == 8) {
+        asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(
+                         taddr),
+                     "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]),
+                     "r"(v[7])
+                     : "memory");
+    } else {
+        asm volatile(
+            "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+            "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+            "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+            "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
+            "r"(v[15])
+            : "memory");
+    }
 }
 
 // Shared-memory matrix descriptor of a K-major tile stored in the canonical

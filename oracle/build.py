@@ -2,9 +2,8 @@
 
 Compiles oracle/oracle.c into oracle/_build/liboracle.so with gcc, OpenMP and
 -ffp-contract=off (the restatement spells out every fused multiply-add).
-The reference's own CUDA sources are jt.code templates (macro-expanded by
-Jittor at run time), so they do not compile standalone and there is no
-oracle/_ref build.
+The reference's own KNN kernel is built from its jt.code template by
+oracle/build_ref.py (into oracle/_ref/).
 """
 
 from __future__ import annotations

@@ -1,6 +1,9 @@
 """knn_indices on the GPU against the bit-exact oracle
 (flow2surf/models/ops/knn.py:35-66, flow2surf/models/ops/cuda/knn_global.cu)."""
 
+import ctypes
+from pathlib import Path
+
 import numpy as np
 import pytest
 import torch
@@ -64,3 +67,43 @@ def test_knn_limits_raise(cuda):
         knn_indices(torch.zeros((1, 3, 16), device="cuda"), 33)
     with pytest.raises(ValueError):
         knn_indices(torch.zeros((1, 3, 4096), device="cuda"), 8)
+
+
+REF_KNN = Path(__file__).resolve().parent.parent / "oracle" / "_ref" / "libref_knn.so"
+
+
+def reference_kernel_knn(features: np.ndarray, k: int) -> np.ndarray:
+    """The reference's own global_knn (knn_global.cu, built from its sources by
+    oracle/build_ref.py) on the same input."""
+    lib = ctypes.CDLL(str(REF_KNN))
+    lib.ref_global_knn.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                   ctypes.c_void_p, ctypes.c_int]
+    B, C, N = features.shape
+    x = torch.from_numpy(np.ascontiguousarray(features)).cuda()
+    out = torch.empty((B, N, k), dtype=torch.int32, device="cuda")
+    torch.cuda.synchronize()
+    assert lib.ref_global_knn(x.data_ptr(), B, C, N, out.data_ptr(), k) == 0
+    torch.cuda.synchronize()
+    return out.cpu().numpy()
+
+
+@pytest.mark.skipif(not REF_KNN.exists(), reason="reference KNN kernel not built (no reference checkout)")
+@pytest.mark.parametrize("k", [16, 32])
+def test_knn_matches_reference_kernel_microbench(cuda, k):
+    """Bit-exact against the reference's own kernel on the KNN micro-benchmark
+    input (256 patches x 1024 points: uniform cube and noisy ellipsoid
+    surfaces), and the oracle with it."""
+    xyz, _ = knn_patches(256, 1024, 64, seed=2)
+    want = reference_kernel_knn(xyz, k)
+    np.testing.assert_array_equal(run(xyz, k), want)
+    np.testing.assert_array_equal(native.knn(xyz, k), want)
+
+
+@pytest.mark.skipif(not REF_KNN.exists(), reason="reference KNN kernel not built (no reference checkout)")
+@pytest.mark.parametrize("b,c,n,k", [(3, 3, 1000, 16), (2, 3, 33, 32), (4, 5, 257, 8),
+                                     (2, 3, 2, 1), (1, 24, 600, 20)])
+def test_knn_matches_reference_kernel_shapes(cuda, b, c, n, k):
+    rng = np.random.default_rng(b * 1000 + n)
+    xyz = rng.normal(size=(b, c, n)).astype(np.float32)
+    xyz[:, :, 1] = xyz[:, :, 0]           # a duplicate point: a zero distance
+    np.testing.assert_array_equal(run(xyz, k), reference_kernel_knn(xyz, k))

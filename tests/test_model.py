@@ -83,6 +83,24 @@ def test_tensor_core_model_matches_oracle(cuda, k, precision, encoder_precision,
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("k,patches,points", [(8, 3, 1000), (32, 3, 999), (16, 5, 777)])
+def test_split_encoder_shapes(cuda, k, patches, points):
+    """The split-bf16 neighbour stage at K = 8 and on ragged batches (the
+    last tile of 128 edge rows only partly filled), trunk fp32 so the encoder
+    dominates the error."""
+    cfg = dict(DEFAULT_CONFIG, k_neighbors=k)
+    params = random_parameters(cfg, seed=2)
+    cloud = sphere_cloud(20000, seed=5)[0]
+    x = patches_from_cloud(cloud, patches, points, seed=k)
+    alpha = np.linspace(0.3, 1.0, patches).astype(np.float32)
+    v = gpu_forward(cfg, params, x, alpha, "fp32", "bf16x3")
+    ref = OracleNet(cfg, params)(x, alpha)
+    err = np.abs(v - ref).max()
+    assert err < VELOCITY_ATOL, f"max abs velocity error {err}"
+    assert np.abs(ref).max() > 1e-2
+
+
+@pytest.mark.gpu
 def test_default_model_reference_golden(cuda, golden):
     fix = golden("model_default")
     params = random_parameters(DEFAULT_CONFIG, seed=int(fix["params_seed"]))
