@@ -42,6 +42,11 @@ __device__ __forceinline__ float4 lds128(uint32_t addr) {
                  : "memory");
     return v;
 }
+__device__ __forceinline__ float lds32(uint32_t addr) {
+    float v;
+    asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+    return v;
+}
 __device__ __forceinline__ void sts128(uint32_t addr, float4 v) {
     asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x), "f"(v.y),
                  "f"(v.z), "f"(v.w)
@@ -242,6 +247,61 @@ __device__ __forceinline__ void write_u_row(unsigned char* sU, const float* sGra
             make_float4(hi[4 * ch], hi[4 * ch + 1], hi[4 * ch + 2], hi[4 * ch + 3]);
         *reinterpret_cast<float4*>(sU + kUBytes + off) =
             make_float4(lo[4 * ch], lo[4 * ch + 1], lo[4 * ch + 2], lo[4 * ch + 3]);
+    }
+}
+
+// write_u_row for the N rows row0 + stride m (m < N) at once: each moment of
+// sGram is read once and feeds N independent chains.
+template <int N>
+__device__ __forceinline__ void write_u_rows(unsigned char* sU, const float* sGram, int row0,
+                                             int stride, const float3 (&pi)[N],
+                                             const float3 (&pj)[N]) {
+    float g[N][6], var[N];
+#pragma unroll
+    for (int m = 0; m < N; ++m) {
+        g[m][0] = pj[m].x - pi[m].x;
+        g[m][1] = pj[m].y - pi[m].y;
+        g[m][2] = pj[m].z - pi[m].z;
+        g[m][3] = pi[m].x;
+        g[m][4] = pi[m].y;
+        g[m][5] = pi[m].z;
+        var[m] = sGram[42];
+    }
+#pragma unroll
+    for (int d = 0; d < 6; ++d) {
+        float t[N];
+        const float a2 = 2.0f * sGram[36 + d];
+#pragma unroll
+        for (int m = 0; m < N; ++m) t[m] = a2;
+#pragma unroll
+        for (int e = 0; e < 6; ++e) {
+            const float ge = sGram[d * 6 + e];
+#pragma unroll
+            for (int m = 0; m < N; ++m) t[m] = fmaf(ge, g[m][e], t[m]);
+        }
+#pragma unroll
+        for (int m = 0; m < N; ++m) var[m] = fmaf(t[m], g[m][d], var[m]);
+    }
+#pragma unroll
+    for (int m = 0; m < N; ++m) {
+        const float rstd = rsqrtf(fmaxf(var[m], 0.0f) + 1e-5f);
+        const float u8[8] = {rstd * g[m][0], rstd * g[m][1], rstd * g[m][2], rstd * g[m][3],
+                             rstd * g[m][4], rstd * g[m][5], rstd,           1.0f};
+        float hi[8], lo[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            hi[e] = f2s_round_tf32(u8[e]);
+            lo[e] = u8[e] - hi[e];
+        }
+        const int row = row0 + stride * m;
+#pragma unroll
+        for (int ch = 0; ch < 2; ++ch) {
+            const uint32_t off = interleaved_offset(row, ch);
+            *reinterpret_cast<float4*>(sU + off) =
+                make_float4(hi[4 * ch], hi[4 * ch + 1], hi[4 * ch + 2], hi[4 * ch + 3]);
+            *reinterpret_cast<float4*>(sU + kUBytes + off) =
+                make_float4(lo[4 * ch], lo[4 * ch + 1], lo[4 * ch + 2], lo[4 * ch + 3]);
+        }
     }
 }
 

@@ -642,6 +642,10 @@ int edge_stage_tc(const EdgeArgs& e, int precision, cudaStream_t st) {
     F2S_REQUIRE(precision == F2S_PRECISION_TF32 || precision == F2S_PRECISION_BF16 ||
                     precision == F2S_PRECISION_BF16X3,
                 "edge_tc: precision %d", precision);
+    if (precision == F2S_PRECISION_BF16X3) {
+        const int status = edge_stage_unified(e, st);
+        if (status != F2S_ERR_UNSUPPORTED) return status;
+    }
     const int mode = precision == F2S_PRECISION_TF32   ? kModeTf32
                      : precision == F2S_PRECISION_BF16 ? kModeBf16
                                                        : kModeSplit;

@@ -1,5 +1,4 @@
-// Fused neighbour stage, split-bf16 precision, with every compute warp in both
-// roles.
+// Fused neighbour stage, split-bf16 precision, as three concurrent roles.
 //
 // Same arithmetic as edge_tc.cu (encoder.py:83-115, neighbor_reduce.py:244-337,
 // hpe.py:14-50, hpe_hidden_forward.cu, neighbor_reduce_forward.cu): per edge
@@ -8,34 +7,32 @@
 // content[j] + content[i] + W_po h + b_po, its LayerNorm, and the max over the
 // K edge rows of each point after the affine + LeakyReLU.
 //
-// Work of a tile of 128 edge rows, per CTA (persistent, one per SM):
-//   16 compute warps, four per TMEM lane quarter (edge rows 32q .. 32q + 31),
-//   each owning a quarter of the hidden channels and a quarter of the output
-//   channels. Per tile they
-//     1. turn the pre-activations of the NEXT tile into hidden rows in place
-//        in TMEM: each warp reads its H/4 fp32 columns, applies GELU and
-//        writes the bf16 high and low halves over the same columns (the MMA
-//        reads its A operand from tensor memory, so the hidden rows never
-//        touch shared memory), then arrives on "A ready";
-//     2. run the epilogue of THIS tile: the accumulator columns of the warp's
-//        output channels go to registers at once (the accumulator is then
-//        released to the next MMA), the neighbour and centre content rows
-//        come from shared memory (staged by the warp's own cp.async copies a
-//        whole tile ahead), the message moments of the four warps of a lane
-//        quarter are combined through TMEM and a named barrier, and the
-//        normalised messages are reduced over the K rows of each point.
-//   1 control warp: computes the u rows [rstd g, rstd, 1] of the tile after
-//   next from the geometry, issues the pre-activation MMAs (into the TMEM
-//   slot the MMA of the tile before has released) and the main MMAs (one
-//   lane; a tcgen05.mma holds its issuing thread until the tensor pipe takes
-//   it, so no compute warp waits on that).
-// So the tensor pipe runs the MMAs of tile t while the compute warps turn
-// tile t + 1's pre-activations into hidden rows and finish tile t - 1: per
-// tile the compute warps issue one GELU pass and one epilogue pass and wait
-// on nothing else in steady state.
+// Persistent CTA (one per SM) over tiles of 128 edge rows, 20 warps:
+//   warps 0-7   hidden rows: two warps per TMEM lane quarter, each half of the
+//               hidden channels. A warp turns the fp32 pre-activations of a
+//               tile into GELU'd bf16 high and low halves in place in TMEM
+//               (each 16-channel chunk: high halves in its first 8 columns,
+//               low halves in the next 8), the A operand the MMA reads from
+//               tensor memory; the hidden rows never touch shared memory.
+//   warps 8-15  epilogue: two warps per lane quarter, each half of the output
+//               channels. The accumulator goes through registers once (then
+//               the next MMA may use it), with the neighbour and centre
+//               content rows staged in shared memory by the warp's own
+//               cp.async copies a whole tile ahead; the messages are written
+//               back over the consumed staged rows, the two halves' moments
+//               meet through TMEM and a named barrier, and the normalised
+//               messages are reduced over the K rows of each point.
+//   warps 16-19 control: compute the u rows [rstd g, rstd, 1] two tiles ahead
+//               (one row per lane, geometry prefetched a further tile ahead);
+//               one lane issues the pre-activation MMAs into the TMEM slot the
+//               MMA before has released and the main MMAs (a tcgen05.mma holds
+//               its issuing thread until the tensor pipe takes it, so no other
+//               role waits on that).
+// The hidden-row warps (MUFU-heavy GELU), the epilogue warps (FMA, shared
+// memory) and the tensor pipe work on consecutive tiles at once.
 //
 // TMEM columns: n_acc accumulators of C_out columns, two pre-activation /
-// hidden-row slots of H columns, 16 columns of message moments.
+// hidden-row slots of H columns, 8 columns of message moments.
 #include <cfloat>
 #include <cstring>
 
@@ -48,9 +45,12 @@ namespace {
 
 using namespace edge;
 
-constexpr int kComputeWarps = 16;
-constexpr int kControlWarp = kComputeWarps;
-constexpr int kThreads = (kComputeWarps + 1) * 32;
+constexpr int kHiddenWarps = 8;
+constexpr int kEpilogueWarps = 8;
+constexpr int kEpiWarp0 = kHiddenWarps;
+constexpr int kControlWarp0 = kHiddenWarps + kEpilogueWarps;
+constexpr int kControlWarps = 4;
+constexpr int kThreads = (kControlWarp0 + kControlWarps) * 32;
 constexpr unsigned kFull = 0xffffffffu;
 
 struct UArgs {
@@ -80,13 +80,13 @@ struct UArgs {
 // Shared-memory layout (byte offsets from the 1024-byte aligned base).
 struct Layout {
     uint32_t b_hi, b_lo, u, wu, gram, cb, ln, sgn, bars, fails, stage;
-    uint32_t stage_bytes;  // per compute warp: 32 neighbour rows + the centre rows of its points
+    uint32_t stage_bytes;  // per epilogue warp: 32 neighbour rows + the centre rows of its points
     uint32_t total;
 };
 
 __host__ __device__ inline Layout layout(int H, int cout, int K) {
     Layout L{};
-    const uint32_t cw = (uint32_t)cout / 4;  // output channels of one compute warp
+    const uint32_t cw = (uint32_t)cout / 2;  // output channels of one epilogue warp
     const uint32_t ppw = 32u / (uint32_t)K;  // points whose rows one warp holds
     const uint32_t b_bytes = (uint32_t)cout * (uint32_t)H * 2u;
     L.b_hi = 0;
@@ -99,24 +99,37 @@ __host__ __device__ inline Layout layout(int H, int cout, int K) {
     L.sgn = L.ln + (uint32_t)cout * 8;
     L.bars = (L.sgn + (uint32_t)cout * 4 + 7) & ~7u;
     L.fails = L.bars + 16 * 8 + 8;
-    L.stage = (L.fails + 2 * kComputeWarps * 4 + 127) & ~127u;
+    L.stage = (L.fails + 2 * kEpilogueWarps * 4 + 16 + 127) & ~127u;
     L.stage_bytes = 32u * cw * 4u + ppw * cw * 4u;
-    L.total = L.stage + kComputeWarps * L.stage_bytes;
+    L.total = L.stage + kEpilogueWarps * L.stage_bytes;
     return L;
 }
 
-// 16-byte chunk position of chunk c of staged row r (rows of nc chunks): XOR
-// swizzles under which the eight lanes of one quarter-warp phase, reading
-// chunk c of eight consecutive rows, hit eight distinct 16-byte bank groups
-// for row pitches of 4, 8 and 12 chunks.
-__device__ __forceinline__ int stage_swizzle(int r, int c, int nc) {
-    if (nc >= 8 && c < 8) return c ^ (r & 7);
-    const int base = nc >= 8 ? 8 : 0;
-    return base + ((c - base) ^ ((r >> 1) & 3));
+// 16-byte chunk position of chunk c of staged row r (rows of a multiple of 8
+// chunks, i.e. of 128 bytes): XOR within each 8-chunk block, so the eight
+// lanes of a quarter-warp phase reading chunk c of eight consecutive rows hit
+// eight distinct 16-byte bank groups.
+__device__ __forceinline__ int stage_swizzle(int r, int c) { return (c & ~7) | ((c ^ r) & 7); }
+
+// The two epilogue warps of lane quarter q.
+__device__ __forceinline__ void quarter_barrier(int q) {
+    asm volatile("bar.sync %0, 64;" ::"r"(q + 1) : "memory");
 }
 
-__device__ __forceinline__ void quarter_barrier(int q) {
-    asm volatile("bar.sync %0, 128;" ::"r"(q + 1) : "memory");
+// The four control warps.
+__device__ __forceinline__ void control_barrier() {
+    asm volatile("bar.sync 5, 128;" ::: "memory");
+}
+
+// Order-preserving map of a float onto an unsigned integer (negative values
+// have all bits flipped, the others the sign bit), so that the integer max is
+// the float max; unorder() inverts it.
+__device__ __forceinline__ uint32_t order_key(float y) {
+    const uint32_t b = __float_as_uint(y);
+    return b ^ ((uint32_t)((int32_t)b >> 31) | 0x80000000u);
+}
+__device__ __forceinline__ float unorder(uint32_t k) {
+    return __uint_as_float(k ^ ((uint32_t)((int32_t)~k >> 31) | 0x80000000u));
 }
 
 // Bounded mbarrier wait by lane 0 of the warp, result shared by the warp.
@@ -126,7 +139,7 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* e
     return __shfl_sync(kFull, ok, 0) != 0;
 }
 
-template <int kNch, bool kK32>
+template <int kNch>  // 16-channel chunks of an epilogue warp (cw / 16)
 __global__ void __launch_bounds__(kThreads, 1)
 edge_unified_kernel(const UArgs a) {
     extern __shared__ __align__(1024) unsigned char edge_u_smem_raw[];
@@ -144,13 +157,14 @@ edge_unified_kernel(const UArgs a) {
     float* sSgn = reinterpret_cast<float*>(smem + L.sgn);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bars);
     uint64_t* pre_full = bars + 0;   // [2] pre-activations of a slot's tile in TMEM
-    uint64_t* a_ready = bars + 2;    // [2] hidden rows of a slot written (16 arrivals)
+    uint64_t* a_ready = bars + 2;    // [2] hidden rows of a slot written (8 arrivals)
     uint64_t* slot_free = bars + 4;  // [2] the MMAs reading a slot are done
     uint64_t* acc_full = bars + 6;   // [2] accumulator holds its tile
-    uint64_t* acc_free = bars + 8;   // [2] accumulator read out (16 arrivals)
+    uint64_t* acc_free = bars + 8;   // [2] accumulator read out (8 arrivals)
     uint64_t* mma_done = bars + 10;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
-    volatile int* sFail = reinterpret_cast<volatile int*>(smem + L.fails);  // [2][16]
+    volatile int* sFail = reinterpret_cast<volatile int*>(smem + L.fails);  // [2][8]
+    volatile int* sCtlFail = sFail + 2 * kEpilogueWarps;  // control warps' failure flag
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int R = a.B * a.M;
@@ -166,62 +180,58 @@ edge_unified_kernel(const UArgs a) {
     if (tid == 0) {
         for (int s = 0; s < 2; ++s) {
             tc::mbar_init(&pre_full[s], 1);
-            tc::mbar_init(&a_ready[s], kComputeWarps);
+            tc::mbar_init(&a_ready[s], kHiddenWarps);
             tc::mbar_init(&slot_free[s], 1);
             tc::mbar_init(&acc_full[s], 1);
-            tc::mbar_init(&acc_free[s], kComputeWarps);
+            tc::mbar_init(&acc_free[s], kEpilogueWarps);
         }
         tc::mbar_init(mma_done, 1);
         tc::fence_barrier_init();
     }
-    if (tid < 2 * kComputeWarps) sFail[tid] = 0;
+    if (tid <= 2 * kEpilogueWarps) sFail[tid] = 0;  // and the control flag
     fence_proxy_async();  // the weights written above, for the tensor cores
-    if (warp == kControlWarp) tc::tmem_alloc(tmem_slot, a.tmem_cols);
+    if (warp == kControlWarp0) tc::tmem_alloc(tmem_slot, a.tmem_cols);
     tc::tc_fence_before();
     __syncthreads();
     tc::tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
-    if (warp == kControlWarp) {
+    if (warp >= kControlWarp0) {
         // ---------------- control: u rows, pre-activation and main MMAs ----------------
-        // geometry of the four rows this lane computes u for (rows lane + 32 m),
-        // fetched in two stages a tile apart so that no load waits on another:
-        // stage 1 reads the neighbour indices and centre points of a tile,
-        // stage 2 (one tile later) the neighbour points they name
-        float4 gi[4], gj[4], ni[4];
-        int nj[4];
-        bool gvalid[4], nvalid[4];
+        // Control warp c computes the u rows of TMEM lanes 32c .. 32c + 31 (one
+        // row per lane); the four meet at a named barrier once the rows of a
+        // tile are in shared memory, and lane 0 of control warp 0 issues the
+        // MMAs. The geometry of a row is fetched in two stages a tile apart so
+        // that no load waits on another: stage 1 reads the neighbour index and
+        // the centre point, stage 2 (one tile later) the neighbour point.
+        const int cwarp = warp - kControlWarp0;
+        const int row = cwarp * 32 + lane;
+        float3 gi, gj, ni;
+        int nj = 0;
+        bool gvalid = false, nvalid = false;
         auto fetch_indices = [&](int t) {
-#pragma unroll
-            for (int m = 0; m < 4; ++m) {
-                const int row = lane + 32 * m;
-                const int p = t * a.ppt + (row >> a.log2K);
-                nvalid[m] = t < n_tiles && p < R;
-                const int pc = nvalid[m] ? p : 0;
-                ni[m] = *reinterpret_cast<const float4*>(a.xyz4 + (size_t)pc * 4);
-                nj[m] = (pc / a.M) * a.M + a.idx[(size_t)pc * K + (row & (K - 1))];
-            }
+            const int p = t * a.ppt + (row >> a.log2K);
+            nvalid = t < n_tiles && p < R;
+            const int pc = nvalid ? p : 0;
+            const float4 v = *reinterpret_cast<const float4*>(a.xyz4 + (size_t)pc * 4);
+            ni = make_float3(v.x, v.y, v.z);
+            nj = (pc / a.M) * a.M + a.idx[(size_t)pc * K + (row & (K - 1))];
         };
         auto fetch_points = [&]() {
-#pragma unroll
-            for (int m = 0; m < 4; ++m) {
-                gi[m] = ni[m];
-                gj[m] = *reinterpret_cast<const float4*>(a.xyz4 + (size_t)nj[m] * 4);
-                gvalid[m] = nvalid[m];
-            }
+            gi = ni;
+            const float4 v = *reinterpret_cast<const float4*>(a.xyz4 + (size_t)nj * 4);
+            gj = make_float3(v.x, v.y, v.z);
+            gvalid = nvalid;
         };
         auto load_geometry = [&](int t) {  // both stages at once (start-up only)
             fetch_indices(t);
             fetch_points();
         };
         auto write_u = [&]() {
-            const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-            for (int m = 0; m < 4; ++m)
-                write_u_row(sU, sGram, lane + 32 * m, gvalid[m] ? gi[m] : zero,
-                            gvalid[m] ? gj[m] : zero);
-            fence_proxy_async();
-            __syncwarp();
+            const float3 zero = make_float3(0.f, 0.f, 0.f);
+            const float3 pi[1] = {gvalid ? gi : zero};
+            const float3 pj[1] = {gvalid ? gj : zero};
+            write_u_rows<1>(sU, sGram, row, 0, pi, pj);
         };
         // pre = LN(W_in g + b_in) of the tile whose u rows are in sU, into slot s
         auto issue_pre = [&](int s) {
@@ -236,17 +246,14 @@ edge_unified_kernel(const UArgs a) {
             tc::umma<true>(d, du_lo, dw, a.idesc_pre, 1u);
             tc::umma_commit(&pre_full[s]);
         };
-        const int hq = H / 4, steps_per_part = hq / 16;
         // W_po h of the tile in slot s into accumulator acc: per K step of 16
         // channels hi*hi + hi*lo + lo*hi, A (the hidden rows) from TMEM
         auto issue_main = [&](int s, int acc) {
             const uint32_t d = tmem_base + (uint32_t)(acc * cout);
             const uint32_t b0 = tc::smem_u32(sB), b1 = tc::smem_u32(sBlo);
             for (int k = 0; k < H / 16; ++k) {
-                const int part = k / steps_per_part, j = k - part * steps_per_part;
-                const uint32_t hi_col =
-                    tmem_base + slot_col0 + (uint32_t)(s * H + part * hq + j * 8);
-                const uint32_t lo_col = hi_col + (uint32_t)(hq / 2);
+                const uint32_t hi_col = tmem_base + slot_col0 + (uint32_t)(s * H + 16 * k);
+                const uint32_t lo_col = hi_col + 8u;
                 const int kb = k >> 2, w = k & 3;
                 const uint64_t db_hi = tc::sw128_desc(b0 + (uint32_t)(kb * cout * 128)) + 2 * w;
                 const uint64_t db_lo = tc::sw128_desc(b1 + (uint32_t)(kb * cout * 128)) + 2 * w;
@@ -255,40 +262,53 @@ edge_unified_kernel(const UArgs a) {
                 tc::umma_tmem_a_f16(d, lo_col, db_hi, a.idesc, 1u);
             }
         };
-        bool ok = true;
-        const int t0 = blockIdx.x, t1 = blockIdx.x + (int)gridDim.x;
+        const bool issuer = cwarp == 0 && lane == 0;
+        // u rows of the current geometry in sU, visible to the tensor cores
+        // once every control warp has passed the barrier; a failure seen by
+        // any control warp before the barrier is seen by all after it
+        auto rows_written = [&](bool ok) -> bool {
+            if (!ok && lane == 0) *sCtlFail = 1;
+            fence_proxy_async();
+            control_barrier();
+            return *sCtlFail == 0;
+        };
+        const int G = (int)gridDim.x;
+        const int t0 = blockIdx.x, t1 = blockIdx.x + G;
         load_geometry(t0);
         write_u();
-        if (lane == 0) issue_pre(0);
-        load_geometry(t1);
-        if (t1 < n_tiles) {
-            ok = warp_wait(&pre_full[0], 0, a.err, lane);  // sU read by pre(t0)
-            if (ok) {
-                write_u();
-                if (lane == 0) issue_pre(1);
-            }
+        bool ok = rows_written(true);
+        if (ok && issuer) issue_pre(0);
+        if (ok && t1 < n_tiles) {
+            load_geometry(t1);
+            const bool waited = warp_wait(&pre_full[0], 0, a.err, lane);  // sU read by pre(t0)
+            if (waited) write_u();
+            ok = rows_written(waited);
+            if (ok && issuer) issue_pre(1);
         }
-        load_geometry(t1 + (int)gridDim.x);        // tile index 2
-        fetch_indices(t1 + 2 * (int)gridDim.x);    // tile index 3, stage 1
-        // per tile index it: the u rows of tile it + 2 (its geometry loaded
-        // one iteration earlier) while the compute warps still produce the
-        // hidden rows of tile it, then MMA(it), then the pre-activations of
-        // tile it + 2 into the slot MMA(it) has released
+        load_geometry(t1 + G);      // tile index 2
+        fetch_indices(t1 + 2 * G);  // tile index 3, stage 1
+        // per tile index it: the u rows of tile it + 2 (their geometry loaded
+        // one iteration earlier) while the hidden-row warps still produce
+        // tile it, then MMA(it), then the pre-activations of tile it + 2 into
+        // the slot MMA(it) has released
         for (int it = 0; ok; ++it) {
-            const int tile = blockIdx.x + it * (int)gridDim.x;
+            const int tile = blockIdx.x + it * G;
             if (tile >= n_tiles) break;
             const int s = it & 1, acc = it % a.n_acc;
-            const int tile2 = tile + 2 * (int)gridDim.x;
+            const int tile2 = tile + 2 * G;
+            bool mine = true;
             if (tile2 < n_tiles) {
-                ok = warp_wait(&pre_full[s ^ 1], (uint32_t)((it + 1) >> 1) & 1u, a.err, lane);
-                if (!ok) break;
-                write_u();
-                fetch_points();                               // tile index it + 3
-                fetch_indices(tile2 + 2 * (int)gridDim.x);    // tile index it + 4
+                mine = warp_wait(&pre_full[s ^ 1], (uint32_t)((it + 1) >> 1) & 1u, a.err, lane);
+                if (mine) {
+                    write_u();
+                    fetch_points();               // tile index it + 3
+                    fetch_indices(tile2 + 2 * G);  // tile index it + 4
+                }
             }
-            int good = 1;
-            if (lane == 0) {
-                good = tc::mbar_wait_spin(&a_ready[s], (uint32_t)(it >> 1) & 1u, a.err);
+            ok = rows_written(mine);
+            if (!ok) break;
+            if (issuer) {
+                bool good = tc::mbar_wait_spin(&a_ready[s], (uint32_t)(it >> 1) & 1u, a.err);
                 if (good && it >= a.n_acc)
                     good = tc::mbar_wait_spin(&acc_free[acc], ((uint32_t)(it / a.n_acc) & 1u) ^ 1u,
                                               a.err);
@@ -298,32 +318,78 @@ edge_unified_kernel(const UArgs a) {
                     tc::umma_commit(&slot_free[s]);
                     tc::umma_commit(&acc_full[acc]);
                 }
+                if (good && tile2 < n_tiles) {
+                    good = tc::mbar_wait_spin(&slot_free[s], (uint32_t)(it >> 1) & 1u, a.err);
+                    if (good) {
+                        tc::tc_fence_after();
+                        issue_pre(s);
+                    }
+                }
+                if (!good) *sCtlFail = 1;  // the others stop after the next barrier
             }
-            ok = __shfl_sync(kFull, good, 0) != 0;
-            if (!ok || tile2 >= n_tiles) continue;
-            ok = warp_wait(&slot_free[s], (uint32_t)(it >> 1) & 1u, a.err, lane);
-            if (ok && lane == 0) {
-                tc::tc_fence_after();
-                issue_pre(s);
-            }
+            __syncwarp();
         }
-        if (lane == 0) {
+        if (issuer) {
             // every MMA issued completes before the CTA frees its memory
             tc::umma_commit(mma_done);
             tc::mbar_drain(mma_done, 0);
         }
+    } else if (warp < kHiddenWarps) {
+        // ---------------- hidden rows ----------------
+        const int q = warp & 3, half = warp >> 2;
+        const uint32_t lane_off = tmem_base + ((uint32_t)(q * 32) << 16);
+        const int chunks = H / 32;  // 16-channel chunks of this warp's half
+        for (int it = 0;; ++it) {
+            const int tile = blockIdx.x + it * (int)gridDim.x;
+            if (tile >= n_tiles) break;
+            const int s = it & 1;
+            if (!warp_wait(&pre_full[s], (uint32_t)(it >> 1) & 1u, a.err, lane)) break;
+            tc::tc_fence_after();
+            const uint32_t col0 = lane_off + slot_col0 + (uint32_t)(s * H + half * (H / 2));
+            // chunk c: fp32 pre-activations in its 16 columns, replaced by the
+            // bf16 high halves (first 8 columns) and low halves (next 8); the
+            // next chunk's load is in flight while this one is computed
+            uint32_t r[2][16];
+            tc::tmem_ld16_issue(col0, r[0]);
+            tc::tmem_ld16_wait(r[0]);
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                if (c >= chunks) break;
+                uint32_t(&cur)[16] = r[c & 1];
+                if (c + 1 < chunks) tc::tmem_ld16_issue(col0 + (uint32_t)(16 * (c + 1)), r[(c + 1) & 1]);
+                uint32_t hi[8], lo[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const float2 o = gelu_as2(
+                        make_float2(__uint_as_float(cur[2 * e]), __uint_as_float(cur[2 * e + 1])));
+                    const __nv_bfloat162 h2 = __floats2bfloat162_rn(o.x, o.y);
+                    hi[e] = *reinterpret_cast<const uint32_t*>(&h2);
+                    const float2 hf = make_float2(__uint_as_float(hi[e] << 16),
+                                                  __uint_as_float(hi[e] & 0xffff0000u));
+                    const float2 rem = fma2(hf, f2(-1.0f), o);  // o - hi, exact
+                    lo[e] = pack_bf16(rem.x, rem.y);
+                }
+                tc::tmem_st_async<8>(col0 + (uint32_t)(16 * c), hi);
+                tc::tmem_st_async<8>(col0 + (uint32_t)(16 * c + 8), lo);
+                if (c + 1 < chunks) tc::tmem_ld16_wait(r[(c + 1) & 1]);
+            }
+            tc::tmem_st_wait();
+            tc::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&a_ready[s]);
+        }
     } else {
-        // ---------------- compute warps ----------------
-        const int q = warp & 3, part = warp >> 2;
+        // ---------------- epilogue ----------------
+        const int ew = warp - kEpiWarp0;
+        const int q = ew & 3, half = ew >> 2;
         const int erow = q * 32 + lane;  // TMEM lane = edge row
         const int kk = erow & (K - 1);
         const int ptw = lane >> a.log2K;  // this lane's point within the warp's points
         const int ppw = 32 >> a.log2K;
         constexpr int nch = kNch, cw = 16 * kNch, nc = cw / 4;
-        const int ch0 = part * cw;
-        const int hq = H / 4;
+        const int ch0 = half * cw;
         const uint32_t lane_off = tmem_base + ((uint32_t)(q * 32) << 16);
-        const uint32_t stage = tc::smem_u32(smem + L.stage) + (uint32_t)warp * L.stage_bytes;
+        const uint32_t stage = tc::smem_u32(smem + L.stage) + (uint32_t)ew * L.stage_bytes;
         const uint32_t centre = stage + 32u * (uint32_t)cw * 4u;
         auto neighbour_row = [&](int t) -> int {
             const int p = t * a.ppt + (erow >> a.log2K);
@@ -337,10 +403,11 @@ edge_unified_kernel(const UArgs a) {
             if (t < n_tiles) {
                 const int jl = max(jrow, 0);
                 const float* src0 = a.content + ch0;
+#pragma unroll 4
                 for (int i = lane; i < 32 * nc; i += 32) {
                     const int r = i / nc, c = i - r * nc;
                     const int j = __shfl_sync(kFull, jl, r);
-                    cp_async16(stage + (uint32_t)(r * cw * 4 + stage_swizzle(r, c, nc) * 16),
+                    cp_async16(stage + (uint32_t)(r * cw * 4 + stage_swizzle(r, c) * 16),
                                src0 + (size_t)j * a.ldc + c * 4);
                 }
                 const int pbase = t * a.ppt + ((q * 32) >> a.log2K);
@@ -353,61 +420,21 @@ edge_unified_kernel(const UArgs a) {
             }
             cp_async_commit();
         };
-        // hidden rows of tile index it into slot it & 1
-        auto gelu_tile = [&](int it) -> bool {
-            const int s = it & 1;
-            if (!warp_wait(&pre_full[s], (uint32_t)(it >> 1) & 1u, a.err, lane)) return false;
-            tc::tc_fence_after();
-            const uint32_t col = lane_off + slot_col0 + (uint32_t)(s * H + part * hq);
-            // all of this warp's pre-activations are read before any hidden
-            // row is written over them (the low halves of the first 16
-            // channels land where the pre-activations of the next 16 were)
-            uint32_t r[2][16];
-            tc::tmem_ld<16>(col, r[0]);
-            if (hq > 16) tc::tmem_ld<16>(col + 16u, r[1]);
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                if (h * 16 >= hq) break;
-                uint32_t hi[8], lo[8];
-#pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    const float2 o = gelu_as2(
-                        make_float2(__uint_as_float(r[h][2 * e]), __uint_as_float(r[h][2 * e + 1])));
-                    const __nv_bfloat162 h2 = __floats2bfloat162_rn(o.x, o.y);
-                    hi[e] = *reinterpret_cast<const uint32_t*>(&h2);
-                    const float2 hf = make_float2(__uint_as_float(hi[e] << 16),
-                                                  __uint_as_float(hi[e] & 0xffff0000u));
-                    const float2 rem = fma2(hf, f2(-1.0f), o);  // o - hi, exact
-                    lo[e] = pack_bf16(rem.x, rem.y);
-                }
-                // channels 16h .. 16h + 15 of this warp's hq: packed columns
-                // 8h .. 8h + 7 of its high half, hq / 2 later the low half
-                tc::tmem_st_async<8>(col + (uint32_t)(8 * h), hi);
-                tc::tmem_st_async<8>(col + (uint32_t)(hq / 2 + 8 * h), lo);
-            }
-            tc::tmem_st_wait();
-            tc::tc_fence_before();
-            __syncwarp();
-            if (lane == 0) tc::mbar_arrive(&a_ready[s]);
-            return true;
-        };
 
         int jcur = neighbour_row(blockIdx.x);
+        int jnext = neighbour_row(blockIdx.x + (int)gridDim.x);  // read a tile ahead
         issue_stage(blockIdx.x, jcur);
-        // a failed wait is carried to the next moment exchange, where the
-        // four warps of the lane quarter stop together (each warp reaches the
-        // quarter's named barrier once per tile until then)
-        bool ok = gelu_tile(0);
         for (int it = 0;; ++it) {
             const int tile = blockIdx.x + it * (int)gridDim.x;
             if (tile >= n_tiles) break;
             const int next = tile + (int)gridDim.x;
-            if (ok && next < n_tiles) ok = gelu_tile(it + 1);
-            // ---- epilogue of tile it ----
             const int acc = it % a.n_acc;
             const uint32_t rj = stage + (uint32_t)(lane * cw * 4);  // this lane's staged row
             const uint32_t ri = centre + (uint32_t)(ptw * cw * 4);
-            if (ok) ok = warp_wait(&acc_full[acc], (uint32_t)(it / a.n_acc) & 1u, a.err, lane);
+            // a failed wait is carried to the moment exchange below, where
+            // the two warps of the lane quarter stop together (each reaches
+            // the quarter's named barrier once per tile until then)
+            bool ok = warp_wait(&acc_full[acc], (uint32_t)(it / a.n_acc) & 1u, a.err, lane);
             if (ok) {
                 tc::tc_fence_after();
                 cp_async_wait(0);
@@ -418,16 +445,19 @@ edge_unified_kernel(const UArgs a) {
                 const uint32_t acol = lane_off + (uint32_t)(acc * cout + ch0);
                 float shift = 0.0f;
                 float2 s1p = f2(0.0f), s2p = f2(0.0f);
-#pragma unroll
+                uint32_t racc[2][16];
+                tc::tmem_ld16_issue(acol, racc[0]);
+                tc::tmem_ld16_wait(racc[0]);
+#pragma unroll 2
                 for (int k = 0; k < nch; ++k) {
-                    uint32_t r[16];
-                    tc::tmem_ld<16>(acol + (uint32_t)(16 * k), r);
+                    uint32_t(&r)[16] = racc[k & 1];
+                    if (k + 1 < nch) tc::tmem_ld16_issue(acol + (uint32_t)(16 * (k + 1)), racc[(k + 1) & 1]);
                     float2 m[8];
                     float2 csum = f2(0.0f);
 #pragma unroll
                     for (int q4 = 0; q4 < 4; ++q4) {
                         const int c = 4 * k + q4;
-                        const uint32_t pos = rj + (uint32_t)(stage_swizzle(lane, c, nc) * 16);
+                        const uint32_t pos = rj + (uint32_t)(stage_swizzle(lane, c) * 16);
                         const float4 nj = lds128(pos);
                         const float4 ni = lds128(ri + (uint32_t)(c * 16));
                         const float4 bb = *reinterpret_cast<const float4*>(sCb + ch0 + 4 * c);
@@ -451,6 +481,7 @@ edge_unified_kernel(const UArgs a) {
                         s1p = add2(s1p, d);
                         s2p = fma2(d, d, s2p);
                     }
+                    if (k + 1 < nch) tc::tmem_ld16_wait(racc[(k + 1) & 1]);
                 }
                 // the accumulator has been read: the next tile's MMA may use it
                 tc::tc_fence_before();
@@ -461,130 +492,97 @@ edge_unified_kernel(const UArgs a) {
                 const float n_p = (float)cw;
                 const uint32_t st[2] = {__float_as_uint(shift + s1 / n_p),
                                         __float_as_uint(fmaxf(s2 - s1 * (s1 / n_p), 0.0f))};
-                tc::tmem_st_async<2>(lane_off + stat_col + (uint32_t)((it & 1) * 8 + part * 2), st);
+                tc::tmem_st_async<2>(lane_off + stat_col + (uint32_t)((it & 1) * 4 + half * 2), st);
                 tc::tmem_st_wait();
             }
-            if (lane == 0) sFail[(it & 1) * kComputeWarps + warp] = ok ? 0 : 1;
+            if (lane == 0) sFail[(it & 1) * kEpilogueWarps + ew] = ok ? 0 : 1;
             tc::tc_fence_before();
             quarter_barrier(q);
             tc::tc_fence_after();
-            bool quarter_ok = true;
-#pragma unroll
-            for (int p = 0; p < 4; ++p) quarter_ok &= sFail[(it & 1) * kComputeWarps + q + 4 * p] == 0;
-            if (!quarter_ok) break;
-            // the four warps' moments, combined pairwise (Chan et al.)
-            uint32_t stats[8];
-            tc::tmem_ld<8>(lane_off + stat_col + (uint32_t)((it & 1) * 8), stats);
-            float mean = 0.0f;
-#pragma unroll
-            for (int p = 0; p < 4; ++p) mean += __uint_as_float(stats[2 * p]);
-            mean *= 0.25f;
-            float m2 = 0.0f;
-#pragma unroll
-            for (int p = 0; p < 4; ++p) {
-                const float dm = __uint_as_float(stats[2 * p]) - mean;
-                m2 += __uint_as_float(stats[2 * p + 1]) + (float)cw * dm * dm;
+            if (sFail[(it & 1) * kEpilogueWarps + q] != 0 ||
+                sFail[(it & 1) * kEpilogueWarps + q + 4] != 0)
+                break;
+            // the two halves' moments, combined pairwise (Chan et al.)
+            uint32_t stats[2][2];
+            {
+                uint32_t s4[8];
+                tc::tmem_ld<8>(lane_off + stat_col, s4);  // both parities; this tile's 4 columns
+                const bool odd = (it & 1) != 0;  // (selects keep s4 in registers)
+                stats[0][0] = odd ? s4[4] : s4[0];
+                stats[0][1] = odd ? s4[5] : s4[1];
+                stats[1][0] = odd ? s4[6] : s4[2];
+                stats[1][1] = odd ? s4[7] : s4[3];
             }
+            const float m0 = __uint_as_float(stats[0][0]), m1 = __uint_as_float(stats[1][0]);
+            const float mean = 0.5f * (m0 + m1);
+            const float dm = m1 - m0;
+            const float m2 = __uint_as_float(stats[0][1]) + __uint_as_float(stats[1][1]) +
+                             dm * dm * (0.5f * (float)cw);
             const float rstd = rsqrtf(m2 / (float)cout + 1e-6f);
             const float nmr = -mean * rstd;
-            const int ep = tile * a.ppt + (erow >> a.log2K);
-            const bool valid_row = jcur >= 0;
-            // normalised message times the sign of the gain; its max over the
-            // K rows of a point, then |gain| x + shift and LeakyReLU(0.2)
-            const float2 rstd2 = f2(rstd), nmr2 = f2(nmr);
-            auto normalised = [&](int k, float (&y)[16]) {
+            // the max over the K rows of each point of the normalised message,
+            // by columns: lane l takes channels l, l + 32, ... of this warp's
+            // cw and walks the rows of each point in the staged messages,
+            // keeping the max and min of (m - mean) rstd (the row's rstd and
+            // -mean rstd come by shuffle); the sign of the gain picks max or
+            // -min, then |gain| x + shift and LeakyReLU(0.2), stored coalesced
+            __syncwarp();  // every lane's messages are in shared memory
+            // channel lane + 32 j of staged row r: chunk (lane / 4 + 8 j), stored
+            // at chunk 8 j + ((lane / 4) ^ (r & 7)) of the row (rows start on
+            // 128-byte boundaries), element lane % 4
+            const uint32_t lane_part = (uint32_t)(((lane >> 2) << 4) | ((lane & 3) << 2));
+            constexpr int nj = cw / 32;  // channels per lane (1, 2, 3)
+            float gain[nj], shift_c[nj], sgn[nj];
 #pragma unroll
-                for (int q4 = 0; q4 < 4; ++q4) {
-                    const int c = 4 * k + q4;
-                    const float4 mv = lds128(rj + (uint32_t)(stage_swizzle(lane, c, nc) * 16));
-                    const float4 sg = *reinterpret_cast<const float4*>(sSgn + ch0 + 4 * c);
-                    const float2 y0 = mul2(fma2(make_float2(mv.x, mv.y), rstd2, nmr2),
-                                           make_float2(sg.x, sg.y));
-                    const float2 y1 = mul2(fma2(make_float2(mv.z, mv.w), rstd2, nmr2),
-                                           make_float2(sg.z, sg.w));
-                    y[4 * q4 + 0] = valid_row ? y0.x : -FLT_MAX;
-                    y[4 * q4 + 1] = valid_row ? y0.y : -FLT_MAX;
-                    y[4 * q4 + 2] = valid_row ? y1.x : -FLT_MAX;
-                    y[4 * q4 + 3] = valid_row ? y1.y : -FLT_MAX;
-                }
-            };
-            if constexpr (kK32) {
-                // one point per warp: warp-wide maxima; lane 0 parks those of
-                // chunk k over the staged row 0 positions of chunk k (lane 0's
-                // own row, already read) and lane c stores channel c
-                float* red = reinterpret_cast<float*>(smem + L.stage + (size_t)warp * L.stage_bytes);
-#pragma unroll
-                for (int k = 0; k < nch; ++k) {
-                    float y[16];
-                    normalised(k, y);
-#pragma unroll
-                    for (int i = 0; i < 16; i += 4) {
-                        float r4[4];
-#pragma unroll
-                        for (int e = 0; e < 4; ++e)
-                            asm("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(r4[e]) : "f"(y[i + e]));
-                        if (lane == 0)
-                            *reinterpret_cast<float4*>(red + 16 * k + i) =
-                                make_float4(r4[0], r4[1], r4[2], r4[3]);
-                    }
-                }
-                __syncwarp();
-                if (ep < R) {
-                    for (int c = lane; c < cw; c += 32) {
-                        const float2 gs = *reinterpret_cast<const float2*>(sLn + 2 * (ch0 + c));
-                        const float t = fmaf(red[c], gs.x, gs.y);
-                        a.out[(size_t)ep * a.ldo + ch0 + c] = fmaxf(t, 0.2f * t);
-                    }
-                }
-                __syncwarp();  // the maxima are read before the next copies land there
-            } else {
-                // K < 32: a butterfly over the K lanes of each point leaves
-                // 16 / K channels of each 16-channel chunk per lane
-#pragma unroll
-                for (int k = 0; k < nch; ++k) {
-                    float y[16];
-                    normalised(k, y);
-                    int off = 0;
-#pragma unroll
-                    for (int sdx = 0; sdx < 4; ++sdx) {
-                        if (sdx < a.log2K) {
-                            const int msk = K >> (sdx + 1);
-                            const bool hi = (lane & msk) != 0;
-                            const int h = 8 >> sdx;
-#pragma unroll
-                            for (int i = 0; i < h; ++i) {
-                                const float send = hi ? y[i] : y[h + i];
-                                const float keep = hi ? y[h + i] : y[i];
-                                y[i] = fmaxf(keep, __shfl_xor_sync(kFull, send, msk));
-                            }
-                            off += hi ? h : 0;
-                        }
-                    }
-                    if (ep < R) {
-                        const int nv = 16 >> a.log2K;
-                        float* o = a.out + (size_t)ep * a.ldo + ch0 + 16 * k + off;
-#pragma unroll
-                        for (int i = 0; i < 16; ++i) {
-                            if (i < nv) {
-                                const float2 gs = *reinterpret_cast<const float2*>(
-                                    sLn + 2 * (ch0 + 16 * k + off + i));
-                                const float t = fmaf(y[i], gs.x, gs.y);
-                                o[i] = fmaxf(t, 0.2f * t);
-                            }
-                        }
-                    }
-                }
-                __syncwarp();
+            for (int j = 0; j < nj; ++j) {
+                const int c = ch0 + lane + 32 * j;
+                gain[j] = sLn[2 * c];
+                shift_c[j] = sLn[2 * c + 1];
+                sgn[j] = sSgn[c];
             }
+            const int pbase = tile * a.ppt + ((q * 32) >> a.log2K);
+            for (int pt = 0; pt < ppw; ++pt) {
+                float mx[nj], mn[nj];
+#pragma unroll
+                for (int j = 0; j < nj; ++j) {
+                    mx[j] = -FLT_MAX;
+                    mn[j] = FLT_MAX;
+                }
+#pragma unroll 4
+                for (int e = 0; e < K; ++e) {
+                    const int row = pt * K + e;
+                    const float re = __shfl_sync(kFull, rstd, row);
+                    const float ne = __shfl_sync(kFull, nmr, row);
+                    const uint32_t rowa =
+                        stage + (uint32_t)(row * cw * 4) + (lane_part ^ (uint32_t)((row & 7) << 4));
+#pragma unroll
+                    for (int j = 0; j < nj; ++j) {
+                        const float x = fmaf(lds32(rowa + (uint32_t)(128 * j)), re, ne);
+                        mx[j] = fmaxf(mx[j], x);
+                        mn[j] = fminf(mn[j], x);
+                    }
+                }
+                const int p = pbase + pt;
+                if (p < R) {
+#pragma unroll
+                    for (int j = 0; j < nj; ++j) {
+                        const float v = sgn[j] > 0.0f ? mx[j] : -mn[j];
+                        const float t = fmaf(v, gain[j], shift_c[j]);
+                        a.out[(size_t)p * a.ldo + ch0 + lane + 32 * j] = fmaxf(t, 0.2f * t);
+                    }
+                }
+            }
+            __syncwarp();  // the messages are read before the next copies land there
             // this tile's staging has been read: bring in the next tile's
-            jcur = neighbour_row(next);
+            jcur = jnext;
             issue_stage(next, jcur);
+            jnext = neighbour_row(next + (int)gridDim.x);
         }
         cp_async_wait(0);  // no copy into shared memory outlives the loop
     }
     tc::tc_fence_before();
     __syncthreads();
-    if (warp == kControlWarp) {
+    if (warp == kControlWarp0) {
         tc::tc_fence_after();
         tc::tmem_dealloc(tmem_base, a.tmem_cols);
     }
@@ -592,7 +590,7 @@ edge_unified_kernel(const UArgs a) {
 
 }  // namespace
 
-// The split-bf16 neighbour stage on the unified kernel when its shape allows:
+// The split-bf16 neighbour stage on the three-role kernel when its shape allows:
 // H in {64, 128}, C_out in {64, 128, 192}, K in {8, 16, 32}, xyz4 geometry;
 // F2S_ERR_UNSUPPORTED otherwise (the caller then uses edge_tc_kernel).
 int edge_stage_unified(const EdgeArgs& e, cudaStream_t st) {
@@ -621,8 +619,8 @@ int edge_stage_unified(const EdgeArgs& e, cudaStream_t st) {
     a.H = e.H;
     a.cout = e.cout;
     a.ppt = kRows / e.K;
-    a.n_acc = 2 * e.cout + 2 * e.H + 16 <= 512 ? 2 : 1;
-    const int cols = a.n_acc * e.cout + 2 * e.H + 16;
+    a.n_acc = 2 * e.cout + 2 * e.H + 8 <= 512 ? 2 : 1;
+    const int cols = a.n_acc * e.cout + 2 * e.H + 8;
     uint32_t tcols = 32;
     while (tcols < (uint32_t)cols) tcols <<= 1;
     a.tmem_cols = tcols;
@@ -649,11 +647,10 @@ int edge_stage_unified(const EdgeArgs& e, cudaStream_t st) {
         kernel<<<grid, kThreads, smem, st>>>(a);
         return check_launch("edge_unified_kernel");
     };
-    const bool k32 = e.K == 32;
     switch (e.cout / 64) {
-        case 1: return k32 ? launch(edge_unified_kernel<1, true>) : launch(edge_unified_kernel<1, false>);
-        case 2: return k32 ? launch(edge_unified_kernel<2, true>) : launch(edge_unified_kernel<2, false>);
-        default: return k32 ? launch(edge_unified_kernel<3, true>) : launch(edge_unified_kernel<3, false>);
+        case 1: return launch(edge_unified_kernel<2>);
+        case 2: return launch(edge_unified_kernel<4>);
+        default: return launch(edge_unified_kernel<6>);
     }
 }
 
