@@ -92,6 +92,20 @@ int f2s_offset_attention(const float* query, const float* key, const float* valu
                          void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * f2s_offset_attention on tcgen05 tensor cores: S = q k^T as split-bf16 MMAs,
+ * the column softmax in two passes (per-key log-sum-exp, then P = exp(S - L)
+ * per key tile with P V as fp16 MMAs from tensor memory); the N x N scores
+ * never reach global memory. d a multiple of 4 up to 64, C a multiple of 64 up
+ * to 256, else F2S_ERR_UNSUPPORTED. Results within ~1e-3 relative of the fp32
+ * entry (fp16 P and V).
+ *   workspace: f2s_offset_attention_tc_workspace_bytes(B, N, d, C) bytes.
+ */
+int f2s_offset_attention_tc_workspace_bytes(int B, int N, int d, int C, size_t* bytes);
+int f2s_offset_attention_tc(const float* query, const float* key, const float* value, int B,
+                            int N, int d, int C, float* out, void* workspace,
+                            size_t workspace_bytes, void* stream);
+
+/*
  * Normalised neighbour-message reduction with HPE geometry, fused into one
  * kernel (hidden and per-edge contributions never reach HBM).
  * Replaces reduce_neighbor_messages (flow2surf/models/ops/neighbor_reduce.py:244-337)
@@ -114,6 +128,21 @@ int f2s_neighbor_reduce(const float* content, const float* geometry, const int32
                         void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * f2s_neighbor_reduce on tcgen05 tensor cores: the HPE output projection as
+ * split-bf16 MMAs (hi*hi + hi*lo + lo*hi, close to fp32), the hidden rows and
+ * the message reduce fused around it in one kernel. Same arguments, workspace
+ * and layouts; D = 6, H in {64, 128}, C in {64, 128, 192}, K in {8, 16, 32},
+ * F2S_ERR_UNSUPPORTED otherwise (nothing is launched then).
+ */
+int f2s_neighbor_reduce_tc(const float* content, const float* geometry, const int32_t* indices,
+                           const float* hpe_input_weight, const float* hpe_input_bias,
+                           const float* hpe_output_weight, const float* hpe_output_bias,
+                           const float* hpe_norm_weight, const float* hpe_norm_bias,
+                           const float* message_norm_weight, const float* message_norm_bias,
+                           int B, int N, int K, int D, int H, int C, float* out, void* workspace,
+                           size_t workspace_bytes, void* stream);
+
+/*
  * Point-wise linear map y = x W^T + b over rows of points: the 1x1
  * Conv1d / Linear of the reference's modules (e.g. transformer.py:37-48 via
  * Jittor's conv/linear) with point-major activations.
@@ -130,6 +159,12 @@ int f2s_neighbor_reduce(const float* content, const float* geometry, const int32
  * hi*hi + hi*lo + lo*hi on tensor cores: close to fp32 accuracy. Accepted by
  * the model's encoder_precision only. */
 #define F2S_PRECISION_BF16X3 3
+/* Trunk only: tf32 tensor cores as F2S_PRECISION_TF32, but the FFN input and
+ * hidden rows stay fp32 (F2S_PRECISION_TF32 stores them as fp16, which
+ * carries tf32's 10-bit mantissa in half the bytes but only fp16's range).
+ * The denoise entry points rerun a denoise in this mode when the fp16 rows
+ * overflowed (device error word 2). */
+#define F2S_PRECISION_TF32_WIDE 4
 int f2s_linear(const void* x, int ldx, const void* weight, const float* bias, float* y, int ldy,
                int rows, int cols, int K, int precision, void* stream);
 
@@ -172,8 +207,9 @@ typedef struct f2s_model_config {
     int32_t num_decoder;                     /* len(decoder_dims)              */
     int32_t decoder_dims[F2S_MAX_DECODER];   /* cfg["decoder_dims"]            */
     int32_t precision;                       /* trunk and decoder contractions:
-                                                F2S_PRECISION_FP32 (CUDA cores) or
-                                                F2S_PRECISION_TF32 (tcgen05)   */
+                                                F2S_PRECISION_FP32 (CUDA cores),
+                                                F2S_PRECISION_TF32 or _TF32_WIDE
+                                                (tcgen05)                      */
     int32_t encoder_precision;               /* neighbour stages and projection
                                                 head: the choices above or
                                                 F2S_PRECISION_BF16X3 (edge

@@ -217,12 +217,11 @@ __device__ __forceinline__ void convert_projection(const float* contrib_w, int H
     }
 }
 
-// The u row [rstd g, rstd, 1] of edge row `row` (g = [x_j - x_i, x_i],
-// rstd = 1 / sqrt(var + 1e-5) of its pre-activations, the variance from the
-// moments in sGram) as tf32 hi at sU and lo at sU + kUBytes.
-__device__ __forceinline__ void write_u_row(unsigned char* sU, const float* sGram, int row,
-                                            const float4& pi, const float4& pj) {
-    const float g[6] = {pj.x - pi.x, pj.y - pi.y, pj.z - pi.z, pi.x, pi.y, pi.z};
+// The u row [rstd g, rstd, 1] of edge row `row` from its geometry g (rstd =
+// 1 / sqrt(var + 1e-5) of its pre-activations, the variance from the moments
+// in sGram) as tf32 hi at sU and lo at sU + kUBytes.
+__device__ __forceinline__ void write_u_row_g(unsigned char* sU, const float* sGram, int row,
+                                              const float (&g)[6]) {
     float var = sGram[42];
 #pragma unroll
     for (int d = 0; d < 6; ++d) {
@@ -250,59 +249,11 @@ __device__ __forceinline__ void write_u_row(unsigned char* sU, const float* sGra
     }
 }
 
-// write_u_row for the N rows row0 + stride m (m < N) at once: each moment of
-// sGram is read once and feeds N independent chains.
-template <int N>
-__device__ __forceinline__ void write_u_rows(unsigned char* sU, const float* sGram, int row0,
-                                             int stride, const float3 (&pi)[N],
-                                             const float3 (&pj)[N]) {
-    float g[N][6], var[N];
-#pragma unroll
-    for (int m = 0; m < N; ++m) {
-        g[m][0] = pj[m].x - pi[m].x;
-        g[m][1] = pj[m].y - pi[m].y;
-        g[m][2] = pj[m].z - pi[m].z;
-        g[m][3] = pi[m].x;
-        g[m][4] = pi[m].y;
-        g[m][5] = pi[m].z;
-        var[m] = sGram[42];
-    }
-#pragma unroll
-    for (int d = 0; d < 6; ++d) {
-        float t[N];
-        const float a2 = 2.0f * sGram[36 + d];
-#pragma unroll
-        for (int m = 0; m < N; ++m) t[m] = a2;
-#pragma unroll
-        for (int e = 0; e < 6; ++e) {
-            const float ge = sGram[d * 6 + e];
-#pragma unroll
-            for (int m = 0; m < N; ++m) t[m] = fmaf(ge, g[m][e], t[m]);
-        }
-#pragma unroll
-        for (int m = 0; m < N; ++m) var[m] = fmaf(t[m], g[m][d], var[m]);
-    }
-#pragma unroll
-    for (int m = 0; m < N; ++m) {
-        const float rstd = rsqrtf(fmaxf(var[m], 0.0f) + 1e-5f);
-        const float u8[8] = {rstd * g[m][0], rstd * g[m][1], rstd * g[m][2], rstd * g[m][3],
-                             rstd * g[m][4], rstd * g[m][5], rstd,           1.0f};
-        float hi[8], lo[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-            hi[e] = f2s_round_tf32(u8[e]);
-            lo[e] = u8[e] - hi[e];
-        }
-        const int row = row0 + stride * m;
-#pragma unroll
-        for (int ch = 0; ch < 2; ++ch) {
-            const uint32_t off = interleaved_offset(row, ch);
-            *reinterpret_cast<float4*>(sU + off) =
-                make_float4(hi[4 * ch], hi[4 * ch + 1], hi[4 * ch + 2], hi[4 * ch + 3]);
-            *reinterpret_cast<float4*>(sU + kUBytes + off) =
-                make_float4(lo[4 * ch], lo[4 * ch + 1], lo[4 * ch + 2], lo[4 * ch + 3]);
-        }
-    }
+// The same for g = [x_j - x_i, x_i] of centre point pi and neighbour pj.
+__device__ __forceinline__ void write_u_row(unsigned char* sU, const float* sGram, int row,
+                                            const float4& pi, const float4& pj) {
+    const float g[6] = {pj.x - pi.x, pj.y - pi.y, pj.z - pi.z, pi.x, pi.y, pi.z};
+    write_u_row_g(sU, sGram, row, g);
 }
 
 }  // namespace edge

@@ -56,7 +56,8 @@ constexpr unsigned kFull = 0xffffffffu;
 struct UArgs {
     const float* content;
     int ldc;
-    const float* xyz4;
+    const float* xyz4;      // (B*M, 4) points, or null with geometry
+    const float* geometry;  // (B*M*K, 6) explicit g = [x_j - x_i, x_i], or null
     const int32_t* idx;
     int B, M, K, log2K, H, cout;
     int ppt;    // points per tile (128 / K)
@@ -206,21 +207,40 @@ edge_unified_kernel(const UArgs a) {
         // the centre point, stage 2 (one tile later) the neighbour point.
         const int cwarp = warp - kControlWarp0;
         const int row = cwarp * 32 + lane;
-        float3 gi, gj, ni;
+        // g = [x_j - x_i, x_i] of the row, from the points (model) or read as
+        // given (operator); g6 for the tile whose u rows are written next,
+        // ng6 / ni / nj the first stage of the tile after
+        float g6[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, ng6[6];
+        float3 ni;
         int nj = 0;
         bool gvalid = false, nvalid = false;
         auto fetch_indices = [&](int t) {
             const int p = t * a.ppt + (row >> a.log2K);
             nvalid = t < n_tiles && p < R;
             const int pc = nvalid ? p : 0;
-            const float4 v = *reinterpret_cast<const float4*>(a.xyz4 + (size_t)pc * 4);
-            ni = make_float3(v.x, v.y, v.z);
-            nj = (pc / a.M) * a.M + a.idx[(size_t)pc * K + (row & (K - 1))];
+            if (a.geometry) {
+                const float* gp = a.geometry + ((size_t)pc * K + (row & (K - 1))) * 6;
+#pragma unroll
+                for (int e = 0; e < 6; ++e) ng6[e] = gp[e];
+            } else {
+                const float4 v = *reinterpret_cast<const float4*>(a.xyz4 + (size_t)pc * 4);
+                ni = make_float3(v.x, v.y, v.z);
+                nj = (pc / a.M) * a.M + a.idx[(size_t)pc * K + (row & (K - 1))];
+            }
         };
         auto fetch_points = [&]() {
-            gi = ni;
-            const float4 v = *reinterpret_cast<const float4*>(a.xyz4 + (size_t)nj * 4);
-            gj = make_float3(v.x, v.y, v.z);
+            if (a.geometry) {
+#pragma unroll
+                for (int e = 0; e < 6; ++e) g6[e] = ng6[e];
+            } else {
+                const float4 v = *reinterpret_cast<const float4*>(a.xyz4 + (size_t)nj * 4);
+                g6[0] = v.x - ni.x;
+                g6[1] = v.y - ni.y;
+                g6[2] = v.z - ni.z;
+                g6[3] = ni.x;
+                g6[4] = ni.y;
+                g6[5] = ni.z;
+            }
             gvalid = nvalid;
         };
         auto load_geometry = [&](int t) {  // both stages at once (start-up only)
@@ -228,10 +248,10 @@ edge_unified_kernel(const UArgs a) {
             fetch_points();
         };
         auto write_u = [&]() {
-            const float3 zero = make_float3(0.f, 0.f, 0.f);
-            const float3 pi[1] = {gvalid ? gi : zero};
-            const float3 pj[1] = {gvalid ? gj : zero};
-            write_u_rows<1>(sU, sGram, row, 0, pi, pj);
+            float g[6];
+#pragma unroll
+            for (int e = 0; e < 6; ++e) g[e] = gvalid ? g6[e] : 0.0f;
+            write_u_row_g(sU, sGram, row, g);
         };
         // pre = LN(W_in g + b_in) of the tile whose u rows are in sU, into slot s
         auto issue_pre = [&](int s) {
@@ -591,13 +611,14 @@ edge_unified_kernel(const UArgs a) {
 }  // namespace
 
 // The split-bf16 neighbour stage on the three-role kernel when its shape allows:
-// H in {64, 128}, C_out in {64, 128, 192}, K in {8, 16, 32}, xyz4 geometry;
+// H in {64, 128}, C_out in {64, 128, 192}, K in {8, 16, 32}, geometry from the
+// points (xyz4) or given;
 // F2S_ERR_UNSUPPORTED otherwise (the caller then uses edge_tc_kernel).
 int edge_stage_unified(const EdgeArgs& e, cudaStream_t st) {
     if (e.B == 0 || e.M == 0) return F2S_OK;
     int log2K = 0;
     while ((1 << log2K) < e.K) ++log2K;
-    if (e.geometry != nullptr || e.xyz4 == nullptr || e.D != 6 || (e.H != 64 && e.H != 128) ||
+    if ((e.geometry == nullptr) == (e.xyz4 == nullptr) || e.D != 6 || (e.H != 64 && e.H != 128) ||
         (e.cout != 64 && e.cout != 128 && e.cout != 192) || (1 << log2K) != e.K || e.K < 8 ||
         e.K > 32 || ((uintptr_t)e.content & 15) != 0 || e.ldc % 4 != 0 ||
         ((uintptr_t)e.contrib_w & 15) != 0)
@@ -611,6 +632,7 @@ int edge_stage_unified(const EdgeArgs& e, cudaStream_t st) {
     a.content = e.content;
     a.ldc = e.ldc;
     a.xyz4 = e.xyz4;
+    a.geometry = e.geometry;
     a.idx = e.idx;
     a.B = e.B;
     a.M = e.M;

@@ -63,6 +63,11 @@ struct Dims {
     int enc_gemm_precision;
 };
 
+// tf32 tensor cores for the trunk (with fp16 or fp32 FFN rows)
+bool trunk_on_tensor_cores(int precision) {
+    return precision == F2S_PRECISION_TF32 || precision == F2S_PRECISION_TF32_WIDE;
+}
+
 int check_config(const f2s_model_config* cfg, Dims& d) {
     F2S_REQUIRE(cfg != nullptr, "model config is null");
     d.K = cfg->k_neighbors;
@@ -95,9 +100,9 @@ int check_config(const f2s_model_config* cfg, Dims& d) {
     }
     d.precision = cfg->precision;
     d.enc_precision = cfg->encoder_precision;
-    F2S_REQUIRE(d.precision == F2S_PRECISION_FP32 || d.precision == F2S_PRECISION_TF32,
-                "trunk precision %d is not F2S_PRECISION_FP32 or F2S_PRECISION_TF32",
-                d.precision);
+    F2S_REQUIRE(d.precision == F2S_PRECISION_FP32 || d.precision == F2S_PRECISION_TF32 ||
+                    d.precision == F2S_PRECISION_TF32_WIDE,
+                "trunk precision %d is not F2S_PRECISION_FP32, _TF32 or _TF32_WIDE", d.precision);
     F2S_REQUIRE(d.enc_precision == F2S_PRECISION_FP32 || d.enc_precision == F2S_PRECISION_TF32 ||
                     d.enc_precision == F2S_PRECISION_BF16X3,
                 "encoder precision %d is not F2S_PRECISION_FP32, _TF32 or _BF16X3",
@@ -225,7 +230,7 @@ Workspace carve(const Dims& d, int B, int M, char* base) {
     w.split_a = split ? (float*)take(R * 2 * d.max_gemm_in) : nullptr;
     w.split_w = split ? (float*)take((size_t)2 * d.max_gemm_w) : nullptr;
     w.feat0_lo = split ? (float*)take(R * d.sd[0]) : nullptr;
-    const bool tf32_trunk = d.precision == F2S_PRECISION_TF32;
+    const bool tf32_trunk = trunk_on_tensor_cores(d.precision);
     w.ffn_w16 = tf32_trunk ? (__half*)take(((size_t)(d.NB > 0 ? d.NB : 1) * 3 * d.C * d.Hf + 1) / 2)
                            : nullptr;
     w.bytes = off;
@@ -661,7 +666,7 @@ int forward(const Dims& d, const Layout& L, const float* P, const float* x_in, c
     F2S_TRY(ln_affine_leaky(w.x, C, P + L.proj_ln_w, P + L.proj_ln_b, R, C, false, st));
     F2S_TRY(trunk(d, L, P, B, M, w.x, w, st));
     // decoder (decoder.py:8-32)
-    const bool tf32_trunk = d.precision == F2S_PRECISION_TF32;
+    const bool tf32_trunk = trunk_on_tensor_cores(d.precision);
     const float* cur = w.x;
     int in_dim = C;
     float* bufs[2] = {w.dec0, w.dec1};
@@ -689,10 +694,11 @@ int trunk(const Dims& d, const Layout& L, const float* P, int B, int M, float* x
     const int C = d.C;
     const int ld_qkv = C + 2 * d.qk;
     // operands of tf32 contractions are rounded to the nearest tf32 where made
-    const bool tf32_trunk = d.precision == F2S_PRECISION_TF32;
+    const bool tf32_trunk = trunk_on_tensor_cores(d.precision);
     const int mstride = d.NB * 6 * C;
     // fp16 FFN operands (tf32 trunk; 16-byte fp16 rows, the register LN path)
-    const bool ffn_fp16 = tf32_trunk && d.Hf % 8 == 0 && C % 8 == 0 && C <= 256 &&
+    const bool ffn_fp16 = d.precision == F2S_PRECISION_TF32 && d.Hf % 8 == 0 && C % 8 == 0 &&
+                          C <= 256 &&
                           w.ffn_w16 != nullptr;
     const int64_t ffn_n = (int64_t)C * d.Hf;  // elements of one FFN weight matrix
     if (ffn_fp16) {
@@ -842,14 +848,18 @@ extern "C" int f2s_neighbor_reduce_workspace_bytes(int B, int N, int C, size_t* 
     return F2S_OK;
 }
 
-extern "C" int f2s_neighbor_reduce(const float* content, const float* geometry,
-                                   const int32_t* indices, const float* hpe_input_weight,
-                                   const float* hpe_input_bias, const float* hpe_output_weight,
-                                   const float* hpe_output_bias, const float* hpe_norm_weight,
-                                   const float* hpe_norm_bias, const float* message_norm_weight,
-                                   const float* message_norm_bias, int B, int N, int K, int D,
-                                   int H, int C, float* out, void* workspace,
-                                   size_t workspace_bytes, void* stream) {
+namespace {
+// The reduce_neighbor_messages operator on the fp32 CUDA-core kernel or (tc)
+// the split-bf16 tensor-core kernel: content (B, 2C, N) and the output
+// (B, C, N) channel-major as the reference has them, transposed point-major
+// through the workspace around the kernel.
+int neighbor_reduce_op(const float* content, const float* geometry, const int32_t* indices,
+                       const float* hpe_input_weight, const float* hpe_input_bias,
+                       const float* hpe_output_weight, const float* hpe_output_bias,
+                       const float* hpe_norm_weight, const float* hpe_norm_bias,
+                       const float* message_norm_weight, const float* message_norm_bias, int B,
+                       int N, int K, int D, int H, int C, float* out, void* workspace,
+                       size_t workspace_bytes, void* stream, bool tc) {
     F2S_REQUIRE(B >= 0 && N >= 0 && K >= 1 && D >= 1 && H >= 1 && C >= 1,
                 "neighbor_reduce: bad shape B=%d N=%d K=%d D=%d H=%d C=%d", B, N, K, D, H, C);
     if (B == 0 || N == 0) return F2S_OK;
@@ -864,7 +874,6 @@ extern "C" int f2s_neighbor_reduce(const float* content, const float* geometry,
     cudaStream_t st = as_stream(stream);
     float* content_pm = static_cast<float*>(workspace);       // (B*N, 2C)
     float* out_pm = content_pm + (size_t)B * N * 2 * C;         // (B*N, C)
-    F2S_TRY(transpose_batched(content, content_pm, B, 2 * C, N, st));
     EdgeArgs ea{};
     ea.content = content_pm;
     ea.ldc = 2 * C;
@@ -886,8 +895,48 @@ extern "C" int f2s_neighbor_reduce(const float* content, const float* geometry,
     ea.ln_b = message_norm_bias;
     ea.out = out_pm;
     ea.ldo = C;
-    F2S_TRY(edge_stage_f32(ea, st));
+    if (tc) {
+        // the shape check first, so an unsupported shape launches nothing
+        int log2K = 0;
+        while ((1 << log2K) < K) ++log2K;
+        F2S_LIMIT(D == 6 && (H == 64 || H == 128) && (C == 64 || C == 128 || C == 192) &&
+                      (1 << log2K) == K && K >= 8 && K <= 32 &&
+                      ((uintptr_t)hpe_output_weight & 15) == 0,
+                  "neighbor_reduce_tc: D=%d H=%d C=%d K=%d outside the tensor-core kernel "
+                  "(D 6, H 64 or 128, C 64, 128 or 192, K 8, 16 or 32)", D, H, C, K);
+    }
+    F2S_TRY(transpose_batched(content, content_pm, B, 2 * C, N, st));
+    F2S_TRY(tc ? edge_stage_unified(ea, st) : edge_stage_f32(ea, st));
     return transpose_batched(out_pm, out, B, N, C, st);
+}
+}  // namespace
+
+extern "C" int f2s_neighbor_reduce(const float* content, const float* geometry,
+                                   const int32_t* indices, const float* hpe_input_weight,
+                                   const float* hpe_input_bias, const float* hpe_output_weight,
+                                   const float* hpe_output_bias, const float* hpe_norm_weight,
+                                   const float* hpe_norm_bias, const float* message_norm_weight,
+                                   const float* message_norm_bias, int B, int N, int K, int D,
+                                   int H, int C, float* out, void* workspace,
+                                   size_t workspace_bytes, void* stream) {
+    return neighbor_reduce_op(content, geometry, indices, hpe_input_weight, hpe_input_bias,
+                              hpe_output_weight, hpe_output_bias, hpe_norm_weight, hpe_norm_bias,
+                              message_norm_weight, message_norm_bias, B, N, K, D, H, C, out,
+                              workspace, workspace_bytes, stream, false);
+}
+
+extern "C" int f2s_neighbor_reduce_tc(const float* content, const float* geometry,
+                                      const int32_t* indices, const float* hpe_input_weight,
+                                      const float* hpe_input_bias, const float* hpe_output_weight,
+                                      const float* hpe_output_bias, const float* hpe_norm_weight,
+                                      const float* hpe_norm_bias, const float* message_norm_weight,
+                                      const float* message_norm_bias, int B, int N, int K, int D,
+                                      int H, int C, float* out, void* workspace,
+                                      size_t workspace_bytes, void* stream) {
+    return neighbor_reduce_op(content, geometry, indices, hpe_input_weight, hpe_input_bias,
+                              hpe_output_weight, hpe_output_bias, hpe_norm_weight, hpe_norm_bias,
+                              message_norm_weight, message_norm_bias, B, N, K, D, H, C, out,
+                              workspace, workspace_bytes, stream, true);
 }
 
 extern "C" int f2s_offset_attention_workspace_bytes(int B, int N, int d, size_t* bytes) {
@@ -913,4 +962,36 @@ extern "C" int f2s_offset_attention(const float* query, const float* key, const 
     F2S_TRY(transpose_batched(key, key_pm, B, d, N, st));
     return attention_f32(query, key_pm, d, value, C, nullptr, 0, out, C, colstats, B, N, d, C,
                          false, st);
+}
+
+extern "C" int f2s_offset_attention_tc_workspace_bytes(int B, int N, int d, int C,
+                                                       size_t* bytes) {
+    F2S_REQUIRE(B >= 0 && N >= 0 && d >= 0 && C >= 0 && bytes, "bad workspace query");
+    const size_t key_floats = ((size_t)B * N * d + 63) & ~size_t(63);
+    *bytes = (key_floats + (size_t)attention_tc_workspace_floats(B, N, C)) * sizeof(float);
+    return F2S_OK;
+}
+
+extern "C" int f2s_offset_attention_tc(const float* query, const float* key, const float* value,
+                                       int B, int N, int d, int C, float* out, void* workspace,
+                                       size_t workspace_bytes, void* stream) {
+    F2S_REQUIRE(B >= 0 && N >= 0 && d >= 1 && C >= 1,
+                "offset_attention: bad shape B=%d N=%d d=%d C=%d", B, N, d, C);
+    if (B == 0 || N == 0) return F2S_OK;
+    F2S_REQUIRE(query && key && value && out && workspace, "offset_attention: null pointer");
+    F2S_LIMIT(d <= 64 && d % 4 == 0 && C % 64 == 0 && C <= 256 && ((uintptr_t)query & 15) == 0,
+              "offset_attention_tc: d=%d C=%d outside the tensor-core kernel (d a multiple of 4 "
+              "up to 64, C a multiple of 64 up to 256)", d, C);
+    size_t need = 0;
+    F2S_TRY(f2s_offset_attention_tc_workspace_bytes(B, N, d, C, &need));
+    if (workspace_bytes < need)
+        return fail(F2S_ERR_WORKSPACE, "offset_attention_tc needs %zu workspace bytes, got %zu",
+                    need, workspace_bytes);
+    cudaStream_t st = as_stream(stream);
+    float* key_pm = static_cast<float*>(workspace);  // (B*N, d)
+    float* attn_ws = key_pm + (((size_t)B * N * d + 63) & ~size_t(63));
+    F2S_TRY(transpose_batched(key, key_pm, B, d, N, st));
+    // the query rows and the transposed key rows share the pitch d
+    return attention_tc(query, key_pm, d, value, C, nullptr, 0, out, C, attn_ws, B, N, d, C,
+                        false, false, st);
 }

@@ -37,8 +37,11 @@ SIGNATURES: dict[str, list] = {
     "f2s_knn": [_p, _i, _i, _i, _i, _p, _p],
     "f2s_offset_attention_workspace_bytes": [_i, _i, _i, _p],
     "f2s_offset_attention": [_p, _p, _p, _i, _i, _i, _i, _p, _p, _sz, _p],
+    "f2s_offset_attention_tc_workspace_bytes": [_i, _i, _i, _i, _p],
+    "f2s_offset_attention_tc": [_p, _p, _p, _i, _i, _i, _i, _p, _p, _sz, _p],
     "f2s_neighbor_reduce_workspace_bytes": [_i, _i, _i, _p],
     "f2s_neighbor_reduce": [_p] * 11 + [_i] * 6 + [_p, _p, _sz, _p],
+    "f2s_neighbor_reduce_tc": [_p] * 11 + [_i] * 6 + [_p, _p, _sz, _p],
     "f2s_model_param_segments": [_p, _p, _p, _i, _p],
     "f2s_model_workspace_bytes": [_p, _i, _i, _p],
     "f2s_model_forward": [_p, _p, _p, _p, _i, _i, _p, _p, _sz, _p],
@@ -106,6 +109,16 @@ DEVICE_ERRORS = {
     1: "a tensor-core kernel gave up on a bounded wait",
     2: "an fp16 intermediate of the tf32 trunk (the FFN hidden rows) was out of the fp16 range",
 }
+
+
+F2S_FP16_RANGE = 2  # device error word: an fp16 FFN row of the tf32 trunk overflowed
+
+
+def read_device_error(stream=None, reset: bool = True) -> int:
+    """The library's device error word (0, 1 or 2); synchronises `stream`."""
+    value = ctypes.c_int(0)
+    check(lib().f2s_device_error(ctypes.byref(value), 1 if reset else 0, stream_handle(stream)))
+    return value.value
 
 
 def check_device_error(stream=None) -> None:

@@ -233,18 +233,34 @@ def denoise_device(model, points: torch.Tensor, patch_size, seed_k, num_steps, r
         seeds = torch.from_numpy(seed_idx.astype(np.int32)).to(points.device)
     plan = build_plan(points, patch_size, seeds, patch_agg_beta)
     alphas = alpha_schedule(num_steps, alpha_clean_power, alpha_noisy_power)
-    if process_group is not None and torch.distributed.get_world_size(process_group) > 1:
-        runner = _ShardedRunner(model, plan, workspace_budget, process_group)
-    else:
-        runner = _Runner(model, plan, workspace_budget)
-    current = points.clone()
-    spare = torch.empty_like(current)
-    for step in range(num_steps - 1, -1, -1):
-        alpha_current = float(alphas[step])
-        alpha_previous = float(alphas[step - 1]) if step > 0 else 0.0
-        runner.step(current, spare, alpha_current, alpha_current - alpha_previous)
-        current, spare = spare, current
-    _lib.check_device_error()
+    sharded = process_group is not None and torch.distributed.get_world_size(process_group) > 1
+
+    def integrate(net):
+        runner = (_ShardedRunner(net, plan, workspace_budget, process_group) if sharded
+                  else _Runner(net, plan, workspace_budget))
+        current = points.clone()
+        spare = torch.empty_like(current)
+        for step in range(num_steps - 1, -1, -1):
+            alpha_current = float(alphas[step])
+            alpha_previous = float(alphas[step - 1]) if step > 0 else 0.0
+            runner.step(current, spare, alpha_current, alpha_current - alpha_previous)
+            current, spare = spare, current
+        return current
+
+    current = integrate(model)
+    status = _lib.read_device_error()
+    if sharded:  # every rank takes the same path
+        flag = torch.tensor([status], dtype=torch.int32, device=points.device)
+        torch.distributed.all_reduce(flag, op=torch.distributed.ReduceOp.MAX, group=process_group)
+        status = int(flag.item())
+    if status == _lib.F2S_FP16_RANGE and hasattr(model, "wide_ffn"):
+        # an fp16 FFN row of the tf32 trunk overflowed somewhere: the whole
+        # denoise again with fp32 FFN rows (still on the device)
+        current = integrate(model.wide_ffn())
+        status = _lib.read_device_error()
+    if status:
+        raise _lib.Flow2SurfError(_lib.F2S_ERR_CUDA, "device error %d: %s" % (
+            status, _lib.DEVICE_ERRORS.get(status, "unknown")))
     return current
 
 

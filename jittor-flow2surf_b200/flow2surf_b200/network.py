@@ -39,10 +39,13 @@ class ModelConfig(ctypes.Structure):
     ]
 
 
-PRECISIONS = {"fp32": 0, "tf32": 1, "bf16x3": 3}
+PRECISIONS = {"fp32": 0, "tf32": 1, "bf16x3": 3, "tf32_wide": 4}
 """Arithmetic of the dense contractions: fp32 CUDA-core kernels, tcgen05
 tensor cores reading the fp32 operands as tf32, or (encoder only) tensor cores
-on operands split into two bf16 halves (hi*hi + hi*lo + lo*hi)."""
+on operands split into two bf16 halves (hi*hi + hi*lo + lo*hi). "tf32" keeps
+the trunk's FFN rows in fp16 (tf32's mantissa, fp16's range); "tf32_wide"
+(trunk only) keeps them in fp32 and is what a tf32 forward is rerun in when
+those fp16 rows overflow."""
 
 
 def model_config(cfg: dict, precision: str = "fp32",
@@ -253,7 +256,7 @@ class Flow2SurfNet:
     def device_blob(self, device) -> torch.Tensor:
         if self._blob is None or self._blob.device != torch.device(device):
             host = pack_parameters(self.cfg, self._params,
-                                   trunk_tf32=self.precision == "tf32",
+                                   trunk_tf32=self.precision in ("tf32", "tf32_wide"),
                                    encoder_tf32=self.encoder_precision == "tf32")
             self._blob = torch.from_numpy(host).to(device)
         return self._blob
@@ -273,12 +276,12 @@ class Flow2SurfNet:
         return self._workspace
 
     def forward_into(self, x_alpha: torch.Tensor, alpha: torch.Tensor, out: torch.Tensor,
-                     workspace: torch.Tensor | None = None) -> torch.Tensor:
+                     workspace: torch.Tensor | None = None, config=None) -> torch.Tensor:
         batch, _, points = x_alpha.shape
         ws = workspace if workspace is not None else self._workspace_for(batch, points,
                                                                          x_alpha.device)
         blob = self.device_blob(x_alpha.device)
-        _lib.call("f2s_model_forward", ctypes.byref(self._config), _lib.ptr(blob),
+        _lib.call("f2s_model_forward", ctypes.byref(config or self._config), _lib.ptr(blob),
                   _lib.ptr(x_alpha), _lib.ptr(alpha), batch, points, _lib.ptr(out),
                   _lib.ptr(ws), ws.numel(), _lib.stream_handle())
         return out
@@ -304,6 +307,13 @@ class Flow2SurfNet:
                   _lib.ptr(alpha), batch, points, _lib.ptr(ws), ws.numel(), _lib.stream_handle())
         return x
 
+    def wide_ffn(self):
+        """This model with the trunk's FFN rows kept in fp32 (precision
+        "tf32_wide", the same packed parameters): where a "tf32" forward's
+        fp16 FFN rows overflow (device error word 2), this one has no range
+        limit."""
+        return _WideFfn(self) if self.precision == "tf32" else self
+
     def __call__(self, x_alpha: torch.Tensor, alpha: torch.Tensor) -> torch.Tensor:
         if x_alpha.dim() != 3 or x_alpha.shape[1] != 3:
             raise ValueError(f"x_alpha must be (B, 3, M), got {tuple(x_alpha.shape)}")
@@ -317,9 +327,33 @@ class Flow2SurfNet:
         out = torch.empty((batch, points, 3), dtype=torch.float32, device=x_alpha.device)
         if out.numel() == 0:
             return out
-        return self.forward_into(x_alpha, alpha, out)
+        self.forward_into(x_alpha, alpha, out)
+        if self.precision == "tf32":
+            # fp16 FFN rows out of range: the same forward with fp32 rows
+            if _lib.read_device_error() == _lib.F2S_FP16_RANGE:
+                self.wide_ffn().forward_into(x_alpha, alpha, out)
+                _lib.check_device_error()
+        return out
 
     execute = __call__
+
+
+class _WideFfn:
+    """A "tf32" Flow2SurfNet run as "tf32_wide" (fp32 FFN rows): same
+    parameters, packing and workspace layout, another model config."""
+
+    def __init__(self, model: Flow2SurfNet):
+        self.model = model
+        self.config = model_config(model.cfg, "tf32_wide", model.encoder_precision)
+
+    def workspace_bytes(self, batch: int, points: int) -> int:
+        size = ctypes.c_size_t()
+        _lib.check(_lib.lib().f2s_model_workspace_bytes(ctypes.byref(self.config), batch, points,
+                                                        ctypes.byref(size)))
+        return size.value
+
+    def forward_into(self, x_alpha, alpha, out, workspace=None):
+        return self.model.forward_into(x_alpha, alpha, out, workspace, config=self.config)
 
 
 def build_model(cfg: dict, precision: str | None = None,

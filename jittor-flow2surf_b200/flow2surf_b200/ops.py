@@ -59,13 +59,18 @@ def _workspace(query: str, *dims) -> torch.Tensor:
 
 
 def offset_attention_aggregate(query: torch.Tensor, key: torch.Tensor,
-                               value: torch.Tensor) -> torch.Tensor:
+                               value: torch.Tensor, *, precision: str = "fp32") -> torch.Tensor:
     """Aggregate values using normalized offset-attention weights.
 
     query (B, N, d), key (B, d, N), value (B, N, C) -> (B, N, C): softmax of
     query . key over the query axis, each row divided by its sum over keys
     plus 1e-9, times value (flow2surf/models/ops/attention.py:15-19,84-106).
+    `precision` "fp32" (CUDA cores, the reference's arithmetic) or "tensor"
+    (tcgen05: split-bf16 scores, fp16 P V; d a multiple of 4 up to 64, C a
+    multiple of 64 up to 256; ~1e-3 relative).
     """
+    if precision not in ("fp32", "tensor"):
+        raise ValueError(f"precision must be 'fp32' or 'tensor', got {precision!r}")
     if query.dim() != 3 or key.dim() != 3 or value.dim() != 3:
         raise ValueError("query, key, and value must be rank-3 tensors")
     if (query.shape[0] != key.shape[0] or query.shape[0] != value.shape[0]
@@ -80,16 +85,21 @@ def offset_attention_aggregate(query: torch.Tensor, key: torch.Tensor,
     if out.numel() == 0:
         return out
     query, key, value = _f32(query), _f32(key), _f32(value)
-    ws = _workspace("f2s_offset_attention_workspace_bytes", batch, points, width)
-    _lib.call("f2s_offset_attention", _lib.ptr(query), _lib.ptr(key), _lib.ptr(value), batch,
-              points, width, channels, _lib.ptr(out), _lib.ptr(ws), ws.numel(),
-              _lib.stream_handle())
+    if precision == "tensor":
+        ws = _workspace("f2s_offset_attention_tc_workspace_bytes", batch, points, width, channels)
+        entry = "f2s_offset_attention_tc"
+    else:
+        ws = _workspace("f2s_offset_attention_workspace_bytes", batch, points, width)
+        entry = "f2s_offset_attention"
+    _lib.call(entry, _lib.ptr(query), _lib.ptr(key), _lib.ptr(value), batch, points, width,
+              channels, _lib.ptr(out), _lib.ptr(ws), ws.numel(), _lib.stream_handle())
     return out
 
 
 def reduce_neighbor_messages(content, geometry, indices, hpe_input_weight, hpe_input_bias,
                              hpe_output_weight, hpe_output_bias, hpe_norm_weight, hpe_norm_bias,
-                             message_norm_weight, message_norm_bias) -> torch.Tensor:
+                             message_norm_weight, message_norm_bias, *,
+                             precision: str = "fp32") -> torch.Tensor:
     """Encode relative geometry and max-reduce normalized neighbor messages.
 
     content  : (B, 2C, N), projected neighbor and center terms
@@ -99,7 +109,12 @@ def reduce_neighbor_messages(content, geometry, indices, hpe_input_weight, hpe_i
 
     flow2surf/models/ops/neighbor_reduce.py:244-337, with the HPE hidden
     layer, its output projection and the reduce fused in one kernel.
+    `precision` "fp32" (CUDA cores) or "bf16x3" (tcgen05: the output
+    projection as split-bf16 MMAs, close to fp32; D 6, H 64 or 128, C 64, 128
+    or 192, K 8, 16 or 32).
     """
+    if precision not in ("fp32", "bf16x3"):
+        raise ValueError(f"precision must be 'fp32' or 'bf16x3', got {precision!r}")
     channels, hidden_channels = hpe_output_weight.shape
     input_hidden_channels, input_channels = hpe_input_weight.shape
     if content.shape[1] != 2 * channels:
@@ -130,7 +145,8 @@ def reduce_neighbor_messages(content, geometry, indices, hpe_input_weight, hpe_i
     ws = _workspace("f2s_neighbor_reduce_workspace_bytes", batch, points, channels)
     args = [_lib.ptr(floats[0]), _lib.ptr(floats[1]), _lib.ptr(indices)]
     args += [_lib.ptr(t) for t in floats[2:]]
-    _lib.call("f2s_neighbor_reduce", *args, batch, points, neighbors, input_channels,
+    entry = "f2s_neighbor_reduce_tc" if precision == "bf16x3" else "f2s_neighbor_reduce"
+    _lib.call(entry, *args, batch, points, neighbors, input_channels,
               hidden_channels, channels, _lib.ptr(out), _lib.ptr(ws), ws.numel(),
               _lib.stream_handle())
     return out

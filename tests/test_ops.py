@@ -113,3 +113,79 @@ def test_offset_attention_shape_errors(cuda):
         offset_attention_aggregate(t(2, 4), t(2, 4, 4), t(2, 4, 4))
     with pytest.raises(ValueError, match="Incompatible"):
         offset_attention_aggregate(t(2, 4, 3), t(2, 3, 5), t(2, 4, 6))
+
+
+def run_reduce_tc(feats, geometry, idx, w):
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()  # noqa: E731
+    wi, bi, wo, bo, gh, bh, gm, bm = w
+    out = reduce_neighbor_messages(t(feats), t(geometry), t(idx), t(wi), t(bi), t(wo), t(bo),
+                                   t(gh), t(bh), t(gm), t(bm), precision="bf16x3")
+    return out.cpu().numpy()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("K,C,H", [(8, 64, 64), (16, 128, 64), (32, 192, 128), (32, 128, 64)])
+def test_reduce_neighbor_messages_tensor_cores(cuda, K, C, H):
+    """The split-bf16 tensor-core kernel behind the operator (max-abs 1e-4:
+    the contraction keeps ~2^-17 relative, the rest is fp32)."""
+    feats, geometry, idx, w = make_stage_inputs(4, 300, K, C, H, seed=K + C + 1)
+    got = run_reduce_tc(feats, geometry, idx, w)
+    want = neighbor_reduce_oracle(feats, geometry.astype(np.float64), idx, *w)
+    np.testing.assert_allclose(got, want, rtol=0, atol=1e-4)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("K", [16, 32])
+def test_reduce_neighbor_messages_tensor_cores_microbench(cuda, K):
+    """The KNN + edge micro-benchmark batch: 256 patches x 1024 points, stage
+    (in, out, H) = (64, 64, 64); every patch on the GPU, a sample of 8 patches
+    (independent of the others) against the float64 oracle."""
+    feats, geometry, idx, w = make_stage_inputs(256, 1024, K, 64, 64, seed=2)
+    got = run_reduce_tc(feats, geometry, idx, w)
+    pick = np.array([0, 37, 100, 127, 128, 170, 211, 255])
+    want = neighbor_reduce_oracle(feats[pick], geometry[pick].astype(np.float64), idx[pick], *w)
+    np.testing.assert_allclose(got[pick], want, rtol=0, atol=1e-4)
+    assert np.isfinite(got).all()
+
+
+@pytest.mark.gpu
+def test_reduce_neighbor_messages_tensor_core_shape_limits(cuda):
+    feats, geometry, idx, w = make_stage_inputs(1, 64, 7, 40, 24, seed=3)
+    with pytest.raises(ValueError, match="outside the tensor-core kernel"):
+        run_reduce_tc(feats, geometry, idx, w)
+
+
+def attention_inputs(B, N, d, C, seed):
+    rng = np.random.default_rng(seed)
+    q = _channel_layer_norm(rng.normal(size=(B, N, d))).astype(np.float32)
+    k = np.transpose(_channel_layer_norm(rng.normal(size=(B, N, d))), (0, 2, 1)).astype(np.float32)
+    v = rng.normal(size=(B, N, C)).astype(np.float32)
+    return q, np.ascontiguousarray(k), v
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("B,N,d,C,sample", [(2, 1024, 48, 192, 2), (3, 100, 48, 192, 3),
+                                            (2, 257, 16, 64, 2), (512, 1024, 48, 192, 4)])
+def test_offset_attention_tensor_cores(cuda, B, N, d, C, sample):
+    """tcgen05 path of the operator (split-bf16 scores, fp16 P V): normwise
+    relative 2e-3 and max-abs 2e-3 of the largest output; the last case is the
+    trunk micro-benchmark's attention (512 patches x 1024 points, d 48, C 192),
+    a sample of its patches against the float64 oracle."""
+    q, k, v = attention_inputs(B, N, d, C, seed=N + d)
+    t = lambda a: torch.from_numpy(a).cuda()  # noqa: E731
+    got = offset_attention_aggregate(t(q), t(k), t(v), precision="tensor").cpu().numpy()
+    pick = np.linspace(0, B - 1, sample).astype(int)
+    want = OracleNet.offset_attention(q[pick].astype(np.float64),
+                                      np.transpose(k[pick], (0, 2, 1)).astype(np.float64),
+                                      v[pick].astype(np.float64))
+    err = got[pick] - want
+    assert np.linalg.norm(err) / np.linalg.norm(want) < 2e-3
+    assert np.abs(err).max() < 2e-3 * np.abs(want).max()
+
+
+@pytest.mark.gpu
+def test_offset_attention_tensor_core_shape_limits(cuda):
+    q, k, v = attention_inputs(1, 64, 8, 40, seed=1)
+    t = lambda a: torch.from_numpy(a).cuda()  # noqa: E731
+    with pytest.raises(ValueError, match="outside the tensor-core kernel"):
+        offset_attention_aggregate(t(q), t(k), t(v), precision="tensor")
