@@ -67,6 +67,9 @@ def parse_args():
                    help="all ranks denoise one cloud of --points, its patches split across "
                         "the GPUs with one NCCL all-reduce of the vote sums per Euler step "
                         "(strong scaling) instead of one cloud per GPU")
+    p.add_argument("--profile-chamfer", action="store_true",
+                   help="instead of the benchmark: two Chamfer evaluations of a denoised-size "
+                        "cloud against a 100,000-point clean sample and exit (ncu case)")
     p.add_argument("--profile-forward", type=int, default=0, metavar="B",
                    help="instead of the benchmark: two model forwards on B synthetic "
                         "1000-point patches and exit (a small case for ncu captures)")
@@ -93,6 +96,50 @@ def profile_forward(args) -> None:
         v = model(x, alpha)
     torch.cuda.synchronize()
     print(json.dumps({"profile_forward": B, "checksum": float(v.abs().sum())}), flush=True)
+
+
+CHAMFER_REFERENCE_POINTS = 100_000
+SIMT_LANE_OPS = 148 * 128 * 1.965e9   # fp32 lanes x boost clock: lane-ops/s of the whole GPU
+CHAMFER_OPS_PER_PAIR = 9              # 3 sub, mul, 2 fma, compare, 2 selects
+
+
+def chamfer_leg(points, reference, repeats: int = 3) -> dict:
+    """Chamfer of `points` (N, 3) against `reference` (R, 3) on the device
+    (flow2surf/evaluation.py:24-28 with the nearest-distance kernel), timed
+    with CUDA events, and its rate against the fp32 SIMT peak."""
+    import torch
+
+    from flow2surf_b200.ops import chamfer_distances
+
+    a, b = points[None].contiguous(), reference[None].contiguous()
+    value = chamfer_distances(a, b)  # warm-up
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    start.record()
+    for _ in range(repeats):
+        value = chamfer_distances(a, b)
+    stop.record()
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(stop) / repeats
+    pairs = 2.0 * a.shape[1] * b.shape[1]
+    rate = pairs / (ms * 1e-3)
+    return {"value": float(value.item()), "ms": ms, "points": int(a.shape[1]),
+            "reference_points": int(b.shape[1]), "pairs_per_s": rate,
+            "roofline": {"bound": "fp32 SIMT", "achieved": rate * CHAMFER_OPS_PER_PAIR / 1e12,
+                         "peak": SIMT_LANE_OPS / 1e12, "unit": "T lane-ops/s",
+                         "frac": rate * CHAMFER_OPS_PER_PAIR / SIMT_LANE_OPS}}
+
+
+def profile_chamfer(args) -> None:
+    """Two Chamfer evaluations (denoise-size cloud vs 100k clean sample)."""
+    import torch
+
+    from flow2surf_b200.synthetic import mesh_cloud
+
+    noisy, _, ref = mesh_cloud(args.points, seed=4, sigma_fraction=0.015, noise_type="laplace",
+                               clean_points=CHAMFER_REFERENCE_POINTS)
+    line = chamfer_leg(torch.from_numpy(noisy).cuda(), torch.from_numpy(ref).cuda(), repeats=1)
+    print(json.dumps({"profile_chamfer": line["ms"]}), flush=True)
 
 
 def workload_config(args, world: int) -> dict:
@@ -455,6 +502,12 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
         dist.all_reduce(e2e, op=dist.ReduceOp.MAX)
     if not np.all(np.isfinite(host_out)) or not torch.isfinite(out).all():
         raise RuntimeError("non-finite denoised output")
+    # quality leg: Chamfer of the denoised cloud against a 100k clean sample of
+    # its surface (the multi-GPU configuration's loss), on the device
+    from flow2surf_b200.synthetic import mesh_cloud
+    reference = mesh_cloud(args.points, seed=4 + cloud_seed, sigma_fraction=0.015,
+                           noise_type="laplace", clean_points=CHAMFER_REFERENCE_POINTS)[2]
+    chamfer = chamfer_leg(out, torch.from_numpy(reference).to(dev))
     if rank != 0:
         return
 
@@ -480,6 +533,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
         "roofline": roofline(kernels, forward_points, dims),
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(cloud.nbytes),
                 "d2h_bytes_per_step": int(host_out.nbytes)},
+        "chamfer": chamfer,
         "gpu_launches": rec.launches * steps // traced_steps,
         "clocks": clocks.summary(),
         "kernel_breakdown": (f"separate traced pass of {traced_steps} steps (CUDA events "
@@ -503,6 +557,9 @@ def main():
         return
     if args.profile_forward > 0:
         profile_forward(args)
+        return
+    if args.profile_chamfer:
+        profile_chamfer(args)
         return
     if world > 1:
         import torch
