@@ -378,6 +378,25 @@ int f2s_chamfer(const float* pred, const float* target, int B, int M, int N, dou
                 void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * Point-to-surface distance: for each point, the squared distance to the
+ * closest point of a triangle mesh and that triangle's index (the smaller
+ * index on ties), in float32. Replaces point_cloud_utils'
+ * closest_points_on_mesh as flow2surf/evaluation.py:31-34 (point_to_surface =
+ * the mean of these squared distances) uses it; the closest point on each
+ * triangle by the region tests of Ericson, Real-Time Collision Detection
+ * (2005), sec. 5.1.5.
+ *   points (M, 3) float32, vertices (V, 3) float32, faces (F, 3) int32 with
+ *   every index in [0, V) (the caller checks; out-of-range indices are clamped
+ *   so nothing is read out of bounds) -> sq_distance (M,) float32,
+ *   face_index (M,) int32.
+ *   workspace: f2s_point_to_mesh_workspace_bytes(M, F) bytes.
+ */
+int f2s_point_to_mesh_workspace_bytes(int M, int F, size_t* bytes);
+int f2s_point_to_mesh(const float* points, int M, const float* vertices, int V,
+                      const int32_t* faces, int F, float* sq_distance, int32_t* face_index,
+                      void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * f2s_chamfer for callers that cannot allocate device memory. No counterpart
  * in the reference: it exists for code that must not call cudaMalloc -- an
  * out-of-memory handler, a host that forbids device allocation once running,

@@ -146,6 +146,145 @@ int one_way(const float* query, const float* ref, int B, int M, int N, unsigned 
     return check_launch("nearest_kernel");
 }
 
+// ---------------------------------------------------------------------------
+// Point-to-triangle-mesh distance (flow2surf/evaluation.py:31-34, which takes
+// it from point_cloud_utils' closest_points_on_mesh): for each point the
+// squared distance to the closest point of the closest triangle. The closest
+// point on a triangle follows the region classification of Ericson,
+// Real-Time Collision Detection (2005), sec. 5.1.5: the point's dot products
+// with the two edges from a vertex decide whether the closest feature is a
+// vertex, an edge or the face, in a fixed order; here written without
+// branches (every region's barycentric pair is formed and the first region
+// that holds is selected), with the per-triangle dot products precomputed.
+// ---------------------------------------------------------------------------
+constexpr int kTriTile = 512;
+constexpr int kTriFloats = 12;  // a (3), ab (3), ac (3), |ab|^2, |ac|^2, ab.ac
+
+__global__ void triangle_prep_kernel(const float* __restrict__ vertices, int V,
+                                     const int32_t* __restrict__ faces, int F,
+                                     float* __restrict__ tri) {
+    for (int f = blockIdx.x * blockDim.x + threadIdx.x; f < F; f += gridDim.x * blockDim.x) {
+        int i[3];
+#pragma unroll
+        for (int e = 0; e < 3; ++e) {
+            const int v = faces[3 * (size_t)f + e];
+            i[e] = v < 0 ? 0 : (v >= V ? V - 1 : v);  // the host checks the range first
+        }
+        const float* a = vertices + 3 * (size_t)i[0];
+        const float* b = vertices + 3 * (size_t)i[1];
+        const float* c = vertices + 3 * (size_t)i[2];
+        const float ab[3] = {b[0] - a[0], b[1] - a[1], b[2] - a[2]};
+        const float ac[3] = {c[0] - a[0], c[1] - a[1], c[2] - a[2]};
+        float* o = tri + (size_t)f * kTriFloats;
+        o[0] = a[0];
+        o[1] = a[1];
+        o[2] = a[2];
+        o[3] = ab[0];
+        o[4] = ab[1];
+        o[5] = ab[2];
+        o[6] = ac[0];
+        o[7] = ac[1];
+        o[8] = ac[2];
+        o[9] = ab[0] * ab[0] + ab[1] * ab[1] + ab[2] * ab[2];
+        o[10] = ac[0] * ac[0] + ac[1] * ac[1] + ac[2] * ac[2];
+        o[11] = ab[0] * ac[0] + ab[1] * ac[1] + ab[2] * ac[2];
+    }
+}
+
+// Squared distance from p to the triangle (a, a + ab, a + ac).
+__device__ __forceinline__ float point_triangle_sq(float px, float py, float pz, const float* t) {
+    const float apx = px - t[0], apy = py - t[1], apz = pz - t[2];
+    const float d1 = t[3] * apx + t[4] * apy + t[5] * apz;  // ab . ap
+    const float d2 = t[6] * apx + t[7] * apy + t[8] * apz;  // ac . ap
+    const float d3 = d1 - t[9];                             // ab . bp
+    const float d4 = d2 - t[11];                            // ac . bp
+    const float d5 = d1 - t[11];                            // ab . cp
+    const float d6 = d2 - t[10];                            // ac . cp
+    const float vc = d1 * d4 - d3 * d2;
+    const float vb = d5 * d2 - d1 * d6;
+    const float va = d3 * d6 - d5 * d4;
+    // face region by default, then the edge and vertex regions in reverse
+    // order of precedence, so the first region that holds wins
+    // (__fdividef: ~2 ulp, a displacement of ~1e-7 of an edge along it)
+    const float inv = __fdividef(1.0f, va + vb + vc);
+    float v = vb * inv, w = vc * inv;
+    const float e43 = d4 - d3, e56 = d5 - d6;
+    if (va <= 0.0f && e43 >= 0.0f && e56 >= 0.0f) {  // edge bc
+        w = __fdividef(e43, e43 + e56);
+        v = 1.0f - w;
+    }
+    if (vb <= 0.0f && d2 >= 0.0f && d6 <= 0.0f) {  // edge ac
+        v = 0.0f;
+        w = __fdividef(d2, d2 - d6);
+    }
+    if (d6 >= 0.0f && d5 <= d6) {  // vertex c
+        v = 0.0f;
+        w = 1.0f;
+    }
+    if (vc <= 0.0f && d1 >= 0.0f && d3 <= 0.0f) {  // edge ab
+        v = __fdividef(d1, d1 - d3);
+        w = 0.0f;
+    }
+    if (d3 >= 0.0f && d4 <= d3) {  // vertex b
+        v = 1.0f;
+        w = 0.0f;
+    }
+    if (d1 <= 0.0f && d2 <= 0.0f) {  // vertex a
+        v = 0.0f;
+        w = 0.0f;
+    }
+    const float dx = apx - (v * t[3] + w * t[6]);
+    const float dy = apy - (v * t[4] + w * t[7]);
+    const float dz = apz - (v * t[5] + w * t[8]);
+    return dx * dx + dy * dy + dz * dz;
+}
+
+// keys[i] = min over triangles f of dist_key(d^2(point_i, f), f); the
+// triangles split across blockIdx.y chunks and folded with atomicMin.
+__global__ void __launch_bounds__(kThreads)
+point_mesh_kernel(const float* __restrict__ points, int M, const float* __restrict__ tri, int F,
+                  int tri_chunk, unsigned long long* __restrict__ keys) {
+    __shared__ float tile[kTriTile * kTriFloats];
+    const int q0 = blockIdx.x * kQueriesPerCta;
+    const int f_lo = blockIdx.y * tri_chunk;
+    const int f_hi = min(F, f_lo + tri_chunk);
+    float px[kQpt], py[kQpt], pz[kQpt], best[kQpt];
+    int bf[kQpt];
+#pragma unroll
+    for (int t = 0; t < kQpt; ++t) {
+        const int i = q0 + threadIdx.x + kThreads * t;
+        const bool in = i < M;
+        px[t] = in ? points[3 * (size_t)i] : 0.0f;
+        py[t] = in ? points[3 * (size_t)i + 1] : 0.0f;
+        pz[t] = in ? points[3 * (size_t)i + 2] : 0.0f;
+        best[t] = INFINITY;
+        bf[t] = -1;
+    }
+    for (int f0 = f_lo; f0 < f_hi; f0 += kTriTile) {
+        const int count = min(kTriTile, f_hi - f0);
+        __syncthreads();
+        for (int j = threadIdx.x; j < count * kTriFloats; j += kThreads)
+            tile[j] = tri[(size_t)f0 * kTriFloats + j];
+        __syncthreads();
+        for (int f = 0; f < count; ++f) {
+            const float* tr = tile + f * kTriFloats;
+#pragma unroll
+            for (int t = 0; t < kQpt; ++t) {
+                const float d = point_triangle_sq(px[t], py[t], pz[t], tr);
+                if (d < best[t]) {
+                    best[t] = d;
+                    bf[t] = f0 + f;
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < kQpt; ++t) {
+        const int i = q0 + threadIdx.x + kThreads * t;
+        if (i < M && bf[t] >= 0) atomicMin(&keys[i], dist_key(best[t], bf[t]));
+    }
+}
+
 int check_sets(const float* first, const float* second, int B, int M, int N) {
     F2S_REQUIRE(B >= 0, "batch must be >= 0");
     F2S_REQUIRE(M >= 1 && N >= 1, "Point sets must be nonempty");
@@ -278,4 +417,47 @@ extern "C" int f2s_chamfer_static(const float* pred, const float* target, int B,
     F2S_TRY(one_way(target, pred, B, N, M, k2, st));
     chamfer_reduce_kernel<<<B, 1024, 0, st>>>(k1, M, k2, N, chamfer);
     return check_launch("chamfer_reduce_kernel");
+}
+
+extern "C" int f2s_point_to_mesh_workspace_bytes(int M, int F, size_t* bytes) {
+    F2S_REQUIRE(M >= 0 && F >= 0 && bytes, "bad workspace query");
+    *bytes = (((size_t)F * kTriFloats * sizeof(float) + 255) & ~size_t(255)) +
+             (size_t)M * sizeof(unsigned long long);
+    return F2S_OK;
+}
+
+extern "C" int f2s_point_to_mesh(const float* points, int M, const float* vertices, int V,
+                                 const int32_t* faces, int F, float* sq_distance,
+                                 int32_t* face_index, void* workspace, size_t workspace_bytes,
+                                 void* stream) {
+    F2S_REQUIRE(M >= 0 && V >= 0 && F >= 0, "point_to_mesh: bad sizes M=%d V=%d F=%d", M, V, F);
+    if (M == 0) return F2S_OK;
+    F2S_REQUIRE(V >= 1 && F >= 1, "point_to_mesh: the mesh is empty (V=%d, F=%d)", V, F);
+    F2S_REQUIRE(points && vertices && faces && sq_distance && face_index && workspace,
+                "point_to_mesh: null pointer");
+    size_t need = 0;
+    F2S_TRY(f2s_point_to_mesh_workspace_bytes(M, F, &need));
+    if (workspace_bytes < need)
+        return fail(F2S_ERR_WORKSPACE, "point_to_mesh needs %zu workspace bytes, got %zu", need,
+                    workspace_bytes);
+    cudaStream_t st = as_stream(stream);
+    TraceScope trace(kTagNearest, st);
+    float* tri = static_cast<float*>(workspace);
+    unsigned long long* keys = reinterpret_cast<unsigned long long*>(
+        static_cast<char*>(workspace) + (((size_t)F * kTriFloats * sizeof(float) + 255) & ~size_t(255)));
+    triangle_prep_kernel<<<grid_1d(F), 256, 0, st>>>(vertices, V, faces, F, tri);
+    F2S_TRY(check_launch("triangle_prep_kernel"));
+    init_keys_kernel<<<grid_1d(M), 256, 0, st>>>(keys, M, F);
+    F2S_TRY(check_launch("init_keys_kernel"));
+    const int qblocks = ceil_div(M, kQueriesPerCta);
+    int splits = (4 * sm_count() + qblocks - 1) / qblocks;
+    const int max_splits = ceil_div(F, kTriTile);
+    splits = splits < 1 ? 1 : (splits > max_splits ? max_splits : splits);
+    const int chunk = ceil_div(ceil_div(F, splits), kTriTile) * kTriTile;
+    dim3 grid(qblocks, ceil_div(F, chunk));
+    F2S_LIMIT(grid.y <= 65535, "point_to_mesh: grid too large");
+    point_mesh_kernel<<<grid, kThreads, 0, st>>>(points, M, tri, F, chunk, keys);
+    F2S_TRY(check_launch("point_mesh_kernel"));
+    unpack_kernel<<<grid_1d(M), 256, 0, st>>>(keys, M, sq_distance, face_index);
+    return check_launch("unpack_kernel");
 }

@@ -59,6 +59,8 @@ SIGNATURES: dict[str, list] = {
     "f2s_nearest": [_p, _p, _i, _i, _i, _p, _p, _p, _p, _p, _sz, _p],
     "f2s_chamfer": [_p, _p, _i, _i, _i, _p, _p, _sz, _p],
     "f2s_chamfer_static": [_p, _p, _i, _i, _i, _p, _p],
+    "f2s_point_to_mesh_workspace_bytes": [_i, _i, _p],
+    "f2s_point_to_mesh": [_p, _i, _p, _i, _p, _i, _p, _p, _p, _sz, _p],
     "f2s_linear": [_p, _i, _p, _p, _p, _i, _i, _i, _i, _i, _p],
     "f2s_device_error": [_p, _i, _p],
     "f2s_selftest_wait_timeout": [_i, _p],

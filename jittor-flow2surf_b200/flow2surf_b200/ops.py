@@ -208,3 +208,35 @@ def chamfer_distances(pred: torch.Tensor, target: torch.Tensor) -> torch.Tensor:
     _lib.call("f2s_chamfer", _lib.ptr(pred), _lib.ptr(target), B, M, N, _lib.ptr(out),
               _lib.ptr(ws), ws.numel(), _lib.stream_handle())
     return out
+
+
+def point_to_mesh_distances(points: torch.Tensor, vertices: torch.Tensor, faces: torch.Tensor):
+    """Squared distance from each point to a triangle mesh and the closest
+    triangle's index: points (M, 3), vertices (V, 3), faces (F, 3) integer ->
+    (sq_distance (M,) float32, face_index (M,) int32). The quantity
+    point_cloud_utils' closest_points_on_mesh returns (as a distance) for
+    flow2surf/evaluation.py:31-34; ties go to the smaller face index."""
+    if points.dim() != 2 or points.shape[1] != 3:
+        raise ValueError(f"points must be (M, 3), got {tuple(points.shape)}")
+    if vertices.dim() != 2 or vertices.shape[1] != 3:
+        raise ValueError(f"vertices must be (V, 3), got {tuple(vertices.shape)}")
+    if faces.dim() != 2 or faces.shape[1] != 3:
+        raise ValueError(f"faces must be (F, 3), got {tuple(faces.shape)}")
+    _require_cuda(points, vertices, faces)
+    M, V, F = points.shape[0], vertices.shape[0], faces.shape[0]
+    dev = points.device
+    dist = torch.empty(M, dtype=torch.float32, device=dev)
+    idx = torch.empty(M, dtype=torch.int32, device=dev)
+    if M == 0:
+        return dist, idx
+    if V == 0 or F == 0:
+        raise ValueError("the mesh is empty")
+    faces = faces.to(torch.int32).contiguous()
+    lo, hi = int(faces.min().item()), int(faces.max().item())
+    if lo < 0 or hi >= V:
+        raise ValueError(f"face indices must lie in [0, {V}), got [{lo}, {hi}]")
+    points, vertices = _f32(points), _f32(vertices)
+    ws = _workspace("f2s_point_to_mesh_workspace_bytes", M, F)
+    _lib.call("f2s_point_to_mesh", _lib.ptr(points), M, _lib.ptr(vertices), V, _lib.ptr(faces), F,
+              _lib.ptr(dist), _lib.ptr(idx), _lib.ptr(ws), ws.numel(), _lib.stream_handle())
+    return dist, idx

@@ -139,3 +139,50 @@ def chamfer_distance(pred, target):
     a, _ = cKDTree(target).query(pred, workers=-1)
     b, _ = cKDTree(pred).query(target, workers=-1)
     return float((a ** 2).mean() + (b ** 2).mean())
+
+
+def closest_point_sq_distances(points, vertices, faces, chunk=256):
+    """Squared distance from each point to a triangle mesh and the closest face
+    (ties to the smaller index), float64: the quantity point_cloud_utils'
+    closest_points_on_mesh gives for flow2surf/evaluation.py:31-34, restated
+    from the region tests of Ericson, Real-Time Collision Detection (2005),
+    sec. 5.1.5 (vertex a, vertex b, edge ab, vertex c, edge ac, edge bc, face,
+    the first region that holds)."""
+    p_all = np.asarray(points, dtype=np.float64)
+    tri = np.asarray(vertices, dtype=np.float64)[np.asarray(faces)]
+    a, b, c = tri[:, 0], tri[:, 1], tri[:, 2]
+    ab, ac = b - a, c - a
+    out_d = np.empty(len(p_all))
+    out_f = np.empty(len(p_all), dtype=np.int64)
+    for s in range(0, len(p_all), chunk):
+        p = p_all[s:s + chunk, None, :]                       # (P, 1, 3)
+        ap, bp, cp = p - a, p - b, p - c
+        d1, d2 = (ab * ap).sum(-1), (ac * ap).sum(-1)
+        d3, d4 = (ab * bp).sum(-1), (ac * bp).sum(-1)
+        d5, d6 = (ab * cp).sum(-1), (ac * cp).sum(-1)
+        vc, vb, va = d1 * d4 - d3 * d2, d5 * d2 - d1 * d6, d3 * d6 - d5 * d4
+        with np.errstate(divide="ignore", invalid="ignore"):
+            denom = va + vb + vc
+            v, w = vb / denom, vc / denom                     # face
+            e43, e56 = d4 - d3, d5 - d6
+            regions = [                                        # lowest precedence first
+                ((va <= 0) & (e43 >= 0) & (e56 >= 0), 1 - e43 / (e43 + e56), e43 / (e43 + e56)),
+                ((vb <= 0) & (d2 >= 0) & (d6 <= 0), 0.0, d2 / (d2 - d6)),
+                ((d6 >= 0) & (d5 <= d6), 0.0, 1.0),
+                ((vc <= 0) & (d1 >= 0) & (d3 <= 0), d1 / (d1 - d3), 0.0),
+                ((d3 >= 0) & (d4 <= d3), 1.0, 0.0),
+                ((d1 <= 0) & (d2 <= 0), 0.0, 0.0),
+            ]
+            for cond, rv, rw in regions:
+                v = np.where(cond, rv, v)
+                w = np.where(cond, rw, w)
+        q = a + v[..., None] * ab + w[..., None] * ac
+        d = ((p - q) ** 2).sum(-1)
+        out_f[s:s + chunk] = d.argmin(1)
+        out_d[s:s + chunk] = d.min(1)
+    return out_d, out_f
+
+
+def point_to_surface(points, vertices, faces):
+    """flow2surf/evaluation.py:31-34: mean squared point-to-mesh distance."""
+    return float(closest_point_sq_distances(points, vertices, faces)[0].mean())

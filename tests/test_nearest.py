@@ -77,3 +77,74 @@ def test_nearest_errors(cuda):
     with pytest.raises(ValueError, match="nonempty"):
         nearest_squared_distances(torch.zeros(2, 0, 3, device="cuda"),
                                   torch.zeros(2, 4, 3, device="cuda"))
+
+
+# ---------------------------------------------------------------------------
+# point-to-surface (flow2surf/evaluation.py:31-34)
+# ---------------------------------------------------------------------------
+
+def _mesh_points(n, seed, sigma=0.02):
+    from flow2surf_b200.synthetic import sample_surface, union_mesh
+
+    v, f = union_mesh(seed)
+    rng = np.random.default_rng(seed)
+    pts = sample_surface(v, f, n, rng).astype(np.float64) + rng.normal(scale=sigma, size=(n, 3))
+    return pts.astype(np.float32), v.astype(np.float32), f.astype(np.int32)
+
+
+@pytest.mark.gpu
+def test_point_to_mesh_matches_oracle(cuda):
+    from flow2surf_b200.evaluation import point_to_surface
+    from flow2surf_b200.ops import point_to_mesh_distances
+    from oracle.inference import closest_point_sq_distances
+
+    pts, v, f = _mesh_points(3000, seed=4)
+    # points exactly on vertices and far away too
+    pts = np.concatenate([pts, v[:50], np.array([[3.0, -2.0, 1.0]], np.float32)])
+    d, fi = point_to_mesh_distances(torch.from_numpy(pts).cuda(), torch.from_numpy(v).cuda(),
+                                    torch.from_numpy(f).cuda())
+    d, fi = d.cpu().numpy(), fi.cpu().numpy()
+    want_d, want_f = closest_point_sq_distances(pts.astype(np.float64), v.astype(np.float64), f)
+    np.testing.assert_allclose(d, want_d, rtol=1e-5, atol=2e-7)
+    assert np.all(d[3000:3050] < 1e-12)          # on a vertex
+    # the face index, except where two faces are equally close (shared
+    # vertices and edges)
+    assert (fi == want_f).mean() > 0.9
+    got = point_to_surface(pts, v, f)
+    assert abs(got - want_d.mean()) <= 1e-6 * want_d.mean()
+
+
+@pytest.mark.gpu
+def test_point_to_mesh_100k_sample(cuda):
+    """The evaluation size: 100,000 noisy points against the 15,896-face
+    synthetic mesh, a sample of 500 points against the float64 oracle."""
+    from flow2surf_b200.ops import point_to_mesh_distances
+    from oracle.inference import closest_point_sq_distances
+
+    pts, v, f = _mesh_points(100_000, seed=5, sigma=0.015)
+    d, _ = point_to_mesh_distances(torch.from_numpy(pts).cuda(), torch.from_numpy(v).cuda(),
+                                   torch.from_numpy(f).cuda())
+    d = d.cpu().numpy()
+    pick = np.random.default_rng(0).choice(len(pts), 500, replace=False)
+    want, _ = closest_point_sq_distances(pts[pick].astype(np.float64), v.astype(np.float64), f)
+    np.testing.assert_allclose(d[pick], want, rtol=1e-5, atol=2e-7)
+    assert np.isfinite(d).all()
+
+
+@pytest.mark.gpu
+def test_point_to_mesh_edge_cases(cuda):
+    from flow2surf_b200.ops import point_to_mesh_distances
+
+    t = lambda a, dt=torch.float32: torch.tensor(a, dtype=dt, device="cuda")  # noqa: E731
+    tri_v = t([[0, 0, 0], [1, 0, 0], [0, 1, 0]])
+    tri_f = t([[0, 1, 2]], torch.int32)
+    pts = t([[0.25, 0.25, 2.0], [2, 0, 0], [-1, -1, 0], [0.5, 0.5, 0.0], [0.5, -1, 0]])
+    d, fi = point_to_mesh_distances(pts, tri_v, tri_f)
+    np.testing.assert_allclose(d.cpu().numpy(), [4.0, 1.0, 2.0, 0.0, 1.0], rtol=0, atol=1e-6)
+    assert fi.cpu().numpy().tolist() == [0] * 5
+    d0, _ = point_to_mesh_distances(t(np.zeros((0, 3))), tri_v, tri_f)
+    assert d0.numel() == 0
+    with pytest.raises(ValueError, match="face indices"):
+        point_to_mesh_distances(pts, tri_v, t([[0, 1, 3]], torch.int32))
+    with pytest.raises(ValueError, match="mesh is empty"):
+        point_to_mesh_distances(pts, tri_v, t(np.zeros((0, 3)), torch.int32))
