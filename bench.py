@@ -18,7 +18,12 @@ over all patches, fusion + Euler).
 flushed between steps); `e2e` is the same metric through the public
 patch_denoise with a pinned host array in and a host array out. The
 `reference` arm times the CPU restatement of the reference's path on the host
-cores (the reference's Jittor is not installed here).
+cores (the reference's Jittor is not installed here) on a bounded sample of
+the same cloud. Two more legs ride on the line, outside the timed steps:
+`chamfer` (the denoised cloud against a 100,000-point clean sample of its
+surface, with its fp32 SIMT roofline) and `one_cloud` (strong scaling: one
+400,000-point cloud split by patch across the ranks, one NCCL all-reduce of
+the vote sums per Euler step, with that all-reduce's own time).
 """
 
 from __future__ import annotations
@@ -59,6 +64,8 @@ def parse_args():
     p.add_argument("--cpu-sample-patches", type=int, default=10,
                    help="patches of the cloud in the bounded CPU-baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-one-cloud", action="store_true",
+                   help="skip the strong-scaling leg (one 400k-point cloud split by patch)")
     p.add_argument("--precision", choices=["fp32", "tf32"], default="tf32",
                    help="arithmetic of the trunk and decoder contractions")
     p.add_argument("--encoder-precision", choices=["fp32", "tf32", "bf16x3"], default="bf16x3",
@@ -128,6 +135,51 @@ def chamfer_leg(points, reference, repeats: int = 3) -> dict:
             "roofline": {"bound": "fp32 SIMT", "achieved": rate * CHAMFER_OPS_PER_PAIR / 1e12,
                          "peak": SIMT_LANE_OPS / 1e12, "unit": "T lane-ops/s",
                          "frac": rate * CHAMFER_OPS_PER_PAIR / SIMT_LANE_OPS}}
+
+
+ONE_CLOUD_POINTS = 400_000
+
+
+def one_cloud_leg(model, world: int, dev, steps: int = 3, warmup: int = 1) -> dict:
+    """Strong scaling: one 400,000-point cloud (the same on every rank) denoised
+    with its patches split across the ranks (each rank builds the patch index
+    of its own patches; one NCCL all-reduce of the float64 vote sums per Euler
+    step). Device time per denoise, max over ranks; the all-reduce's own time
+    from CUDA events around it."""
+    import torch
+    import torch.distributed as dist
+
+    from flow2surf_b200.inference import denoise_device, patch_seed_count
+
+    group = dist.group.WORLD if world > 1 else None
+    pts = torch.from_numpy(make_cloud(ONE_CLOUD_POINTS, 0)).to(dev)
+    run = lambda ev=None: denoise_device(model, pts, rng=np.random.default_rng(0),  # noqa: E731
+                                         process_group=group, collective_events=ev, **DENOISE)
+    for _ in range(warmup):
+        run()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    events: list = []
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        run(events)
+    stop.record()
+    torch.cuda.synchronize(dev)
+    t = torch.tensor([start.elapsed_time(stop) / steps,
+                      sum(a.elapsed_time(b) for a, b in events) / steps],
+                     dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, ar_ms = t.tolist()
+    return {"points": ONE_CLOUD_POINTS,
+            "patches": patch_seed_count(ONE_CLOUD_POINTS, DENOISE["patch_size"], DENOISE["seed_k"]),
+            "ranks": world, "scaling": "strong", "steps": steps, "ms_per_step": ms,
+            "value": ONE_CLOUD_POINTS / (ms * 1e-3), "unit": UNIT,
+            "allreduce_ms_per_step": ar_ms if world > 1 else 0.0,
+            "allreduce_bytes_per_step": (DENOISE["num_steps"] * ONE_CLOUD_POINTS * 24
+                                         if world > 1 else 0)}
 
 
 def profile_chamfer(args) -> None:
@@ -508,6 +560,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
     reference = mesh_cloud(args.points, seed=4 + cloud_seed, sigma_fraction=0.015,
                            noise_type="laplace", clean_points=CHAMFER_REFERENCE_POINTS)[2]
     chamfer = chamfer_leg(out, torch.from_numpy(reference).to(dev))
+    one_cloud = None if args.one_cloud or args.no_one_cloud else one_cloud_leg(model, world, dev)
     if rank != 0:
         return
 
@@ -534,6 +587,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(cloud.nbytes),
                 "d2h_bytes_per_step": int(host_out.nbytes)},
         "chamfer": chamfer,
+        "one_cloud": one_cloud,
         "gpu_launches": rec.launches * steps // traced_steps,
         "clocks": clocks.summary(),
         "kernel_breakdown": (f"separate traced pass of {traced_steps} steps (CUDA events "

@@ -113,6 +113,61 @@ def build_plan(points: torch.Tensor, patch_size: int, seeds: torch.Tensor,
                        weight_sum)
 
 
+def gather_patch_rows(local: torch.Tensor, num_patches: int, group) -> torch.Tensor:
+    """The rows of every rank's patch range in patch order: `local` holds this
+    rank's rows of `shard_range` at its top, padded to the largest range
+    (ceil(P / world) rows); one all-gather, then each rank's real rows."""
+    import torch.distributed as dist
+
+    world = dist.get_world_size(group)
+    chunk = local.shape[0]
+    parts = [torch.empty_like(local) for _ in range(world)]
+    dist.all_gather(parts, local.contiguous(), group=group)
+    rows = []
+    for r in range(world):
+        begin, end = shard_range(num_patches, r, world)
+        if end - begin > chunk:
+            raise ValueError("gather_patch_rows: a rank's range exceeds the padded chunk")
+        rows.append(parts[r][:end - begin])
+    return torch.cat(rows).contiguous()
+
+
+def build_plan_sharded(points: torch.Tensor, patch_size: int, seeds: torch.Tensor,
+                       patch_agg_beta: float, group) -> DenoisePlan:
+    """build_plan for one cloud split across the ranks of `group`: each rank
+    builds the patch index of its own patch range (`shard_range`), one
+    all-gather (NCCL) per array assembles every patch's neighbours, radial
+    distances and weights on every rank, and the fusion structure is built
+    from them. The patch index of a seed does not depend on the other seeds,
+    so the plan is the one build_plan gives, bit for bit."""
+    import torch.distributed as dist
+
+    n = points.shape[0]
+    P = seeds.shape[0]
+    dev = points.device
+    world, rank = dist.get_world_size(group), dist.get_rank(group)
+    chunk = -(-P // world)  # the largest range
+    begin, end = shard_range(P, rank, world)
+    local_n = torch.zeros((chunk, patch_size), dtype=torch.int32, device=dev)
+    local_r = torch.zeros((chunk, patch_size), dtype=torch.float64, device=dev)
+    local_w = torch.zeros((chunk, patch_size), dtype=torch.float64, device=dev)
+    if end > begin:
+        _lib.call("f2s_patch_index", _lib.ptr(points), n, _lib.ptr(seeds[begin:]), end - begin,
+                  patch_size, float(patch_agg_beta), _lib.ptr(local_n), _lib.ptr(local_r),
+                  _lib.ptr(local_w), _lib.stream_handle())
+    neighbors, radial, weights = (gather_patch_rows(x, P, group)
+                                  for x in (local_n, local_r, local_w))
+    offsets = torch.empty(n + 1, dtype=torch.int32, device=dev)
+    entries = torch.empty(P * patch_size, dtype=torch.int32, device=dev)
+    weight_sum = torch.empty(n, dtype=torch.float64, device=dev)
+    ws = _workspace("f2s_fusion_workspace_bytes", n, device=dev)
+    _lib.call("f2s_fusion_build", _lib.ptr(neighbors), _lib.ptr(weights), P, patch_size, n,
+              _lib.ptr(offsets), _lib.ptr(entries), _lib.ptr(weight_sum), _lib.ptr(ws),
+              ws.numel(), _lib.stream_handle())
+    return DenoisePlan(n, patch_size, seeds, neighbors, radial, weights, offsets, entries,
+                       weight_sum)
+
+
 class _Runner:
     """Reusable device buffers for the integration loop of one plan."""
 
@@ -188,6 +243,8 @@ class _ShardedRunner(_Runner):
                                            dist.get_world_size(group))
         self.vote_sum = torch.empty((plan.num_points, 3), dtype=torch.float64,
                                     device=plan.seeds.device)
+        # CUDA-event pairs around each all-reduce when timing is asked for
+        self.collective_events: list | None = None
 
     def step(self, points: torch.Tensor, out: torch.Tensor, alpha_current: float,
              alpha_step: float) -> None:
@@ -197,7 +254,14 @@ class _ShardedRunner(_Runner):
         _lib.call("f2s_fuse_partial", _lib.ptr(votes), _lib.ptr(plan.offsets),
                   _lib.ptr(plan.entries), _lib.ptr(plan.weights), plan.num_points,
                   plan.patch_size, self.begin, self.end, _lib.ptr(self.vote_sum), stream)
-        self.dist.all_reduce(self.vote_sum, group=self.group)
+        if self.collective_events is not None:
+            start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record()
+            self.dist.all_reduce(self.vote_sum, group=self.group)
+            stop.record()
+            self.collective_events.append((start, stop))
+        else:
+            self.dist.all_reduce(self.vote_sum, group=self.group)
         _lib.call("f2s_euler_from_sum", _lib.ptr(points), _lib.ptr(self.vote_sum),
                   _lib.ptr(plan.weight_sum), _lib.ptr(plan.offsets), plan.num_points,
                   ctypes.c_float(alpha_step), _lib.ptr(out), None, stream)
@@ -206,7 +270,7 @@ class _ShardedRunner(_Runner):
 def denoise_device(model, points: torch.Tensor, patch_size, seed_k, num_steps, rng=None,
                    patch_seed_idx=None, patch_agg_beta=4.0, alpha_clean_power=1.0,
                    alpha_noisy_power=1.0, workspace_budget=DEFAULT_WORKSPACE_BUDGET,
-                   process_group=None):
+                   process_group=None, collective_events=None):
     """patch_denoise on a cloud already on the GPU ((N, 3) float32 CUDA
     tensor); returns the denoised cloud as a new CUDA tensor.
 
@@ -214,7 +278,10 @@ def denoise_device(model, points: torch.Tensor, patch_size, seed_k, num_steps, r
     rank), every rank passes the same cloud and seeds and the patches are
     split across the ranks (`shard_range`); every rank returns the same
     result. The per-step sum then adds the ranks' partial float64 sums, which
-    can differ from the one-GPU order in the last bit of a float64 sum."""
+    can differ from the one-GPU order in the last bit of a float64 sum. Each
+    rank builds the patch index of its own patches (`build_plan_sharded`).
+    `collective_events`, if a list, receives a (start, stop) CUDA-event pair
+    around each per-step all-reduce."""
     if rng is None:
         rng = np.random.default_rng(0)
     num_points = points.shape[0]
@@ -231,13 +298,16 @@ def denoise_device(model, points: torch.Tensor, patch_size, seed_k, num_steps, r
         if np.any((seed_idx < 0) | (seed_idx >= num_points)):
             raise ValueError("patch_seed_idx contains an out-of-range point index")
         seeds = torch.from_numpy(seed_idx.astype(np.int32)).to(points.device)
-    plan = build_plan(points, patch_size, seeds, patch_agg_beta)
-    alphas = alpha_schedule(num_steps, alpha_clean_power, alpha_noisy_power)
     sharded = process_group is not None and torch.distributed.get_world_size(process_group) > 1
+    plan = (build_plan_sharded(points, patch_size, seeds, patch_agg_beta, process_group)
+            if sharded else build_plan(points, patch_size, seeds, patch_agg_beta))
+    alphas = alpha_schedule(num_steps, alpha_clean_power, alpha_noisy_power)
 
     def integrate(net):
         runner = (_ShardedRunner(net, plan, workspace_budget, process_group) if sharded
                   else _Runner(net, plan, workspace_budget))
+        if sharded and collective_events is not None:
+            runner.collective_events = collective_events
         current = points.clone()
         spare = torch.empty_like(current)
         for step in range(num_steps - 1, -1, -1):

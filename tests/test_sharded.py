@@ -96,6 +96,36 @@ def test_partial_sums_all_reduce_gloo(tmp_path):
     assert np.mean(got == want) > 0.99
 
 
+def _gather_rank(rank, world, port, P, result_path):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from flow2surf_b200.inference import gather_patch_rows
+        chunk = -(-P // world)
+        begin, end = shard_range(P, rank, world)
+        local = torch.full((chunk, 4), -1, dtype=torch.int32)
+        local[:end - begin] = torch.arange(begin, end, dtype=torch.int32)[:, None] * 10 + \
+            torch.arange(4, dtype=torch.int32)
+        full = gather_patch_rows(local, P, None)
+        if rank == 0:
+            np.save(result_path, full.numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("P,world", [(7, 2), (150, 3), (2, 3)])
+def test_gather_patch_rows_gloo(tmp_path, P, world):
+    """Each rank's patch-index rows (padded to the largest range) come back in
+    patch order on every rank: the assembly build_plan_sharded does after the
+    ranks' own patch indices."""
+    result = str(tmp_path / "rows.npy")
+    mp.start_processes(_gather_rank, args=(world, free_port(), P, result), nprocs=world,
+                       start_method="spawn")
+    got = np.load(result)
+    want = np.arange(P)[:, None] * 10 + np.arange(4)
+    np.testing.assert_array_equal(got, want)
+
+
 # ---------------------------------------------------------------- GPU ----
 
 def dev(a):
