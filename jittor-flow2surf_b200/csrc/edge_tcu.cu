@@ -133,10 +133,13 @@ __device__ __forceinline__ float unorder(uint32_t k) {
     return __uint_as_float(k ^ ((uint32_t)((int32_t)~k >> 31) | 0x80000000u));
 }
 
-// Bounded mbarrier wait by lane 0 of the warp, result shared by the warp.
+// Bounded mbarrier wait by lane 0 of the warp, result shared by the warp;
+// kPoll waits without the suspend hint (the control warps).
+template <bool kPoll = false>
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* err, int lane) {
     int ok = 1;
-    if (lane == 0) ok = tc::mbar_wait_spin(bar, parity, err) ? 1 : 0;
+    if (lane == 0)
+        ok = (kPoll ? tc::mbar_wait_poll(bar, parity, err) : tc::mbar_wait_spin(bar, parity, err)) ? 1 : 0;
     return __shfl_sync(kFull, ok, 0) != 0;
 }
 
@@ -208,11 +211,15 @@ edge_unified_kernel(const UArgs a) {
         const int cwarp = warp - kControlWarp0;
         const int row = cwarp * 32 + lane;
         // g = [x_j - x_i, x_i] of the row, from the points (model) or read as
-        // given (operator); g6 for the tile whose u rows are written next,
-        // ng6 / ni / nj the first stage of the tile after
-        float g6[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, ng6[6];
-        float3 ni;
-        int nj = 0;
+        // given (operator). Stage 1 (fetch_indices) loads the centre point and
+        // the neighbour index (or the given g) of a tile; stage 2
+        // (fetch_points, one tile later) the neighbour point; write_u (one
+        // more tile later) forms g, so no instruction waits on a load issued
+        // in the same iteration.
+        float4 pj = make_float4(0.f, 0.f, 0.f, 0.f);
+        float3 pi = make_float3(0.f, 0.f, 0.f), ni = pi;
+        float g6[6], ng6[6];
+        int nj = 0, nbase = 0;  // neighbour index within its patch, the patch's first row
         bool gvalid = false, nvalid = false;
         auto fetch_indices = [&](int t) {
             const int p = t * a.ppt + (row >> a.log2K);
@@ -225,7 +232,8 @@ edge_unified_kernel(const UArgs a) {
             } else {
                 const float4 v = *reinterpret_cast<const float4*>(a.xyz4 + (size_t)pc * 4);
                 ni = make_float3(v.x, v.y, v.z);
-                nj = (pc / a.M) * a.M + a.idx[(size_t)pc * K + (row & (K - 1))];
+                nbase = (pc / a.M) * a.M;
+                nj = a.idx[(size_t)pc * K + (row & (K - 1))];
             }
         };
         auto fetch_points = [&]() {
@@ -233,13 +241,8 @@ edge_unified_kernel(const UArgs a) {
 #pragma unroll
                 for (int e = 0; e < 6; ++e) g6[e] = ng6[e];
             } else {
-                const float4 v = *reinterpret_cast<const float4*>(a.xyz4 + (size_t)nj * 4);
-                g6[0] = v.x - ni.x;
-                g6[1] = v.y - ni.y;
-                g6[2] = v.z - ni.z;
-                g6[3] = ni.x;
-                g6[4] = ni.y;
-                g6[5] = ni.z;
+                pi = ni;
+                pj = *reinterpret_cast<const float4*>(a.xyz4 + (size_t)(nbase + nj) * 4);
             }
             gvalid = nvalid;
         };
@@ -249,9 +252,21 @@ edge_unified_kernel(const UArgs a) {
         };
         auto write_u = [&]() {
             float g[6];
+            if (!a.geometry) {
+                g6[0] = pj.x - pi.x;
+                g6[1] = pj.y - pi.y;
+                g6[2] = pj.z - pi.z;
+                g6[3] = pi.x;
+                g6[4] = pi.y;
+                g6[5] = pi.z;
+            }
 #pragma unroll
             for (int e = 0; e < 6; ++e) g[e] = gvalid ? g6[e] : 0.0f;
             write_u_row_g(sU, sGram, row, g);
+            // the rows for the tensor cores; fenced here, before the next
+            // prefetch loads are issued, since the fence waits for this
+            // thread's outstanding memory operations
+            fence_proxy_async();
         };
         // pre = LN(W_in g + b_in) of the tile whose u rows are in sU, into slot s
         auto issue_pre = [&](int s) {
@@ -283,12 +298,12 @@ edge_unified_kernel(const UArgs a) {
             }
         };
         const bool issuer = cwarp == 0 && lane == 0;
-        // u rows of the current geometry in sU, visible to the tensor cores
-        // once every control warp has passed the barrier; a failure seen by
-        // any control warp before the barrier is seen by all after it
+        // u rows of the current geometry in sU (each thread fenced its own),
+        // visible to the tensor cores once every control warp has passed the
+        // barrier; a failure seen by any control warp before the barrier is
+        // seen by all after it
         auto rows_written = [&](bool ok) -> bool {
             if (!ok && lane == 0) *sCtlFail = 1;
-            fence_proxy_async();
             control_barrier();
             return *sCtlFail == 0;
         };
@@ -300,7 +315,7 @@ edge_unified_kernel(const UArgs a) {
         if (ok && issuer) issue_pre(0);
         if (ok && t1 < n_tiles) {
             load_geometry(t1);
-            const bool waited = warp_wait(&pre_full[0], 0, a.err, lane);  // sU read by pre(t0)
+            const bool waited = warp_wait<true>(&pre_full[0], 0, a.err, lane);  // sU read by pre(t0)
             if (waited) write_u();
             ok = rows_written(waited);
             if (ok && issuer) issue_pre(1);
@@ -318,7 +333,7 @@ edge_unified_kernel(const UArgs a) {
             const int tile2 = tile + 2 * G;
             bool mine = true;
             if (tile2 < n_tiles) {
-                mine = warp_wait(&pre_full[s ^ 1], (uint32_t)((it + 1) >> 1) & 1u, a.err, lane);
+                mine = warp_wait<true>(&pre_full[s ^ 1], (uint32_t)((it + 1) >> 1) & 1u, a.err, lane);
                 if (mine) {
                     write_u();
                     fetch_points();               // tile index it + 3
@@ -328,9 +343,9 @@ edge_unified_kernel(const UArgs a) {
             ok = rows_written(mine);
             if (!ok) break;
             if (issuer) {
-                bool good = tc::mbar_wait_spin(&a_ready[s], (uint32_t)(it >> 1) & 1u, a.err);
+                bool good = tc::mbar_wait_poll(&a_ready[s], (uint32_t)(it >> 1) & 1u, a.err);
                 if (good && it >= a.n_acc)
-                    good = tc::mbar_wait_spin(&acc_free[acc], ((uint32_t)(it / a.n_acc) & 1u) ^ 1u,
+                    good = tc::mbar_wait_poll(&acc_free[acc], ((uint32_t)(it / a.n_acc) & 1u) ^ 1u,
                                               a.err);
                 if (good) {
                     tc::tc_fence_after();
@@ -339,7 +354,7 @@ edge_unified_kernel(const UArgs a) {
                     tc::umma_commit(&acc_full[acc]);
                 }
                 if (good && tile2 < n_tiles) {
-                    good = tc::mbar_wait_spin(&slot_free[s], (uint32_t)(it >> 1) & 1u, a.err);
+                    good = tc::mbar_wait_poll(&slot_free[s], (uint32_t)(it >> 1) & 1u, a.err);
                     if (good) {
                         tc::tc_fence_after();
                         issue_pre(s);

@@ -90,6 +90,34 @@ __device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, i
     return false;
 }
 
+// try_wait without a suspend hint: returns at once when the phase is still
+// open (the hardware's own short wait aside), so a polling thread sees the
+// phase complete without waking from a suspended state.
+__device__ __forceinline__ bool mbar_try_wait_now(uint64_t* bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
+// Bounded wait on mbar_try_wait_now polls: for the one warp of a pipeline
+// whose hand-offs set its pace (a suspended waiter may wake up to the hint's
+// length late). It costs issue slots while it polls, so the other roles keep
+// mbar_wait_spin. Bound and error word as in mbar_wait_spin.
+__device__ __forceinline__ bool mbar_wait_poll(uint64_t* bar, uint32_t parity, int* err) {
+    for (uint32_t i = 0; i < kSpinLimit; ++i) {
+        if (mbar_try_wait_now(bar, parity)) return true;
+        if ((i & 63u) == 63u && *reinterpret_cast<volatile int*>(err) != kTcOk) return false;
+    }
+    atomicExch(err, kTcWaitTimeout);
+    return false;
+}
+
 // Bounded wait that ignores the error word: used on the way out for copies
 // and MMAs already in flight, which must complete before the CTA releases its
 // shared or tensor memory. False when the phase did not complete in time.
