@@ -277,8 +277,13 @@ int f2s_trunk_forward(const f2s_model_config* cfg, const float* params, float* x
  * (inference.py:19-41) given its first index (the reference's
  * rng.integers(N), drawn by the caller).
  *   points (N, 3) float32 -> selected (count,) int32.
- *   workspace: f2s_fps_workspace_bytes() bytes (used only when one CTA's
- *   share of the cloud does not fit in shared memory, N > ~114k).
+ *   workspace: f2s_fps_workspace_bytes() bytes (used only when an 8-CTA
+ *   cluster's shared memory cannot hold the cloud, N > 114,688).
+ * Up to 114,688 points one thread-block cluster runs the loop; up to one
+ * CTA per SM x 14,336 points (2.1 M on a B200) a cooperative grid with one
+ * bounded grid-wide wait per seed (a wait that runs out sets the device
+ * error word, f2s_device_error, to 1 and the selection is not valid);
+ * beyond that the cluster keeps the running minima in the workspace.
  */
 int f2s_fps_workspace_bytes(int64_t N, size_t* bytes);
 int f2s_fps(const float* points, int64_t N, int64_t count, int64_t first, int32_t* selected,

@@ -5,6 +5,7 @@
 #include <cooperative_groups.h>
 
 #include "kernels.cuh"
+#include "tc_common.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -116,6 +117,90 @@ fps_kernel(const float* __restrict__ pts, int N, int count, int first, int slice
         __syncthreads();
     }
     cluster.sync();  // no CTA exits while a peer may still read its `part`
+}
+
+// The same sampling for clouds beyond one cluster's shared memory: one
+// cooperative grid of up to one CTA per SM, each CTA's slice (xyz and the
+// running minimum) resident in its shared memory. Per seed every CTA reduces
+// its slice to one (distance, -index) key, folds it into the seed's slot in
+// global memory with a 64-bit atomicMax and counts itself in on an arrival
+// counter; one thread per CTA polls the counter (a bounded wait: it gives up
+// after kFpsPollLimit polls, records kTcWaitTimeout in the device error word
+// and the grid returns) and reads the winner. Same arithmetic and tie-break
+// as fps_kernel, so the seeds are identical; slots and counter are zeroed by
+// the host before the launch.
+constexpr int kFpsGridThreads = 512;
+constexpr uint32_t kFpsPollLimit = 1u << 22;
+
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_gpu(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__global__ void __launch_bounds__(kFpsGridThreads)
+fps_grid_kernel(const float* __restrict__ pts, int N, int count, int first, int slice,
+                unsigned long long* __restrict__ slots, unsigned* __restrict__ arrived,
+                int32_t* __restrict__ sel, int* __restrict__ err) {
+    extern __shared__ __align__(16) float4 fps_sm[];
+    __shared__ unsigned long long red[33];
+    __shared__ int s_cur;
+    const int lo = blockIdx.x * slice;
+    const int hi = min(N, lo + slice);
+    const int tid = threadIdx.x;
+    for (int n = lo + tid; n < hi; n += kFpsGridThreads)
+        fps_sm[n - lo] = make_float4(pts[3 * n], pts[3 * n + 1], pts[3 * n + 2], INFINITY);
+    if (blockIdx.x == 0 && tid == 0) sel[0] = first;
+    int cur = first;
+    __syncthreads();
+    const unsigned grid = gridDim.x;
+    for (int i = 1; i < count; ++i) {
+        const float cx = pts[3 * cur], cy = pts[3 * cur + 1], cz = pts[3 * cur + 2];
+        unsigned long long best = 0ull;
+        for (int n = lo + tid; n < hi; n += kFpsGridThreads) {
+            const float4 p = fps_sm[n - lo];
+            float d = __fsub_rn(p.x, cx);
+            d = __fmul_rn(d, d);
+            float w = __fsub_rn(p.y, cy);
+            w = __fmul_rn(w, w);
+            d = __fadd_rn(d, w);
+            w = __fsub_rn(p.z, cz);
+            w = __fmul_rn(w, w);
+            d = __fadd_rn(d, w);
+            const float m = d < p.w ? d : p.w;
+            fps_sm[n - lo].w = m;
+            best = u64max(best, ((unsigned long long)__float_as_uint(m) << 32) |
+                                    (0xffffffffu - (unsigned)n));
+        }
+        best = block_max_u64(best, red);
+        if (tid == 0) {
+            atomicMax(&slots[i], best);
+            __threadfence();  // the slot's update is visible before the arrival
+            atomicAdd(arrived, 1u);
+            const unsigned target = (unsigned)i * grid;
+            int next = -1;
+            uint32_t poll = 0;
+            for (; poll < kFpsPollLimit; ++poll) {
+                if (ld_acquire_gpu(arrived) >= target) {
+                    next = (int)(0xffffffffu - (unsigned)(ld_relaxed_gpu(&slots[i]) & 0xffffffffu));
+                    break;
+                }
+                if ((poll & 255u) == 255u && *reinterpret_cast<volatile int*>(err) != tc::kTcOk)
+                    break;
+            }
+            if (poll == kFpsPollLimit) atomicExch(err, tc::kTcWaitTimeout);
+            s_cur = next;
+        }
+        __syncthreads();
+        cur = s_cur;
+        if (cur < 0) return;  // a wait gave up: the whole CTA leaves
+        if (blockIdx.x == 0 && tid == 0) sel[i] = cur;
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -484,7 +569,10 @@ using namespace f2s;
 
 extern "C" int f2s_fps_workspace_bytes(int64_t N, size_t* bytes) {
     F2S_REQUIRE(N >= 0 && bytes, "bad workspace query");
-    *bytes = (size_t)N * sizeof(float);
+    // the larger of: a running minimum per point (cluster path beyond the
+    // grid's shared memory), a 64-bit slot per seed plus the arrival counter
+    // (cooperative grid path)
+    *bytes = ((size_t)N + 2) * sizeof(unsigned long long);
     return F2S_OK;
 }
 
@@ -502,6 +590,41 @@ extern "C" int f2s_fps(const float* points, int64_t N, int64_t count, int64_t fi
     cs = cs < 1 ? 1 : (cs > kFpsMaxCluster ? kFpsMaxCluster : cs);
     const int slice = ceil_div(n, cs);
     const bool smem = slice <= kFpsSmemPoints;
+    const int grid = sm_count();
+    const int grid_slice = ceil_div(n, grid > 0 ? grid : 1);
+    if (!smem && grid > 0 && grid_slice <= kFpsSmemPoints &&
+        (int64_t)count * grid < (1ll << 32)) {
+        // cooperative grid, one CTA per SM, every slice in shared memory
+        const size_t need = ((size_t)count + 2) * sizeof(unsigned long long);
+        F2S_REQUIRE(workspace != nullptr, "fps: a workspace is needed for %d points", n);
+        if (workspace_bytes < need)
+            return fail(F2S_ERR_WORKSPACE, "fps needs %zu workspace bytes, got %zu", need,
+                        workspace_bytes);
+        int* err = tc_error_word();
+        if (!err) return fail(F2S_ERR_CUDA, "device error word unavailable");
+        cudaStream_t st = as_stream(stream);
+        auto* slots = static_cast<unsigned long long*>(workspace);
+        auto* arrived = reinterpret_cast<unsigned*>(slots + count);
+        TraceScope trace(kTagFps, st);
+        F2S_CUDA_TRY(cudaMemsetAsync(workspace, 0, need, st));
+        const size_t smem_bytes = (size_t)grid_slice * 16;
+        F2S_CUDA_TRY(cudaFuncSetAttribute(fps_grid_kernel,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)smem_bytes));
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(grid);
+        cfg.blockDim = dim3(kFpsGridThreads);
+        cfg.dynamicSmemBytes = smem_bytes;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeCooperative;
+        attr[0].val.cooperative = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        F2S_CUDA_TRY(cudaLaunchKernelEx(&cfg, fps_grid_kernel, points, n, (int)count,
+                                        (int)first, grid_slice, slots, arrived, selected, err));
+        return check_launch("fps_grid_kernel");
+    }
     if (!smem) {
         F2S_REQUIRE(workspace != nullptr, "fps: a workspace is needed for %d points", n);
         if (workspace_bytes < (size_t)N * sizeof(float))

@@ -34,10 +34,12 @@ def test_fps_reference_golden(cuda, golden, case):
     np.testing.assert_array_equal(got.cpu().numpy(), fix[f"{case}_indices"])
 
 
-@pytest.mark.parametrize("n,count", [(50_000, 150), (100_000, 60), (130_000, 40), (257, 257)])
+@pytest.mark.parametrize("n,count", [(50_000, 150), (100_000, 60), (130_000, 40), (257, 257),
+                                     (400_000, 300), (2_400_000, 12)])
 def test_fps_bit_exact(cuda, n, count):
-    """Covers one CTA, 8-CTA clusters with the slice in shared memory, and
-    the global-memory slice path (130k points)."""
+    """Covers one CTA, 8-CTA clusters with the slice in shared memory, the
+    cooperative grid (130k and 400k points) and the cluster with the running
+    minima in global memory (2.4M points)."""
     pts = mesh_cloud(n, seed=4)[0] if n >= 1000 else sphere_cloud(n, seed=1)[0]
     first = 17 % n
     got = farthest_point_indices(dev(pts), count, first).cpu().numpy()
