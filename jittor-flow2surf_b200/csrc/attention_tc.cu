@@ -347,6 +347,8 @@ attn_tc_colstats_kernel(const __grid_constant__ CUtensorMap map_hi,
 
 // ---------------------------------------------------------------------------
 // pass 2: out = h - (sum_j p_ij V_j) / (sum_j p_ij + 1e-9), p_ij = exp(S_ij - L_j)
+// Every hand-off of the per-key-tile chain S -> softmax -> P V sets the pace,
+// so its waits poll without the suspend hint (mbar_wait_poll).
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(kOutThreads, 1)
 attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
@@ -434,15 +436,15 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
             tma_load_3d(sQ + kQBytes, &map_qlo, q_full, 0, q0, b);
             for (int i = 0; i < kKStages && i < nk; ++i) load_k(i);
             for (int i = 0; i < 2 && i < nk; ++i) load_v(i);
-            ok = tc::mbar_wait(q_full, 0, a.err);
+            ok = tc::mbar_wait_poll(q_full, 0, a.err);
             if (!ok) tc::mbar_drain(q_full, 0);
             const uint32_t q_hi = tc::smem_u32(sQ), q_lo = q_hi + kQBytes;
             auto issue_s = [&](int i) -> bool {
                 const int ks = i % kKStages;
-                if (!tc::mbar_wait(&k_full[ks], (uint32_t)(i / kKStages) & 1u, a.err)) return false;
+                if (!tc::mbar_wait_poll(&k_full[ks], (uint32_t)(i / kKStages) & 1u, a.err)) return false;
                 k_landed = i + 1;
                 const int s = i & 1;
-                if (!tc::mbar_wait(&s_empty[s], ((uint32_t)(i >> 1) & 1u) ^ 1u, a.err)) return false;
+                if (!tc::mbar_wait_poll(&s_empty[s], ((uint32_t)(i >> 1) & 1u) ^ 1u, a.err)) return false;
                 tc::tc_fence_after();
                 const uint32_t k_hi = tc::smem_u32(sK + (2 * ks) * kKBytes), k_lo = k_hi + kKBytes;
                 const uint32_t d = tmem + (uint32_t)(s * 64);
@@ -465,8 +467,8 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
                     break;
                 }
                 // P_i written by the softmax threads, V_i landed
-                if (!tc::mbar_wait(p_full, (uint32_t)i & 1u, a.err) ||
-                    !tc::mbar_wait(&v_full[i & 1], (uint32_t)(i >> 1) & 1u, a.err)) {
+                if (!tc::mbar_wait_poll(p_full, (uint32_t)i & 1u, a.err) ||
+                    !tc::mbar_wait_poll(&v_full[i & 1], (uint32_t)(i >> 1) & 1u, a.err)) {
                     ok = false;
                     break;
                 }
@@ -484,7 +486,7 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
                 // S_i is done with its K tile (issued before P V_i, so waiting here
                 // never holds P V_i back): refill that stage with tile i + kKStages
                 if (i + kKStages < nk) {
-                    if (!tc::mbar_wait(&k_empty[i % kKStages], (uint32_t)(i / kKStages) & 1u, a.err)) {
+                    if (!tc::mbar_wait_poll(&k_empty[i % kKStages], (uint32_t)(i / kKStages) & 1u, a.err)) {
                         ok = false;
                         break;
                     }
@@ -493,7 +495,7 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
 
                 // P V_{i-1} is done with its V tile: refill that stage with tile i + 1
                 if (i >= 1 && i + 1 < nk) {
-                    if (!tc::mbar_wait(&v_empty[(i - 1) & 1], (uint32_t)((i - 1) >> 1) & 1u, a.err)) {
+                    if (!tc::mbar_wait_poll(&v_empty[(i - 1) & 1], (uint32_t)((i - 1) >> 1) & 1u, a.err)) {
                         ok = false;
                         break;
                     }
@@ -526,7 +528,7 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
         for (int i = 0; i < nk; ++i) {
             const int s = i & 1;
             const uint32_t ph = (uint32_t)(i >> 1) & 1u;
-            if (stid == 0) sFlag[s] = tc::mbar_wait(&s_full[s], ph, a.err) ? 1 : 0;
+            if (stid == 0) sFlag[s] = tc::mbar_wait_poll(&s_full[s], ph, a.err) ? 1 : 0;
             named_sync_out();
             if (!sFlag[s]) {
                 ok = false;
@@ -568,7 +570,7 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
             if (i > 1) {
                 if (stid == 0)
                     sFlag[2 + s] =
-                        tc::mbar_wait(&pv_done[s], (uint32_t)((i - 2) >> 1) & 1u, a.err) ? 1 : 0;
+                        tc::mbar_wait_poll(&pv_done[s], (uint32_t)((i - 2) >> 1) & 1u, a.err) ? 1 : 0;
                 named_sync_out();
                 if (!sFlag[2 + s]) {
                     ok = false;
@@ -585,7 +587,7 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
         if (ok) {
             sDen[half * kRows + row] = den;
             if (stid == 0)
-                sFlag[4] = tc::mbar_wait(&pv_done[(nk - 1) & 1], (uint32_t)((nk - 1) >> 1) & 1u,
+                sFlag[4] = tc::mbar_wait_poll(&pv_done[(nk - 1) & 1], (uint32_t)((nk - 1) >> 1) & 1u,
                                          a.err) ? 1 : 0;
             named_sync_out();
             ok = sFlag[4] != 0;
@@ -606,7 +608,7 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
                     tc::mbar_arrive_expect_tx(h_full, nbox * kBox);
                     for (int j = 0; j < nbox; ++j)
                         tma_load_3d(sV + j * kBox, &map_h, h_full, j * 32, q0, b);
-                    go = tc::mbar_wait(h_full, 0, a.err);
+                    go = tc::mbar_wait_poll(h_full, 0, a.err);
                     if (!go) tc::mbar_drain(h_full, 0);
                 }
                 sFlag[5] = go ? 1 : 0;

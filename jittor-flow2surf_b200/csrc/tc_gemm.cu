@@ -33,7 +33,6 @@ __device__ int g_tc_error = 0;
 
 namespace {
 
-constexpr int kThreads = 320;
 constexpr int kEpilogueThreads = 256;
 constexpr int kTileM = 128;
 constexpr size_t kSmemLimit = 227 * 1024;
@@ -43,6 +42,7 @@ struct TcGemmArgs {
     int bn;
     int k_blocks;
     int stages;
+    int b_res;          // the CTA's weight tiles (all K) stay in shared memory
     int acc_cols;       // TMEM columns of one accumulator buffer
     uint32_t idesc;
     uint32_t idesc_dual;  // SwiGLU: N = 2 BN over the adjacent W / W2 tiles
@@ -105,6 +105,20 @@ __device__ __forceinline__ void bulk_wait_read() {
     asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(kPending) : "memory");
 }
 
+// 16 consecutive values of a per-column vector from `col0` (zeros past `cols`;
+// cols is a multiple of 4 on the TMA path).
+__device__ __forceinline__ void load_cols16(const float* v, int col0, int cols, float (&out)[16]) {
+#pragma unroll
+    for (int i = 0; i < 16; i += 4) {
+        const float4 x = v && col0 + i < cols ? __ldg(reinterpret_cast<const float4*>(v + col0 + i))
+                                              : make_float4(0.f, 0.f, 0.f, 0.f);
+        out[i] = x.x;
+        out[i + 1] = x.y;
+        out[i + 2] = x.z;
+        out[i + 3] = x.w;
+    }
+}
+
 // 32 consecutive values of a per-column vector from `col0` (zeros past `cols`;
 // cols is a multiple of 4 on the TMA path).
 __device__ __forceinline__ void load_cols32(const float* v, int col0, int cols, float (&out)[32]) {
@@ -120,13 +134,18 @@ __device__ __forceinline__ void load_cols32(const float* v, int col0, int cols, 
 }
 
 // kSplit (with kTf32): map_a2 / map_b2 hold the low parts of A / W.
-template <bool kTf32, int kEpi, bool kSplit>
-__global__ void __launch_bounds__(kThreads, 1)
+// kEW: epilogue warps, 8, or 16 for the SwiGLU epilogue with fp16 rows (its
+// SiLU on the special-function unit needs four warps per SM sub-partition to
+// hide the latency of the exponential and reciprocal).
+template <bool kTf32, int kEpi, bool kSplit, int kEW = 8>
+__global__ void __launch_bounds__(64 + 32 * kEW, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_a2,
                const __grid_constant__ CUtensorMap map_b, const __grid_constant__ CUtensorMap map_b2,
                const __grid_constant__ CUtensorMap map_y, const TcGemmArgs g) {
     constexpr bool kDual = kEpi == kEpiSwiGlu;
     static_assert(!(kSplit && (kDual || !kTf32)), "3xTF32 runs the single-matrix tf32 form");
+    static_assert(kEW == 8 || (kEW == 16 && kDual), "16 epilogue warps: the SwiGLU form only");
+    constexpr int kEpiThreads = 32 * kEW;
     extern __shared__ __align__(1024) unsigned char tc_smem_raw[];
     // 1024-byte alignment of the tile region (SWIZZLE_128B atoms)
     unsigned char* smem = reinterpret_cast<unsigned char*>(
@@ -134,22 +153,46 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     const int S = g.stages;
     const uint32_t a_bytes = kTileM * 128;
     const uint32_t b_bytes = (uint32_t)g.bn * 128;
-    // stage: A (A_lo), then W (W2 for SwiGLU, W_lo for 3xTF32)
+    // stage: A (A_lo), then W (W2 for SwiGLU, W_lo for 3xTF32). With b_res
+    // the W tiles of every K block are loaded once, after the stages, and a
+    // stage holds A only.
     const uint32_t a_stage = a_bytes * (kSplit ? 2 : 1);
-    const uint32_t stage_bytes = a_stage + b_bytes * ((kDual || kSplit) ? 2 : 1);
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)S * stage_bytes);
+    const uint32_t b_stage = b_bytes * ((kDual || kSplit) ? 2 : 1);
+    const uint32_t stage_bytes = a_stage + (g.b_res ? 0u : b_stage);
+    unsigned char* b_region = smem + (size_t)S * stage_bytes;
+    const size_t tiles_bytes = (size_t)S * stage_bytes + (g.b_res ? (size_t)g.k_blocks * b_stage : 0);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + tiles_bytes);
     uint64_t* empty = full + S;
     uint64_t* tfull = empty + S;      // [2]
     uint64_t* tempty = tfull + 2;     // [2]
     uint64_t* mma_done = tempty + 2;  // [1]
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+    uint64_t* b_full = mma_done + 1;  // [1] the resident W tiles
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(b_full + 1);
     // per tile parity: set by the one polling epilogue lane when its wait
     // failed, read by every epilogue warp after their named barrier
     int* epi_fail = reinterpret_cast<int*>(tmem_slot + 1);  // [2]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_tiles_n = (g.cols + g.bn - 1) / g.bn;
-    const int n_tiles = ((g.rows + kTileM - 1) / kTileM) * n_tiles_n;
+    const int m_tiles = (g.rows + kTileM - 1) / kTileM;
+    // the i-th output tile of this CTA; false past its last. Streaming W:
+    // tiles in row-major order, strided by the grid. Resident W: the grid is
+    // n_tiles_n x groups, CTA c keeps N tile c % n_tiles_n and walks the row
+    // blocks c / n_tiles_n, + groups, ...
+    auto tile_at = [&](int i, int& m0, int& n0) -> bool {
+        int mb, nb;
+        if (g.b_res) {
+            nb = (int)blockIdx.x % n_tiles_n;
+            mb = (int)blockIdx.x / n_tiles_n + i * ((int)gridDim.x / n_tiles_n);
+        } else {
+            const int t = (int)blockIdx.x + i * (int)gridDim.x;
+            mb = t / n_tiles_n;
+            nb = t - mb * n_tiles_n;
+        }
+        m0 = mb * kTileM;
+        n0 = nb * g.bn;
+        return mb < m_tiles;
+    };
     uint32_t tmem_cols = 32;
     while (tmem_cols < (uint32_t)(2 * g.acc_cols)) tmem_cols <<= 1;
 
@@ -160,9 +203,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         }
         for (int b = 0; b < 2; ++b) {
             tc::mbar_init(&tfull[b], 1);
-            tc::mbar_init(&tempty[b], kEpilogueThreads);
+            tc::mbar_init(&tempty[b], kEpiThreads);
         }
         tc::mbar_init(mma_done, 1);
+        tc::mbar_init(b_full, 1);
         epi_fail[0] = epi_fail[1] = 0;
         tc::fence_barrier_init();
         tc::prefetch_tensormap(&map_a);
@@ -184,9 +228,21 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             uint32_t pending = 0;        // stages whose last load may still be in flight
             uint32_t pending_phase = 0;  // the phase each of those loads completes
             bool ok = true;
-            for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
-                const int m0 = (tile / n_tiles_n) * kTileM;
-                const int n0 = (tile % n_tiles_n) * g.bn;
+            if (g.b_res) {
+                // the CTA's W tiles, every K block, once
+                int m0, n0;
+                tile_at(0, m0, n0);
+                tc::mbar_arrive_expect_tx(b_full, (uint32_t)g.k_blocks * b_stage);
+                for (int kb = 0; kb < g.k_blocks; ++kb) {
+                    unsigned char* bs = b_region + (size_t)kb * b_stage;
+                    const int k0 = kb * (kTf32 ? 32 : 64);
+                    tc::tma_load_2d(bs, &map_b, b_full, k0, n0);
+                    if (kDual || kSplit) tc::tma_load_2d(bs + b_bytes, &map_b2, b_full, k0, n0);
+                }
+            }
+            for (int i = 0; ok; ++i) {
+                int m0, n0;
+                if (!tile_at(i, m0, n0)) break;
                 for (int kb = 0; kb < g.k_blocks; ++kb) {
                     if (!tc::mbar_wait(&empty[stage], phase ^ 1u, g.err)) {
                         ok = false;
@@ -198,9 +254,11 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                     const int k0 = kb * (kTf32 ? 32 : 64);
                     tc::tma_load_2d(st, &map_a, &full[stage], k0, m0);
                     if (kSplit) tc::tma_load_2d(st + a_bytes, &map_a2, &full[stage], k0, m0);
-                    tc::tma_load_2d(st + a_stage, &map_b, &full[stage], k0, n0);
-                    if (kDual || kSplit)
-                        tc::tma_load_2d(st + a_stage + b_bytes, &map_b2, &full[stage], k0, n0);
+                    if (!g.b_res) {
+                        tc::tma_load_2d(st + a_stage, &map_b, &full[stage], k0, n0);
+                        if (kDual || kSplit)
+                            tc::tma_load_2d(st + a_stage + b_bytes, &map_b2, &full[stage], k0, n0);
+                    }
                     pending |= 1u << stage;
                     pending_phase = (pending_phase & ~(1u << stage)) | (phase << stage);
                     if (++stage == S) {
@@ -213,6 +271,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                 // let the copies already issued land before the CTA exits
                 for (int s = 0; s < S; ++s)
                     if (pending & (1u << s)) tc::mbar_drain(&full[s], (pending_phase >> s) & 1u);
+                if (g.b_res) tc::mbar_drain(b_full, 0);
             }
         }
     } else if (warp == 1) {
@@ -223,7 +282,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             int iter = 0;
             bool ok = true;
             constexpr int kSteps = 4;  // 128 bytes of K per stage / 32 bytes per instruction
-            for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x, ++iter) {
+            if (g.b_res && !tc::mbar_wait(b_full, 0, g.err)) ok = false;
+            for (int i = 0; ok; ++i, ++iter) {
+                int m0, n0;
+                if (!tile_at(i, m0, n0)) break;
                 const int buf = iter & 1;
                 const uint32_t tph = (uint32_t)(iter >> 1) & 1u;
                 if (!tc::mbar_wait(&tempty[buf], tph ^ 1u, g.err)) {
@@ -239,12 +301,14 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                     }
                     tc::tc_fence_after();
                     const uint32_t st = tc::smem_u32(smem + (size_t)stage * stage_bytes);
+                    const uint32_t sb = g.b_res ? tc::smem_u32(b_region + (size_t)kb * b_stage)
+                                                : st + a_stage;
                     // the stage's descriptors once; K step k adds 32 bytes = 2 in
                     // the start-address field (address >> 4)
                     const uint64_t a0 = tc::sw128_desc(st);
-                    const uint64_t b0 = tc::sw128_desc(st + a_stage);
+                    const uint64_t b0 = tc::sw128_desc(sb);
                     const uint64_t a_lo0 = kSplit ? tc::sw128_desc(st + a_bytes) : 0;
-                    const uint64_t b_lo0 = kSplit ? tc::sw128_desc(st + a_stage + b_bytes) : 0;
+                    const uint64_t b_lo0 = kSplit ? tc::sw128_desc(sb + b_bytes) : 0;
                     const uint32_t idesc = kDual ? g.idesc_dual : g.idesc;
 #pragma unroll
                     for (int k = 0; k < kSteps; ++k) {
@@ -271,34 +335,87 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         }
         __syncwarp();
     } else {
-        // ---------------- epilogue (warps 2..9) ----------------
-        // two warps per TMEM lane quarter, taking alternate 32-column chunks
+        // ---------------- epilogue (warps 2 .. 1 + kEW) ----------------
+        // kEW / 4 warps per TMEM lane quarter, taking alternate 32-column chunks
         const int quarter = warp & 3;
         const int ew = warp - 2;
-        const int chunk_half = ew >> 2;
-        unsigned char* epi_smem = smem + (size_t)S * stage_bytes + 1024;  // 1024-byte aligned
-        // TMA path: two swizzled 32 x 32 boxes per warp, alternating
-        unsigned char* boxes = epi_smem + (size_t)ew * 2 * kEpiBox;
+        const int chunk_half = ew >> 2;  // the warp's place in its quarter
+        unsigned char* epi_smem = smem + tiles_bytes + 1024;  // 1024-byte aligned
+        // TMA path: two swizzled 32 x 32 boxes per warp, alternating (fp32
+        // boxes of kEpiBox bytes); with 16 warps one 2 KB fp16 box per warp
+        // (a warp stores one box per tile, so its previous store has long
+        // finished reading when the next tile's box is written, and the
+        // shared memory goes to operand stages instead)
+        constexpr uint32_t kBoxSlot = kEW == 16 ? 2048u : kEpiBox;
+        constexpr int kSlots = kEW == 16 ? 1 : 2;
+        unsigned char* boxes = epi_smem + (size_t)ew * kSlots * kBoxSlot;
         // transposing path: 32 x 33 staging buffers (two for SwiGLU)
         float* stage_buf = reinterpret_cast<float*>(epi_smem) + ew * (kDual ? 2 : 1) * 32 * 33;
         float* stage_buf2 = stage_buf + 32 * 33;  // SwiGLU value accumulator
         int iter = 0;
         int boxes_sent = 0;
-        for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++iter) {
+        for (int i = 0;; ++i, ++iter) {
+            int m0, n0;
+            if (!tile_at(i, m0, n0)) break;
             const int buf = iter & 1;
             const uint32_t tph = (uint32_t)(iter >> 1) & 1u;
             // one lane polls, the other epilogue warps wait on the named barrier
             volatile int* fail = epi_fail + (iter & 1);
             if (ew == 0 && lane == 0 && !tc::mbar_wait(&tfull[buf], tph, g.err)) *fail = 1;
-            asm volatile("bar.sync 1, %0;" ::"n"(kEpilogueThreads) : "memory");
+            asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
             if (*fail) break;
             tc::tc_fence_after();
-            const int m0 = (tile / n_tiles_n) * kTileM;
-            const int n0 = (tile % n_tiles_n) * g.bn;
             const int row0 = m0 + quarter * 32;  // first of this warp's 32 rows
             const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) +
                                    (uint32_t)(buf * g.acc_cols);
-            if (g.tma_epi) {
+            if constexpr (kEW == 16) {
+                // SwiGLU into fp16 rows: warp place c of its quarter takes the
+                // 32-column chunks c, c + 4, ... in two halves of 16 columns
+                // (gate and value accumulators and both biases of a half in
+                // registers), one 32 x 32 fp16 box per chunk, stored by TMA
+                for (int c0 = chunk_half * 32; c0 < g.bn; c0 += 32 * (kEW / 4)) {
+                    const int col0 = n0 + c0;
+                    if (col0 >= g.cols) break;  // warp-uniform
+                    unsigned char* box = boxes;
+                    // the box's previous store must have read it
+                    if (lane == 0 && boxes_sent >= 1) bulk_wait_read<0>();
+                    __syncwarp();
+                    bool out_of_range = false;
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        uint32_t rv[16], ru[16];
+                        tc::tmem_ld16_issue(t_row + (uint32_t)(c0 + 16 * h), rv);
+                        tc::tmem_ld16_issue(t_row + (uint32_t)(g.bn + c0 + 16 * h), ru);
+                        float b[16], b2[16];
+                        load_cols16(g.bias, col0 + 16 * h, g.cols, b);
+                        load_cols16(g.bias2, col0 + 16 * h, g.cols, b2);
+                        tc::tmem_ld16_wait(rv);
+                        tc::tmem_ld16_wait(ru);
+                        float o[16];
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            o[j] = f2s_silu_approx(__uint_as_float(rv[j]) + b[j]) *
+                                   (__uint_as_float(ru[j]) + b2[j]);
+                            // fp16 keeps tf32's 10-bit mantissa; a value the
+                            // format cannot hold is reported, not clamped
+                            out_of_range |= !(fabsf(o[j]) < 65504.0f);
+                        }
+#pragma unroll
+                        for (int ch = 0; ch < 2; ++ch)
+                            *reinterpret_cast<uint4*>(box + sw64_offset(lane, 2 * h + ch)) = make_uint4(
+                                pack_half2(o[8 * ch], o[8 * ch + 1]), pack_half2(o[8 * ch + 2], o[8 * ch + 3]),
+                                pack_half2(o[8 * ch + 4], o[8 * ch + 5]), pack_half2(o[8 * ch + 6], o[8 * ch + 7]));
+                    }
+                    if (out_of_range) atomicExch(g.err, tc::kTcFp16Range);
+                    fence_proxy_async_shared();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_2d(&map_y, box, col0, row0);
+                        bulk_commit();
+                    }
+                    ++boxes_sent;
+                }
+            } else if (g.tma_epi) {
                 // thread = row: the epilogue in registers, one swizzled box per
                 // 32 columns, written to global memory by one TMA store (or
                 // reduce-add for the residual, so y is never read here)
@@ -329,7 +446,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                             if (g.round_tf32) v[i] = f2s_round_tf32(v[i]);
                         }
                     }
-                    unsigned char* box = boxes + (boxes_sent & 1) * kEpiBox;
+                    unsigned char* box = boxes + (boxes_sent & 1) * kBoxSlot;
                     // the box's previous store must have read it
                     if (lane == 0 && boxes_sent >= 2) bulk_wait_read<1>();
                     __syncwarp();
@@ -462,13 +579,13 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-template <bool kTf32, int kEpi, bool kSplit = false>
+template <bool kTf32, int kEpi, bool kSplit = false, int kEW = 8>
 int launch_tc(const CUtensorMap& ma, const CUtensorMap& ma2, const CUtensorMap& mb,
               const CUtensorMap& mb2, const CUtensorMap& my, const TcGemmArgs& g, size_t smem,
               int grid, cudaStream_t st) {
-    auto kernel = tc_gemm_kernel<kTf32, kEpi, kSplit>;
+    auto kernel = tc_gemm_kernel<kTf32, kEpi, kSplit, kEW>;
     F2S_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    kernel<<<grid, kThreads, smem, st>>>(ma, ma2, mb, mb2, my, g);
+    kernel<<<grid, 64 + 32 * kEW, smem, st>>>(ma, ma2, mb, mb2, my, g);
     return check_launch("tc_gemm_kernel");
 }
 
@@ -614,35 +731,57 @@ int tc_gemm(const TcGemmOp& op, cudaStream_t st) {
         F2S_TRY(make_tensor_map_2d_typed(&my, op.Y, op.y_fp16 ? kTmaF16 : kTmaF32, op.y_fp16 ? 64 : 128,
                                          op.rows, op.cols, op.ldy, 32, 32));
     else my = ma;
-    const size_t stage_bytes =
-        (size_t)kTileM * 128 * (split ? 2 : 1) + (size_t)bn * 128 * ((dual || split) ? 2 : 1);
-    // epilogue region: the transposing path's 32 x 33 buffers or the TMA
-    // path's two 4 KB boxes per warp, whichever is larger
-    size_t stage_buf_bytes = (size_t)(kEpilogueThreads / 32) * (dual ? 2 : 1) * 32 * 33 * sizeof(float);
-    const size_t box_bytes = (size_t)(kEpilogueThreads / 32) * 2 * kEpiBox;
-    stage_buf_bytes = stage_buf_bytes > box_bytes ? stage_buf_bytes : box_bytes;
-    int stages = (int)((kSmemLimit - 1024 - 1024 - stage_buf_bytes) / stage_bytes);
+    const size_t a_stage_bytes = (size_t)kTileM * 128 * (split ? 2 : 1);
+    const size_t b_stage_bytes = (size_t)bn * 128 * ((dual || split) ? 2 : 1);
+    // epilogue region: the TMA path's two 4 KB boxes per warp, or the
+    // transposing path's 32 x 33 buffers
+    // SwiGLU into fp16 rows runs 16 epilogue warps with 2 KB boxes
+    const bool wide_epi = dual && op.y_fp16 && g.tma_epi;
+    const size_t stage_buf_bytes =
+        wide_epi    ? (size_t)16 * 2048
+        : g.tma_epi ? (size_t)(kEpilogueThreads / 32) * 2 * kEpiBox
+                    : (size_t)(kEpilogueThreads / 32) * (dual ? 2 : 1) * 32 * 33 * sizeof(float);
+    const size_t fixed = 1024 + 1024 + stage_buf_bytes;  // alignment slack, barriers, epilogue
+    const int m_tiles = ceil_div(op.rows, kTileM), n_tiles_n = ceil_div(op.cols, bn);
+    const int sms = sm_count();
+    // Resident W: when one N tile's weights over all of K fit beside two A
+    // stages and every CTA gets at least two row blocks, each CTA loads its
+    // W tiles once instead of once per output tile (a small-K GEMM otherwise
+    // moves more W than A bytes from L2 into shared memory).
+    const size_t b_region = (size_t)g.k_blocks * b_stage_bytes;
+    int groups = n_tiles_n <= sms ? sms / n_tiles_n : 0;
+    groups = groups < m_tiles ? groups : m_tiles;
+    g.b_res = groups >= 1 && m_tiles >= 2 * groups &&
+              fixed + b_region + 4 * a_stage_bytes <= kSmemLimit;
+    const size_t stage_bytes = a_stage_bytes + (g.b_res ? 0 : b_stage_bytes);
+    const size_t resident = g.b_res ? b_region : 0;
+    int stages = (int)((kSmemLimit - fixed - resident) / stage_bytes);
     stages = stages > 8 ? 8 : stages;
     F2S_LIMIT(stages >= 2, "tc_gemm: tile too large for shared memory");
     g.stages = stages;
-    // alignment slack, tiles, barriers + TMEM slot (< 1 KB, keeping the
-    // epilogue region 1024-byte aligned for its swizzled boxes), epilogue region
-    const size_t smem = 1024 + stages * stage_bytes + 1024 + stage_buf_bytes;
-    const int tiles = ceil_div(op.rows, kTileM) * ceil_div(op.cols, bn);
-    const int grid = tiles < sm_count() ? tiles : sm_count();
+    // alignment slack, tiles (+ resident W), barriers + TMEM slot (< 1 KB,
+    // keeping the epilogue region 1024-byte aligned for its swizzled boxes),
+    // epilogue region
+    const size_t smem = 1024 + stages * stage_bytes + resident + 1024 + stage_buf_bytes;
+    const int tiles = m_tiles * n_tiles_n;
+    const int grid = g.b_res ? n_tiles_n * groups : (tiles < sms ? tiles : sms);
     TraceScope trace(op.tag, st);
     if (split) return launch_tc<true, kEpiStore, true>(ma, ma2, mb, mb2, my, g, smem, grid, st);
     if (op.tf32) {
         switch (op.epilogue) {
             case kEpiStore: return launch_tc<true, kEpiStore>(ma, ma2, mb, mb2, my, g, smem, grid, st);
             case kEpiGatedResidual: return launch_tc<true, kEpiGatedResidual>(ma, ma2, mb, mb2, my, g, smem, grid, st);
-            case kEpiSwiGlu: return launch_tc<true, kEpiSwiGlu>(ma, ma2, mb, mb2, my, g, smem, grid, st);
+            case kEpiSwiGlu:
+                if (wide_epi) return launch_tc<true, kEpiSwiGlu, false, 16>(ma, ma2, mb, mb2, my, g, smem, grid, st);
+                return launch_tc<true, kEpiSwiGlu>(ma, ma2, mb, mb2, my, g, smem, grid, st);
         }
     } else {
         switch (op.epilogue) {
             case kEpiStore: return launch_tc<false, kEpiStore>(ma, ma2, mb, mb2, my, g, smem, grid, st);
             case kEpiGatedResidual: return launch_tc<false, kEpiGatedResidual>(ma, ma2, mb, mb2, my, g, smem, grid, st);
-            case kEpiSwiGlu: return launch_tc<false, kEpiSwiGlu>(ma, ma2, mb, mb2, my, g, smem, grid, st);
+            case kEpiSwiGlu:
+                if (wide_epi) return launch_tc<false, kEpiSwiGlu, false, 16>(ma, ma2, mb, mb2, my, g, smem, grid, st);
+                return launch_tc<false, kEpiSwiGlu>(ma, ma2, mb, mb2, my, g, smem, grid, st);
         }
     }
     return fail(F2S_ERR_INVALID_ARGUMENT, "tc_gemm: bad epilogue");
