@@ -149,15 +149,20 @@ int f2s_neighbor_reduce_tc(const float* content, const float* geometry, const in
  *   x (rows, ldx >= K), weight (cols, K), bias (cols) or NULL -> y (rows, ldy) fp32.
  *   precision F2S_PRECISION_FP32: fp32 CUDA-core kernel;
  *   F2S_PRECISION_TF32: tcgen05 tensor cores reading fp32 x/weight as tf32;
- *   F2S_PRECISION_BF16: tcgen05 tensor cores, x and weight are bf16.
+ *   F2S_PRECISION_BF16: tcgen05 tensor cores, x and weight are bf16;
+ *   F2S_PRECISION_BF16X3: x is fp32, split into bf16 high and low parts in
+ *   shared memory by the kernel; weight points at the bf16 high parts of W
+ *   (cols, K) followed by its bf16 low parts (cols, K); y = hi*hi + hi*lo +
+ *   lo*hi on tensor cores (about 1e-5 relative to sum |x||w|).
  * Rows (ldx, ldy) must be 16-byte pitched for the tensor-core precisions.
  */
 #define F2S_PRECISION_FP32 0
 #define F2S_PRECISION_TF32 1
 #define F2S_PRECISION_BF16 2
 /* Operands split as x = hi + lo (both bf16) and contracted as
- * hi*hi + hi*lo + lo*hi on tensor cores: close to fp32 accuracy. Accepted by
- * the model's encoder_precision only. */
+ * hi*hi + hi*lo + lo*hi on tensor cores: close to fp32 accuracy. The model's
+ * encoder_precision (edge contraction, content and head GEMMs) and
+ * f2s_linear. */
 #define F2S_PRECISION_BF16X3 3
 /* Trunk only: tf32 tensor cores as F2S_PRECISION_TF32, but the FFN input and
  * hidden rows stay fp32 (F2S_PRECISION_TF32 stores them as fp16, which

@@ -40,9 +40,6 @@ struct GemmArgs {
     bool fp16_operands;
     const void* W16;
     const void* W2_16;     // fp16 copy of W2 (SwiGLU)
-    // F2S_PRECISION_BF16X3: A already split (A = tf32 high parts, A_lo the
-    // remainders, both with leading dimension lda); null to split here
-    const float* A_lo;
 };
 int gemm_f32(const GemmArgs& args, cudaStream_t stream);
 
@@ -56,6 +53,8 @@ struct TcGemmOp {
     const void* W2;          // SwiGLU value weights (cols x K)
     const void* A_lo;        // 3xTF32: low parts of A (rows x K, lda) and W (cols x K);
     const void* W_lo;        //   A and W then hold the tf32-rounded high parts
+    bool split_in;           // split bf16: A is fp32 (split into bf16 high and low parts
+                             //   in shared memory), W / W_lo the bf16 parts of the weights
     const float* bias;
     const float* bias2;
     void* Y;
@@ -77,6 +76,9 @@ int tc_gemm(const TcGemmOp& op, cudaStream_t stream);
 // hi = x rounded to the nearest tf32, lo = x - hi; hi and lo are (rows, K)
 // with leading dimension K: the operand split of the 3xTF32 GEMM.
 int split_tf32(const float* x, int ldx, int rows, int K, float* hi, float* lo, cudaStream_t stream);
+// hi = bf16(x), lo = bf16(x - hi) (round to nearest), (rows, K) each with
+// leading dimension K: the weight split of the split-bf16 GEMM.
+int split_bf16(const float* x, int ldx, int rows, int K, void* hi, void* lo, cudaStream_t stream);
 // N tile with the least padding for `cols` output columns.
 int tc_pick_bn(int cols, bool swiglu);
 

@@ -1,6 +1,7 @@
 // Flow2SurfNet forward (flow2surf/models/network.py:75-82) as a sequence of
 // sm_100a kernels over point-major activations, plus the parameter-blob and
 // workspace layouts and the operator entry points that share its kernels.
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
 #include <cfloat>
@@ -189,9 +190,7 @@ Layout make_layout(const Dims& d) {
 struct Workspace {
     float *xyz4, *feat0, *content, *cat, *x, *h, *qkv, *colstats, *offs, *ffh, *dec0, *dec1;
     float *cond, *mod, *attn;
-    float *split_a, *split_w;  // 3xTF32 operand halves (split-bf16 encoder only)
-    // split-bf16 encoder: feat0 holds tf32 high parts, feat0_lo the remainders
-    float* feat0_lo;
+    float* split_w;  // split-bf16 encoder: bf16 high and low parts of a GEMM's weights
     // tf32 trunk: the FFN input (w.h after the second modulation) and hidden
     // rows (w.ffh) are fp16, and the FFN GEMMs read fp16 copies of their
     // weights made at the start of every forward: per block gate, value
@@ -227,9 +226,7 @@ Workspace carve(const Dims& d, int B, int M, char* base) {
     w.mod = (float*)take((size_t)B * (d.NB > 0 ? d.NB : 1) * 6 * d.C);
     w.attn = (float*)take((size_t)attention_tc_workspace_floats(B, M, d.C));
     const bool split = d.enc_gemm_precision == F2S_PRECISION_BF16X3;
-    w.split_a = split ? (float*)take(R * 2 * d.max_gemm_in) : nullptr;
-    w.split_w = split ? (float*)take((size_t)2 * d.max_gemm_w) : nullptr;
-    w.feat0_lo = split ? (float*)take(R * d.sd[0]) : nullptr;
+    w.split_w = split ? (float*)take((size_t)d.max_gemm_w) : nullptr;  // 2 x bf16 per weight
     const bool tf32_trunk = trunk_on_tensor_cores(d.precision);
     w.ffn_w16 = tf32_trunk ? (__half*)take(((size_t)(d.NB > 0 ? d.NB : 1) * 3 * d.C * d.Hf + 1) / 2)
                            : nullptr;
@@ -469,37 +466,28 @@ GemmArgs gemm_args(const float* A, int lda, const float* W, const float* bias, f
 
 // One dense contraction of the forward at the configured precision: the fp32
 // CUDA-core kernel, the tcgen05 kernel reading the fp32 operands as tf32, or
-// (F2S_PRECISION_BF16X3 here) the 3xTF32 tcgen05 kernel on operands split
-// into split_a (2 x rows x K floats) and split_w (2 x cols x K).
-int linear_op(const GemmArgs& g, int precision, cudaStream_t st, float* split_a = nullptr,
-              float* split_w = nullptr) {
+// (F2S_PRECISION_BF16X3 here) the split-bf16 tcgen05 kernel, which splits the
+// fp32 A rows into bf16 high and low parts in shared memory; the weights'
+// parts are made here into split_w (2 x cols x K bf16).
+int linear_op(const GemmArgs& g, int precision, cudaStream_t st, void* split_w = nullptr) {
     if (precision == F2S_PRECISION_FP32) return gemm_f32(g, st);
     if (precision == F2S_PRECISION_BF16X3) {
-        // the split operands are K-contiguous; TMA rows need 16-byte pitches
-        if (g.K % 4 != 0 || g.epilogue != kEpiStore || !split_a || !split_w) {
-            if (g.A_lo) return fail(F2S_ERR_INVALID_ARGUMENT, "pre-split operand on the fp32 path");
+        // fp32 A rows and bf16 weight rows by TMA: 16-byte pitches and base
+        if (g.K % 8 != 0 || g.lda % 4 != 0 || ((uintptr_t)g.A & 15) != 0 ||
+            g.epilogue != kEpiStore || !split_w)
             return gemm_f32(g, st);
-        }
-        const float* a_hi = g.A_lo ? g.A : split_a;
-        const float* a_lo = g.A_lo ? g.A_lo : split_a + (size_t)g.rows * g.K;
-        float* w_hi = split_w;
-        float* w_lo = split_w + (size_t)g.cols * g.K;
-        if (!g.A_lo) {
-            TraceScope trace(g.tag, st);
-            F2S_TRY(split_tf32(g.A, g.lda, g.rows, g.K, split_a, split_a + (size_t)g.rows * g.K, st));
-        } else if (g.lda % 4 != 0 || ((uintptr_t)g.A & 15) != 0 || ((uintptr_t)g.A_lo & 15) != 0) {
-            return fail(F2S_ERR_INVALID_ARGUMENT, "pre-split operand rows must be 16-byte aligned");
-        }
+        __nv_bfloat16* w_hi = static_cast<__nv_bfloat16*>(split_w);
+        __nv_bfloat16* w_lo = w_hi + (size_t)g.cols * g.K;
         {
             TraceScope trace(g.tag, st);
-            F2S_TRY(split_tf32(g.W, g.K, g.cols, g.K, w_hi, w_lo, st));
+            F2S_TRY(split_bf16(g.W, g.K, g.cols, g.K, w_hi, w_lo, st));
         }
         TcGemmOp op{};
-        op.A = a_hi;
-        op.A_lo = a_lo;
-        op.lda = g.A_lo ? g.lda : g.K;
+        op.A = g.A;
+        op.lda = g.lda;
         op.W = w_hi;
         op.W_lo = w_lo;
+        op.split_in = true;
         op.bias = g.bias;
         op.Y = g.Y;
         op.ldy = g.ldy;
@@ -507,8 +495,10 @@ int linear_op(const GemmArgs& g, int precision, cudaStream_t st, float* split_a 
         op.rows = g.rows;
         op.cols = g.cols;
         op.K = g.K;
-        op.bn = tc_pick_bn(g.cols, true);  // N tile <= 128: two stages of four operand tiles fit
-        op.tf32 = true;
+        // N tiles up to 192: two stages of fp32 A (32 KB) and the W parts fit
+        op.bn = tc_pick_bn(g.cols, false);
+        if (op.bn > 192) op.bn = tc_pick_bn(g.cols, true);
+        op.tf32 = false;
         op.epilogue = kEpiStore;
         op.tag = g.tag;
         return tc_gemm(op, st);
@@ -589,7 +579,7 @@ int forward(const Dims& d, const Layout& L, const float* P, const float* x_in, c
                                               (int)smem));
             kernel<<<grid, 256, smem, st>>>(x_in, B, M, P + L.in_w, P + L.in_b, P + L.in_ln_w,
                                             P + L.in_ln_b, P + L.in_out_w, P + L.in_out_b, S0,
-                                            w.xyz4, w.feat0, w.feat0_lo);
+                                            w.xyz4, w.feat0, nullptr);
             return check_launch("input_embed_lane_kernel");
         };
         if (S0 <= 16) F2S_TRY(launch(input_embed_lane_kernel<16>, 16));
@@ -609,21 +599,17 @@ int forward(const Dims& d, const Layout& L, const float* P, const float* x_in, c
         F2S_TRY(check_launch("input_embed_kernel"));
     }
     F2S_TRY(knn_launch(x_in, B, 3, M, d.K, w.idx, st));
-    // neighbour stages; with the split encoder the first stage's input
-    // arrives already split (fin = tf32 high parts, fin_lo = remainders); the
-    // edge stages write plain fp32 rows (a second output there costs the
-    // register-bound edge kernel more than the split kernel it saves)
+    // neighbour stages (the split encoder's GEMMs split their fp32 inputs
+    // into bf16 parts in shared memory)
     int col = 0;
     const float* fin = w.feat0;
-    const float* fin_lo = d.sd[0] <= 64 ? w.feat0_lo : nullptr;
     int ldin = d.sd[0];
     for (int s = 0; s < d.S; ++s) {
         const StageParams& sp = L.stage[s];
         const int cin = d.si[s], cout = d.sd[s];
         GemmArgs gc = gemm_args(fin, ldin, P + sp.content_w, nullptr, w.content, 2 * cout, R,
                                 2 * cout, cin);  // tag: gemm_content
-        gc.A_lo = fin_lo;
-        F2S_TRY(linear_op(gc, d.enc_gemm_precision, st, w.split_a, w.split_w));
+        F2S_TRY(linear_op(gc, d.enc_gemm_precision, st, w.split_w));
         EdgeArgs ea{};
         ea.content = w.content;
         ea.ldc = 2 * cout;
@@ -652,7 +638,6 @@ int forward(const Dims& d, const Layout& L, const float* P, const float* x_in, c
         if (edge_status == F2S_ERR_UNSUPPORTED) edge_status = edge_stage_f32(ea, st);
         F2S_TRY(edge_status);
         fin = w.cat + col;
-        fin_lo = nullptr;
         ldin = d.sum_stage;
         col += cout;
     }
@@ -661,7 +646,7 @@ int forward(const Dims& d, const Layout& L, const float* P, const float* x_in, c
         GemmArgs g = gemm_args(w.cat, d.sum_stage, P + L.proj_w, nullptr, w.x, C, R, C,
                                d.sum_stage);
         g.tag = kTagGemmHead;
-        F2S_TRY(linear_op(g, d.enc_gemm_precision, st, w.split_a, w.split_w));
+        F2S_TRY(linear_op(g, d.enc_gemm_precision, st, w.split_w));
     }
     F2S_TRY(ln_affine_leaky(w.x, C, P + L.proj_ln_w, P + L.proj_ln_b, R, C, false, st));
     F2S_TRY(trunk(d, L, P, B, M, w.x, w, st));

@@ -18,6 +18,7 @@
 // Operands are bf16 (kind::f16) or fp32 read as tf32 (kind::tf32), or
 // (3xTF32) pairs x = hi + lo of tf32 values with the products hi*hi + hi*lo +
 // lo*hi accumulated, which leaves only the lo*lo term (2^-22 relative) out.
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
 #include <mutex>
@@ -133,17 +134,31 @@ __device__ __forceinline__ void load_cols32(const float* v, int col0, int cols, 
     }
 }
 
-// kSplit (with kTf32): map_a2 / map_b2 hold the low parts of A / W.
+// Threads of one CTA: TMA producer and MMA warps, kEW epilogue warps, and for
+// the split-bf16 form four operand-split warps.
+template <bool kTf32, bool kSplit, int kEW>
+constexpr int gemm_threads() {
+    return 64 + 32 * kEW + ((kSplit && !kTf32) ? 128 : 0);
+}
+
+// kSplit with kTf32 (3xTF32): map_a2 / map_b2 hold the low parts of A / W.
+// kSplit without kTf32 (split bf16): A is fp32, loaded by TMA as two 32-column
+// boxes per 64-column K block; four split warps turn each row of a stage into
+// its bf16 high and low parts in place (the row's 256 fp32 bytes become 128
+// bytes of each, in the same swizzled 128-byte slots of the two boxes, so a
+// thread only ever overwrites its own row); map_b / map_b2 hold the bf16
+// high and low parts of W; the MMA issues hi*hi + hi*lo + lo*hi.
 // kEW: epilogue warps, 8, or 16 for the SwiGLU epilogue with fp16 rows (its
 // SiLU on the special-function unit needs four warps per SM sub-partition to
 // hide the latency of the exponential and reciprocal).
 template <bool kTf32, int kEpi, bool kSplit, int kEW = 8>
-__global__ void __launch_bounds__(64 + 32 * kEW, 1)
+__global__ void __launch_bounds__(gemm_threads<kTf32, kSplit, kEW>(), 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_a2,
                const __grid_constant__ CUtensorMap map_b, const __grid_constant__ CUtensorMap map_b2,
                const __grid_constant__ CUtensorMap map_y, const TcGemmArgs g) {
     constexpr bool kDual = kEpi == kEpiSwiGlu;
-    static_assert(!(kSplit && (kDual || !kTf32)), "3xTF32 runs the single-matrix tf32 form");
+    constexpr bool kSplitIn = kSplit && !kTf32;
+    static_assert(!(kSplit && (kDual || kEpi != kEpiStore)), "split forms: the plain epilogue");
     static_assert(kEW == 8 || (kEW == 16 && kDual), "16 epilogue warps: the SwiGLU form only");
     constexpr int kEpiThreads = 32 * kEW;
     extern __shared__ __align__(1024) unsigned char tc_smem_raw[];
@@ -167,7 +182,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     uint64_t* tempty = tfull + 2;     // [2]
     uint64_t* mma_done = tempty + 2;  // [1]
     uint64_t* b_full = mma_done + 1;  // [1] the resident W tiles
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(b_full + 1);
+    uint64_t* conv = b_full + 1;      // [S] split bf16: the stage's A split
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(conv + S);
     // per tile parity: set by the one polling epilogue lane when its wait
     // failed, read by every epilogue warp after their named barrier
     int* epi_fail = reinterpret_cast<int*>(tmem_slot + 1);  // [2]
@@ -200,6 +216,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         for (int s = 0; s < S; ++s) {
             tc::mbar_init(&full[s], 1);
             tc::mbar_init(&empty[s], 1);
+            if (kSplitIn) tc::mbar_init(&conv[s], 128);
         }
         for (int b = 0; b < 2; ++b) {
             tc::mbar_init(&tfull[b], 1);
@@ -252,8 +269,13 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                     unsigned char* st = smem + (size_t)stage * stage_bytes;
                     tc::mbar_arrive_expect_tx(&full[stage], stage_bytes);
                     const int k0 = kb * (kTf32 ? 32 : 64);
-                    tc::tma_load_2d(st, &map_a, &full[stage], k0, m0);
-                    if (kSplit) tc::tma_load_2d(st + a_bytes, &map_a2, &full[stage], k0, m0);
+                    if constexpr (kSplitIn) {  // fp32 A: two boxes of 32 columns
+                        tc::tma_load_2d(st, &map_a, &full[stage], k0, m0);
+                        tc::tma_load_2d(st + a_bytes, &map_a, &full[stage], k0 + 32, m0);
+                    } else {
+                        tc::tma_load_2d(st, &map_a, &full[stage], k0, m0);
+                        if (kSplit) tc::tma_load_2d(st + a_bytes, &map_a2, &full[stage], k0, m0);
+                    }
                     if (!g.b_res) {
                         tc::tma_load_2d(st + a_stage, &map_b, &full[stage], k0, n0);
                         if (kDual || kSplit)
@@ -295,7 +317,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                 tc::tc_fence_after();
                 const uint32_t d = tmem_base + (uint32_t)(buf * g.acc_cols);
                 for (int kb = 0; kb < g.k_blocks; ++kb) {
-                    if (!tc::mbar_wait(&full[stage], phase, g.err)) {
+                    if (!tc::mbar_wait(&full[stage], phase, g.err) ||
+                        (kSplitIn && !tc::mbar_wait_poll(&conv[stage], phase, g.err))) {
                         ok = false;
                         break;
                     }
@@ -334,6 +357,59 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             tc::mbar_drain(mma_done, 0);
         }
         __syncwarp();
+    } else if (kSplitIn && warp >= 2 + kEW) {
+        // ---------------- operand split (warps 2 + kEW .. 5 + kEW) ----------------
+        // thread = row of the A tile: the row's 64 fp32 values of the stage
+        // (two boxes, 128-byte swizzle) are read, then its bf16 high parts are
+        // written over the first box's row and the low parts over the second's
+        const int r = (int)threadIdx.x - (64 + kEpiThreads);
+        int stage = 0;
+        uint32_t phase = 0;
+        bool ok = true;
+        for (int i = 0; ok; ++i) {
+            int m0, n0;
+            if (!tile_at(i, m0, n0)) break;
+            for (int kb = 0; kb < g.k_blocks; ++kb) {
+                int landed = 1;
+                if (lane == 0) landed = tc::mbar_wait_poll(&full[stage], phase, g.err) ? 1 : 0;
+                if (!__shfl_sync(0xffffffffu, landed, 0)) {
+                    ok = false;
+                    break;
+                }
+                unsigned char* st = smem + (size_t)stage * stage_bytes;
+                float4 x[16];  // x[q] = K columns 4q .. 4q + 3 of the block
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    x[c] = *reinterpret_cast<const float4*>(st + sw128_offset(r, c));
+                    x[8 + c] = *reinterpret_cast<const float4*>(st + a_bytes + sw128_offset(r, c));
+                }
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {  // bf16 chunk c: K columns 8c .. 8c + 7
+                    const float v[8] = {x[2 * c].x,     x[2 * c].y,     x[2 * c].z,     x[2 * c].w,
+                                        x[2 * c + 1].x, x[2 * c + 1].y, x[2 * c + 1].z, x[2 * c + 1].w};
+                    uint32_t h[4], l[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const __nv_bfloat162 hb = __floats2bfloat162_rn(v[2 * e], v[2 * e + 1]);
+                        const float2 hf = __bfloat1622float2(hb);
+                        const __nv_bfloat162 lb =
+                            __floats2bfloat162_rn(v[2 * e] - hf.x, v[2 * e + 1] - hf.y);
+                        h[e] = *reinterpret_cast<const uint32_t*>(&hb);
+                        l[e] = *reinterpret_cast<const uint32_t*>(&lb);
+                    }
+                    *reinterpret_cast<uint4*>(st + sw128_offset(r, c)) = make_uint4(h[0], h[1], h[2], h[3]);
+                    *reinterpret_cast<uint4*>(st + a_bytes + sw128_offset(r, c)) =
+                        make_uint4(l[0], l[1], l[2], l[3]);
+                }
+                // the parts are read by the tensor cores (async proxy)
+                fence_proxy_async_shared();
+                tc::mbar_arrive(&conv[stage]);
+                if (++stage == S) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
+            }
+        }
     } else {
         // ---------------- epilogue (warps 2 .. 1 + kEW) ----------------
         // kEW / 4 warps per TMEM lane quarter, taking alternate 32-column chunks
@@ -585,7 +661,7 @@ int launch_tc(const CUtensorMap& ma, const CUtensorMap& ma2, const CUtensorMap& 
               int grid, cudaStream_t st) {
     auto kernel = tc_gemm_kernel<kTf32, kEpi, kSplit, kEW>;
     F2S_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    kernel<<<grid, 64 + 32 * kEW, smem, st>>>(ma, ma2, mb, mb2, my, g);
+    kernel<<<grid, gemm_threads<kTf32, kSplit, kEW>(), smem, st>>>(ma, ma2, mb, mb2, my, g);
     return check_launch("tc_gemm_kernel");
 }
 
@@ -673,9 +749,14 @@ int tc_gemm(const TcGemmOp& op, cudaStream_t st) {
     F2S_REQUIRE(op.A && op.W && op.Y && op.K > 0, "tc_gemm: bad operands");
     const bool dual = op.epilogue == kEpiSwiGlu;
     const bool split = op.A_lo != nullptr;
+    const bool split_in = op.split_in;
     F2S_REQUIRE(!dual || op.W2, "tc_gemm: SwiGLU needs W2");
-    F2S_REQUIRE(!split || (op.W_lo && op.tf32 && op.epilogue == kEpiStore),
+    F2S_REQUIRE(!split || (op.W_lo && op.tf32 && op.epilogue == kEpiStore && !split_in),
                 "tc_gemm: 3xTF32 needs W_lo, tf32 operands and the plain epilogue");
+    F2S_REQUIRE(!split_in || (op.W_lo && !op.tf32 && !op.fp16 && op.epilogue == kEpiStore &&
+                              op.lda % 4 == 0 && ((uintptr_t)op.A & 15) == 0),
+                "tc_gemm: split bf16 needs fp32 A rows of 16-byte pitch, W / W_lo in bf16 and "
+                "the plain epilogue");
     F2S_REQUIRE(op.epilogue != kEpiGatedResidual || (op.gate && op.rows_per_patch > 0 && !op.y_bf16),
                 "tc_gemm: gated residual needs a gate and an fp32 output");
     int bn = op.bn;
@@ -688,10 +769,13 @@ int tc_gemm(const TcGemmOp& op, cudaStream_t st) {
     CUtensorMap ma, ma2, mb, mb2;
     const int bk = op.tf32 ? 32 : 64;
     const TmaType ot = op.tf32 ? kTmaF32 : op.fp16 ? kTmaF16 : kTmaBF16;
-    F2S_TRY(make_tensor_map_2d_typed(&ma, op.A, ot, 128, op.rows, op.K, op.lda, kTileM, bk));
+    // split bf16: fp32 A in boxes of 32 columns (two per 64-column K block)
+    if (split_in) F2S_TRY(make_tensor_map_2d_typed(&ma, op.A, kTmaF32, 128, op.rows, op.K, op.lda, kTileM, 32));
+    else F2S_TRY(make_tensor_map_2d_typed(&ma, op.A, ot, 128, op.rows, op.K, op.lda, kTileM, bk));
     F2S_TRY(make_tensor_map_2d_typed(&mb, op.W, ot, 128, op.cols, op.K, op.K, bn, bk));
     if (dual) F2S_TRY(make_tensor_map_2d_typed(&mb2, op.W2, ot, 128, op.cols, op.K, op.K, bn, bk));
     else if (split) F2S_TRY(make_tensor_map_2d(&mb2, op.W_lo, true, op.cols, op.K, op.K, bn, bk));
+    else if (split_in) F2S_TRY(make_tensor_map_2d_typed(&mb2, op.W_lo, kTmaBF16, 128, op.cols, op.K, op.K, bn, bk));
     else mb2 = mb;
     if (split) F2S_TRY(make_tensor_map_2d(&ma2, op.A_lo, true, op.rows, op.K, op.lda, kTileM, bk));
     else ma2 = ma;
@@ -731,8 +815,8 @@ int tc_gemm(const TcGemmOp& op, cudaStream_t st) {
         F2S_TRY(make_tensor_map_2d_typed(&my, op.Y, op.y_fp16 ? kTmaF16 : kTmaF32, op.y_fp16 ? 64 : 128,
                                          op.rows, op.cols, op.ldy, 32, 32));
     else my = ma;
-    const size_t a_stage_bytes = (size_t)kTileM * 128 * (split ? 2 : 1);
-    const size_t b_stage_bytes = (size_t)bn * 128 * ((dual || split) ? 2 : 1);
+    const size_t a_stage_bytes = (size_t)kTileM * 128 * ((split || split_in) ? 2 : 1);
+    const size_t b_stage_bytes = (size_t)bn * 128 * ((dual || split || split_in) ? 2 : 1);
     // epilogue region: the TMA path's two 4 KB boxes per warp, or the
     // transposing path's 32 x 33 buffers
     // SwiGLU into fp16 rows runs 16 epilogue warps with 2 KB boxes
@@ -767,6 +851,7 @@ int tc_gemm(const TcGemmOp& op, cudaStream_t st) {
     const int grid = g.b_res ? n_tiles_n * groups : (tiles < sms ? tiles : sms);
     TraceScope trace(op.tag, st);
     if (split) return launch_tc<true, kEpiStore, true>(ma, ma2, mb, mb2, my, g, smem, grid, st);
+    if (split_in) return launch_tc<false, kEpiStore, true>(ma, ma2, mb, mb2, my, g, smem, grid, st);
     if (op.tf32) {
         switch (op.epilogue) {
             case kEpiStore: return launch_tc<true, kEpiStore>(ma, ma2, mb, mb2, my, g, smem, grid, st);
@@ -817,6 +902,33 @@ __global__ void split_tf32_x4_kernel(const float4* __restrict__ x, int ldx4, int
     }
 }
 }  // namespace
+
+namespace {
+// hi = bf16(x), lo = bf16(x - hi), both (rows, K) with leading dimension K.
+__global__ void split_bf16_kernel(const float* __restrict__ x, int ldx, int rows, int K,
+                                  __nv_bfloat16* __restrict__ hi, __nv_bfloat16* __restrict__ lo) {
+    const int64_t total = (int64_t)rows * K;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = i / K, c = i - r * K;
+        const float v = x[r * ldx + c];
+        const __nv_bfloat16 h = __float2bfloat16_rn(v);
+        hi[i] = h;
+        lo[i] = __float2bfloat16_rn(v - __bfloat162float(h));
+    }
+}
+}  // namespace
+
+int split_bf16(const float* x, int ldx, int rows, int K, void* hi, void* lo, cudaStream_t st) {
+    if (rows == 0 || K == 0) return F2S_OK;
+    const int64_t total = (int64_t)rows * K;
+    const int64_t cap = (int64_t)sm_count() * 16;
+    int64_t blocks = (total + 255) / 256;
+    blocks = blocks < cap ? blocks : cap;
+    split_bf16_kernel<<<(int)blocks, 256, 0, st>>>(x, ldx, rows, K, static_cast<__nv_bfloat16*>(hi),
+                                                   static_cast<__nv_bfloat16*>(lo));
+    return check_launch("split_bf16_kernel");
+}
 
 int split_tf32(const float* x, int ldx, int rows, int K, float* hi, float* lo, cudaStream_t st) {
     if (rows == 0 || K == 0) return F2S_OK;
@@ -888,12 +1000,18 @@ extern "C" int f2s_linear(const void* x, int ldx, const void* weight, const floa
         g.tag = f2s::kTagGemmContent;
         return f2s::gemm_f32(g, st);
     }
-    F2S_REQUIRE(precision == F2S_PRECISION_TF32 || precision == F2S_PRECISION_BF16,
+    F2S_REQUIRE(precision == F2S_PRECISION_TF32 || precision == F2S_PRECISION_BF16 ||
+                    precision == F2S_PRECISION_BF16X3,
                 "linear: unknown precision %d", precision);
     f2s::TcGemmOp op{};
     op.A = x;
     op.lda = ldx;
     op.W = weight;
+    if (precision == F2S_PRECISION_BF16X3) {
+        // fp32 x split in the kernel; weight = bf16 high parts then low parts
+        op.split_in = true;
+        op.W_lo = static_cast<const __nv_bfloat16*>(weight) + (size_t)cols * K;
+    }
     op.bias = bias;
     op.Y = y;
     op.ldy = ldy;
@@ -901,6 +1019,7 @@ extern "C" int f2s_linear(const void* x, int ldx, const void* weight, const floa
     op.cols = cols;
     op.K = K;
     op.bn = f2s::tc_pick_bn(cols, false);
+    if (op.split_in && op.bn > 192) op.bn = f2s::tc_pick_bn(cols, true);
     op.tf32 = precision == F2S_PRECISION_TF32;
     op.epilogue = f2s::kEpiStore;
     op.rows_per_patch = 1;

@@ -328,11 +328,14 @@ class Flow2SurfNet:
         if out.numel() == 0:
             return out
         self.forward_into(x_alpha, alpha, out)
-        if self.precision == "tf32":
+        status = _lib.read_device_error()
+        if status == _lib.F2S_FP16_RANGE and self.precision == "tf32":
             # fp16 FFN rows out of range: the same forward with fp32 rows
-            if _lib.read_device_error() == _lib.F2S_FP16_RANGE:
-                self.wide_ffn().forward_into(x_alpha, alpha, out)
-                _lib.check_device_error()
+            self.wide_ffn().forward_into(x_alpha, alpha, out)
+            status = _lib.read_device_error()
+        if status:  # a bounded wait that ran out (or a range error outside tf32)
+            raise _lib.Flow2SurfError(_lib.F2S_ERR_CUDA, "device error %d: %s" % (
+                status, _lib.DEVICE_ERRORS.get(status, "unknown")))
         return out
 
     execute = __call__

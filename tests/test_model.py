@@ -215,3 +215,12 @@ def test_bounded_wait_that_runs_out_is_reported(cuda):
     v = gpu_forward(DEFAULT_CONFIG, params, x, alpha, precision="tf32", encoder_precision="bf16x3")
     _lib.check_device_error()
     assert np.isfinite(v).all()
+    # a forward during which the word is set (here: set just before it) is
+    # reported by the model call, not returned; the read clears the word
+    model = build_model(DEFAULT_CONFIG, precision="tf32", encoder_precision="bf16x3")
+    model.load_parameters(params)
+    xt, at = torch.from_numpy(x).cuda(), torch.from_numpy(alpha).cuda()
+    _lib.call("f2s_selftest_wait_timeout", 4096, _lib.stream_handle())
+    with pytest.raises(_lib.Flow2SurfError, match="device error 1"):
+        model(xt, at)
+    np.testing.assert_array_equal(model(xt, at).cpu().numpy(), v)

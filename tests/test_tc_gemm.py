@@ -13,12 +13,12 @@ from flow2surf_b200 import _lib
 
 pytestmark = pytest.mark.gpu
 
-PRECISION = {"fp32": 0, "tf32": 1, "bf16": 2}
+PRECISION = {"fp32": 0, "tf32": 1, "bf16": 2, "bf16x3": 3}
 
 
 def linear(x, w, b, precision):
     rows, K = x.shape
-    cols = w.shape[0]
+    cols = w.shape[0] // 2 if precision == "bf16x3" else w.shape[0]  # bf16x3: hi then lo
     y = torch.empty((rows, cols), dtype=torch.float32, device="cuda")
     _lib.call("f2s_linear", x.data_ptr(), x.stride(0), w.data_ptr(),
               b.data_ptr() if b is not None else None, y.data_ptr(), y.stride(0), rows, cols, K,
@@ -33,7 +33,7 @@ def device_error():
     return v.value
 
 
-@pytest.mark.parametrize("precision", ["bf16", "tf32", "fp32"])
+@pytest.mark.parametrize("precision", ["bf16", "tf32", "fp32", "bf16x3"])
 @pytest.mark.parametrize("rows,cols,K", [(1000, 288, 192), (300, 192, 1536), (129, 3, 64),
                                          (5000, 128, 64), (1024, 1536, 192), (257, 384, 128),
                                          (77, 100, 40), (20000, 288, 192), (20000, 1536, 192)])
@@ -51,6 +51,15 @@ def test_linear_matches_float64(cuda, precision, rows, cols, K):
         xd, wd = x.to(torch.bfloat16), w.to(torch.bfloat16)
         ref = xd.double() @ wd.double().T + b.double()
         tol = 1e-5
+    elif precision == "bf16x3":
+        if K % 8:
+            pytest.skip("bf16 weight rows need a 16-byte pitch")
+        # fp32 x (split in the kernel); W as its bf16 high parts, then low parts
+        w_hi = w.to(torch.bfloat16)
+        w_lo = (w - w_hi.float()).to(torch.bfloat16)
+        xd, wd = x, torch.cat([w_hi, w_lo])
+        ref = x.double() @ w.double().T + b.double()
+        tol = 2e-5
     else:
         if precision == "tf32" and K % 4:
             pytest.skip("tf32 rows need a 16-byte pitch")
