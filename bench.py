@@ -61,7 +61,7 @@ def parse_args():
     p.add_argument("--impl", choices=["b200", "reference"], default="b200")
     p.add_argument("--points", type=int, default=50_000)
     p.add_argument("--seed-k", type=int, default=DENOISE["seed_k"])
-    p.add_argument("--cpu-sample-patches", type=int, default=10,
+    p.add_argument("--cpu-sample-patches", type=int, default=60,
                    help="patches of the cloud in the bounded CPU-baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-one-cloud", action="store_true",
