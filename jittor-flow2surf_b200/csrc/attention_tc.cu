@@ -33,14 +33,13 @@ namespace {
 
 constexpr int kRows = 128;        // keys (pass 1) / queries (pass 2) per CTA
 constexpr int kDPad = 64;         // padded q/k width: 64 bf16 = 128 bytes
-constexpr int kKeyTile = 64;      // keys per pass-2 tile
+constexpr int kKeyTile = 128;     // keys per pass-2 tile
 constexpr float kPScale = 32768.0f;  // 2^15: fp16 P = p * kPScale (p <= 1)
-constexpr int kKStages = 3;       // pass-2 K tiles in flight
 constexpr int kStatWarps = 8;     // pass 1: two statistics warps per TMEM lane quarter
 constexpr int kThreads = (kStatWarps + 1) * 32;  // pass 1: + one TMA / MMA warp
-// pass 2: warps 0-7 softmax / epilogue (two per TMEM lane quarter, one half of
-// each key tile and of the output columns each), warp 8 TMA + MMA
-constexpr int kOutWarps = 8;
+// pass 2: warps 0-15 softmax / epilogue (four per TMEM lane quarter, a
+// quarter of each key tile and of the output columns each), warp 16 TMA + MMA
+constexpr int kOutWarps = 16;
 constexpr int kOutThreads = (kOutWarps + 1) * 32;
 constexpr unsigned kFull = 0xffffffffu;
 
@@ -175,8 +174,9 @@ struct AttnArgs {
     int round_tf32;
     int vec4;           // pass 2: h / out rows 16-byte aligned
     int tma_epi;        // pass 2: h / out tiles by TMA (16-byte pitches and bases)
-    uint32_t idesc_s;   // bf16, M = 128, N = 128 (pass 1) / 64 (pass 2)
+    uint32_t idesc_s;   // bf16, M = 128, N = 128
     uint32_t idesc_pv;  // fp16 (kind::f16), M = 128, N = C
+    int k_stages;       // pass 2: K tiles in flight (2, or 1 where shared memory is short)
     int* err;
 };
 
@@ -347,8 +347,12 @@ attn_tc_colstats_kernel(const __grid_constant__ CUtensorMap map_hi,
 
 // ---------------------------------------------------------------------------
 // pass 2: out = h - (sum_j p_ij V_j) / (sum_j p_ij + 1e-9), p_ij = exp(S_ij - L_j)
-// Every hand-off of the per-key-tile chain S -> softmax -> P V sets the pace,
-// so its waits poll without the suspend hint (mbar_wait_poll).
+// Key tiles of 128: one S product (M = 128 queries, N = 128 keys) costs the
+// tensor pipe what one of 64 keys does, and each tile's S -> softmax -> P V
+// hand-off chain is paid half as often. S has one TMEM buffer (the next S is
+// issued as soon as every softmax thread has read the current one into
+// registers), P two. Every hand-off sets the pace, so its waits poll without
+// the suspend hint (mbar_wait_poll).
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(kOutThreads, 1)
 attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
@@ -362,47 +366,48 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
     unsigned char* smem = reinterpret_cast<unsigned char*>(
         (reinterpret_cast<uintptr_t>(attn_smem_raw) + 1023) & ~uintptr_t(1023));
     const int C = a.C;
+    const int KS = a.k_stages;                       // K tiles in flight (1 or 2)
     constexpr uint32_t kQBytes = kRows * 128;        // 128 queries x 64 bf16
-    constexpr uint32_t kKBytes = kKeyTile * 128;     // 64 keys x 64 bf16
-    const uint32_t v_bytes = (uint32_t)C * 128;      // one key tile of V^T: C rows x 64 fp16 keys
+    constexpr uint32_t kKBytes = kKeyTile * 128;     // 128 keys x 64 bf16
+    const uint32_t v_half = (uint32_t)C * 128;       // V^T of 64 keys: C rows x 64 fp16
+    const uint32_t v_bytes = 2 * v_half;             // V^T of one key tile
     unsigned char* sQ = smem;                                  // hi, lo
-    unsigned char* sK = sQ + 2 * kQBytes;                      // kKStages x (hi, lo)
-    unsigned char* sV = sK + 2 * kKStages * kKBytes;           // 2 stages (4 x v_bytes: the epilogue's h tile)
+    unsigned char* sK = sQ + 2 * kQBytes;                      // KS x (hi, lo)
+    unsigned char* sV = sK + 2 * KS * kKBytes;                 // 2 stages (= the epilogue's h tile)
     const int nk = (a.N + kKeyTile - 1) / kKeyTile;
-    // the patch's per-key log-sum-exp values times log2(e), nk * 64 of them
-    float* sL = reinterpret_cast<float*>(sV + 4 * v_bytes);
+    // the patch's per-key log-sum-exp values times log2(e), nk * 128 of them
+    float* sL = reinterpret_cast<float*>(sV + 2 * v_bytes);
     // softmax go / stop decisions: [0, 2) S ready, [2, 4) P free (by tile
     // parity), [4] output ready, [5] h tile landed; written by thread 0
     // before a named barrier
     int* sFlag = reinterpret_cast<int*>(sL + nk * kKeyTile);
-    float* sDen = reinterpret_cast<float*>(sFlag + 8);  // [2][128] partial row sums
+    float* sDen = reinterpret_cast<float*>(sFlag + 8);  // [4][128] partial row sums
     uint64_t* bars = reinterpret_cast<uint64_t*>(
-        (reinterpret_cast<uintptr_t>(sDen + 2 * kRows) + 7) & ~uintptr_t(7));
+        (reinterpret_cast<uintptr_t>(sDen + 4 * kRows) + 7) & ~uintptr_t(7));
     uint64_t* q_full = bars;        // [1]
-    uint64_t* k_full = bars + 1;    // [kKStages]
-    uint64_t* k_empty = bars + 4;   // [kKStages]
-    uint64_t* v_full = bars + 7;    // [2]
-    uint64_t* v_empty = bars + 9;   // [2]
-    uint64_t* s_full = bars + 11;   // [2]
-    uint64_t* s_empty = bars + 13;  // [2]  (128 arrivals)
-    uint64_t* p_full = bars + 15;   // [1]  (128 arrivals)
-    uint64_t* pv_done = bars + 16;  // [2]  by P buffer
-    uint64_t* done = bars + 18;     // [1]
-    uint64_t* h_full = bars + 19;   // [1]  epilogue: h tile
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
+    uint64_t* k_full = bars + 1;    // [2]
+    uint64_t* k_empty = bars + 3;   // [2]
+    uint64_t* v_full = bars + 5;    // [2]
+    uint64_t* v_empty = bars + 7;   // [2]
+    uint64_t* s_full = bars + 9;    // [1]
+    uint64_t* s_empty = bars + 10;  // [1]  (one arrival per softmax thread)
+    uint64_t* p_full = bars + 11;   // [1]  (one arrival per softmax thread)
+    uint64_t* pv_done = bars + 12;  // [2]  by P buffer
+    uint64_t* done = bars + 14;     // [1]
+    uint64_t* h_full = bars + 15;   // [1]  epilogue: h tile
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
 
     const int b = blockIdx.x / a.tiles;
     const int q0 = (blockIdx.x - b * a.tiles) * kRows;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    // TMEM: S double buffer at columns [0, 128), P (fp16, two keys per column:
-    // the P V product's A operand) double buffer at [128, 192), O at
-    // [256, 256 + C)
+    // TMEM: S at columns [0, 128), P (fp16, two keys per column: the P V
+    // product's A operand) double buffer at [128, 256), O at [256, 256 + C)
     constexpr uint32_t kPCol = 128;
     constexpr uint32_t kOCol = 256;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < 20; ++i)
-            tc::mbar_init(&bars[i], (i == 13 || i == 14 || i == 15) ? kOutWarps * 32 : 1);
+        for (int i = 0; i < 16; ++i)
+            tc::mbar_init(&bars[i], (i == 10 || i == 11) ? kOutWarps * 32 : 1);
         tc::fence_barrier_init();
     }
     if (warp == 0) tc::tmem_alloc(tmem_slot, 512);
@@ -414,57 +419,81 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
     if (warp == kOutWarps) {
         if (lane == 0) {
             bool ok = true;
-            // K tiles run kKStages deep and are refilled as soon as their S
-            // product completes; V tiles two deep, refilled once the P V
-            // product before the current one completes
+            // K tiles run KS deep, V tiles two deep; both are refilled while
+            // the softmax threads work on the current tile
             int k_issued = 0, k_landed = 0, v_issued = 0, v_landed = 0;
             auto load_k = [&](int i) {
-                const int ks = i % kKStages;
+                const int ks = i % KS;
                 tc::mbar_arrive_expect_tx(&k_full[ks], 2 * kKBytes);
                 tma_load_3d(sK + (2 * ks) * kKBytes, &map_khi, &k_full[ks], kDPad, i * kKeyTile, b);
                 tma_load_3d(sK + (2 * ks + 1) * kKBytes, &map_klo, &k_full[ks], kDPad, i * kKeyTile, b);
                 k_issued = i + 1;
             };
-            auto load_v = [&](int i) {
+            auto load_v = [&](int i) {  // two boxes of 64 keys
                 const int vs = i & 1;
                 tc::mbar_arrive_expect_tx(&v_full[vs], v_bytes);
                 tma_load_3d(sV + vs * v_bytes, &map_vt, &v_full[vs], i * kKeyTile, 0, b);
+                tma_load_3d(sV + vs * v_bytes + v_half, &map_vt, &v_full[vs], i * kKeyTile + 64, 0, b);
                 v_issued = i + 1;
             };
             tc::mbar_arrive_expect_tx(q_full, 2 * kQBytes);
             tma_load_3d(sQ, &map_qhi, q_full, 0, q0, b);
             tma_load_3d(sQ + kQBytes, &map_qlo, q_full, 0, q0, b);
-            for (int i = 0; i < kKStages && i < nk; ++i) load_k(i);
+            for (int i = 0; i < KS && i < nk; ++i) load_k(i);
             for (int i = 0; i < 2 && i < nk; ++i) load_v(i);
             ok = tc::mbar_wait_poll(q_full, 0, a.err);
             if (!ok) tc::mbar_drain(q_full, 0);
             const uint32_t q_hi = tc::smem_u32(sQ), q_lo = q_hi + kQBytes;
             auto issue_s = [&](int i) -> bool {
-                const int ks = i % kKStages;
-                if (!tc::mbar_wait_poll(&k_full[ks], (uint32_t)(i / kKStages) & 1u, a.err)) return false;
+                const int ks = i % KS;
+                if (!tc::mbar_wait_poll(&k_full[ks], (uint32_t)(i / KS) & 1u, a.err)) return false;
                 k_landed = i + 1;
-                const int s = i & 1;
-                if (!tc::mbar_wait_poll(&s_empty[s], ((uint32_t)(i >> 1) & 1u) ^ 1u, a.err)) return false;
+                // S_{i-1} has been read by every softmax thread
+                if (!tc::mbar_wait_poll(s_empty, ((uint32_t)i & 1u) ^ 1u, a.err)) return false;
                 tc::tc_fence_after();
                 const uint32_t k_hi = tc::smem_u32(sK + (2 * ks) * kKBytes), k_lo = k_hi + kKBytes;
-                const uint32_t d = tmem + (uint32_t)(s * 64);
 #pragma unroll
                 for (int kk = 0; kk < a.d_steps; ++kk) {  // 16 channels per MMA
                     const uint32_t o = kk * 32;
-                    tc::umma<false>(d, tc::sw128_desc(q_hi + o), tc::sw128_desc(k_hi + o), a.idesc_s,
+                    tc::umma<false>(tmem, tc::sw128_desc(q_hi + o), tc::sw128_desc(k_hi + o), a.idesc_s,
                                     kk ? 1u : 0u);
-                    tc::umma<false>(d, tc::sw128_desc(q_hi + o), tc::sw128_desc(k_lo + o), a.idesc_s, 1u);
-                    tc::umma<false>(d, tc::sw128_desc(q_lo + o), tc::sw128_desc(k_hi + o), a.idesc_s, 1u);
+                    tc::umma<false>(tmem, tc::sw128_desc(q_hi + o), tc::sw128_desc(k_lo + o), a.idesc_s, 1u);
+                    tc::umma<false>(tmem, tc::sw128_desc(q_lo + o), tc::sw128_desc(k_hi + o), a.idesc_s, 1u);
                 }
-                tc::umma_commit(&s_full[s]);
+                tc::umma_commit(s_full);
                 tc::umma_commit(&k_empty[ks]);
                 return true;
             };
             if (ok) ok = issue_s(0);
             for (int i = 0; i < nk && ok; ++i) {
-                if (i + 1 < nk && !issue_s(i + 1)) {
-                    ok = false;
-                    break;
+                if (i + 1 < nk) {
+                    if (KS == 1) {  // the one K stage: S_i is done with it
+                        if (!tc::mbar_wait_poll(&k_empty[0], (uint32_t)i & 1u, a.err)) {
+                            ok = false;
+                            break;
+                        }
+                        load_k(i + 1);
+                    }
+                    if (!issue_s(i + 1)) {
+                        ok = false;
+                        break;
+                    }
+                }
+                // S_i is done with its K stage: tile i + 2 goes there
+                if (KS == 2 && i + 2 < nk) {
+                    if (!tc::mbar_wait_poll(&k_empty[i & 1], (uint32_t)(i >> 1) & 1u, a.err)) {
+                        ok = false;
+                        break;
+                    }
+                    load_k(i + 2);
+                }
+                // P V_{i-1} is done with its V stage: tile i + 1 goes there
+                if (i >= 1 && i + 1 < nk) {
+                    if (!tc::mbar_wait_poll(&v_empty[(i - 1) & 1], (uint32_t)((i - 1) >> 1) & 1u, a.err)) {
+                        ok = false;
+                        break;
+                    }
+                    load_v(i + 1);
                 }
                 // P_i written by the softmax threads, V_i landed
                 if (!tc::mbar_wait_poll(p_full, (uint32_t)i & 1u, a.err) ||
@@ -477,34 +506,16 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
                 const uint32_t v0 = tc::smem_u32(sV + (i & 1) * v_bytes);
                 const uint32_t pa = tmem + kPCol + (uint32_t)((i & 1) * (kKeyTile / 2));
 #pragma unroll
-                for (int kk = 0; kk < 4; ++kk)  // 16 keys (8 TMEM columns, 32 bytes of V^T) per MMA
+                for (int kk = 0; kk < 8; ++kk)  // 16 keys (8 TMEM columns, 32 bytes of a V^T box) per MMA
                     tc::umma_tmem_a_f16(tmem + kOCol, pa + (uint32_t)(kk * 8),
-                                        tc::sw128_desc(v0 + kk * 32), a.idesc_pv,
-                                        (i | kk) ? 1u : 0u);
+                                        tc::sw128_desc(v0 + (uint32_t)(kk >> 2) * v_half + (kk & 3) * 32),
+                                        a.idesc_pv, (i | kk) ? 1u : 0u);
                 tc::umma_commit(&pv_done[i & 1]);
                 tc::umma_commit(&v_empty[i & 1]);
-                // S_i is done with its K tile (issued before P V_i, so waiting here
-                // never holds P V_i back): refill that stage with tile i + kKStages
-                if (i + kKStages < nk) {
-                    if (!tc::mbar_wait_poll(&k_empty[i % kKStages], (uint32_t)(i / kKStages) & 1u, a.err)) {
-                        ok = false;
-                        break;
-                    }
-                    load_k(i + kKStages);
-                }
-
-                // P V_{i-1} is done with its V tile: refill that stage with tile i + 1
-                if (i >= 1 && i + 1 < nk) {
-                    if (!tc::mbar_wait_poll(&v_empty[(i - 1) & 1], (uint32_t)((i - 1) >> 1) & 1u, a.err)) {
-                        ok = false;
-                        break;
-                    }
-                    load_v(i + 1);
-                }
             }
             // K / V copies still in flight land before the CTA exits
             for (int i = k_landed; i < k_issued; ++i)
-                tc::mbar_drain(&k_full[i % kKStages], (uint32_t)(i / kKStages) & 1u);
+                tc::mbar_drain(&k_full[i % KS], (uint32_t)(i / KS) & 1u);
             for (int i = v_landed; i < v_issued; ++i)
                 tc::mbar_drain(&v_full[i & 1], (uint32_t)(i >> 1) & 1u);
             tc::umma_commit(done);
@@ -512,23 +523,22 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
         }
         __syncwarp();
     } else {
-        // one thread per (query row, half of the key tile / output columns);
-        // thread 0 does every wait and publishes the outcome, so the eight
-        // softmax warps always take the same path
-        const int quarter = warp & 3, half = warp >> 2;
+        // one thread per (query row, quarter of the key tile / output
+        // columns); thread 0 does every wait and publishes the outcome, so
+        // the sixteen softmax warps always take the same path
+        const int quarter = warp & 3, qtr = warp >> 2;
         const int row = quarter * 32 + lane;
-        const int stid = threadIdx.x;  // 0 .. 255
+        const int stid = threadIdx.x;  // 0 .. 511
         const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
         constexpr float kLog2e = 1.44269504088896341f;
         for (int j = stid; j < nk * kKeyTile; j += kOutWarps * 32)
             sL[j] = j < a.N ? a.colstats[(size_t)b * a.N + j] * kLog2e : 0.0f;
         float den = 0.0f;
         bool ok = true;
-        const int k0 = half * 32;  // this thread's keys within a tile
+        const int k0 = qtr * 32;  // this thread's keys within a tile
         for (int i = 0; i < nk; ++i) {
             const int s = i & 1;
-            const uint32_t ph = (uint32_t)(i >> 1) & 1u;
-            if (stid == 0) sFlag[s] = tc::mbar_wait_poll(&s_full[s], ph, a.err) ? 1 : 0;
+            if (stid == 0) sFlag[s] = tc::mbar_wait_poll(s_full, (uint32_t)i & 1u, a.err) ? 1 : 0;
             named_sync_out();
             if (!sFlag[s]) {
                 ok = false;
@@ -536,11 +546,11 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
             }
             tc::tc_fence_after();
             float p[32];
-            tc::tmem_ld32(tmem + lane_base + (uint32_t)(s * 64 + k0), p);
+            tc::tmem_ld32(tmem + lane_base + (uint32_t)k0, p);
             tc::tc_fence_before();
-            tc::mbar_arrive(&s_empty[s]);
+            tc::mbar_arrive(s_empty);
             // p = exp(S - L) = 2^(S log2 e - L log2 e), computed while the
-            // previous tile's P V product may still run
+            // next S product and the previous P V product may run
             const int valid = min(kKeyTile, a.N - i * kKeyTile) - k0;
             const float* Lt = sL + i * kKeyTile + k0;
 #pragma unroll
@@ -583,18 +593,18 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
             tc::mbar_arrive(p_full);
         }
         // wait for the last P V product, then write h - O / (den + 1e-9); the
-        // row sum adds the two halves' partial sums
+        // row sum adds the four quarters' partial sums
         if (ok) {
-            sDen[half * kRows + row] = den;
+            sDen[qtr * kRows + row] = den;
             if (stid == 0)
                 sFlag[4] = tc::mbar_wait_poll(&pv_done[(nk - 1) & 1], (uint32_t)((nk - 1) >> 1) & 1u,
-                                         a.err) ? 1 : 0;
+                                              a.err) ? 1 : 0;
             named_sync_out();
             ok = sFlag[4] != 0;
-            den = sDen[row] + sDen[kRows + row];
+            den = (sDen[row] + sDen[kRows + row]) + (sDen[2 * kRows + row] + sDen[3 * kRows + row]);
         }
-        const int cw = C / 2;          // this thread's output columns [c_begin, c_begin + cw)
-        const int c_begin = half * cw;
+        const int cw = C / 4;          // this thread's output columns [c_begin, c_begin + cw)
+        const int c_begin = qtr * cw;  // (a multiple of 16)
         if (ok && a.tma_epi) {
             // the tile through shared memory: h (C / 32 boxes of 128 rows x
             // 32 floats, 128-byte swizzle) lands by TMA in the V buffers, which
@@ -618,19 +628,21 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
             if (go) {
                 tc::tc_fence_after();
                 const float inv = (1.0f / kPScale) / (den + 1e-9f);  // O holds 2^15 sum p v
-                for (int c0 = c_begin; c0 < c_begin + cw; c0 += 32) {
-                    float o[32];
-                    tc::tmem_ld32(tmem + lane_base + kOCol + (uint32_t)c0, o);
+                for (int c0 = c_begin; c0 < c_begin + cw; c0 += 16) {
+                    uint32_t o[16];
+                    tc::tmem_ld<16>(tmem + lane_base + kOCol + (uint32_t)c0, o);
                     unsigned char* box = sV + (c0 / 32) * kBox;
+                    const int ch0 = (c0 % 32) / 4;  // first 16-byte chunk of the row
 #pragma unroll
-                    for (int ch = 0; ch < 8; ++ch) {
-                        float4* cell = reinterpret_cast<float4*>(box + sw128_offset(row, ch));
+                    for (int ch = 0; ch < 4; ++ch) {
+                        float4* cell = reinterpret_cast<float4*>(box + sw128_offset(row, ch0 + ch));
                         const float4 hv = a.h ? *cell : make_float4(0.f, 0.f, 0.f, 0.f);
-                        const float* oc = o + ch * 4;
-                        float4 r = a.h ? make_float4(hv.x - oc[0] * inv, hv.y - oc[1] * inv,
-                                                     hv.z - oc[2] * inv, hv.w - oc[3] * inv)
-                                       : make_float4(oc[0] * inv, oc[1] * inv, oc[2] * inv,
-                                                     oc[3] * inv);
+                        const float o0 = __uint_as_float(o[4 * ch]) * inv;
+                        const float o1 = __uint_as_float(o[4 * ch + 1]) * inv;
+                        const float o2 = __uint_as_float(o[4 * ch + 2]) * inv;
+                        const float o3 = __uint_as_float(o[4 * ch + 3]) * inv;
+                        float4 r = a.h ? make_float4(hv.x - o0, hv.y - o1, hv.z - o2, hv.w - o3)
+                                       : make_float4(o0, o1, o2, o3);
                         if (a.round_tf32)
                             r = make_float4(f2s_round_tf32(r.x), f2s_round_tf32(r.y),
                                             f2s_round_tf32(r.z), f2s_round_tf32(r.w));
@@ -649,33 +661,15 @@ attn_tc_output_kernel(const __grid_constant__ CUtensorMap map_qhi,
             const float inv = (1.0f / kPScale) / (den + 1e-9f);  // O holds 2^15 sum p v
             const int qrow = q0 + row;
             const size_t grow = (size_t)b * a.N + qrow;
-            for (int c0 = c_begin; c0 < c_begin + cw; c0 += 32) {
-                float o[32];
-                tc::tmem_ld32(tmem + lane_base + kOCol + (uint32_t)c0, o);
+            for (int c0 = c_begin; c0 < c_begin + cw; c0 += 16) {
+                uint32_t o[16];
+                tc::tmem_ld<16>(tmem + lane_base + kOCol + (uint32_t)c0, o);
                 if (qrow < a.N) {
-                    if (a.vec4) {  // 16-byte rows: float4 loads and stores
-                        float* dst = a.out + grow * a.ldo + c0;
-                        const float* hr = a.h ? a.h + grow * a.ldh + c0 : nullptr;
 #pragma unroll
-                        for (int i = 0; i < 32; i += 4) {
-                            const float4 hv = hr ? *reinterpret_cast<const float4*>(hr + i)
-                                                 : make_float4(0.f, 0.f, 0.f, 0.f);
-                            float4 r = make_float4(hv.x - o[i] * inv, hv.y - o[i + 1] * inv,
-                                                   hv.z - o[i + 2] * inv, hv.w - o[i + 3] * inv);
-                            if (!hr) r = make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv,
-                                                     o[i + 3] * inv);
-                            if (a.round_tf32)
-                                r = make_float4(f2s_round_tf32(r.x), f2s_round_tf32(r.y),
-                                                f2s_round_tf32(r.z), f2s_round_tf32(r.w));
-                            *reinterpret_cast<float4*>(dst + i) = r;
-                        }
-                    } else {
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) {
-                            const float av = o[i] * inv;
-                            const float r = a.h ? a.h[grow * a.ldh + c0 + i] - av : av;
-                            a.out[grow * a.ldo + c0 + i] = a.round_tf32 ? f2s_round_tf32(r) : r;
-                        }
+                    for (int i = 0; i < 16; ++i) {
+                        const float av = __uint_as_float(o[i]) * inv;
+                        const float r = a.h ? a.h[grow * a.ldh + c0 + i] - av : av;
+                        a.out[grow * a.ldo + c0 + i] = a.round_tf32 ? f2s_round_tf32(r) : r;
                     }
                 }
             }
@@ -724,13 +718,13 @@ int attention_tc(const float* q, const float* k, int ldqk, const float* v, int l
     }
     CUtensorMap map_hi_q, map_lo_q, map_hi_k, map_lo_k, map_vt;
     const int64_t row_bytes = 2 * kDPad * 2;  // q and k halves: 256 bytes per point
-    // pass 1 reads 128-row boxes of both q and k; pass 2 reads 128-row q and 64-row k boxes
+    // 128-row boxes of q and k (both passes); V^T in boxes of 64 keys (128 bytes of fp16)
     F2S_TRY(make_tensor_map_3d(&map_hi_q, qk_hi, false, 2 * kDPad, N, B, row_bytes, row_bytes * N, kDPad, kRows));
     F2S_TRY(make_tensor_map_3d(&map_lo_q, qk_lo, false, 2 * kDPad, N, B, row_bytes, row_bytes * N, kDPad, kRows));
     F2S_TRY(make_tensor_map_3d(&map_hi_k, qk_hi, false, 2 * kDPad, N, B, row_bytes, row_bytes * N, kDPad, kKeyTile));
     F2S_TRY(make_tensor_map_3d(&map_lo_k, qk_lo, false, 2 * kDPad, N, B, row_bytes, row_bytes * N, kDPad, kKeyTile));
     F2S_TRY(make_tensor_map_3d_typed(&map_vt, vT, kTmaF16, N, C, B, (int64_t)n_pad * 2,
-                                     (int64_t)n_pad * 2 * C, kKeyTile, C));
+                                     (int64_t)n_pad * 2 * C, 64, C));
 
     AttnArgs a{};
     a.N = N;
@@ -773,9 +767,14 @@ int attention_tc(const float* q, const float* k, int ldqk, const float* v, int l
         a.tiles = ceil_div(N, kRows);
         a.idesc_s = tc::make_idesc(kRows, kKeyTile, 1u);
         a.idesc_pv = tc::make_idesc(kRows, C, 0u);
-        const size_t smem = 1024 + 2 * kRows * 128 + 2 * kKStages * kKeyTile * 128 + 4 * (size_t)C * 128 +
-                            (size_t)ceil_div(N, kKeyTile) * kKeyTile * 4 + 32 + 2 * kRows * 4 + 8 +
-                            20 * 8 + 16;
+        // alignment slack, Q, K stages, two V^T stages, log-sum-exp row,
+        // flags, partial row sums, barriers and the TMEM slot
+        auto smem_for = [&](int k_stages) -> size_t {
+            return 1024 + 2 * kRows * 128 + 2 * (size_t)k_stages * kKeyTile * 128 + 2 * (size_t)C * 256 +
+                   (size_t)ceil_div(N, kKeyTile) * kKeyTile * 4 + 32 + 4 * kRows * 4 + 8 + 16 * 8 + 16;
+        };
+        a.k_stages = smem_for(2) <= 227 * 1024 ? 2 : 1;
+        const size_t smem = smem_for(a.k_stages);
         F2S_LIMIT(smem <= 227 * 1024, "attention_tc: %zu bytes of shared memory", smem);
         F2S_CUDA_TRY(cudaFuncSetAttribute(attn_tc_output_kernel,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));

@@ -165,12 +165,15 @@ def attention_inputs(B, N, d, C, seed):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("B,N,d,C,sample", [(2, 1024, 48, 192, 2), (3, 100, 48, 192, 3),
-                                            (2, 257, 16, 64, 2), (512, 1024, 48, 192, 4)])
+                                            (2, 257, 16, 64, 2), (512, 1024, 48, 192, 4),
+                                            (2, 900, 48, 256, 2)])
 def test_offset_attention_tensor_cores(cuda, B, N, d, C, sample):
     """tcgen05 path of the operator (split-bf16 scores, fp16 P V): normwise
-    relative 2e-3 and max-abs 2e-3 of the largest output; the last case is the
-    trunk micro-benchmark's attention (512 patches x 1024 points, d 48, C 192),
-    a sample of its patches against the float64 oracle."""
+    relative 2e-3 and max-abs 2e-3 of the largest output; the fourth case is
+    the trunk micro-benchmark's attention (512 patches x 1024 points, d 48,
+    C 192), a sample of its patches against the float64 oracle. Key tiles are
+    128 wide: C = 256 leaves shared memory for one K stage only, and with
+    N = 900 the last tile's second 64-key V box lies wholly past N."""
     q, k, v = attention_inputs(B, N, d, C, seed=N + d)
     t = lambda a: torch.from_numpy(a).cuda()  # noqa: E731
     got = offset_attention_aggregate(t(q), t(k), t(v), precision="tensor").cpu().numpy()
