@@ -162,6 +162,13 @@ __global__ void v_transpose_kernel(const float* __restrict__ v, int ldv, int N, 
     if (out_of_range) atomicExch(err, tc::kTcFp16Range);
 }
 
+// Zero keys [N, n_pad) of every V^T row (a producer wrote keys [0, N)).
+__global__ void vt_pad_kernel(__half* __restrict__ vT, int rows, int N, int n_pad) {
+    const int pad = n_pad - N;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < rows * pad; i += gridDim.x * blockDim.x)
+        vT[(size_t)(i / pad) * n_pad + N + i % pad] = __float2half_rn(0.0f);
+}
+
 struct AttnArgs {
     int N, C, n_pad;
     int d_steps;      // 16-channel MMA steps covering the d real q/k channels (the padding is 0)
@@ -691,30 +698,48 @@ int attention_tc_workspace_floats(int B, int N, int C) {
     return B * N * 128 + (B * C * n_pad + 1) / 2 + B * N;
 }
 
-// q, k: (B*N rows, ldqk), width d (<= 64); v (ldv), width C (multiple of 32,
+bool attention_tc_supported(const float* q, const float* k, int ldqk, int d, int C) {
+    return d <= kDPad && C % 64 == 0 && C <= 256 && ldqk % 4 == 0 && ((uintptr_t)q & 15) == 0 &&
+           ((uintptr_t)k & 15) == 0;
+}
+
+__half* attention_tc_vt(float* workspace, int B, int N) {
+    return reinterpret_cast<__half*>(workspace + (size_t)B * N * 128);
+}
+
+// q, k: (B*N rows, ldqk), width d (<= 64); v (ldv), width C (multiple of 64,
 // <= 256); out = h - A (or A). workspace: attention_tc_workspace_floats floats.
+// vt_ready: V^T keys [0, N) are already in the workspace (attention_tc_vt),
+// written by the producer of v (v is then not read).
 int attention_tc(const float* q, const float* k, int ldqk, const float* v, int ldv,
                  const float* h, int ldh, float* out, int ldo, float* workspace, int B, int N,
-                 int d, int C, bool normalize_qk, bool round_tf32, cudaStream_t st) {
+                 int d, int C, bool normalize_qk, bool round_tf32, cudaStream_t st,
+                 bool vt_ready) {
     if (B == 0 || N == 0) return F2S_OK;
-    if (d > kDPad || C % 64 != 0 || C > 256 || ldqk % 4 != 0 ||
-        ((uintptr_t)q & 15) != 0 || ((uintptr_t)k & 15) != 0)
+    if (!attention_tc_supported(q, k, ldqk, d, C))
         return fail(F2S_ERR_UNSUPPORTED, "attention shape outside the tensor-core kernel");
     int* err = tc_error_word();
     if (!err) return fail(F2S_ERR_CUDA, "attention_tc: device error word unavailable");
     const int n_pad = (N + 7) & ~7;  // 16-byte fp16 rows of V^T
     __nv_bfloat16* qk_hi = reinterpret_cast<__nv_bfloat16*>(workspace);
     __nv_bfloat16* qk_lo = qk_hi + (size_t)B * N * 2 * kDPad;
-    __half* vT = reinterpret_cast<__half*>(workspace + (size_t)B * N * 128);
+    __half* vT = attention_tc_vt(workspace, B, N);
     float* colstats = workspace + (size_t)B * N * 128 + ((size_t)B * C * n_pad + 1) / 2;
     {
         TraceScope trace(kTagRowNorm, st);
         qk_split_kernel<<<ceil_div(B * N, 8), 256, 0, st>>>(q, k, ldqk, B * N, d, normalize_qk,
                                                              qk_hi, qk_lo);
         F2S_TRY(check_launch("qk_split_kernel"));
-        dim3 grid(ceil_div(n_pad, 64), ceil_div(C, 64), B);
-        v_transpose_kernel<<<grid, 256, 0, st>>>(v, ldv, N, C, n_pad, vT, err);
-        F2S_TRY(check_launch("v_transpose_kernel"));
+        if (!vt_ready) {
+            dim3 grid(ceil_div(n_pad, 64), ceil_div(C, 64), B);
+            v_transpose_kernel<<<grid, 256, 0, st>>>(v, ldv, N, C, n_pad, vT, err);
+            F2S_TRY(check_launch("v_transpose_kernel"));
+        } else if (n_pad > N) {
+            const int total = B * C * (n_pad - N);
+            vt_pad_kernel<<<ceil_div(total, 256) < 1024 ? ceil_div(total, 256) : 1024, 256, 0, st>>>(
+                vT, B * C, N, n_pad);
+            F2S_TRY(check_launch("vt_pad_kernel"));
+        }
     }
     CUtensorMap map_hi_q, map_lo_q, map_hi_k, map_lo_k, map_vt;
     const int64_t row_bytes = 2 * kDPad * 2;  // q and k halves: 256 bytes per point

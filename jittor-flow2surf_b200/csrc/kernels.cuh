@@ -1,6 +1,8 @@
 // Internal launch functions shared by the C-ABI translation units.
 #pragma once
 
+#include <cuda_fp16.h>
+
 #include "common.cuh"
 
 namespace f2s {
@@ -40,6 +42,13 @@ struct GemmArgs {
     bool fp16_operands;
     const void* W16;
     const void* W2_16;     // fp16 copy of W2 (SwiGLU)
+    // tensor-core plain-store path: output columns >= vt_col0 (a multiple of
+    // 32) are not stored in Y but, in fp16, transposed per patch of vt_M rows
+    // into vt (patch, column - vt_col0, row in patch) with row pitch vt_npad
+    // (the V^T operand of attention_tc); values outside the fp16 range set
+    // the device error word to 2
+    __half* vt;
+    int vt_col0, vt_C, vt_npad, vt_M;
 };
 int gemm_f32(const GemmArgs& args, cudaStream_t stream);
 
@@ -53,6 +62,8 @@ struct TcGemmOp {
     const void* W2;          // SwiGLU value weights (cols x K)
     const void* A_lo;        // 3xTF32: low parts of A (rows x K, lda) and W (cols x K);
     const void* W_lo;        //   A and W then hold the tf32-rounded high parts
+    __half* vt;              // as GemmArgs::vt (plain store, TMA epilogue)
+    int vt_col0, vt_C, vt_npad, vt_M;
     bool split_in;           // split bf16: A is fp32 (split into bf16 high and low parts
                              //   in shared memory), W / W_lo the bf16 parts of the weights
     const float* bias;
@@ -113,9 +124,15 @@ int attention_f32(const float* q, const float* k, int ldqk, const float* v, int 
 // attention_tc_workspace_floats(B, N, C) floats. F2S_ERR_UNSUPPORTED for
 // shapes it does not cover.
 int attention_tc_workspace_floats(int B, int N, int C);
+// Whether attention_tc takes this shape (else it returns F2S_ERR_UNSUPPORTED).
+bool attention_tc_supported(const float* q, const float* k, int ldqk, int d, int C);
+// Where attention_tc keeps V^T (fp16, (B, C, (N + 7) & ~7)) in its workspace;
+// a producer that writes it there passes vt_ready.
+__half* attention_tc_vt(float* workspace, int B, int N);
 int attention_tc(const float* q, const float* k, int ldqk, const float* v, int ldv,
                  const float* h, int ldh, float* out, int ldo, float* workspace, int B, int N,
-                 int d, int C, bool normalize_qk, bool round_tf32, cudaStream_t stream);
+                 int d, int C, bool normalize_qk, bool round_tf32, cudaStream_t stream,
+                 bool vt_ready = false);
 
 // ---- edge.cu ----
 // Fused neighbour stage: per edge (i, j = idx[i, k]) the HPE hidden

@@ -526,6 +526,11 @@ int linear_op(const GemmArgs& g, int precision, cudaStream_t st, void* split_w =
         op.W2 = g.W2_16;
     }
     op.y_fp16 = g.y_fp16;
+    op.vt = g.vt;
+    op.vt_col0 = g.vt_col0;
+    op.vt_C = g.vt_C;
+    op.vt_npad = g.vt_npad;
+    op.vt_M = g.vt_M;
     op.round_tf32 = g.round_tf32;
     op.epilogue = g.epilogue;
     op.tag = g.tag;
@@ -704,12 +709,27 @@ int trunk(const Dims& d, const Layout& L, const float* P, int B, int M, float* x
         F2S_TRY(ln_modulate(x, C, w.h, C, mod, mstride, 0, C, R, M, C, tf32_trunk, st));
         GemmArgs gq = gemm_args(w.h, C, P + bp.qkv_w, nullptr, w.qkv, ld_qkv, R, ld_qkv, C);
         gq.tag = kTagGemmQkv;
+        // with the tensor-core attention, the GEMM writes V straight into the
+        // attention's fp16 V^T (V starts at column 2 qk, a multiple of 32)
+        const bool attn_tc = tf32_trunk && attention_tc_supported(w.qkv, w.qkv + d.qk, ld_qkv, d.qk, C);
+        const bool vt_fused = attn_tc && (2 * d.qk) % 32 == 0 && ld_qkv % 4 == 0;
+        if (vt_fused) {
+            gq.vt = attention_tc_vt(w.attn, B, M);
+            gq.vt_col0 = 2 * d.qk;
+            gq.vt_C = C;
+            gq.vt_npad = (M + 7) & ~7;
+            gq.vt_M = M;
+        }
         F2S_TRY(linear_op(gq, d.precision, st));
         int attn_status = F2S_ERR_UNSUPPORTED;
-        if (tf32_trunk)  // q, k LayerNorm inside the tensor-core path's prep kernel
+        if (attn_tc)  // q, k LayerNorm inside the tensor-core path's prep kernel
             attn_status = attention_tc(w.qkv, w.qkv + d.qk, ld_qkv, w.qkv + 2 * d.qk, ld_qkv,
-                                       w.h, C, w.offs, C, w.attn, B, M, d.qk, C, true, true, st);
+                                       w.h, C, w.offs, C, w.attn, B, M, d.qk, C, true, true, st,
+                                       vt_fused);
         if (attn_status == F2S_ERR_UNSUPPORTED) {
+            // (never with V already in V^T form: attention_tc takes every shape
+            // attention_tc_supported accepts)
+            if (vt_fused) return fail(F2S_ERR_INVALID_ARGUMENT, "attention: V only in V^T form");
             F2S_TRY(qk_norm(w.qkv, ld_qkv, R, d.qk, st));
             attn_status = attention_f32(w.qkv, w.qkv + d.qk, ld_qkv, w.qkv + 2 * d.qk, ld_qkv,
                                         w.h, C, w.offs, C, w.colstats, B, M, d.qk, C, tf32_trunk,

@@ -58,6 +58,8 @@ struct TcGemmArgs {
     int rows_per_patch;
     int round_tf32;
     int tma_epi;        // fp32 output written by TMA store / reduce-add boxes
+    __half* vt;         // columns >= vt_col0: fp16, transposed per patch of vt_M rows
+    int vt_col0, vt_C, vt_npad, vt_M;
     int* err;
 };
 
@@ -521,6 +523,55 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                             v[i] += b[i];
                             if (g.round_tf32) v[i] = f2s_round_tf32(v[i]);
                         }
+                        if (g.vt && col0 >= g.vt_col0) {
+                            // a chunk of V: column c of this row goes to
+                            // vt[patch][c][row in patch] in fp16; a warp's 32
+                            // rows of one column are contiguous there
+                            const int pb0 = row0 / g.vt_M, key0 = row0 - pb0 * g.vt_M;
+                            if (key0 + 32 <= g.vt_M && (key0 & 7) == 0 && row0 + 32 <= g.rows &&
+                                col0 + 32 <= g.cols) {  // warp-uniform
+                                // 32 rows of one patch, 16-byte aligned there: the
+                                // chunk transposed through this warp's box slot
+                                // (rows of 40 halves: the 16-byte reads of eight
+                                // consecutive columns hit distinct banks), then
+                                // each lane stores one column's 32 keys as four
+                                // 16-byte stores
+                                __half* t = reinterpret_cast<__half*>(boxes + (boxes_sent & 1) * kBoxSlot);
+                                if (lane == 0) bulk_wait_read<0>();  // no box store still reads the slot
+                                __syncwarp();
+                                bool out_of_range = false;
+#pragma unroll
+                                for (int i = 0; i < 32; ++i) {
+                                    out_of_range |= !(fabsf(v[i]) < 65504.0f);
+                                    t[i * 40 + lane] = __float2half_rn(v[i]);
+                                }
+                                if (out_of_range) atomicExch(g.err, tc::kTcFp16Range);
+                                __syncwarp();
+                                const uint4* src = reinterpret_cast<const uint4*>(t + lane * 40);
+                                uint4* dst = reinterpret_cast<uint4*>(
+                                    g.vt + ((size_t)pb0 * g.vt_C + (col0 - g.vt_col0 + lane)) * g.vt_npad + key0);
+#pragma unroll
+                                for (int j = 0; j < 4; ++j) dst[j] = src[j];
+                                __syncwarp();  // the slot is read before it is written again
+                                continue;
+                            }
+                            const int r = row0 + lane;
+                            if (r < g.rows) {
+                                const int pb = r / g.vt_M;
+                                __half* dst = g.vt + ((size_t)pb * g.vt_C + (col0 - g.vt_col0)) * g.vt_npad +
+                                              (r - pb * g.vt_M);
+                                bool out_of_range = false;
+#pragma unroll
+                                for (int i = 0; i < 32; ++i) {
+                                    if (col0 + i < g.cols) {
+                                        out_of_range |= !(fabsf(v[i]) < 65504.0f);
+                                        dst[(size_t)i * g.vt_npad] = __float2half_rn(v[i]);
+                                    }
+                                }
+                                if (out_of_range) atomicExch(g.err, tc::kTcFp16Range);
+                            }
+                            continue;  // nothing of this chunk goes to Y
+                        }
                     }
                     unsigned char* box = boxes + (boxes_sent & 1) * kBoxSlot;
                     // the box's previous store must have read it
@@ -801,6 +852,11 @@ int tc_gemm(const TcGemmOp& op, cudaStream_t st) {
     g.gate_stride = op.gate_stride;
     g.rows_per_patch = op.rows_per_patch > 0 ? op.rows_per_patch : 1;
     g.round_tf32 = op.round_tf32 ? 1 : 0;
+    g.vt = op.vt;
+    g.vt_col0 = op.vt_col0;
+    g.vt_C = op.vt_C;
+    g.vt_npad = op.vt_npad;
+    g.vt_M = op.vt_M > 0 ? op.vt_M : 1;
     g.err = err;
     // fp32 output with 16-byte rows, columns and per-column vectors: the
     // epilogue writes 32 x 32 boxes by TMA (store, or reduce-add for the residual)
@@ -810,6 +866,10 @@ int tc_gemm(const TcGemmOp& op, cudaStream_t st) {
                 (op.epilogue != kEpiGatedResidual || (aligned16(op.gate) && op.gate_stride % 4 == 0));
     F2S_REQUIRE(!op.y_fp16 || (g.tma_epi && op.epilogue != kEpiGatedResidual),
                 "tc_gemm: fp16 output needs the TMA epilogue (16-byte rows and vectors), no residual");
+    F2S_REQUIRE(!op.vt || (g.tma_epi && op.epilogue == kEpiStore && !split && !split_in &&
+                           !op.y_fp16 && op.vt_col0 % 32 == 0 && op.vt_M > 0 &&
+                           op.vt_npad >= op.vt_M),
+                "tc_gemm: the V^T output needs the plain TMA epilogue and a 32-aligned first column");
     CUtensorMap my;
     if (g.tma_epi)
         F2S_TRY(make_tensor_map_2d_typed(&my, op.Y, op.y_fp16 ? kTmaF16 : kTmaF32, op.y_fp16 ? 64 : 128,

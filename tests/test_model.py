@@ -83,6 +83,24 @@ def test_tensor_core_model_matches_oracle(cuda, k, precision, encoder_precision,
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("points", [777, 1001])
+def test_tensor_core_trunk_ragged_patches(cuda, points):
+    """The bench's mode on patches whose size is not a multiple of 8: the qkv
+    GEMM writes V straight into the attention's fp16 V^T, whose rows are padded
+    to a multiple of 8 keys (the padding zeroed), and the last 128-key tile is
+    partly past the patch."""
+    cfg = dict(DEFAULT_CONFIG, k_neighbors=16)
+    params = random_parameters(cfg, seed=3)
+    cloud = sphere_cloud(20000, seed=6)[0]
+    x = patches_from_cloud(cloud, 3, points, seed=points)
+    alpha = np.array([0.4, 0.8, 1.0], dtype=np.float32)
+    v = gpu_forward(cfg, params, x, alpha, "tf32", "bf16x3")
+    ref = OracleNet(cfg, params)(x, alpha)
+    assert np.linalg.norm(v - ref) / np.linalg.norm(ref) < 1e-3
+    assert np.abs(v - ref).max() < VELOCITY_ATOL
+
+
+@pytest.mark.gpu
 @pytest.mark.parametrize("k,patches,points", [(8, 3, 1000), (32, 3, 999), (16, 5, 777)])
 def test_split_encoder_shapes(cuda, k, patches, points):
     """The split-bf16 neighbour stage at K = 8 and on ragged batches (the
