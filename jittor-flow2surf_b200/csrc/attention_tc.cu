@@ -707,14 +707,21 @@ __half* attention_tc_vt(float* workspace, int B, int N) {
     return reinterpret_cast<__half*>(workspace + (size_t)B * N * 128);
 }
 
+void attention_tc_qk(float* workspace, int B, int N, void** hi, void** lo) {
+    __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(workspace);
+    *hi = h;
+    *lo = h + (size_t)B * N * 2 * kDPad;
+}
+
 // q, k: (B*N rows, ldqk), width d (<= 64); v (ldv), width C (multiple of 64,
 // <= 256); out = h - A (or A). workspace: attention_tc_workspace_floats floats.
 // vt_ready: V^T keys [0, N) are already in the workspace (attention_tc_vt),
-// written by the producer of v (v is then not read).
+// written by the producer of v (v is then not read); qk_ready: likewise the
+// q / k bf16 rows (attention_tc_qk; q and k are then not read).
 int attention_tc(const float* q, const float* k, int ldqk, const float* v, int ldv,
                  const float* h, int ldh, float* out, int ldo, float* workspace, int B, int N,
                  int d, int C, bool normalize_qk, bool round_tf32, cudaStream_t st,
-                 bool vt_ready) {
+                 bool vt_ready, bool qk_ready) {
     if (B == 0 || N == 0) return F2S_OK;
     if (!attention_tc_supported(q, k, ldqk, d, C))
         return fail(F2S_ERR_UNSUPPORTED, "attention shape outside the tensor-core kernel");
@@ -727,9 +734,11 @@ int attention_tc(const float* q, const float* k, int ldqk, const float* v, int l
     float* colstats = workspace + (size_t)B * N * 128 + ((size_t)B * C * n_pad + 1) / 2;
     {
         TraceScope trace(kTagRowNorm, st);
-        qk_split_kernel<<<ceil_div(B * N, 8), 256, 0, st>>>(q, k, ldqk, B * N, d, normalize_qk,
-                                                             qk_hi, qk_lo);
-        F2S_TRY(check_launch("qk_split_kernel"));
+        if (!qk_ready) {
+            qk_split_kernel<<<ceil_div(B * N, 8), 256, 0, st>>>(q, k, ldqk, B * N, d, normalize_qk,
+                                                                 qk_hi, qk_lo);
+            F2S_TRY(check_launch("qk_split_kernel"));
+        }
         if (!vt_ready) {
             dim3 grid(ceil_div(n_pad, 64), ceil_div(C, 64), B);
             v_transpose_kernel<<<grid, 256, 0, st>>>(v, ldv, N, C, n_pad, vT, err);

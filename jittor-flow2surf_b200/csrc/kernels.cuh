@@ -49,6 +49,10 @@ struct GemmArgs {
     // the device error word to 2
     __half* vt;
     int vt_col0, vt_C, vt_npad, vt_M;
+    // with vt: the q and k columns [0, 96) (q / k width 48) LayerNorm'd and
+    // split into the attention's bf16 rows (attention_tc_qk) instead of Y
+    void* qk_hi;
+    void* qk_lo;
 };
 int gemm_f32(const GemmArgs& args, cudaStream_t stream);
 
@@ -64,6 +68,8 @@ struct TcGemmOp {
     const void* W_lo;        //   A and W then hold the tf32-rounded high parts
     __half* vt;              // as GemmArgs::vt (plain store, TMA epilogue)
     int vt_col0, vt_C, vt_npad, vt_M;
+    void* qk_hi;             // as GemmArgs::qk_hi / qk_lo
+    void* qk_lo;
     bool split_in;           // split bf16: A is fp32 (split into bf16 high and low parts
                              //   in shared memory), W / W_lo the bf16 parts of the weights
     const float* bias;
@@ -129,10 +135,14 @@ bool attention_tc_supported(const float* q, const float* k, int ldqk, int d, int
 // Where attention_tc keeps V^T (fp16, (B, C, (N + 7) & ~7)) in its workspace;
 // a producer that writes it there passes vt_ready.
 __half* attention_tc_vt(float* workspace, int B, int N);
+// Where attention_tc keeps the LayerNorm'd q / k rows as bf16 high and low
+// parts (rows of [q 64 | k 64], zero padded); a producer that writes them
+// passes qk_ready.
+void attention_tc_qk(float* workspace, int B, int N, void** hi, void** lo);
 int attention_tc(const float* q, const float* k, int ldqk, const float* v, int ldv,
                  const float* h, int ldh, float* out, int ldo, float* workspace, int B, int N,
                  int d, int C, bool normalize_qk, bool round_tf32, cudaStream_t stream,
-                 bool vt_ready = false);
+                 bool vt_ready = false, bool qk_ready = false);
 
 // ---- edge.cu ----
 // Fused neighbour stage: per edge (i, j = idx[i, k]) the HPE hidden

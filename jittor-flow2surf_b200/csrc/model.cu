@@ -531,6 +531,8 @@ int linear_op(const GemmArgs& g, int precision, cudaStream_t st, void* split_w =
     op.vt_C = g.vt_C;
     op.vt_npad = g.vt_npad;
     op.vt_M = g.vt_M;
+    op.qk_hi = g.qk_hi;
+    op.qk_lo = g.qk_lo;
     op.round_tf32 = g.round_tf32;
     op.epilogue = g.epilogue;
     op.tag = g.tag;
@@ -719,13 +721,16 @@ int trunk(const Dims& d, const Layout& L, const float* P, int B, int M, float* x
             gq.vt_C = C;
             gq.vt_npad = (M + 7) & ~7;
             gq.vt_M = M;
+            // and, at the q / k width the fused epilogue has, the q and k
+            // rows LayerNorm'd and split for the attention as well
+            if (d.qk == 48) attention_tc_qk(w.attn, B, M, &gq.qk_hi, &gq.qk_lo);
         }
         F2S_TRY(linear_op(gq, d.precision, st));
         int attn_status = F2S_ERR_UNSUPPORTED;
         if (attn_tc)  // q, k LayerNorm inside the tensor-core path's prep kernel
             attn_status = attention_tc(w.qkv, w.qkv + d.qk, ld_qkv, w.qkv + 2 * d.qk, ld_qkv,
                                        w.h, C, w.offs, C, w.attn, B, M, d.qk, C, true, true, st,
-                                       vt_fused);
+                                       vt_fused, gq.qk_hi != nullptr);
         if (attn_status == F2S_ERR_UNSUPPORTED) {
             // (never with V already in V^T form: attention_tc takes every shape
             // attention_tc_supported accepts)

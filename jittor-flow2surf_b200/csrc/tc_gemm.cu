@@ -60,8 +60,15 @@ struct TcGemmArgs {
     int tma_epi;        // fp32 output written by TMA store / reduce-add boxes
     __half* vt;         // columns >= vt_col0: fp16, transposed per patch of vt_M rows
     int vt_col0, vt_C, vt_npad, vt_M;
+    // columns [0, 2 kQkD): the attention's q and k rows, LayerNorm'd and split
+    // into bf16 high / low parts (rows of [q 64 | k 64], zero padded)
+    __nv_bfloat16* qk_hi;
+    __nv_bfloat16* qk_lo;
     int* err;
 };
+
+// q / k width of the fused q/k epilogue: three 32-column chunks hold q and k.
+constexpr int kQkD = 48;
 
 constexpr uint32_t kEpiBox = 32 * 128;  // one 32-row x 32-column fp32 box, 128-byte swizzle
 
@@ -498,7 +505,83 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                 // 32 columns, written to global memory by one TMA store (or
                 // reduce-add for the residual, so y is never read here)
                 const int row = min(row0 + lane, g.rows - 1);
-                for (int c0 = chunk_half * 32; c0 < g.bn; c0 += 64) {
+                int c_begin = chunk_half * 32, c_step = 64;
+                if constexpr (kEpi == kEpiStore) {
+                    if (g.qk_hi && n0 == 0) {
+                        // the q and k columns: the first warp of the quarter
+                        // takes all three chunks (a row's LayerNorm needs all
+                        // of its q or k), the second the tile's other chunks
+                        if (chunk_half == 0) {
+                            float x[3][32];
+#pragma unroll
+                            for (int ch = 0; ch < 3; ++ch) {
+                                tc::tmem_ld32(t_row + (uint32_t)(32 * ch), x[ch]);
+                                if (g.bias) {
+                                    float b[32];
+                                    load_cols32(g.bias, 32 * ch, g.cols, b);
+#pragma unroll
+                                    for (int i = 0; i < 32; ++i) x[ch][i] += b[i];
+                                }
+                            }
+                            {  // every lane: rows past the end are clipped by the stores
+#pragma unroll
+                                for (int part = 0; part < 2; ++part) {
+                                    // ChannelLayerNorm without affine, eps 1e-6
+                                    // (layers.py:20-27, transformer.py:59-63)
+                                    float y[kQkD];
+#pragma unroll
+                                    for (int i = 0; i < kQkD; ++i)
+                                        y[i] = x[(part * kQkD + i) >> 5][(part * kQkD + i) & 31];
+                                    float sum = 0.0f;
+#pragma unroll
+                                    for (int i = 0; i < kQkD; ++i) sum += y[i];
+                                    const float mean = sum / (float)kQkD;
+                                    float qq = 0.0f;
+#pragma unroll
+                                    for (int i = 0; i < kQkD; ++i) qq = fmaf(y[i] - mean, y[i] - mean, qq);
+                                    const float rstd = rsqrtf(qq / (float)kQkD + 1e-6f);
+                                    uint32_t h[32], l[32];  // 64 bf16 of each part, zero padded
+#pragma unroll
+                                    for (int e = 0; e < 32; ++e) {
+                                        const float v0 = 2 * e < kQkD ? (y[2 * e] - mean) * rstd : 0.0f;
+                                        const float v1 = 2 * e + 1 < kQkD ? (y[2 * e + 1] - mean) * rstd : 0.0f;
+                                        const __nv_bfloat162 hb = __floats2bfloat162_rn(v0, v1);
+                                        const __nv_bfloat162 lb = __floats2bfloat162_rn(
+                                            v0 - __bfloat162float(hb.x), v1 - __bfloat162float(hb.y));
+                                        h[e] = *reinterpret_cast<const uint32_t*>(&hb);
+                                        l[e] = *reinterpret_cast<const uint32_t*>(&lb);
+                                    }
+                                    // the warp's 32 rows x 64 bf16 of each part as one
+                                    // swizzled box, stored by TMA (map_a2: high
+                                    // parts, map_b2: low parts; unused by this form)
+#pragma unroll
+                                    for (int w = 0; w < 2; ++w) {
+                                        const uint32_t* src = w == 0 ? h : l;
+                                        unsigned char* box = boxes + (boxes_sent & 1) * kBoxSlot;
+                                        if (lane == 0 && boxes_sent >= 2) bulk_wait_read<1>();
+                                        __syncwarp();
+#pragma unroll
+                                        for (int j = 0; j < 8; ++j)
+                                            *reinterpret_cast<uint4*>(box + sw128_offset(lane, j)) =
+                                                make_uint4(src[4 * j], src[4 * j + 1], src[4 * j + 2], src[4 * j + 3]);
+                                        fence_proxy_async_shared();
+                                        __syncwarp();
+                                        if (lane == 0) {
+                                            tma_store_2d(w == 0 ? &map_a2 : &map_b2, box, part * 64, row0);
+                                            bulk_commit();
+                                        }
+                                        ++boxes_sent;
+                                    }
+                                }
+                            }
+                            c_begin = g.bn;  // nothing else for this warp
+                        } else {
+                            c_begin = 2 * kQkD;
+                            c_step = 32;
+                        }
+                    }
+                }
+                for (int c0 = c_begin; c0 < g.bn; c0 += c_step) {
                     const int col0 = n0 + c0;
                     float v[32];
                     tc::tmem_ld32(t_row + (uint32_t)c0, v);
@@ -830,6 +913,11 @@ int tc_gemm(const TcGemmOp& op, cudaStream_t st) {
     else mb2 = mb;
     if (split) F2S_TRY(make_tensor_map_2d(&ma2, op.A_lo, true, op.rows, op.K, op.lda, kTileM, bk));
     else ma2 = ma;
+    if (op.qk_hi && op.qk_lo && !dual && !split && !split_in) {
+        // the fused q/k rows (bf16, 128 per row): 32-row x 64-column boxes
+        F2S_TRY(make_tensor_map_2d_typed(&ma2, op.qk_hi, kTmaBF16, 128, op.rows, 128, 128, 32, 64));
+        F2S_TRY(make_tensor_map_2d_typed(&mb2, op.qk_lo, kTmaBF16, 128, op.rows, 128, 128, 32, 64));
+    }
 
     TcGemmArgs g{};
     g.rows = op.rows;
@@ -857,6 +945,8 @@ int tc_gemm(const TcGemmOp& op, cudaStream_t st) {
     g.vt_C = op.vt_C;
     g.vt_npad = op.vt_npad;
     g.vt_M = op.vt_M > 0 ? op.vt_M : 1;
+    g.qk_hi = static_cast<__nv_bfloat16*>(op.qk_hi);
+    g.qk_lo = static_cast<__nv_bfloat16*>(op.qk_lo);
     g.err = err;
     // fp32 output with 16-byte rows, columns and per-column vectors: the
     // epilogue writes 32 x 32 boxes by TMA (store, or reduce-add for the residual)
@@ -870,6 +960,10 @@ int tc_gemm(const TcGemmOp& op, cudaStream_t st) {
                            !op.y_fp16 && op.vt_col0 % 32 == 0 && op.vt_M > 0 &&
                            op.vt_npad >= op.vt_M),
                 "tc_gemm: the V^T output needs the plain TMA epilogue and a 32-aligned first column");
+    F2S_REQUIRE(!op.qk_hi || (op.vt && op.qk_lo && op.vt_col0 == 2 * kQkD && bn >= 2 * kQkD &&
+                              op.cols >= 2 * kQkD),
+                "tc_gemm: the q/k output needs the V^T output at column %d and an N tile of >= %d",
+                2 * kQkD, 2 * kQkD);
     CUtensorMap my;
     if (g.tma_epi)
         F2S_TRY(make_tensor_map_2d_typed(&my, op.Y, op.y_fp16 ? kTmaF16 : kTmaF32, op.y_fp16 ? 64 : 128,
