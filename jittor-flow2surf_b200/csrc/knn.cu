@@ -101,14 +101,34 @@ knn_kernel(const float* __restrict__ features, int C_runtime, int N, int k, int 
     const int tile = blockIdx.x - b * tiles_per_patch;
     const float* f = features + (size_t)b * C * N;
 
-    for (int j = threadIdx.x; j < N; j += blockDim.x) {
-        float norm = 0.0f;
-        for (int c = 0; c < C; ++c) {
-            const float v = f[(size_t)c * N + j];
-            s_feat[(size_t)c * N + j] = v;
-            norm = __fmaf_rn(v, v, norm);
+    // xyz (CFIX = 3): one float4 (x, y, z, |p|^2) per point, zero padded to
+    // SLOTS * 32, so a slot is one 16-byte load with no bounds check
+    float4* s_pts = reinterpret_cast<float4*>(s_feat);
+    if constexpr (CFIX == 3) {
+        for (int j = threadIdx.x; j < SLOTS * 32; j += blockDim.x) {
+            float4 p = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (j < N) {
+                p.x = f[j];
+                p.y = f[(size_t)N + j];
+                p.z = f[2 * (size_t)N + j];
+                float norm = 0.0f;
+                norm = __fmaf_rn(p.x, p.x, norm);
+                norm = __fmaf_rn(p.y, p.y, norm);
+                norm = __fmaf_rn(p.z, p.z, norm);
+                p.w = norm;
+            }
+            s_pts[j] = p;
         }
-        s_norm[j] = norm;
+    } else {
+        for (int j = threadIdx.x; j < N; j += blockDim.x) {
+            float norm = 0.0f;
+            for (int c = 0; c < C; ++c) {
+                const float v = f[(size_t)c * N + j];
+                s_feat[(size_t)c * N + j] = v;
+                norm = __fmaf_rn(v, v, norm);
+            }
+            s_norm[j] = norm;
+        }
     }
     __syncthreads();
     const float* fe = s_feat;
@@ -123,21 +143,41 @@ knn_kernel(const float* __restrict__ features, int C_runtime, int N, int k, int 
     const int q_begin = tile * kQueriesPerCta;
     const int q_end = min(N, q_begin + kQueriesPerCta);
     for (int q = q_begin + warp; q < q_end; q += kWarps) {
-        const float qn = s_norm[q];
-        // Inner products accumulate channel by channel (channel-outer loop so
-        // the slot loop unrolls); per (q, j) the order is c = 0, 1, ... as in
-        // the reference.
+        float qn;
+        // Inner products accumulate channel by channel; per (q, j) the order
+        // is c = 0, 1, ... as in the reference.
+        // ip[r] becomes the slot's d = |q|^2 + |p|^2 - 2 q.p
         float ip[SLOTS];
+        if constexpr (CFIX == 3) {
+            const float4 qp = s_pts[q];
+            qn = qp.w;
 #pragma unroll
-        for (int r = 0; r < SLOTS; ++r) ip[r] = 0.0f;
-        for (int c = 0; c < C; ++c) {
-            const float* row = fe + (size_t)c * N;
-            const float qc = row[q];
+            for (int r = 0; r < SLOTS; ++r) {
+                const float4 p = s_pts[r * 32 + lane];
+                float t = __fmaf_rn(qp.x, p.x, 0.0f);
+                t = __fmaf_rn(qp.y, p.y, t);
+                t = __fmaf_rn(qp.z, p.z, t);
+                ip[r] = __fmaf_rn(-2.0f, t, __fadd_rn(qn, p.w));
+            }
+        } else {
+            qn = s_norm[q];
+            // channel-outer loop so the slot loop unrolls
+#pragma unroll
+            for (int r = 0; r < SLOTS; ++r) ip[r] = 0.0f;
+            for (int c = 0; c < C; ++c) {
+                const float* row = fe + (size_t)c * N;
+                const float qc = row[q];
+#pragma unroll
+                for (int r = 0; r < SLOTS; ++r) {
+                    const int j = r * 32 + lane;
+                    const float fj = j < N ? row[j] : 0.0f;
+                    ip[r] = __fmaf_rn(qc, fj, ip[r]);
+                }
+            }
 #pragma unroll
             for (int r = 0; r < SLOTS; ++r) {
                 const int j = r * 32 + lane;
-                const float fj = j < N ? row[j] : 0.0f;
-                ip[r] = __fmaf_rn(qc, fj, ip[r]);
+                ip[r] = __fmaf_rn(-2.0f, ip[r], __fadd_rn(qn, j < N ? s_norm[j] : 0.0f));
             }
         }
         uint32_t key[SLOTS];
@@ -146,7 +186,7 @@ knn_kernel(const float* __restrict__ features, int C_runtime, int N, int k, int 
             const int j = r * 32 + lane;
             uint32_t kk = 0xffffffffu;
             if (j < N && j != q) {
-                const float d = __fmaf_rn(-2.0f, ip[r], __fadd_rn(qn, s_norm[j]));
+                const float d = ip[r];
                 kk = f2s_ordered_bits(d);
             }
             key[r] = kk;
@@ -289,8 +329,9 @@ template <int SLOTS, int CFIX>
 int launch_knn(const float* features, int B, int C, int N, int k, int actual_k, int32_t* out,
                cudaStream_t stream) {
     const int n_pad = (N + 3) & ~3;
-    const size_t smem = (size_t)n_pad * 4 + (size_t)kWarps * 256 * 4 + (size_t)kWarps * 64 * 8 +
-                        (size_t)C * N * 4;
+    // the features: (C, N) floats, or for xyz one float4 per slot position
+    const size_t feat = CFIX == 3 ? (size_t)SLOTS * 32 * 16 : (size_t)C * N * 4;
+    const size_t smem = (size_t)n_pad * 4 + (size_t)kWarps * 256 * 4 + (size_t)kWarps * 64 * 8 + feat;
     auto kernel = knn_kernel<SLOTS, CFIX>;
     if (smem > 48 * 1024)
         F2S_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
