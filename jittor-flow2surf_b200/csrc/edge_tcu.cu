@@ -49,7 +49,8 @@ constexpr int kHiddenWarps = 8;
 constexpr int kEpilogueWarps = 8;
 constexpr int kEpiWarp0 = kHiddenWarps;
 constexpr int kControlWarp0 = kHiddenWarps + kEpilogueWarps;
-constexpr int kControlWarps = 4;
+constexpr int kControlWarps = 4;  // three u-row writers and the MMA issuer
+constexpr int kWriterWarps = 3;
 constexpr int kThreads = (kControlWarp0 + kControlWarps) * 32;
 constexpr unsigned kFull = 0xffffffffu;
 
@@ -117,11 +118,6 @@ __device__ __forceinline__ void quarter_barrier(int q) {
     asm volatile("bar.sync %0, 64;" ::"r"(q + 1) : "memory");
 }
 
-// The four control warps.
-__device__ __forceinline__ void control_barrier() {
-    asm volatile("bar.sync 5, 128;" ::: "memory");
-}
-
 // Order-preserving map of a float onto an unsigned integer (negative values
 // have all bits flipped, the others the sign bit), so that the integer max is
 // the float max; unorder() inverts it.
@@ -166,9 +162,9 @@ edge_unified_kernel(const UArgs a) {
     uint64_t* acc_full = bars + 6;   // [2] accumulator holds its tile
     uint64_t* acc_free = bars + 8;   // [2] accumulator read out (8 arrivals)
     uint64_t* mma_done = bars + 10;
+    uint64_t* u_full = bars + 11;    // [1] u rows of the next tile in sU (one arrival per writer)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
     volatile int* sFail = reinterpret_cast<volatile int*>(smem + L.fails);  // [2][8]
-    volatile int* sCtlFail = sFail + 2 * kEpilogueWarps;  // control warps' failure flag
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int R = a.B * a.M;
@@ -190,9 +186,10 @@ edge_unified_kernel(const UArgs a) {
             tc::mbar_init(&acc_free[s], kEpilogueWarps);
         }
         tc::mbar_init(mma_done, 1);
+        tc::mbar_init(u_full, kWriterWarps * 32);
         tc::fence_barrier_init();
     }
-    if (tid <= 2 * kEpilogueWarps) sFail[tid] = 0;  // and the control flag
+    if (tid < 2 * kEpilogueWarps) sFail[tid] = 0;
     fence_proxy_async();  // the weights written above, for the tensor cores
     if (warp == kControlWarp0) tc::tmem_alloc(tmem_slot, a.tmem_cols);
     tc::tc_fence_before();
@@ -216,57 +213,52 @@ edge_unified_kernel(const UArgs a) {
         // (fetch_points, one tile later) the neighbour point; write_u (one
         // more tile later) forms g, so no instruction waits on a load issued
         // in the same iteration.
-        float4 pj = make_float4(0.f, 0.f, 0.f, 0.f);
-        float3 pi = make_float3(0.f, 0.f, 0.f), ni = pi;
-        float g6[6], ng6[6];
-        int nj = 0, nbase = 0;  // neighbour index within its patch, the patch's first row
-        bool gvalid = false, nvalid = false;
-        auto fetch_indices = [&](int t) {
-            const int p = t * a.ppt + (row >> a.log2K);
-            nvalid = t < n_tiles && p < R;
-            const int pc = nvalid ? p : 0;
+        struct RowGeo {
+            float4 pj;
+            float3 pi, ni;
+            float g6[6], ng6[6];
+            int nj, nbase;  // neighbour index within its patch, the patch's first row
+            bool gvalid, nvalid;
+            int row;        // TMEM lane / u row
+        };
+        auto fetch_indices = [&](RowGeo& r, int t) {
+            const int p = t * a.ppt + (r.row >> a.log2K);
+            r.nvalid = t < n_tiles && p < R;
+            const int pc = r.nvalid ? p : 0;
             if (a.geometry) {
-                const float* gp = a.geometry + ((size_t)pc * K + (row & (K - 1))) * 6;
+                const float* gp = a.geometry + ((size_t)pc * K + (r.row & (K - 1))) * 6;
 #pragma unroll
-                for (int e = 0; e < 6; ++e) ng6[e] = gp[e];
+                for (int e = 0; e < 6; ++e) r.ng6[e] = gp[e];
             } else {
                 const float4 v = *reinterpret_cast<const float4*>(a.xyz4 + (size_t)pc * 4);
-                ni = make_float3(v.x, v.y, v.z);
-                nbase = (pc / a.M) * a.M;
-                nj = a.idx[(size_t)pc * K + (row & (K - 1))];
+                r.ni = make_float3(v.x, v.y, v.z);
+                r.nbase = (pc / a.M) * a.M;
+                r.nj = a.idx[(size_t)pc * K + (r.row & (K - 1))];
             }
         };
-        auto fetch_points = [&]() {
+        auto fetch_points = [&](RowGeo& r) {
             if (a.geometry) {
 #pragma unroll
-                for (int e = 0; e < 6; ++e) g6[e] = ng6[e];
+                for (int e = 0; e < 6; ++e) r.g6[e] = r.ng6[e];
             } else {
-                pi = ni;
-                pj = *reinterpret_cast<const float4*>(a.xyz4 + (size_t)(nbase + nj) * 4);
+                r.pi = r.ni;
+                r.pj = *reinterpret_cast<const float4*>(a.xyz4 + (size_t)(r.nbase + r.nj) * 4);
             }
-            gvalid = nvalid;
+            r.gvalid = r.nvalid;
         };
-        auto load_geometry = [&](int t) {  // both stages at once (start-up only)
-            fetch_indices(t);
-            fetch_points();
-        };
-        auto write_u = [&]() {
+        auto write_u = [&](RowGeo& r) {
             float g[6];
             if (!a.geometry) {
-                g6[0] = pj.x - pi.x;
-                g6[1] = pj.y - pi.y;
-                g6[2] = pj.z - pi.z;
-                g6[3] = pi.x;
-                g6[4] = pi.y;
-                g6[5] = pi.z;
+                r.g6[0] = r.pj.x - r.pi.x;
+                r.g6[1] = r.pj.y - r.pi.y;
+                r.g6[2] = r.pj.z - r.pi.z;
+                r.g6[3] = r.pi.x;
+                r.g6[4] = r.pi.y;
+                r.g6[5] = r.pi.z;
             }
 #pragma unroll
-            for (int e = 0; e < 6; ++e) g[e] = gvalid ? g6[e] : 0.0f;
-            write_u_row_g(sU, sGram, row, g);
-            // the rows for the tensor cores; fenced here, before the next
-            // prefetch loads are issued, since the fence waits for this
-            // thread's outstanding memory operations
-            fence_proxy_async();
+            for (int e = 0; e < 6; ++e) g[e] = r.gvalid ? r.g6[e] : 0.0f;
+            write_u_row_g(sU, sGram, r.row, g);
         };
         // pre = LN(W_in g + b_in) of the tile whose u rows are in sU, into slot s
         auto issue_pre = [&](int s) {
@@ -297,77 +289,91 @@ edge_unified_kernel(const UArgs a) {
                 tc::umma_tmem_a_f16(d, lo_col, db_hi, a.idesc, 1u);
             }
         };
-        const bool issuer = cwarp == 0 && lane == 0;
-        // u rows of the current geometry in sU (each thread fenced its own),
-        // visible to the tensor cores once every control warp has passed the
-        // barrier; a failure seen by any control warp before the barrier is
-        // seen by all after it
-        auto rows_written = [&](bool ok) -> bool {
-            if (!ok && lane == 0) *sCtlFail = 1;
-            control_barrier();
-            return *sCtlFail == 0;
-        };
         const int G = (int)gridDim.x;
         const int t0 = blockIdx.x, t1 = blockIdx.x + G;
-        load_geometry(t0);
-        write_u();
-        bool ok = rows_written(true);
-        if (ok && issuer) issue_pre(0);
-        if (ok && t1 < n_tiles) {
-            load_geometry(t1);
-            const bool waited = warp_wait<true>(&pre_full[0], 0, a.err, lane);  // sU read by pre(t0)
-            if (waited) write_u();
-            ok = rows_written(waited);
-            if (ok && issuer) issue_pre(1);
-        }
-        load_geometry(t1 + G);      // tile index 2
-        fetch_indices(t1 + 2 * G);  // tile index 3, stage 1
-        // per tile index it: the u rows of tile it + 2 (their geometry loaded
-        // one iteration earlier) while the hidden-row warps still produce
-        // tile it, then MMA(it), then the pre-activations of tile it + 2 into
-        // the slot MMA(it) has released
-        for (int it = 0; ok; ++it) {
-            const int tile = blockIdx.x + it * G;
-            if (tile >= n_tiles) break;
-            const int s = it & 1, acc = it % a.n_acc;
-            const int tile2 = tile + 2 * G;
-            bool mine = true;
-            if (tile2 < n_tiles) {
-                mine = warp_wait<true>(&pre_full[s ^ 1], (uint32_t)((it + 1) >> 1) & 1u, a.err, lane);
-                if (mine) {
-                    write_u();
-                    fetch_points();               // tile index it + 3
-                    fetch_indices(tile2 + 2 * G);  // tile index it + 4
-                }
-            }
-            ok = rows_written(mine);
-            if (!ok) break;
-            if (issuer) {
-                bool good = tc::mbar_wait_poll(&a_ready[s], (uint32_t)(it >> 1) & 1u, a.err);
-                if (good && it >= a.n_acc)
-                    good = tc::mbar_wait_poll(&acc_free[acc], ((uint32_t)(it / a.n_acc) & 1u) ^ 1u,
-                                              a.err);
+        if (cwarp == kWriterWarps) {
+            // ---- issuer: per tile index it, MMA(it) once its hidden rows are
+            // in TMEM, then the pre-activations of tile it + 2 into the slot
+            // MMA(it) releases, once the writers have its u rows in sU ----
+            if (lane == 0) {
+                bool good = tc::mbar_wait_poll(u_full, 0u, a.err);  // u rows of t0
                 if (good) {
+                    tc::tc_fence_after();
+                    issue_pre(0);
+                }
+                if (good && t1 < n_tiles) {
+                    good = tc::mbar_wait_poll(u_full, 1u, a.err);
+                    if (good) {
+                        tc::tc_fence_after();
+                        issue_pre(1);
+                    }
+                }
+                for (int it = 0; good; ++it) {
+                    const int tile = blockIdx.x + it * G;
+                    if (tile >= n_tiles) break;
+                    const int s = it & 1, acc = it % a.n_acc;
+                    good = tc::mbar_wait_poll(&a_ready[s], (uint32_t)(it >> 1) & 1u, a.err);
+                    if (good && it >= a.n_acc)
+                        good = tc::mbar_wait_poll(&acc_free[acc], ((uint32_t)(it / a.n_acc) & 1u) ^ 1u,
+                                                  a.err);
+                    if (!good) break;
                     tc::tc_fence_after();
                     issue_main(s, acc);
                     tc::umma_commit(&slot_free[s]);
                     tc::umma_commit(&acc_full[acc]);
-                }
-                if (good && tile2 < n_tiles) {
-                    good = tc::mbar_wait_poll(&slot_free[s], (uint32_t)(it >> 1) & 1u, a.err);
-                    if (good) {
-                        tc::tc_fence_after();
-                        issue_pre(s);
+                    if (tile + 2 * G < n_tiles) {
+                        // u rows of tile index it + 2: the (it + 2)-th phase of u_full
+                        good = tc::mbar_wait_poll(u_full, (uint32_t)it & 1u, a.err) &&
+                               tc::mbar_wait_poll(&slot_free[s], (uint32_t)(it >> 1) & 1u, a.err);
+                        if (good) {
+                            tc::tc_fence_after();
+                            issue_pre(s);
+                        }
                     }
                 }
-                if (!good) *sCtlFail = 1;  // the others stop after the next barrier
+                // every MMA issued completes before the CTA frees its memory
+                tc::umma_commit(mma_done);
+                tc::mbar_drain(mma_done, 0);
             }
             __syncwarp();
-        }
-        if (issuer) {
-            // every MMA issued completes before the CTA frees its memory
-            tc::umma_commit(mma_done);
-            tc::mbar_drain(mma_done, 0);
+        } else {
+            // ---- u-row writers: rows cwarp * 32 + lane, and for the first
+            // writer also 96 + lane; the u rows of tile index it + 2
+            // (geometry loaded one iteration earlier) as soon as pre(it + 1)
+            // has read sU, each thread fencing its rows and arriving on u_full ----
+            RowGeo rg[2] = {};
+            rg[0].row = cwarp * 32 + lane;
+            rg[1].row = 96 + lane;
+            const bool two = cwarp == 0;  // warp-uniform
+            auto each = [&](auto&& f) {
+                f(rg[0]);
+                if (two) f(rg[1]);
+            };
+            auto write_all = [&]() {
+                each(write_u);
+                // the rows for the tensor cores, before the next prefetch loads
+                fence_proxy_async();
+                tc::mbar_arrive(u_full);
+            };
+            each([&](RowGeo& r) { fetch_indices(r, t0); fetch_points(r); });
+            write_all();
+            bool ok = true;
+            if (t1 < n_tiles) {
+                each([&](RowGeo& r) { fetch_indices(r, t1); fetch_points(r); });
+                ok = warp_wait<true>(&pre_full[0], 0, a.err, lane);  // sU read by pre(t0)
+                if (ok) write_all();
+            }
+            each([&](RowGeo& r) { fetch_indices(r, t1 + G); fetch_points(r); });  // tile index 2
+            each([&](RowGeo& r) { fetch_indices(r, t1 + 2 * G); });              // tile index 3, stage 1
+            for (int it = 0; ok; ++it) {
+                const int tile2 = blockIdx.x + (it + 2) * G;
+                if (tile2 >= n_tiles) break;
+                if (!warp_wait<true>(&pre_full[(it & 1) ^ 1], (uint32_t)((it + 1) >> 1) & 1u, a.err, lane))
+                    break;
+                write_all();
+                // tile index it + 3, stage 2; tile index it + 4, stage 1
+                each([&](RowGeo& r) { fetch_points(r); fetch_indices(r, tile2 + 2 * G); });
+            }
         }
     } else if (warp < kHiddenWarps) {
         // ---------------- hidden rows ----------------
