@@ -81,7 +81,7 @@ struct UArgs {
 
 // Shared-memory layout (byte offsets from the 1024-byte aligned base).
 struct Layout {
-    uint32_t b_hi, b_lo, u, wu, gram, cb, ln, sgn, bars, fails, stage;
+    uint32_t b_hi, b_lo, u, wu, gram, cb, ln, sgn, bars, fails, rn, stage;
     uint32_t stage_bytes;  // per epilogue warp: 32 neighbour rows + the centre rows of its points
     uint32_t total;
 };
@@ -101,7 +101,9 @@ __host__ __device__ inline Layout layout(int H, int cout, int K) {
     L.sgn = L.ln + (uint32_t)cout * 8;
     L.bars = (L.sgn + (uint32_t)cout * 4 + 7) & ~7u;
     L.fails = L.bars + 16 * 8 + 8;
-    L.stage = (L.fails + 2 * kEpilogueWarps * 4 + 16 + 127) & ~127u;
+    // per epilogue warp, its 32 rows' (rstd, -mean rstd) for the column pass
+    L.rn = (L.fails + 2 * kEpilogueWarps * 4 + 16 + 15) & ~15u;
+    L.stage = (L.rn + kEpilogueWarps * 32 * 8 + 127) & ~127u;
     L.stage_bytes = 32u * cw * 4u + ppw * cw * 4u;
     L.total = L.stage + kEpilogueWarps * L.stage_bytes;
     return L;
@@ -567,11 +569,17 @@ edge_unified_kernel(const UArgs a) {
             // keeping the max and min of (m - mean) rstd (the row's rstd and
             // -mean rstd come by shuffle); the sign of the gain picks max or
             // -min, then |gain| x + shift and LeakyReLU(0.2), stored coalesced
-            __syncwarp();  // every lane's messages are in shared memory
+            // the row's normalisation, read back by every lane as one broadcast
+            float2* rn_w = reinterpret_cast<float2*>(smem + L.rn) + ew * 32;
+            rn_w[lane] = make_float2(rstd, nmr);
+            __syncwarp();  // every lane's messages and normalisation are in shared memory
             // channel lane + 32 j of staged row r: chunk (lane / 4 + 8 j), stored
             // at chunk 8 j + ((lane / 4) ^ (r & 7)) of the row (rows start on
             // 128-byte boundaries), element lane % 4
             const uint32_t lane_part = (uint32_t)(((lane >> 2) << 4) | ((lane & 3) << 2));
+            uint32_t lp[8];  // this lane's offset in a row with r & 7 = i
+#pragma unroll
+            for (int i = 0; i < 8; ++i) lp[i] = lane_part ^ (uint32_t)(i << 4);
             constexpr int nj = cw / 32;  // channels per lane (1, 2, 3)
             float gain[nj], shift_c[nj], sgn[nj];
 #pragma unroll
@@ -583,31 +591,34 @@ edge_unified_kernel(const UArgs a) {
             }
             const int pbase = tile * a.ppt + ((q * 32) >> a.log2K);
             for (int pt = 0; pt < ppw; ++pt) {
-                float mx[nj], mn[nj];
+                // even and odd rows in separate max / min chains
+                float mx[2][nj], mn[2][nj];
 #pragma unroll
                 for (int j = 0; j < nj; ++j) {
-                    mx[j] = -FLT_MAX;
-                    mn[j] = FLT_MAX;
+                    mx[0][j] = mx[1][j] = -FLT_MAX;
+                    mn[0][j] = mn[1][j] = FLT_MAX;
                 }
-#pragma unroll 4
-                for (int e = 0; e < K; ++e) {
-                    const int row = pt * K + e;
-                    const float re = __shfl_sync(kFull, rstd, row);
-                    const float ne = __shfl_sync(kFull, nmr, row);
-                    const uint32_t rowa =
-                        stage + (uint32_t)(row * cw * 4) + (lane_part ^ (uint32_t)((row & 7) << 4));
+#pragma unroll 1
+                for (int e0 = 0; e0 < K; e0 += 8) {  // K is a multiple of 8: row & 7 = i
+                    const uint32_t base = stage + (uint32_t)((pt * K + e0) * cw * 4);
 #pragma unroll
-                    for (int j = 0; j < nj; ++j) {
-                        const float x = fmaf(lds32(rowa + (uint32_t)(128 * j)), re, ne);
-                        mx[j] = fmaxf(mx[j], x);
-                        mn[j] = fminf(mn[j], x);
+                    for (int i = 0; i < 8; ++i) {
+                        const float2 rn = rn_w[pt * K + e0 + i];
+                        const uint32_t rowa = base + (uint32_t)(i * cw * 4) + lp[i];
+#pragma unroll
+                        for (int j = 0; j < nj; ++j) {
+                            const float x = fmaf(lds32(rowa + (uint32_t)(128 * j)), rn.x, rn.y);
+                            mx[i & 1][j] = fmaxf(mx[i & 1][j], x);
+                            mn[i & 1][j] = fminf(mn[i & 1][j], x);
+                        }
                     }
                 }
                 const int p = pbase + pt;
                 if (p < R) {
 #pragma unroll
                     for (int j = 0; j < nj; ++j) {
-                        const float v = sgn[j] > 0.0f ? mx[j] : -mn[j];
+                        const float v = sgn[j] > 0.0f ? fmaxf(mx[0][j], mx[1][j])
+                                                      : -fminf(mn[0][j], mn[1][j]);
                         const float t = fmaf(v, gain[j], shift_c[j]);
                         a.out[(size_t)p * a.ldo + ch0 + lane + 32 * j] = fmaxf(t, 0.2f * t);
                     }
