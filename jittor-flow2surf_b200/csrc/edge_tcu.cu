@@ -496,7 +496,6 @@ edge_unified_kernel(const UArgs a) {
                     uint32_t(&r)[16] = racc[k & 1];
                     if (k + 1 < nch) tc::tmem_ld16_issue(acol + (uint32_t)(16 * (k + 1)), racc[(k + 1) & 1]);
                     float2 m[8];
-                    float2 csum = f2(0.0f);
 #pragma unroll
                     for (int q4 = 0; q4 < 4; ++q4) {
                         const int c = 4 * k + q4;
@@ -514,9 +513,13 @@ edge_unified_kernel(const UArgs a) {
                                                   make_float2(bb.z, bb.w)));
                         sts128(pos, make_float4(m[2 * q4].x, m[2 * q4].y, m[2 * q4 + 1].x,
                                                 m[2 * q4 + 1].y));
-                        csum = add2(csum, add2(m[2 * q4], m[2 * q4 + 1]));
                     }
-                    if (k == 0) shift = (csum.x + csum.y) * (1.0f / 16.0f);
+                    if (k == 0) {  // the shift: the mean of the first 16 channels
+                        float2 csum = f2(0.0f);
+#pragma unroll
+                        for (int i = 0; i < 8; i += 2) csum = add2(csum, add2(m[i], m[i + 1]));
+                        shift = (csum.x + csum.y) * (1.0f / 16.0f);
+                    }
                     const float2 ns = f2(-shift);
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
