@@ -22,12 +22,12 @@
 //               back over the consumed staged rows, the two halves' moments
 //               meet through TMEM and a named barrier, and the normalised
 //               messages are reduced over the K rows of each point.
-//   warps 16-19 control: compute the u rows [rstd g, rstd, 1] two tiles ahead
-//               (one row per lane, geometry prefetched a further tile ahead);
-//               one lane issues the pre-activation MMAs into the TMEM slot the
-//               MMA before has released and the main MMAs (a tcgen05.mma holds
-//               its issuing thread until the tensor pipe takes it, so no other
-//               role waits on that).
+//   warps 16-19 control: warps 16-18 compute the u rows [rstd g, rstd, 1]
+//               two tiles ahead (geometry prefetched a further tile ahead);
+//               lane 0 of warp 19 issues the pre-activation MMAs into the
+//               TMEM slot the MMA before has released and the main MMAs (a
+//               tcgen05.mma holds its issuing thread until the tensor pipe
+//               takes it, so no other role waits on that).
 // The hidden-row warps (MUFU-heavy GELU), the epilogue warps (FMA, shared
 // memory) and the tensor pipe work on consecutive tiles at once.
 //
@@ -120,17 +120,6 @@ __device__ __forceinline__ void quarter_barrier(int q) {
     asm volatile("bar.sync %0, 64;" ::"r"(q + 1) : "memory");
 }
 
-// Order-preserving map of a float onto an unsigned integer (negative values
-// have all bits flipped, the others the sign bit), so that the integer max is
-// the float max; unorder() inverts it.
-__device__ __forceinline__ uint32_t order_key(float y) {
-    const uint32_t b = __float_as_uint(y);
-    return b ^ ((uint32_t)((int32_t)b >> 31) | 0x80000000u);
-}
-__device__ __forceinline__ float unorder(uint32_t k) {
-    return __uint_as_float(k ^ ((uint32_t)((int32_t)~k >> 31) | 0x80000000u));
-}
-
 // Bounded mbarrier wait by lane 0 of the warp, result shared by the warp;
 // kPoll waits without the suspend hint (the control warps).
 template <bool kPoll = false>
@@ -201,14 +190,11 @@ edge_unified_kernel(const UArgs a) {
 
     if (warp >= kControlWarp0) {
         // ---------------- control: u rows, pre-activation and main MMAs ----------------
-        // Control warp c computes the u rows of TMEM lanes 32c .. 32c + 31 (one
-        // row per lane); the four meet at a named barrier once the rows of a
-        // tile are in shared memory, and lane 0 of control warp 0 issues the
-        // MMAs. The geometry of a row is fetched in two stages a tile apart so
-        // that no load waits on another: stage 1 reads the neighbour index and
-        // the centre point, stage 2 (one tile later) the neighbour point.
+        // Control warps 0-2 write the 128 u rows of a tile (warp 0 two rows
+        // per lane: rows lane and 96 + lane; warps 1 and 2 one row each) and
+        // signal them on an mbarrier; lane 0 of control warp 3 issues the
+        // MMAs.
         const int cwarp = warp - kControlWarp0;
-        const int row = cwarp * 32 + lane;
         // g = [x_j - x_i, x_i] of the row, from the points (model) or read as
         // given (operator). Stage 1 (fetch_indices) loads the centre point and
         // the neighbour index (or the given g) of a tile; stage 2
