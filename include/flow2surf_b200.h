@@ -370,7 +370,14 @@ int f2s_euler_from_sum(const float* points, const double* vote_sum, const double
  *   first (B, M, 3), second (B, N, 3) float32 ->
  *   first_distance (B, M), second_index (B, M) int32,
  *   second_distance (B, N), first_index (B, N) int32.
- *   workspace: f2s_nearest_workspace_bytes() bytes (one 64-bit key per point).
+ *   When both sets hold 4096 points or more, each is sorted into a uniform
+ *   grid over its bounding box and a query searches rings of cells around
+ *   its own until no unvisited point can beat or tie its best; the results
+ *   are the all-pairs scan's, bit for bit (the lexicographic minimum of
+ *   (distance, index); points with a non-finite coordinate are never
+ *   nearest).
+ *   workspace: f2s_nearest_workspace_bytes() bytes (a 64-bit key per point,
+ *   and for the grid search about 52 bytes more per point).
  */
 int f2s_nearest_workspace_bytes(int B, int M, int N, size_t* bytes);
 int f2s_nearest(const float* first, const float* second, int B, int M, int N,

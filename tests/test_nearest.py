@@ -41,6 +41,58 @@ def test_nearest_ties_and_duplicates(cuda):
         np.testing.assert_array_equal(g, w)
 
 
+def _grid_cases():
+    """Point-set pairs of at least 4096 points each, so that the grid search
+    runs, with the distributions that stress it."""
+    rng = np.random.default_rng(11)
+
+    def sphere(n, r=1.0):
+        v = rng.normal(size=(n, 3))
+        return (r * v / np.linalg.norm(v, axis=1, keepdims=True)).astype(np.float32)
+
+    cases = {}
+    noisy, _, reference = mesh_cloud(12_000, seed=5, sigma_fraction=0.01, clean_points=15_000)
+    cases["surface"] = (noisy[None], reference[None])
+    scale = np.array([1.0, 1e-3, 50.0]).reshape(3, 1, 1)  # a different box per item
+    cases["cube_batch"] = ((rng.random((3, 6000, 3)) * scale).astype(np.float32),
+                           ((rng.random((3, 7000, 3)) * 1.4 - 0.2) * scale).astype(np.float32))
+    # most points in one tiny cluster: the item falls back to the plain scan
+    cluster = np.concatenate([rng.random((6000, 3)) * 1e-4, rng.random((200, 3)) * 10])
+    cases["cluster"] = (cluster[None].astype(np.float32), rng.random((1, 5000, 3)).astype(np.float32))
+    # an integer lattice: thousands of exact ties, decided by the index
+    cases["lattice"] = (rng.integers(0, 8, (1, 9000, 3)).astype(np.float32),
+                        (rng.integers(-1, 9, (1, 6000, 3)) + 0.5 * rng.integers(0, 2, (1, 6000, 3)))
+                        .astype(np.float32))
+    # small extent far from the origin (the cell-index rounding allowance)
+    cases["offset"] = ((rng.random((1, 8000, 3)) * 1e-2 + 1000).astype(np.float32),
+                       (rng.random((1, 5000, 3)) * 1.2e-2 + 1000 - 1e-3).astype(np.float32))
+    cases["plane"] = (np.c_[rng.random((8000, 2)), np.zeros(8000)][None].astype(np.float32),
+                      rng.random((1, 5000, 3)).astype(np.float32))
+    # NaN and infinite coordinates in both sets: never a nearest point
+    a = rng.random((1, 7000, 3))
+    a[rng.random(a.shape) < 0.01] = np.nan
+    b = rng.random((1, 6000, 3))
+    b[rng.random(b.shape) < 0.01] = np.inf
+    b[0, :5] = -np.inf
+    cases["nonfinite"] = (a.astype(np.float32), b.astype(np.float32))
+    # queries far outside the other set's box
+    cases["far"] = (sphere(6000)[None], np.concatenate([sphere(4500, 40.0), sphere(1000)])[None])
+    return cases
+
+
+@pytest.mark.parametrize("name", ["surface", "cube_batch", "cluster", "lattice", "offset", "plane",
+                                  "nonfinite", "far"])
+def test_nearest_grid_bit_exact(cuda, name):
+    """Sets of 4096 points or more take the grid search; it must give the
+    plain scan's (distance, index) winners bit for bit, ties and non-finite
+    points included."""
+    first, second = _grid_cases()[name]
+    got = [t.cpu().numpy() for t in nearest_squared_distances(dev(first), dev(second))]
+    want = native.nearest_squared_distances(first, second)
+    for g, w in zip(got, want):
+        np.testing.assert_array_equal(g, w)
+
+
 def test_nearest_reference_golden(cuda, golden):
     fix = golden("nearest")
     d1, i2, d2, i1 = [t.cpu().numpy() for t in

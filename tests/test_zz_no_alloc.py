@@ -3,8 +3,10 @@
 Some callers cannot call cudaMalloc (an out-of-memory handler, a host that
 forbids device allocation once running, work that must not synchronise the
 device), so this variant keeps its scratch in a built-in device array instead
-of a caller workspace. It must give what f2s_chamfer gives, bit for bit (the
-same kernels run on the same inputs), and once a device has been set up by a
+of a caller workspace. It must give what f2s_chamfer gives, bit for bit (both
+take the lexicographic minimum of (distance, index): this entry by the plain
+scan, f2s_chamfer by the grid search once both sets hold 4096 points or
+more), and once a device has been set up by a
 first call it must not change the device memory in use. This file sorts
 last so that, if it fails, a run that stops at the first failure has already
 run every other test.
