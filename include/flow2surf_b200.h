@@ -438,6 +438,115 @@ int f2s_point_to_mesh(const float* points, int M, const float* vertices, int V,
 int f2s_chamfer_static(const float* pred, const float* target, int B, int M, int N,
                        double* chamfer, void* stream);
 
+/* ------------------------------------------------------------------------ */
+/* Training gradients and losses                                            */
+/* ------------------------------------------------------------------------ */
+
+/*
+ * Coordinate gradients of the nearest squared distances: the backward of
+ * f2s_nearest (flow2surf/training/cuda/nearest_distance_backward.cu:11-40,
+ * _NearestDistanceFunction.grad, training/distances.py:40-62).
+ * second_index (B, M) / first_index (B, N) are f2s_nearest's index outputs;
+ * grad_first_distance (B, M) / grad_second_distance (B, N) may be NULL (zero).
+ * grad_first (B, M, 3), grad_second (B, N, 3) are written (the matched
+ * points' terms added with float atomics, as in the reference).
+ */
+int f2s_nearest_backward(const float* first, const float* second, int B, int M, int N,
+                         const int32_t* second_index, const int32_t* first_index,
+                         const float* grad_first_distance, const float* grad_second_distance,
+                         float* grad_first, float* grad_second, void* stream);
+
+/*
+ * Density-aware Chamfer loss per batch item (dcd_loss, training/losses.py:8-41):
+ * loss (B,) float32 (float64 sums). With grad_pred / grad_target (both or
+ * neither), also the gradients of sum_b grad_loss[b] loss[b] (grad_loss NULL
+ * = ones) with respect to pred (B, M, 3) and target (B, N, 3); the
+ * reciprocal multiplicities are constants, as under the reference's autograd.
+ *   workspace: f2s_dcd_loss_workspace_bytes(B, M, N) bytes.
+ */
+int f2s_dcd_loss_workspace_bytes(int B, int M, int N, size_t* bytes);
+int f2s_dcd_loss(const float* pred, const float* target, int B, int M, int N, float alpha,
+                 float* loss, const float* grad_loss, float* grad_pred, float* grad_target,
+                 void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Velocity loss per batch item (velocity_loss, training/losses.py:44-47):
+ * mean over M of the squared L2 error of (B, M, 3) velocities; loss,
+ * grad_pred and grad_target may each be NULL (grad_loss NULL = ones).
+ */
+int f2s_velocity_loss(const float* pred, const float* target, int B, int M, float* loss,
+                      const float* grad_loss, float* grad_pred, float* grad_target,
+                      void* stream);
+
+/*
+ * Backward of the HPE activation, moment LayerNorm (eps 1e-5) + exact GELU
+ * (hpe_activation_grad, flow2surf/models/ops/hpe.py:82-96 and
+ * cuda/hpe_activation_backward.cu:10-66): preactivation and grad_hidden
+ * (rows, H), H <= 256 -> grad_preactivation (rows, H) (may be grad_hidden
+ * itself), grad_norm_weight (H), grad_norm_bias (H) (summed in a fixed order).
+ */
+int f2s_hpe_activation_backward_workspace_bytes(int64_t rows, int H, size_t* bytes);
+int f2s_hpe_activation_backward(const float* preactivation, int64_t rows, int H,
+                                const float* norm_weight, const float* norm_bias,
+                                const float* grad_hidden, float* grad_preactivation,
+                                float* grad_norm_weight, float* grad_norm_bias, void* workspace,
+                                size_t workspace_bytes, void* stream);
+
+/*
+ * Backward of the normalised message max-reduction
+ * (_reduce_messages_grad, flow2surf/models/ops/neighbor_reduce.py:57-72 and
+ * cuda/neighbor_reduce_backward.cu:20-84): content (B, 2C, N), contribution
+ * (B, N, K, C), indices (B, N, K) int32, the message norm weight / bias (C),
+ * grad_output (B, C, N) -> grad_content (B, 2C, N), grad_contribution
+ * (B, N, K, C), grad_norm_weight / grad_norm_bias (C). The upstream gradient
+ * of a (point, channel) goes to every edge whose recomputed activation
+ * equals the maximum over the point's edges (all exact ties). C <= 256.
+ */
+int f2s_neighbor_messages_backward_workspace_bytes(int B, int N, int C, size_t* bytes);
+int f2s_neighbor_messages_backward(const float* content, const float* contribution,
+                                   const int32_t* indices, int B, int N, int K, int C,
+                                   const float* norm_weight, const float* norm_bias,
+                                   const float* grad_output, float* grad_content,
+                                   float* grad_contribution, float* grad_norm_weight,
+                                   float* grad_norm_bias, void* workspace, size_t workspace_bytes,
+                                   void* stream);
+
+/*
+ * The whole backward of reduce_neighbor_messages
+ * (_NeighborMessageFunction.grad, neighbor_reduce.py:155-237): the HPE rows
+ * and the contribution recomputed, the message backward, then through the
+ * output projection, the HPE activation and the input projection. Same
+ * operand layouts as f2s_neighbor_reduce; every gradient output is written.
+ * D <= 8, H <= 256, C <= 256.
+ */
+int f2s_neighbor_reduce_backward_workspace_bytes(int B, int N, int K, int D, int H, int C,
+                                                 size_t* bytes);
+int f2s_neighbor_reduce_backward(
+    const float* content, const float* geometry, const int32_t* indices,
+    const float* hpe_input_weight, const float* hpe_input_bias, const float* hpe_output_weight,
+    const float* hpe_output_bias, const float* hpe_norm_weight, const float* hpe_norm_bias,
+    const float* message_norm_weight, const float* message_norm_bias, int B, int N, int K, int D,
+    int H, int C, const float* grad_output, float* grad_content, float* grad_geometry,
+    float* grad_hpe_input_weight, float* grad_hpe_input_bias, float* grad_hpe_output_weight,
+    float* grad_hpe_output_bias, float* grad_hpe_norm_weight, float* grad_hpe_norm_bias,
+    float* grad_message_norm_weight, float* grad_message_norm_bias, void* workspace,
+    size_t workspace_bytes, void* stream);
+
+/*
+ * Backward of offset_attention_aggregate (_aggregate_cuda_grad,
+ * flow2surf/models/ops/attention.py:46-63 and cuda/offset_attention_backward.cu):
+ * query (B, N, d), key (B, d, N), value (B, N, C), the forward's output
+ * (B, N, C) and grad_output (B, N, C) -> grad_query, grad_key, grad_value
+ * (same shapes as the inputs), fp32. The N x N probabilities of up to 8
+ * batch items at a time are held in the workspace.
+ */
+int f2s_offset_attention_backward_workspace_bytes(int B, int N, int d, int C, size_t* bytes);
+int f2s_offset_attention_backward(const float* query, const float* key, const float* value,
+                                  int B, int N, int d, int C, const float* output,
+                                  const float* grad_output, float* grad_query, float* grad_key,
+                                  float* grad_value, void* workspace, size_t workspace_bytes,
+                                  void* stream);
+
 #ifdef __cplusplus
 }
 #endif

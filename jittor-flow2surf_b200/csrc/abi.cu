@@ -79,7 +79,7 @@ const char* const kTagNames[kTagCount] = {
     "gemm_head",    "row_norm",     "gemm_qkv",      "attn_colstats", "attn_output",
     "gemm_proj",    "gemm_swiglu",  "gemm_ff2",      "gemm_decoder", "fps",
     "patch_index",  "fusion_build", "gather",        "fuse_euler",   "nearest",
-    "transpose"};
+    "transpose",    "training"};
 
 }  // namespace
 

@@ -47,6 +47,7 @@ enum TraceTag {
     kTagFuseEuler,
     kTagNearest,
     kTagTranspose,
+    kTagTraining,
     kTagCount
 };
 

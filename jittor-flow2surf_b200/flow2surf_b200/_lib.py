@@ -64,6 +64,19 @@ SIGNATURES: dict[str, list] = {
     "f2s_linear": [_p, _i, _p, _p, _p, _i, _i, _i, _i, _i, _p],
     "f2s_device_error": [_p, _i, _p],
     "f2s_selftest_wait_timeout": [_i, _p],
+    "f2s_nearest_backward": [_p, _p, _i, _i, _i, _p, _p, _p, _p, _p, _p, _p],
+    "f2s_dcd_loss_workspace_bytes": [_i, _i, _i, _p],
+    "f2s_dcd_loss": [_p, _p, _i, _i, _i, _f, _p, _p, _p, _p, _p, _sz, _p],
+    "f2s_velocity_loss": [_p, _p, _i, _i, _p, _p, _p, _p, _p],
+    "f2s_hpe_activation_backward_workspace_bytes": [_i64, _i, _p],
+    "f2s_hpe_activation_backward": [_p, _i64, _i, _p, _p, _p, _p, _p, _p, _p, _sz, _p],
+    "f2s_neighbor_messages_backward_workspace_bytes": [_i, _i, _i, _p],
+    "f2s_neighbor_messages_backward": [_p, _p, _p, _i, _i, _i, _i] + [_p] * 7 + [_p, _sz, _p],
+    "f2s_neighbor_reduce_backward_workspace_bytes": [_i] * 6 + [_p],
+    "f2s_neighbor_reduce_backward": [_p] * 11 + [_i] * 6 + [_p] * 11 + [_p, _sz, _p],
+    "f2s_offset_attention_backward_workspace_bytes": [_i, _i, _i, _i, _p],
+    "f2s_offset_attention_backward": [_p, _p, _p, _i, _i, _i, _i, _p, _p, _p, _p, _p, _p, _sz,
+                                      _p],
 }
 
 _RESTYPES = {"f2s_last_error": ctypes.c_char_p, "f2s_trace_tag_name": ctypes.c_char_p}

@@ -79,6 +79,14 @@ def offset_attention_aggregate(query: torch.Tensor, key: torch.Tensor,
         raise ValueError(f"Incompatible attention shapes: {tuple(query.shape)}, "
                          f"{tuple(key.shape)}, {tuple(value.shape)}")
     _require_cuda(query, key, value)
+    if _needs_grad(query, key, value):
+        if precision != "fp32":
+            raise ValueError("the tensor-core attention has no backward; use precision='fp32'")
+        return _OffsetAttention.apply(query, key, value)
+    return _attention_forward(query, key, value, precision)
+
+
+def _attention_forward(query, key, value, precision="fp32"):
     batch, points, width = query.shape
     channels = value.shape[2]
     out = torch.empty((batch, points, channels), dtype=torch.float32, device=query.device)
@@ -94,6 +102,36 @@ def offset_attention_aggregate(query: torch.Tensor, key: torch.Tensor,
     _lib.call(entry, _lib.ptr(query), _lib.ptr(key), _lib.ptr(value), batch, points, width,
               channels, _lib.ptr(out), _lib.ptr(ws), ws.numel(), _lib.stream_handle())
     return out
+
+
+class _OffsetAttention(torch.autograd.Function):
+    """Exact offset attention with its backward (_OffsetAttentionFunction,
+    flow2surf/models/ops/attention.py:66-81): the forward on the fp32 kernels,
+    the backward recomputing the probabilities per batch chunk."""
+
+    @staticmethod
+    def forward(ctx, query, key, value):
+        query, key, value = _f32(query), _f32(key), _f32(value)
+        out = _attention_forward(query, key, value)
+        ctx.save_for_backward(query, key, value, out)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        query, key, value, out = ctx.saved_tensors
+        batch, points, width = query.shape
+        channels = value.shape[2]
+        gq, gk, gv = torch.empty_like(query), torch.empty_like(key), torch.empty_like(value)
+        if out.numel() == 0:
+            return gq.zero_(), gk.zero_(), gv.zero_()
+        grad_output = _f32(grad_output)
+        ws = _workspace("f2s_offset_attention_backward_workspace_bytes", batch, points, width,
+                        channels)
+        _lib.call("f2s_offset_attention_backward", _lib.ptr(query), _lib.ptr(key),
+                  _lib.ptr(value), batch, points, width, channels, _lib.ptr(out),
+                  _lib.ptr(grad_output), _lib.ptr(gq), _lib.ptr(gk), _lib.ptr(gv), _lib.ptr(ws),
+                  ws.numel(), _lib.stream_handle())
+        return gq, gk, gv
 
 
 def reduce_neighbor_messages(content, geometry, indices, hpe_input_weight, hpe_input_bias,
@@ -134,6 +172,18 @@ def reduce_neighbor_messages(content, geometry, indices, hpe_input_weight, hpe_i
                hpe_output_bias, hpe_norm_weight, hpe_norm_bias, message_norm_weight,
                message_norm_bias)
     _require_cuda(*tensors)
+    if _needs_grad(*tensors):
+        if precision != "fp32":
+            raise ValueError("the tensor-core neighbour stage has no backward; use "
+                             "precision='fp32'")
+        return _NeighborMessages.apply(*tensors)
+    return _neighbor_forward(tensors, precision)
+
+
+def _neighbor_forward(tensors, precision="fp32"):
+    content, geometry, indices = tensors[:3]
+    channels, hidden_channels = tensors[5].shape
+    input_channels = geometry.shape[-1]
     batch, points, neighbors = indices.shape
     out = torch.empty((batch, channels, points), dtype=torch.float32, device=content.device)
     if out.numel() == 0:
@@ -150,6 +200,91 @@ def reduce_neighbor_messages(content, geometry, indices, hpe_input_weight, hpe_i
               hidden_channels, channels, _lib.ptr(out), _lib.ptr(ws), ws.numel(),
               _lib.stream_handle())
     return out
+
+
+class _NeighborMessages(torch.autograd.Function):
+    """reduce_neighbor_messages with its backward (_NeighborMessageFunction,
+    flow2surf/models/ops/neighbor_reduce.py:113-237): the fp32 fused forward,
+    and a backward that recomputes the HPE rows and the contribution."""
+
+    @staticmethod
+    def forward(ctx, *tensors):
+        tensors = tuple(t.contiguous() if i == 2 else _f32(t) for i, t in enumerate(tensors))
+        ctx.save_for_backward(*tensors)
+        return _neighbor_forward(tensors)
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        t = ctx.saved_tensors
+        content, geometry, indices = t[:3]
+        channels, hidden = t[5].shape
+        batch, points, neighbors = indices.shape
+        dims = geometry.shape[-1]
+        grads = [torch.empty_like(x) for i, x in enumerate(t) if i != 2]
+        if content.numel() == 0 or indices.numel() == 0:
+            return tuple(None if i == 2 else torch.zeros_like(x) for i, x in enumerate(t))
+        grad_output = _f32(grad_output)
+        ws = _workspace("f2s_neighbor_reduce_backward_workspace_bytes", batch, points,
+                        neighbors, dims, hidden, channels)
+        _lib.call("f2s_neighbor_reduce_backward", *[_lib.ptr(x) for x in t], batch, points,
+                  neighbors, dims, hidden, channels, _lib.ptr(grad_output),
+                  *[_lib.ptr(g) for g in grads], _lib.ptr(ws), ws.numel(), _lib.stream_handle())
+        return (grads[0], grads[1], None, *grads[2:])
+
+
+def hpe_activation_grad(preactivation: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor,
+                        grad_hidden: torch.Tensor):
+    """Gradients of the HPE activation (moment LayerNorm, eps 1e-5, then the
+    exact GELU) with respect to the pre-activations (..., H), the norm weight
+    and the norm bias (flow2surf/models/ops/hpe.py:82-96)."""
+    if preactivation.shape != grad_hidden.shape:
+        raise ValueError(f"grad_hidden {tuple(grad_hidden.shape)} does not match "
+                         f"preactivation {tuple(preactivation.shape)}")
+    H = preactivation.shape[-1]
+    if weight.shape != (H,) or bias.shape != (H,):
+        raise ValueError(f"norm weight and bias must be ({H},)")
+    _require_cuda(preactivation, weight, bias, grad_hidden)
+    pre, w, b, gh = (_f32(x) for x in (preactivation, weight, bias, grad_hidden))
+    rows = pre.numel() // H if H else 0
+    gp, gw, gb = torch.empty_like(pre), torch.empty_like(w), torch.empty_like(b)
+    if rows == 0:
+        return gp, gw.zero_(), gb.zero_()
+    size = ctypes.c_size_t()
+    _lib.check(_lib.lib().f2s_hpe_activation_backward_workspace_bytes(rows, H, ctypes.byref(size)))
+    ws = torch.empty(size.value, dtype=torch.uint8, device=pre.device)
+    _lib.call("f2s_hpe_activation_backward", _lib.ptr(pre), rows, H, _lib.ptr(w), _lib.ptr(b),
+              _lib.ptr(gh), _lib.ptr(gp), _lib.ptr(gw), _lib.ptr(gb), _lib.ptr(ws), ws.numel(),
+              _lib.stream_handle())
+    return gp, gw, gb
+
+
+def reduce_messages_grad(content, contribution, indices, weight, bias, output, grad_output):
+    """Gradients of the normalised message max-reduction
+    (_reduce_messages_grad, flow2surf/models/ops/neighbor_reduce.py:57-72):
+    content (B, 2C, N), contribution (B, N, K, C), indices (B, N, K) int32,
+    weight / bias (C,), the forward's output and grad_output (B, C, N) ->
+    grad_content, grad_contribution, grad_weight, grad_bias. The edges that
+    reach each maximum (all exact ties) are found from the recomputed
+    activations, so `output` is accepted for the reference's signature only."""
+    del output
+    _require_cuda(content, contribution, indices, weight, bias, grad_output)
+    if indices.dtype != torch.int32:
+        raise ValueError(f"indices must be int32, got {indices.dtype}")
+    B, N, K = indices.shape
+    C = contribution.shape[-1]
+    content, contribution, weight, bias, grad_output = (
+        _f32(x) for x in (content, contribution, weight, bias, grad_output))
+    indices = indices.contiguous()
+    gc, gk = torch.empty_like(content), torch.empty_like(contribution)
+    gw, gb = torch.empty_like(weight), torch.empty_like(bias)
+    if B == 0:
+        return gc, gk, gw.zero_(), gb.zero_()
+    ws = _workspace("f2s_neighbor_messages_backward_workspace_bytes", B, N, C)
+    _lib.call("f2s_neighbor_messages_backward", _lib.ptr(content), _lib.ptr(contribution),
+              _lib.ptr(indices), B, N, K, C, _lib.ptr(weight), _lib.ptr(bias),
+              _lib.ptr(grad_output), _lib.ptr(gc), _lib.ptr(gk), _lib.ptr(gw), _lib.ptr(gb),
+              _lib.ptr(ws), ws.numel(), _lib.stream_handle())
+    return gc, gk, gw, gb
 
 
 def nearest_squared_distances(first: torch.Tensor, second: torch.Tensor):
@@ -171,6 +306,16 @@ def nearest_squared_distances(first: torch.Tensor, second: torch.Tensor):
     if first.dtype != second.dtype:
         raise ValueError(f"Dtypes differ: {first.dtype} and {second.dtype}")
     _require_cuda(first, second)
+    if _needs_grad(first, second):
+        return _NearestDistance.apply(first, second)
+    return _nearest_forward(first, second)
+
+
+def _needs_grad(*tensors) -> bool:
+    return torch.is_grad_enabled() and any(t.requires_grad for t in tensors)
+
+
+def _nearest_forward(first, second):
     first, second = _f32(first), _f32(second)
     B, M, _ = first.shape
     N = second.shape[1]
@@ -186,6 +331,34 @@ def nearest_squared_distances(first: torch.Tensor, second: torch.Tensor):
               _lib.ptr(i2), _lib.ptr(d2), _lib.ptr(i1), _lib.ptr(ws), ws.numel(),
               _lib.stream_handle())
     return d1, i2, d2, i1
+
+
+class _NearestDistance(torch.autograd.Function):
+    """Nearest squared distances with the exact coordinate gradient
+    (_NearestDistanceFunction, flow2surf/training/distances.py:20-62)."""
+
+    @staticmethod
+    def forward(ctx, first, second):
+        first, second = _f32(first), _f32(second)
+        d1, i2, d2, i1 = _nearest_forward(first, second)
+        ctx.save_for_backward(first, second, i2, i1)
+        ctx.mark_non_differentiable(i2, i1)
+        return d1, i2, d2, i1
+
+    @staticmethod
+    def backward(ctx, g1, _gi2, g2, _gi1):
+        first, second, i2, i1 = ctx.saved_tensors
+        B, M, _ = first.shape
+        N = second.shape[1]
+        gf = torch.empty_like(first)
+        gs = torch.empty_like(second)
+        g1 = None if g1 is None else _f32(g1)
+        g2 = None if g2 is None else _f32(g2)
+        _lib.call("f2s_nearest_backward", _lib.ptr(first), _lib.ptr(second), B, M, N,
+                  _lib.ptr(i2), _lib.ptr(i1), _lib.ptr(g1) if g1 is not None else None,
+                  _lib.ptr(g2) if g2 is not None else None, _lib.ptr(gf), _lib.ptr(gs),
+                  _lib.stream_handle())
+        return gf, gs
 
 
 def chamfer_distances(pred: torch.Tensor, target: torch.Tensor) -> torch.Tensor:
