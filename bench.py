@@ -77,6 +77,10 @@ def parse_args():
     p.add_argument("--profile-chamfer", action="store_true",
                    help="instead of the benchmark: two Chamfer evaluations of a denoised-size "
                         "cloud against a 100,000-point clean sample and exit (ncu case)")
+    p.add_argument("--profile-training", action="store_true",
+                   help="instead of the benchmark: time the training losses and backward "
+                        "passes at the reference's training shapes (64 patches of 1024 "
+                        "points, K 32) and exit")
     p.add_argument("--profile-forward", type=int, default=0, metavar="B",
                    help="instead of the benchmark: two model forwards on B synthetic "
                         "1000-point patches and exit (a small case for ncu captures)")
@@ -191,6 +195,73 @@ def profile_chamfer(args) -> None:
                                clean_points=CHAMFER_REFERENCE_POINTS)
     line = chamfer_leg(torch.from_numpy(noisy).cuda(), torch.from_numpy(ref).cuda(), repeats=1)
     print(json.dumps({"profile_chamfer": line["ms"]}), flush=True)
+
+
+def _event_ms(fn, repeats: int = 3) -> float:
+    import torch
+
+    for _ in range(3):  # warm-up (the caching allocator reaches its working set too)
+        fn()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    start.record()
+    for _ in range(repeats):
+        fn()
+    stop.record()
+    torch.cuda.synchronize()
+    return start.elapsed_time(stop) / repeats
+
+
+def profile_training(args) -> None:
+    """The training losses and backward passes at the reference's training
+    shapes (configs/default.yaml: 8 meshes x 8 patches of 1024 points, K 32,
+    feature width 192, dcd_alpha 8000; the last neighbour stage: 6 geometry
+    inputs, HPE width 128, 192 channels), forward + backward each, timed with
+    CUDA events on synthetic inputs."""
+    import torch
+
+    from flow2surf_b200.losses import dcd_loss, velocity_loss
+    from flow2surf_b200.ops import offset_attention_aggregate, reduce_neighbor_messages
+
+    B, N, K, D, H, C, d = 64, 1024, 32, 6, 128, 192, 48
+    g = torch.Generator(device="cuda").manual_seed(0)
+
+    def rnd(*shape, scale=1.0, grad=True):
+        return (torch.randn(*shape, generator=g, device="cuda") * scale).requires_grad_(grad)
+
+    out = {}
+    pred, target = rnd(B, N, 3, scale=0.3), rnd(B, N, 3, scale=0.3, grad=False)
+    out["dcd_loss_ms"] = _event_ms(lambda: dcd_loss(pred, target, 8000.0).sum().backward())
+    vp, vt = rnd(B, N, 3), rnd(B, N, 3, grad=False)
+    out["velocity_loss_ms"] = _event_ms(lambda: velocity_loss(vp, vt).sum().backward())
+    content = rnd(B, 2 * C, N)
+    geometry = rnd(B, N, K, D)
+    idx = torch.randint(0, N, (B, N, K), generator=g, device="cuda", dtype=torch.int32)
+    params = [rnd(H, D, scale=0.5), rnd(H, scale=0.1), rnd(C, H, scale=H ** -0.5),
+              rnd(C, scale=0.1), (1 + rnd(H, scale=0.1, grad=False)).requires_grad_(),
+              rnd(H, scale=0.1), (1 + rnd(C, scale=0.1, grad=False)).requires_grad_(),
+              rnd(C, scale=0.1)]
+    go = torch.randn(B, C, N, generator=g, device="cuda")
+    fwd = _event_ms(lambda: reduce_neighbor_messages(content, geometry, idx, *params).detach())
+    both = _event_ms(lambda: (reduce_neighbor_messages(content, geometry, idx, *params) * go)
+                     .sum().backward())
+    out["neighbor_reduce_forward_ms"] = fwd
+    out["neighbor_reduce_backward_ms"] = both - fwd
+    q = torch.nn.functional.layer_norm(torch.randn(B, N, d, generator=g, device="cuda"), (d,))
+    k = torch.nn.functional.layer_norm(torch.randn(B, N, d, generator=g, device="cuda"),
+                                       (d,)).transpose(1, 2).contiguous()
+    q.requires_grad_()
+    k.requires_grad_()
+    v = rnd(B, N, C)
+    ga = torch.randn(B, N, C, generator=g, device="cuda")
+    afwd = _event_ms(lambda: offset_attention_aggregate(q, k, v).detach())
+    aboth = _event_ms(lambda: (offset_attention_aggregate(q, k, v) * ga).sum().backward())
+    out["offset_attention_forward_ms"] = afwd
+    out["offset_attention_backward_ms"] = aboth - afwd
+    flops = B * 2.0 * N * N * (3 * d + 2 * C)  # S, dV, G V^T, dQ, dK
+    out["offset_attention_backward_tflops"] = flops / ((aboth - afwd) * 1e-3) / 1e12
+    out["shapes"] = {"patches": B, "points": N, "k": K, "hpe": H, "channels": C, "qk": d}
+    print(json.dumps({"profile_training": out}), flush=True)
 
 
 def workload_config(args, world: int) -> dict:
@@ -613,6 +684,9 @@ def main():
         return
     if args.profile_chamfer:
         profile_chamfer(args)
+        return
+    if args.profile_training:
+        profile_training(args)
         return
     if world > 1:
         import torch

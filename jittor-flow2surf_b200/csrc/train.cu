@@ -20,6 +20,10 @@
 #include "kernels.cuh"
 
 namespace f2s {
+
+int transpose_batched(const float* in, float* out, int B, int rows, int cols,
+                      cudaStream_t stream);
+
 namespace {
 
 constexpr int kBlock = 256;
@@ -34,19 +38,26 @@ size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 // ---------------------------------------------------------------------------
 // Column sums of per-block partials in a fixed order: out[c] = sum over p of
-// part[p * cols + c] (+ out[c] when accumulate).
+// part[p * pitch + c], in float64.
 // ---------------------------------------------------------------------------
 __global__ void sum_partials_kernel(const float* __restrict__ part, int parts, int cols,
-                                    float* __restrict__ out) {
+                                    int pitch, float* __restrict__ out) {
     const int c = blockIdx.x * blockDim.x + threadIdx.x;
     if (c >= cols) return;
     double s = 0.0;
-    for (int p = 0; p < parts; ++p) s += (double)part[(size_t)p * cols + c];
+    for (int p = 0; p < parts; ++p) s += (double)part[(size_t)p * pitch + c];
     out[c] = (float)s;
 }
 
 int sum_partials(const float* part, int parts, int cols, float* out, cudaStream_t st) {
-    sum_partials_kernel<<<(cols + 255) / 256, 256, 0, st>>>(part, parts, cols, out);
+    sum_partials_kernel<<<(cols + 255) / 256, 256, 0, st>>>(part, parts, cols, cols, out);
+    return check_launch("sum_partials_kernel");
+}
+
+// the same with partial rows pitch floats apart (cols <= pitch)
+int sum_partials_strided(const float* part, int parts, int cols, int pitch, float* out,
+                         cudaStream_t st) {
+    sum_partials_kernel<<<(cols + 255) / 256, 256, 0, st>>>(part, parts, cols, pitch, out);
     return check_launch("sum_partials_kernel");
 }
 
@@ -391,20 +402,11 @@ int hpe_activation_backward(const float* pre, int64_t rows, int H, const float* 
 // Neighbour-message reduction backward (neighbor_reduce_backward.cu:20-84)
 // ---------------------------------------------------------------------------
 
-__global__ void zero_neighbor_rows_kernel(float* __restrict__ grad_content, int B, int C, int N) {
-    const int64_t per = (int64_t)C * N, total = (int64_t)B * per;
-    for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
-         e += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t b = e / per;
-        grad_content[b * 2 * per + (e - b * per)] = 0.0f;
-    }
-}
-
 // The message of edge k of point n, channels lane + 32 t, normalised: returns
 // the activation in act (LeakyReLU 0.2 of the affine LayerNorm, two-pass,
 // eps 1e-6), the normalised values, slope and inv_std.
 template <int kCPL>
-__device__ __forceinline__ void edge_message(const float* __restrict__ content,
+__device__ __forceinline__ void edge_message(const float* __restrict__ content_pm,
                                              const float* __restrict__ contribution, int64_t b,
                                              int n, int j, int64_t edge, int C, int N,
                                              const float (&center)[kCPL], const float (&wv)[kCPL],
@@ -418,7 +420,7 @@ __device__ __forceinline__ void edge_message(const float* __restrict__ content,
 #pragma unroll
     for (int t = 0; t < kCPL; ++t) {
         const int c = lane + 32 * t;
-        m[t] = c < C ? content[(b * 2 * C + c) * N + j] + center[t] + contribution[edge * C + c]
+        m[t] = c < C ? content_pm[(b * N + j) * 2 * C + c] + center[t] + contribution[edge * C + c]
                      : 0.0f;
         s += m[t];
     }
@@ -440,12 +442,13 @@ __device__ __forceinline__ void edge_message(const float* __restrict__ content,
     }
 }
 
-// A warp per point: the K edges' activations recomputed once for the maximum
-// of each channel, then again to route the upstream gradient to every edge
-// that reaches it (all exact ties), through the LayerNorm to the message:
-// grad_contribution[edge] stored, the neighbour part added into
-// grad_content[:, :C, j] (atomics), the centre part summed into
-// grad_content[:, C:, n]; the norm weight / bias gradients into per-block
+// A warp per point, on a point-major copy of the content (B, N, 2C): the K
+// edges' activations recomputed once for the maximum of each channel, then
+// again to route the upstream gradient to every edge that reaches it (all
+// exact ties), through the LayerNorm to the message: grad_contribution[edge]
+// stored, the neighbour part added into row j of the point-major gradient
+// grad_pm (B, N, 2C) (atomics, channels [0, C)), the centre part summed into
+// channels [C, 2C) of row n; the norm weight / bias gradients into per-block
 // partial rows. A neighbour index outside [0, N) reads the point itself and
 // scatters nothing.
 template <int kCPL>
@@ -453,7 +456,7 @@ __global__ void __launch_bounds__(kBlock)
 messages_grad_kernel(const float* __restrict__ content, const float* __restrict__ contribution,
                      const int32_t* __restrict__ indices, int B, int N, int K, int C,
                      const float* __restrict__ weight, const float* __restrict__ bias,
-                     const float* __restrict__ grad_output, float* __restrict__ grad_content,
+                     const float* __restrict__ grad_output, float* __restrict__ grad_pm,
                      float* __restrict__ grad_contribution, float* __restrict__ part_w,
                      float* __restrict__ part_b) {
     extern __shared__ float red[];  // [8][C]
@@ -477,7 +480,7 @@ messages_grad_kernel(const float* __restrict__ content, const float* __restrict_
 #pragma unroll
         for (int t = 0; t < kCPL; ++t) {
             const int c = lane + 32 * t;
-            center[t] = c < C ? content[(b * 2 * C + C + c) * N + n] : 0.0f;
+            center[t] = c < C ? content[(b * N + n) * 2 * C + C + c] : 0.0f;
             up[t] = c < C ? grad_output[(b * C + c) * N + n] : 0.0f;
             mx[t] = -FLT_MAX;
             csum[t] = 0.0f;
@@ -519,7 +522,7 @@ messages_grad_kernel(const float* __restrict__ content, const float* __restrict_
                 if (c < C) {
                     const float gr = inv_std * (wt[t] - t1 - nrm[t] * t2);
                     grad_contribution[edge * C + c] = gr;
-                    if (valid) atomicAdd(&grad_content[(b * 2 * C + c) * N + j], gr);
+                    if (valid) atomicAdd(&grad_pm[(b * N + j) * 2 * C + c], gr);
                     csum[t] += gr;
                 }
             }
@@ -527,7 +530,7 @@ messages_grad_kernel(const float* __restrict__ content, const float* __restrict_
 #pragma unroll
         for (int t = 0; t < kCPL; ++t) {
             const int c = lane + 32 * t;
-            if (c < C) grad_content[(b * 2 * C + C + c) * N + n] = csum[t];
+            if (c < C) grad_pm[(b * N + n) * 2 * C + C + c] = csum[t];
         }
     }
     block_channel_partial<kCPL>(aw, C, red, part_w + (size_t)blockIdx.x * C);
@@ -540,22 +543,23 @@ int messages_grad_blocks(int64_t points) {
     return (int)(b < 1 ? 1 : (b < cap ? b : cap));
 }
 
+// content_pm and grad_pm: B * N * 2C floats each of workspace.
 int messages_backward(const float* content, const float* contribution, const int32_t* indices,
                       int B, int N, int K, int C, const float* w, const float* b,
                       const float* grad_output, float* grad_content, float* grad_contribution,
-                      float* grad_w, float* grad_b, float* part, cudaStream_t st) {
+                      float* grad_w, float* grad_b, float* part, float* content_pm,
+                      float* grad_pm, cudaStream_t st) {
     const int64_t points = (int64_t)B * N;
-    zero_neighbor_rows_kernel<<<blocks_for((int64_t)B * C * N), kBlock, 0, st>>>(grad_content, B,
-                                                                                 C, N);
-    F2S_TRY(check_launch("zero_neighbor_rows_kernel"));
+    F2S_TRY(transpose_batched(content, content_pm, B, 2 * C, N, st));
+    F2S_CUDA_TRY(cudaMemsetAsync(grad_pm, 0, (size_t)points * 2 * C * sizeof(float), st));
     const int blocks = messages_grad_blocks(points);
     float* part_w = part;
     float* part_b = part + (size_t)blocks * C;
     const size_t smem = (size_t)8 * C * sizeof(float);
 #define F2S_MSG_GRAD(CPL)                                                                      \
-    messages_grad_kernel<CPL><<<blocks, kBlock, smem, st>>>(content, contribution, indices, B, \
-                                                            N, K, C, w, b, grad_output,        \
-                                                            grad_content, grad_contribution,   \
+    messages_grad_kernel<CPL><<<blocks, kBlock, smem, st>>>(content_pm, contribution, indices, \
+                                                            B, N, K, C, w, b, grad_output,     \
+                                                            grad_pm, grad_contribution,        \
                                                             part_w, part_b)
     const int cpl = (C + 31) / 32;
     if (cpl <= 1) F2S_MSG_GRAD(1);
@@ -565,6 +569,7 @@ int messages_backward(const float* content, const float* contribution, const int
     else F2S_MSG_GRAD(8);
 #undef F2S_MSG_GRAD
     F2S_TRY(check_launch("messages_grad_kernel"));
+    F2S_TRY(transpose_batched(grad_pm, grad_content, B, N, 2 * C, st));
     F2S_TRY(sum_partials(part_w, blocks, C, grad_w, st));
     return sum_partials(part_b, blocks, C, grad_b, st);
 }
@@ -633,38 +638,46 @@ __global__ void transpose_small_kernel(const float* __restrict__ in, int rows, i
 }
 
 // Partial sums over a slice of rows of X^T Y (X: R x I, Y: R x J, row-major):
-// part[s][i][j]; blockIdx.z = slice s of rows_per_slice rows, a 32 x 32 tile
-// of (i, j) per block of 32 x 8 threads (4 outputs each).
+// part[s][i][j]; blockIdx.z = slice s of rows_per_slice rows, a 64 x 64 tile
+// of (i, j) per block of 256 threads (4 x 4 outputs each), 16 rows a step.
 __global__ void __launch_bounds__(256)
 xty_partial_kernel(const float* __restrict__ X, int I, const float* __restrict__ Y, int J,
                    int64_t R, int64_t rows_per_slice, float* __restrict__ part) {
-    __shared__ float xs[32][33], ys[32][33];
-    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
-    const int i0 = blockIdx.x * 32, j0 = blockIdx.y * 32;
+    __shared__ __align__(16) float xs[16][64 + 4], ys[16][64 + 4];
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+    const int i0 = blockIdx.x * 64, j0 = blockIdx.y * 64;
     const int64_t r_lo = (int64_t)blockIdx.z * rows_per_slice;
     const int64_t r_hi = r_lo + rows_per_slice < R ? r_lo + rows_per_slice : R;
-    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    for (int64_t r0 = r_lo; r0 < r_hi; r0 += 32) {
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const int rr = ty + 8 * u;
+    float acc[4][4] = {};
+    for (int64_t r0 = r_lo; r0 < r_hi; r0 += 16) {
+        for (int e = threadIdx.x; e < 16 * 64; e += 256) {
+            const int rr = e >> 6, cc = e & 63;
             const int64_t r = r0 + rr;
-            xs[rr][tx] = (r < r_hi && i0 + tx < I) ? X[r * I + i0 + tx] : 0.0f;
-            ys[rr][tx] = (r < r_hi && j0 + tx < J) ? Y[r * J + j0 + tx] : 0.0f;
+            xs[rr][cc] = (r < r_hi && i0 + cc < I) ? X[r * I + i0 + cc] : 0.0f;
+            ys[rr][cc] = (r < r_hi && j0 + cc < J) ? Y[r * J + j0 + cc] : 0.0f;
         }
         __syncthreads();
-#pragma unroll 8
-        for (int rr = 0; rr < 32; ++rr) {
-            const float y = ys[rr][tx];
 #pragma unroll
-            for (int u = 0; u < 4; ++u) acc[u] += xs[rr][ty + 8 * u] * y;
+        for (int rr = 0; rr < 16; ++rr) {
+            const float4 a4 = *reinterpret_cast<const float4*>(&xs[rr][ty * 4]);
+            const float4 b4 = *reinterpret_cast<const float4*>(&ys[rr][tx * 4]);
+            const float a[4] = {a4.x, a4.y, a4.z, a4.w}, bv[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+#pragma unroll
+                for (int v = 0; v < 4; ++v) acc[u][v] += a[u] * bv[v];
         }
         __syncthreads();
     }
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
-        const int i = i0 + ty + 8 * u, j = j0 + tx;
-        if (i < I && j < J) part[((size_t)blockIdx.z * I + i) * J + j] = acc[u];
+        const int i = i0 + ty * 4 + u;
+        if (i >= I) continue;
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+            const int j = j0 + tx * 4 + v;
+            if (j < J) part[((size_t)blockIdx.z * I + i) * J + j] = acc[u][v];
+        }
     }
 }
 
@@ -689,7 +702,7 @@ int xty(const float* X, int I, const float* Y, int J, int64_t R, float* out, flo
         float* part, cudaStream_t st) {
     const int64_t per = slice_rows(R);
     const int slices = (int)((R + per - 1) / per);
-    xty_partial_kernel<<<dim3((I + 31) / 32, (J + 31) / 32, slices), 256, 0, st>>>(X, I, Y, J, R,
+    xty_partial_kernel<<<dim3((I + 63) / 64, (J + 63) / 64, slices), 256, 0, st>>>(X, I, Y, J, R,
                                                                                   per, part);
     F2S_TRY(check_launch("xty_partial_kernel"));
     F2S_TRY(sum_partials(part, slices, I * J, out, st));
@@ -699,26 +712,69 @@ int xty(const float* X, int I, const float* Y, int J, int64_t R, float* out, flo
     return sum_partials(part, slices, I, colsum, st);
 }
 
-// A warp per row: grad_geometry[r][d] = sum_h grad_pre[r][h] W_in[h][d].
+// A warp per row: grad_geometry[r][d] = sum_h grad_pre[r][h] W_in[h][d]; and,
+// per lane for its channels h = lane + 32 t, the input projection's weight
+// gradient sum_r grad_pre[r][h] geometry[r][d] and bias gradient
+// sum_r grad_pre[r][h], into per-block partial rows (H x D, then H).
+template <int kCPL>
 __global__ void __launch_bounds__(kBlock)
-geometry_grad_kernel(const float* __restrict__ grad_pre, int64_t rows, int H, int D,
-                     const float* __restrict__ w_in, float* __restrict__ grad_geometry) {
+geometry_grad_kernel(const float* __restrict__ grad_pre, const float* __restrict__ geometry,
+                     int64_t rows, int H, int D, const float* __restrict__ w_in,
+                     float* __restrict__ grad_geometry, float* __restrict__ part) {
+    extern __shared__ float red[];  // [8][H * (D + 1)]
     const int lane = threadIdx.x & 31;
     const int wpb = blockDim.x >> 5;
+    float aw[kCPL][8], ab[kCPL];
+#pragma unroll
+    for (int t = 0; t < kCPL; ++t) {
+        ab[t] = 0.0f;
+#pragma unroll
+        for (int d = 0; d < 8; ++d) aw[t][d] = 0.0f;
+    }
     for (int64_t row = (int64_t)blockIdx.x * wpb + (threadIdx.x >> 5); row < rows;
          row += (int64_t)gridDim.x * wpb) {
-        float acc[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
-        for (int h = lane; h < H; h += 32) {
-            const float g = grad_pre[row * H + h];
+        float geo[8], acc[8];
 #pragma unroll
-            for (int d = 0; d < 8; ++d)
-                if (d < D) acc[d] += g * w_in[h * D + d];
+        for (int d = 0; d < 8; ++d) {
+            geo[d] = d < D ? geometry[row * D + d] : 0.0f;
+            acc[d] = 0.0f;
+        }
+#pragma unroll
+        for (int t = 0; t < kCPL; ++t) {
+            const int h = lane + 32 * t;
+            if (h >= H) continue;
+            const float g = grad_pre[row * H + h];
+            ab[t] += g;
+#pragma unroll
+            for (int d = 0; d < 8; ++d) {
+                if (d >= D) continue;
+                acc[d] += g * w_in[h * D + d];
+                aw[t][d] += g * geo[d];
+            }
         }
 #pragma unroll
         for (int d = 0; d < 8; ++d) {
-            const float s = warp_sum(acc[d]);
-            if (lane == d && d < D) grad_geometry[row * D + d] = s;
+            const float sum = warp_sum(acc[d]);
+            if (lane == d && d < D) grad_geometry[row * D + d] = sum;
         }
+    }
+    // per-block partial: H * D weight entries (row-major, as W_in), then H biases
+    const int W = H * (D + 1);
+    const int warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int t = 0; t < kCPL; ++t) {
+        const int h = lane + 32 * t;
+        if (h >= H) continue;
+#pragma unroll
+        for (int d = 0; d < 8; ++d)
+            if (d < D) red[warp * W + h * D + d] = aw[t][d];
+        red[warp * W + H * D + h] = ab[t];
+    }
+    __syncthreads();
+    for (int c = threadIdx.x; c < W; c += blockDim.x) {
+        float s = 0.0f;
+        for (int w = 0; w < wpb; ++w) s += red[w * W + c];
+        part[(size_t)blockIdx.x * W + c] = s;
     }
 }
 
@@ -743,7 +799,7 @@ struct Bmm {
 };
 
 __global__ void __launch_bounds__(256) bmm_kernel(const Bmm p) {
-    __shared__ float As[16][64 + 4], Bs[16][64 + 4];
+    __shared__ __align__(16) float As[16][64 + 4], Bs[16][64 + 4];
     const int b = blockIdx.z;
     const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
     const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
@@ -761,12 +817,9 @@ __global__ void __launch_bounds__(256) bmm_kernel(const Bmm p) {
         __syncthreads();
 #pragma unroll
         for (int kk = 0; kk < 16; ++kk) {
-            float a[4], bv[4];
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                a[u] = As[kk][ty * 4 + u];
-                bv[u] = Bs[kk][tx * 4 + u];
-            }
+            const float4 a4 = *reinterpret_cast<const float4*>(&As[kk][ty * 4]);
+            const float4 b4 = *reinterpret_cast<const float4*>(&Bs[kk][tx * 4]);
+            const float a[4] = {a4.x, a4.y, a4.z, a4.w}, bv[4] = {b4.x, b4.y, b4.z, b4.w};
 #pragma unroll
             for (int u = 0; u < 4; ++u)
 #pragma unroll
@@ -893,7 +946,8 @@ AttnSpace attn_space(int B, int N, int C) {
 // The full neighbour-reduction backward: workspace layout
 // ---------------------------------------------------------------------------
 struct NrSpace {
-    size_t pre, hidden, contrib, gcontrib, ghidden, wout_t, win_t, part, bytes;
+    size_t pre, hidden, contrib, gcontrib, ghidden, wout_t, win_t, wsplit, wtsplit, content_pm,
+        grad_pm, part, bytes;
 };
 
 NrSpace nr_space(int B, int N, int K, int D, int H, int C) {
@@ -906,10 +960,16 @@ NrSpace nr_space(int B, int N, int K, int D, int H, int C) {
     s.ghidden = align256(s.gcontrib + R * C * 4);
     s.wout_t = align256(s.ghidden + R * H * 4);
     s.win_t = align256(s.wout_t + (size_t)C * H * 4);
-    s.part = align256(s.win_t + (size_t)H * D * 4);
+    s.wsplit = align256(s.win_t + (size_t)H * D * 4);      // W_out as bf16 high, low
+    s.wtsplit = align256(s.wsplit + (size_t)C * H * 4);    // W_out^T as bf16 high, low
+    s.content_pm = align256(s.wtsplit + (size_t)C * H * 4);
+    s.grad_pm = align256(s.content_pm + (size_t)B * N * 2 * C * 4);
+    s.part = align256(s.grad_pm + (size_t)B * N * 2 * C * 4);
     // partial rows: the per-block kernels (<= 8 per SM) and the row slices
     const size_t blocks = (size_t)sm_count() * 8;
     size_t part = 2 * blocks * (size_t)(H > C ? H : C);
+    const size_t geo = blocks * (size_t)H * (D + 1);
+    part = part > geo ? part : geo;
     const size_t ch = (size_t)C * H, hd = (size_t)H * D;
     const size_t slices = (size_t)kSlices * (ch > hd ? ch : hd);
     part = part > slices ? part : slices;
@@ -1025,7 +1085,9 @@ extern "C" int f2s_hpe_activation_backward(const float* preactivation, int64_t r
 extern "C" int f2s_neighbor_messages_backward_workspace_bytes(int B, int N, int C,
                                                               size_t* bytes) {
     F2S_REQUIRE(B >= 0 && N >= 0 && C >= 1 && bytes, "bad workspace query");
-    *bytes = (size_t)2 * messages_grad_blocks((int64_t)B * N) * C * sizeof(float);
+    const size_t part = align256((size_t)2 * messages_grad_blocks((int64_t)B * N) * C * 4);
+    const size_t pm = align256((size_t)B * N * 2 * C * 4);
+    *bytes = part + 2 * pm;
     return F2S_OK;
 }
 
@@ -1051,9 +1113,14 @@ extern "C" int f2s_neighbor_messages_backward(const float* content, const float*
                     workspace_bytes);
     cudaStream_t st = as_stream(stream);
     TraceScope trace(kTagTraining, st);
+    char* ws = static_cast<char*>(workspace);
+    const size_t part = align256((size_t)2 * messages_grad_blocks((int64_t)B * N) * C * 4);
+    const size_t pm = align256((size_t)B * N * 2 * C * 4);
     return messages_backward(content, contribution, indices, B, N, K, C, norm_weight, norm_bias,
                              grad_output, grad_content, grad_contribution, grad_norm_weight,
-                             grad_norm_bias, static_cast<float*>(workspace), st);
+                             grad_norm_bias, reinterpret_cast<float*>(ws),
+                             reinterpret_cast<float*>(ws + part),
+                             reinterpret_cast<float*>(ws + part + pm), st);
 }
 
 extern "C" int f2s_neighbor_reduce_backward_workspace_bytes(int B, int N, int K, int D, int H,
@@ -1115,46 +1182,48 @@ extern "C" int f2s_neighbor_reduce_backward(
     else F2S_HPE_FWD(8);
 #undef F2S_HPE_FWD
     F2S_TRY(check_launch("hpe_forward_rows_kernel"));
-    GemmArgs g{};
-    g.A = hidden;
-    g.lda = H;
-    g.W = hpe_output_weight;  // (C x H): contribution = hidden W_out^T + b_out
-    g.bias = hpe_output_bias;
-    g.Y = contrib;
-    g.ldy = C;
-    g.rows = (int)R;
-    g.cols = C;
-    g.K = H;
-    g.epilogue = kEpiStore;
-    g.tag = kTagTraining;
+    // the two projection products on the tensor cores as split bf16 (the
+    // fp32 rows split in the GEMM, W_out and its transpose split here;
+    // about 1e-5 relative to sum |x| |w|)
     F2S_LIMIT(R <= INT32_MAX, "neighbor_reduce_backward: %lld edge rows", (long long)R);
-    F2S_TRY(gemm_f32(g, st));
+    void* wsplit = ws + s.wsplit;
+    void* wtsplit = ws + s.wtsplit;
+    F2S_TRY(split_bf16(hpe_output_weight, H, C, H, wsplit,
+                       static_cast<char*>(wsplit) + (size_t)C * H * 2, st));
+    F2S_TRY(f2s_linear(hidden, H, wsplit, hpe_output_bias, contrib, C, (int)R, C, H,
+                       F2S_PRECISION_BF16X3, stream));
     // the message reduction's backward (neighbor_reduce.py:186-202)
     F2S_TRY(messages_backward(content, contrib, indices, B, N, K, C, message_norm_weight,
                               message_norm_bias, grad_output, grad_content, gcontrib,
-                              grad_message_norm_weight, grad_message_norm_bias, part, st));
+                              grad_message_norm_weight, grad_message_norm_bias, part,
+                              reinterpret_cast<float*>(ws + s.content_pm),
+                              reinterpret_cast<float*>(ws + s.grad_pm), st));
     // grad_hidden = grad_contribution W_out; the output projection's gradients
     transpose_small_kernel<<<blocks_for((int64_t)C * H), kBlock, 0, st>>>(hpe_output_weight, C, H,
                                                                           wout_t);
     F2S_TRY(check_launch("transpose_small_kernel"));
-    g.A = gcontrib;
-    g.lda = C;
-    g.W = wout_t;  // (H x C)
-    g.bias = nullptr;
-    g.Y = ghidden;
-    g.ldy = H;
-    g.cols = H;
-    g.K = C;
-    F2S_TRY(gemm_f32(g, st));
+    F2S_TRY(split_bf16(wout_t, C, H, C, wtsplit, static_cast<char*>(wtsplit) + (size_t)C * H * 2,
+                       st));
+    F2S_TRY(f2s_linear(gcontrib, C, wtsplit, nullptr, ghidden, H, (int)R, H, C,
+                       F2S_PRECISION_BF16X3, stream));
     F2S_TRY(xty(gcontrib, C, hidden, H, R, grad_hpe_output_weight, grad_hpe_output_bias, part, st));
     // the HPE activation's backward, in place over grad_hidden (its rows are
     // read before they are written, one warp per row)
     F2S_TRY(hpe_activation_backward(pre, R, H, hpe_norm_weight, hpe_norm_bias, ghidden, ghidden,
                                     grad_hpe_norm_weight, grad_hpe_norm_bias, part, st));
     // the input projection's gradients (neighbor_reduce.py:219-224)
-    geometry_grad_kernel<<<rb, kBlock, 0, st>>>(ghidden, R, H, D, hpe_input_weight, grad_geometry);
+    const size_t gsmem = (size_t)8 * H * (D + 1) * sizeof(float);
+#define F2S_GEO_GRAD(CPL)                                                                          \
+    geometry_grad_kernel<CPL><<<rb, kBlock, gsmem, st>>>(ghidden, geometry, R, H, D,               \
+                                                         hpe_input_weight, grad_geometry, part)
+    if (hcpl <= 1) F2S_GEO_GRAD(1);
+    else if (hcpl <= 2) F2S_GEO_GRAD(2);
+    else if (hcpl <= 4) F2S_GEO_GRAD(4);
+    else F2S_GEO_GRAD(8);
+#undef F2S_GEO_GRAD
     F2S_TRY(check_launch("geometry_grad_kernel"));
-    return xty(ghidden, H, geometry, D, R, grad_hpe_input_weight, grad_hpe_input_bias, part, st);
+    F2S_TRY(sum_partials_strided(part, rb, H * D, H * (D + 1), grad_hpe_input_weight, st));
+    return sum_partials_strided(part + H * D, rb, H, H * (D + 1), grad_hpe_input_bias, st);
 }
 
 extern "C" int f2s_offset_attention_backward_workspace_bytes(int B, int N, int d, int C,
