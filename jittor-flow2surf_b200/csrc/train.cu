@@ -638,41 +638,72 @@ __global__ void transpose_small_kernel(const float* __restrict__ in, int rows, i
 }
 
 // Partial sums over a slice of rows of X^T Y (X: R x I, Y: R x J, row-major):
-// part[s][i][j]; blockIdx.z = slice s of rows_per_slice rows, a 64 x 64 tile
-// of (i, j) per block of 256 threads (4 x 4 outputs each), 16 rows a step.
+// part[s][i][j], and with colsum the slice's column sums of X into
+// colsum[s][i] (from the blocks of the first j tile); blockIdx.z = slice s
+// of rows_per_slice rows, a 64 x 64 tile of (i, j) per block of 256 threads
+// (4 x 4 outputs each), 16 rows a step, the next step's rows loaded into
+// registers while the current one is multiplied (two shared-memory buffers).
 __global__ void __launch_bounds__(256)
 xty_partial_kernel(const float* __restrict__ X, int I, const float* __restrict__ Y, int J,
-                   int64_t R, int64_t rows_per_slice, float* __restrict__ part) {
-    __shared__ __align__(16) float xs[16][64 + 4], ys[16][64 + 4];
+                   int64_t R, int64_t rows_per_slice, float* __restrict__ part,
+                   float* __restrict__ colsum) {
+    __shared__ __align__(16) float xs[2][16][64 + 4], ys[2][16][64 + 4];
     const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
     const int i0 = blockIdx.x * 64, j0 = blockIdx.y * 64;
     const int64_t r_lo = (int64_t)blockIdx.z * rows_per_slice;
     const int64_t r_hi = r_lo + rows_per_slice < R ? r_lo + rows_per_slice : R;
     float acc[4][4] = {};
-    for (int64_t r0 = r_lo; r0 < r_hi; r0 += 16) {
-        for (int e = threadIdx.x; e < 16 * 64; e += 256) {
-            const int rr = e >> 6, cc = e & 63;
+    float cs[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    const bool sums = colsum != nullptr && blockIdx.y == 0 && tx == 0;
+    // this thread's four staging slots of each operand: rows e >> 6, columns e & 63
+    float xr[4], yr[4];
+    auto fetch = [&](int64_t r0) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int e = threadIdx.x + 256 * u, rr = e >> 6, cc = e & 63;
             const int64_t r = r0 + rr;
-            xs[rr][cc] = (r < r_hi && i0 + cc < I) ? X[r * I + i0 + cc] : 0.0f;
-            ys[rr][cc] = (r < r_hi && j0 + cc < J) ? Y[r * J + j0 + cc] : 0.0f;
+            xr[u] = (r < r_hi && i0 + cc < I) ? X[r * I + i0 + cc] : 0.0f;
+            yr[u] = (r < r_hi && j0 + cc < J) ? Y[r * J + j0 + cc] : 0.0f;
         }
-        __syncthreads();
+    };
+    auto stash = [&](int buf) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int e = threadIdx.x + 256 * u, rr = e >> 6, cc = e & 63;
+            xs[buf][rr][cc] = xr[u];
+            ys[buf][rr][cc] = yr[u];
+        }
+    };
+    fetch(r_lo);
+    stash(0);
+    __syncthreads();
+    int buf = 0;
+    for (int64_t r0 = r_lo; r0 < r_hi; r0 += 16) {
+        const bool more = r0 + 16 < r_hi;
+        if (more) fetch(r0 + 16);
 #pragma unroll
         for (int rr = 0; rr < 16; ++rr) {
-            const float4 a4 = *reinterpret_cast<const float4*>(&xs[rr][ty * 4]);
-            const float4 b4 = *reinterpret_cast<const float4*>(&ys[rr][tx * 4]);
+            const float4 a4 = *reinterpret_cast<const float4*>(&xs[buf][rr][ty * 4]);
+            const float4 b4 = *reinterpret_cast<const float4*>(&ys[buf][rr][tx * 4]);
             const float a[4] = {a4.x, a4.y, a4.z, a4.w}, bv[4] = {b4.x, b4.y, b4.z, b4.w};
 #pragma unroll
-            for (int u = 0; u < 4; ++u)
+            for (int u = 0; u < 4; ++u) {
+                cs[u] += a[u];
 #pragma unroll
                 for (int v = 0; v < 4; ++v) acc[u][v] += a[u] * bv[v];
+            }
         }
-        __syncthreads();
+        if (more) {
+            stash(buf ^ 1);  // the other buffer: its last readers passed the barrier below
+            __syncthreads();
+            buf ^= 1;
+        }
     }
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
         const int i = i0 + ty * 4 + u;
         if (i >= I) continue;
+        if (sums) colsum[(size_t)blockIdx.z * I + i] = cs[u];
 #pragma unroll
         for (int v = 0; v < 4; ++v) {
             const int j = j0 + tx * 4 + v;
@@ -681,35 +712,23 @@ xty_partial_kernel(const float* __restrict__ X, int I, const float* __restrict__
     }
 }
 
-// Partial column sums of X (R x I) over slices of rows: part[s][i].
-__global__ void colsum_partial_kernel(const float* __restrict__ X, int I, int64_t R,
-                                      int64_t rows_per_slice, float* __restrict__ part) {
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= I) return;
-    const int64_t r_lo = (int64_t)blockIdx.y * rows_per_slice;
-    const int64_t r_hi = r_lo + rows_per_slice < R ? r_lo + rows_per_slice : R;
-    float s = 0.0f;
-    for (int64_t r = r_lo; r < r_hi; ++r) s += X[r * I + i];
-    part[(size_t)blockIdx.y * I + i] = s;
-}
-
 constexpr int kSlices = 128;  // row slices of the parameter reductions
 
 int64_t slice_rows(int64_t R) { return (R + kSlices - 1) / kSlices; }
 
-// out (I x J) = X^T Y and, with colsum, colsum = the column sums of X.
+// out (I x J) = X^T Y and, with colsum, colsum = the column sums of X
+// (part: slices x (I x J + I) floats).
 int xty(const float* X, int I, const float* Y, int J, int64_t R, float* out, float* colsum,
         float* part, cudaStream_t st) {
     const int64_t per = slice_rows(R);
     const int slices = (int)((R + per - 1) / per);
-    xty_partial_kernel<<<dim3((I + 63) / 64, (J + 63) / 64, slices), 256, 0, st>>>(X, I, Y, J, R,
-                                                                                  per, part);
+    float* part_cs = part + (size_t)slices * I * J;
+    xty_partial_kernel<<<dim3((I + 63) / 64, (J + 63) / 64, slices), 256, 0, st>>>(
+        X, I, Y, J, R, per, part, colsum ? part_cs : nullptr);
     F2S_TRY(check_launch("xty_partial_kernel"));
     F2S_TRY(sum_partials(part, slices, I * J, out, st));
     if (!colsum) return F2S_OK;
-    colsum_partial_kernel<<<dim3((I + 255) / 256, slices), 256, 0, st>>>(X, I, R, per, part);
-    F2S_TRY(check_launch("colsum_partial_kernel"));
-    return sum_partials(part, slices, I, colsum, st);
+    return sum_partials(part_cs, slices, I, colsum, st);
 }
 
 // A warp per row: grad_geometry[r][d] = sum_h grad_pre[r][h] W_in[h][d]; and,
@@ -724,12 +743,16 @@ geometry_grad_kernel(const float* __restrict__ grad_pre, const float* __restrict
     extern __shared__ float red[];  // [8][H * (D + 1)]
     const int lane = threadIdx.x & 31;
     const int wpb = blockDim.x >> 5;
-    float aw[kCPL][8], ab[kCPL];
+    float aw[kCPL][8], ab[kCPL], wr[kCPL][8];
 #pragma unroll
     for (int t = 0; t < kCPL; ++t) {
         ab[t] = 0.0f;
+        const int h = lane + 32 * t;
 #pragma unroll
-        for (int d = 0; d < 8; ++d) aw[t][d] = 0.0f;
+        for (int d = 0; d < 8; ++d) {
+            aw[t][d] = 0.0f;
+            wr[t][d] = (h < H && d < D) ? w_in[h * D + d] : 0.0f;
+        }
     }
     for (int64_t row = (int64_t)blockIdx.x * wpb + (threadIdx.x >> 5); row < rows;
          row += (int64_t)gridDim.x * wpb) {
@@ -748,7 +771,7 @@ geometry_grad_kernel(const float* __restrict__ grad_pre, const float* __restrict
 #pragma unroll
             for (int d = 0; d < 8; ++d) {
                 if (d >= D) continue;
-                acc[d] += g * w_in[h * D + d];
+                acc[d] += g * wr[t][d];
                 aw[t][d] += g * geo[d];
             }
         }
@@ -970,7 +993,7 @@ NrSpace nr_space(int B, int N, int K, int D, int H, int C) {
     size_t part = 2 * blocks * (size_t)(H > C ? H : C);
     const size_t geo = blocks * (size_t)H * (D + 1);
     part = part > geo ? part : geo;
-    const size_t ch = (size_t)C * H, hd = (size_t)H * D;
+    const size_t ch = (size_t)C * H + C, hd = (size_t)H * D + H;
     const size_t slices = (size_t)kSlices * (ch > hd ? ch : hd);
     part = part > slices ? part : slices;
     s.bytes = align256(s.part + part * 4);
