@@ -734,27 +734,26 @@ int xty(const float* X, int I, const float* Y, int J, int64_t R, float* out, flo
 // A warp per row: grad_geometry[r][d] = sum_h grad_pre[r][h] W_in[h][d]; and,
 // per lane for its channels h = lane + 32 t, the input projection's weight
 // gradient sum_r grad_pre[r][h] geometry[r][d] and bias gradient
-// sum_r grad_pre[r][h], into per-block partial rows (H x D, then H).
+// sum_r grad_pre[r][h], accumulated in the warp's own rows of shared memory
+// (a lane touches only its channels' entries) and summed over the warps into
+// one partial row per block (H x D, then H). W_in is read from shared memory.
 template <int kCPL>
 __global__ void __launch_bounds__(kBlock)
 geometry_grad_kernel(const float* __restrict__ grad_pre, const float* __restrict__ geometry,
                      int64_t rows, int H, int D, const float* __restrict__ w_in,
                      float* __restrict__ grad_geometry, float* __restrict__ part) {
-    extern __shared__ float red[];  // [8][H * (D + 1)]
+    extern __shared__ float sm[];  // W_in [H * D], then [8][H * (D + 1)] accumulators
     const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
     const int wpb = blockDim.x >> 5;
-    float aw[kCPL][8], ab[kCPL], wr[kCPL][8];
-#pragma unroll
-    for (int t = 0; t < kCPL; ++t) {
-        ab[t] = 0.0f;
-        const int h = lane + 32 * t;
-#pragma unroll
-        for (int d = 0; d < 8; ++d) {
-            aw[t][d] = 0.0f;
-            wr[t][d] = (h < H && d < D) ? w_in[h * D + d] : 0.0f;
-        }
-    }
-    for (int64_t row = (int64_t)blockIdx.x * wpb + (threadIdx.x >> 5); row < rows;
+    const int W = H * (D + 1);
+    float* wsm = sm;
+    float* red = sm + H * D;
+    for (int e = threadIdx.x; e < H * D; e += blockDim.x) wsm[e] = w_in[e];
+    for (int e = threadIdx.x; e < wpb * W; e += blockDim.x) red[e] = 0.0f;
+    __syncthreads();
+    float* mine = red + warp * W;
+    for (int64_t row = (int64_t)blockIdx.x * wpb + warp; row < rows;
          row += (int64_t)gridDim.x * wpb) {
         float geo[8], acc[8];
 #pragma unroll
@@ -767,12 +766,12 @@ geometry_grad_kernel(const float* __restrict__ grad_pre, const float* __restrict
             const int h = lane + 32 * t;
             if (h >= H) continue;
             const float g = grad_pre[row * H + h];
-            ab[t] += g;
+            mine[H * D + h] += g;
 #pragma unroll
             for (int d = 0; d < 8; ++d) {
                 if (d >= D) continue;
-                acc[d] += g * wr[t][d];
-                aw[t][d] += g * geo[d];
+                acc[d] += g * wsm[h * D + d];
+                mine[h * D + d] += g * geo[d];
             }
         }
 #pragma unroll
@@ -780,18 +779,6 @@ geometry_grad_kernel(const float* __restrict__ grad_pre, const float* __restrict
             const float sum = warp_sum(acc[d]);
             if (lane == d && d < D) grad_geometry[row * D + d] = sum;
         }
-    }
-    // per-block partial: H * D weight entries (row-major, as W_in), then H biases
-    const int W = H * (D + 1);
-    const int warp = threadIdx.x >> 5;
-#pragma unroll
-    for (int t = 0; t < kCPL; ++t) {
-        const int h = lane + 32 * t;
-        if (h >= H) continue;
-#pragma unroll
-        for (int d = 0; d < 8; ++d)
-            if (d < D) red[warp * W + h * D + d] = aw[t][d];
-        red[warp * W + H * D + h] = ab[t];
     }
     __syncthreads();
     for (int c = threadIdx.x; c < W; c += blockDim.x) {
@@ -1235,7 +1222,7 @@ extern "C" int f2s_neighbor_reduce_backward(
     F2S_TRY(hpe_activation_backward(pre, R, H, hpe_norm_weight, hpe_norm_bias, ghidden, ghidden,
                                     grad_hpe_norm_weight, grad_hpe_norm_bias, part, st));
     // the input projection's gradients (neighbor_reduce.py:219-224)
-    const size_t gsmem = (size_t)8 * H * (D + 1) * sizeof(float);
+    const size_t gsmem = ((size_t)H * D + (size_t)8 * H * (D + 1)) * sizeof(float);
 #define F2S_GEO_GRAD(CPL)                                                                          \
     geometry_grad_kernel<CPL><<<rb, kBlock, gsmem, st>>>(ghidden, geometry, R, H, D,               \
                                                          hpe_input_weight, grad_geometry, part)
