@@ -640,37 +640,49 @@ __global__ void transpose_small_kernel(const float* __restrict__ in, int rows, i
 // Partial sums over a slice of rows of X^T Y (X: R x I, Y: R x J, row-major):
 // part[s][i][j], and with colsum the slice's column sums of X into
 // colsum[s][i] (from the blocks of the first j tile); blockIdx.z = slice s
-// of rows_per_slice rows, a 64 x 64 tile of (i, j) per block of 256 threads
-// (4 x 4 outputs each), 16 rows a step, the next step's rows loaded into
-// registers while the current one is multiplied (two shared-memory buffers).
+// of rows_per_slice rows, a 96 x 128 tile of (i, j) per block of 256 threads
+// (16 x 16, 6 x 8 outputs each), 16 rows a step, the next step's rows
+// loaded into registers while the current one is multiplied (two
+// shared-memory buffers).
+constexpr int kXtyI = 96, kXtyJ = 128;
+
 __global__ void __launch_bounds__(256)
 xty_partial_kernel(const float* __restrict__ X, int I, const float* __restrict__ Y, int J,
                    int64_t R, int64_t rows_per_slice, float* __restrict__ part,
                    float* __restrict__ colsum) {
-    __shared__ __align__(16) float xs[2][16][64 + 4], ys[2][16][64 + 4];
+    __shared__ __align__(16) float xs[2][16][kXtyI + 4], ys[2][16][kXtyJ + 4];
     const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
-    const int i0 = blockIdx.x * 64, j0 = blockIdx.y * 64;
+    const int i0 = blockIdx.x * kXtyI, j0 = blockIdx.y * kXtyJ;
     const int64_t r_lo = (int64_t)blockIdx.z * rows_per_slice;
     const int64_t r_hi = r_lo + rows_per_slice < R ? r_lo + rows_per_slice : R;
-    float acc[4][4] = {};
-    float cs[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    float acc[6][8] = {};
+    float cs[6] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
     const bool sums = colsum != nullptr && blockIdx.y == 0 && tx == 0;
-    // this thread's four staging slots of each operand: rows e >> 6, columns e & 63
-    float xr[4], yr[4];
+    // staging: X rows 16 x 96 (6 per thread), Y rows 16 x 128 (8 per thread)
+    float xr[6], yr[8];
     auto fetch = [&](int64_t r0) {
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const int e = threadIdx.x + 256 * u, rr = e >> 6, cc = e & 63;
+        for (int u = 0; u < 6; ++u) {
+            const int e = threadIdx.x + 256 * u, rr = e / kXtyI, cc = e - rr * kXtyI;
             const int64_t r = r0 + rr;
             xr[u] = (r < r_hi && i0 + cc < I) ? X[r * I + i0 + cc] : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int e = threadIdx.x + 256 * u, rr = e >> 7, cc = e & 127;
+            const int64_t r = r0 + rr;
             yr[u] = (r < r_hi && j0 + cc < J) ? Y[r * J + j0 + cc] : 0.0f;
         }
     };
     auto stash = [&](int buf) {
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const int e = threadIdx.x + 256 * u, rr = e >> 6, cc = e & 63;
+        for (int u = 0; u < 6; ++u) {
+            const int e = threadIdx.x + 256 * u, rr = e / kXtyI, cc = e - rr * kXtyI;
             xs[buf][rr][cc] = xr[u];
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int e = threadIdx.x + 256 * u, rr = e >> 7, cc = e & 127;
             ys[buf][rr][cc] = yr[u];
         }
     };
@@ -683,14 +695,21 @@ xty_partial_kernel(const float* __restrict__ X, int I, const float* __restrict__
         if (more) fetch(r0 + 16);
 #pragma unroll
         for (int rr = 0; rr < 16; ++rr) {
-            const float4 a4 = *reinterpret_cast<const float4*>(&xs[buf][rr][ty * 4]);
-            const float4 b4 = *reinterpret_cast<const float4*>(&ys[buf][rr][tx * 4]);
-            const float a[4] = {a4.x, a4.y, a4.z, a4.w}, bv[4] = {b4.x, b4.y, b4.z, b4.w};
+            // this thread's rows i0 + 6 ty .. + 5 and columns j0 + 4 tx, + 64
+            // (6 ty floats = 24 ty bytes: 8-byte aligned, so three 8-byte
+            // loads; the Y columns 4 tx and 64 + 4 tx are 16-byte aligned)
+            const float2 a0 = *reinterpret_cast<const float2*>(&xs[buf][rr][ty * 6]);
+            const float2 a1 = *reinterpret_cast<const float2*>(&xs[buf][rr][ty * 6 + 2]);
+            const float2 a2 = *reinterpret_cast<const float2*>(&xs[buf][rr][ty * 6 + 4]);
+            const float4 b0 = *reinterpret_cast<const float4*>(&ys[buf][rr][tx * 4]);
+            const float4 b1 = *reinterpret_cast<const float4*>(&ys[buf][rr][64 + tx * 4]);
+            const float a[6] = {a0.x, a0.y, a1.x, a1.y, a2.x, a2.y};
+            const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
+            for (int u = 0; u < 6; ++u) {
                 cs[u] += a[u];
 #pragma unroll
-                for (int v = 0; v < 4; ++v) acc[u][v] += a[u] * bv[v];
+                for (int v = 0; v < 8; ++v) acc[u][v] += a[u] * bv[v];
             }
         }
         if (more) {
@@ -700,19 +719,19 @@ xty_partial_kernel(const float* __restrict__ X, int I, const float* __restrict__
         }
     }
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-        const int i = i0 + ty * 4 + u;
+    for (int u = 0; u < 6; ++u) {
+        const int i = i0 + ty * 6 + u;
         if (i >= I) continue;
         if (sums) colsum[(size_t)blockIdx.z * I + i] = cs[u];
 #pragma unroll
-        for (int v = 0; v < 4; ++v) {
-            const int j = j0 + tx * 4 + v;
+        for (int v = 0; v < 8; ++v) {
+            const int j = j0 + (v < 4 ? tx * 4 + v : 64 + tx * 4 + v - 4);
             if (j < J) part[((size_t)blockIdx.z * I + i) * J + j] = acc[u][v];
         }
     }
 }
 
-constexpr int kSlices = 128;  // row slices of the parameter reductions
+constexpr int kSlices = 256;  // row slices of the parameter reductions
 
 int64_t slice_rows(int64_t R) { return (R + kSlices - 1) / kSlices; }
 
@@ -723,7 +742,7 @@ int xty(const float* X, int I, const float* Y, int J, int64_t R, float* out, flo
     const int64_t per = slice_rows(R);
     const int slices = (int)((R + per - 1) / per);
     float* part_cs = part + (size_t)slices * I * J;
-    xty_partial_kernel<<<dim3((I + 63) / 64, (J + 63) / 64, slices), 256, 0, st>>>(
+    xty_partial_kernel<<<dim3((I + kXtyI - 1) / kXtyI, (J + kXtyJ - 1) / kXtyJ, slices), 256, 0, st>>>(
         X, I, Y, J, R, per, part, colsum ? part_cs : nullptr);
     F2S_TRY(check_launch("xty_partial_kernel"));
     F2S_TRY(sum_partials(part, slices, I * J, out, st));
