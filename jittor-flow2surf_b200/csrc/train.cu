@@ -828,33 +828,56 @@ struct Bmm {
 };
 
 __global__ void __launch_bounds__(256) bmm_kernel(const Bmm p) {
-    __shared__ __align__(16) float As[16][64 + 4], Bs[16][64 + 4];
+    __shared__ __align__(16) float As[2][16][64 + 4], Bs[2][16][64 + 4];
     const int b = blockIdx.z;
     const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
     const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
     const float* A = p.A + b * p.sAb;
     const float* Bp = p.B + b * p.sBb;
     float acc[4][4] = {};
-    for (int k0 = 0; k0 < p.K; k0 += 16) {
-        for (int e = threadIdx.x; e < 16 * 64; e += 256) {
-            const int kk = e >> 6, mm = e & 63;
-            const int m = m0 + mm, k = k0 + kk;
-            As[kk][mm] = (m < p.M && k < p.K) ? A[m * p.sAm + k * p.sAk] : 0.0f;
-            const int n = n0 + mm;
-            Bs[kk][mm] = (n < p.N && k < p.K) ? Bp[k * p.sBk + n * p.sBn] : 0.0f;
+    // staging slots of this thread: k rows e >> 6, m / n columns e & 63; the
+    // next 16-deep step is loaded into registers while the current one is
+    // multiplied (two shared-memory buffers)
+    float ar[4], br[4];
+    auto fetch = [&](int k0) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int e = threadIdx.x + 256 * u, kk = e >> 6, mm = e & 63;
+            const int k = k0 + kk, m = m0 + mm, n = n0 + mm;
+            ar[u] = (m < p.M && k < p.K) ? A[m * p.sAm + k * p.sAk] : 0.0f;
+            br[u] = (n < p.N && k < p.K) ? Bp[k * p.sBk + n * p.sBn] : 0.0f;
         }
-        __syncthreads();
+    };
+    auto stash = [&](int buf) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int e = threadIdx.x + 256 * u, kk = e >> 6, mm = e & 63;
+            As[buf][kk][mm] = ar[u];
+            Bs[buf][kk][mm] = br[u];
+        }
+    };
+    fetch(0);
+    stash(0);
+    __syncthreads();
+    int buf = 0;
+    for (int k0 = 0; k0 < p.K; k0 += 16) {
+        const bool more = k0 + 16 < p.K;
+        if (more) fetch(k0 + 16);
 #pragma unroll
         for (int kk = 0; kk < 16; ++kk) {
-            const float4 a4 = *reinterpret_cast<const float4*>(&As[kk][ty * 4]);
-            const float4 b4 = *reinterpret_cast<const float4*>(&Bs[kk][tx * 4]);
+            const float4 a4 = *reinterpret_cast<const float4*>(&As[buf][kk][ty * 4]);
+            const float4 b4 = *reinterpret_cast<const float4*>(&Bs[buf][kk][tx * 4]);
             const float a[4] = {a4.x, a4.y, a4.z, a4.w}, bv[4] = {b4.x, b4.y, b4.z, b4.w};
 #pragma unroll
             for (int u = 0; u < 4; ++u)
 #pragma unroll
                 for (int v = 0; v < 4; ++v) acc[u][v] += a[u] * bv[v];
         }
-        __syncthreads();
+        if (more) {
+            stash(buf ^ 1);  // the other buffer: its last readers passed the barrier below
+            __syncthreads();
+            buf ^= 1;
+        }
     }
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
