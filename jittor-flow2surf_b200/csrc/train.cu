@@ -1236,14 +1236,21 @@ extern "C" int f2s_neighbor_reduce_backward(
     F2S_TRY(check_launch("hpe_forward_rows_kernel"));
     // the two projection products on the tensor cores as split bf16 (the
     // fp32 rows split in the GEMM, W_out and its transpose split here;
-    // about 1e-5 relative to sum |x| |w|)
+    // about 1e-5 relative to sum |x| |w|), which need 16-byte bf16 rows;
+    // other widths on the fp32 CUDA-core GEMM
     F2S_LIMIT(R <= INT32_MAX, "neighbor_reduce_backward: %lld edge rows", (long long)R);
+    const bool tensor = H % 8 == 0 && C % 8 == 0;
     void* wsplit = ws + s.wsplit;
     void* wtsplit = ws + s.wtsplit;
-    F2S_TRY(split_bf16(hpe_output_weight, H, C, H, wsplit,
-                       static_cast<char*>(wsplit) + (size_t)C * H * 2, st));
-    F2S_TRY(f2s_linear(hidden, H, wsplit, hpe_output_bias, contrib, C, (int)R, C, H,
-                       F2S_PRECISION_BF16X3, stream));
+    if (tensor) {
+        F2S_TRY(split_bf16(hpe_output_weight, H, C, H, wsplit,
+                           static_cast<char*>(wsplit) + (size_t)C * H * 2, st));
+        F2S_TRY(f2s_linear(hidden, H, wsplit, hpe_output_bias, contrib, C, (int)R, C, H,
+                           F2S_PRECISION_BF16X3, stream));
+    } else {
+        F2S_TRY(f2s_linear(hidden, H, hpe_output_weight, hpe_output_bias, contrib, C, (int)R, C,
+                           H, F2S_PRECISION_FP32, stream));
+    }
     // the message reduction's backward (neighbor_reduce.py:186-202)
     F2S_TRY(messages_backward(content, contrib, indices, B, N, K, C, message_norm_weight,
                               message_norm_bias, grad_output, grad_content, gcontrib,
@@ -1254,10 +1261,15 @@ extern "C" int f2s_neighbor_reduce_backward(
     transpose_small_kernel<<<blocks_for((int64_t)C * H), kBlock, 0, st>>>(hpe_output_weight, C, H,
                                                                           wout_t);
     F2S_TRY(check_launch("transpose_small_kernel"));
-    F2S_TRY(split_bf16(wout_t, C, H, C, wtsplit, static_cast<char*>(wtsplit) + (size_t)C * H * 2,
-                       st));
-    F2S_TRY(f2s_linear(gcontrib, C, wtsplit, nullptr, ghidden, H, (int)R, H, C,
-                       F2S_PRECISION_BF16X3, stream));
+    if (tensor) {
+        F2S_TRY(split_bf16(wout_t, C, H, C, wtsplit,
+                           static_cast<char*>(wtsplit) + (size_t)C * H * 2, st));
+        F2S_TRY(f2s_linear(gcontrib, C, wtsplit, nullptr, ghidden, H, (int)R, H, C,
+                           F2S_PRECISION_BF16X3, stream));
+    } else {
+        F2S_TRY(f2s_linear(gcontrib, C, wout_t, nullptr, ghidden, H, (int)R, H, C,
+                           F2S_PRECISION_FP32, stream));
+    }
     F2S_TRY(xty(gcontrib, C, hidden, H, R, grad_hpe_output_weight, grad_hpe_output_bias, part, st));
     // the HPE activation's backward, in place over grad_hidden (its rows are
     // read before they are written, one warp per row)

@@ -147,7 +147,7 @@ def test_reduce_messages_grad_ties(cuda):
     close(got[0], want[0])
 
 
-@pytest.mark.parametrize("N,K,H,C", [(128, 16, 64, 64), (96, 32, 128, 192)])
+@pytest.mark.parametrize("N,K,H,C", [(128, 16, 64, 64), (96, 32, 128, 192), (80, 8, 36, 44)])
 def test_reduce_neighbor_messages_backward(cuda, N, K, H, C):
     rng = np.random.default_rng(N + C)
     B, D = 2, 6
