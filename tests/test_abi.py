@@ -59,3 +59,35 @@ def test_operator_rejects_cpu_tensors():
         knn_indices(torch.zeros(1, 3, 8), 4)
     with pytest.raises(ValueError, match="k must be >= 1"):
         knn_indices(torch.zeros(1, 3, 8), 0)
+
+
+def test_training_entries_validate_on_the_host():
+    """The backward and loss entries check sizes, pointers, limits and
+    workspace sizes before any device work, and a zero batch is a no-op."""
+    import ctypes
+
+    lib = _lib.lib()
+    bad = _lib.F2S_ERR_INVALID_ARGUMENT
+    assert lib.f2s_nearest_backward(None, None, 1, 0, 4, None, None, None, None, None, None,
+                                    None) == bad
+    assert lib.f2s_nearest_backward(None, None, 0, 4, 4, None, None, None, None, None, None,
+                                    None) == _lib.F2S_OK
+    assert lib.f2s_nearest_backward(None, None, 1, 4, 4, None, None, None, None, None, None,
+                                    None) == bad
+    assert b"null pointer" in lib.f2s_last_error()
+    f = ctypes.c_float(1.0)
+    assert lib.f2s_dcd_loss(None, None, 1, 4, 0, f, None, None, None, None, None, 0, None) == bad
+    assert lib.f2s_velocity_loss(None, None, 1, 0, None, None, None, None, None) == bad
+    assert lib.f2s_hpe_activation_backward(None, ctypes.c_int64(8), 300, None, None, None, None,
+                                           None, None, None, 0, None) == _lib.F2S_ERR_UNSUPPORTED
+    assert b"at most 256" in lib.f2s_last_error()
+    assert lib.f2s_neighbor_messages_backward(None, None, None, 1, 8, 4, 320, None, None, None,
+                                              None, None, None, None, None, 0,
+                                              None) == _lib.F2S_ERR_UNSUPPORTED
+    size = ctypes.c_size_t()
+    assert lib.f2s_offset_attention_backward_workspace_bytes(2, 64, 16, 32,
+                                                             ctypes.byref(size)) == _lib.F2S_OK
+    assert size.value >= 2 * 2 * 64 * 64 * 4
+    assert lib.f2s_neighbor_reduce_backward_workspace_bytes(1, 16, 8, 6, 64, 64,
+                                                            ctypes.byref(size)) == _lib.F2S_OK
+    assert size.value > 0
