@@ -281,7 +281,7 @@ __global__ void grid_prepare_kernel(const GridPair P) {
          i += (int64_t)gridDim.x * blockDim.x)
         S.counts[i] = 0;
     const int t = blockIdx.x * blockDim.x + threadIdx.x;
-    if (t < 6 * P.B) S.box[t] = 0xffffffffu;
+    for (int e = t; e < 6 * P.B; e += gridDim.x * blockDim.x) S.box[e] = 0xffffffffu;
     if (blockIdx.y == 0 && t < 3) P.counters[t] = 0u;
 }
 

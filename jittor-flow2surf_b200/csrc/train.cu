@@ -1278,8 +1278,14 @@ extern "C" int f2s_neighbor_reduce_backward(
     // the input projection's gradients (neighbor_reduce.py:219-224)
     const size_t gsmem = ((size_t)H * D + (size_t)8 * H * (D + 1)) * sizeof(float);
 #define F2S_GEO_GRAD(CPL)                                                                          \
-    geometry_grad_kernel<CPL><<<rb, kBlock, gsmem, st>>>(ghidden, geometry, R, H, D,               \
-                                                         hpe_input_weight, grad_geometry, part)
+    do {                                                                                           \
+        F2S_CUDA_TRY(cudaFuncSetAttribute(geometry_grad_kernel<CPL>,                               \
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize,             \
+                                          (int)gsmem));                                            \
+        geometry_grad_kernel<CPL><<<rb, kBlock, gsmem, st>>>(ghidden, geometry, R, H, D,           \
+                                                             hpe_input_weight, grad_geometry,      \
+                                                             part);                                \
+    } while (0)
     if (hcpl <= 1) F2S_GEO_GRAD(1);
     else if (hcpl <= 2) F2S_GEO_GRAD(2);
     else if (hcpl <= 4) F2S_GEO_GRAD(4);
