@@ -247,6 +247,9 @@ def profile_training(args) -> None:
                      .sum().backward())
     out["neighbor_reduce_forward_ms"] = fwd
     out["neighbor_reduce_backward_ms"] = both - fwd
+    out["neighbor_reduce_forward_bf16x3_ms"] = _event_ms(
+        lambda: reduce_neighbor_messages(content, geometry, idx, *params,
+                                         precision="bf16x3").detach())
     q = torch.nn.functional.layer_norm(torch.randn(B, N, d, generator=g, device="cuda"), (d,))
     k = torch.nn.functional.layer_norm(torch.randn(B, N, d, generator=g, device="cuda"),
                                        (d,)).transpose(1, 2).contiguous()

@@ -149,7 +149,8 @@ def reduce_neighbor_messages(content, geometry, indices, hpe_input_weight, hpe_i
     layer, its output projection and the reduce fused in one kernel.
     `precision` "fp32" (CUDA cores) or "bf16x3" (tcgen05: the output
     projection as split-bf16 MMAs, close to fp32; D 6, H 64 or 128, C 64, 128
-    or 192, K 8, 16 or 32).
+    or 192, K 8, 16 or 32). Differentiable in both: the backward recomputes
+    the stage in fp32 (neighbor_reduce.py:155-237).
     """
     if precision not in ("fp32", "bf16x3"):
         raise ValueError(f"precision must be 'fp32' or 'bf16x3', got {precision!r}")
@@ -173,10 +174,7 @@ def reduce_neighbor_messages(content, geometry, indices, hpe_input_weight, hpe_i
                message_norm_bias)
     _require_cuda(*tensors)
     if _needs_grad(*tensors):
-        if precision != "fp32":
-            raise ValueError("the tensor-core neighbour stage has no backward; use "
-                             "precision='fp32'")
-        return _NeighborMessages.apply(*tensors)
+        return _NeighborMessages.apply(precision, *tensors)
     return _neighbor_forward(tensors, precision)
 
 
@@ -204,14 +202,16 @@ def _neighbor_forward(tensors, precision="fp32"):
 
 class _NeighborMessages(torch.autograd.Function):
     """reduce_neighbor_messages with its backward (_NeighborMessageFunction,
-    flow2surf/models/ops/neighbor_reduce.py:113-237): the fp32 fused forward,
-    and a backward that recomputes the HPE rows and the contribution."""
+    flow2surf/models/ops/neighbor_reduce.py:113-237): the fused forward (fp32,
+    or the split-bf16 tensor-core kernel, about 1e-5 relative to it), and a
+    backward that recomputes the HPE rows and the contribution in fp32 (the
+    gradient of the fp32 function at the same inputs)."""
 
     @staticmethod
-    def forward(ctx, *tensors):
+    def forward(ctx, precision, *tensors):
         tensors = tuple(t.contiguous() if i == 2 else _f32(t) for i, t in enumerate(tensors))
         ctx.save_for_backward(*tensors)
-        return _neighbor_forward(tensors)
+        return _neighbor_forward(tensors, precision)
 
     @staticmethod
     def backward(ctx, grad_output):
@@ -222,14 +222,14 @@ class _NeighborMessages(torch.autograd.Function):
         dims = geometry.shape[-1]
         grads = [torch.empty_like(x) for i, x in enumerate(t) if i != 2]
         if content.numel() == 0 or indices.numel() == 0:
-            return tuple(None if i == 2 else torch.zeros_like(x) for i, x in enumerate(t))
+            return (None,) + tuple(None if i == 2 else torch.zeros_like(x) for i, x in enumerate(t))
         grad_output = _f32(grad_output)
         ws = _workspace("f2s_neighbor_reduce_backward_workspace_bytes", batch, points,
                         neighbors, dims, hidden, channels)
         _lib.call("f2s_neighbor_reduce_backward", *[_lib.ptr(x) for x in t], batch, points,
                   neighbors, dims, hidden, channels, _lib.ptr(grad_output),
                   *[_lib.ptr(g) for g in grads], _lib.ptr(ws), ws.numel(), _lib.stream_handle())
-        return (grads[0], grads[1], None, *grads[2:])
+        return (None, grads[0], grads[1], None, *grads[2:])
 
 
 def hpe_activation_grad(preactivation: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor,

@@ -147,8 +147,14 @@ def test_reduce_messages_grad_ties(cuda):
     close(got[0], want[0])
 
 
-@pytest.mark.parametrize("N,K,H,C", [(128, 16, 64, 64), (96, 32, 128, 192), (80, 8, 36, 44)])
-def test_reduce_neighbor_messages_backward(cuda, N, K, H, C):
+@pytest.mark.parametrize("N,K,H,C,precision", [(128, 16, 64, 64, "fp32"),
+                                               (96, 32, 128, 192, "fp32"),
+                                               (80, 8, 36, 44, "fp32"),
+                                               (96, 32, 128, 192, "bf16x3")])
+def test_reduce_neighbor_messages_backward(cuda, N, K, H, C, precision):
+    """The whole neighbour-stage backward; with the split-bf16 forward the
+    backward is the same fp32 recompute, so its gradients are checked to the
+    same bound."""
     rng = np.random.default_rng(N + C)
     B, D = 2, 6
     content = rng.normal(size=(B, 2 * C, N))
@@ -167,8 +173,9 @@ def test_reduce_neighbor_messages_backward(cuda, N, K, H, C):
     go[ot.near_tie_mask(content, contribution, idx, params[6], params[7])] = 0.0
     inputs = [dev(content, True), dev(geometry, True), torch.from_numpy(idx).cuda()]
     inputs += [dev(p, True) for p in params]
-    out = reduce_neighbor_messages(*inputs)
-    close(out, ot.reduce_neighbor_messages(content, geometry, idx, *params), norm=1e-5)
+    out = reduce_neighbor_messages(*inputs, precision=precision)
+    close(out, ot.reduce_neighbor_messages(content, geometry, idx, *params),
+          norm=1e-5 if precision == "fp32" else 1e-4)
     (out * dev(go)).sum().backward()
     want = ot.reduce_neighbor_messages_backward(content, geometry, idx, *params, go)
     got = [inputs[0].grad, inputs[1].grad] + [t.grad for t in inputs[3:]]
