@@ -980,17 +980,20 @@ column_jacobian_kernel(const float* __restrict__ P, float* __restrict__ D,
 constexpr int kAttnChunk = 8;  // batch items per pass (2 N^2 floats each)
 
 struct AttnSpace {
-    size_t P, D, Gh, r, bytes;
+    size_t P, D, Gh, r, GhT, VT, KT, bytes;
 };
 
-AttnSpace attn_space(int B, int N, int C) {
+AttnSpace attn_space(int B, int N, int d, int C) {
     const size_t chunk = (size_t)(B < kAttnChunk ? B : kAttnChunk);
     AttnSpace s;
     s.P = 0;
     s.D = align256(s.P + chunk * N * N * 4);
     s.Gh = align256(s.D + chunk * N * N * 4);
     s.r = align256(s.Gh + chunk * N * C * 4);
-    s.bytes = align256(s.r + chunk * N * 4);
+    s.GhT = align256(s.r + chunk * N * 4);      // G^ transposed, (C, N) per item
+    s.VT = align256(s.GhT + chunk * N * C * 4);  // V transposed, (C, N) per item
+    s.KT = align256(s.VT + chunk * N * C * 4);   // K transposed, (N, d) per item
+    s.bytes = align256(s.KT + chunk * N * d * 4);
     return s;
 }
 
@@ -1299,7 +1302,7 @@ extern "C" int f2s_neighbor_reduce_backward(
 extern "C" int f2s_offset_attention_backward_workspace_bytes(int B, int N, int d, int C,
                                                              size_t* bytes) {
     F2S_REQUIRE(B >= 0 && N >= 0 && d >= 1 && C >= 1 && bytes, "bad workspace query");
-    *bytes = attn_space(B, N, C).bytes;
+    *bytes = attn_space(B, N, d, C).bytes;
     return F2S_OK;
 }
 
@@ -1314,7 +1317,7 @@ extern "C" int f2s_offset_attention_backward(const float* query, const float* ke
     F2S_REQUIRE(query && key && value && output && grad_output && grad_query && grad_key &&
                     grad_value && workspace,
                 "offset_attention_backward: null pointer");
-    const AttnSpace s = attn_space(B, N, C);
+    const AttnSpace s = attn_space(B, N, d, C);
     if (workspace_bytes < s.bytes)
         return fail(F2S_ERR_WORKSPACE,
                     "offset_attention_backward needs %zu workspace bytes, got %zu", s.bytes,
@@ -1324,6 +1327,9 @@ extern "C" int f2s_offset_attention_backward(const float* query, const float* ke
     float* D = reinterpret_cast<float*>(ws + s.D);
     float* Gh = reinterpret_cast<float*>(ws + s.Gh);
     float* r = reinterpret_cast<float*>(ws + s.r);
+    float* GhT = reinterpret_cast<float*>(ws + s.GhT);
+    float* VT = reinterpret_cast<float*>(ws + s.VT);
+    float* KT = reinterpret_cast<float*>(ws + s.KT);
     cudaStream_t st = as_stream(stream);
     TraceScope trace(kTagTraining, st);
     const int64_t NN = (int64_t)N * N;
@@ -1345,13 +1351,20 @@ extern "C" int f2s_offset_attention_backward(const float* query, const float* ke
         F2S_TRY(bmm(Bmm{P, NN, 1, N, Gh, (int64_t)N * C, C, 1, grad_value + (size_t)b0 * N * C,
                         (int64_t)N * C, C, N, C, N},
                     nb, st));
-        // D = G^ V^T, then dS = P (D - r - c) per key column
-        F2S_TRY(bmm(Bmm{Gh, (int64_t)N * C, C, 1, v, (int64_t)N * C, 1, C, D, NN, N, N, N, C}, nb,
-                    st));
+        // D = G^ V^T on transposed copies of G^ and V, so both operands are
+        // read along rows (i and j contiguous); then dS = P (D - r - c) per
+        // key column
+        F2S_TRY(transpose_batched(Gh, GhT, nb, N, C, st));
+        F2S_TRY(transpose_batched(v, VT, nb, N, C, st));
+        F2S_TRY(bmm(Bmm{GhT, (int64_t)C * N, 1, N, VT, (int64_t)C * N, N, 1, D, NN, N, N, N, C},
+                    nb, st));
         column_jacobian_kernel<<<dim3((N + 31) / 32, nb), 256, 0, st>>>(P, D, r, N);
         F2S_TRY(check_launch("column_jacobian_kernel"));
-        // dQ = dS K^T, dK = Q^T dS
-        F2S_TRY(bmm(Bmm{D, NN, N, 1, k, (int64_t)d * N, 1, N, grad_query + (size_t)b0 * N * d,
+        // dQ = dS K^T from dS transposed (into P, which is no longer needed)
+        // and K transposed, so both operands are read along rows; dK = Q^T dS
+        F2S_TRY(transpose_batched(D, P, nb, N, N, st));
+        F2S_TRY(transpose_batched(k, KT, nb, d, N, st));
+        F2S_TRY(bmm(Bmm{P, NN, 1, N, KT, (int64_t)N * d, d, 1, grad_query + (size_t)b0 * N * d,
                         (int64_t)N * d, d, N, d, N},
                     nb, st));
         F2S_TRY(bmm(Bmm{q, (int64_t)N * d, 1, d, D, NN, N, 1, grad_key + (size_t)b0 * d * N,
