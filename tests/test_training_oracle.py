@@ -133,7 +133,7 @@ def test_messages_backward_matches_autograd():
 def test_messages_backward_routes_to_every_tie():
     """Two identical edges (the same neighbour, no contribution difference)
     tie for the maximum wherever either wins: the reference kernel gives each
-    the full upstream gradient (neighbor_reduce_backward.cu:58-60)."""
+    the full upstream gradient (neighbor_reduce_backward.cu:59-62)."""
     content, contribution, idx, w, b, go = _message_case(5, K=4)
     idx[:, :, 1] = idx[:, :, 0]
     contribution[:, :, 1] = contribution[:, :, 0]
