@@ -732,6 +732,7 @@ xty_partial_kernel(const float* __restrict__ X, int I, const float* __restrict__
 }
 
 constexpr int kSlices = 256;  // row slices of the parameter reductions
+constexpr int kWgradSlices = 2048;  // row slices of the input projection's weight gradient
 
 int64_t slice_rows(int64_t R) { return (R + kSlices - 1) / kSlices; }
 
@@ -750,60 +751,75 @@ int xty(const float* X, int I, const float* Y, int J, int64_t R, float* out, flo
     return sum_partials(part_cs, slices, I, colsum, st);
 }
 
-// A warp per row: grad_geometry[r][d] = sum_h grad_pre[r][h] W_in[h][d]; and,
-// per lane for its channels h = lane + 32 t, the input projection's weight
-// gradient sum_r grad_pre[r][h] geometry[r][d] and bias gradient
-// sum_r grad_pre[r][h], accumulated in the warp's own rows of shared memory
-// (a lane touches only its channels' entries) and summed over the warps into
-// one partial row per block (H x D, then H). W_in is read from shared memory.
-template <int kCPL>
+// One thread per edge row: grad_geometry[r][d] = sum_h grad_pre[r][h]
+// W_in[h][d] (D <= 8), W_in broadcast from shared memory; the row read as
+// 16-byte chunks when H is a multiple of 4 (rows 16-byte aligned), else by
+// single floats.
 __global__ void __launch_bounds__(kBlock)
-geometry_grad_kernel(const float* __restrict__ grad_pre, const float* __restrict__ geometry,
-                     int64_t rows, int H, int D, const float* __restrict__ w_in,
-                     float* __restrict__ grad_geometry, float* __restrict__ part) {
-    extern __shared__ float sm[];  // W_in [H * D], then [8][H * (D + 1)] accumulators
-    const int lane = threadIdx.x & 31;
-    const int warp = threadIdx.x >> 5;
-    const int wpb = blockDim.x >> 5;
-    const int W = H * (D + 1);
-    float* wsm = sm;
-    float* red = sm + H * D;
+geometry_grad_kernel(const float* __restrict__ grad_pre, int64_t rows, int H, int D,
+                     const float* __restrict__ w_in, float* __restrict__ grad_geometry) {
+    extern __shared__ float wsm[];  // [H][D]
     for (int e = threadIdx.x; e < H * D; e += blockDim.x) wsm[e] = w_in[e];
-    for (int e = threadIdx.x; e < wpb * W; e += blockDim.x) red[e] = 0.0f;
     __syncthreads();
-    float* mine = red + warp * W;
-    for (int64_t row = (int64_t)blockIdx.x * wpb + warp; row < rows;
-         row += (int64_t)gridDim.x * wpb) {
-        float geo[8], acc[8];
+    const bool vec = (H & 3) == 0;
+    for (int64_t row = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; row < rows;
+         row += (int64_t)gridDim.x * blockDim.x) {
+        const float* gr = grad_pre + row * H;
+        float acc[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+        for (int h4 = 0; h4 < (H + 3) / 4; ++h4) {
+            float gv[4];
+            if (vec) {
+                const float4 g = reinterpret_cast<const float4*>(gr)[h4];
+                gv[0] = g.x;
+                gv[1] = g.y;
+                gv[2] = g.z;
+                gv[3] = g.w;
+            } else {
 #pragma unroll
-        for (int d = 0; d < 8; ++d) {
-            geo[d] = d < D ? geometry[row * D + d] : 0.0f;
-            acc[d] = 0.0f;
-        }
+                for (int u = 0; u < 4; ++u) gv[u] = 4 * h4 + u < H ? gr[4 * h4 + u] : 0.0f;
+            }
 #pragma unroll
-        for (int t = 0; t < kCPL; ++t) {
-            const int h = lane + 32 * t;
-            if (h >= H) continue;
-            const float g = grad_pre[row * H + h];
-            mine[H * D + h] += g;
+            for (int u = 0; u < 4; ++u) {
+                if (4 * h4 + u >= H) break;
+                const float* w = wsm + (4 * h4 + u) * D;
 #pragma unroll
-            for (int d = 0; d < 8; ++d) {
-                if (d >= D) continue;
-                acc[d] += g * wsm[h * D + d];
-                mine[h * D + d] += g * geo[d];
+                for (int d = 0; d < 8; ++d)
+                    if (d < D) acc[d] = fmaf(gv[u], w[d], acc[d]);
             }
         }
 #pragma unroll
-        for (int d = 0; d < 8; ++d) {
-            const float sum = warp_sum(acc[d]);
-            if (lane == d && d < D) grad_geometry[row * D + d] = sum;
-        }
+        for (int d = 0; d < 8; ++d)
+            if (d < D) grad_geometry[row * D + d] = acc[d];
     }
-    __syncthreads();
-    for (int c = threadIdx.x; c < W; c += blockDim.x) {
-        float s = 0.0f;
-        for (int w = 0; w < wpb; ++w) s += red[w * W + c];
-        part[(size_t)blockIdx.x * W + c] = s;
+}
+
+// One thread per hidden channel h over a slice of edge rows (blockIdx.x): the
+// input projection's weight gradient sum_r grad_pre[r][h] geometry[r][d] and
+// bias gradient sum_r grad_pre[r][h], as one partial row per slice (H x D,
+// then H).
+__global__ void __launch_bounds__(256)
+input_weight_grad_kernel(const float* __restrict__ grad_pre, const float* __restrict__ geometry,
+                         int64_t rows, int64_t rows_per_slice, int H, int D,
+                         float* __restrict__ part) {
+    const int h = threadIdx.x;
+    const int64_t r_lo = (int64_t)blockIdx.x * rows_per_slice;
+    const int64_t r_hi = r_lo + rows_per_slice < rows ? r_lo + rows_per_slice : rows;
+    float aw[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+    float ab = 0.0f;
+    if (h < H) {
+#pragma unroll 4
+        for (int64_t r = r_lo; r < r_hi; ++r) {
+            const float g = grad_pre[r * H + h];
+            ab += g;
+#pragma unroll
+            for (int d = 0; d < 8; ++d)
+                if (d < D) aw[d] = fmaf(g, geometry[r * D + d], aw[d]);
+        }
+        float* out = part + (size_t)blockIdx.x * H * (D + 1);
+#pragma unroll
+        for (int d = 0; d < 8; ++d)
+            if (d < D) out[h * D + d] = aw[d];
+        out[H * D + h] = ab;
     }
 }
 
@@ -1023,7 +1039,7 @@ NrSpace nr_space(int B, int N, int K, int D, int H, int C) {
     // partial rows: the per-block kernels (<= 8 per SM) and the row slices
     const size_t blocks = (size_t)sm_count() * 8;
     size_t part = 2 * blocks * (size_t)(H > C ? H : C);
-    const size_t geo = blocks * (size_t)H * (D + 1);
+    const size_t geo = (size_t)kWgradSlices * H * (D + 1);
     part = part > geo ? part : geo;
     const size_t ch = (size_t)C * H + C, hd = (size_t)H * D + H;
     const size_t slices = (size_t)kSlices * (ch > hd ? ch : hd);
@@ -1279,24 +1295,16 @@ extern "C" int f2s_neighbor_reduce_backward(
     F2S_TRY(hpe_activation_backward(pre, R, H, hpe_norm_weight, hpe_norm_bias, ghidden, ghidden,
                                     grad_hpe_norm_weight, grad_hpe_norm_bias, part, st));
     // the input projection's gradients (neighbor_reduce.py:219-224)
-    const size_t gsmem = ((size_t)H * D + (size_t)8 * H * (D + 1)) * sizeof(float);
-#define F2S_GEO_GRAD(CPL)                                                                          \
-    do {                                                                                           \
-        F2S_CUDA_TRY(cudaFuncSetAttribute(geometry_grad_kernel<CPL>,                               \
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize,             \
-                                          (int)gsmem));                                            \
-        geometry_grad_kernel<CPL><<<rb, kBlock, gsmem, st>>>(ghidden, geometry, R, H, D,           \
-                                                             hpe_input_weight, grad_geometry,      \
-                                                             part);                                \
-    } while (0)
-    if (hcpl <= 1) F2S_GEO_GRAD(1);
-    else if (hcpl <= 2) F2S_GEO_GRAD(2);
-    else if (hcpl <= 4) F2S_GEO_GRAD(4);
-    else F2S_GEO_GRAD(8);
-#undef F2S_GEO_GRAD
+    const size_t gsmem = (size_t)H * D * sizeof(float);
+    geometry_grad_kernel<<<blocks_for(R), kBlock, gsmem, st>>>(ghidden, R, H, D, hpe_input_weight,
+                                                                grad_geometry);
     F2S_TRY(check_launch("geometry_grad_kernel"));
-    F2S_TRY(sum_partials_strided(part, rb, H * D, H * (D + 1), grad_hpe_input_weight, st));
-    return sum_partials_strided(part + H * D, rb, H, H * (D + 1), grad_hpe_input_bias, st);
+    const int64_t per = (R + kWgradSlices - 1) / kWgradSlices;
+    const int slices = (int)((R + per - 1) / per);
+    input_weight_grad_kernel<<<slices, 256, 0, st>>>(ghidden, geometry, R, per, H, D, part);
+    F2S_TRY(check_launch("input_weight_grad_kernel"));
+    F2S_TRY(sum_partials_strided(part, slices, H * D, H * (D + 1), grad_hpe_input_weight, st));
+    return sum_partials_strided(part + H * D, slices, H, H * (D + 1), grad_hpe_input_bias, st);
 }
 
 extern "C" int f2s_offset_attention_backward_workspace_bytes(int B, int N, int d, int C,

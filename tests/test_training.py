@@ -150,6 +150,7 @@ def test_reduce_messages_grad_ties(cuda):
 @pytest.mark.parametrize("N,K,H,C,precision", [(128, 16, 64, 64, "fp32"),
                                                (96, 32, 128, 192, "fp32"),
                                                (80, 8, 36, 44, "fp32"),
+                                               (40, 8, 50, 24, "fp32"),
                                                (96, 32, 128, 192, "bf16x3")])
 def test_reduce_neighbor_messages_backward(cuda, N, K, H, C, precision):
     """The whole neighbour-stage backward; with the split-bf16 forward the
