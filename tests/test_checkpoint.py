@@ -1,4 +1,4 @@
-"""Checkpoint loading (SURVEY f2): the reference's model.save / model.load
+"""Checkpoint loading: the reference's model.save / model.load
 format (a pickled {state-dict name: array} dict, flow2surf/training/
 checkpoint.py:72-74, predict.py:46) into Flow2SurfNet, on CPU."""
 
