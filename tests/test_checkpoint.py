@@ -1,6 +1,7 @@
 """Checkpoint loading: the reference's model.save / model.load
-format (a pickled {state-dict name: array} dict, flow2surf/training/
-checkpoint.py:72-74, predict.py:46) into Flow2SurfNet, on CPU."""
+format (a pickled {state-dict name: array} dict, written by model.save at
+flow2surf/training/optimization.py:41-42 and training/checkpoint.py:153,
+read by predict.py:46) into Flow2SurfNet, on CPU."""
 
 import collections
 import os
