@@ -21,9 +21,13 @@ patch_denoise with a pinned host array in and a host array out. The
 cores (the reference's Jittor is not installed here) on a bounded sample of
 the same cloud. Two more legs ride on the line, outside the timed steps:
 `chamfer` (the denoised cloud against a 100,000-point clean sample of its
-surface, with its fp32 SIMT roofline) and `one_cloud` (strong scaling: one
+surface, by the exact grid search), `one_cloud` (strong scaling: one
 400,000-point cloud split by patch across the ranks, one NCCL all-reduce of
-the vote sums per Euler step, with that all-reduce's own time).
+the vote sums per Euler step, with that all-reduce's own time) and `batch`
+(the multi-GPU batch: 64 clouds of 100,000 points with noise sigma drawn
+from U[0.005, 0.025] x the bounding-box diagonal, sharded by cloud over the
+ranks, each denoised and scored by its Chamfer distance against a 100,000-point
+clean sample of its surface).
 """
 
 from __future__ import annotations
@@ -66,6 +70,8 @@ def parse_args():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-one-cloud", action="store_true",
                    help="skip the strong-scaling leg (one 400k-point cloud split by patch)")
+    p.add_argument("--no-batch", action="store_true",
+                   help="skip the batch leg (64 clouds of 100k points sharded by cloud)")
     p.add_argument("--precision", choices=["fp32", "tf32"], default="tf32",
                    help="arithmetic of the trunk and decoder contractions")
     p.add_argument("--encoder-precision", choices=["fp32", "tf32", "bf16x3"], default="bf16x3",
@@ -292,6 +298,68 @@ def workload_config(args, world: int) -> dict:
                         "the float64 vote sums (24 bytes per point) per Euler step"
                         if args.one_cloud else f"shard by cloud, {world} GPU(s), no collective"),
     }
+
+
+BATCH_CLOUDS = 64
+BATCH_POINTS = 100_000
+
+
+def batch_leg(model, world: int, rank: int, dev) -> dict:
+    """The multi-GPU batch: 64 synthetic clouds of 100,000 points (the
+    denoise cloud's mesh and Laplace-noise recipe, sigma drawn from
+    U[0.005, 0.025] x the bounding-box diagonal per cloud), sharded by cloud
+    (rank r takes clouds r, r + N, ...; no collective). Each cloud is
+    denoised and its Chamfer distance to a 100,000-point clean sample of its
+    surface computed on the device. Device time of a rank's whole shard, max
+    over ranks; value = all 64 clouds' points / that time (total work fixed:
+    strong scaling by cloud)."""
+    import torch
+    import torch.distributed as dist
+
+    from flow2surf_b200.inference import denoise_device
+    from flow2surf_b200.ops import chamfer_distances
+    from flow2surf_b200.synthetic import mesh_cloud
+
+    mine = list(range(rank, BATCH_CLOUDS, world))
+    clouds, refs = [], []
+    for i in mine:
+        sigma = float(np.random.default_rng(1000 + i).uniform(0.005, 0.025))
+        noisy, _, ref = mesh_cloud(BATCH_POINTS, seed=1000 + i, sigma_fraction=sigma,
+                                   noise_type="laplace", clean_points=BATCH_POINTS)
+        clouds.append(torch.from_numpy(noisy).to(dev))
+        refs.append(torch.from_numpy(ref).to(dev)[None])
+    losses = torch.zeros(len(mine), dtype=torch.float64, device=dev)
+
+    def shard():
+        for n, (pts, ref) in enumerate(zip(clouds, refs)):
+            out = denoise_device(model, pts, rng=np.random.default_rng(mine[n]), **DENOISE)
+            losses[n:n + 1] = chamfer_distances(out[None], ref)
+
+    if mine:  # warm-up on the shard's first cloud
+        out = denoise_device(model, clouds[0], rng=np.random.default_rng(mine[0]), **DENOISE)
+        chamfer_distances(out[None], refs[0])
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    shard()
+    stop.record()
+    torch.cuda.synchronize(dev)
+    t = torch.tensor([start.elapsed_time(stop), float(losses.sum().item())],
+                     dtype=torch.float64, device=dev)
+    if world > 1:
+        ms_max = t[:1].clone()
+        dist.all_reduce(ms_max, op=dist.ReduceOp.MAX)
+        loss_sum = t[1:].clone()
+        dist.all_reduce(loss_sum, op=dist.ReduceOp.SUM)
+        t = torch.cat([ms_max, loss_sum])
+    ms, loss_sum = t.tolist()
+    return {"clouds": BATCH_CLOUDS, "points_per_cloud": BATCH_POINTS, "ranks": world,
+            "sharding": "by cloud, no collective", "scaling": "strong", "ms": ms,
+            "value": BATCH_CLOUDS * BATCH_POINTS / (ms * 1e-3), "unit": UNIT,
+            "chamfer_mean": loss_sum / BATCH_CLOUDS,
+            "noise": "Laplace, sigma U[0.005, 0.025] x bbox diagonal per cloud"}
 
 
 def make_cloud(points: int, rank: int):
@@ -634,6 +702,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
                            noise_type="laplace", clean_points=CHAMFER_REFERENCE_POINTS)[2]
     chamfer = chamfer_leg(out, torch.from_numpy(reference).to(dev))
     one_cloud = None if args.one_cloud or args.no_one_cloud else one_cloud_leg(model, world, dev)
+    batch = None if args.one_cloud or args.no_batch else batch_leg(model, world, rank, dev)
     if rank != 0:
         return
 
@@ -661,6 +730,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
                 "d2h_bytes_per_step": int(host_out.nbytes)},
         "chamfer": chamfer,
         "one_cloud": one_cloud,
+        "batch": batch,
         "gpu_launches": rec.launches * steps // traced_steps,
         "clocks": clocks.summary(),
         "kernel_breakdown": (f"separate traced pass of {traced_steps} steps (CUDA events "
