@@ -91,3 +91,27 @@ def test_training_entries_validate_on_the_host():
     assert lib.f2s_neighbor_reduce_backward_workspace_bytes(1, 16, 8, 6, 64, 64,
                                                             ctypes.byref(size)) == _lib.F2S_OK
     assert size.value > 0
+
+
+def test_nearest_workspace_covers_the_grid_search():
+    """Below 4096 points in either set the nearest / Chamfer workspace is the
+    64-bit keys alone; from 4096 points in both sets it also holds both grids
+    (cell counts and starts, sorted points, the far-search list), growing
+    with the sets."""
+    import ctypes
+
+    lib = _lib.lib()
+    size = ctypes.c_size_t()
+
+    def ws(B, M, N):
+        assert lib.f2s_nearest_workspace_bytes(B, M, N, ctypes.byref(size)) == _lib.F2S_OK
+        return size.value
+
+    assert ws(2, 4095, 100_000) == 2 * (4095 + 100_000) * 8
+    assert ws(1, 300, 257) == (300 + 257) * 8
+    small, large = ws(1, 4096, 4096), ws(1, 50_000, 100_000)
+    assert small > (4096 + 4096) * 8
+    assert large > small and large > (50_000 + 100_000) * 8
+    assert ws(4, 50_000, 100_000) > large
+    assert lib.f2s_nearest_workspace_bytes(-1, 1, 1, ctypes.byref(size)) == \
+        _lib.F2S_ERR_INVALID_ARGUMENT
